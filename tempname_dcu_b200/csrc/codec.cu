@@ -1,0 +1,162 @@
+// Standalone TACO codec kernels and the ordered BF16 source reduction.
+//
+// Reference parity: src/taco/codec.hip encode_kernel (:78-119), decode_kernel
+// (:121-135), reduce_kernel (:137-148) and the C ABI (:162-197).  The B200
+// versions use one warp per H128 group (butterflies in registers + lane
+// shuffles, hardware cvt.rn.satfinite.e4m3x2) instead of a 128-thread block
+// with shared-memory tree reductions.  The same device functions (codec.cuh)
+// are what the fused GEMM epilogues and the reduce-scatter consumer use.
+#include "codec.cuh"
+
+namespace tdb {
+namespace taco {
+
+constexpr int kWarpsPerBlock = 8;
+
+__global__ void __launch_bounds__(256) encode_kernel(const uint16_t* __restrict__ input,
+                                                     uint8_t* __restrict__ packet, int64_t groups) {
+  const int lane = threadIdx.x & 31;
+  const int64_t g = int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (g >= groups) return;
+  const int64_t elements = groups * kGroup;
+  const uint2 raw = reinterpret_cast<const uint2*>(input + g * kGroup)[lane];
+  float x[4] = {bf16_bits_to_float(raw.x & 0xffff), bf16_bits_to_float(raw.x >> 16),
+                bf16_bits_to_float(raw.y & 0xffff), bf16_bits_to_float(raw.y >> 16)};
+  GroupScales s;
+  const uint32_t word = encode_group_warp(x, lane, s);
+  reinterpret_cast<uint32_t*>(packet + g * kGroup)[lane] = word;
+  if (lane == 0) {
+    float* quant = reinterpret_cast<float*>(packet + elements);
+    quant[g] = s.quant;
+    quant[groups + g] = s.adaptive;
+  }
+}
+
+__global__ void __launch_bounds__(256) decode_kernel(const uint8_t* __restrict__ packet,
+                                                     uint16_t* __restrict__ output, int64_t groups) {
+  const int lane = threadIdx.x & 31;
+  const int64_t g = int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (g >= groups) return;
+  const int64_t elements = groups * kGroup;
+  const float* scales = reinterpret_cast<const float*>(packet + elements);
+  const uint32_t word = reinterpret_cast<const uint32_t*>(packet + g * kGroup)[lane];
+  float v[4];
+  decode_group_warp(word, scales[g], scales[groups + g], lane, v);
+  uint2 out;
+  out.x = uint32_t(float_to_bf16_bits(v[0])) | (uint32_t(float_to_bf16_bits(v[1])) << 16);
+  out.y = uint32_t(float_to_bf16_bits(v[2])) | (uint32_t(float_to_bf16_bits(v[3])) << 16);
+  reinterpret_cast<uint2*>(output + g * kGroup)[lane] = out;
+}
+
+// Ordered sum over `world` sources, BF16 rounding after every addition, source
+// order 0..world-1 with the local partial spliced in at `rank`.  `remote` holds
+// the world-1 remote sources in ascending rank order excluding `rank`.
+__global__ void reduce_kernel(const uint16_t* __restrict__ local, const uint16_t* __restrict__ remote,
+                              uint16_t* __restrict__ output, int64_t elements, int rank, int world) {
+  const int64_t i8 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  if (i8 >= elements) return;
+  if (i8 + 8 <= elements) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (int src = 0; src < world; ++src) {
+      const uint16_t* p = src == rank ? local : remote + int64_t(src < rank ? src : src - 1) * elements;
+      const uint4 v = *reinterpret_cast<const uint4*>(p + i8);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] = bf16_bits_to_float(float_to_bf16_bits(acc[2 * j] + bf16_bits_to_float(w[j] & 0xffff)));
+        acc[2 * j + 1] = bf16_bits_to_float(float_to_bf16_bits(acc[2 * j + 1] + bf16_bits_to_float(w[j] >> 16)));
+      }
+    }
+    uint4 o;
+    o.x = uint32_t(float_to_bf16_bits(acc[0])) | (uint32_t(float_to_bf16_bits(acc[1])) << 16);
+    o.y = uint32_t(float_to_bf16_bits(acc[2])) | (uint32_t(float_to_bf16_bits(acc[3])) << 16);
+    o.z = uint32_t(float_to_bf16_bits(acc[4])) | (uint32_t(float_to_bf16_bits(acc[5])) << 16);
+    o.w = uint32_t(float_to_bf16_bits(acc[6])) | (uint32_t(float_to_bf16_bits(acc[7])) << 16);
+    *reinterpret_cast<uint4*>(output + i8) = o;
+  } else {
+    for (int64_t i = i8; i < elements; ++i) {
+      float acc = 0.f;
+      for (int src = 0; src < world; ++src) {
+        const uint16_t* p = src == rank ? local : remote + int64_t(src < rank ? src : src - 1) * elements;
+        acc = bf16_bits_to_float(float_to_bf16_bits(acc + bf16_bits_to_float(p[i])));
+      }
+      output[i] = float_to_bf16_bits(acc);
+    }
+  }
+}
+
+// Test probe: hardware E4M3 conversion of an fp32 array (one code per value).
+__global__ void e4m3_probe_kernel(const float* __restrict__ in, uint8_t* __restrict__ codes,
+                                  float* __restrict__ decoded, int64_t n) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint16_t pair = e4m3x2(in[i], 0.0f);
+  codes[i] = uint8_t(pair & 0xff);
+  decoded[i] = e4m3_to_float(i < 256 ? uint32_t(i) : uint32_t(pair & 0xff));
+}
+
+}  // namespace taco
+}  // namespace tdb
+
+using namespace tdb;
+
+static bool valid_elements(int64_t n) { return n > 0 && n % taco::kGroup == 0 && n / taco::kGroup <= 0x7fffffffLL; }
+
+static bool overlaps(const void* a, int64_t abytes, const void* b, int64_t bbytes) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+  return a0 < b0 + uintptr_t(bbytes) && b0 < a0 + uintptr_t(abytes);
+}
+
+TDB_API int tdb_taco_encode(const void* input, void* packet, int64_t elements, void* stream) {
+  if (!input || !packet || !valid_elements(elements))
+    return tdb_host::fail(int(cudaErrorInvalidValue), "encode: bad pointers or element count");
+  if (overlaps(input, elements * 2, packet, elements / 128 * 136))
+    return tdb_host::fail(int(cudaErrorInvalidValue), "encode: input and packet overlap");
+  if (reinterpret_cast<uintptr_t>(input) % 8 || reinterpret_cast<uintptr_t>(packet) % 4)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "encode: misaligned buffers");
+  const int64_t groups = elements / taco::kGroup;
+  const int64_t blocks = (groups + taco::kWarpsPerBlock - 1) / taco::kWarpsPerBlock;
+  taco::encode_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(input), static_cast<uint8_t*>(packet), groups);
+  return int(cudaGetLastError());
+}
+
+TDB_API int tdb_taco_decode(const void* packet, void* output, int64_t elements, void* stream) {
+  if (!packet || !output || !valid_elements(elements))
+    return tdb_host::fail(int(cudaErrorInvalidValue), "decode: bad pointers or element count");
+  if (overlaps(output, elements * 2, packet, elements / 128 * 136))
+    return tdb_host::fail(int(cudaErrorInvalidValue), "decode: packet and output overlap");
+  if (reinterpret_cast<uintptr_t>(output) % 8 || reinterpret_cast<uintptr_t>(packet) % 4)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "decode: misaligned buffers");
+  const int64_t groups = elements / taco::kGroup;
+  const int64_t blocks = (groups + taco::kWarpsPerBlock - 1) / taco::kWarpsPerBlock;
+  taco::decode_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(packet), static_cast<uint16_t*>(output), groups);
+  return int(cudaGetLastError());
+}
+
+TDB_API int tdb_taco_reduce(const void* local, const void* remote, void* output, int64_t elements, int rank,
+                            int world, void* stream) {
+  if (!local || !remote || !output || elements <= 0 || world < 2 || world > 128 || rank < 0 || rank >= world)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "reduce: bad arguments");
+  if (overlaps(remote, elements * 2 * (world - 1), output, elements * 2))
+    return tdb_host::fail(int(cudaErrorInvalidValue), "reduce: remote and output overlap");
+  if ((reinterpret_cast<uintptr_t>(local) | reinterpret_cast<uintptr_t>(remote) |
+       reinterpret_cast<uintptr_t>(output)) % 16 || (elements % 8 && world > 1 && (elements * 2) % 16))
+    return tdb_host::fail(int(cudaErrorInvalidValue), "reduce: buffers must be 16-byte aligned");
+  const int64_t threads = (elements + 7) / 8;
+  const int64_t blocks = (threads + 255) / 256;
+  taco::reduce_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(local), static_cast<const uint16_t*>(remote), static_cast<uint16_t*>(output),
+      elements, rank, world);
+  return int(cudaGetLastError());
+}
+
+TDB_API int tdb_e4m3_probe(const float* in, uint8_t* codes, float* decoded, int64_t n, void* stream) {
+  if (!in || !codes || !decoded || n <= 0) return tdb_host::fail(int(cudaErrorInvalidValue), "probe: bad args");
+  taco::e4m3_probe_kernel<<<unsigned((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(in, codes,
+                                                                                                   decoded, n);
+  return int(cudaGetLastError());
+}

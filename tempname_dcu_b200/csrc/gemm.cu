@@ -1,0 +1,264 @@
+// Plain (single-GPU) tcgen05 GEMM entry point with fused epilogues.
+//
+// Reference parity: the reference runs every linear layer through
+// torch.mm / F.linear (python/flux_dcu/model.py:116,123-124,139-141 and the
+// operator chunk GEMM python/flux_dcu/runtime.py:195).  Here those GEMMs are
+// one persistent tcgen05 kernel; bias, exact-erf GELU (model.py:261), GELU
+// backward, residual adds and fp32 weight-gradient accumulation
+// (model.py:401-408) are fused into the epilogue instead of separate kernels.
+#include "gemm.cuh"
+#include "tensor_map.h"
+
+namespace tdb {
+namespace gemm {
+
+enum EpiMode : int {
+  kStore = 0,         // C(bf16) = alpha * acc
+  kBias = 1,          // C(bf16) = acc + bias[n]
+  kBiasGelu = 2,      // Z = bf16(acc + bias[n]) -> aux_out;  C(bf16) = gelu(Z)
+  kGeluBwd = 3,       // C(bf16) = acc * gelu'(aux[m,n])
+  kAccF32 = 4,        // C(fp32) = acc + beta * C
+  kBiasResidual = 5,  // C(bf16) = acc + bias[n] + aux[m,n]
+};
+
+struct EpiParams {
+  void* C;
+  int64_t ldc;
+  int M, N;
+  const uint16_t* bias;
+  const uint16_t* aux;
+  int64_t ld_aux;
+  uint16_t* aux_out;
+  float alpha, beta;
+};
+
+__device__ __forceinline__ void load_bf16x32(const uint16_t* p, float (&v)[32]) {
+  const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 w = q[i];
+    const uint32_t a[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[8 * i + 2 * j] = bf16_bits_to_float(a[j] & 0xffff);
+      v[8 * i + 2 * j + 1] = bf16_bits_to_float(a[j] >> 16);
+    }
+  }
+}
+
+__device__ __forceinline__ void store_bf16x32(uint16_t* p, const float (&v)[32]) {
+  uint4* q = reinterpret_cast<uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
+    w.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
+    w.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
+    w.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
+    q[i] = w;
+  }
+}
+
+template <int MODE>
+struct PlainEpi {
+  EpiParams p;
+
+  __device__ __forceinline__ void tile_begin(int, int) {}
+  __device__ __forceinline__ void tile_end(int, int, int, int) {}
+
+  __device__ __forceinline__ void chunk(int row, int col, const uint32_t (&r)[32]) {
+    if (row >= p.M || col >= p.N) return;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    const bool full = col + 32 <= p.N;
+    if (MODE == kAccF32) {
+      float* c = static_cast<float*>(p.C) + int64_t(row) * p.ldc + col;
+      if (full) {
+        float4* c4 = reinterpret_cast<float4*>(c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          if (p.beta != 0.f) {
+            const float4 old = c4[i];
+            o.x += p.beta * old.x; o.y += p.beta * old.y; o.z += p.beta * old.z; o.w += p.beta * old.w;
+          }
+          c4[i] = o;
+        }
+      } else {
+        _Pragma("unroll") for (int j = 0; j < 32; ++j) if (col + j < p.N) c[j] = v[j] + (p.beta != 0.f ? p.beta * c[j] : 0.f);
+      }
+      return;
+    }
+    if (MODE == kStore) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= p.alpha;
+    }
+    if (MODE == kBias || MODE == kBiasGelu || MODE == kBiasResidual) {
+      if (p.bias) {
+        if (full) {
+          float b[32];
+          load_bf16x32(p.bias + col, b);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += b[j];
+        } else {
+          _Pragma("unroll") for (int j = 0; j < 32; ++j) if (col + j < p.N) v[j] += bf16_bits_to_float(p.bias[col + j]);
+        }
+      }
+    }
+    if (MODE == kBiasResidual) {
+      const uint16_t* a = p.aux + int64_t(row) * p.ld_aux + col;
+      if (full) {
+        float res[32];
+        load_bf16x32(a, res);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += res[j];
+      } else {
+        _Pragma("unroll") for (int j = 0; j < 32; ++j) if (col + j < p.N) v[j] += bf16_bits_to_float(a[j]);
+      }
+    }
+    if (MODE == kBiasGelu) {
+      uint16_t* z = p.aux_out + int64_t(row) * p.ld_aux + col;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = bf16_bits_to_float(float_to_bf16_bits(v[j]));
+      if (full) {
+        store_bf16x32(z, v);
+      } else {
+        _Pragma("unroll") for (int j = 0; j < 32; ++j) if (col + j < p.N) z[j] = float_to_bf16_bits(v[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+    }
+    if (MODE == kGeluBwd) {
+      const uint16_t* a = p.aux + int64_t(row) * p.ld_aux + col;
+      if (full) {
+        float zz[32];
+        load_bf16x32(a, zz);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = bf16_bits_to_float(float_to_bf16_bits(v[j])) * gelu_erf_grad(zz[j]);
+      } else {
+        _Pragma("unroll") for (int j = 0; j < 32; ++j) if (col + j < p.N) v[j] = bf16_bits_to_float(float_to_bf16_bits(v[j])) * gelu_erf_grad(bf16_bits_to_float(a[j]));
+      }
+    }
+    uint16_t* c = static_cast<uint16_t*>(p.C) + int64_t(row) * p.ldc + col;
+    if (full) {
+      store_bf16x32(c, v);
+    } else {
+      _Pragma("unroll") for (int j = 0; j < 32; ++j) if (col + j < p.N) c[j] = float_to_bf16_bits(v[j]);
+    }
+  }
+};
+
+template <int BN, bool A_MN, bool B_MN, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int K,
+                TileOrder order, EpiParams ep, int* status) {
+  PlainEpi<MODE> epi{ep};
+  gemm_mainloop<BN, A_MN, B_MN>(&tmA, &tmB, K, order, epi, status);
+}
+
+template <int BN, bool A_MN, bool B_MN, int MODE>
+static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiParams& ep,
+                  cudaStream_t stream) {
+  using Cfg = Config<BN>;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, MODE>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return tdb_host::fail(int(e), "cudaFuncSetAttribute(gemm) failed");
+    attr_set[dev & 63] = true;
+  }
+  TileOrder order;
+  order.num_m = (M + BM - 1) / BM;
+  order.num_n = (N + BN - 1) / BN;
+  order.group_m = 16;
+  order.table = nullptr;
+  order.num_tiles = order.num_m * order.num_n;
+  const int grid = order.num_tiles < tdb_host::sm_count() ? order.num_tiles : tdb_host::sm_count();
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, K, order, ep, tdb_host::status_ptr());
+  return int(cudaGetLastError());
+}
+
+template <int BN, bool A_MN, bool B_MN>
+static int dispatch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                         const EpiParams& ep, cudaStream_t s) {
+  switch (mode) {
+    case kStore: return launch<BN, A_MN, B_MN, kStore>(ta, tb, M, N, K, ep, s);
+    case kBias: return launch<BN, A_MN, B_MN, kBias>(ta, tb, M, N, K, ep, s);
+    case kBiasGelu: return launch<BN, A_MN, B_MN, kBiasGelu>(ta, tb, M, N, K, ep, s);
+    case kGeluBwd: return launch<BN, A_MN, B_MN, kGeluBwd>(ta, tb, M, N, K, ep, s);
+    case kAccF32: return launch<BN, A_MN, B_MN, kAccF32>(ta, tb, M, N, K, ep, s);
+    case kBiasResidual: return launch<BN, A_MN, B_MN, kBiasResidual>(ta, tb, M, N, K, ep, s);
+  }
+  return tdb_host::fail(int(cudaErrorInvalidValue), "unknown epilogue mode %d", mode);
+}
+
+template <int BN>
+static int dispatch_major(int a_mn, int b_mn, int mode, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
+                          int K, const EpiParams& ep, cudaStream_t s) {
+  if (!a_mn && !b_mn) return dispatch_mode<BN, false, false>(mode, ta, tb, M, N, K, ep, s);
+  if (!a_mn && b_mn) return dispatch_mode<BN, false, true>(mode, ta, tb, M, N, K, ep, s);
+  if (a_mn && b_mn) return dispatch_mode<BN, true, true>(mode, ta, tb, M, N, K, ep, s);
+  return dispatch_mode<BN, true, false>(mode, ta, tb, M, N, K, ep, s);
+}
+
+// Builds the TMA map of one operand.  K-major: rows = mn extent, inner = K,
+// box {64, tile_mn}.  MN-major: rows = K, inner = mn extent, box {64, 64}.
+int make_operand_map(CUtensorMap* map, const void* ptr, bool mn_major, int mn, int K, int64_t ld, int tile_mn) {
+  if (!mn_major)
+    return tdb_host::make_tmap_2d(map, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(K), uint64_t(mn),
+                                  uint64_t(ld), BK, uint32_t(tile_mn), CU_TENSOR_MAP_SWIZZLE_128B);
+  return tdb_host::make_tmap_2d(map, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(mn), uint64_t(K),
+                                uint64_t(ld), 64, BK, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace gemm
+}  // namespace tdb
+
+using namespace tdb;
+using namespace tdb::gemm;
+
+// C = epilogue(A * B^T).  a_mn / b_mn select the storage of A ([M,K] vs [K,M])
+// and B ([N,K] vs [K,N]); lda / ldb are the row strides of that storage in
+// elements.  C is bf16 [M, ldc] except for mode 4 (fp32).  bn = 0 picks the
+// tile width automatically (256 unless that leaves SMs idle).
+TDB_API int tdb_gemm(const void* A, int a_mn, int64_t lda, const void* B, int b_mn, int64_t ldb, void* C,
+                     int64_t ldc, int M, int N, int K, int mode, const void* bias, const void* aux, int64_t ld_aux,
+                     void* aux_out, float alpha, float beta, int bn, void* stream) {
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: bad pointers or sizes");
+  if (K % 8 || (a_mn && M % 8) || (b_mn && N % 8) || N % 8 || ldc % 8)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: K, N, ldc (and M / N for MN-major) must be multiples of 8");
+  if ((mode == kBiasGelu && (!aux_out || ld_aux % 8)) || ((mode == kGeluBwd || mode == kBiasResidual) && (!aux || ld_aux % 8)))
+    return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: epilogue mode %d needs an aligned aux tensor", mode);
+  if (bias && (reinterpret_cast<uintptr_t>(bias) % 16))
+    return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: bias must be 16-byte aligned");
+  if (bn == 0) {
+    const int sms = tdb_host::sm_count();
+    const int tiles256 = ((M + 127) / 128) * ((N + 255) / 256);
+    bn = (tiles256 >= sms || N <= 128) ? 256 : 128;
+    if (N <= 128) bn = 128;
+  }
+  if (bn != 128 && bn != 256) return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: bn must be 128 or 256");
+  CUtensorMap ta, tb;
+  int rc = make_operand_map(&ta, A, a_mn, M, K, lda, BM);
+  if (rc) return rc;
+  rc = make_operand_map(&tb, B, b_mn, N, K, ldb, bn);
+  if (rc) return rc;
+  EpiParams ep;
+  ep.C = C;
+  ep.ldc = ldc;
+  ep.M = M;
+  ep.N = N;
+  ep.bias = static_cast<const uint16_t*>(bias);
+  ep.aux = static_cast<const uint16_t*>(aux);
+  ep.ld_aux = ld_aux;
+  ep.aux_out = static_cast<uint16_t*>(aux_out);
+  ep.alpha = alpha;
+  ep.beta = beta;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bn == 256) return dispatch_major<256>(a_mn, b_mn, mode, ta, tb, M, N, K, ep, s);
+  return dispatch_major<128>(a_mn, b_mn, mode, ta, tb, M, N, K, ep, s);
+}

@@ -1,0 +1,242 @@
+// Persistent warp-specialised tcgen05 GEMM mainloop for sm_100a.
+//
+//   D[M,N] = sum_k A[m,k] * B[n,k]        (fp32 accumulation in TMEM)
+//
+// A is "K-major" ([M,K] rows, K contiguous) or "MN-major" ([K,M] rows, M
+// contiguous); likewise B ([N,K] or [K,N]).  Those three storage cases cover
+// every linear layer of training: forward X*W^T (K,K), data gradient dY*W
+// (K,MN) and weight gradient dY^T*X (MN,MN) without any transpose kernel.
+//
+// Roles (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer (one elected lane) + TMEM allocator
+//   warp 1      MMA issuer: one thread issues tcgen05.mma.cta_group::1.kind::f16
+//   warps 2..5  epilogue: tcgen05.ld 32x32b from TMEM -> registers -> Epi
+// Pipelines:
+//   smem ring of STAGES (A,B) tiles, full[] (TMA tx) / empty[] (tcgen05.commit)
+//   two TMEM accumulators (2*BN columns), tmem_full[] / tmem_empty[]
+// Every mbarrier wait is bounded (common.cuh); on expiry the CTA abandons its
+// loops, drains in-flight copies / MMAs with bounded waits, frees TMEM and
+// returns with the status word set.  There is no TMA multicast.
+#pragma once
+#include "common.cuh"
+
+namespace tdb {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one 128B swizzle row
+constexpr int kThreads = 192;
+
+template <int BN>
+struct Config {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;  // two accumulators
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+// Output-tile order.  Grouped raster (GROUP_M m-blocks per band) for L2 reuse,
+// or an explicit device table of tile ids (used by the fused collective
+// kernels to impose the common tile-to-rank production order).
+struct TileOrder {
+  int num_m, num_n;
+  int group_m;
+  const int* table;  // optional: table[i] = m_blk * num_n + n_blk
+  int num_tiles;
+
+  __device__ __forceinline__ void tile(int i, int& m_blk, int& n_blk) const {
+    if (table) {
+      const int t = table[i];
+      m_blk = t / num_n;
+      n_blk = t % num_n;
+      return;
+    }
+    const int width = group_m * num_n;
+    const int group = i / width;
+    const int first = group * group_m;
+    const int gsize = min(num_m - first, group_m);
+    const int r = i % width;
+    m_blk = first + r % gsize;
+    n_blk = r / gsize;
+  }
+};
+
+struct alignas(8) Barriers {
+  uint64_t full[8];
+  uint64_t empty[8];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// Descriptor of a K-major SW128 tile: rows of 128 bytes, 8-row atoms of
+// 1024 bytes.  LBO is unused for swizzled K-major operands (encoded as 16).
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) { return smem_desc_sw128(saddr, 16, 1024); }
+
+// Descriptor of an MN-major SW128 tile stored as boxes of [64 K rows][64 MN
+// elements]: 8-row K groups are 1024 bytes apart (SBO), 64-element MN chunks
+// are one box (64*128 bytes) apart (LBO).
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr) {
+  return smem_desc_sw128(saddr, BK * 128, 1024);
+}
+
+template <int BN, bool A_MN, bool B_MN, class Epi>
+__device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUtensorMap* tmB, int K,
+                                              const TileOrder& order, Epi& epi, int* status) {
+  using Cfg = Config<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + S * Cfg::kStageBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->tmem_full[b], 1);
+      mbar_init(&bars->tmem_empty[b], 4);
+    }
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&bars->tmem_base, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(tmA);
+    prefetch_tmap(tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+  volatile int* abort_flag = &bars->abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int i = blockIdx.x; i < order.num_tiles && ok; i += gridDim.x) {
+        int mb, nb;
+        order.tile(i, mb, nb);
+        const int m0 = mb * BM, n0 = nb * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t round = it / S;
+          if (!mbar_wait(&bars->empty[s], (round & 1) ^ 1, status, 10)) { ok = false; *abort_flag = 1; break; }
+          if (*abort_flag) { ok = false; break; }
+          uint8_t* sa = smem + s * Cfg::kStageBytes;
+          uint8_t* sb = sa + Cfg::kABytes;
+          mbar_arrive_expect_tx(&bars->full[s], Cfg::kStageBytes);
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            tma_load_2d(sa, tmA, &bars->full[s], k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(sa + j * (BK * 128), tmA, &bars->full[s], m0 + 64 * j, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d(sb, tmB, &bars->full[s], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * (BK * 128), tmB, &bars->full[s], n0 + 64 * j, k0);
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: wait (bounded) for every stage that may still have bytes in flight.
+        for (uint32_t j = (it >= S ? it - S : 0); j < it; ++j)
+          mbar_wait(&bars->full[j % S], (j / S) & 1, status, 11);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(BM, BN, A_MN, B_MN);
+      uint32_t it = 0;
+      int tc = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int i = blockIdx.x; i < order.num_tiles && ok; i += gridDim.x, ++tc) {
+        const int b = tc & 1;
+        const uint32_t use = tc >> 1;
+        if (!mbar_wait(&bars->tmem_empty[b], (use & 1) ^ 1, status, 20)) { ok = false; *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t dcol = tmem_base + b * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t round = it / S;
+          if (!mbar_wait(&bars->full[s], round & 1, status, 21)) { ok = false; *abort_flag = 1; break; }
+          if (*abort_flag) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * Cfg::kStageBytes);
+          const uint32_t sb = sa + Cfg::kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? desc_mnmajor(sa + k * 16 * 128) : desc_kmajor(sa + k * 32);
+            const uint64_t bd = B_MN ? desc_mnmajor(sb + k * 16 * 128) : desc_kmajor(sb + k * 32);
+            umma_f16_ss(dcol, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit(&bars->empty[s]);
+        }
+        if (ok) umma_commit(&bars->tmem_full[b]);
+      }
+      // Make sure every MMA has landed before TMEM can be released.
+      if (issued) {
+        umma_commit(&bars->drain);
+        mbar_wait(&bars->drain, 0, status, 22);
+      }
+    }
+  } else {
+    // ---------------- Epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
+    const int row_in_tile = quarter * 32 + lane;
+    int tc = 0;
+    for (int i = blockIdx.x; i < order.num_tiles; i += gridDim.x, ++tc) {
+      int mb, nb;
+      order.tile(i, mb, nb);
+      const int b = tc & 1;
+      const uint32_t use = tc >> 1;
+      bool ok = mbar_wait(&bars->tmem_full[b], use & 1, status, 30);
+      if (*abort_flag) ok = false;
+      if (!ok) { *abort_flag = 1; break; }
+      tc_fence_after();
+      epi.tile_begin(mb, nb);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (uint32_t(quarter * 32) << 16) + b * BN + c * 32, r);
+        tmem_wait_ld();
+        if (c == BN / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->tmem_empty[b]);
+        }
+        epi.chunk(mb * BM + row_in_tile, nb * BN + c * 32, r);
+      }
+      epi.tile_end(mb, nb, quarter, lane);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+}  // namespace gemm
+}  // namespace tdb

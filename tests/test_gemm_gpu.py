@@ -1,0 +1,99 @@
+"""tcgen05 GEMM (csrc/gemm.cu) against a plain fp32 PyTorch reference."""
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    import torch
+    return (torch.linalg.vector_norm(a.float() - b.float()) / torch.linalg.vector_norm(b.float()).clamp_min(1e-30)).item()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (300, 264, 200), (1024, 1536, 512),
+                                   (2048, 4096, 1024)])
+def test_linear_kk(cuda, M, N, K):
+    import torch
+    from tempname_dcu_b200.ops import gemm as g
+    torch.manual_seed(0)
+    x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    w = torch.randn(N, K, device=cuda).to(torch.bfloat16)
+    y = g.linear(x, w)
+    ref = x.float() @ w.float().t()
+    assert _rel(y, ref) < 5e-3
+    g_status = __import__("tempname_dcu_b200.ops.native", fromlist=["x"]).read_status()
+    assert g_status[0] == 0
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_both_tile_widths(cuda, bn):
+    import torch
+    from tempname_dcu_b200.ops import gemm as g
+    torch.manual_seed(1)
+    x = torch.randn(512, 256, device=cuda).to(torch.bfloat16)
+    w = torch.randn(768, 256, device=cuda).to(torch.bfloat16)
+    y = g.gemm(x, w, bn=bn)
+    assert _rel(y, x.float() @ w.float().t()) < 5e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (384, 640, 192), (2048, 1024, 512)])
+def test_data_gradient_b_mn_major(cuda, M, N, K):
+    import torch
+    from tempname_dcu_b200.ops import gemm as g
+    torch.manual_seed(2)
+    dy = torch.randn(M, N, device=cuda).to(torch.bfloat16)
+    w = torch.randn(N, K, device=cuda).to(torch.bfloat16)
+    dx = g.matmul_nt(dy, w)
+    assert _rel(dx, dy.float() @ w.float()) < 5e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (512, 384, 320), (2048, 512, 768)])
+def test_weight_gradient_mn_mn_accumulate(cuda, M, N, K):
+    import torch
+    from tempname_dcu_b200.ops import gemm as g
+    torch.manual_seed(3)
+    dy = torch.randn(M, N, device=cuda).to(torch.bfloat16)
+    x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    acc = torch.randn(N, K, device=cuda)
+    base = acc.clone()
+    g.weight_grad(dy, x, acc, accumulate=True)
+    ref = base + dy.float().t() @ x.float()
+    assert _rel(acc, ref) < 2e-3
+    fresh = g.weight_grad(dy, x)
+    assert _rel(fresh, dy.float().t() @ x.float()) < 2e-3
+
+
+def test_fused_epilogues(cuda):
+    import torch
+    import torch.nn.functional as F
+    from tempname_dcu_b200.ops import gemm as g
+    torch.manual_seed(4)
+    M, N, K = 384, 512, 256
+    x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda) / 16).to(torch.bfloat16)
+    b = torch.randn(N, device=cuda).to(torch.bfloat16)
+    res = torch.randn(M, N, device=cuda).to(torch.bfloat16)
+    z_ref = x.float() @ w.float().t() + b.float()
+    y = g.linear(x, w, b)
+    assert _rel(y, z_ref) < 5e-3
+    act, pre = g.linear_gelu(x, w, b)
+    assert _rel(pre, z_ref) < 5e-3
+    assert _rel(act, F.gelu(pre.float())) < 5e-3
+    out = g.linear_residual(x, w, b, res)
+    assert _rel(out, z_ref + res.float()) < 5e-3
+    # GELU backward: dz = (dy @ w2) * gelu'(pre)
+    dy = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    w2 = (torch.randn(K, N, device=cuda) / 16).to(torch.bfloat16)
+    dz = g.matmul_nt(dy, w2, gelu_pre=pre)
+    pre_f = pre.float().requires_grad_(True)
+    F.gelu(pre_f).backward((dy.float() @ w2.float()))
+    assert _rel(dz, pre_f.grad) < 1e-2
+
+
+def test_large_k_and_many_tiles(cuda):
+    import torch
+    from tempname_dcu_b200.ops import gemm as g
+    torch.manual_seed(5)
+    x = torch.randn(1024, 4096, device=cuda).to(torch.bfloat16)
+    w = torch.randn(4096, 4096, device=cuda).to(torch.bfloat16)
+    y = g.linear(x, w)
+    assert _rel(y, x.float() @ w.float().t()) < 5e-3
