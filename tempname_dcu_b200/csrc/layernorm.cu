@@ -1,0 +1,220 @@
+// LayerNorm forward / backward for the pre-LN transformer (hidden <= 8192).
+//
+// Reference parity: python/flux_dcu/model.py:229-233 (F.layer_norm with
+// weight, bias and eps 1e-5 on the sequence-parallel residual rows).
+//
+// Forward: one CTA per row, each thread owns VPT contiguous elements
+// (VPT/8 16-byte loads); two-pass mean/variance from registers; saves
+// mean and rstd (fp32) for the backward.
+// Backward: each CTA handles ROWS rows; dx (optionally plus an incoming
+// residual gradient) is written directly, and dgamma/dbeta are accumulated in
+// registers and written as per-CTA partials; a second kernel sums the
+// partials in fixed CTA order into the fp32 gradient accumulators, so the
+// result is bitwise deterministic (no floating-point atomics).
+#include "common.cuh"
+
+namespace tdb {
+namespace ln {
+
+template <int VPT>
+__device__ __forceinline__ void load_row(const uint16_t* p, float (&v)[VPT]) {
+#pragma unroll
+  for (int i = 0; i < VPT / 8; ++i) {
+    const uint4 w = reinterpret_cast<const uint4*>(p)[i];
+    const uint32_t a[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[8 * i + 2 * j] = bf16_bits_to_float(a[j] & 0xffff);
+      v[8 * i + 2 * j + 1] = bf16_bits_to_float(a[j] >> 16);
+    }
+  }
+}
+
+template <int VPT>
+__device__ __forceinline__ void store_row(uint16_t* p, const float (&v)[VPT]) {
+#pragma unroll
+  for (int i = 0; i < VPT / 8; ++i) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * i], v[8 * i + 1]);
+    w.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
+    w.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
+    w.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
+    reinterpret_cast<uint4*>(p)[i] = w;
+  }
+}
+
+// Block-wide sum (blockDim.x <= 1024, multiple of 32).
+__device__ __forceinline__ float block_sum(float v, float* scratch) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += scratch[i];
+  return t;
+}
+
+template <int VPT>
+__global__ void ln_fwd_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma,
+                              const uint16_t* __restrict__ beta, uint16_t* __restrict__ y, float* __restrict__ mean_out,
+                              float* __restrict__ rstd_out, int H, float eps) {
+  __shared__ float scratch[32];
+  const int64_t row = blockIdx.x;
+  const int c0 = threadIdx.x * VPT;
+  float v[VPT];
+  load_row<VPT>(x + row * H + c0, v);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) s += v[i];
+  const float mean = block_sum(s, scratch) / float(H);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const float d = v[i] - mean;
+    q += d * d;
+  }
+  const float var = block_sum(q, scratch) / float(H);
+  const float rstd = rsqrtf(var + eps);
+  float g[VPT], b[VPT];
+  load_row<VPT>(gamma + c0, g);
+  load_row<VPT>(beta + c0, b);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) v[i] = (v[i] - mean) * rstd * g[i] + b[i];
+  store_row<VPT>(y + row * H + c0, v);
+  if (threadIdx.x == 0) {
+    mean_out[row] = mean;
+    rstd_out[row] = rstd;
+  }
+}
+
+constexpr int kBwdRows = 16;
+
+template <int VPT>
+__global__ void ln_bwd_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma,
+                              const float* __restrict__ mean_in, const float* __restrict__ rstd_in,
+                              const uint16_t* __restrict__ dy, const uint16_t* __restrict__ dres,
+                              uint16_t* __restrict__ dx, float* __restrict__ partial, int rows, int H) {
+  __shared__ float scratch[32];
+  const int c0 = threadIdx.x * VPT;
+  float g[VPT], dg[VPT], db[VPT];
+  load_row<VPT>(gamma + c0, g);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) dg[i] = db[i] = 0.f;
+  const int first = blockIdx.x * kBwdRows;
+  for (int r = first; r < first + kBwdRows && r < rows; ++r) {
+    float xv[VPT], gy[VPT];
+    load_row<VPT>(x + int64_t(r) * H + c0, xv);
+    load_row<VPT>(dy + int64_t(r) * H + c0, gy);
+    const float mean = mean_in[r], rstd = rstd_in[r];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const float xh = (xv[i] - mean) * rstd;
+      xv[i] = xh;
+      dg[i] += gy[i] * xh;
+      db[i] += gy[i];
+      const float d = gy[i] * g[i];
+      gy[i] = d;
+      s1 += d;
+      s2 += d * xh;
+    }
+    const float c2 = block_sum(s1, scratch) / float(H);
+    const float c1 = block_sum(s2, scratch) / float(H);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) gy[i] = (gy[i] - xv[i] * c1 - c2) * rstd;
+    if (dres) {
+      float rr[VPT];
+      load_row<VPT>(dres + int64_t(r) * H + c0, rr);
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) gy[i] += rr[i];
+    }
+    store_row<VPT>(dx + int64_t(r) * H + c0, gy);
+  }
+  float* pg = partial + int64_t(blockIdx.x) * 2 * H;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    pg[c0 + i] = dg[i];
+    pg[H + c0 + i] = db[i];
+  }
+}
+
+// Sum the per-CTA partials in CTA order and add into the fp32 accumulators.
+__global__ void ln_reduce_partials(const float* __restrict__ partial, int nparts, int H, float* __restrict__ dgamma,
+                                   float* __restrict__ dbeta, int accumulate) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= 2 * H) return;
+  float s = 0.f;
+  for (int p = 0; p < nparts; ++p) s += partial[int64_t(p) * 2 * H + c];
+  float* dst = c < H ? dgamma + c : dbeta + (c - H);
+  *dst = accumulate ? *dst + s : s;
+}
+
+template <int VPT>
+static int fwd_launch(const void* x, const void* g, const void* b, void* y, float* mean, float* rstd, int rows, int H,
+                      float eps, cudaStream_t s) {
+  ln_fwd_kernel<VPT><<<rows, H / VPT, 0, s>>>(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(g),
+                                              static_cast<const uint16_t*>(b), static_cast<uint16_t*>(y), mean, rstd,
+                                              H, eps);
+  return int(cudaGetLastError());
+}
+
+template <int VPT>
+static int bwd_launch(const void* x, const void* g, const float* mean, const float* rstd, const void* dy,
+                      const void* dres, void* dx, float* partial, int rows, int H, cudaStream_t s) {
+  const int blocks = (rows + kBwdRows - 1) / kBwdRows;
+  ln_bwd_kernel<VPT><<<blocks, H / VPT, 0, s>>>(
+      static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(g), mean, rstd, static_cast<const uint16_t*>(dy),
+      static_cast<const uint16_t*>(dres), static_cast<uint16_t*>(dx), partial, rows, H);
+  return int(cudaGetLastError());
+}
+
+static int pick_vpt(int H) {
+  // threads = H / VPT must be a multiple of 32 and <= 1024
+  for (int vpt : {32, 16, 8, 64}) {
+    if (H % vpt == 0 && (H / vpt) % 32 == 0 && H / vpt <= 1024) return vpt;
+  }
+  return 0;
+}
+
+}  // namespace ln
+}  // namespace tdb
+
+using namespace tdb::ln;
+
+TDB_API int tdb_layernorm_fwd(const void* x, const void* gamma, const void* beta, void* y, float* mean, float* rstd,
+                              int rows, int H, float eps, void* stream) {
+  const int vpt = pick_vpt(H);
+  if (!vpt || rows <= 0) return tdb_host::fail(int(cudaErrorInvalidValue), "layernorm: unsupported hidden size %d", H);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (vpt) {
+    case 8: return fwd_launch<8>(x, gamma, beta, y, mean, rstd, rows, H, eps, s);
+    case 16: return fwd_launch<16>(x, gamma, beta, y, mean, rstd, rows, H, eps, s);
+    case 32: return fwd_launch<32>(x, gamma, beta, y, mean, rstd, rows, H, eps, s);
+    default: return fwd_launch<64>(x, gamma, beta, y, mean, rstd, rows, H, eps, s);
+  }
+}
+
+// Scratch: `partial` holds ceil(rows/16) * 2 * H floats.
+TDB_API int tdb_layernorm_bwd_scratch_floats(int rows, int H) { return ((rows + kBwdRows - 1) / kBwdRows) * 2 * H; }
+
+TDB_API int tdb_layernorm_bwd(const void* x, const void* gamma, const float* mean, const float* rstd, const void* dy,
+                              const void* dres, void* dx, float* dgamma, float* dbeta, float* partial, int rows, int H,
+                              int accumulate, void* stream) {
+  const int vpt = pick_vpt(H);
+  if (!vpt || rows <= 0 || !partial)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "layernorm bwd: unsupported hidden size %d", H);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc;
+  switch (vpt) {
+    case 8: rc = bwd_launch<8>(x, gamma, mean, rstd, dy, dres, dx, partial, rows, H, s); break;
+    case 16: rc = bwd_launch<16>(x, gamma, mean, rstd, dy, dres, dx, partial, rows, H, s); break;
+    case 32: rc = bwd_launch<32>(x, gamma, mean, rstd, dy, dres, dx, partial, rows, H, s); break;
+    default: rc = bwd_launch<64>(x, gamma, mean, rstd, dy, dres, dx, partial, rows, H, s); break;
+  }
+  if (rc) return rc;
+  const int nparts = (rows + kBwdRows - 1) / kBwdRows;
+  ln_reduce_partials<<<(2 * H + 255) / 256, 256, 0, s>>>(partial, nparts, H, dgamma, dbeta, accumulate);
+  return int(cudaGetLastError());
+}

@@ -1,0 +1,141 @@
+// Fused optimizer-side kernels over flat parameter buffers:
+//   * deterministic sum of squares (fp64 per-block partials, ordered finish)
+//   * clip coefficient min(1, max_norm / (sqrt(total) + 1e-6)) on the device
+//   * fused AdamW with fp32 masters: decoupled weight decay on the matrix
+//     ranges only, Adam moments, bf16 parameter write-back and gradient reset
+//     in one pass, reading the clip coefficient from device memory (no host
+//     synchronisation inside the step).
+//
+// Reference parity: python/flux_dcu/model.py:279-292 (global_grad_norm with
+// replicated parameters counted once), :381-388 (AdamW betas (0.9, 0.95),
+// eps 1e-8, wd on ndim >= 2 only, fp32 masters) and :410-420 (clip, step,
+// copy masters into the bf16 model parameters).
+#include "common.cuh"
+
+namespace tdb {
+namespace optim {
+
+constexpr int kThreads = 256;
+constexpr int kBlocksMax = 1184;  // 8 per SM on 148 SMs
+
+__global__ void sumsq_partial_kernel(const float* __restrict__ g, int64_t n, double* __restrict__ partial) {
+  __shared__ double sh[kThreads];
+  double s = 0.0;
+  const int64_t n4 = n / 4;
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  for (int64_t i = int64_t(blockIdx.x) * kThreads + threadIdx.x; i < n4; i += int64_t(gridDim.x) * kThreads) {
+    const float4 v = g4[i];
+    // squares of the fp32 values, accumulated in fp64
+    s += double(v.x) * v.x + double(v.y) * v.y + double(v.z) * v.z + double(v.w) * v.w;
+  }
+  for (int64_t i = n4 * 4 + int64_t(blockIdx.x) * kThreads + threadIdx.x; i < n; i += int64_t(gridDim.x) * kThreads)
+    s += double(g[i]) * g[i];
+  sh[threadIdx.x] = s;
+  __syncthreads();
+  for (int st = kThreads / 2; st; st >>= 1) {
+    if (threadIdx.x < st) sh[threadIdx.x] += sh[threadIdx.x + st];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) partial[blockIdx.x] = sh[0];
+}
+
+__global__ void sumsq_finish_kernel(const double* __restrict__ partial, int nparts, double* __restrict__ out,
+                                    int accumulate) {
+  if (threadIdx.x || blockIdx.x) return;
+  double s = 0.0;
+  for (int i = 0; i < nparts; ++i) s += partial[i];
+  *out = accumulate ? *out + s : s;
+}
+
+// norm_out = sqrt(total); coef = min(1, max_norm / (norm + 1e-6)); finite
+// flag cleared when the norm or the loss is not finite.
+__global__ void clip_kernel(const double* __restrict__ total, float max_norm, double* __restrict__ norm_out,
+                            float* __restrict__ coef, const float* __restrict__ loss, int* __restrict__ finite) {
+  const double norm = sqrt(*total);
+  *norm_out = norm;
+  const float c = float(double(max_norm) / (norm + 1e-6));
+  *coef = c < 1.f ? c : 1.f;
+  const bool ok = isfinite(norm) && (loss == nullptr || isfinite(*loss));
+  if (!ok) *finite = 0;
+}
+
+struct WdRanges {
+  int64_t lo0, hi0, lo1, hi1;
+  __device__ __forceinline__ bool has_wd(int64_t i) const { return (i >= lo0 && i < hi0) || (i >= lo1 && i < hi1); }
+};
+
+__global__ void adamw_kernel(float* __restrict__ master, float* __restrict__ grad, float* __restrict__ m,
+                             float* __restrict__ v, uint16_t* __restrict__ param, int64_t n, WdRanges wd, float lr,
+                             float beta1, float beta2, float eps, float weight_decay, float bc1, float bc2_sqrt,
+                             const float* __restrict__ coef_ptr, const int* __restrict__ finite, int zero_grad) {
+  if (finite && *finite == 0) return;  // non-finite step: leave state untouched
+  const float coef = coef_ptr ? *coef_ptr : 1.f;
+  const float step = lr / bc1;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    float p = master[i];
+    const float g = grad[i] * coef;
+    if (wd.has_wd(i)) p *= 1.f - lr * weight_decay;
+    const float mi = beta1 * m[i] + (1.f - beta1) * g;
+    const float vi = beta2 * v[i] + (1.f - beta2) * g * g;
+    m[i] = mi;
+    v[i] = vi;
+    const float denom = sqrtf(vi) / bc2_sqrt + eps;
+    p -= step * (mi / denom);
+    master[i] = p;
+    param[i] = float_to_bf16_bits(p);
+    if (zero_grad) grad[i] = 0.f;
+  }
+}
+
+// fp32 -> bf16 copy (initial parameter materialisation).
+__global__ void to_bf16_kernel(const float* __restrict__ src, uint16_t* __restrict__ dst, int64_t n) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    dst[i] = float_to_bf16_bits(src[i]);
+}
+
+static int grid_for(int64_t n) {
+  int64_t b = (n + kThreads - 1) / kThreads;
+  return int(b < kBlocksMax ? (b > 0 ? b : 1) : kBlocksMax);
+}
+
+}  // namespace optim
+}  // namespace tdb
+
+using namespace tdb::optim;
+
+TDB_API int tdb_sumsq_partials_count() { return kBlocksMax; }
+
+// out (+)= sum(g^2) in fp64; `partial` must hold tdb_sumsq_partials_count() doubles.
+TDB_API int tdb_sumsq(const float* g, int64_t n, double* partial, double* out, int accumulate, void* stream) {
+  if (n < 0 || (reinterpret_cast<uintptr_t>(g) % 16)) return tdb_host::fail(int(cudaErrorInvalidValue), "sumsq: bad args");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(n / 4 + 1);
+  sumsq_partial_kernel<<<grid, kThreads, 0, s>>>(g, n, partial);
+  sumsq_finish_kernel<<<1, 32, 0, s>>>(partial, grid, out, accumulate);
+  return int(cudaGetLastError());
+}
+
+TDB_API int tdb_clip_coef(const double* total, float max_norm, double* norm_out, float* coef, const float* loss,
+                          int* finite, void* stream) {
+  clip_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(total, max_norm, norm_out, coef, loss, finite);
+  return int(cudaGetLastError());
+}
+
+TDB_API int tdb_adamw(float* master, float* grad, float* m, float* v, void* param, int64_t n, int64_t wd_lo0,
+                      int64_t wd_hi0, int64_t wd_lo1, int64_t wd_hi1, float lr, float beta1, float beta2, float eps,
+                      float weight_decay, int step, const float* coef, const int* finite, int zero_grad,
+                      void* stream) {
+  if (step < 1 || n <= 0) return tdb_host::fail(int(cudaErrorInvalidValue), "adamw: bad step/size");
+  const float bc1 = 1.f - powf(beta1, float(step));
+  const float bc2_sqrt = sqrtf(1.f - powf(beta2, float(step)));
+  WdRanges wd{wd_lo0, wd_hi0, wd_lo1, wd_hi1};
+  adamw_kernel<<<grid_for(n), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      master, grad, m, v, static_cast<uint16_t*>(param), n, wd, lr, beta1, beta2, eps, weight_decay, bc1, bc2_sqrt,
+      coef, finite, zero_grad);
+  return int(cudaGetLastError());
+}
+
+TDB_API int tdb_to_bf16(const float* src, void* dst, int64_t n, void* stream) {
+  to_bf16_kernel<<<grid_for(n), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(src, static_cast<uint16_t*>(dst), n);
+  return int(cudaGetLastError());
+}

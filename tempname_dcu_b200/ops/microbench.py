@@ -1,0 +1,150 @@
+"""Kernel microbenchmarks with CUDA-event timing.
+
+    python -m tempname_dcu_b200.ops.microbench gemm [--shapes M,N,K:...] [--iters 20]
+    python -m tempname_dcu_b200.ops.microbench ncu-gemm M N K [--mode fwd|dgrad|wgrad]
+
+Each measurement: warm-up launches, then ``iters`` timed launches, each
+preceded by a write of a 256 MB buffer (larger than the 126 MB L2) so that
+operands come from HBM; CUDA events on the launching stream bracket only the
+kernel.  Results are TFLOP/s and the fraction of the measured cuBLAS bf16
+peak recorded in MEASURED_PEAKS.json (when present).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+# GPT-6.7B linear-layer shapes per micro-batch (M = 2048 tokens) at TP=1.
+DEFAULT_SHAPES = [
+    ("qkv.fwd", 2048, 12288, 4096, "fwd"),
+    ("attn_out.fwd", 2048, 4096, 4096, "fwd"),
+    ("fc1.fwd", 2048, 16384, 4096, "fwd"),
+    ("fc2.fwd", 2048, 4096, 16384, "fwd"),
+    ("lm_head.fwd", 2048, 50304, 4096, "fwd"),
+    ("fc1.dgrad", 2048, 4096, 16384, "dgrad"),
+    ("fc2.dgrad", 2048, 16384, 4096, "dgrad"),
+    ("fc1.wgrad", 16384, 4096, 2048, "wgrad"),
+    ("fc2.wgrad", 4096, 16384, 2048, "wgrad"),
+    ("qkv.tp8.fwd", 2048, 1536, 4096, "fwd"),
+    ("attn_out.tp8.fwd", 2048, 4096, 512, "fwd"),
+]
+
+
+def _peaks():
+    path = Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+    if path.is_file():
+        data = json.loads(path.read_text())
+        return data.get("bf16_tflops", 1590.0), data.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def _operands(torch, M, N, K, kind, device):
+    g = torch.Generator(device=device).manual_seed(0)
+    if kind == "fwd":      # x[M,K] @ w[N,K]^T
+        a = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+        b = torch.randn(N, K, device=device, generator=g).to(torch.bfloat16)
+    elif kind == "dgrad":  # dy[M,K'] @ w[K',N] where the GEMM is M x N x K
+        a = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+        b = torch.randn(K, N, device=device, generator=g).to(torch.bfloat16)
+    else:                  # dw[M,N] = dy[K,M]^T @ x[K,N]
+        a = torch.randn(K, M, device=device, generator=g).to(torch.bfloat16)
+        b = torch.randn(K, N, device=device, generator=g).to(torch.bfloat16)
+    return a, b
+
+
+def _ours(gemm, a, b, kind, out):
+    if kind == "fwd":
+        return lambda: gemm.gemm(a, b, out=out)
+    if kind == "dgrad":
+        return lambda: gemm.gemm(a, b, b_mn=True, out=out)
+    return lambda: gemm.gemm(a, b, a_mn=True, b_mn=True, out=out, mode=gemm.ACC_F32, beta=0.0)
+
+
+def _cublas(torch, a, b, kind, out):
+    if kind == "fwd":
+        return lambda: torch.matmul(a, b.t(), out=out)
+    if kind == "dgrad":
+        return lambda: torch.matmul(a, b, out=out)
+    return lambda: torch.matmul(a.t(), b, out=out)
+
+
+def time_fn(torch, fn, iters, warmup=3, flush=None):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        if flush is not None:
+            flush.add_(1)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        fn()
+        end.record()
+        torch.cuda.synchronize()
+        times.append(start.elapsed_time(end))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def bench_gemm(shapes, iters):
+    import torch
+    from . import gemm, native
+    device = torch.device("cuda", 0)
+    peak, _, source = _peaks()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+    rows = []
+    for name, M, N, K, kind in shapes:
+        a, b = _operands(torch, M, N, K, kind, device)
+        out_dtype = torch.float32 if kind == "wgrad" else torch.bfloat16
+        out = torch.empty(M, N, dtype=out_dtype, device=device)
+        ref_out = torch.empty(M, N, dtype=torch.bfloat16, device=device)
+        ours = time_fn(torch, _ours(gemm, a, b, kind, out), iters, flush=flush)
+        theirs = time_fn(torch, _cublas(torch, a, b, kind, ref_out), iters, flush=flush)
+        ref = _cublas(torch, a.float(), b.float(), kind, None)()
+        err = ((out.float() - ref).norm() / ref.norm()).item()
+        flops = 2.0 * M * N * K
+        rows.append(dict(name=name, M=M, N=N, K=K, kind=kind, ours_ms=ours, cublas_ms=theirs,
+                         ours_tflops=flops / ours / 1e9, cublas_tflops=flops / theirs / 1e9,
+                         frac_of_peak=flops / ours / 1e9 / peak, speedup_vs_cublas=theirs / ours,
+                         rel_err=err, peak_source=source))
+        print(json.dumps(rows[-1]), flush=True)
+    native.raise_on_status()
+    return rows
+
+
+def main(argv=None):
+    parser = argparse.ArgumentParser()
+    sub = parser.add_subparsers(dest="cmd", required=True)
+    p = sub.add_parser("gemm")
+    p.add_argument("--shapes", default="")
+    p.add_argument("--iters", type=int, default=20)
+    q = sub.add_parser("ncu-gemm", help="a few launches of one GEMM shape (for ncu captures)")
+    q.add_argument("M", type=int)
+    q.add_argument("N", type=int)
+    q.add_argument("K", type=int)
+    q.add_argument("--mode", default="fwd", choices=("fwd", "dgrad", "wgrad"))
+    q.add_argument("--launches", type=int, default=3)
+    args = parser.parse_args(argv)
+    if args.cmd == "gemm":
+        shapes = DEFAULT_SHAPES
+        if args.shapes:
+            shapes = []
+            for item in args.shapes.split(":"):
+                M, N, K, *kind = item.split(",")
+                shapes.append((item, int(M), int(N), int(K), kind[0] if kind else "fwd"))
+        bench_gemm(shapes, args.iters)
+    else:
+        import torch
+        from . import gemm
+        a, b = _operands(torch, args.M, args.N, args.K, args.mode, torch.device("cuda", 0))
+        out = torch.empty(args.M, args.N, dtype=torch.float32 if args.mode == "wgrad" else torch.bfloat16,
+                          device="cuda")
+        fn = _ours(gemm, a, b, args.mode, out)
+        for _ in range(args.launches):
+            fn()
+        torch.cuda.synchronize()
+
+
+if __name__ == "__main__":
+    main()
