@@ -582,6 +582,7 @@ TDB_API int tdb_attn_fwd(const void* qkv, int64_t ld, void* out, int64_t ld_out,
   dim3 grid((seq + FWD_BM - 1) / FWD_BM, Hl, mb);
   fwd_kernel<<<grid, FWD_THREADS, kFwdSmem, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(qkv), ld, static_cast<uint16_t*>(out), ld_out, lse, seq, Hl, scale);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
@@ -604,12 +605,15 @@ TDB_API int tdb_attn_bwd(const void* qkv, int64_t ld, const void* out, int64_t l
   const int64_t warps = int64_t(rows) * Hl;
   bwd_pre_kernel<<<unsigned((warps * 32 + 255) / 256), 256, 0, s>>>(
       static_cast<const uint16_t*>(out), ld_out, static_cast<const uint16_t*>(dout), ld_dout, dsum, seq, Hl, rows);
+  tdb_host::launched(1);
   dim3 grid((seq + BWD_B - 1) / BWD_B, Hl, mb);
   bwd_dkdv_kernel<<<grid, BWD_THREADS, kDkdvSmem, s>>>(static_cast<const uint16_t*>(qkv), ld,
                                                        static_cast<const uint16_t*>(dout), ld_dout, lse, dsum,
                                                        static_cast<uint16_t*>(dqkv), ld_dqkv, seq, Hl, scale);
+  tdb_host::launched(1);
   bwd_dq_kernel<<<grid, BWD_THREADS, kDqSmem, s>>>(static_cast<const uint16_t*>(qkv), ld,
                                                    static_cast<const uint16_t*>(dout), ld_dout, lse, dsum,
                                                    static_cast<uint16_t*>(dqkv), ld_dqkv, seq, Hl, scale);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }

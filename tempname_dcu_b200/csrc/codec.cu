@@ -120,6 +120,7 @@ TDB_API int tdb_taco_encode(const void* input, void* packet, int64_t elements, v
   const int64_t blocks = (groups + taco::kWarpsPerBlock - 1) / taco::kWarpsPerBlock;
   taco::encode_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(input), static_cast<uint8_t*>(packet), groups);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
@@ -134,6 +135,7 @@ TDB_API int tdb_taco_decode(const void* packet, void* output, int64_t elements, 
   const int64_t blocks = (groups + taco::kWarpsPerBlock - 1) / taco::kWarpsPerBlock;
   taco::decode_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(packet), static_cast<uint16_t*>(output), groups);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
@@ -151,6 +153,7 @@ TDB_API int tdb_taco_reduce(const void* local, const void* remote, void* output,
   taco::reduce_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(local), static_cast<const uint16_t*>(remote), static_cast<uint16_t*>(output),
       elements, rank, world);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
@@ -158,5 +161,6 @@ TDB_API int tdb_e4m3_probe(const float* in, uint8_t* codes, float* decoded, int6
   if (!in || !codes || !decoded || n <= 0) return tdb_host::fail(int(cudaErrorInvalidValue), "probe: bad args");
   taco::e4m3_probe_kernel<<<unsigned((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(in, codes,
                                                                                                    decoded, n);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }

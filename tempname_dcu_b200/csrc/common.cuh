@@ -259,6 +259,8 @@ namespace tdb_host {
 // Thread-local last error text for the C ABI.
 void set_error(const char* fmt, ...);
 int fail(int code, const char* fmt, ...);
+// Count kernels launched by the library (read with tdb_launch_count).
+void launched(int n);
 // Device address of the status word on the current device (cached per device).
 int* status_ptr();
 // SM count of the current device (cached).

@@ -76,6 +76,7 @@ TDB_API int tdb_bias_residual(const void* x, const void* bias, const void* res, 
   bias_residual_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(bias), static_cast<const uint16_t*>(res),
       static_cast<uint16_t*>(out), rows, cols);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
@@ -88,6 +89,8 @@ TDB_API int tdb_colsum(const void* x, int64_t ld, int rows, int cols, float* par
   const int nparts = (rows + kColRows - 1) / kColRows;
   dim3 grid((cols / 2 + 255) / 256, nparts);
   colsum_partial_kernel<<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), ld, rows, cols, partial);
+  tdb_host::launched(1);
   colsum_finish_kernel<<<(cols + 255) / 256, 256, 0, s>>>(partial, nparts, cols, out, accumulate);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }

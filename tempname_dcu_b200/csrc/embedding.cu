@@ -123,6 +123,7 @@ TDB_API int tdb_embedding_fwd(const int64_t* tokens, const void* table, int64_t 
   fwd_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(tokens, static_cast<const uint16_t*>(table), start,
                                                                   local_vocab, static_cast<const uint16_t*>(pos),
                                                                   pos_offset, seq, H, static_cast<uint16_t*>(out));
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
@@ -130,6 +131,7 @@ TDB_API int tdb_add_positions(void* x, const void* pos, int64_t offset, int seq,
   if (H % 8 || rows <= 0) return tdb_host::fail(int(cudaErrorInvalidValue), "positions: H must be a multiple of 8");
   add_pos_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint16_t*>(x),
                                                                       static_cast<const uint16_t*>(pos), offset, seq, H);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
@@ -137,6 +139,7 @@ TDB_API int tdb_embedding_bwd(const int64_t* sorted_tokens, const int64_t* sorte
                               int64_t start, int64_t local_vocab, int H, float* grad, void* stream) {
   bwd_table_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       sorted_tokens, sorted_rows, rows, static_cast<const uint16_t*>(dy), start, local_vocab, H, grad);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
@@ -144,5 +147,6 @@ TDB_API int tdb_position_bwd(const void* dy, int rows, int64_t offset, int seq, 
                              void* stream) {
   bwd_pos_kernel<<<seq, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint16_t*>(dy), rows, offset,
                                                                       seq, H, grad_pos);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }

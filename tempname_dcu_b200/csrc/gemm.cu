@@ -178,6 +178,7 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, in
   order.num_tiles = order.num_m * order.num_n;
   const int grid = order.num_tiles < tdb_host::sm_count() ? order.num_tiles : tdb_host::sm_count();
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, K, order, ep, tdb_host::status_ptr());
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 

@@ -157,6 +157,7 @@ static int fwd_launch(const void* x, const void* g, const void* b, void* y, floa
   ln_fwd_kernel<VPT><<<rows, H / VPT, 0, s>>>(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(g),
                                               static_cast<const uint16_t*>(b), static_cast<uint16_t*>(y), mean, rstd,
                                               H, eps);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
@@ -167,6 +168,7 @@ static int bwd_launch(const void* x, const void* g, const float* mean, const flo
   ln_bwd_kernel<VPT><<<blocks, H / VPT, 0, s>>>(
       static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(g), mean, rstd, static_cast<const uint16_t*>(dy),
       static_cast<const uint16_t*>(dres), static_cast<uint16_t*>(dx), partial, rows, H);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
@@ -216,5 +218,6 @@ TDB_API int tdb_layernorm_bwd(const void* x, const void* gamma, const float* mea
   if (rc) return rc;
   const int nparts = (rows + kBwdRows - 1) / kBwdRows;
   ln_reduce_partials<<<(2 * H + 255) / 256, 256, 0, s>>>(partial, nparts, H, dgamma, dbeta, accumulate);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }

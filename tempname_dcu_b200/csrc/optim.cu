@@ -111,13 +111,16 @@ TDB_API int tdb_sumsq(const float* g, int64_t n, double* partial, double* out, i
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int grid = grid_for(n / 4 + 1);
   sumsq_partial_kernel<<<grid, kThreads, 0, s>>>(g, n, partial);
+  tdb_host::launched(1);
   sumsq_finish_kernel<<<1, 32, 0, s>>>(partial, grid, out, accumulate);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
 TDB_API int tdb_clip_coef(const double* total, float max_norm, double* norm_out, float* coef, const float* loss,
                           int* finite, void* stream) {
   clip_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(total, max_norm, norm_out, coef, loss, finite);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
@@ -132,10 +135,12 @@ TDB_API int tdb_adamw(float* master, float* grad, float* m, float* v, void* para
   adamw_kernel<<<grid_for(n), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       master, grad, m, v, static_cast<uint16_t*>(param), n, wd, lr, beta1, beta2, eps, weight_decay, bc1, bc2_sqrt,
       coef, finite, zero_grad);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
 TDB_API int tdb_to_bf16(const float* src, void* dst, int64_t n, void* stream) {
   to_bf16_kernel<<<grid_for(n), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(src, static_cast<uint16_t*>(dst), n);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }

@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -35,6 +36,9 @@ int fail(int code, const char* fmt, ...) {
   va_end(ap);
   return code;
 }
+
+static std::atomic<long long> g_launches{0};
+void launched(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 int* status_ptr() {
   static int* cache[64] = {nullptr};
@@ -106,6 +110,9 @@ static constexpr int kAbiVersion = 3;
 
 TDB_API int tdb_abi_version() { return kAbiVersion; }
 
+// Number of kernels launched through this library since load (host counter).
+TDB_API long long tdb_launch_count() { return tdb_host::g_launches.load(); }
+
 TDB_API const char* tdb_last_error() { return tdb_host::g_error; }
 
 TDB_API const char* tdb_error_string(int code) { return cudaGetErrorString(static_cast<cudaError_t>(code)); }
@@ -133,6 +140,7 @@ __global__ void tdb_delay_kernel(unsigned long long cycles) {
 TDB_API int tdb_diagnostic_delay(unsigned long long cycles, void* stream) {
   if (cycles == 0 || cycles > 100000000ull) return tdb_host::fail(int(cudaErrorInvalidValue), "delay cycles out of range");
   tdb_delay_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(cycles);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 

@@ -153,6 +153,7 @@ TDB_API int tdb_xent_stats(const void* logits, int64_t ld, const int64_t* target
     return tdb_host::fail(int(cudaErrorInvalidValue), "xent: columns and ld must be multiples of 8");
   stats_kernel<<<rows, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(logits), ld, targets, vocab_start, valid_cols, cols, stats);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }
 
@@ -160,7 +161,11 @@ TDB_API int tdb_xent_combine(const float* all_stats, int world, int rows, float*
                              float* loss_out, float loss_scale, int accumulate, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   combine_kernel<<<(rows + 255) / 256, 256, 0, s>>>(all_stats, world, rows, gstats, row_loss);
-  if (loss_out) loss_sum_kernel<<<1, 1024, 0, s>>>(row_loss, rows, loss_scale, loss_out, accumulate);
+  tdb_host::launched(1);
+  if (loss_out) {
+    loss_sum_kernel<<<1, 1024, 0, s>>>(row_loss, rows, loss_scale, loss_out, accumulate);
+    tdb_host::launched(1);
+  }
   return int(cudaGetLastError());
 }
 
@@ -169,5 +174,6 @@ TDB_API int tdb_xent_grad(void* logits, int64_t ld, const int64_t* targets, int6
   if (cols % 8 || ld % 8) return tdb_host::fail(int(cudaErrorInvalidValue), "xent grad: bad alignment");
   grad_kernel<<<rows, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint16_t*>(logits), ld, targets,
                                                                         vocab_start, valid_cols, cols, gstats, scale);
+  tdb_host::launched(1);
   return int(cudaGetLastError());
 }

@@ -1,0 +1,301 @@
+"""Sequence/tensor-parallel GPT on the sm_100a kernels.
+
+The training micro-step is an explicit forward/backward schedule over the
+native kernels (no per-op autograd graph):
+
+forward, per layer (x: SP rows [m/W, h])::
+
+    ln1 = LN(x); ln1f = AG(ln1); qkv = ln1f Wqkv^T + b       (column-parallel)
+    a = causal_flash_attention(qkv)                           (local heads)
+    x1 = x + RS(a Wo^T) + bo                                  (row-parallel, operator)
+    ln2 = LN(x1); ln2f = AG(ln2); z = ln2f W1^T + b1; h = gelu(z)
+    x2 = x1 + RS(h W2^T) + b2                                 (row-parallel, operator)
+
+backward mirrors it: data gradients through the transposed GEMMs (the
+collective order reversed), weight gradients accumulated directly into the
+fp32 gradient buffer by the GEMM epilogue, bias gradients by deterministic
+column sums, GELU backward fused into the FC2 data-gradient epilogue.
+The LM head is the tied vocabulary-sharded embedding; the vocab-parallel
+cross-entropy writes its gradient over the logits in place, so the backward
+starts inside the loss.
+
+Everything is deterministic (no floating-point atomics), so arms that only
+reorder production produce bitwise-identical losses, norms and weights.
+
+Reference parity: python/flux_dcu/model.py:178-292 (GPT, SumScatter,
+ColumnLinear, RowLinear, VocabCrossEntropy, replicated-gradient all-reduce,
+global grad norm) and :339-476 (train_window).
+"""
+from __future__ import annotations
+
+import math
+
+from .config import HEAD_DIM, native_shape_ok, validate_config
+from .params import FlatParams, gpt_param_specs
+
+ARMS = ("flux", "flux_taco", "flux_taco_interleaved", "flux_taco_interleaved_arrival",
+        "flux_taco_interleaved_arrival_selective")
+
+
+class NcclRowOperator:
+    """Row-parallel output projection without fusion: GEMM, NCCL
+    reduce-scatter, bias + residual.  (With one rank: one fused GEMM.)"""
+
+    calls = 0
+
+    def __init__(self, tp):
+        self.tp = tp
+
+    def forward(self, a_full, weight, bias, residual):
+        from ..ops import gemm as G
+        from ..ops import kernels as K
+        self.calls += 1
+        if self.tp.world == 1:
+            return G.linear_residual(a_full, weight, bias, residual)
+        partial = G.linear(a_full, weight)
+        out = self.tp.scatter_sum(partial)
+        return K.bias_residual(out, bias, residual, out=out)
+
+    def state(self):
+        return dict(backend="nccl-reduce-scatter", calls=self.calls)
+
+
+class GPT:
+    """One rank's shard of the TP/SP GPT with flat parameter storage."""
+
+    def __init__(self, config, arm="flux", group=None, *, device="cuda", seed=1234, operator_factory=None,
+                 execution_plan=None, materialize=True):
+        import torch
+        from ..parallel.tp import TPGroup
+        self.tp = TPGroup(group)
+        self.world, self.rank = self.tp.world, self.tp.rank
+        self.config = c = validate_config(config, self.world)
+        if not native_shape_ok(c, self.world):
+            raise ValueError("the sm_100a kernels need head_dim 128 and 8-aligned shard widths")
+        if arm not in ARMS and arm != "nccl":
+            raise ValueError(f"unknown arm {arm}")
+        self.arm = arm
+        self.device = torch.device(device)
+        self.seed = seed
+        self.h, self.f = c["hidden"], c["ffn"]
+        self.heads_local = c["heads"] // self.world
+        self.m = c["sequence"] * c["micro_batch"]
+        self.ml = self.m // self.world
+        self.vocab_local = c["padded_vocab"] // self.world
+        self.vocab_start = self.rank * self.vocab_local
+        self.valid_vocab_local = max(0, min(self.vocab_local, c["vocab"] - self.vocab_start))
+        self.params = FlatParams(gpt_param_specs(c, self.world), self.device, rank=self.rank, seed=seed,
+                                 materialize=materialize)
+        self.forward_calls = 0
+        self.operators = []
+        factory = operator_factory
+        for index in range(c["layers"]):
+            for role, k in (("attn", self.h // self.world), ("mlp", self.f // self.world)):
+                if factory is None:
+                    self.operators.append(NcclRowOperator(self.tp))
+                else:
+                    plan = execution_plan["roles"][role] if execution_plan else None
+                    self.operators.append(factory(m=self.m, n=self.h, k=k, group=group, arm=arm,
+                                                  chunk_rows=c["chunk_rows"], plan=plan))
+        self._scratch = {}
+
+    # ------------------------------------------------------------ helpers
+    def _buf(self, key, numel, dtype):
+        import torch
+        t = self._scratch.get(key)
+        if t is None or t.numel() < numel or t.dtype != dtype:
+            t = torch.empty(numel, dtype=dtype, device=self.device)
+            self._scratch[key] = t
+        return t[:numel]
+
+    def P(self, name):
+        return self.params.p(name)
+
+    def Gr(self, name):
+        return self.params.g(name)
+
+    # ------------------------------------------------------------ forward
+    def _embed(self, tokens):
+        import torch
+        from ..ops import kernels as K
+        c = self.config
+        out = torch.empty((self.m, self.h), dtype=torch.bfloat16, device=self.device)
+        if self.world == 1:
+            K.embedding_fwd(tokens, self.P("embedding"), 0, out, self.P("position"), 0, c["sequence"])
+            return out
+        K.embedding_fwd(tokens, self.P("embedding"), self.vocab_start, out)
+        x = self.tp.scatter_sum(out)
+        K.add_positions(x, self.P("position"), self.rank * self.ml, c["sequence"])
+        return x
+
+    def _layer_fwd(self, i, x):
+        from ..ops import gemm as G
+        from ..ops import kernels as K
+        c, p = self.config, f"layers.{i}."
+        eps = c["layer_norm_epsilon"]
+        ln1, mean1, rstd1 = K.layernorm_fwd(x, self.P(p + "ln1_weight"), self.P(p + "ln1_bias"), eps)
+        ln1f = self.tp.gather(ln1)
+        qkv = G.linear(ln1f, self.P(p + "qkv_weight"), self.P(p + "qkv_bias"))
+        attn, lse = K.attention_fwd(qkv, c["micro_batch"], c["sequence"], self.heads_local)
+        x1 = self.operators[2 * i].forward(attn, self.P(p + "attn_weight"), self.P(p + "attn_bias"), x)
+        ln2, mean2, rstd2 = K.layernorm_fwd(x1, self.P(p + "ln2_weight"), self.P(p + "ln2_bias"), eps)
+        ln2f = self.tp.gather(ln2)
+        h1, z = G.linear_gelu(ln2f, self.P(p + "fc1_weight"), self.P(p + "fc1_bias"))
+        x2 = self.operators[2 * i + 1].forward(h1, self.P(p + "fc2_weight"), self.P(p + "fc2_bias"), x1)
+        return x2, (x, mean1, rstd1, ln1f, qkv, attn, lse, x1, mean2, rstd2, ln2f, z, h1)
+
+    def forward_backward(self, tokens, targets, loss_acc=None, *, grad_scale=None, loss_scale=None):
+        """One micro-batch: forward, loss (added into ``loss_acc``) and the
+        full backward, accumulating fp32 gradients.  ``tokens``/``targets``
+        are the flattened micro-batch [micro_batch*sequence] (int64, device)."""
+        import torch
+        from ..ops import gemm as G
+        from ..ops import kernels as K
+        c = self.config
+        if tokens.shape != (self.m,) or targets.shape != (self.m,):
+            raise ValueError("tokens/targets must hold the full flattened micro-batch")
+        accum = c["accumulation_steps"]
+        grad_scale = 1.0 / (self.m * accum) if grad_scale is None else grad_scale
+        loss_scale = 1.0 / (self.m * accum) if loss_scale is None else loss_scale
+        if loss_acc is None:
+            loss_acc = torch.zeros((), dtype=torch.float32, device=self.device)
+        self.forward_calls += 1
+        # ---- forward
+        x = self._embed(tokens)
+        saved = []
+        for i in range(c["layers"]):
+            x, s = self._layer_fwd(i, x)
+            saved.append(s)
+        xl = x
+        eps = c["layer_norm_epsilon"]
+        lnf, meanf, rstdf = K.layernorm_fwd(xl, self.P("final_weight"), self.P("final_bias"), eps)
+        lnff = self.tp.gather(lnf)
+        logits = G.linear(lnff, self.P("embedding"))  # [m, V/W]
+        stats = K.xent_stats(logits, targets, self.vocab_start, self.valid_vocab_local)
+        all_stats = self.tp.all_gather_stacked(stats)
+        gstats = self._buf("gstats", self.m * 2, torch.float32).view(self.m, 2)
+        row_loss = self._buf("row_loss", self.m, torch.float32)
+        K.xent_combine(all_stats, self.world, self.m, gstats, row_loss, loss_acc, loss_scale, accumulate=True)
+        # ---- backward (starts inside the loss: logits <- dlogits)
+        K.xent_grad(logits, targets, self.vocab_start, self.valid_vocab_local, gstats, grad_scale)
+        dlnff = G.matmul_nt(logits, self.P("embedding"))
+        G.weight_grad(logits, lnff, self.Gr("embedding"))
+        del logits
+        dlnf = self.tp.scatter_sum(dlnff)
+        ln_scratch = self._buf("ln_scratch", K.layernorm_scratch_floats(self.ml, self.h), torch.float32)
+        dx = K.layernorm_bwd(xl, self.P("final_weight"), meanf, rstdf, dlnf, self.Gr("final_weight"),
+                             self.Gr("final_bias"), ln_scratch)
+        for i in reversed(range(c["layers"])):
+            dx = self._layer_bwd(i, dx, saved[i], ln_scratch)
+            saved[i] = None
+        # ---- embedding / positions
+        K.position_bwd(dx, self.rank * self.ml if self.world > 1 else 0, c["sequence"], self.Gr("position"))
+        dfull = self.tp.gather(dx)
+        sorted_tokens, order = torch.sort(tokens, stable=True)
+        K.embedding_bwd(sorted_tokens, order, dfull, self.vocab_start, self.vocab_local, self.Gr("embedding"))
+        return loss_acc
+
+    def _colsum(self, x, name):
+        import torch
+        from ..ops import kernels as K
+        scratch = self._buf("colsum", K.colsum_scratch_floats(x.shape[0], x.shape[1]), torch.float32)
+        K.colsum(x, self.Gr(name), scratch, accumulate=True)
+
+    def _layer_bwd(self, i, dx2, saved, ln_scratch):
+        from ..ops import gemm as G
+        from ..ops import kernels as K
+        c, p = self.config, f"layers.{i}."
+        x, mean1, rstd1, ln1f, qkv, attn, lse, x1, mean2, rstd2, ln2f, z, h1 = saved
+        # FC2 (row-parallel): x2 = x1 + RS(h1 W2^T) + b2
+        self._colsum(dx2, p + "fc2_bias")
+        dyf = self.tp.gather(dx2)
+        dz = G.matmul_nt(dyf, self.P(p + "fc2_weight"), gelu_pre=z)
+        G.weight_grad(dyf, h1, self.Gr(p + "fc2_weight"))
+        # FC1 (column-parallel)
+        self._colsum(dz, p + "fc1_bias")
+        dln2f = G.matmul_nt(dz, self.P(p + "fc1_weight"))
+        G.weight_grad(dz, ln2f, self.Gr(p + "fc1_weight"))
+        dln2 = self.tp.scatter_sum(dln2f)
+        dx1 = K.layernorm_bwd(x1, self.P(p + "ln2_weight"), mean2, rstd2, dln2, self.Gr(p + "ln2_weight"),
+                              self.Gr(p + "ln2_bias"), ln_scratch, dres=dx2)
+        # attention out (row-parallel)
+        self._colsum(dx1, p + "attn_bias")
+        dyf = self.tp.gather(dx1)
+        dattn = G.matmul_nt(dyf, self.P(p + "attn_weight"))
+        G.weight_grad(dyf, attn, self.Gr(p + "attn_weight"))
+        dqkv = K.attention_bwd(qkv, attn, dattn, lse, c["micro_batch"], c["sequence"], self.heads_local)
+        # QKV (column-parallel)
+        self._colsum(dqkv, p + "qkv_bias")
+        dln1f = G.matmul_nt(dqkv, self.P(p + "qkv_weight"))
+        G.weight_grad(dqkv, ln1f, self.Gr(p + "qkv_weight"))
+        dln1 = self.tp.scatter_sum(dln1f)
+        return K.layernorm_bwd(x, self.P(p + "ln1_weight"), mean1, rstd1, dln1, self.Gr(p + "ln1_weight"),
+                               self.Gr(p + "ln1_bias"), ln_scratch, dres=dx1)
+
+    # ------------------------------------------------------------ gradients
+    def reduce_replicated_gradients(self):
+        lo, hi = self.params.replicated_range
+        if self.world > 1 and hi > lo:
+            self.tp.all_reduce_(self.params.grad[lo:hi])
+
+    def global_grad_norm_sq(self, out):
+        """fp64 sum of squares over this rank's sharded gradients plus (rank 0
+        only) the replicated ones, all-reduced over the group."""
+        import torch
+        from ..ops import kernels as K
+        partial = self._buf("sumsq_partial", K.sumsq_partials_count(), torch.float64)
+        lo, hi = self.params.sharded_range
+        K.sumsq(self.params.grad[lo:hi], partial, out, accumulate=False)
+        if self.rank == 0:
+            rlo, rhi = self.params.replicated_range
+            K.sumsq(self.params.grad[rlo:rhi], partial, out, accumulate=True)
+        self.tp.all_reduce_(out)
+        return out
+
+    def named_parameters(self):
+        return self.params.named_parameters()
+
+    def parameter_count(self):
+        return self.params.numel_logical()
+
+
+class Optimizer:
+    """Fused AdamW over the flat buffers with global-norm clipping computed on
+    the device (betas (0.9, 0.95), eps 1e-8, decoupled decay on matrices)."""
+
+    def __init__(self, model, lr, weight_decay, max_grad_norm, betas=(0.9, 0.95), eps=1e-8):
+        import torch
+        self.model, self.lr, self.wd, self.max_norm = model, lr, weight_decay, max_grad_norm
+        self.betas, self.eps = betas, eps
+        self.step_count = 0
+        dev = model.device
+        self.norm_sq = torch.zeros((), dtype=torch.float64, device=dev)
+        self.norm = torch.zeros((), dtype=torch.float64, device=dev)
+        self.coef = torch.ones((), dtype=torch.float32, device=dev)
+        self.finite = torch.ones((), dtype=torch.int32, device=dev)
+
+    def step(self, loss=None):
+        from ..ops import kernels as K
+        m = self.model
+        m.reduce_replicated_gradients()
+        m.global_grad_norm_sq(self.norm_sq)
+        self.finite.fill_(1)
+        K.clip_coef(self.norm_sq, self.max_norm, self.norm, self.coef, loss, self.finite)
+        self.step_count += 1
+        P = m.params
+        K.adamw(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.param, wd_ranges=P.decay_ranges, lr=self.lr,
+                beta1=self.betas[0], beta2=self.betas[1], eps=self.eps, weight_decay=self.wd,
+                step=self.step_count, coef=self.coef, finite=self.finite, zero_grad=True)
+        return self.norm
+
+
+def build_model(config, arm="flux", group=None, codec=None, *, device="cuda", seed=1234, operator_factory=None,
+                execution_plan=None):
+    """Build one rank's model.  ``operator_factory(m, n, k, group, arm,
+    chunk_rows, plan)`` builds the row-parallel operators (the fused
+    GEMM+reduce-scatter of ``runtime.FluxB200`` for the five arms); None
+    uses plain NCCL."""
+    if arm in ARMS[3:] and operator_factory is not None and execution_plan is None:
+        raise ValueError("arrival/selective arms need a frozen execution plan")
+    return GPT(config, arm, group, device=device, seed=seed, operator_factory=operator_factory,
+               execution_plan=execution_plan)

@@ -23,6 +23,7 @@ c_void_p, c_int, c_int64, c_float, c_uint64 = ctypes.c_void_p, ctypes.c_int, cty
 # name -> argtypes (all return c_int status unless listed in _RESTYPE)
 SIGNATURES = {
     "tdb_abi_version": [],
+    "tdb_launch_count": [],
     "tdb_last_error": [],
     "tdb_error_string": [c_int],
     "tdb_read_status": [c_void_p],
@@ -34,7 +35,8 @@ SIGNATURES = {
     "tdb_taco_reduce": [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p],
     "tdb_e4m3_probe": [c_void_p, c_void_p, c_void_p, c_int64, c_void_p],
 }
-_RESTYPE = {"tdb_last_error": ctypes.c_char_p, "tdb_error_string": ctypes.c_char_p}
+_RESTYPE = {"tdb_last_error": ctypes.c_char_p, "tdb_error_string": ctypes.c_char_p,
+            "tdb_launch_count": ctypes.c_longlong}
 
 _LOCK = threading.Lock()
 _LIB = None
@@ -120,3 +122,8 @@ def raise_on_status() -> None:
         clear_status()
         raise NativeError(f"device status {code} ({STATUS_NAMES.get(code, 'unknown')}) at site {where} "
                           f"detail=({d0},{d1})")
+
+
+def launch_count() -> int:
+    """Kernels launched through libtdb.so in this process so far."""
+    return int(lib().tdb_launch_count())

@@ -1,0 +1,149 @@
+"""Training loop: the public training API of the framework.
+
+``Trainer(config, arm, group, ...)`` owns one rank's model and optimizer;
+``Trainer.step(tokens, targets)`` runs one optimizer step over
+``accumulation_steps`` micro-batches and returns the step's (loss, grad norm)
+as device scalars.  Token tensors may live in pinned host memory: each
+micro-batch is copied to the device asynchronously inside the step.
+
+``train_window`` reproduces the reference's timed window record (warm-up
+steps, timed steps, losses, grad norms, parameter digests, memory peaks,
+operator counters): python/flux_dcu/model.py:339-476, with device-side
+timing (CUDA events, max over ranks) instead of host wall clock.
+"""
+from __future__ import annotations
+
+import hashlib
+
+from .models.config import parameter_counts, validate_config
+from .models.gpt import GPT, Optimizer
+
+
+def tensor_digest(named_tensors):
+    """sha256 over (name, shape, dtype, raw bytes) of each tensor, in order."""
+    import torch
+    digest = hashlib.sha256()
+    for name, tensor in named_tensors:
+        value = tensor.detach().cpu().contiguous()
+        digest.update(name.encode())
+        digest.update(str(tuple(value.shape)).encode())
+        digest.update(str(value.dtype).encode())
+        digest.update(value.view(torch.uint8).numpy().tobytes())
+    return digest.hexdigest()
+
+
+def synthetic_batches(config, steps=1, seed=4321, pin=True):
+    """Uniform random tokens in [0, vocab): a list of (tokens, labels) of
+    shape [accumulation_steps, micro_batch*sequence] per step (CPU, pinned)."""
+    import torch
+    c = validate_config(config, 1)
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    out = []
+    for _ in range(steps):
+        stream = torch.randint(0, c["vocab"], (c["accumulation_steps"], c["micro_batch"], c["sequence"] + 1),
+                               generator=gen)
+        tokens = stream[:, :, :-1].reshape(c["accumulation_steps"], -1).contiguous()
+        labels = stream[:, :, 1:].reshape(c["accumulation_steps"], -1).contiguous()
+        if pin and torch.cuda.is_available():
+            tokens, labels = tokens.pin_memory(), labels.pin_memory()
+        out.append((tokens, labels))
+    return out
+
+
+class Trainer:
+    def __init__(self, config, arm="flux", group=None, *, device="cuda", seed=1234, operator_factory=None,
+                 execution_plan=None):
+        import torch
+        self.model = GPT(config, arm, group, device=device, seed=seed, operator_factory=operator_factory,
+                         execution_plan=execution_plan)
+        c = self.config = self.model.config
+        self.optimizer = Optimizer(self.model, c["learning_rate"], c["weight_decay"], c["max_grad_norm"])
+        self.device = self.model.device
+        self.loss = torch.zeros((), dtype=torch.float32, device=self.device)
+        accum, m = c["accumulation_steps"], self.model.m
+        self._tokens = torch.empty((accum, m), dtype=torch.int64, device=self.device)
+        self._labels = torch.empty((accum, m), dtype=torch.int64, device=self.device)
+
+    def step(self, tokens, labels):
+        """One optimizer step over ``accumulation_steps`` micro-batches.
+
+        tokens/labels: int64 [accumulation_steps, micro_batch*sequence] on the
+        host (pinned, copied asynchronously here) or on the device."""
+        c = self.config
+        if tokens.device.type != "cuda":
+            self._tokens.copy_(tokens, non_blocking=True)
+            self._labels.copy_(labels, non_blocking=True)
+            tokens, labels = self._tokens, self._labels
+        self.loss.zero_()
+        for micro in range(c["accumulation_steps"]):
+            self.model.forward_backward(tokens[micro], labels[micro], self.loss)
+        norm = self.optimizer.step(self.loss)
+        return self.loss, norm
+
+
+def train_window(config, arm, group, warmup_steps, timed_steps, *, seed=1234, token_seed=4321, operator_factory=None,
+                 execution_plan=None):
+    """Train a fresh model for warm-up + timed steps; returns the reference
+    window record plus device-timed ``elapsed_seconds`` (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    for name, value in (("warmup_steps", warmup_steps), ("timed_steps", timed_steps)):
+        if type(value) is not int or value < 1:
+            raise ValueError(f"invalid {name}")
+    trainer = Trainer(config, arm, group, seed=seed, operator_factory=operator_factory,
+                      execution_plan=execution_plan)
+    model = trainer.model
+    c = trainer.config
+    world = model.world
+    counts = parameter_counts(c, world)
+    actual = model.parameter_count()
+    if actual != counts["parameters_per_rank"]:
+        raise RuntimeError("actual parameter count differs from the configuration")
+    initial = tensor_digest(model.named_parameters())
+    (tokens, labels), = synthetic_batches(c, 1, token_seed)
+    input_hash = tensor_digest([(f"tokens.{i}", tokens[i]) for i in range(len(tokens))] +
+                               [(f"labels.{i}", labels[i]) for i in range(len(labels))])
+    tokens, labels = tokens.to(trainer.device), labels.to(trainer.device)
+    for _ in range(warmup_steps):
+        trainer.step(tokens, labels)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(group=group)
+    torch.cuda.reset_peak_memory_stats()
+    calls_before = model.forward_calls
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    losses, norms = [], []
+    start.record()
+    for _ in range(timed_steps):
+        loss, norm = trainer.step(tokens, labels)
+        losses.append(loss.clone())
+        norms.append(norm.clone())
+    end.record()
+    torch.cuda.synchronize()
+    local = start.elapsed_time(end) / 1000.0
+    elapsed = torch.tensor(local, dtype=torch.float64, device=trainer.device)
+    if world > 1:
+        dist.all_reduce(elapsed, op=dist.ReduceOp.MAX, group=group)
+    forwards = model.forward_calls - calls_before
+    if forwards != timed_steps * c["accumulation_steps"]:
+        raise RuntimeError("wrong formal forward count")
+    return dict(elapsed_seconds=float(elapsed.item()), local_elapsed_seconds=local, timed_steps=timed_steps,
+                warmup_steps=warmup_steps, losses=[float(x.item()) for x in losses],
+                grad_norms=[float(x.item()) for x in norms],
+                tokens_per_step=c["sequence"] * c["micro_batch"] * c["accumulation_steps"],
+                initialization_sha256=initial, input_sha256=input_hash,
+                final_parameters_sha256=tensor_digest(model.named_parameters()),
+                actual_model_config={k: v for k, v in c.items()}, parameter_counts=counts,
+                actual_parameters_per_rank=actual, dtype="bfloat16", optimizer="AdamW-fp32-master",
+                deterministic_algorithms=True,
+                gradient_policy="fp32 gradient accumulation in the GEMM epilogue; replicated gradients summed; "
+                                "replicated norm counted once",
+                optimizer_weight_decay_policy="matrix parameters only; biases and LayerNorm vectors excluded",
+                model_implementation="tempname_dcu_b200-tp-sp-gpt-sm100a-v1",
+                attention_implementation="hand-written causal flash attention (sm_100a)",
+                timing="CUDA events on the compute stream, max over ranks", rank=model.rank,
+                operator_counters=dict(model_forwards=forwards, target_modules=2 * c["layers"],
+                                       actual_calls_per_instance=[getattr(op, "calls", 0) for op in model.operators]),
+                operator_states=[op.state() for op in model.operators if hasattr(op, "state")],
+                memory=dict(peak_allocated_bytes=torch.cuda.max_memory_allocated(),
+                            peak_reserved_bytes=torch.cuda.max_memory_reserved()))
