@@ -11,6 +11,8 @@
 // registers and written as per-CTA partials; a second kernel sums the
 // partials in fixed CTA order into the fp32 gradient accumulators, so the
 // result is bitwise deterministic (no floating-point atomics).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace tdb {
@@ -218,6 +220,91 @@ TDB_API int tdb_layernorm_bwd(const void* x, const void* gamma, const float* mea
   if (rc) return rc;
   const int nparts = (rows + kBwdRows - 1) / kBwdRows;
   ln_reduce_partials<<<(2 * H + 255) / 256, 256, 0, s>>>(partial, nparts, H, dgamma, dbeta, accumulate);
+  tdb_host::launched(1);
+  return int(cudaGetLastError());
+}
+
+// ===========================================================================
+// Allocation-free LayerNorm backward: tdb_layernorm_bwd_noalloc
+//
+// This entry point has no counterpart in the reference.  It exists for callers
+// that cannot call cudaMalloc (or any allocating routine) at the point where
+// they need the LayerNorm backward: for example a host application whose
+// memory planner has already reserved all device memory up front, so a fresh
+// allocation would fail or fragment it, or code in the middle of a stream of
+// asynchronous work that must not risk the implicit device-wide
+// synchronisation cudaMalloc / cudaFree can cause.  Such a caller supplies only
+// the inputs and outputs; the per-block partial sums live in a fixed array of
+// this library instead of a caller-provided scratch buffer.
+//
+// Limits and behaviour:
+//   * The scratch is one file-scope device array of kNoAllocScratchFloats fp32
+//     values (4 MiB).  Every GPU that loads this library holds it until the
+//     process exits.  A call needs ceil(rows / 16) * 2 * H floats; larger
+//     problems are rejected with cudaErrorInvalidValue and a message naming the
+//     limit (use tdb_layernorm_bwd with your own scratch for those).
+//   * The first call on a device looks up the array's device address with
+//     cudaGetSymbolAddress while that device is current, and caches it per
+//     device.  Make that first call before any stream capture begins.
+//   * Nothing in the array has to start at zero: every partial that is read
+//     is written earlier by the same call.  The array keeps the contents of the
+//     last call.
+//   * All calls on one device share the array, so calls that can overlap on
+//     the GPU (different streams without ordering between them) race and give
+//     wrong results.  Order such calls on one stream or with events.
+//   * No cudaMalloc, cudaFree or other allocating routine is called.
+// ===========================================================================
+namespace tdb {
+namespace ln {
+constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+static float* g_noalloc_addr[64];
+static std::mutex g_noalloc_mutex;
+}  // namespace ln
+}  // namespace tdb
+
+// Largest scratch (in floats) the allocation-free entry point can serve.
+TDB_API long long tdb_layernorm_bwd_noalloc_max_floats() { return tdb::ln::kNoAllocScratchFloats; }
+
+TDB_API int tdb_layernorm_bwd_noalloc(const void* x, const void* gamma, const float* mean, const float* rstd,
+                                      const void* dy, const void* dres, void* dx, float* dgamma, float* dbeta,
+                                      int rows, int H, int accumulate, void* stream) {
+  const int vpt = pick_vpt(H);
+  if (!vpt || rows <= 0)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "layernorm bwd (no-alloc): unsupported hidden size %d", H);
+  const int64_t need = int64_t((rows + kBwdRows - 1) / kBwdRows) * 2 * H;
+  if (need > tdb::ln::kNoAllocScratchFloats)
+    return tdb_host::fail(int(cudaErrorInvalidValue),
+                          "layernorm bwd (no-alloc): rows=%d H=%d needs %lld scratch floats but the built-in array "
+                          "holds at most %lld; call tdb_layernorm_bwd with caller-provided scratch instead",
+                          rows, H, (long long)need, (long long)tdb::ln::kNoAllocScratchFloats);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return tdb_host::fail(int(e), "layernorm bwd (no-alloc): cudaGetDevice failed");
+  if (dev < 0 || dev >= 64) return tdb_host::fail(int(cudaErrorInvalidDevice), "layernorm bwd (no-alloc): device %d", dev);
+  float* scratch = tdb::ln::g_noalloc_addr[dev];
+  if (scratch == nullptr) {
+    std::lock_guard<std::mutex> guard(tdb::ln::g_noalloc_mutex);
+    if (tdb::ln::g_noalloc_addr[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, tdb::ln::g_noalloc_scratch);
+      if (e != cudaSuccess)
+        return tdb_host::fail(int(e), "layernorm bwd (no-alloc): cudaGetSymbolAddress failed on device %d", dev);
+      tdb::ln::g_noalloc_addr[dev] = static_cast<float*>(p);
+    }
+    scratch = tdb::ln::g_noalloc_addr[dev];
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc;
+  switch (vpt) {
+    case 8: rc = bwd_launch<8>(x, gamma, mean, rstd, dy, dres, dx, scratch, rows, H, s); break;
+    case 16: rc = bwd_launch<16>(x, gamma, mean, rstd, dy, dres, dx, scratch, rows, H, s); break;
+    case 32: rc = bwd_launch<32>(x, gamma, mean, rstd, dy, dres, dx, scratch, rows, H, s); break;
+    default: rc = bwd_launch<64>(x, gamma, mean, rstd, dy, dres, dx, scratch, rows, H, s); break;
+  }
+  if (rc) return rc;
+  const int nparts = (rows + kBwdRows - 1) / kBwdRows;
+  ln_reduce_partials<<<(2 * H + 255) / 256, 256, 0, s>>>(scratch, nparts, H, dgamma, dbeta, accumulate);
   tdb_host::launched(1);
   return int(cudaGetLastError());
 }
