@@ -66,7 +66,7 @@ struct PlainEpi {
   __device__ __forceinline__ void tile_begin(int, int) {}
   __device__ __forceinline__ void tile_end(int, int, int, int) {}
 
-  __device__ __forceinline__ void chunk(int row, int col, const uint32_t (&r)[32]) {
+  __device__ __forceinline__ void chunk(int row, int col, int /*c*/, const uint32_t (&r)[32]) {
     if (row >= p.M || col >= p.N) return;
     float v[32];
 #pragma unroll

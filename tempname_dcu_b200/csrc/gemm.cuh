@@ -216,7 +216,7 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
       if (!ok) { *abort_flag = 1; break; }
       tc_fence_after();
       epi.tile_begin(mb, nb);
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + (uint32_t(quarter * 32) << 16) + b * BN + c * 32, r);
@@ -226,7 +226,7 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars->tmem_empty[b]);
         }
-        epi.chunk(mb * BM + row_in_tile, nb * BN + c * 32, r);
+        epi.chunk(mb * BM + row_in_tile, nb * BN + c * 32, c, r);
       }
       epi.tile_end(mb, nb, quarter, lane);
     }

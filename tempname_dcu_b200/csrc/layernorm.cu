@@ -176,7 +176,7 @@ static int bwd_launch(const void* x, const void* g, const float* mean, const flo
 
 static int pick_vpt(int H) {
   // threads = H / VPT must be a multiple of 32 and <= 1024
-  for (int vpt : {32, 16, 8, 64}) {
+  for (int vpt : {8, 16, 32, 64}) {
     if (H % vpt == 0 && (H / vpt) % 32 == 0 && H / vpt <= 1024) return vpt;
   }
   return 0;

@@ -94,7 +94,7 @@ class GPT:
                 if factory is None:
                     self.operators.append(NcclRowOperator(self.tp))
                 else:
-                    plan = execution_plan["roles"][role] if execution_plan else None
+                    plan = execution_plan["roles"][role] if (execution_plan and arm in ARMS[3:]) else None
                     self.operators.append(factory(m=self.m, n=self.h, k=k, group=group, arm=arm,
                                                   chunk_rows=c["chunk_rows"], plan=plan))
         self._scratch = {}

@@ -148,5 +148,17 @@ def manifest() -> dict:
     return json.loads(MANIFEST.read_text()) if MANIFEST.is_file() else {}
 
 
+def manifest_for_rows() -> dict:
+    """Build identity recorded in rank rows: library bytes hash and a source
+    hash over every csrc file (the analogue of the reference's codec build
+    manifest, python/flux_dcu/codec.py:72-109)."""
+    blob = b"".join(p.name.encode() + p.read_bytes() for p in sorted(sources() + headers()))
+    m = manifest()
+    return dict(library=str(LIBRARY), library_sha256=_sha(LIBRARY.read_bytes()) if LIBRARY.is_file() else None,
+                identity=dict(source_sha256=_sha(blob), flags=ARCH_FLAGS + NVCC_FLAGS,
+                              nvcc_version=m.get("nvcc_version")),
+                link_key=m.get("link"))
+
+
 if __name__ == "__main__":
     print(build(verbose=True))

@@ -1,5 +1,330 @@
-"""Placeholder; replaced by the fused operator runtime."""
+"""The five-arm tensor-parallel overlap operator on B200.
+
+``FluxB200(m, n, k, group, arm, codec=None, chunk_rows=128, plan=None)``
+computes the row-parallel projection ``out = RS(input @ weight^T) (+ residual
++ bias)`` with ONE fused persistent kernel (``csrc/gemm_rs.cu``): tcgen05 GEMM
+tiles are produced in the arm's schedule (``mapping.schedule``) and pushed by
+the epilogue into the destination rank's receive slot over NVLink (BF16, or
+TACO-encoded for the selected blocks), and the same kernel then performs the
+ordered BF16 reduction of this rank's blocks, polling per-block counters --
+in schedule order ("ordered") or per lane, ready block first ("per-lane
+ready", arrival arms).
+
+``initialize_context`` / ``shutdown_context`` manage the per-(device, group)
+state shared by all operators: the symmetric heap (receive slots for two
+alternating buffer sets and the per-block counters), the call epoch and the
+failure flag.  Any exception during a call poisons the operator and the
+context; a poisoned context refuses further calls.
+
+Reference parity: python/flux_dcu/runtime.py:18-321 (initialize_context,
+shutdown_context, FluxDCU.forward / profile_call / state) and
+mapping.py (schedules, selection, wire bytes).
+"""
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import json
+import threading
+
+from .mapping import ARRIVAL_ARMS, BACKEND, block_selection, schedule, selection_statistics, tile_table
+from .ops import native
+
+native.register("tdb_gemm_rs", [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
+                                ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
+                                ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int, ctypes.c_uint, ctypes.c_void_p,
+                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_double,
+                                ctypes.c_void_p])
+native.register("tdb_gemm_rs_signals_per_block", [ctypes.c_int, ctypes.c_int, ctypes.c_int])
+
+_CONTEXTS = {}
+_LOCK = threading.Lock()
+FLAGS_BYTES = 1 << 16
+PEER_WAIT_SECONDS = 20.0
+
+
+class Context:
+    """Per-(device, group) shared state of the fused operators."""
+
+    def __init__(self, tp, capacity_bytes):
+        import torch
+        from .parallel.symmetric import SymmetricHeap
+        self.tp = tp
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.recv_bytes = int(capacity_bytes)
+        self.heap = SymmetricHeap(tp, FLAGS_BYTES + self.recv_bytes)
+        self.flags_off = 0
+        self.recv_off = FLAGS_BYTES
+        self.epoch = 0
+        self.targets = [0, 0]
+        self.failed = False
+        self.closed = False
+        self.submission_lock = threading.Lock()
+        self.calls = 0
+
+    def next_call(self, signals_per_block):
+        """(set, expected counter) for the next fused call; identical on all
+        ranks because every rank makes the same sequence of calls."""
+        s = self.epoch & 1
+        self.targets[s] += signals_per_block
+        self.epoch += 1
+        return s, self.targets[s]
+
+
+def initialize_context(group, capacity_bytes=None):
+    """Collectively create (or return) the context of ``group`` on the current
+    device.  All ranks must call it in the same order."""
+    import torch
+    from .parallel.tp import TPGroup
+    key = (torch.cuda.current_device(), id(group))
+    with _LOCK:
+        ctx = _CONTEXTS.get(key)
+        if ctx is not None:
+            if ctx.closed or ctx.failed:
+                raise RuntimeError("this FluxB200 context is closed or previously failed")
+            if capacity_bytes is not None and capacity_bytes > ctx.recv_bytes:
+                raise ValueError("context receive capacity too small for this operator; create the context "
+                                 "with the model's largest projection first")
+            return ctx
+        tp = TPGroup(group)
+        if tp.world < 2:
+            raise ValueError("the fused operator needs a group of at least two ranks")
+        ctx = Context(tp, capacity_bytes or (64 << 20))
+        _CONTEXTS[key] = ctx
+        return ctx
+
+
+def shutdown_context(group):
+    """Collective, ordered teardown (call on every rank before destroying the group)."""
+    import torch
+    key = (torch.cuda.current_device(), id(group))
+    with _LOCK:
+        ctx = _CONTEXTS.pop(key, None)
+    if ctx is None:
+        return
+    if not ctx.submission_lock.acquire(blocking=False):
+        raise RuntimeError("cannot shut down a context during operator submission")
+    try:
+        ctx.heap.close()
+        ctx.closed = True
+    finally:
+        ctx.submission_lock.release()
+
+
+def receive_bytes(m, n, chunk_rows):
+    """Receive capacity of one operator shape: 2 sets x (m / chunk_rows) slots
+    of chunk_rows x n BF16 (a TACO packet fits in a BF16 slot)."""
+    return 2 * (m // chunk_rows) * chunk_rows * n * 2
+
+
+class FluxB200:
+    """Fused GEMM + reduce-scatter for one projection shape and arm."""
+
+    def __init__(self, m, n, k, group, arm, codec=None, chunk_rows=128, plan=None, diagnostic_delay_cycles=0,
+                 b_mn=False, tile_n=None):
+        import torch
+        if type(diagnostic_delay_cycles) is not int or not 0 <= diagnostic_delay_cycles <= 100_000_000:
+            raise ValueError("diagnostic_delay_cycles must be an integer in [0, 100000000]")
+        self.context = initialize_context(group, receive_bytes(m, n, chunk_rows))
+        tp = self.context.tp
+        self.group, self.arm, self.codec = group, arm, codec
+        self.rank, self.world = tp.rank, tp.world
+        self.device = self.context.device
+        self.m, self.n, self.k, self.chunk_rows = m, n, k, chunk_rows
+        self.b_mn = bool(b_mn)
+        self.diagnostic_delay_cycles = diagnostic_delay_cycles
+        self.last_profile_delay = None
+        self.plan = json.loads(json.dumps(plan, allow_nan=False)) if plan is not None else None
+        self.order = schedule(m, n, k, self.world, chunk_rows, arm, self.plan)
+        self.selection_mask = block_selection(m, n, k, self.world, chunk_rows, arm, self.plan)
+        self.consumer_policy = "per_lane_ready" if arm in ARRIVAL_ARMS else "ordered"
+        self.quantized = any(self.selection_mask)
+        self.mapping_sha256 = hashlib.sha256(json.dumps(self.order, sort_keys=True).encode()).hexdigest()
+        if self.plan is not None:
+            from .planning import role_digest
+            self.plan_sha256 = role_digest(self.plan)
+        else:
+            self.plan_sha256 = None
+        base = schedule(m, n, k, self.world, chunk_rows, "flux_taco_interleaved")
+        self.arrival_order_changed = ([x["physical"] for x in self.order] != [x["physical"] for x in base]
+                                      if self.plan else False)
+        self.selection = selection_statistics(m, n, self.world, chunk_rows, self.selection_mask)
+        # Tile width: every rank derives it from the shape alone.
+        sms = native.lib().tdb_sm_count(torch.cuda.current_device())
+        self.bn = tile_n or (256 if (m // 128) * (n // 256) >= sms else 128)
+        self.tiles = tile_table(m, n, self.world, chunk_rows, arm, self.plan, block_m=128, block_n=self.bn, k=k)
+        self.tile_table = torch.tensor(self.tiles, dtype=torch.int32, device=self.device)
+        self.qmask = torch.tensor([int(x) for x in self.selection_mask], dtype=torch.uint8, device=self.device)
+        self.per = m // self.world // chunk_rows
+        local_in_order = [item["within"] for item in self.order if item["destination"] == self.rank]
+        self.consume = torch.tensor(local_in_order, dtype=torch.int32, device=self.device)
+        self.signals = int(native.lib().tdb_gemm_rs_signals_per_block(chunk_rows, n, self.bn))
+        self.slot_bytes = chunk_rows * n * 2
+        self.packet_bytes = chunk_rows * n // 128 * 136
+        self.calls = self.validation_calls = 0
+        self.failed = False
+        self.profile_enabled = False
+        self.validate_next_call = False
+        self.events = []
+        self._last = None
+        # delay target: first tile (in production order) of the first lane-0 block
+        first0 = next((it for it in self.order if it["lane"] == 0), None)
+        n_tiles = n // self.bn
+        self._delay_tile = ((first0["row"] // 128), 0) if first0 else (-1, -1)
+        self._n_tiles = n_tiles
+
+    # ------------------------------------------------------------------ call
+    def _check(self, input_, weight):
+        import torch
+        wshape = (self.k, self.n) if self.b_mn else (self.n, self.k)
+        for label, value, shape in (("input", input_, (self.m, self.k)), ("weight", weight, wshape)):
+            if (tuple(value.shape) != shape or value.dtype != torch.bfloat16 or not value.is_cuda
+                    or not value.is_contiguous()):
+                raise ValueError(f"{label} must be contiguous BF16 {shape} on the current device")
+        if self.failed or self.context.failed or self.context.closed:
+            raise RuntimeError("this operator/context previously failed or was closed and cannot be reused")
+
+    def forward(self, input_, weight, bias=None, residual=None, out=None):
+        import torch
+        self._check(input_, weight)
+        ctx = self.context
+        if not ctx.submission_lock.acquire(blocking=False):
+            raise RuntimeError("concurrent submissions to one FluxB200 context are unsupported")
+        try:
+            rows = self.m // self.world
+            if out is None:
+                out = torch.empty((rows, self.n), dtype=torch.bfloat16, device=self.device)
+            set_, expected = ctx.next_call(self.signals)
+            timeline = None
+            delay = 0
+            if self.profile_enabled:
+                timeline = torch.full((2 * self.per,), 2 ** 63 - 1, dtype=torch.int64, device=self.device)
+                if self.diagnostic_delay_cycles and self.rank == 0:
+                    delay = self.diagnostic_delay_cycles
+                    first0 = next(it for it in self.order if it["lane"] == 0)
+                    self.last_profile_delay = dict(physical=first0["physical"], lane=0, rank=0,
+                                                   cycles=self.diagnostic_delay_cycles)
+            heap = ctx.heap
+            native.check(native.lib().tdb_gemm_rs(
+                input_.data_ptr(), input_.stride(0), weight.data_ptr(), int(self.b_mn), weight.stride(0), self.m,
+                self.n, self.k, self.bn, self.tile_table.data_ptr(), heap.peers.data_ptr(), self.world, self.rank,
+                self.chunk_rows, ctx.recv_off, self.slot_bytes, ctx.flags_off, set_, expected,
+                self.qmask.data_ptr(), out.data_ptr(), 0 if bias is None else bias.data_ptr(),
+                0 if residual is None else residual.data_ptr(), self.consume.data_ptr(),
+                1 if self.consumer_policy == "per_lane_ready" else 0,
+                0 if timeline is None else timeline.data_ptr(), delay, self._delay_tile[0], self._delay_tile[1],
+                PEER_WAIT_SECONDS, native.stream_ptr()), "fused gemm_rs")
+            self._last = (set_, expected, timeline)
+            self.calls += 1
+            ctx.calls += 1
+            if self.validate_next_call:
+                from .validation import validate_operator_buffers
+                validate_operator_buffers(self, input_, weight, out)
+                native.raise_on_status()
+                self.validate_next_call = False
+                self.validation_calls += 1
+            return out
+        except BaseException:
+            self.failed = ctx.failed = True
+            raise
+        finally:
+            ctx.submission_lock.release()
+
+    __call__ = forward
+
+    # ---------------------------------------------------- validation hooks
+    def _slot_view(self, set_, source, within, nbytes, dtype, shape):
+        ctx = self.context
+        off = ctx.recv_off + ((set_ * self.world + source) * self.per + within) * self.slot_bytes
+        return ctx.heap.view(off, shape, dtype)
+
+    def validation_tensors(self):
+        import torch
+        set_ = self._last[0] if self._last else 0
+        out = []
+        for within in range(self.per):
+            physical = self.rank * self.per + within
+            for s in range(self.world):
+                if self.selection_mask[physical] and s != self.rank:
+                    continue
+                out.append((f"receive.{within}.{s}", self._slot_view(set_, s, within, self.slot_bytes,
+                                                                     torch.bfloat16, (self.chunk_rows, self.n))))
+        return out
+
+    def validation_packets(self):
+        import torch
+        set_ = self._last[0] if self._last else 0
+        out = []
+        elements = self.chunk_rows * self.n
+        for within in range(self.per):
+            physical = self.rank * self.per + within
+            if not self.selection_mask[physical]:
+                continue
+            for s in range(self.world):
+                if s == self.rank:
+                    continue
+                out.append((f"packet.{within}.{s}", self._slot_view(set_, s, within, self.packet_bytes,
+                                                                    torch.uint8, (self.packet_bytes,)), elements))
+        return out
+
+    # ------------------------------------------------------------ profiling
+    def profile_call(self, input_, weight, bias=None, residual=None):
+        """Separate diagnostic call recording per-block ready / consumed device
+        timestamps (globaltimer, ns) of this rank's blocks; with a diagnostic
+        delay, rank 0 holds back the signal of the first lane-0 tile."""
+        import torch
+        torch.cuda.synchronize()
+        self.profile_enabled = True
+        try:
+            result = self.forward(input_, weight, bias, residual)
+            torch.cuda.synchronize()
+            native.raise_on_status()
+            timeline = self._last[2].cpu().tolist()
+        finally:
+            self.profile_enabled = False
+        origin = min(t for t in timeline[0::2]) if timeline else 0
+        rows = []
+        for within in range(self.per):
+            physical = self.rank * self.per + within
+            rows.append(dict(stage="consumer", physical=physical, lane=within % 2,
+                             start_ms=(timeline[2 * within] - origin) / 1e6,
+                             end_ms=(timeline[2 * within + 1] - origin) / 1e6))
+        self.events = rows
+        return result, dict(events=rows, transport_lanes=2, consumer_policy=self.consumer_policy,
+                            diagnostic_delay=self.last_profile_delay,
+                            clock="device globaltimer (ns), receiver-local",
+                            diagnostic_limitation="Artificial skew tests mechanism availability, not normal-workload "
+                                                  "performance")
+
+    # ----------------------------------------------------------------- state
+    def state(self):
+        quantization = ("selective_remote_h128_e4m3" if self.arm.endswith("_selective") else
+                        "all_remote_h128_e4m3" if self.arm != "flux" else "none")
+        return dict(backend=BACKEND, arm=self.arm, rank=self.rank, calls=self.calls,
+                    shape=[self.m, self.n, self.k], chunk_rows=self.chunk_rows,
+                    production_schedule=self.order, mapping_sha256=self.mapping_sha256,
+                    gemms_per_call=1, collectives_per_call=1, fused_kernel="tdb::rs::gemm_rs_kernel",
+                    tile_n=self.bn, tiles_per_call=len(self.tiles), quantization=quantization,
+                    selection_mask=list(self.selection_mask),
+                    selection_granularity="physical_receiver_block_all_remote_sources",
+                    selected_remote_blocks_by_source=self.selection["selected_remote_blocks_by_source"],
+                    remote_wire_bytes_by_source=self.selection["remote_wire_bytes_by_source"],
+                    remote_wire_bytes_per_source=self.selection["remote_wire_bytes_by_source"][self.rank],
+                    actual_remote_wire_bytes_per_rank=self.selection["remote_wire_bytes_by_source"][self.rank],
+                    plan_sha256=self.plan_sha256, arrival_order_changed=self.arrival_order_changed,
+                    reduction_order=list(range(self.world)), rounding="bf16_after_each_source",
+                    scratch_bytes=receive_bytes(self.m, self.n, self.chunk_rows), original_cuda_flux=False,
+                    cta_level_swizzle=True, transport_lanes=2, lane_assignment="physical_within_destination_mod_2",
+                    consumer_policy=self.consumer_policy, validation_calls=self.validation_calls,
+                    diagnostic_delay_cycles=self.diagnostic_delay_cycles, diagnostic_delay_in_normal_forward=False,
+                    scheduling_granularity="tcgen05_tile_128x%d" % self.bn,
+                    overlap_claim="epilogue peer stores overlap the MMA of later tiles in one kernel")
 
 
 def operator_factory_for(arm):
-    return None
+    """Factory for ``GPT(operator_factory=...)``: a FluxB200 per row-parallel projection."""
+    def factory(m, n, k, group, arm=arm, chunk_rows=128, plan=None):
+        return FluxB200(m, n, k, group, arm, chunk_rows=chunk_rows, plan=plan)
+    return factory

@@ -1,0 +1,67 @@
+"""Kernel-time breakdown of training micro-steps (torch.profiler / CUPTI).
+
+    python -m tempname_dcu_b200.utils.trace [--layers L] [--micro 1] [--chrome out.json]
+
+Runs warm-up micro-steps, then profiles ``--micro`` micro-batches of the GPT
+training step and prints the device time per kernel name (sum, count, share),
+plus the total device time and the host wall time of the profiled region.
+The chrome trace (optional) shows the overlap of streams.  Numbers taken under
+the profiler are for shares only, never benchmark values.
+
+Reference parity: the reference records torch.profiler chrome traces per
+operator role (python/flux_dcu/worker.py:317-325) and operator event rows
+(runtime.py:270-292).
+"""
+from __future__ import annotations
+
+import argparse
+import collections
+import json
+import time
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--micro", type=int, default=1)
+    ap.add_argument("--chrome", default="")
+    ap.add_argument("--json", default="")
+    args = ap.parse_args(argv)
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    from ..models.config import BENCH_CONFIG
+    from ..train import Trainer, synthetic_batches
+    cfg = dict(BENCH_CONFIG, layers=args.layers)
+    trainer = Trainer(cfg, "flux", None)
+    (tokens, labels), = synthetic_batches(trainer.config, 1)
+    tokens, labels = tokens.cuda(), labels.cuda()
+    trainer.step(tokens, labels)
+    torch.cuda.synchronize()
+    model = trainer.model
+    with profile(activities=[ProfilerActivity.CUDA, ProfilerActivity.CPU]) as prof:
+        t0 = time.perf_counter()
+        for i in range(args.micro):
+            model.forward_backward(tokens[i], labels[i], trainer.loss)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    if args.chrome:
+        prof.export_chrome_trace(args.chrome)
+    per = collections.defaultdict(lambda: [0.0, 0])
+    for evt in prof.events():
+        if evt.device_type == torch.autograd.DeviceType.CUDA:
+            per[evt.name][0] += evt.device_time_total if hasattr(evt, "device_time_total") else evt.cuda_time_total
+            per[evt.name][1] += 1
+    total = sum(v[0] for v in per.values())
+    rows = sorted(per.items(), key=lambda kv: -kv[1][0])
+    print(f"profiled {args.micro} micro-batch(es), {args.layers} layers: device {total / 1e3:.2f} ms, "
+          f"host wall {wall * 1e3:.2f} ms")
+    for name, (us, n) in rows[:40]:
+        print(f"{us / 1e3:10.3f} ms {100 * us / total:6.2f}% x{n:<6d} {name[:110]}")
+    if args.json:
+        with open(args.json, "w") as fh:
+            json.dump(dict(total_us=total, wall_s=wall, kernels=[dict(name=k, us=v[0], count=v[1])
+                                                                  for k, v in rows]), fh, indent=1)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,123 @@
+"""Fused GEMM + reduce-scatter (csrc/gemm_rs.cu) on 2+ GPUs, every arm,
+against the independent references with the reference's numerical gates
+(python/flux_dcu/worker.py:281-312):
+
+* vs plain BF16 GEMM + all-to-all + ordered sum: <= 1% (flux), <= 5% (TACO);
+* vs the same with the independent codec on the selected remote blocks: <= 1%;
+* arms that only reorder production are bitwise equal (B == C == D, E == E
+  with the base order);
+* changed-input reuse <= 1% and the previous output stays untouched.
+
+Runs as child processes over NCCL (one per GPU, NVLS off); skipped with fewer
+than two GPUs.
+"""
+import os
+import socket
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, result_path):
+    import json
+    import math
+    from datetime import timedelta
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    group = dist.group.WORLD
+    from tempname_dcu_b200.mapping import ARMS
+    from tempname_dcu_b200.ops import native
+    from tempname_dcu_b200.planning import make_role, base_order
+    from tempname_dcu_b200.runtime import FluxB200, shutdown_context
+    from tempname_dcu_b200.worker import projection_reference, relative_error
+    out = {}
+    try:
+        m, n, chunk = 2048, 4096, 128
+        for k in (512, 2048):
+            gen = torch.Generator(device="cuda").manual_seed(1234 + 173 * rank + k)
+            x = torch.randn((m, k), generator=gen, device="cuda").to(torch.bfloat16)
+            w = (torch.randn((n, k), generator=gen, device="cuda") / math.sqrt(k)).to(torch.bfloat16)
+            per = m // world // chunk
+            blocks = per * world
+            rev = [d * per + (per - 1 - i) for i in range(per) for d in range(world)]
+            plan_d = make_role(m, n, k, world, chunk, order=rev)
+            mask = [(i % 3) == 0 for i in range(blocks)]
+            plan_e = make_role(m, n, k, world, chunk, order=rev, mask=mask)
+            outputs = {}
+            for arm, plan in ((ARMS[0], None), (ARMS[1], None), (ARMS[2], None), (ARMS[3], plan_d),
+                              (ARMS[4], plan_e)):
+                op = FluxB200(m, n, k, group, arm, chunk_rows=chunk, plan=plan)
+                op.validate_next_call = True
+                y = op.forward(x, w)
+                torch.cuda.synchronize()
+                native.raise_on_status()
+                sel = mask if arm == ARMS[4] else None
+                plain, coded = projection_reference(x, w, rank, world, group, arm != "flux", sel, chunk)
+                e_plain, e_codec = relative_error(y, plain), relative_error(y, coded)
+                kept = y.clone()
+                x2 = (x * 0.75 + 0.125).to(torch.bfloat16)
+                y2 = op.forward(x2, w)
+                _, coded2 = projection_reference(x2, w, rank, world, group, arm != "flux", sel, chunk)
+                e_reuse = relative_error(y2, coded2)
+                outputs[arm] = kept
+                out[f"{arm}.k{k}"] = dict(plain=e_plain, codec=e_codec, reuse=e_reuse,
+                                          kept=bool(torch.equal(kept, y.clone())))
+            out[f"bitwise.k{k}"] = dict(
+                b_c=bool(torch.equal(outputs[ARMS[1]], outputs[ARMS[2]])),
+                c_d=bool(torch.equal(outputs[ARMS[2]], outputs[ARMS[3]])))
+            plan_e_base = dict(plan_e, arrival_order=base_order(m, n, k, world, chunk))
+            ebase = FluxB200(m, n, k, group, ARMS[4], chunk_rows=chunk, plan=plan_e_base).forward(x, w)
+            out[f"bitwise.k{k}"]["e_ebase"] = bool(torch.equal(ebase, outputs[ARMS[4]]))
+            # fused bias + residual
+            bias = torch.randn(n, device="cuda").to(torch.bfloat16)
+            res = torch.randn(m // world, n, device="cuda").to(torch.bfloat16)
+            y = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk).forward(x, w, bias, res)
+            plain, _ = projection_reference(x, w, rank, world, group, False)
+            ref = ((res.float() + plain.float()).to(torch.bfloat16).float() + bias.float()).to(torch.bfloat16)
+            out[f"bias_residual.k{k}"] = relative_error(y, ref)
+        torch.cuda.synchronize()
+        native.raise_on_status()
+        shutdown_context(group)
+    finally:
+        if rank == 0:
+            with open(result_path, "w") as fh:
+                json.dump(out, fh)
+        dist.destroy_process_group()
+
+
+def test_fused_gemm_rs_all_arms(tmp_path):
+    import json
+    import torch
+    import torch.multiprocessing as mp
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs at least two GPUs")
+    world = 2
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    path = str(tmp_path / "result.json")
+    mp.spawn(_worker, args=(world, _free_port(), path), nprocs=world, join=True)
+    res = json.load(open(path))
+    for key, value in res.items():
+        if key.startswith("bitwise"):
+            assert all(value.values()), (key, value)
+        elif key.startswith("bias_residual"):
+            assert value <= 0.01, (key, value)
+        else:
+            arm = key.split(".")[0]
+            assert value["plain"] <= (0.01 if arm == "flux" else 0.05), (key, value)
+            assert value["codec"] <= 0.01, (key, value)
+            assert value["reuse"] <= 0.01, (key, value)
+            assert value["kept"], key
