@@ -226,17 +226,24 @@ __device__ __forceinline__ bool elect_one() {
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t x) { return __uint_as_float(uint32_t(x) << 16); }
 
-// Round-to-nearest-even fp32 -> bf16 bits; NaN stays a quiet NaN.
+// Round-to-nearest-even fp32 -> bf16 bits.  On the device this is the
+// single hardware cvt.rn.bf16.f32; the host version rounds the bit pattern
+// (identical for every finite input; a NaN stays a NaN in both).
 __host__ __device__ __forceinline__ uint16_t float_to_bf16_bits(float f) {
 #ifdef __CUDA_ARCH__
-  uint32_t bits = __float_as_uint(f);
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 #else
   uint32_t bits;
   memcpy(&bits, &f, 4);
-#endif
   if ((bits & 0x7fffffffu) > 0x7f800000u) return uint16_t((bits >> 16) | 0x0040u);
   bits += 0x7fffu + ((bits >> 16) & 1u);
   return uint16_t(bits >> 16);
+#endif
+}
+
+// acc <- bf16(acc + x), the ordered-reduction step, in registers.
+__device__ __forceinline__ float bf16_add(float acc, float x) {
+  return __bfloat162float(__float2bfloat16_rn(acc + x));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -63,6 +63,8 @@ template <int MODE>
 struct PlainEpi {
   EpiParams p;
 
+  static constexpr int kSmemBytes = 0;
+  __device__ __forceinline__ void set_smem(uint8_t*) {}
   __device__ __forceinline__ void tile_begin(int, int) {}
   __device__ __forceinline__ void tile_end(int, int, int, int) {}
 

@@ -27,9 +27,9 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one 128B swizzle row
 constexpr int kThreads = 192;
 
-template <int BN>
+template <int BN, int STAGES = (BN == 256 ? 4 : 6)>
 struct Config {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kStages = STAGES;
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -84,10 +84,12 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr) {
   return smem_desc_sw128(saddr, BK * 128, 1024);
 }
 
-template <int BN, bool A_MN, bool B_MN, class Epi>
+// Epi may own shared memory (Epi::kSmemBytes, placed after the barriers);
+// the epilogue warps receive it through epi.set_smem().
+template <int BN, bool A_MN, bool B_MN, class Epi, int STAGES = Config<BN>::kStages>
 __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUtensorMap* tmB, int K,
                                               const TileOrder& order, Epi& epi, int* status) {
-  using Cfg = Config<BN>;
+  using Cfg = Config<BN, STAGES>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -203,6 +205,7 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
     }
   } else {
     // ---------------- Epilogue (warps 2..5) ----------------
+    epi.set_smem(reinterpret_cast<uint8_t*>(bars) + 256);
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
     const int row_in_tile = quarter * 32 + lane;
     int tc = 0;

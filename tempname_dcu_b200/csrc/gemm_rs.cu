@@ -66,6 +66,7 @@ struct Params {
   long long delay_cycles;  // diagnostic: delay the signal of tile (delay_mb, delay_nb)
   int delay_mb, delay_nb;
   uint64_t wait_ns;
+  unsigned long long* phases;  // optional [grid][4]: start, produce done, first block ready, end
 };
 
 __device__ __forceinline__ uint8_t* slot_ptr(const Params& p, int rank_of_heap, int source, int within) {
@@ -81,6 +82,14 @@ __device__ __forceinline__ uint32_t* flag_ptr(const Params& p, int rank_of_heap,
 __device__ __forceinline__ void red_release_sys(uint32_t* addr, uint32_t v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
+
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
   uint32_t v;
@@ -117,13 +126,16 @@ __device__ __forceinline__ void encode_group_thread(float (&x)[128], uint32_t (&
     amax = fmaxf(amax, fabsf(x[j]));
   }
   q = fminf(fmaxf(fmaxf(amax, 1e-12f) / 448.0f, 1e-12f), 1e6f);
+  // Multiply by the correctly rounded reciprocal instead of 128 divisions;
+  // differs from f / q by at most one ulp before the 3-bit-mantissa rounding.
+  const float rq = __frcp_rn(q);
 #pragma unroll
   for (int w = 0; w < 32; ++w) {
     float y[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float f = isfinite(x[4 * w + j]) ? x[4 * w + j] : 0.0f;
-      y[j] = fminf(fmaxf(f / q, -448.0f), 448.0f);
+      y[j] = fminf(fmaxf(f * rq, -448.0f), 448.0f);
     }
     words[w] = uint32_t(taco::e4m3x2(y[0], y[1])) | (uint32_t(taco::e4m3x2(y[2], y[3])) << 16);
   }
@@ -131,15 +143,29 @@ __device__ __forceinline__ void encode_group_thread(float (&x)[128], uint32_t (&
 
 template <int BN>
 struct PushEpi {
+  // Per epilogue warp: a 32-row x BN-column BF16 slab (also holds the TACO
+  // payload bytes of those rows), XOR-swizzled in 16-byte chunks so that
+  // both the row-per-lane writes and the row-contiguous reads are
+  // conflict-free.
+  static constexpr int kRowBytes = BN * 2;
+  static constexpr int kChunks = kRowBytes / 16;  // 16-byte chunks per row
+  static constexpr int kSmemBytes = 4 * 32 * kRowBytes;
   const Params* p;
   int* status;
-  // per-tile state
+  uint8_t* stage_base;
   int within, dest, row0;
   bool quant;
   uint8_t* slot;
   float grp[128];
+  float qs[BN / 128], as_[BN / 128];
 
-  __device__ __forceinline__ void tile_begin(int mb, int nb) {
+  __device__ __forceinline__ void set_smem(uint8_t* ptr) { stage_base = ptr; }
+
+  __device__ __forceinline__ uint8_t* stage() const { return stage_base + ((threadIdx.x >> 5) & 3) * 32 * kRowBytes; }
+
+  __device__ __forceinline__ static int swz(int row, int chunk) { return chunk ^ (row & (kChunks - 1)); }
+
+  __device__ __forceinline__ void tile_begin(int mb, int /*nb*/) {
     const int m0 = mb * BM;
     const int physical = m0 / p->chunk_rows;
     dest = physical / p->per;
@@ -149,11 +175,10 @@ struct PushEpi {
     slot = slot_ptr(*p, dest, p->rank, within);
   }
 
-  __device__ __forceinline__ void chunk(int row, int col, int c, const uint32_t (&r)[32]) {
-    const int rib = row0 + (row % BM);  // row inside the block
-    const int N = p->N;
+  __device__ __forceinline__ void chunk(int /*row*/, int /*col*/, int c, const uint32_t (&r)[32]) {
+    const int lane = threadIdx.x & 31;
+    uint4* srow = reinterpret_cast<uint4*>(stage() + lane * kRowBytes);
     if (!quant) {
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(slot) + int64_t(rib) * N + col);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         uint4 w;
@@ -161,7 +186,7 @@ struct PushEpi {
         w.y = pack_bf16x2(__uint_as_float(r[8 * i + 2]), __uint_as_float(r[8 * i + 3]));
         w.z = pack_bf16x2(__uint_as_float(r[8 * i + 4]), __uint_as_float(r[8 * i + 5]));
         w.w = pack_bf16x2(__uint_as_float(r[8 * i + 6]), __uint_as_float(r[8 * i + 7]));
-        dst[i] = w;
+        srow[swz(lane, c * 4 + i)] = w;
       }
       return;
     }
@@ -173,32 +198,78 @@ struct PushEpi {
       uint32_t words[32];
       float q, a;
       encode_group_thread(grp, words, q, a);
-      const int gcol = col - 96;
-      const int64_t elements = int64_t(p->chunk_rows) * N;
-      const int64_t groups = elements / 128;
-      const int64_t g = (int64_t(rib) * N + gcol) / 128;
-      uint4* pay = reinterpret_cast<uint4*>(slot + int64_t(rib) * N + gcol);
+      const int gi = c >> 2;  // group index inside the tile row
 #pragma unroll
-      for (int i = 0; i < 8; ++i) pay[i] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
-      float* scales = reinterpret_cast<float*>(slot + elements);
-      scales[g] = q;
-      scales[groups + g] = a;
+      for (int i = 0; i < 8; ++i)
+        srow[swz(lane, gi * 8 + i)] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
+      qs[gi] = q;
+      as_[gi] = a;
     }
   }
 
-  __device__ __forceinline__ void tile_end(int mb, int nb, int /*quarter*/, int lane) {
-    __threadfence_system();
+  __device__ __forceinline__ void tile_end(int mb, int nb, int quarter, int lane) {
     __syncwarp();
-    if (lane == 0) {
-      if (p->delay_cycles > 0 && mb == p->delay_mb && nb == p->delay_nb) {
-        const long long t0 = clock64();
-        while (clock64() - t0 < p->delay_cycles) {
-        }
+    const int N = p->N;
+    const int n0 = nb * BN;
+    const int rib0 = row0 + quarter * 32;  // first block row of this warp
+    const uint8_t* st = stage();
+    if (!quant) {
+      // bf16: each row is kRowBytes contiguous in the destination
+      constexpr int kRowsPerIter = 32 / kChunks;  // 1 (BN=256) or 2 (BN=128)
+#pragma unroll 4
+      for (int j = 0; j < 32; j += kRowsPerIter) {
+        const int rr = j + lane / kChunks, ch = lane % kChunks;
+        const uint4 v = reinterpret_cast<const uint4*>(st + rr * kRowBytes)[swz(rr, ch)];
+        uint16_t* dst = reinterpret_cast<uint16_t*>(slot) + int64_t(rib0 + rr) * N + n0;
+        reinterpret_cast<uint4*>(dst)[ch] = v;
       }
-      red_release_sys(flag_ptr(*p, dest, within, p->rank), 1u);
+    } else {
+      // TACO payload: BN bytes per row (BN/128 groups of 128 codes)
+      constexpr int kPayChunks = BN / 16;
+      constexpr int kRowsPerIter = 32 / kPayChunks;  // 2 (BN=256) or 4 (BN=128)
+#pragma unroll 4
+      for (int j = 0; j < 32; j += kRowsPerIter) {
+        const int rr = j + lane / kPayChunks, ch = lane % kPayChunks;
+        const uint4 v = reinterpret_cast<const uint4*>(st + rr * kRowBytes)[swz(rr, ch)];
+        uint8_t* dst = slot + int64_t(rib0 + rr) * N + n0;
+        reinterpret_cast<uint4*>(dst)[ch] = v;
+      }
+      const int64_t elements = int64_t(p->chunk_rows) * N;
+      const int64_t groups = elements / 128;
+      const int64_t g0 = (int64_t(rib0 + lane) * N + n0) / 128;
+      float* scales = reinterpret_cast<float*>(slot + elements);
+#pragma unroll
+      for (int t = 0; t < BN / 128; ++t) {
+        scales[g0 + t] = qs[t];
+        scales[groups + g0 + t] = as_[t];
+      }
     }
+    // Signals are issued once per CTA after the produce phase (signal_tiles).
+    __syncwarp();
   }
 };
+
+// After its produce phase a CTA makes all of its peer stores visible with a
+// single system-scope fence and then adds 4 (one per epilogue warp) to the
+// (block, source) counter of every tile it produced, in production order.
+// The diagnostic delay holds back the signal of one tile only.
+__device__ void signal_tiles(const Params& p, const gemm::TileOrder& order) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  for (int i = blockIdx.x; i < order.num_tiles; i += gridDim.x) {
+    int mb, nb;
+    order.tile(i, mb, nb);
+    const int physical = (mb * BM) / p.chunk_rows;
+    const int dest = physical / p.per, within = physical % p.per;
+    if (p.delay_cycles > 0 && mb == p.delay_mb && nb == p.delay_nb) {
+      const long long t0 = clock64();
+      while (clock64() - t0 < p.delay_cycles) {
+      }
+    }
+    red_release_sys(flag_ptr(p, dest, within, p.rank), 4u);
+  }
+}
 
 // Block readiness: all W sources delivered (acquire).
 __device__ __forceinline__ bool block_ready(const Params& p, int within) {
@@ -207,42 +278,148 @@ __device__ __forceinline__ bool block_ready(const Params& p, int within) {
   return true;
 }
 
-__device__ void consume_block(const Params& p, int within, int part, int nparts) {
+__device__ __forceinline__ void unpack8(const uint4& w, float (&v)[8]) {
+  const uint32_t a[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[2 * j] = bf16_bits_to_float(a[j] & 0xffff);
+    v[2 * j + 1] = bf16_bits_to_float(a[j] >> 16);
+  }
+}
+
+constexpr int kMaxWorld = 8;
+
+// One 16-byte vector (8 outputs) of a BF16 block: ordered source sum, then
+// residual, then bias.
+__device__ __forceinline__ uint4 reduce_vec8(const Params& p, uint64_t local_base, int within, int64_t v) {
+  uint4 src[kMaxWorld];
+#pragma unroll
+  for (int s = 0; s < kMaxWorld; ++s)
+    if (s < p.W)
+      src[s] = __ldcg(reinterpret_cast<const uint4*>(
+                          local_base + p.recv_off + (uint64_t(p.set * p.W + s) * p.per + within) * p.slot_bytes) + v);
+  const int64_t ov = int64_t(within) * p.chunk_rows * p.N / 8 + v;
+  uint4 rw = make_uint4(0, 0, 0, 0), bw = make_uint4(0, 0, 0, 0);
+  if (p.residual) rw = reinterpret_cast<const uint4*>(p.residual)[ov];
+  if (p.bias) bw = reinterpret_cast<const uint4*>(p.bias)[uint32_t(v) % uint32_t(p.N >> 3)];
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int s = 0; s < kMaxWorld; ++s) {
+    if (s < p.W) {
+      float x[8];
+      unpack8(src[s], x);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = bf16_bits_to_float(float_to_bf16_bits(acc[j] + x[j]));
+    }
+  }
+  if (p.residual) {
+    float x[8];
+    unpack8(rw, x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = bf16_bits_to_float(float_to_bf16_bits(x[j] + acc[j]));
+  }
+  if (p.bias) {
+    float x[8];
+    unpack8(bw, x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = bf16_bits_to_float(float_to_bf16_bits(acc[j] + x[j]));
+  }
+  uint4 o;
+  o.x = pack_bf16x2(acc[0], acc[1]);
+  o.y = pack_bf16x2(acc[2], acc[3]);
+  o.z = pack_bf16x2(acc[4], acc[5]);
+  o.w = pack_bf16x2(acc[6], acc[7]);
+  return o;
+}
+
+// BF16 blocks of a batch (list of `count` block ids).  Vector v of a block
+// always belongs to thread (v mod stride) of the partition -- independent of
+// which blocks this CTA found ready -- and a thread chains its vectors across
+// the batch's blocks so that four of them are in flight at once.
+__device__ void consume_bf16_batch(const Params& p, const int* blocks, int count, int part, int nparts) {
+  const int64_t nvec = int64_t(p.chunk_rows) * p.N / 8;
+  const int64_t stride = int64_t(nparts) * blockDim.x;
+  const int64_t t0 = int64_t(part) * blockDim.x + threadIdx.x;
+  if (t0 >= nvec) return;
+  const uint64_t local_base = p.peers[p.rank];
+  constexpr int U = 4;
+  int bi = 0;
+  int64_t v = t0;
+  while (bi < count) {
+    int ib[U];
+    int64_t iv[U];
+    int n = 0;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (bi < count) {
+        ib[u] = blocks[bi];
+        iv[u] = v;
+        n = u + 1;
+        v += stride;
+        if (v >= nvec) {
+          ++bi;
+          v = t0;
+        }
+      }
+    }
+    uint4 o[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (u < n) o[u] = reduce_vec8(p, local_base, ib[u], iv[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (u < n) reinterpret_cast<uint4*>(p.out)[int64_t(ib[u]) * nvec + iv[u]] = o[u];
+  }
+}
+
+// TACO block: one warp per H128 group; all sources' payload words and scales
+// are loaded before the register decodes.
+__device__ void consume_block_taco(const Params& p, int within, int part, int nparts) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = blockDim.x >> 5;
   const int gpr = p.N / 128;
   const int items = p.chunk_rows * gpr;
-  const int physical = p.rank * p.per + within;
-  const bool quant = p.qmask[physical] != 0;
   const int64_t elements = int64_t(p.chunk_rows) * p.N;
   const int64_t groups = elements / 128;
   for (int it = part * nw + warp; it < items; it += nparts * nw) {
     const int rho = it / gpr, g = it % gpr;
-    const int64_t e0 = int64_t(rho) * p.N + g * 128 + lane * 4;  // element offset in block
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int s = 0; s < p.W; ++s) {
+    const int64_t e0 = int64_t(rho) * p.N + g * 128 + lane * 4;
+    const int64_t gi = int64_t(rho) * gpr + g;
+    uint32_t word[kMaxWorld];
+    uint2 plain[kMaxWorld];
+    float qv[kMaxWorld], av[kMaxWorld];
+#pragma unroll
+    for (int s = 0; s < kMaxWorld; ++s) {
+      if (s >= p.W) continue;
       const uint8_t* slot = slot_ptr(p, p.rank, s, within);
-      float v[4];
-      if (quant && s != p.rank) {
-        // Peer-written data: read at L2 (.cg) so no stale L1 line can be hit.
-        const uint32_t word = __ldcg(reinterpret_cast<const unsigned int*>(slot + e0));
+      if (s != p.rank) {
         const float* scales = reinterpret_cast<const float*>(slot + elements);
-        const int64_t gi = int64_t(rho) * gpr + g;
-        taco::decode_group_warp(word, __ldcg(scales + gi), __ldcg(scales + groups + gi), lane, v);
+        word[s] = __ldcg(reinterpret_cast<const unsigned int*>(slot + e0));
+        qv[s] = __ldcg(scales + gi);
+        av[s] = __ldcg(scales + groups + gi);
+      } else {
+        plain[s] = __ldcg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(slot) + e0));
+      }
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < kMaxWorld; ++s) {
+      if (s >= p.W) continue;
+      float v[4];
+      if (s != p.rank) {
+        taco::decode_group_warp(word[s], qv[s], av[s], lane, v);
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[j] = bf16_bits_to_float(float_to_bf16_bits(v[j]));
       } else {
-        const uint2 w = __ldcg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(slot) + e0));
-        v[0] = bf16_bits_to_float(w.x & 0xffff);
-        v[1] = bf16_bits_to_float(w.x >> 16);
-        v[2] = bf16_bits_to_float(w.y & 0xffff);
-        v[3] = bf16_bits_to_float(w.y >> 16);
+        v[0] = bf16_bits_to_float(plain[s].x & 0xffff);
+        v[1] = bf16_bits_to_float(plain[s].x >> 16);
+        v[2] = bf16_bits_to_float(plain[s].y & 0xffff);
+        v[3] = bf16_bits_to_float(plain[s].y >> 16);
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[j] = bf16_bits_to_float(float_to_bf16_bits(acc[j] + v[j]));
     }
-    const int64_t orow = int64_t(within) * p.chunk_rows + rho;
-    const int64_t o = orow * p.N + g * 128 + lane * 4;
+    const int64_t o = (int64_t(within) * p.chunk_rows + rho) * p.N + g * 128 + lane * 4;
     if (p.residual) {
       const uint2 w = *reinterpret_cast<const uint2*>(p.residual + o);
       const float rr[4] = {bf16_bits_to_float(w.x & 0xffff), bf16_bits_to_float(w.x >> 16),
@@ -258,58 +435,104 @@ __device__ void consume_block(const Params& p, int within, int part, int nparts)
       for (int j = 0; j < 4; ++j) acc[j] = bf16_bits_to_float(float_to_bf16_bits(acc[j] + bb[j]));
     }
     uint2 ow;
-    ow.x = uint32_t(float_to_bf16_bits(acc[0])) | (uint32_t(float_to_bf16_bits(acc[1])) << 16);
-    ow.y = uint32_t(float_to_bf16_bits(acc[2])) | (uint32_t(float_to_bf16_bits(acc[3])) << 16);
+    ow.x = pack_bf16x2(acc[0], acc[1]);
+    ow.y = pack_bf16x2(acc[2], acc[3]);
     *reinterpret_cast<uint2*>(p.out + o) = ow;
   }
 }
 
+// Consumer.  Ordered policy: all CTAs take the longest prefix (in
+// consumption order) of complete blocks; per-lane ready: the CTAs of lane l
+// take every complete block of lane l.  Flags are polled by all threads in
+// parallel with relaxed system-scope loads; a thread that sees a complete
+// counter issues an acquire fence before the CTA barrier, after which the
+// block's data is read (at L2).  The BF16 blocks of one batch are reduced
+// together; TACO blocks one after another.
 __device__ void consume_phase(const Params& p, int* status) {
-  __shared__ int pick;
-  // Partition: ordered = all CTAs; per-lane = CTAs of parity l consume lane-l blocks.
+  __shared__ int s_bf[64], s_tq[64];
+  __shared__ int s_nb, s_nq;
+  __shared__ int s_missing[64];
+  __shared__ unsigned long long s_done;
   int part = blockIdx.x, nparts = gridDim.x, lane_id = -1;
   if (p.policy == 1) {
     lane_id = blockIdx.x & 1;
     part = blockIdx.x >> 1;
     nparts = (gridDim.x + 1 - lane_id) >> 1;
   }
-  uint64_t done = 0;
-  int remaining = 0;
+  uint64_t mine = 0;
   for (int k = 0; k < p.per; ++k)
-    if (lane_id < 0 || (p.consume[k] % 2) == lane_id) ++remaining;
+    if (lane_id < 0 || (p.consume[k] % 2) == lane_id) mine |= 1ull << k;
+  if (threadIdx.x == 0) s_done = 0;
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(p.peers[p.rank] + p.flags_off) +
+                          uint64_t(p.set) * p.per * p.W;
   const uint64_t t_start = globaltimer();
-  while (remaining > 0) {
+  bool first = true;
+  __syncthreads();
+  while (s_done != mine) {
+    // parallel poll: s_missing[w] = number of sources of block w not complete
+    for (int i = threadIdx.x; i < p.per; i += blockDim.x) s_missing[i] = 0;
+    __syncthreads();
+    bool saw = false;
+    for (int i = threadIdx.x; i < p.per * p.W; i += blockDim.x) {
+      if (ld_relaxed_sys(flags + i) < p.expected) atomicAdd(&s_missing[i / p.W], 1);
+      else saw = true;
+    }
+    if (saw) fence_acq_rel_sys();
+    __syncthreads();
     if (threadIdx.x == 0) {
-      int chosen = -1;
-      while (chosen < 0) {
-        for (int k = 0; k < p.per; ++k) {
-          const int w = p.consume[k];
-          if ((done >> k) & 1) continue;
-          if (lane_id >= 0 && (w % 2) != lane_id) continue;
-          if (block_ready(p, w)) { chosen = k; break; }
-          if (p.policy == 0) break;  // ordered: only the next block in order
-        }
-        if (chosen < 0 && globaltimer() - t_start > p.wait_ns) {
-          record_status(status, kTimeoutPeerFlag, 40, p.rank, int(done));
-          chosen = -2;
+      const uint64_t done = s_done;
+      int nb = 0, nq = 0;
+      uint64_t taken = 0;
+      for (int k = 0; k < p.per; ++k) {
+        if (!((mine >> k) & 1) || ((done >> k) & 1)) continue;
+        const int w = p.consume[k];
+        if (s_missing[w] == 0) {
+          if (p.qmask[p.rank * p.per + w]) s_tq[nq++] = w;
+          else s_bf[nb++] = w;
+          taken |= 1ull << k;
+        } else if (p.policy == 0) {
+          break;  // ordered: stop at the first incomplete block
         }
       }
-      pick = chosen;
-      if (chosen >= 0 && p.timeline) atomicMin(&p.timeline[2 * p.consume[chosen]], (unsigned long long)globaltimer());
+      if (nb + nq == 0 && globaltimer() - t_start > p.wait_ns) {
+        record_status(status, kTimeoutPeerFlag, 40, p.rank, int(done));
+        nb = -1;
+      }
+      s_nb = nb;
+      s_nq = nq;
+      const unsigned long long now = globaltimer();
+      if (nb + nq > 0) {
+        if (first && p.phases) p.phases[4 * (blockIdx.x % 1024) + 2] = now;
+        if (p.timeline) {
+          for (int i = 0; i < nb; ++i) atomicMin(&p.timeline[2 * s_bf[i]], now);
+          for (int i = 0; i < nq; ++i) atomicMin(&p.timeline[2 * s_tq[i]], now);
+        }
+        s_done = done | taken;
+      }
     }
     __syncthreads();
-    const int k = pick;
-    __syncthreads();
-    if (k < 0) return;
-    consume_block(p, p.consume[k], part, nparts);
-    done |= 1ull << k;
-    --remaining;
+    const int nb = s_nb, nq = s_nq;
+    if (nb < 0) return;
+    if (nb + nq == 0) {
+      __nanosleep(200);
+      continue;
+    }
+    first = false;
+    if (nb) consume_bf16_batch(p, s_bf, nb, part, nparts);
+    for (int i = 0; i < nq; ++i) consume_block_taco(p, s_tq[i], part, nparts);
     if (p.timeline) {
       __syncthreads();
-      if (threadIdx.x == 0) atomicMax(&p.timeline[2 * p.consume[k] + 1], (unsigned long long)globaltimer());
+      if (threadIdx.x == 0) {
+        const unsigned long long now = globaltimer();
+        for (int i = 0; i < nb; ++i) atomicMax(&p.timeline[2 * s_bf[i] + 1], now);
+        for (int i = 0; i < nq; ++i) atomicMax(&p.timeline[2 * s_tq[i] + 1], now);
+      }
     }
+    __syncthreads();
   }
 }
+
+constexpr int kStages = 3;
 
 template <int BN, bool B_MN>
 __global__ void __launch_bounds__(gemm::kThreads, 1)
@@ -318,33 +541,50 @@ __global__ void __launch_bounds__(gemm::kThreads, 1)
   PushEpi<BN> epi;
   epi.p = &p;
   epi.status = status;
-  gemm::gemm_mainloop<BN, false, B_MN>(&tmA, &tmB, K, order, epi, status);
+  unsigned long long* ph = p.phases ? p.phases + 4 * blockIdx.x : nullptr;
+  if (ph && threadIdx.x == 0) ph[0] = globaltimer();
+  gemm::gemm_mainloop<BN, false, B_MN, PushEpi<BN>, kStages>(&tmA, &tmB, K, order, epi, status);
+  signal_tiles(p, order);
+  if (ph && threadIdx.x == 0) ph[1] = globaltimer();
+}
+
+// Consumer kernel: launched right after the producer on the same stream, at
+// full occupancy.  It only waits for flags of blocks produced by other GPUs
+// (the local producer kernel has completed), with bounded polling.
+constexpr int kReduceThreads = 256;
+
+__global__ void __launch_bounds__(kReduceThreads)
+    rs_reduce_kernel(const __grid_constant__ Params p, int* status) {
+  unsigned long long* ph = p.phases ? p.phases + 4 * (blockIdx.x % 1024) : nullptr;
   consume_phase(p, status);
+  if (ph && threadIdx.x == 0) ph[3] = globaltimer();
 }
 
 template <int BN, bool B_MN>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int K, const gemm::TileOrder& order, const Params& p,
                   int grid, cudaStream_t stream) {
-  using Cfg = gemm::Config<BN>;
+  using Cfg = gemm::Config<BN, kStages>;
+  constexpr int kSmem = Cfg::kSmemBytes + PushEpi<BN>::kSmemBytes;
+  static_assert(kSmem <= 227 * 1024, "fused GEMM-RS shared memory budget");
   auto kern = gemm_rs_kernel<BN, B_MN>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs: cudaFuncSetAttribute failed");
     attr[dev & 63] = true;
   }
   int* status = tdb_host::status_ptr();
-  CUtensorMap a = ta, b = tb;
-  int k = K;
-  gemm::TileOrder o = order;
-  Params pp = p;
-  void* args[] = {&a, &b, &k, &o, &pp, &status};
-  cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(gemm::kThreads),
-                                              args, Cfg::kSmemBytes, stream);
-  if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs: cooperative launch failed (grid %d)", grid);
+  kern<<<grid, gemm::kThreads, kSmem, stream>>>(ta, tb, K, order, p, status);
   tdb_host::launched(1);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs: producer launch failed");
+  const int rgrid = 4 * tdb_host::sm_count();
+  rs_reduce_kernel<<<rgrid, kReduceThreads, 0, stream>>>(p, status);
+  tdb_host::launched(1);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs: consumer launch failed");
   return 0;
 }
 
@@ -369,8 +609,9 @@ TDB_API int tdb_gemm_rs(const void* A, int64_t lda, const void* B, int b_mn, int
                         uint64_t recv_off, uint64_t slot_bytes, uint64_t flags_off, int set, unsigned int expected,
                         const uint8_t* qmask, void* out, const void* bias, const void* residual, const int* consume,
                         int policy, unsigned long long* timeline, long long delay_cycles, int delay_mb, int delay_nb,
-                        double wait_seconds, void* stream) {
-  if (!A || !B || !out || !tile_table || !peers || !qmask || !consume || W < 2 || rank < 0 || rank >= W)
+                        double wait_seconds, unsigned long long* phases, void* stream) {
+  if (!A || !B || !out || !tile_table || !peers || !qmask || !consume || W < 2 || W > rs::kMaxWorld || rank < 0 ||
+      rank >= W)
     return tdb_host::fail(int(cudaErrorInvalidValue), "gemm_rs: bad pointers or ranks");
   if (bn != 128 && bn != 256) return tdb_host::fail(int(cudaErrorInvalidValue), "gemm_rs: bn must be 128 or 256");
   if (chunk_rows % rs::BM || m % (W * chunk_rows) || N % bn || N % 128 || K % 8)
@@ -417,8 +658,9 @@ TDB_API int tdb_gemm_rs(const void* A, int64_t lda, const void* B, int b_mn, int
   p.delay_mb = delay_mb;
   p.delay_nb = delay_nb;
   p.wait_ns = uint64_t(wait_seconds * 1e9);
+  p.phases = phases;
   const int sms = tdb_host::sm_count();
-  const int grid = order.num_tiles < sms ? (order.num_tiles > 2 ? order.num_tiles : 2) : sms;
+  const int grid = order.num_tiles < sms ? order.num_tiles : sms;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (bn == 256) return b_mn ? rs::launch<256, true>(ta, tb, K, order, p, grid, s)
                              : rs::launch<256, false>(ta, tb, K, order, p, grid, s);

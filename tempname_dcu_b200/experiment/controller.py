@@ -1,0 +1,284 @@
+"""Prepare, run and audit an isolated single-node B200 five-arm comparison.
+
+    tempname_dcu_b200/experiment/run_init.sh [--execute] [--out DIR] [--world-size N] ...
+
+Without ``--execute`` the controller only prints the plan (no torch import,
+no files written).  With it: freeze a snapshot of the sources (+ manifest
+sha256) and the native library, then run one ``torchrun`` per job
+(preflight -> calibrate -> operator windows -> training windows) in its own
+process group with a timeout, validate every job's rank rows, freeze the
+calibrated plan after the calibrate job, check that the TACO arms trained
+bitwise identically, and write ``report.json`` / ``report.md``.  SIGTERM
+stops only this controller's worker process group.  ``--report`` audits a
+finished directory read-only.
+
+Reference parity: tools/dcu/phase6/init.py:1-279 and run_init.sh (CLI,
+preview, snapshot, job loop, stop_process, batch-state.json).
+"""
+from __future__ import annotations
+
+import argparse
+from datetime import datetime, timezone
+import os
+from pathlib import Path
+import shutil
+import signal
+import subprocess
+import sys
+import uuid
+
+from . import protocol as p
+
+REPO = Path(__file__).resolve().parents[2]
+PACKAGE = REPO / "tempname_dcu_b200"
+
+
+def arguments(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--trials", type=int, default=1)
+    ap.add_argument("--blocks", type=int, default=10,
+                    help="five-arm blocks per trial; 1 is a short test, multiples of 10 are balanced")
+    ap.add_argument("--execute", action="store_true", help="without this flag only print the plan")
+    ap.add_argument("--out", type=Path)
+    ap.add_argument("--python", default=sys.executable)
+    ap.add_argument("--world-size", type=int, choices=(2, 4, 8), default=8)
+    ap.add_argument("--chunk-rows", type=int)
+    ap.add_argument("--warmup-steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--operator-warmup", type=int, default=100)
+    ap.add_argument("--operator-iters", type=int, default=200)
+    ap.add_argument("--quant-budget", type=float, default=0.25)
+    ap.add_argument("--calibration-iters", type=int, default=5)
+    ap.add_argument("--calibration-pairs", type=int, default=3)
+    ap.add_argument("--calibration-warmup", type=int, default=2)
+    ap.add_argument("--calibration-min-gain", type=float, default=0.002)
+    scopes = ap.add_mutually_exclusive_group()
+    scopes.add_argument("--operator-only", action="store_true")
+    scopes.add_argument("--preflight-only", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="separate per-block timeline profile after timing")
+    ap.add_argument("--small-model", action="store_true", help="diagnostic 2-layer model, not GPT-6.7B results")
+    ap.add_argument("--bench-model", action="store_true", help="GPT-6.7B with vocab 50257 (padded) and 8 micro-batches")
+    ap.add_argument("--worker-timeout", type=int, default=7200)
+    ap.add_argument("--report", action="store_true", help="read-only audit of a completed --out directory")
+    args = ap.parse_args(argv)
+    p.orders(args.trials, args.blocks)
+    p.require(args.warmup_steps >= 0 and args.operator_warmup >= 0, "warm-up counts must be non-negative")
+    p.require(args.steps > 0 and args.operator_iters > 0 and args.worker_timeout > 0,
+              "timing counts and timeout must be positive")
+    args.calibration = dict(warmup=args.calibration_warmup, iterations=args.calibration_iters,
+                            training_pairs=args.calibration_pairs, confirmation_pairs=args.calibration_pairs,
+                            min_gain=args.calibration_min_gain, quant_budget=args.quant_budget)
+    p.validate_calibration_options(args.calibration)
+    p.require(not args.report or (args.out is not None and not args.execute and not args.operator_only
+                                  and not args.preflight_only), "--report needs --out and cannot execute a stage")
+    p.require(not (args.small_model and args.bench_model), "choose one model preset")
+    model = dict(p.SMALL_MODEL if args.small_model else p.BENCH_MODEL if args.bench_model else p.MODEL)
+    if args.chunk_rows is not None:
+        model["chunk_rows"] = args.chunk_rows
+    p.validate_model(model, args.world_size)
+    p.require(model["sequence"] * model["micro_batch"] // args.world_size // model["chunk_rows"] >= 2,
+              "at least two blocks per destination are needed to distinguish the schedules")
+    args.model = model
+    if args.out is None:
+        stamp = datetime.now(timezone.utc).strftime("%Y%m%d-%H%M%S-%f")
+        args.out = REPO / "logs" / "experiment" / f"five-arm-{stamp}"
+    args.out = args.out.expanduser().resolve()
+    args.scope = "preflight" if args.preflight_only else "operator" if args.operator_only else "train"
+    p.require(args.report or args.scope != "train" or args.warmup_steps >= 1,
+              "full training needs at least one warm-up step for the per-operator checks")
+    return args
+
+
+def source_files():
+    files = []
+    for path in PACKAGE.rglob("*"):
+        if not path.is_file() or "__pycache__" in path.parts or "_native" in path.parts:
+            continue
+        if path.suffix in (".pyc", ".so", ".o"):
+            continue
+        files.append(path)
+    for name in ("bench.py", "__graft_entry__.py", "README.md", "DESIGN.md"):
+        if (REPO / name).is_file():
+            files.append(REPO / name)
+    return sorted(set(files))
+
+
+def plan_for(args, manifest=None, run_id=None):
+    config = dict(protocol=p.PROTOCOL, run_id=run_id or "PREVIEW", world_size=args.world_size, model=args.model,
+                  timing=dict(warmup_steps=args.warmup_steps, timed_steps=args.steps,
+                              operator_warmup=args.operator_warmup, operator_iterations=args.operator_iters),
+                  seed=1234, token_seed=4321, build_dir=str(args.out / "build"), profile=args.profile,
+                  source_manifest_sha256=p.digest(manifest) if manifest is not None else "PREVIEW",
+                  recommended_image=p.RECOMMENDED_IMAGE, backend=p.BACKEND, calibration=args.calibration,
+                  execution_plan=None, execution_plan_sha256=None)
+    return dict(config=config, scope=args.scope, trials=args.trials, blocks=args.blocks,
+                counterbalanced=p.balanced(args.blocks), schedule=p.orders(args.trials, args.blocks),
+                jobs=p.jobs(args.trials, args.blocks, args.scope))
+
+
+def command_for(python, source_root, directory, job, world):
+    return [python, "-m", "torch.distributed.run", "--standalone", "--nnodes=1", f"--nproc_per_node={world}",
+            "--local-addr", "127.0.0.1", "-m", "tempname_dcu_b200.worker", "--config", str(directory / "config.json"),
+            "--out", str(directory), "--stage", job["stage"], "--arm", job["arm"]]
+
+
+def stop_process(process):
+    """Terminate this controller's worker process group only (SIGTERM, then SIGKILL)."""
+    if process.poll() is not None:
+        return
+    try:
+        os.killpg(process.pid, signal.SIGTERM)
+        process.wait(timeout=10)
+    except ProcessLookupError:
+        pass
+    except subprocess.TimeoutExpired:
+        try:
+            os.killpg(process.pid, signal.SIGKILL)
+        except ProcessLookupError:
+            pass
+        process.wait(timeout=10)
+
+
+def launch(command, directory, source_root, timeout):
+    env = os.environ.copy()
+    env["PYTHONPATH"] = str(source_root)
+    env["PYTHONDONTWRITEBYTECODE"] = "1"
+    env["PYTHONUNBUFFERED"] = "1"
+    env.setdefault("OMP_NUM_THREADS", "1")
+    with (directory / "process.log").open("w") as log:
+        process = subprocess.Popen(command, stdout=log, stderr=subprocess.STDOUT, cwd=source_root, env=env,
+                                   start_new_session=True)
+        try:
+            code = process.wait(timeout=timeout)
+        except BaseException:
+            stop_process(process)
+            raise
+    if code:
+        tail = (directory / "process.log").read_text(errors="replace").splitlines()[-35:]
+        raise RuntimeError(f"worker exited {code}; {directory / 'process.log'}\n" + "\n".join(tail))
+
+
+def execute(args):
+    from . import report as reporting
+    p.require(not args.out.exists(), "output directory exists; use a fresh --out")
+    python = shutil.which(args.python)
+    p.require(python is not None, f"python executable not found: {args.python}")
+    files = source_files()
+    manifest = {str(f.relative_to(REPO)): p.sha(f) for f in files}
+    plan = plan_for(args, manifest=manifest, run_id=uuid.uuid4().hex)
+    args.out.mkdir(parents=True, exist_ok=False)
+    state = dict(protocol=p.PROTOCOL, run_id=plan["config"]["run_id"], status="preparing", completed=False,
+                 scope=args.scope, finished_jobs=0)
+    p.write(args.out / "batch-state.json", state)
+    try:
+        source_root = args.out / "sources"
+        for f in files:
+            dest = source_root / f.relative_to(REPO)
+            dest.parent.mkdir(parents=True, exist_ok=True)
+            shutil.copyfile(f, dest)
+            p.require(p.sha(dest) == manifest[str(f.relative_to(REPO))], "source changed while freezing")
+        # The frozen sources import their own native library: build it once into the snapshot.
+        from ..ops import _build
+        library = _build.build()
+        native_dir = source_root / "tempname_dcu_b200" / "_native"
+        native_dir.mkdir(parents=True, exist_ok=True)
+        shutil.copyfile(library, native_dir / "libtdb.so")
+        shutil.copyfile(_build.MANIFEST, native_dir / "manifest.json")
+        (args.out / "build").mkdir()
+        shutil.copyfile(library, args.out / "build" / "libtdb.so")
+        p.write(args.out / "source-manifest.json", manifest)
+        p.write(args.out / "plan.json", plan)
+        completed = []
+        p.write(args.out / "completed-jobs.json", completed)
+        identities = environment = native = execution_plan = None
+        groups = {}
+        for job in plan["jobs"]:
+            directory = args.out / "results" / job["directory"]
+            directory.mkdir(parents=True, exist_ok=False)
+            job_config = p.config_for_job(plan["config"], job, execution_plan)
+            p.write(directory / "config.json", job_config)
+            command = command_for(python, source_root, directory, job, args.world_size)
+            p.write(directory / "command.json", dict(job=job, command=command, environment={
+                k: v for k, v in os.environ.items()
+                if k.startswith(("NCCL_", "TORCH_NCCL_")) or k in ("CUDA_VISIBLE_DEVICES", "OMP_NUM_THREADS")}))
+            state.update(status="running", active_job=job)
+            p.write(args.out / "batch-state.json", state)
+            print(f"[{job['index'] + 1}/{len(plan['jobs'])}] {job['directory']}", flush=True)
+            launch(command, directory, source_root, args.worker_timeout)
+            rows = p.validate_rows([p.read(directory / f"rank{r}.json") for r in range(args.world_size)], job,
+                                   job_config)
+            env = [r["environment_identity"] for r in rows]
+            p.require(environment is None or env == environment, "hardware/software changed between workers")
+            environment = env
+            built = [r["codec_build"] for r in rows]
+            p.require(native is None or built == native, "native library changed between workers")
+            native = built
+            reporting.validate_artifacts(args.out, directory, rows, job_config)
+            if job["stage"] == "calibrate":
+                p.require(execution_plan is None, "calibration runs once per fresh experiment")
+                execution_plan = p.calibration_from_rows(rows, job_config)
+                reporting.validate_calibration_evidence(args.out, directory, rows, job_config)
+                p.write(args.out / "selection-plan.json", execution_plan)
+                state.update(execution_plan_sha256=p.digest(execution_plan))
+            elif job["stage"] == "train":
+                identity = p.training_identity(rows)
+                p.require(identities is None or identity == identities, "initial weights/input differ across windows")
+                identities = identity
+                group = groups.setdefault((job["trial"], job["block"]), {})
+                group[job["arm"]] = rows
+                for other in p.FULL_TACO_ARMS[1:]:
+                    if "flux_taco" in group and other in group:
+                        p.compare_taco_trajectories(group["flux_taco"], group[other])
+            done = dict(job=job, command_sha256=p.sha(directory / "command.json"),
+                        rank_sha256={f"rank{r}.json": p.sha(directory / f"rank{r}.json")
+                                     for r in range(args.world_size)})
+            if job["stage"] == "calibrate":
+                done.update(execution_plan_sha256=p.digest(execution_plan),
+                            selection_plan_file_sha256=p.sha(args.out / "selection-plan.json"))
+            completed.append(done)
+            p.write(args.out / "completed-jobs.json", completed)
+            state.update(finished_jobs=len(completed))
+            p.write(args.out / "batch-state.json", state)
+        report = reporting.replay(args.out)
+        p.write(args.out / "report.json", report)
+        (args.out / "report.md").write_text(reporting.markdown(report))
+        state.update(status="completed" if args.scope == "train" else args.scope + "_completed", completed=True,
+                     active_job=None, report_sha256=p.sha(args.out / "report.json"),
+                     formal_optimizer_steps=report["formal_optimizer_steps"])
+        p.write(args.out / "batch-state.json", state)
+        print(f"completed scope: {args.scope}\nreport: {args.out / 'report.md'}", flush=True)
+    except BaseException as exc:
+        state.update(status="interrupted" if isinstance(exc, KeyboardInterrupt) else "failed", completed=False,
+                     error=f"{type(exc).__name__}: {exc}")
+        p.write(args.out / "batch-state.json", state)
+        raise
+
+
+def main(argv=None):
+    args = arguments(argv)
+    if args.report:
+        from . import report as reporting
+        print(reporting.markdown(reporting.replay(args.out)))
+    elif args.execute:
+        def terminate(_number, _frame):
+            raise KeyboardInterrupt("received SIGTERM")
+        previous = signal.signal(signal.SIGTERM, terminate)
+        try:
+            execute(args)
+        finally:
+            signal.signal(signal.SIGTERM, previous)
+    else:
+        import json
+        print(json.dumps(dict(preview=True, writes_files=False, uses_gpu=False, output=str(args.out),
+                              **plan_for(args)), ensure_ascii=False, indent=2))
+
+
+if __name__ == "__main__":
+    try:
+        main()
+    except KeyboardInterrupt:
+        print("interrupted; only this controller's worker process group was terminated", file=sys.stderr)
+        raise SystemExit(130)
+    except (ValueError, RuntimeError, OSError, subprocess.TimeoutExpired) as error:
+        print(f"ERROR: {error}", file=sys.stderr)
+        raise SystemExit(1)

@@ -98,6 +98,25 @@ class GPT:
                     self.operators.append(factory(m=self.m, n=self.h, k=k, group=group, arm=arm,
                                                   chunk_rows=c["chunk_rows"], plan=plan))
         self._scratch = {}
+        # Backward reduce-scatters of the column-parallel data gradients
+        # (dX = RS(dY W)) run through the same fused kernel (BF16, ordered)
+        # whenever the forward projections do.
+        self._bwd_rs = {}
+        if factory is not None and self.world > 1:
+            from ..runtime import FluxB200
+            for k in (3 * self.h // self.world, self.f // self.world, self.vocab_local):
+                if k not in self._bwd_rs:
+                    self._bwd_rs[k] = FluxB200(self.m, self.h, k, group, "flux", chunk_rows=c["chunk_rows"],
+                                               b_mn=True)
+
+    def _dgrad_rs(self, dy, weight):
+        """RS(dy @ weight) -> [m/W, h]: fused kernel when available, else
+        GEMM + NCCL reduce-scatter."""
+        from ..ops import gemm as G
+        op = self._bwd_rs.get(dy.shape[1])
+        if op is not None:
+            return op.forward(dy, weight)
+        return self.tp.scatter_sum(G.matmul_nt(dy, weight))
 
     # ------------------------------------------------------------ helpers
     def _buf(self, key, numel, dtype):
@@ -178,10 +197,9 @@ class GPT:
         K.xent_combine(all_stats, self.world, self.m, gstats, row_loss, loss_acc, loss_scale, accumulate=True)
         # ---- backward (starts inside the loss: logits <- dlogits)
         K.xent_grad(logits, targets, self.vocab_start, self.valid_vocab_local, gstats, grad_scale)
-        dlnff = G.matmul_nt(logits, self.P("embedding"))
+        dlnf = self._dgrad_rs(logits, self.P("embedding"))
         G.weight_grad(logits, lnff, self.Gr("embedding"))
         del logits
-        dlnf = self.tp.scatter_sum(dlnff)
         ln_scratch = self._buf("ln_scratch", K.layernorm_scratch_floats(self.ml, self.h), torch.float32)
         dx = K.layernorm_bwd(xl, self.P("final_weight"), meanf, rstdf, dlnf, self.Gr("final_weight"),
                              self.Gr("final_bias"), ln_scratch)
@@ -213,9 +231,8 @@ class GPT:
         G.weight_grad(dyf, h1, self.Gr(p + "fc2_weight"))
         # FC1 (column-parallel)
         self._colsum(dz, p + "fc1_bias")
-        dln2f = G.matmul_nt(dz, self.P(p + "fc1_weight"))
+        dln2 = self._dgrad_rs(dz, self.P(p + "fc1_weight"))
         G.weight_grad(dz, ln2f, self.Gr(p + "fc1_weight"))
-        dln2 = self.tp.scatter_sum(dln2f)
         dx1 = K.layernorm_bwd(x1, self.P(p + "ln2_weight"), mean2, rstd2, dln2, self.Gr(p + "ln2_weight"),
                               self.Gr(p + "ln2_bias"), ln_scratch, dres=dx2)
         # attention out (row-parallel)
@@ -226,9 +243,8 @@ class GPT:
         dqkv = K.attention_bwd(qkv, attn, dattn, lse, c["micro_batch"], c["sequence"], self.heads_local)
         # QKV (column-parallel)
         self._colsum(dqkv, p + "qkv_bias")
-        dln1f = G.matmul_nt(dqkv, self.P(p + "qkv_weight"))
+        dln1 = self._dgrad_rs(dqkv, self.P(p + "qkv_weight"))
         G.weight_grad(dqkv, ln1f, self.Gr(p + "qkv_weight"))
-        dln1 = self.tp.scatter_sum(dln1f)
         return K.layernorm_bwd(x, self.P(p + "ln1_weight"), mean1, rstd1, dln1, self.Gr(p + "ln1_weight"),
                                self.Gr(p + "ln1_bias"), ln_scratch, dres=dx1)
 

@@ -1,0 +1,114 @@
+"""Operator benchmark of the fused GEMM + reduce-scatter against GEMM + NCCL.
+
+    python -m torch.distributed.run --nproc-per-node N -m tempname_dcu_b200.ops.opbench [--iters 50]
+
+For each role of GPT-6.7B (attention-out K = h/N, FC2 K = f/N; M = 2048,
+N = 4096) and each arm, times the fused kernel and the unfused baseline
+(tcgen05 GEMM, then NCCL reduce_scatter_tensor, then bias + residual) with
+CUDA events, max over ranks, and reports the fraction of the fused path's
+roofline: max(FLOPs / measured bf16 peak, remote bytes sent per rank / 770
+GB/s NVLink peer bandwidth).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+from pathlib import Path
+
+NVLINK_GBS = 770.0
+
+
+def _peak():
+    path = Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+    if path.is_file():
+        return json.loads(path.read_text()).get("bf16_tflops", 1590.0), "measured"
+    return 1590.0, "fallback"
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--arms", default="all")
+    args = ap.parse_args(argv)
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    group = dist.group.WORLD
+    from ..mapping import ARMS, wire_bytes
+    from ..planning import make_role
+    from ..runtime import FluxB200, shutdown_context
+    from . import gemm as G
+    from . import kernels as K
+    from . import native
+    peak, source = _peak()
+    m, n, chunk = 2048, 4096, 128
+    arms = ARMS if args.arms == "all" else tuple(args.arms.split(","))
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        t = torch.tensor(s.elapsed_time(e) / args.iters * 1000.0, dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    rows = []
+    for role, k in (("attn", 4096 // world), ("mlp", 16384 // world)):
+        gen = torch.Generator(device="cuda").manual_seed(7 + rank)
+        x = torch.randn((m, k), generator=gen, device="cuda").to(torch.bfloat16)
+        w = (torch.randn((n, k), generator=gen, device="cuda") / math.sqrt(k)).to(torch.bfloat16)
+        bias = torch.zeros(n, device="cuda", dtype=torch.bfloat16)
+        res = torch.zeros(m // world, n, device="cuda", dtype=torch.bfloat16)
+        partial = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        rs_out = torch.empty(m // world, n, device="cuda", dtype=torch.bfloat16)
+
+        def baseline():
+            G.linear(x, w, out=partial)
+            dist.reduce_scatter_tensor(rs_out, partial)
+            K.bias_residual(rs_out, bias, res, out=rs_out)
+        base_us = timed(baseline)
+        gemm_us = timed(lambda: G.linear(x, w, out=partial))
+        flops = 2.0 * m * n * k
+        compute_us = flops / (peak * 1e12) * 1e6
+        for arm in arms:
+            plan = make_role(m, n, k, world, chunk) if arm in ARMS[3:] else None
+            op = FluxB200(m, n, k, group, arm, chunk_rows=chunk, plan=plan)
+            us = timed(lambda: op.forward(x, w, bias, res))
+            op.enable_phase_profile(True)
+            op.forward(x, w, bias, res)
+            torch.cuda.synchronize()
+            phases = op.phase_summary()
+            op.enable_phase_profile(False)
+            quant = op.quantized
+            link_us = wire_bytes(m, n, world, quant) / (NVLINK_GBS * 1e9) * 1e6
+            roof = max(compute_us, link_us)
+            rows.append(dict(role=role, arm=arm, world=world, m=m, n=n, k=k, fused_us=round(us, 2),
+                             gemm_plus_nccl_rs_us=round(base_us, 2), gemm_only_us=round(gemm_us, 2),
+                             speedup_vs_nccl=round(base_us / us, 3), roofline_us=round(roof, 2),
+                             roofline_fraction=round(roof / us, 3), bound="link" if link_us > compute_us else "compute",
+                             wire_bytes_per_rank=wire_bytes(m, n, world, quant), peak_source=source,
+                             phases=phases))
+    native.raise_on_status()
+    if rank == 0:
+        for r in rows:
+            print(json.dumps(r), flush=True)
+    shutdown_context(group)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -36,7 +36,7 @@ native.register("tdb_gemm_rs", [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p
                                 ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int, ctypes.c_uint, ctypes.c_void_p,
                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                 ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_double,
-                                ctypes.c_void_p])
+                                ctypes.c_void_p, ctypes.c_void_p])
 native.register("tdb_gemm_rs_signals_per_block", [ctypes.c_int, ctypes.c_int, ctypes.c_int])
 
 _CONTEXTS = {}
@@ -169,6 +169,8 @@ class FluxB200:
         self.validate_next_call = False
         self.events = []
         self._last = None
+        # optional per-CTA phase stamps (globaltimer): [grid, 4]
+        self.phase_buffer = None
         # delay target: first tile (in production order) of the first lane-0 block
         first0 = next((it for it in self.order if it["lane"] == 0), None)
         n_tiles = n // self.bn
@@ -215,7 +217,8 @@ class FluxB200:
                 0 if residual is None else residual.data_ptr(), self.consume.data_ptr(),
                 1 if self.consumer_policy == "per_lane_ready" else 0,
                 0 if timeline is None else timeline.data_ptr(), delay, self._delay_tile[0], self._delay_tile[1],
-                PEER_WAIT_SECONDS, native.stream_ptr()), "fused gemm_rs")
+                PEER_WAIT_SECONDS, 0 if self.phase_buffer is None else self.phase_buffer.data_ptr(),
+                native.stream_ptr()), "fused gemm_rs")
             self._last = (set_, expected, timeline)
             self.calls += 1
             ctx.calls += 1
@@ -233,6 +236,28 @@ class FluxB200:
             ctx.submission_lock.release()
 
     __call__ = forward
+
+    def enable_phase_profile(self, on=True):
+        """Record per-CTA {start, produce done, first block ready, end} device
+        timestamps of every following call (diagnostics only)."""
+        import torch
+        self.phase_buffer = torch.zeros((1024, 4), dtype=torch.int64, device=self.device) if on else None
+
+    def phase_summary(self):
+        """Mean/max over CTAs of produce, wait and consume durations (us) of the last call."""
+        import torch
+        t = self.phase_buffer.cpu().double()
+        prod = t[t[:, 0] > 0]
+        cons = t[t[:, 2] > 0]
+        produce = (prod[:, 1] - prod[:, 0]) / 1e3
+        end_of_produce = prod[:, 1].max()
+        wait = (cons[:, 2] - end_of_produce).clamp_min(0) / 1e3
+        consume = (cons[:, 3] - cons[:, 2]) / 1e3
+        total = (t[:, 3].max() - prod[:, 0].min()).item() / 1e3
+        return dict(ctas=int(prod.shape[0]), kernel_span_us=round(total, 2),
+                    produce_mean_us=round(produce.mean().item(), 2), produce_max_us=round(produce.max().item(), 2),
+                    wait_mean_us=round(wait.mean().item(), 2), wait_max_us=round(wait.max().item(), 2),
+                    consume_mean_us=round(consume.mean().item(), 2), consume_max_us=round(consume.max().item(), 2))
 
     # ---------------------------------------------------- validation hooks
     def _slot_view(self, set_, source, within, nbytes, dtype, shape):

@@ -80,15 +80,20 @@ def validate_operator_buffers(op, input_, weight, output):
     good = torch.ones((), dtype=torch.bool, device=device)
     details = []
     finite_checked = packets_checked = 0
+    verdicts = []
     try:
         for name, tensor in [("input", input_), ("weight", weight), ("output", output),
                              *op.validation_tensors()]:
             if not isinstance(tensor, torch.Tensor) or tensor.dtype != torch.bfloat16 or not tensor.is_cuda:
                 raise ValueError(f"invalid BF16 tensor in validation: {name}")
-            good = good & torch.isfinite(tensor).all()
+            ok = torch.isfinite(tensor).all()
+            verdicts.append((name, ok))
+            good = good & ok
             finite_checked += 1
         for name, packet, elements in op.validation_packets():
-            good = good & packet_tensor_valid(packet, elements)
+            ok = packet_tensor_valid(packet, elements)
+            verdicts.append((name, ok))
+            good = good & ok
             packets_checked += 1
     except (ValueError, TypeError, KeyError, IndexError) as exc:
         good = torch.zeros((), dtype=torch.bool, device=device)
@@ -97,6 +102,12 @@ def validate_operator_buffers(op, input_, weight, output):
     if dist.is_initialized() and op.world > 1:
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=op.group)
     if int(flag.item()) != 1:
+        bad = [name for name, ok in verdicts if not bool(ok.item())]
+        if bad:
+            details.append("failing here: " + ", ".join(bad[:8]))
+            import sys
+            print(f"[validation rank {dist.get_rank() if dist.is_initialized() else 0}] non-finite or invalid: "
+                  f"{bad[:8]}", file=sys.stderr, flush=True)
         raise RuntimeError("full-buffer finite/packet validation failed on at least one rank"
                            + (": " + "; ".join(details) if details else ""))
     return dict(passed=True, finite_tensors_checked=finite_checked, packets_checked=packets_checked,
