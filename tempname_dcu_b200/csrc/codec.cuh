@@ -14,6 +14,8 @@
 // 4L..4L+3.  Butterfly strides 1 and 2 stay inside a thread; strides 4..64
 // are lane-xor shuffles with masks 1..16.
 #pragma once
+#include <string.h>
+
 #include "common.cuh"
 
 namespace tdb {
@@ -31,19 +33,29 @@ __device__ __forceinline__ uint16_t e4m3x2(float lo, float hi) {
   return r;
 }
 
+__host__ __device__ __forceinline__ float bits_as_float(uint32_t u) {
+#ifdef __CUDA_ARCH__
+  return __uint_as_float(u);
+#else
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+#endif
+}
+
 // E4M3FN code -> fp32 (exact).  0x7f / 0xff are NaN in E4M3FN.
-__device__ __forceinline__ float e4m3_to_float(uint32_t code) {
+__host__ __device__ __forceinline__ float e4m3_to_float(uint32_t code) {
   const uint32_t mag = code & 0x7fu;
   float v;
   if (mag == 0x7fu) {
-    v = __uint_as_float(0x7fc00000u);
+    v = bits_as_float(0x7fc00000u);
   } else if (mag < 8u) {
     v = float(mag) * 0.001953125f;  // subnormal: mag * 2^-9
   } else {
     // normal: exponent field e = mag>>3 (bias 7), mantissa m = mag&7
     // value = (1 + m/8) * 2^(e-7) -> build the fp32 bit pattern directly
     const uint32_t e = (mag >> 3) + 120u;  // 127 - 7
-    v = __uint_as_float((e << 23) | ((mag & 7u) << 20));
+    v = bits_as_float((e << 23) | ((mag & 7u) << 20));
   }
   return (code & 0x80u) ? -v : v;
 }

@@ -119,6 +119,23 @@ def receive_bytes(m, n, chunk_rows):
     return 2 * (m // chunk_rows) * chunk_rows * n * 2
 
 
+def operator_layout(m, n, k, world, rank, arm, plan=None, chunk_rows=128, bn=256):
+    """Pure (CPU) description of one fused call: production schedule, wire
+    format per physical block, the device tile table, this rank's
+    consumption order and the number of counter signals per (block, source).
+    Every rank derives the same tables from the same arguments."""
+    order = schedule(m, n, k, world, chunk_rows, arm, plan)
+    mask = block_selection(m, n, k, world, chunk_rows, arm, plan)
+    tiles = tile_table(m, n, world, chunk_rows, arm, plan, block_m=128, block_n=bn, k=k)
+    consume = [item["within"] for item in order if item["destination"] == rank]
+    signals = (chunk_rows // 128) * (n // bn) * 4
+    first0 = next((item for item in order if item["lane"] == 0), None)
+    delay_tile = (first0["row"] // 128, 0) if first0 else (-1, -1)
+    return dict(order=order, selection_mask=mask, tiles=tiles, consume=consume, signals=signals,
+                per=m // world // chunk_rows, delay_tile=delay_tile,
+                consumer_policy="per_lane_ready" if arm in ARRIVAL_ARMS else "ordered")
+
+
 class FluxB200:
     """Fused GEMM + reduce-scatter for one projection shape and arm."""
 
