@@ -7,6 +7,7 @@
 // backward, residual adds and fp32 weight-gradient accumulation
 // (model.py:401-408) are fused into the epilogue instead of separate kernels.
 #include "gemm.cuh"
+#include "gemm2.cuh"
 #include "tensor_map.h"
 
 namespace tdb {
@@ -184,6 +185,76 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, in
   return int(cudaGetLastError());
 }
 
+// ---------------------------------------------------------------------------
+// 2-CTA (cta_group::2) path: 256 x 256 tiles on SM pairs.
+// ---------------------------------------------------------------------------
+constexpr int k2Stages = 6;
+
+template <bool A_MN, bool B_MN, int MODE>
+__global__ void __launch_bounds__(gemm2::kThreads, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int K,
+                 TileOrder order, EpiParams ep, int* status) {
+  PlainEpi<MODE> epi{ep};
+  gemm2::mainloop<A_MN, B_MN, PlainEpi<MODE>, k2Stages>(&tmA, &tmB, K, order, epi, status);
+}
+
+template <bool A_MN, bool B_MN, int MODE>
+static int launch2(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiParams& ep,
+                   cudaStream_t stream) {
+  using Cfg = gemm2::Config<k2Stages>;
+  auto kern = gemm2_kernel<A_MN, B_MN, MODE>;
+  static int max_clusters[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(gemm2::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!max_clusters[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm2: cudaFuncSetAttribute failed");
+    cfg.gridDim = dim3(2 * tdb_host::sm_count() / 2);
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess || n <= 0) return tdb_host::fail(int(e), "gemm2: no active 2-CTA clusters possible");
+    max_clusters[dev & 63] = n;
+  }
+  TileOrder order;
+  order.num_m = (M + 255) / 256;
+  order.num_n = (N + 255) / 256;
+  order.group_m = 8;
+  order.table = nullptr;
+  order.num_tiles = order.num_m * order.num_n;
+  const int clusters = order.num_tiles < max_clusters[dev & 63] ? order.num_tiles : max_clusters[dev & 63];
+  cfg.gridDim = dim3(2 * clusters);
+  int* status = tdb_host::status_ptr();
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, K, order, ep, status);
+  tdb_host::launched(1);
+  if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm2: launch failed");
+  return 0;
+}
+
+template <bool A_MN, bool B_MN>
+static int dispatch2(int mode, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                     const EpiParams& ep, cudaStream_t s) {
+  switch (mode) {
+    case kStore: return launch2<A_MN, B_MN, kStore>(ta, tb, M, N, K, ep, s);
+    case kBias: return launch2<A_MN, B_MN, kBias>(ta, tb, M, N, K, ep, s);
+    case kBiasGelu: return launch2<A_MN, B_MN, kBiasGelu>(ta, tb, M, N, K, ep, s);
+    case kGeluBwd: return launch2<A_MN, B_MN, kGeluBwd>(ta, tb, M, N, K, ep, s);
+    case kAccF32: return launch2<A_MN, B_MN, kAccF32>(ta, tb, M, N, K, ep, s);
+    case kBiasResidual: return launch2<A_MN, B_MN, kBiasResidual>(ta, tb, M, N, K, ep, s);
+  }
+  return tdb_host::fail(int(cudaErrorInvalidValue), "unknown epilogue mode %d", mode);
+}
+
 template <int BN, bool A_MN, bool B_MN>
 static int dispatch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
                          const EpiParams& ep, cudaStream_t s) {
@@ -241,14 +312,19 @@ TDB_API int tdb_gemm(const void* A, int a_mn, int64_t lda, const void* B, int b_
   if (bn == 0) {
     const int sms = tdb_host::sm_count();
     const int tiles256 = ((M + 127) / 128) * ((N + 255) / 256);
-    bn = (tiles256 >= sms || N <= 128) ? 256 : 128;
+    const int pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+    if (M >= 256 && N >= 256 && pair_tiles >= sms / 2 && K >= 256)
+      bn = 512;  // 2-CTA 256 x 256 tiles
+    else
+      bn = (tiles256 >= sms || N <= 128) ? 256 : 128;
     if (N <= 128) bn = 128;
   }
-  if (bn != 128 && bn != 256) return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: bn must be 128 or 256");
+  if (bn != 128 && bn != 256 && bn != 512)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: bn must be 128, 256 or 512 (2-CTA)");
   CUtensorMap ta, tb;
   int rc = make_operand_map(&ta, A, a_mn, M, K, lda, BM);
   if (rc) return rc;
-  rc = make_operand_map(&tb, B, b_mn, N, K, ldb, bn);
+  rc = make_operand_map(&tb, B, b_mn, N, K, ldb, bn == 512 ? 128 : bn);
   if (rc) return rc;
   EpiParams ep;
   ep.C = C;
@@ -262,6 +338,12 @@ TDB_API int tdb_gemm(const void* A, int a_mn, int64_t lda, const void* B, int b_
   ep.alpha = alpha;
   ep.beta = beta;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bn == 512) {
+    if (!a_mn && !b_mn) return dispatch2<false, false>(mode, ta, tb, M, N, K, ep, s);
+    if (!a_mn && b_mn) return dispatch2<false, true>(mode, ta, tb, M, N, K, ep, s);
+    if (a_mn && b_mn) return dispatch2<true, true>(mode, ta, tb, M, N, K, ep, s);
+    return dispatch2<true, false>(mode, ta, tb, M, N, K, ep, s);
+  }
   if (bn == 256) return dispatch_major<256>(a_mn, b_mn, mode, ta, tb, M, N, K, ep, s);
   return dispatch_major<128>(a_mn, b_mn, mode, ta, tb, M, N, K, ep, s);
 }

@@ -97,3 +97,43 @@ def test_large_k_and_many_tiles(cuda):
     w = torch.randn(4096, 4096, device=cuda).to(torch.bfloat16)
     y = g.linear(x, w)
     assert _rel(y, x.float() @ w.float().t()) < 5e-3
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 320), (600, 520, 200), (2048, 4096, 1024)])
+def test_two_cta_tiles_all_layouts(cuda, a_mn, b_mn, M, N, K):
+    """cta_group::2 (SM-pair) 256x256 tiles, requested with bn=512."""
+    import torch
+    from tempname_dcu_b200.ops import gemm as g
+    torch.manual_seed(6)
+    A = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    B = torch.randn(N, K, device=cuda).to(torch.bfloat16)
+    a = A.t().contiguous() if a_mn else A
+    b = B.t().contiguous() if b_mn else B
+    ref = A.float() @ B.float().t()
+    if a_mn:
+        out = g.gemm(a, b, a_mn=True, b_mn=b_mn, mode=g.ACC_F32, bn=512)
+        assert _rel(out, ref) < 2e-3
+    else:
+        out = g.gemm(a, b, a_mn=a_mn, b_mn=b_mn, bn=512)
+        assert _rel(out, ref) < 5e-3
+    from tempname_dcu_b200.ops import native
+    assert native.read_status()[0] == 0
+
+
+def test_two_cta_fused_epilogues(cuda):
+    import torch
+    import torch.nn.functional as F
+    from tempname_dcu_b200.ops import gemm as g
+    torch.manual_seed(7)
+    M, N, K = 512, 1024, 512
+    x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda) / 16).to(torch.bfloat16)
+    b = torch.randn(N, device=cuda).to(torch.bfloat16)
+    res = torch.randn(M, N, device=cuda).to(torch.bfloat16)
+    z_ref = x.float() @ w.float().t() + b.float()
+    pre = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    act = g.gemm(x, w, mode=g.BIAS_GELU, bias=b, aux_out=pre, bn=512)
+    assert _rel(pre, z_ref) < 5e-3 and _rel(act, F.gelu(pre.float())) < 5e-3
+    out = g.gemm(x, w, mode=g.BIAS_RESIDUAL, bias=b, aux=res, bn=512)
+    assert _rel(out, z_ref + res.float()) < 5e-3
