@@ -219,7 +219,7 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
       if (!ok) { *abort_flag = 1; break; }
       tc_fence_after();
       epi.tile_begin(mb, nb);
-#pragma unroll
+#pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + (uint32_t(quarter * 32) << 16) + b * BN + c * 32, r);

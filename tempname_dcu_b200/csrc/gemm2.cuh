@@ -252,7 +252,7 @@ __device__ __forceinline__ void mainloop(const CUtensorMap* tmA, const CUtensorM
       if (!ok) { *abort_flag = 1; break; }
       tc_fence_after();
       epi.tile_begin(mb, nt);
-#pragma unroll
+#pragma unroll 1
       for (int c = 0; c < kTileN / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + (uint32_t(quarter * 32) << 16) + b * kTileN + c * 32, r);

@@ -161,6 +161,12 @@ struct PushEpi {
 
   __device__ __forceinline__ void set_smem(uint8_t* ptr) { stage_base = ptr; }
 
+  template <int Q>
+  __device__ __forceinline__ void stash(const uint32_t (&r)[32]) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) grp[Q * 32 + j] = bf16_bits_to_float(float_to_bf16_bits(__uint_as_float(r[j])));
+  }
+
   __device__ __forceinline__ uint8_t* stage() const { return stage_base + ((threadIdx.x >> 5) & 3) * 32 * kRowBytes; }
 
   __device__ __forceinline__ static int swz(int row, int chunk) { return chunk ^ (row & (kChunks - 1)); }
@@ -191,9 +197,14 @@ struct PushEpi {
       return;
     }
     // TACO: gather the 128-column group (4 chunks) in registers, BF16 rounded.
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      grp[(c & 3) * 32 + j] = bf16_bits_to_float(float_to_bf16_bits(__uint_as_float(r[j])));
+    // The chunk index is a runtime value (the epilogue loop is not unrolled),
+    // so dispatch to a compile-time register offset.
+    switch (c & 3) {
+      case 0: stash<0>(r); break;
+      case 1: stash<1>(r); break;
+      case 2: stash<2>(r); break;
+      default: stash<3>(r); break;
+    }
     if ((c & 3) == 3) {
       uint32_t words[32];
       float q, a;
@@ -202,8 +213,13 @@ struct PushEpi {
 #pragma unroll
       for (int i = 0; i < 8; ++i)
         srow[swz(lane, gi * 8 + i)] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
-      qs[gi] = q;
-      as_[gi] = a;
+      if (gi == 0) {
+        qs[0] = q;
+        as_[0] = a;
+      } else if (BN / 128 > 1) {
+        qs[BN / 128 - 1] = q;
+        as_[BN / 128 - 1] = a;
+      }
     }
   }
 
