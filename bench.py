@@ -31,7 +31,7 @@ import threading
 import time
 
 METRIC = "GPT-6.7B TP8 train tokens/s (max over ranks) at 1/2/4/8 B200; fused-op roofline %"
-# Best published predecessor number (MA11, 8xH100, GPT-6.7B TP8).
+# Best published predecessor number: MA11 on 8xH100, GPT-6.7B TP8, train tokens/s.
 BASELINE_TOKENS_PER_S = 18177.69
 
 
@@ -241,7 +241,7 @@ def main():
                         tokens_per_step=tokens_per_step, arm=args.arm if args.impl == "ours" else None,
                         l2="inputs larger than L2 (13 GB of bf16 weights streamed per step); no flush",
                         model_tflops_per_gpu=round(flops / (ms_per_step / 1000.0) / world / 1e12, 1),
-                        baseline_ref="BASELINE.md row 10 (MA11, 8xH100): 18177.69 tok/s",
+                        baseline_ref="published MA11 (8xH100, GPT-6.7B TP8): 18177.69 tok/s",
                         final_loss=final_loss, e2e_last_loss=loss_value),
             clocks=clocks,
             e2e=dict(value=round(tokens_per_step * 1000.0 / e2e_ms, 2), unit="tokens/s",

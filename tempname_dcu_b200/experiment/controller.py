@@ -97,7 +97,7 @@ def source_files():
         if path.suffix in (".pyc", ".so", ".o"):
             continue
         files.append(path)
-    for name in ("bench.py", "__graft_entry__.py", "README.md", "DESIGN.md"):
+    for name in ("bench.py", "__graft_entry__.py", "README.md"):
         if (REPO / name).is_file():
             files.append(REPO / name)
     return sorted(set(files))

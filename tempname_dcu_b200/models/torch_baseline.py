@@ -99,7 +99,7 @@ class BaselineTrainer:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         c = self.config = validate_config(config, self.world)
-        self.device = torch.device(device, torch.cuda.current_device())
+        self.device = torch.device("cpu") if device == "cpu" else torch.device(device, torch.cuda.current_device())
         h, f, L, W = c["hidden"], c["ffn"], c["layers"], self.world
         gen = torch.Generator(device=self.device).manual_seed(seed + 1000003 * self.rank)
 
@@ -121,12 +121,15 @@ class BaselineTrainer:
                                     fc1_w=p((f // W, h)), fc1_b=p((f // W,), fill=0.0),
                                     fc2_w=p((h, f // W), 0.02 / math.sqrt(2 * L)), fc2_b=p((h,), fill=0.0)))
         self.all = list(self.params.values()) + [v for layer in self.layers for v in layer.values()]
+        replicated = {"position", "final_w", "final_b", "ln1_w", "ln1_b", "ln2_w", "ln2_b", "attn_b", "fc2_b"}
+        names = list(self.params) + [k for layer in self.layers for k in layer]
+        self.replicated = [n in replicated for n in names]
         self.masters = [torch.nn.Parameter(q.detach().float().clone()) for q in self.all]
         decay = [m for q, m in zip(self.all, self.masters) if q.ndim >= 2]
         no_decay = [m for q, m in zip(self.all, self.masters) if q.ndim < 2]
         self.opt = torch.optim.AdamW([dict(params=decay, weight_decay=c["weight_decay"]),
                                       dict(params=no_decay, weight_decay=0.0)], lr=c["learning_rate"],
-                                     betas=(0.9, 0.95), eps=1e-8, fused=True)
+                                     betas=(0.9, 0.95), eps=1e-8, fused=self.device.type == "cuda")
 
     def _forward(self, tokens, targets):
         torch, F, c, W, g = self.torch, self.F, self.config, self.world, self.group
@@ -162,7 +165,7 @@ class BaselineTrainer:
 
     def step(self, tokens, labels):
         torch, c = self.torch, self.config
-        if tokens.device.type != "cuda":
+        if tokens.device != self.device:
             tokens, labels = tokens.to(self.device, non_blocking=True), labels.to(self.device, non_blocking=True)
         accum = c["accumulation_steps"]
         loss_sum = torch.zeros((), device=self.device)
@@ -176,18 +179,20 @@ class BaselineTrainer:
                 if mstr.grad is None:
                     mstr.grad = q.grad.float()
                 else:
-                    mstr.grad.add_(q.grad)
+                    mstr.grad.add_(q.grad.float())
                 q.grad = None
-        if self.world > 1:
-            for q, mstr in zip(self.all, self.masters):
-                if q.ndim < 2 and q.shape[0] == c["hidden"] or q is self.params["position"]:
-                    self.dist.all_reduce(mstr.grad, group=self.group)
         grads = [mstr.grad for mstr in self.masters]
-        norm = torch.linalg.vector_norm(torch.stack([torch.linalg.vector_norm(x.float()) for x in grads]))
+        rep = [g for g, r in zip(grads, self.replicated) if r]
+        shard = [g for g, r in zip(grads, self.replicated) if not r]
         if self.world > 1:
-            sq = norm.double() ** 2
+            flat = torch.cat([g.reshape(-1) for g in rep])
+            self.dist.all_reduce(flat, group=self.group)
+            torch._foreach_copy_(rep, [x.view_as(g) for x, g in zip(flat.split([g.numel() for g in rep]), rep)])
+        sq = torch.stack([torch.linalg.vector_norm(x).double() ** 2 for x in shard]).sum()
+        if self.world > 1:
             self.dist.all_reduce(sq, group=self.group)
-            norm = sq.sqrt()
+        sq = sq + torch.stack([torch.linalg.vector_norm(x).double() ** 2 for x in rep]).sum()
+        norm = sq.sqrt()
         coef = (c["max_grad_norm"] / (norm + 1e-6)).clamp(max=1.0).float()
         torch._foreach_mul_(grads, coef)
         self.opt.step()
