@@ -1,0 +1,375 @@
+// Causal flash attention forward on the 5th-generation tensor cores
+// (tcgen05.mma + TMEM accumulators + TMA), head_dim 128, bf16 in / fp32 acc.
+//
+// Reference parity: python/flux_dcu/model.py:250-256 (causal SDPA over the
+// local heads, no dropout).  Same I/O contract as the mma.sync kernel in
+// attention.cu: qkv [tokens, 3, Hl, 128] (row stride ld), out [tokens, Hl,
+// 128] (row stride ld_out), lse [mb, Hl, seq] = m + log2(l) of the scores
+// scaled by scale*log2(e).
+//
+// One CTA = 128 queries of one (batch, head); key/value tiles of 128.
+//   warp 0      TMA producer: Q once, then K/V tiles through a 3-slot ring in
+//               exactly the order the MMA warp consumes them
+//               (K0, K1, V0, K2, V1, K3, ...); allocates 512 TMEM columns
+//   warp 1      MMA issuer (one thread):  S_j = Q K_j^T into TMEM S[j%2]
+//               (double-buffered, so S_{j+1} overlaps softmax j), then
+//               O += P_j V_j into the TMEM O accumulator
+//   warps 2..5  softmax: thread = one query row (TMEM lane), so row max and
+//               row sum need no shuffles.  P_j (bf16) goes to shared memory
+//               in the SW128 K-major layout the MMA reads.  The running max
+//               is only raised when it grows by more than 2^8 (exact: P <= 256
+//               stays representable, O and l use the same stale max), so the
+//               O correction (tcgen05.ld/st of the accumulator) is rare.
+// TMEM columns: S0 [0,128), S1 [128,256), O [256,384).
+// All waits are bounded (common.cuh); there is no TMA multicast.
+#include "common.cuh"
+#include "tensor_map.h"
+
+namespace tdb {
+namespace attn_tc {
+
+constexpr int BM = 128, BN = 128, D = 128;
+constexpr int kThreads = 192;
+constexpr int kBox = 128 * 128;  // one [128 rows][64 bf16] SW128 box = 16 KB
+constexpr int kTile = 2 * kBox;  // a 128 x 128 bf16 tile = two boxes
+constexpr int kSlots = 3;
+constexpr int kTmemCols = 512;
+constexpr int kOCol = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescale = 8.0f;  // raise the running max only past 2^8 growth
+
+struct alignas(8) Bars {
+  uint64_t q_full;
+  uint64_t kv_full[kSlots];
+  uint64_t kv_empty[kSlots];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t pv_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+constexpr int kSmem = kTile + kSlots * kTile + 2 * kTile + 1024 + 256;
+static_assert(kSmem <= 232448, "shared memory budget");
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// Generic-proxy shared-memory writes -> visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// K-major SW128 operand spanning two 64-column boxes: K step k (16 elements).
+__device__ __forceinline__ uint64_t desc_k(uint32_t base, int k) {
+  return smem_desc_sw128(base + (k >> 2) * kBox + (k & 3) * 32, 16, 1024);
+}
+// MN-major SW128 operand (V: [128 keys][128 d], d contiguous, two 64-column
+// boxes 16 KB apart): K step k = 16 key rows.
+__device__ __forceinline__ uint64_t desc_mn(uint32_t base, int k) {
+  return smem_desc_sw128(base + k * 16 * 128, kBox, 1024);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fwd_kernel(const __grid_constant__ CUtensorMap tm, uint16_t* __restrict__ out, int64_t ld_out,
+               float* __restrict__ lse, int seq, int Hl, int mb, float scale, int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + kTile;
+  uint8_t* sP = sKV + kSlots * kTile;
+  Bars* bars = reinterpret_cast<Bars*>(sP + 2 * kTile);
+
+  const int hb = blockIdx.x;  // (head, batch) fastest: all heads of the heaviest query tile launch first
+  const int h = hb % Hl, b = hb / Hl;
+  const int nq = seq / BM;
+  const int qb = nq - 1 - int(blockIdx.y);
+  const int n = qb + 1;  // causal: key tiles 0..qb
+  const int row0 = b * seq;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&bars->kv_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->p_full[i], 4);
+    }
+    mbar_init(&bars->pv_done, 1);
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+    if (lane == 0) prefetch_tmap(&tm);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  volatile int* abort_flag = &bars->abort_flag;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      mbar_arrive_expect_tx(&bars->q_full, kTile);
+      tma_load_2d(sQ, &tm, &bars->q_full, h * D, row0 + qb * BM);
+      tma_load_2d(sQ + kBox, &tm, &bars->q_full, h * D + 64, row0 + qb * BM);
+      const int total = 2 * n;
+      int i = 0;
+      bool ok = true;
+      for (; i < total && ok; ++i) {
+        // item i of the consumption order K0, K1, V0, K2, V1, K3, ..., V_{n-1}
+        bool is_v;
+        int j;
+        if (n == 1) {
+          is_v = i == 1;
+          j = 0;
+        } else if (i < 2) {
+          is_v = false;
+          j = i;
+        } else {
+          const int t = i - 2;  // V_{t/2} (even t) then K_{t/2+2} (odd t) while K tiles remain
+          const int k_left = n - 2;
+          if (t < 2 * k_left) {
+            is_v = (t & 1) == 0;
+            j = is_v ? t >> 1 : (t >> 1) + 2;
+          } else {
+            is_v = true;
+            j = t - k_left;
+          }
+        }
+        const int s = i % kSlots;
+        const uint32_t round = i / kSlots;
+        if (!mbar_wait(&bars->kv_empty[s], (round & 1) ^ 1, status, 60)) { ok = false; *abort_flag = 1; break; }
+        if (*abort_flag) { ok = false; break; }
+        uint8_t* dst = sKV + s * kTile;
+        const int col = (is_v ? 2 * Hl + h : Hl + h) * D;
+        mbar_arrive_expect_tx(&bars->kv_full[s], kTile);
+        tma_load_2d(dst, &tm, &bars->kv_full[s], col, row0 + j * BN);
+        tma_load_2d(dst + kBox, &tm, &bars->kv_full[s], col + 64, row0 + j * BN);
+      }
+      // Never leave a copy in flight: wait (bounded) for Q and the last loads.
+      mbar_wait(&bars->q_full, 0, status, 61);
+      if (!ok)
+        for (int k = (i >= kSlots ? i - kSlots : 0); k < i; ++k)
+          mbar_wait(&bars->kv_full[k % kSlots], (k / kSlots) & 1, status, 62);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idS = idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idO = idesc_bf16(BM, D, false, true);
+      bool ok = mbar_wait(&bars->q_full, 0, status, 70);
+      bool issued = false;
+      uint32_t it = 0;
+      const uint32_t sq = smem_u32(sQ);
+      auto next_slot = [&](uint32_t& addr) -> bool {
+        const int s = it % kSlots;
+        if (!mbar_wait(&bars->kv_full[s], (it / kSlots) & 1, status, 71)) return false;
+        if (*abort_flag) return false;
+        tc_fence_after();
+        addr = smem_u32(sKV + s * kTile);
+        return true;
+      };
+      auto issue_s = [&](int j) -> bool {
+        uint32_t sk;
+        if (!next_slot(sk)) return false;
+        const uint32_t d = tmem + (j & 1) * BN;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_f16_ss(d, desc_k(sq, k), desc_k(sk, k), idS, k > 0 ? 1u : 0u);
+        umma_commit(&bars->kv_empty[it % kSlots]);
+        umma_commit(&bars->s_full[j & 1]);
+        ++it;
+        issued = true;
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        if (!mbar_wait(&bars->p_full[j & 1], (j >> 1) & 1, status, 72)) return false;
+        tc_fence_after();
+        uint32_t sv;
+        if (!next_slot(sv)) return false;
+        const uint32_t sp = smem_u32(sP + (j & 1) * kTile);
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k)
+          umma_f16_ss(tmem + kOCol, desc_k(sp, k), desc_mn(sv, k), idO, (j | k) != 0 ? 1u : 0u);
+        umma_commit(&bars->kv_empty[it % kSlots]);
+        umma_commit(&bars->pv_done);
+        ++it;
+        issued = true;
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && n > 1) ok = issue_s(1);
+      for (int j = 0; j < n && ok; ++j) {
+        ok = issue_pv(j);
+        if (ok && j + 2 < n) ok = issue_s(j + 2);
+      }
+      if (!ok) *abort_flag = 1;
+      if (issued) {
+        umma_commit(&bars->drain);
+        mbar_wait(&bars->drain, 0, status, 73);
+      }
+    }
+  } else {
+    // ---------------- softmax / correction / epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row within the tile (= TMEM lane)
+    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const float sl2 = scale * kLog2e;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    const uint32_t prow_sw = uint32_t(r & 7);
+    for (int j = 0; j < n && ok; ++j) {
+      if (!mbar_wait(&bars->s_full[j & 1], (j >> 1) & 1, status, 80)) { ok = false; break; }
+      if (*abort_flag) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sr[4][32];
+      const uint32_t sbase = tmem + lane_off + (j & 1) * BN;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(sbase + c * 32, sr[c]);
+      tmem_wait_ld();
+      const bool diag = j == n - 1;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float v = __uint_as_float(sr[c][e]);
+          mx = (!diag || c * 32 + e <= r) ? fmaxf(mx, v) : mx;
+        }
+      const float cand = fmaxf(m, mx * sl2);
+      float alpha = 1.f;
+      bool rescale = false;
+      if (j == 0) {
+        m = cand;
+      } else if (cand > m + kRescale) {
+        alpha = ex2(m - cand);
+        m = cand;
+        rescale = true;
+      }
+      float sum = 0.f;
+      const uint32_t prow = smem_u32(sP + (j & 1) * kTile) + r * 128;
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c0 = c8 * 8 + 2 * e;
+          const float s0 = __uint_as_float(sr[c0 >> 5][c0 & 31]);
+          const float s1 = __uint_as_float(sr[(c0 + 1) >> 5][(c0 + 1) & 31]);
+          const float p0 = (!diag || c0 <= r) ? ex2(fmaf(s0, sl2, -m)) : 0.f;
+          const float p1 = (!diag || c0 + 1 <= r) ? ex2(fmaf(s1, sl2, -m)) : 0.f;
+          sum += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        const uint32_t addr = prow + (c8 >> 3) * kBox + (((uint32_t(c8 & 7)) ^ prow_sw) << 4);
+        st_shared_v4(addr, pk[0], pk[1], pk[2], pk[3]);
+      }
+      l = l * alpha + sum;
+      fence_async_smem();
+      if (j > 0) {
+        // O correction needs PV_{j-1} landed; it was issued a full softmax step ago.
+        if (!mbar_wait(&bars->pv_done, (j - 1) & 1, status, 81)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            const uint32_t oaddr = tmem + lane_off + kOCol + c * 32;
+            tmem_ld_32x32b_x32(oaddr, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st_32x32b_x32(oaddr, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[j & 1]);
+    }
+    if (!ok) *abort_flag = 1;
+    if (ok && mbar_wait(&bars->pv_done, (n - 1) & 1, status, 82)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      uint16_t* orow = out + int64_t(row0 + qb * BM + r) * ld_out + h * D;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(tmem + lane_off + kOCol + c * 32, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+          w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+          w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+          w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c * 32 + 8 * v) = w;
+        }
+      }
+      lse[(int64_t(b) * Hl + h) * seq + qb * BM + r] = m + log2f(l);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+  (void)mb;
+}
+
+}  // namespace attn_tc
+}  // namespace tdb
+
+// qkv [mb*seq, ld] (Q|K|V column blocks of Hl*128), out [mb*seq, ld_out],
+// lse [mb, Hl, seq].  Requires seq % 128 == 0 and 16-byte aligned rows.
+TDB_API int tdb_attn_fwd_tc(const void* qkv, int64_t ld, void* out, int64_t ld_out, float* lse, int mb, int seq,
+                            int Hl, float scale, void* stream) {
+  using namespace tdb::attn_tc;
+  if (!qkv || !out || !lse || mb <= 0 || seq <= 0 || Hl <= 0 || seq % BM || ld % 8 || ld_out % 8 ||
+      ld < int64_t(3) * Hl * D || ld_out < int64_t(Hl) * D || reinterpret_cast<uintptr_t>(out) % 16)
+    return tdb_host::fail(int(cudaErrorInvalidValue),
+                          "attention fwd (tcgen05): needs seq %% 128 == 0, 16-byte aligned rows (seq=%d)", seq);
+  CUtensorMap tm;
+  int rc = tdb_host::make_tmap_2d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(3) * Hl * D,
+                                  uint64_t(mb) * seq, uint64_t(ld), 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  static bool init = false;
+  if (!init) {
+    cudaError_t e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return tdb_host::fail(int(e), "attention fwd (tcgen05): smem attribute");
+    init = true;
+  }
+  dim3 grid(Hl * mb, seq / BM);
+  fwd_kernel<<<grid, kThreads, kSmem, static_cast<cudaStream_t>(stream)>>>(
+      tm, static_cast<uint16_t*>(out), ld_out, lse, seq, Hl, mb, scale, tdb_host::status_ptr());
+  tdb_host::launched(1);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : tdb_host::fail(int(e), "attention fwd (tcgen05) launch: %s", cudaGetErrorString(e));
+}

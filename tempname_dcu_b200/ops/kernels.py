@@ -18,6 +18,7 @@ native.register("tdb_layernorm_fwd", [V, V, V, V, V, V, I, I, F, V])
 native.register("tdb_layernorm_bwd", [V, V, V, V, V, V, V, V, V, V, I, I, I, V])
 native.register("tdb_layernorm_bwd_scratch_floats", [I, I])
 native.register("tdb_attn_fwd", [V, I64, V, I64, V, I, I, I, F, V])
+native.register("tdb_attn_fwd_tc", [V, I64, V, I64, V, I, I, I, F, V])
 native.register("tdb_attn_bwd", [V, I64, V, I64, V, I64, V, V, V, I64, I, I, I, F, V])
 native.register("tdb_xent_stats", [V, I64, V, I64, I, I, I, V, V])
 native.register("tdb_xent_combine", [V, I, I, V, V, V, F, I, V])
@@ -83,16 +84,24 @@ def layernorm_bwd(x, weight, mean, rstd, dy, dgamma, dbeta, scratch, dres=None, 
 
 
 # ---------------------------------------------------------------- attention
-def attention_fwd(qkv, mb, seq, heads_local, out=None, lse=None, scale=None):
-    """qkv [mb*seq, 3*Hl*128] -> (out [mb*seq, Hl*128], lse [mb, Hl, seq])."""
+def attention_fwd(qkv, mb, seq, heads_local, out=None, lse=None, scale=None, impl=None):
+    """qkv [mb*seq, 3*Hl*128] -> (out [mb*seq, Hl*128], lse [mb, Hl, seq]).
+
+    impl "tc" = tcgen05/TMEM kernel (attn_tc.cu, needs seq % 128 == 0 and
+    16-byte aligned rows), "mma" = the mma.sync kernel (attention.cu, any
+    seq); default: "tc" whenever it applies."""
     torch = _t()
     D = 128
     _need(qkv.shape[1] >= 3 * heads_local * D and qkv.stride(1) == 1, "qkv must be [tokens, 3*Hl*128]")
     scale = 1.0 / math.sqrt(D) if scale is None else scale
     out = torch.empty((mb * seq, heads_local * D), dtype=torch.bfloat16, device=qkv.device) if out is None else out
     lse = torch.empty((mb, heads_local, seq), dtype=torch.float32, device=qkv.device) if lse is None else lse
-    native.check(native.lib().tdb_attn_fwd(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0),
-                                           lse.data_ptr(), mb, seq, heads_local, float(scale), _s()), "attention fwd")
+    if impl is None:
+        impl = "tc" if seq % 128 == 0 and qkv.stride(0) % 8 == 0 and out.stride(0) % 8 == 0 \
+            and qkv.data_ptr() % 16 == 0 and out.data_ptr() % 16 == 0 else "mma"
+    fn = native.lib().tdb_attn_fwd_tc if impl == "tc" else native.lib().tdb_attn_fwd
+    native.check(fn(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0), lse.data_ptr(), mb, seq,
+                    heads_local, float(scale), _s()), f"attention fwd ({impl})")
     return out, lse
 
 

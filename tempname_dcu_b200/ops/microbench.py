@@ -2,6 +2,8 @@
 
     python -m tempname_dcu_b200.ops.microbench gemm [--shapes M,N,K:...] [--iters 20]
     python -m tempname_dcu_b200.ops.microbench ncu-gemm M N K [--mode fwd|dgrad|wgrad]
+    python -m tempname_dcu_b200.ops.microbench attn [--seq 2048 --heads 32 --mb 1] [--iters 20]
+    python -m tempname_dcu_b200.ops.microbench ncu-attn [--impl tc] [--seq 2048 --heads 8]
 
 Each measurement: warm-up launches, then ``iters`` timed launches, each
 preceded by a write of a 256 MB buffer (larger than the 126 MB L2) so that
@@ -113,6 +115,52 @@ def bench_gemm(shapes, iters):
     return rows
 
 
+def attn_flops(mb, seq, heads, causal=True):
+    """Forward FLOPs of causal attention, head_dim 128 (QK^T and PV, half the square)."""
+    flops = 4.0 * mb * heads * seq * seq * 128
+    return flops / 2 if causal else flops
+
+
+def bench_attn(mb, seq, heads, iters):
+    import torch
+    from . import kernels, native
+    device = torch.device("cuda", 0)
+    peak, _, source = _peaks()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+    g = torch.Generator(device=device).manual_seed(0)
+    qkv = torch.randn(mb * seq, 3 * heads * 128, device=device, generator=g).to(torch.bfloat16)
+    out = torch.empty(mb * seq, heads * 128, dtype=torch.bfloat16, device=device)
+    lse = torch.empty(mb, heads, seq, dtype=torch.float32, device=device)
+    fl = attn_flops(mb, seq, heads)
+    rows = []
+    for impl in ("tc", "mma"):
+        ms = time_fn(torch, lambda: kernels.attention_fwd(qkv, mb, seq, heads, out=out, lse=lse, impl=impl), iters,
+                     flush=flush)
+        rows.append(dict(op="attn.fwd", impl=impl, mb=mb, seq=seq, heads=heads, ms=ms, tflops=fl / ms / 1e9,
+                         frac_of_peak=fl / ms / 1e9 / peak, peak_source=source))
+        print(json.dumps(rows[-1]), flush=True)
+    dout = torch.randn_like(out)
+    dqkv = torch.empty_like(qkv)
+    dsum = torch.empty(mb, heads, seq, dtype=torch.float32, device=device)
+    kernels.attention_fwd(qkv, mb, seq, heads, out=out, lse=lse)
+    ms = time_fn(torch, lambda: kernels.attention_bwd(qkv, out, dout, lse, mb, seq, heads, dqkv=dqkv, dsum=dsum),
+                 iters, flush=flush)
+    rows.append(dict(op="attn.bwd", impl="mma", mb=mb, seq=seq, heads=heads, ms=ms, tflops=2.5 * fl / ms / 1e9,
+                     frac_of_peak=2.5 * fl / ms / 1e9 / peak, peak_source=source))
+    print(json.dumps(rows[-1]), flush=True)
+    try:  # library kernel, for context only
+        from flash_attn import flash_attn_func
+        q, k, v = qkv.reshape(mb, seq, 3, heads, 128).unbind(2)
+        ms = time_fn(torch, lambda: flash_attn_func(q, k, v, causal=True), iters, flush=flush)
+        rows.append(dict(op="attn.fwd", impl="flash_attn (library)", mb=mb, seq=seq, heads=heads, ms=ms,
+                         tflops=fl / ms / 1e9))
+        print(json.dumps(rows[-1]), flush=True)
+    except Exception as exc:  # noqa: BLE001
+        print(json.dumps(dict(op="attn.fwd", impl="flash_attn (library)", unavailable=str(exc)[:200])))
+    native.raise_on_status()
+    return rows
+
+
 def main(argv=None):
     parser = argparse.ArgumentParser()
     sub = parser.add_subparsers(dest="cmd", required=True)
@@ -125,8 +173,27 @@ def main(argv=None):
     q.add_argument("K", type=int)
     q.add_argument("--mode", default="fwd", choices=("fwd", "dgrad", "wgrad"))
     q.add_argument("--launches", type=int, default=3)
+    r = sub.add_parser("attn")
+    r.add_argument("--mb", type=int, default=1)
+    r.add_argument("--seq", type=int, default=2048)
+    r.add_argument("--heads", type=int, default=32)
+    r.add_argument("--iters", type=int, default=20)
+    t = sub.add_parser("ncu-attn", help="a few launches of the attention forward (for ncu captures)")
+    t.add_argument("--impl", default="tc", choices=("tc", "mma"))
+    t.add_argument("--seq", type=int, default=2048)
+    t.add_argument("--heads", type=int, default=8)
+    t.add_argument("--launches", type=int, default=3)
     args = parser.parse_args(argv)
-    if args.cmd == "gemm":
+    if args.cmd == "attn":
+        bench_attn(args.mb, args.seq, args.heads, args.iters)
+    elif args.cmd == "ncu-attn":
+        import torch
+        from . import kernels
+        qkv = torch.randn(args.seq, 3 * args.heads * 128, device="cuda").to(torch.bfloat16)
+        for _ in range(args.launches):
+            kernels.attention_fwd(qkv, 1, args.seq, args.heads, impl=args.impl)
+        torch.cuda.synchronize()
+    elif args.cmd == "gemm":
         shapes = DEFAULT_SHAPES
         if args.shapes:
             shapes = []

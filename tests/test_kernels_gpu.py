@@ -75,6 +75,26 @@ def test_attention_fwd_bwd(cuda, mb, seq, Hl):
     assert torch.equal(dqkv, dqkv2)
 
 
+@pytest.mark.parametrize("mb,seq,Hl", [(1, 128, 1), (1, 256, 2), (2, 384, 3), (1, 2048, 2)])
+@pytest.mark.parametrize("impl", ["tc", "mma"])
+def test_attention_fwd_impls_against_fp32(cuda, mb, seq, Hl, impl):
+    """Both forward kernels (tcgen05 and mma.sync) against fp32 math, lse included."""
+    import torch
+    from tempname_dcu_b200.ops import kernels as k
+    from tempname_dcu_b200.ops import native
+    torch.manual_seed(11)
+    qkv = (torch.randn(mb * seq, 3 * Hl * 128, device=cuda) * 1.5).to(torch.bfloat16)
+    out, lse = k.attention_fwd(qkv, mb, seq, Hl, impl=impl)
+    q, kk, v = qkv.float().reshape(mb, seq, 3, Hl, 128).permute(2, 0, 3, 1, 4).unbind(0)
+    s = (q @ kk.transpose(-1, -2)) / math.sqrt(128)
+    s = s.masked_fill(torch.ones(seq, seq, device=cuda, dtype=torch.bool).triu(1), float("-inf"))
+    ref = (torch.softmax(s, -1) @ v).transpose(1, 2).reshape(mb * seq, Hl * 128)
+    lse_ref = torch.logsumexp(s, -1) * (1.0 / math.log(2.0))
+    assert _rel(out, ref) < 1e-2
+    assert (lse - lse_ref).abs().max().item() < 2e-2
+    assert native.read_status()[0] == 0
+
+
 @pytest.mark.parametrize("world", [1, 2])
 def test_vocab_parallel_cross_entropy(cuda, world):
     import torch
