@@ -587,6 +587,19 @@ TDB_API int tdb_attn_fwd(const void* qkv, int64_t ld, void* out, int64_t ld_out,
 }
 
 // dsum: scratch [mb, Hl, seq] fp32.  dqkv [mb*seq, ld_dqkv] receives dQ|dK|dV.
+// Dsum[b, h, i] = sum_d dO[i, h, d] * O[i, h, d]  (one warp per (token, head)).
+TDB_API int tdb_attn_bwd_pre(const void* out, int64_t ld_out, const void* dout, int64_t ld_dout, float* dsum, int mb,
+                             int seq, int Hl, void* stream) {
+  if (!out || !dout || !dsum || mb <= 0 || seq <= 0 || Hl <= 0)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "attention bwd pre: bad arguments");
+  const int rows = mb * seq;
+  const int64_t warps = int64_t(rows) * Hl;
+  tdb::attn::bwd_pre_kernel<<<unsigned((warps * 32 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(out), ld_out, static_cast<const uint16_t*>(dout), ld_dout, dsum, seq, Hl, rows);
+  tdb_host::launched(1);
+  return int(cudaGetLastError());
+}
+
 TDB_API int tdb_attn_bwd(const void* qkv, int64_t ld, const void* out, int64_t ld_out, const void* dout,
                          int64_t ld_dout, const float* lse, float* dsum, void* dqkv, int64_t ld_dqkv, int mb, int seq,
                          int Hl, float scale, void* stream) {
@@ -601,11 +614,8 @@ TDB_API int tdb_attn_bwd(const void* qkv, int64_t ld, const void* out, int64_t l
     init = true;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int rows = mb * seq;
-  const int64_t warps = int64_t(rows) * Hl;
-  bwd_pre_kernel<<<unsigned((warps * 32 + 255) / 256), 256, 0, s>>>(
-      static_cast<const uint16_t*>(out), ld_out, static_cast<const uint16_t*>(dout), ld_dout, dsum, seq, Hl, rows);
-  tdb_host::launched(1);
+  int rc = tdb_attn_bwd_pre(out, ld_out, dout, ld_dout, dsum, mb, seq, Hl, stream);
+  if (rc) return rc;
   dim3 grid((seq + BWD_B - 1) / BWD_B, Hl, mb);
   bwd_dkdv_kernel<<<grid, BWD_THREADS, kDkdvSmem, s>>>(static_cast<const uint16_t*>(qkv), ld,
                                                        static_cast<const uint16_t*>(dout), ld_dout, lse, dsum,

@@ -8,7 +8,7 @@
 // scaled by scale*log2(e).
 //
 // One CTA = 128 queries of one (batch, head); key/value tiles of 128.
-//   warp 0      TMA producer: Q once, then K/V tiles through a 3-slot ring in
+//   warp 0      TMA producer: Q once, then K/V tiles through a 4-slot ring in
 //               exactly the order the MMA warp consumes them
 //               (K0, K1, V0, K2, V1, K3, ...); allocates 512 TMEM columns
 //   warp 1      MMA issuer (one thread):  S_j = Q K_j^T into TMEM S[j%2]
@@ -32,7 +32,7 @@ constexpr int BM = 128, BN = 128, D = 128;
 constexpr int kThreads = 192;
 constexpr int kBox = 128 * 128;  // one [128 rows][64 bf16] SW128 box = 16 KB
 constexpr int kTile = 2 * kBox;  // a 128 x 128 bf16 tile = two boxes
-constexpr int kSlots = 3;
+constexpr int kSlots = 4;
 constexpr int kTmemCols = 512;
 constexpr int kOCol = 256;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -344,6 +344,495 @@ __global__ void __launch_bounds__(kThreads, 1)
   (void)mb;
 }
 
+
+// ===========================================================================
+// Backward (deterministic, no atomics), two tcgen05 kernels after the
+// Dsum pre-pass:  P = exp2(S*scale*log2e - lse),  dS = P * (dP - Dsum).
+// ===========================================================================
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// K-major SW128 operand of 64 rows spanning two 64-column boxes (8 KB each).
+__device__ __forceinline__ uint64_t desc_k64(uint32_t base, int k) {
+  return smem_desc_sw128(base + (k >> 2) * 8192 + (k & 3) * 32, 16, 1024);
+}
+// MN-major SW128 operand [K = 64 rows][N = 128] stored as two [64][64] boxes.
+__device__ __forceinline__ uint64_t desc_mn64(uint32_t base, int k) {
+  return smem_desc_sw128(base + k * 16 * 128, 8192, 1024);
+}
+// One [128 rows][64 cols] K-major box (16 KB): K step k.
+__device__ __forceinline__ uint64_t desc_box(uint32_t base, int k) {
+  return smem_desc_sw128(base + k * 32, 16, 1024);
+}
+
+// Store 64 bf16 values (packed pairs) as row r of a [128][64] SW128 box.
+__device__ __forceinline__ void store_row64(uint32_t box, int r, const uint32_t (&pk)[32]) {
+  const uint32_t row = box + r * 128, sw = uint32_t(r & 7);
+#pragma unroll
+  for (int c8 = 0; c8 < 8; ++c8)
+    st_shared_v4(row + ((uint32_t(c8) ^ sw) << 4), pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
+}
+
+// Write 128 fp32 TMEM columns of this thread's row (times mul) as bf16.
+__device__ __forceinline__ void tmem_row_to_bf16(uint32_t taddr, float mul, uint16_t* dst) {
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t o[32];
+    tmem_ld_32x32b_x32(taddr + c * 32, o);
+    tmem_wait_ld();
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      uint4 w;
+      w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * mul, __uint_as_float(o[8 * v + 1]) * mul);
+      w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * mul, __uint_as_float(o[8 * v + 3]) * mul);
+      w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * mul, __uint_as_float(o[8 * v + 5]) * mul);
+      w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * mul, __uint_as_float(o[8 * v + 7]) * mul);
+      *reinterpret_cast<uint4*>(dst + c * 32 + 8 * v) = w;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dQ: CTA = 128 queries; key/value tiles of 64 through a 6-slot ring
+// (K0, V0, K1, V1, ...).  K_j stays until dQ += dS_j K_j has read it.
+// TMEM: S[2] cols 0/64, dP[2] cols 128/192, dQ cols 256..383.
+// ---------------------------------------------------------------------------
+namespace dqk {
+constexpr int kKV = 64 * 128 * 2;   // [64 keys][128 d] = two 8 KB boxes
+constexpr int kDS = 128 * 64 * 2;   // [128 q][64 keys] = one 16 KB box
+constexpr int kSlots = 6;
+constexpr int kSmem = 2 * kTile + kSlots * kKV + 2 * kDS + 1024 + 256;
+static_assert(kSmem <= 232448, "shared memory budget");
+struct alignas(8) Bars {
+  uint64_t q_full;
+  uint64_t kv_full[kSlots];
+  uint64_t kv_empty[kSlots];
+  uint64_t s_full[2];
+  uint64_t ds_full[2];
+  uint64_t dq_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+}  // namespace dqk
+
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_dq_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tkv,
+                  const __grid_constant__ CUtensorMap tdo, const float* __restrict__ lse,
+                  const float* __restrict__ dsum, uint16_t* __restrict__ dqkv, int64_t ld_dqkv, int seq, int Hl,
+                  float scale, int* status) {
+  constexpr int kSlots = dqk::kSlots, kKV = dqk::kKV, kDS = dqk::kDS;
+  using Bars = dqk::Bars;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sDO = sQ + kTile;
+  uint8_t* sKV = sDO + kTile;
+  uint8_t* sDS = sKV + kSlots * kKV;
+  Bars* bars = reinterpret_cast<Bars*>(sDS + 2 * kDS);
+
+  const int hb = blockIdx.x;
+  const int h = hb % Hl, b = hb / Hl;
+  const int nq = seq / BM;
+  const int qb = nq - 1 - int(blockIdx.y);
+  const int n = 2 * qb + 2;  // 64-key tiles up to the diagonal
+  const int row0 = b * seq;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&bars->kv_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->ds_full[i], 4);
+    }
+    mbar_init(&bars->dq_done, 1);
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+    if (lane == 0) {
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tkv);
+      prefetch_tmap(&tdo);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  volatile int* abort_flag = &bars->abort_flag;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars->q_full, 2 * kTile);
+      tma_load_2d(sQ, &tq, &bars->q_full, h * D, row0 + qb * BM);
+      tma_load_2d(sQ + kBox, &tq, &bars->q_full, h * D + 64, row0 + qb * BM);
+      tma_load_2d(sDO, &tdo, &bars->q_full, h * D, row0 + qb * BM);
+      tma_load_2d(sDO + kBox, &tdo, &bars->q_full, h * D + 64, row0 + qb * BM);
+      int i = 0;
+      bool ok = true;
+      for (; i < 2 * n; ++i) {
+        const int s = i % kSlots;
+        if (!mbar_wait(&bars->kv_empty[s], ((i / kSlots) & 1) ^ 1, status, 90)) { ok = false; *abort_flag = 1; break; }
+        if (*abort_flag) { ok = false; break; }
+        const int j = i >> 1;
+        const int col = ((i & 1) ? 2 * Hl + h : Hl + h) * D;
+        uint8_t* dst = sKV + s * kKV;
+        mbar_arrive_expect_tx(&bars->kv_full[s], kKV);
+        tma_load_2d(dst, &tkv, &bars->kv_full[s], col, row0 + j * 64);
+        tma_load_2d(dst + 8192, &tkv, &bars->kv_full[s], col + 64, row0 + j * 64);
+      }
+      mbar_wait(&bars->q_full, 0, status, 91);
+      if (!ok)
+        for (int k = (i >= kSlots ? i - kSlots : 0); k < i; ++k)
+          mbar_wait(&bars->kv_full[k % kSlots], (k / kSlots) & 1, status, 92);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(BM, 64, false, false);
+      constexpr uint32_t idQ = idesc_bf16(BM, D, false, true);
+      bool ok = mbar_wait(&bars->q_full, 0, status, 100);
+      bool issued = false;
+      const uint32_t sq = smem_u32(sQ), sdo = smem_u32(sDO);
+      auto item = [&](int i, uint32_t& addr) -> bool {
+        const int s = i % kSlots;
+        if (!mbar_wait(&bars->kv_full[s], (i / kSlots) & 1, status, 101)) return false;
+        if (*abort_flag) return false;
+        tc_fence_after();
+        addr = smem_u32(sKV + s * kKV);
+        return true;
+      };
+      auto issue_sdp = [&](int j) -> bool {
+        uint32_t sk, sv;
+        if (!item(2 * j, sk)) return false;
+        const uint32_t dS_ = tmem + (j & 1) * 64, dP_ = tmem + 128 + (j & 1) * 64;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_f16_ss(dS_, desc_k(sq, k), desc_k64(sk, k), idS, k > 0 ? 1u : 0u);
+        if (!item(2 * j + 1, sv)) return false;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_f16_ss(dP_, desc_k(sdo, k), desc_k64(sv, k), idS, k > 0 ? 1u : 0u);
+        umma_commit(&bars->kv_empty[(2 * j + 1) % kSlots]);
+        umma_commit(&bars->s_full[j & 1]);
+        issued = true;
+        return true;
+      };
+      if (ok) ok = issue_sdp(0);
+      if (ok && n > 1) ok = issue_sdp(1);
+      for (int j = 0; j < n && ok; ++j) {
+        if (!mbar_wait(&bars->ds_full[j & 1], (j >> 1) & 1, status, 102)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sds = smem_u32(sDS + (j & 1) * kDS);
+        const uint32_t sk = smem_u32(sKV + ((2 * j) % kSlots) * kKV);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) umma_f16_ss(tmem + 256, desc_box(sds, k), desc_mn64(sk, k), idQ, (j | k) ? 1u : 0u);
+        umma_commit(&bars->kv_empty[(2 * j) % kSlots]);
+        umma_commit(&bars->dq_done);
+        if (j + 2 < n) ok = issue_sdp(j + 2);
+      }
+      if (!ok) *abort_flag = 1;
+      if (issued) {
+        umma_commit(&bars->drain);
+        mbar_wait(&bars->drain, 0, status, 103);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int qi = qb * BM + r;
+    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const float sl2 = scale * kLog2e;
+    const int64_t stat = (int64_t(b) * Hl + h) * seq + qi;
+    const float L = lse[stat], Dr = dsum[stat];
+    bool ok = true;
+    int waited = 0;  // dq_done phases observed
+    for (int j = 0; j < n && ok; ++j) {
+      if (!mbar_wait(&bars->s_full[j & 1], (j >> 1) & 1, status, 110)) { ok = false; break; }
+      if (*abort_flag) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sv[2][32], pv[2][32];
+      tmem_ld_32x32b_x32(tmem + lane_off + (j & 1) * 64, sv[0]);
+      tmem_ld_32x32b_x32(tmem + lane_off + (j & 1) * 64 + 32, sv[1]);
+      tmem_ld_32x32b_x32(tmem + lane_off + 128 + (j & 1) * 64, pv[0]);
+      tmem_ld_32x32b_x32(tmem + lane_off + 128 + (j & 1) * 64 + 32, pv[1]);
+      tmem_wait_ld();
+      if (j >= 2) {  // dS buffer j%2 was read by dQ_{j-2}
+        if (!mbar_wait(&bars->dq_done, waited & 1, status, 111)) { ok = false; break; }
+        ++waited;
+      }
+      const int kbase = j * 64;
+      uint32_t pk[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        float d2[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int c = 2 * e + u;
+          const float s = __uint_as_float(sv[c >> 5][c & 31]);
+          const float dp = __uint_as_float(pv[c >> 5][c & 31]);
+          const float p = kbase + c <= qi ? ex2(fmaf(s, sl2, -L)) : 0.f;
+          d2[u] = p * (dp - Dr);
+        }
+        pk[e] = pack_bf16x2(d2[0], d2[1]);
+      }
+      store_row64(smem_u32(sDS + (j & 1) * kDS), r, pk);
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->ds_full[j & 1]);
+    }
+    if (!ok) *abort_flag = 1;
+    while (ok && waited < n) {
+      if (!mbar_wait(&bars->dq_done, waited & 1, status, 112)) ok = false;
+      ++waited;
+    }
+    if (ok) {
+      tc_fence_after();
+      tmem_row_to_bf16(tmem + lane_off + 256, scale, dqkv + int64_t(row0 + qi) * ld_dqkv + h * D);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---------------------------------------------------------------------------
+// dK, dV: CTA = 128 keys; query tiles of 64 (Q_i, dO_i, lse_i, Dsum_i)
+// through a 3-slot ring.  S^T = K Q_i^T, dP^T = V dO_i^T (thread = key row),
+// dV += P^T dO_i, dK += dS^T Q_i (the Q_i / dO_i tiles serve as the K-major B
+// operand of the first pair and the MN-major B operand of the second).
+// TMEM: S^T[2] cols 0/64, dP^T[2] cols 128/192, dV 256.., dK 384..
+// ---------------------------------------------------------------------------
+namespace dkv {
+constexpr int kQ = 64 * 128 * 2;  // [64 q][128 d] = two 8 KB boxes
+constexpr int kSlot = 2 * kQ;     // Q_i then dO_i
+constexpr int kP = 128 * 64 * 2;  // [128 keys][64 q] box
+constexpr int kSlots = 3;
+constexpr int kSmem = 2 * kTile + kSlots * kSlot + 4 * kP + kSlots * 512 + 1024 + 256;
+static_assert(kSmem <= 232448, "shared memory budget");
+struct alignas(8) Bars {
+  uint64_t kv_full;
+  uint64_t q_full[kSlots];
+  uint64_t q_empty[kSlots];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t mm_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+}  // namespace dkv
+
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tkv, const __grid_constant__ CUtensorMap tq,
+                    const __grid_constant__ CUtensorMap tdo, const float* __restrict__ lse,
+                    const float* __restrict__ dsum, uint16_t* __restrict__ dqkv, int64_t ld_dqkv, int seq, int Hl,
+                    float scale, int* status) {
+  constexpr int kSlots = dkv::kSlots, kQ = dkv::kQ, kSlot = dkv::kSlot, kP = dkv::kP;
+  using Bars = dkv::Bars;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + kTile;
+  uint8_t* sRing = sV + kTile;
+  uint8_t* sPT = sRing + kSlots * kSlot;   // 2 buffers
+  uint8_t* sDST = sPT + 2 * kP;            // 2 buffers
+  float* sStat = reinterpret_cast<float*>(sDST + 2 * kP);  // per slot: lse[64], dsum[64]
+  Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(sStat) + kSlots * 512);
+
+  const int hb = blockIdx.x;
+  const int h = hb % Hl, b = hb / Hl;
+  const int nq = seq / BM;
+  const int kb = int(blockIdx.y);  // heaviest (kb = 0) first
+  const int t0 = 2 * kb;           // first 64-query tile that sees these keys
+  const int n = 2 * nq - t0;
+  const int row0 = b * seq;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* lse_h = lse + (int64_t(b) * Hl + h) * seq;
+  const float* dsum_h = dsum + (int64_t(b) * Hl + h) * seq;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->kv_full, 1);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&bars->q_full[s], 1);
+      mbar_init(&bars->q_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->p_full[i], 4);
+    }
+    mbar_init(&bars->mm_done, 1);
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+    if (lane == 0) {
+      prefetch_tmap(&tkv);
+      prefetch_tmap(&tq);
+      prefetch_tmap(&tdo);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  volatile int* abort_flag = &bars->abort_flag;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars->kv_full, 2 * kTile);
+      tma_load_2d(sK, &tkv, &bars->kv_full, (Hl + h) * D, row0 + kb * BM);
+      tma_load_2d(sK + kBox, &tkv, &bars->kv_full, (Hl + h) * D + 64, row0 + kb * BM);
+      tma_load_2d(sV, &tkv, &bars->kv_full, (2 * Hl + h) * D, row0 + kb * BM);
+      tma_load_2d(sV + kBox, &tkv, &bars->kv_full, (2 * Hl + h) * D + 64, row0 + kb * BM);
+      int i = 0;
+      bool ok = true;
+      for (; i < n; ++i) {
+        const int s = i % kSlots;
+        if (!mbar_wait(&bars->q_empty[s], ((i / kSlots) & 1) ^ 1, status, 120)) { ok = false; *abort_flag = 1; break; }
+        if (*abort_flag) { ok = false; break; }
+        const int q0 = (t0 + i) * 64;
+        uint8_t* dst = sRing + s * kSlot;
+        float* st = sStat + s * 128;
+        mbar_arrive_expect_tx(&bars->q_full[s], kSlot + 512);
+        tma_load_2d(dst, &tq, &bars->q_full[s], h * D, row0 + q0);
+        tma_load_2d(dst + 8192, &tq, &bars->q_full[s], h * D + 64, row0 + q0);
+        tma_load_2d(dst + kQ, &tdo, &bars->q_full[s], h * D, row0 + q0);
+        tma_load_2d(dst + kQ + 8192, &tdo, &bars->q_full[s], h * D + 64, row0 + q0);
+        bulk_load(st, lse_h + q0, 256, &bars->q_full[s]);
+        bulk_load(st + 64, dsum_h + q0, 256, &bars->q_full[s]);
+      }
+      mbar_wait(&bars->kv_full, 0, status, 121);
+      if (!ok)
+        for (int k = (i >= kSlots ? i - kSlots : 0); k < i; ++k)
+          mbar_wait(&bars->q_full[k % kSlots], (k / kSlots) & 1, status, 122);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(BM, 64, false, false);
+      constexpr uint32_t idG = idesc_bf16(BM, D, false, true);
+      bool ok = mbar_wait(&bars->kv_full, 0, status, 130);
+      bool issued = false;
+      const uint32_t sk = smem_u32(sK), sv = smem_u32(sV);
+      auto issue_sdp = [&](int i) -> bool {
+        const int s = i % kSlots;
+        if (!mbar_wait(&bars->q_full[s], (i / kSlots) & 1, status, 131)) return false;
+        if (*abort_flag) return false;
+        tc_fence_after();
+        const uint32_t sq = smem_u32(sRing + s * kSlot), sdo = sq + kQ;
+        const uint32_t dS_ = tmem + (i & 1) * 64, dP_ = tmem + 128 + (i & 1) * 64;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_f16_ss(dS_, desc_k(sk, k), desc_k64(sq, k), idS, k > 0 ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_f16_ss(dP_, desc_k(sv, k), desc_k64(sdo, k), idS, k > 0 ? 1u : 0u);
+        umma_commit(&bars->s_full[i & 1]);
+        issued = true;
+        return true;
+      };
+      if (ok) ok = issue_sdp(0);
+      if (ok && n > 1) ok = issue_sdp(1);
+      for (int i = 0; i < n && ok; ++i) {
+        if (!mbar_wait(&bars->p_full[i & 1], (i >> 1) & 1, status, 132)) { ok = false; break; }
+        tc_fence_after();
+        const int s = i % kSlots;
+        const uint32_t sq = smem_u32(sRing + s * kSlot), sdo = sq + kQ;
+        const uint32_t spt = smem_u32(sPT + (i & 1) * kP), sdst = smem_u32(sDST + (i & 1) * kP);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) umma_f16_ss(tmem + 256, desc_box(spt, k), desc_mn64(sdo, k), idG, (i | k) ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) umma_f16_ss(tmem + 384, desc_box(sdst, k), desc_mn64(sq, k), idG, (i | k) ? 1u : 0u);
+        umma_commit(&bars->q_empty[s]);
+        umma_commit(&bars->mm_done);
+        if (i + 2 < n) ok = issue_sdp(i + 2);
+      }
+      if (!ok) *abort_flag = 1;
+      if (issued) {
+        umma_commit(&bars->drain);
+        mbar_wait(&bars->drain, 0, status, 133);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int kj = kb * BM + r;  // this thread's key
+    const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const float sl2 = scale * kLog2e;
+    bool ok = true;
+    int waited = 0;
+    for (int i = 0; i < n && ok; ++i) {
+      if (!mbar_wait(&bars->s_full[i & 1], (i >> 1) & 1, status, 140)) { ok = false; break; }
+      // the lse / Dsum rows of this tile arrived with Q_i (same transaction barrier)
+      if (!mbar_wait(&bars->q_full[i % kSlots], (i / kSlots) & 1, status, 141)) { ok = false; break; }
+      if (*abort_flag) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sv[2][32], pv[2][32];
+      tmem_ld_32x32b_x32(tmem + lane_off + (i & 1) * 64, sv[0]);
+      tmem_ld_32x32b_x32(tmem + lane_off + (i & 1) * 64 + 32, sv[1]);
+      tmem_ld_32x32b_x32(tmem + lane_off + 128 + (i & 1) * 64, pv[0]);
+      tmem_ld_32x32b_x32(tmem + lane_off + 128 + (i & 1) * 64 + 32, pv[1]);
+      tmem_wait_ld();
+      if (i >= 2) {  // P^T / dS^T buffers i%2 were read by the GEMMs of step i-2
+        if (!mbar_wait(&bars->mm_done, waited & 1, status, 142)) { ok = false; break; }
+        ++waited;
+      }
+      const float* st = sStat + (i % kSlots) * 128;
+      const int q0 = (t0 + i) * 64;
+      uint32_t pp[32], dd[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        float p2[2], d2[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int c = 2 * e + u;
+          const float s = __uint_as_float(sv[c >> 5][c & 31]);
+          const float dp = __uint_as_float(pv[c >> 5][c & 31]);
+          const float p = q0 + c >= kj ? ex2(fmaf(s, sl2, -st[c])) : 0.f;
+          p2[u] = p;
+          d2[u] = p * (dp - st[64 + c]);
+        }
+        pp[e] = pack_bf16x2(p2[0], p2[1]);
+        dd[e] = pack_bf16x2(d2[0], d2[1]);
+      }
+      store_row64(smem_u32(sPT + (i & 1) * kP), r, pp);
+      store_row64(smem_u32(sDST + (i & 1) * kP), r, dd);
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[i & 1]);
+    }
+    if (!ok) *abort_flag = 1;
+    while (ok && waited < n) {
+      if (!mbar_wait(&bars->mm_done, waited & 1, status, 143)) ok = false;
+      ++waited;
+    }
+    if (ok) {
+      tc_fence_after();
+      uint16_t* rowp = dqkv + int64_t(row0 + kj) * ld_dqkv;
+      tmem_row_to_bf16(tmem + lane_off + 256, 1.f, rowp + (2 * Hl + h) * D);
+      tmem_row_to_bf16(tmem + lane_off + 384, scale, rowp + (Hl + h) * D);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
 }  // namespace attn_tc
 }  // namespace tdb
 
@@ -372,4 +861,56 @@ TDB_API int tdb_attn_fwd_tc(const void* qkv, int64_t ld, void* out, int64_t ld_o
   tdb_host::launched(1);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : tdb_host::fail(int(e), "attention fwd (tcgen05) launch: %s", cudaGetErrorString(e));
+}
+
+TDB_API int tdb_attn_bwd_pre(const void* out, int64_t ld_out, const void* dout, int64_t ld_dout, float* dsum, int mb,
+                             int seq, int Hl, void* stream);
+
+// Backward on the tensor cores: Dsum pre-pass, then the dK/dV and dQ
+// kernels.  Same contract as tdb_attn_bwd; needs seq % 128 == 0.
+TDB_API int tdb_attn_bwd_tc(const void* qkv, int64_t ld, const void* out, int64_t ld_out, const void* dout,
+                            int64_t ld_dout, const float* lse, float* dsum, void* dqkv, int64_t ld_dqkv, int mb,
+                            int seq, int Hl, float scale, void* stream) {
+  using namespace tdb::attn_tc;
+  if (!qkv || !out || !dout || !lse || !dsum || !dqkv || mb <= 0 || seq <= 0 || Hl <= 0 || seq % BM || ld % 8 ||
+      ld_dout % 8 || ld_dqkv % 8 || ld < int64_t(3) * Hl * D || ld_dqkv < int64_t(3) * Hl * D ||
+      ld_dout < int64_t(Hl) * D || reinterpret_cast<uintptr_t>(dqkv) % 16 ||
+      reinterpret_cast<uintptr_t>(lse) % 16 || reinterpret_cast<uintptr_t>(dsum) % 16)
+    return tdb_host::fail(int(cudaErrorInvalidValue),
+                          "attention bwd (tcgen05): needs seq %% 128 == 0 and 16-byte aligned rows (seq=%d)", seq);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = tdb_attn_bwd_pre(out, ld_out, dout, ld_dout, dsum, mb, seq, Hl, stream);
+  if (rc) return rc;
+  CUtensorMap tkv128, tkv64, tdo128, tdo64;
+  const uint64_t rows = uint64_t(mb) * seq;
+  if ((rc = tdb_host::make_tmap_2d(&tkv128, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(3) * Hl * D, rows,
+                                   uint64_t(ld), 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = tdb_host::make_tmap_2d(&tkv64, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(3) * Hl * D, rows,
+                                   uint64_t(ld), 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = tdb_host::make_tmap_2d(&tdo128, dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(Hl) * D, rows,
+                                   uint64_t(ld_dout), 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = tdb_host::make_tmap_2d(&tdo64, dout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(Hl) * D, rows,
+                                   uint64_t(ld_dout), 64, 64, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  static bool init = false;
+  if (!init) {
+    cudaError_t e = cudaFuncSetAttribute(bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dkv::kSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dqk::kSmem);
+    if (e != cudaSuccess) return tdb_host::fail(int(e), "attention bwd (tcgen05): smem attribute");
+    init = true;
+  }
+  const dim3 grid(Hl * mb, seq / BM);
+  uint16_t* dq = static_cast<uint16_t*>(dqkv);
+  bwd_dkdv_kernel<<<grid, kThreads, dkv::kSmem, s>>>(tkv128, tkv64, tdo64, lse, dsum, dq, ld_dqkv, seq, Hl, scale,
+                                                      tdb_host::status_ptr());
+  tdb_host::launched(1);
+  bwd_dq_kernel<<<grid, kThreads, dqk::kSmem, s>>>(tkv128, tkv64, tdo128, lse, dsum, dq, ld_dqkv, seq, Hl, scale,
+                                                    tdb_host::status_ptr());
+  tdb_host::launched(1);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : tdb_host::fail(int(e), "attention bwd (tcgen05) launch: %s", cudaGetErrorString(e));
 }

@@ -97,6 +97,61 @@ __global__ void e4m3_probe_kernel(const float* __restrict__ in, uint8_t* __restr
   decoded[i] = e4m3_to_float(i < 256 ? uint32_t(i) : uint32_t(pair & 0xff));
 }
 
+
+// Codec statistics per block of rows, for the selective arm's error budget
+// (no counterpart in the reference, whose calibration is timing-only).  One
+// CTA per block of `block_rows` x `cols`; warp w walks groups w, w+8, ...;
+// per group: sum x^2, max |x| and sum (bf16(decode(encode(x))) - x)^2, each
+// accumulated in fp64 per warp and combined in warp order (deterministic).
+// out[block] = {sumsq, amax, err_sumsq}.
+__global__ void __launch_bounds__(256) block_stats_kernel(const uint16_t* __restrict__ input, int64_t groups_per_block,
+                                                          double* __restrict__ out) {
+  __shared__ double part[kWarpsPerBlock][3];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint16_t* base = input + int64_t(blockIdx.x) * groups_per_block * kGroup;
+  double sq = 0.0, amax = 0.0, err = 0.0;
+  for (int64_t g = warp; g < groups_per_block; g += kWarpsPerBlock) {
+    const uint2 raw = reinterpret_cast<const uint2*>(base + g * kGroup)[lane];
+    float x[4] = {bf16_bits_to_float(raw.x & 0xffff), bf16_bits_to_float(raw.x >> 16),
+                  bf16_bits_to_float(raw.y & 0xffff), bf16_bits_to_float(raw.y >> 16)};
+    GroupScales s;
+    const uint32_t word = encode_group_warp(x, lane, s);
+    float y[4];
+    decode_group_warp(word, s.quant, s.adaptive, lane, y);
+    float gsq = 0.f, gmax = 0.f, gerr = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d = bf16_bits_to_float(float_to_bf16_bits(y[j])) - x[j];
+      gsq += x[j] * x[j];
+      gmax = fmaxf(gmax, fabsf(x[j]));
+      gerr += d * d;
+    }
+    gsq = warp_sum(gsq);
+    gmax = warp_max(gmax);
+    gerr = warp_sum(gerr);
+    sq += gsq;
+    amax = fmax(amax, double(gmax));
+    err += gerr;
+  }
+  if (lane == 0) {
+    part[warp][0] = sq;
+    part[warp][1] = amax;
+    part[warp][2] = err;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0.0, m = 0.0, e = 0.0;
+    for (int w = 0; w < kWarpsPerBlock; ++w) {
+      a += part[w][0];
+      m = fmax(m, part[w][1]);
+      e += part[w][2];
+    }
+    out[3 * blockIdx.x + 0] = a;
+    out[3 * blockIdx.x + 1] = m;
+    out[3 * blockIdx.x + 2] = e;
+  }
+}
+
 }  // namespace taco
 }  // namespace tdb
 
@@ -161,6 +216,17 @@ TDB_API int tdb_e4m3_probe(const float* in, uint8_t* codes, float* decoded, int6
   if (!in || !codes || !decoded || n <= 0) return tdb_host::fail(int(cudaErrorInvalidValue), "probe: bad args");
   taco::e4m3_probe_kernel<<<unsigned((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(in, codes,
                                                                                                    decoded, n);
+  tdb_host::launched(1);
+  return int(cudaGetLastError());
+}
+
+// input bf16 [blocks * block_elements]; out fp64 [blocks, 3].
+TDB_API int tdb_taco_block_stats(const void* input, int64_t block_elements, int blocks, double* out, void* stream) {
+  if (!input || !out || blocks <= 0 || !valid_elements(block_elements) ||
+      reinterpret_cast<uintptr_t>(input) % 8)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "block stats: bad arguments");
+  taco::block_stats_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(input), block_elements / taco::kGroup, out);
   tdb_host::launched(1);
   return int(cudaGetLastError());
 }

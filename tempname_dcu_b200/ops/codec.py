@@ -98,6 +98,21 @@ class Codec:
             raise ValueError("diagnostic delay needs 0 < cycles <= 100000000")
         native.check(self.lib.tdb_diagnostic_delay(cycles, native.stream_ptr(stream)), "diagnostic delay")
 
+    def block_stats(self, source, block_rows: int, stream=None):
+        """Per block of ``block_rows`` rows of a [rows, n] bf16 tensor: fp64
+        [blocks, 3] = (sum x^2, max |x|, sum (roundtrip(x) - x)^2), where
+        roundtrip is encode -> decode -> bf16.  Used for the selective arm's
+        error budget; deterministic."""
+        torch = _torch()
+        _check(source, torch.bfloat16, "input")
+        if source.ndim != 2 or type(block_rows) is not int or block_rows <= 0 or source.shape[0] % block_rows:
+            raise ValueError("expected [rows, n] with rows a multiple of block_rows")
+        blocks = source.shape[0] // block_rows
+        out = torch.empty((blocks, 3), dtype=torch.float64, device=source.device)
+        native.check(self.lib.tdb_taco_block_stats(source.data_ptr(), block_rows * source.shape[1], blocks,
+                                                   out.data_ptr(), native.stream_ptr(stream)), "codec block stats")
+        return out
+
     def e4m3_probe(self, values):
         """Hardware E4M3 conversion of fp32 values (test hook): (codes, decode(index))."""
         torch = _torch()

@@ -20,6 +20,7 @@ native.register("tdb_layernorm_bwd_scratch_floats", [I, I])
 native.register("tdb_attn_fwd", [V, I64, V, I64, V, I, I, I, F, V])
 native.register("tdb_attn_fwd_tc", [V, I64, V, I64, V, I, I, I, F, V])
 native.register("tdb_attn_bwd", [V, I64, V, I64, V, I64, V, V, V, I64, I, I, I, F, V])
+native.register("tdb_attn_bwd_tc", [V, I64, V, I64, V, I64, V, V, V, I64, I, I, I, F, V])
 native.register("tdb_xent_stats", [V, I64, V, I64, I, I, I, V, V])
 native.register("tdb_xent_combine", [V, I, I, V, V, V, F, I, V])
 native.register("tdb_xent_grad", [V, I64, V, I64, I, I, I, V, F, V])
@@ -105,16 +106,24 @@ def attention_fwd(qkv, mb, seq, heads_local, out=None, lse=None, scale=None, imp
     return out, lse
 
 
-def attention_bwd(qkv, out, dout, lse, mb, seq, heads_local, dqkv=None, dsum=None, scale=None):
+def attention_bwd(qkv, out, dout, lse, mb, seq, heads_local, dqkv=None, dsum=None, scale=None, impl=None):
+    """dqkv [mb*seq, 3*Hl*128] from (qkv, out, dout, lse); deterministic.
+
+    impl "tc" = tcgen05 kernels (attn_tc.cu, seq % 128 == 0, 16-byte aligned
+    rows), "mma" = mma.sync kernels (attention.cu); default "tc" when it applies."""
     torch = _t()
     D = 128
     scale = 1.0 / math.sqrt(D) if scale is None else scale
     dqkv = torch.empty_like(qkv) if dqkv is None else dqkv
     dsum = torch.empty((mb, heads_local, seq), dtype=torch.float32, device=qkv.device) if dsum is None else dsum
-    native.check(native.lib().tdb_attn_bwd(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0),
-                                           dout.data_ptr(), dout.stride(0), lse.data_ptr(), dsum.data_ptr(),
-                                           dqkv.data_ptr(), dqkv.stride(0), mb, seq, heads_local, float(scale),
-                                           _s()), "attention bwd")
+    if impl is None:
+        aligned = all(t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0 for t in (qkv, dout, dqkv)) \
+            and lse.data_ptr() % 16 == 0 and dsum.data_ptr() % 16 == 0
+        impl = "tc" if seq % 128 == 0 and aligned else "mma"
+    fn = native.lib().tdb_attn_bwd_tc if impl == "tc" else native.lib().tdb_attn_bwd
+    native.check(fn(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0), dout.data_ptr(), dout.stride(0),
+                    lse.data_ptr(), dsum.data_ptr(), dqkv.data_ptr(), dqkv.stride(0), mb, seq, heads_local,
+                    float(scale), _s()), f"attention bwd ({impl})")
     return dqkv
 
 

@@ -143,11 +143,14 @@ def bench_attn(mb, seq, heads, iters):
     dqkv = torch.empty_like(qkv)
     dsum = torch.empty(mb, heads, seq, dtype=torch.float32, device=device)
     kernels.attention_fwd(qkv, mb, seq, heads, out=out, lse=lse)
-    ms = time_fn(torch, lambda: kernels.attention_bwd(qkv, out, dout, lse, mb, seq, heads, dqkv=dqkv, dsum=dsum),
-                 iters, flush=flush)
-    rows.append(dict(op="attn.bwd", impl="mma", mb=mb, seq=seq, heads=heads, ms=ms, tflops=2.5 * fl / ms / 1e9,
-                     frac_of_peak=2.5 * fl / ms / 1e9 / peak, peak_source=source))
-    print(json.dumps(rows[-1]), flush=True)
+    for impl in ("tc", "mma"):
+        ms = time_fn(torch, lambda: kernels.attention_bwd(qkv, out, dout, lse, mb, seq, heads, dqkv=dqkv, dsum=dsum,
+                                                          impl=impl), iters, flush=flush)
+        # algorithmic backward FLOPs = 2.5x forward (5 GEMMs); the deterministic
+        # two-kernel schedule executes 7
+        rows.append(dict(op="attn.bwd", impl=impl, mb=mb, seq=seq, heads=heads, ms=ms, tflops=2.5 * fl / ms / 1e9,
+                         frac_of_peak=2.5 * fl / ms / 1e9 / peak, peak_source=source))
+        print(json.dumps(rows[-1]), flush=True)
     try:  # library kernel, for context only
         from flash_attn import flash_attn_func
         q, k, v = qkv.reshape(mb, seq, 3, heads, 128).unbind(2)

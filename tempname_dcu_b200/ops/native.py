@@ -33,6 +33,7 @@ SIGNATURES = {
     "tdb_taco_encode": [c_void_p, c_void_p, c_int64, c_void_p],
     "tdb_taco_decode": [c_void_p, c_void_p, c_int64, c_void_p],
     "tdb_taco_reduce": [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p],
+    "tdb_taco_block_stats": [c_void_p, c_int64, c_int, c_void_p, c_void_p],
     "tdb_e4m3_probe": [c_void_p, c_void_p, c_void_p, c_int64, c_void_p],
 }
 _RESTYPE = {"tdb_last_error": ctypes.c_char_p, "tdb_error_string": ctypes.c_char_p,

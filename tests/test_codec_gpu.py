@@ -122,3 +122,24 @@ def test_diagnostic_delay_bounds(cuda):
         codec().delay(0)
     with pytest.raises(ValueError):
         codec().delay(100_000_001)
+
+
+def test_block_stats_against_fp64_oracle(cuda):
+    """Per-block codec statistics (sumsq, amax, roundtrip error) vs the oracle."""
+    import torch
+    from tempname_dcu_b200.ops.codec import codec
+    torch.manual_seed(5)
+    rows, cols, block_rows = 8, 256, 2
+    x = (torch.randn(rows, cols, device=cuda) * torch.linspace(0.01, 30, rows, device=cuda)[:, None]).to(torch.bfloat16)
+    stats = codec().block_stats(x, block_rows).cpu()
+    assert stats.shape == (rows // block_rows, 3) and stats.dtype == torch.float64
+    for b in range(rows // block_rows):
+        part = x[b * block_rows:(b + 1) * block_rows].float().cpu().reshape(-1).tolist()
+        rt = [ref.bf16_round(v) for v in ref.decode(ref.encode(part))]
+        sumsq = sum(v * v for v in part)
+        err = sum((a - v) ** 2 for a, v in zip(rt, part))
+        assert abs(stats[b, 0].item() - sumsq) <= 1e-5 * sumsq
+        assert stats[b, 1].item() == max(abs(v) for v in part)
+        assert abs(stats[b, 2].item() - err) <= 0.05 * err + 1e-12 * sumsq
+    again = codec().block_stats(x, block_rows).cpu()
+    assert torch.equal(stats, again)
