@@ -88,6 +88,57 @@ __device__ __forceinline__ uint64_t desc_mn(uint32_t base, int k) {
   return smem_desc_sw128(base + k * 16 * 128, kBox, 1024);
 }
 
+// Row maximum of 128 scores held by this thread; 8 independent chains so the
+// dependent-latency stalls overlap.  MASK: causal diagonal tile (col > row is
+// excluded).
+template <bool MASK>
+__device__ __forceinline__ float row_max(const uint32_t (&sr)[4][32], int r) {
+  float mx[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < 128; ++c) {
+    const float v = __uint_as_float(sr[c >> 5][c & 31]);
+    if (!MASK || c <= r) mx[c & 7] = fmaxf(mx[c & 7], v);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) mx[i] = fmaxf(mx[i], mx[i + 4]);
+  return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+}
+
+// P = exp2(s*sl2 - m) for the 128 scores of this row, stored as bf16 into the
+// SW128 K-major P tile (row r, two 64-column boxes); returns the row sum
+// (8 independent accumulators).
+template <bool MASK>
+__device__ __forceinline__ float exp_store_row(const uint32_t (&sr)[4][32], int r, float sl2, float m, uint32_t prow,
+                                               uint32_t sw) {
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  const float neg = -m;
+#pragma unroll
+  for (int c8 = 0; c8 < 16; ++c8) {
+    uint32_t pk[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c0 = c8 * 8 + 2 * e;
+      float p0 = ex2(fmaf(__uint_as_float(sr[c0 >> 5][c0 & 31]), sl2, neg));
+      float p1 = ex2(fmaf(__uint_as_float(sr[(c0 + 1) >> 5][(c0 + 1) & 31]), sl2, neg));
+      if (MASK) {
+        p0 = c0 <= r ? p0 : 0.f;
+        p1 = c0 + 1 <= r ? p1 : 0.f;
+      }
+      acc[2 * e] += p0;
+      acc[2 * e + 1] += p1;
+      pk[e] = pack_bf16x2(p0, p1);
+    }
+    st_shared_v4(prow + (c8 >> 3) * kBox + ((uint32_t(c8 & 7) ^ sw) << 4), pk[0], pk[1], pk[2], pk[3]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i] += acc[i + 4];
+  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tm, uint16_t* __restrict__ out, int64_t ld_out,
                float* __restrict__ lse, int seq, int Hl, int mb, float scale, int* status) {
@@ -252,18 +303,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(sbase + c * 32, sr[c]);
       tmem_wait_ld();
-      const bool diag = j == n - 1;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float v = __uint_as_float(sr[c][e]);
-          mx = (!diag || c * 32 + e <= r) ? fmaxf(mx, v) : mx;
-        }
-      const float cand = fmaxf(m, mx * sl2);
+      float mx, sum = 0.f;
       float alpha = 1.f;
       bool rescale = false;
+      const uint32_t prow = smem_u32(sP + (j & 1) * kTile) + r * 128;
+      if (j == n - 1) {
+        mx = row_max<true>(sr, r);
+      } else {
+        mx = row_max<false>(sr, r);
+      }
+      const float cand = fmaxf(m, mx * sl2);
       if (j == 0) {
         m = cand;
       } else if (cand > m + kRescale) {
@@ -271,23 +320,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = cand;
         rescale = true;
       }
-      float sum = 0.f;
-      const uint32_t prow = smem_u32(sP + (j & 1) * kTile) + r * 128;
-#pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c0 = c8 * 8 + 2 * e;
-          const float s0 = __uint_as_float(sr[c0 >> 5][c0 & 31]);
-          const float s1 = __uint_as_float(sr[(c0 + 1) >> 5][(c0 + 1) & 31]);
-          const float p0 = (!diag || c0 <= r) ? ex2(fmaf(s0, sl2, -m)) : 0.f;
-          const float p1 = (!diag || c0 + 1 <= r) ? ex2(fmaf(s1, sl2, -m)) : 0.f;
-          sum += p0 + p1;
-          pk[e] = pack_bf16x2(p0, p1);
-        }
-        const uint32_t addr = prow + (c8 >> 3) * kBox + (((uint32_t(c8 & 7)) ^ prow_sw) << 4);
-        st_shared_v4(addr, pk[0], pk[1], pk[2], pk[3]);
+      if (j == n - 1) {
+        sum = exp_store_row<true>(sr, r, sl2, m, prow, prow_sw);
+      } else {
+        sum = exp_store_row<false>(sr, r, sl2, m, prow, prow_sw);
       }
       l = l * alpha + sum;
       fence_async_smem();
@@ -394,6 +430,47 @@ __device__ __forceinline__ void tmem_row_to_bf16(uint32_t taddr, float mul, uint
       w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * mul, __uint_as_float(o[8 * v + 7]) * mul);
       *reinterpret_cast<uint4*>(dst + c * 32 + 8 * v) = w;
     }
+  }
+}
+
+// dS row (64 keys) of the dQ kernel: ds = exp2(s*sl2 - lse) * (dp - Dsum).
+// MASK: keys c > lim are causally excluded.
+template <bool MASK>
+__device__ __forceinline__ void dq_row(const uint32_t (&sv)[2][32], const uint32_t (&pv)[2][32], float sl2, float L,
+                                       float Dr, int lim, uint32_t (&pk)[32]) {
+  const float nl = -L;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    float d2[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int c = 2 * e + u;
+      float p = ex2(fmaf(__uint_as_float(sv[c >> 5][c & 31]), sl2, nl));
+      if (MASK) p = c <= lim ? p : 0.f;
+      d2[u] = p * (__uint_as_float(pv[c >> 5][c & 31]) - Dr);
+    }
+    pk[e] = pack_bf16x2(d2[0], d2[1]);
+  }
+}
+
+// P^T and dS^T rows (64 queries) of the dK/dV kernel; lse / Dsum per query
+// column from shared memory.  MASK: queries c < lim are causally excluded.
+template <bool MASK>
+__device__ __forceinline__ void dkdv_row(const uint32_t (&sv)[2][32], const uint32_t (&pv)[2][32], float sl2,
+                                         const float* st, int lim, uint32_t (&pp)[32], uint32_t (&dd)[32]) {
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    const float2 lse2 = *reinterpret_cast<const float2*>(st + 2 * e);
+    const float2 ds2 = *reinterpret_cast<const float2*>(st + 64 + 2 * e);
+    float p0 = ex2(fmaf(__uint_as_float(sv[(2 * e) >> 5][(2 * e) & 31]), sl2, -lse2.x));
+    float p1 = ex2(fmaf(__uint_as_float(sv[(2 * e + 1) >> 5][(2 * e + 1) & 31]), sl2, -lse2.y));
+    if (MASK) {
+      p0 = 2 * e >= lim ? p0 : 0.f;
+      p1 = 2 * e + 1 >= lim ? p1 : 0.f;
+    }
+    pp[e] = pack_bf16x2(p0, p1);
+    dd[e] = pack_bf16x2(p0 * (__uint_as_float(pv[(2 * e) >> 5][(2 * e) & 31]) - ds2.x),
+                        p1 * (__uint_as_float(pv[(2 * e + 1) >> 5][(2 * e + 1) & 31]) - ds2.y));
   }
 }
 
@@ -571,20 +648,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&bars->dq_done, waited & 1, status, 111)) { ok = false; break; }
         ++waited;
       }
-      const int kbase = j * 64;
       uint32_t pk[32];
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        float d2[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int c = 2 * e + u;
-          const float s = __uint_as_float(sv[c >> 5][c & 31]);
-          const float dp = __uint_as_float(pv[c >> 5][c & 31]);
-          const float p = kbase + c <= qi ? ex2(fmaf(s, sl2, -L)) : 0.f;
-          d2[u] = p * (dp - Dr);
-        }
-        pk[e] = pack_bf16x2(d2[0], d2[1]);
+      if (j >= 2 * qb) {
+        dq_row<true>(sv, pv, sl2, L, Dr, qi - j * 64, pk);
+      } else {
+        dq_row<false>(sv, pv, sl2, L, Dr, 0, pk);
       }
       store_row64(smem_u32(sDS + (j & 1) * kDS), r, pk);
       fence_async_smem();
@@ -791,22 +859,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++waited;
       }
       const float* st = sStat + (i % kSlots) * 128;
-      const int q0 = (t0 + i) * 64;
       uint32_t pp[32], dd[32];
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        float p2[2], d2[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int c = 2 * e + u;
-          const float s = __uint_as_float(sv[c >> 5][c & 31]);
-          const float dp = __uint_as_float(pv[c >> 5][c & 31]);
-          const float p = q0 + c >= kj ? ex2(fmaf(s, sl2, -st[c])) : 0.f;
-          p2[u] = p;
-          d2[u] = p * (dp - st[64 + c]);
-        }
-        pp[e] = pack_bf16x2(p2[0], p2[1]);
-        dd[e] = pack_bf16x2(d2[0], d2[1]);
+      if (i < 2) {
+        dkdv_row<true>(sv, pv, sl2, st, kj - (t0 + i) * 64, pp, dd);
+      } else {
+        dkdv_row<false>(sv, pv, sl2, st, 0, pp, dd);
       }
       store_row64(smem_u32(sPT + (i & 1) * kP), r, pp);
       store_row64(smem_u32(sDST + (i & 1) * kP), r, dd);
