@@ -8,18 +8,22 @@
 // scaled by scale*log2(e).
 //
 // One CTA = 128 queries of one (batch, head); key/value tiles of 128.
-//   warp 0      TMA producer: Q once, then K/V tiles through a 4-slot ring in
+//   warp 0      TMA producer: Q once, then K/V tiles through a 5-slot ring in
 //               exactly the order the MMA warp consumes them
 //               (K0, K1, V0, K2, V1, K3, ...); allocates 512 TMEM columns
 //   warp 1      MMA issuer (one thread):  S_j = Q K_j^T into TMEM S[j%2]
 //               (double-buffered, so S_{j+1} overlaps softmax j), then
-//               O += P_j V_j into the TMEM O accumulator
-//   warps 2..5  softmax: thread = one query row (TMEM lane), so row max and
-//               row sum need no shuffles.  P_j (bf16) goes to shared memory
-//               in the SW128 K-major layout the MMA reads.  The running max
-//               is only raised when it grows by more than 2^8 (exact: P <= 256
-//               stays representable, O and l use the same stale max), so the
-//               O correction (tcgen05.ld/st of the accumulator) is rare.
+//               O += P_j V_j into the TMEM O accumulator, with P_j read
+//               straight from TMEM (written over S_j by the softmax warps), so
+//               shared memory only carries Q, K and V
+//   warps 2..9  softmax: two warps per TMEM lane quarter, each thread one
+//               query row and 64 of its 128 columns, so row max and row sum
+//               need no shuffles (the two halves meet once per step through
+//               shared memory).  P_j (bf16) is stored back into TMEM.
+//               The running max is only raised when it grows by more than
+//               2^8 (exact: P <= 256 stays representable, O and l use the
+//               same stale max), so the O correction (tcgen05.ld/st of the
+//               accumulator) is rare.
 // TMEM columns: S0 [0,128), S1 [128,256), O [256,384).
 // All waits are bounded (common.cuh); there is no TMA multicast.
 #include "common.cuh"
@@ -29,10 +33,9 @@ namespace tdb {
 namespace attn_tc {
 
 constexpr int BM = 128, BN = 128, D = 128;
-constexpr int kThreads = 192;
 constexpr int kBox = 128 * 128;  // one [128 rows][64 bf16] SW128 box = 16 KB
 constexpr int kTile = 2 * kBox;  // a 128 x 128 bf16 tile = two boxes
-constexpr int kSlots = 4;
+constexpr int kSlots = 5;
 constexpr int kTmemCols = 512;
 constexpr int kOCol = 256;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -48,9 +51,12 @@ struct alignas(8) Bars {
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
+  int vote[2][2][4];    // per (parity, half, quarter): this warp can go on
+  float red[2][2][BM];  // per (parity, half, row): partial row max (row sum at the end)
 };
 
-constexpr int kSmem = kTile + kSlots * kTile + 2 * kTile + 1024 + 256;
+constexpr int kThreads = 320;  // TMA warp, MMA warp, 8 softmax / score warps
+constexpr int kSmem = kTile + kSlots * kTile + 1024 + int(sizeof(Bars));
 static_assert(kSmem <= 232448, "shared memory budget");
 
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -88,55 +94,64 @@ __device__ __forceinline__ uint64_t desc_mn(uint32_t base, int k) {
   return smem_desc_sw128(base + k * 16 * 128, kBox, 1024);
 }
 
-// Row maximum of 128 scores held by this thread; 8 independent chains so the
-// dependent-latency stalls overlap.  MASK: causal diagonal tile (col > row is
-// excluded).
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Row maximum over this thread's 64 columns; 8 independent chains.  MASK:
+// columns c > lim are causally excluded.
 template <bool MASK>
-__device__ __forceinline__ float row_max(const uint32_t (&sr)[4][32], int r) {
+__device__ __forceinline__ float row_max64(const uint32_t (&sr)[2][32], int lim) {
   float mx[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
 #pragma unroll
-  for (int c = 0; c < 128; ++c) {
+  for (int c = 0; c < 64; ++c) {
     const float v = __uint_as_float(sr[c >> 5][c & 31]);
-    if (!MASK || c <= r) mx[c & 7] = fmaxf(mx[c & 7], v);
+    if (!MASK || c <= lim) mx[c & 7] = fmaxf(mx[c & 7], v);
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) mx[i] = fmaxf(mx[i], mx[i + 4]);
   return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
 }
 
-// P = exp2(s*sl2 - m) for the 128 scores of this row, stored as bf16 into the
-// SW128 K-major P tile (row r, two 64-column boxes); returns the row sum
-// (8 independent accumulators).
+// P = exp2(s*sl2 - m) for this thread's 64 columns as 32 packed bf16 pairs;
+// returns the partial row sum (8 accumulators).
 template <bool MASK>
-__device__ __forceinline__ float exp_store_row(const uint32_t (&sr)[4][32], int r, float sl2, float m, uint32_t prow,
-                                               uint32_t sw) {
+__device__ __forceinline__ float exp_row64(const uint32_t (&sr)[2][32], int lim, float sl2, float m,
+                                           uint32_t (&pk)[32]) {
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   const float neg = -m;
 #pragma unroll
-  for (int c8 = 0; c8 < 16; ++c8) {
-    uint32_t pk[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int c0 = c8 * 8 + 2 * e;
-      float p0 = ex2(fmaf(__uint_as_float(sr[c0 >> 5][c0 & 31]), sl2, neg));
-      float p1 = ex2(fmaf(__uint_as_float(sr[(c0 + 1) >> 5][(c0 + 1) & 31]), sl2, neg));
-      if (MASK) {
-        p0 = c0 <= r ? p0 : 0.f;
-        p1 = c0 + 1 <= r ? p1 : 0.f;
-      }
-      acc[2 * e] += p0;
-      acc[2 * e + 1] += p1;
-      pk[e] = pack_bf16x2(p0, p1);
+  for (int e = 0; e < 32; ++e) {
+    const int c0 = 2 * e;
+    float p0 = ex2(fmaf(__uint_as_float(sr[c0 >> 5][c0 & 31]), sl2, neg));
+    float p1 = ex2(fmaf(__uint_as_float(sr[(c0 + 1) >> 5][(c0 + 1) & 31]), sl2, neg));
+    if (MASK) {
+      p0 = c0 <= lim ? p0 : 0.f;
+      p1 = c0 + 1 <= lim ? p1 : 0.f;
     }
-    st_shared_v4(prow + (c8 >> 3) * kBox + ((uint32_t(c8 & 7) ^ sw) << 4), pk[0], pk[1], pk[2], pk[3]);
+    acc[(2 * e) & 7] += p0;
+    acc[(2 * e + 1) & 7] += p1;
+    pk[e] = pack_bf16x2(p0, p1);
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) acc[i] += acc[i + 4];
   return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16: A (M=128 rows = TMEM lanes,
+// bf16 pairs packed along columns, 8 columns per K=16 step) read straight
+// from tensor memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -146,8 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + kTile;
-  uint8_t* sP = sKV + kSlots * kTile;
-  Bars* bars = reinterpret_cast<Bars*>(sP + 2 * kTile);
+  Bars* bars = reinterpret_cast<Bars*>(sKV + kSlots * kTile);
 
   const int hb = blockIdx.x;  // (head, batch) fastest: all heads of the heaviest query tile launch first
   const int h = hb % Hl, b = hb / Hl;
@@ -165,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->p_full[i], 4);
+      mbar_init(&bars->p_full[i], 8);
     }
     mbar_init(&bars->pv_done, 1);
     mbar_init(&bars->drain, 1);
@@ -263,10 +277,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         uint32_t sv;
         if (!next_slot(sv)) return false;
-        const uint32_t sp = smem_u32(sP + (j & 1) * kTile);
+        // P_j (bf16 pairs) sits in the first 64 columns of TMEM buffer S[j%2].
+        const uint32_t tp = tmem + (j & 1) * BN;
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k)
-          umma_f16_ss(tmem + kOCol, desc_k(sp, k), desc_mn(sv, k), idO, (j | k) != 0 ? 1u : 0u);
+          umma_f16_ts(tmem + kOCol, tp + 8 * k, desc_mn(sv, k), idO, (j | k) != 0 ? 1u : 0u);
         umma_commit(&bars->kv_empty[it % kSlots]);
         umma_commit(&bars->pv_done);
         ++it;
@@ -286,33 +301,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax / correction / epilogue (warps 2..5) ----------------
+    // ---------------- softmax / correction / epilogue (warps 2..9) ----------------
+    // Two warps per TMEM lane quarter: `half` owns key columns [64*half, +64)
+    // of S and d columns [64*half, +64) of O.  The row max is combined
+    // through shared memory (64-thread named barrier per quarter); each half
+    // keeps its own partial row sum until the epilogue.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;  // query row within the tile (= TMEM lane)
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
+    const uint32_t bar_id = 1 + quarter;
     const float sl2 = scale * kLog2e;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    const uint32_t prow_sw = uint32_t(r & 7);
-    for (int j = 0; j < n && ok; ++j) {
-      if (!mbar_wait(&bars->s_full[j & 1], (j >> 1) & 1, status, 80)) { ok = false; break; }
-      if (*abort_flag) { ok = false; break; }
-      tc_fence_after();
-      uint32_t sr[4][32];
-      const uint32_t sbase = tmem + lane_off + (j & 1) * BN;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(sbase + c * 32, sr[c]);
-      tmem_wait_ld();
-      float mx, sum = 0.f;
+    // Every iteration runs one exchange barrier in both warps of the pair,
+    // whatever happens, so a bounded wait that expires in one of them can
+    // never leave the other stuck on the named barrier.
+    for (int j = 0; j < n; ++j) {
+      if (ok && !mbar_wait(&bars->s_full[j & 1], (j >> 1) & 1, status, 80)) ok = false;
+      if (*abort_flag) ok = false;
+      ok = __all_sync(0xffffffffu, ok);
+      uint32_t sr[2][32];
+      const bool diag = j == n - 1;
+      const int lim = r - 64 * half;  // diagonal tile: column c of this half is visible iff c <= lim
+      float mx = -INFINITY;
+      if (ok) {
+        tc_fence_after();
+        const uint32_t sbase = tmem + lane_off + (j & 1) * BN + 64 * half;
+        tmem_ld_32x32b_x32(sbase, sr[0]);
+        tmem_ld_32x32b_x32(sbase + 32, sr[1]);
+        tmem_wait_ld();
+        mx = diag ? row_max64<true>(sr, lim) : row_max64<false>(sr, lim);
+      }
+      bars->red[j & 1][half][r] = mx;
+      if (lane == 0) bars->vote[j & 1][half][quarter] = ok ? 1 : 0;
+      named_barrier(bar_id, 64);
+      ok = ok && bars->vote[j & 1][half ^ 1][quarter] != 0;
+      if (!ok) continue;
+      mx = fmaxf(mx, bars->red[j & 1][half ^ 1][r]);
+      const float cand = fmaxf(m, mx * sl2);
       float alpha = 1.f;
       bool rescale = false;
-      const uint32_t prow = smem_u32(sP + (j & 1) * kTile) + r * 128;
-      if (j == n - 1) {
-        mx = row_max<true>(sr, r);
-      } else {
-        mx = row_max<false>(sr, r);
-      }
-      const float cand = fmaxf(m, mx * sl2);
       if (j == 0) {
         m = cand;
       } else if (cand > m + kRescale) {
@@ -320,22 +349,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = cand;
         rescale = true;
       }
-      if (j == n - 1) {
-        sum = exp_store_row<true>(sr, r, sl2, m, prow, prow_sw);
-      } else {
-        sum = exp_store_row<false>(sr, r, sl2, m, prow, prow_sw);
-      }
+      // P overwrites S in place (columns [32*half, +32) of the buffer hold the
+      // bf16 pairs of keys [64*half, +64)); both halves have read their S
+      // values before the exchange barrier above.
+      uint32_t pk[32];
+      const float sum = diag ? exp_row64<true>(sr, lim, sl2, m, pk) : exp_row64<false>(sr, lim, sl2, m, pk);
+      tmem_st_32x32b_x32(tmem + lane_off + (j & 1) * BN + 32 * half, pk);
       l = l * alpha + sum;
-      fence_async_smem();
+      tmem_wait_st();
       if (j > 0) {
         // O correction needs PV_{j-1} landed; it was issued a full softmax step ago.
-        if (!mbar_wait(&bars->pv_done, (j - 1) & 1, status, 81)) { ok = false; break; }
+        ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done, (j - 1) & 1, status, 81));
+        if (!ok) continue;
         tc_fence_after();
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
             uint32_t o[32];
-            const uint32_t oaddr = tmem + lane_off + kOCol + c * 32;
+            const uint32_t oaddr = tmem + lane_off + kOCol + 64 * half + c * 32;
             tmem_ld_32x32b_x32(oaddr, o);
             tmem_wait_ld();
 #pragma unroll
@@ -350,14 +381,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&bars->p_full[j & 1]);
     }
     if (!ok) *abort_flag = 1;
+    // combine the two partial row sums (one more barrier in both warps)
+    // (parity n & 1: its last readers finished before the barrier of step n-1)
+    bars->red[n & 1][half][r] = l;
+    if (lane == 0) bars->vote[n & 1][half][quarter] = ok ? 1 : 0;
+    named_barrier(bar_id, 64);
+    ok = ok && bars->vote[n & 1][half ^ 1][quarter] != 0;
+    l += bars->red[n & 1][half ^ 1][r];
     if (ok && mbar_wait(&bars->pv_done, (n - 1) & 1, status, 82)) {
       tc_fence_after();
       const float inv = 1.f / l;
-      uint16_t* orow = out + int64_t(row0 + qb * BM + r) * ld_out + h * D;
+      uint16_t* orow = out + int64_t(row0 + qb * BM + r) * ld_out + h * D + 64 * half;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + kOCol + c * 32, o);
+        tmem_ld_32x32b_x32(tmem + lane_off + kOCol + 64 * half + c * 32, o);
         tmem_wait_ld();
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
@@ -369,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint4*>(orow + c * 32 + 8 * v) = w;
         }
       }
-      lse[(int64_t(b) * Hl + h) * seq + qb * BM + r] = m + log2f(l);
+      if (half == 0) lse[(int64_t(b) * Hl + h) * seq + qb * BM + r] = m + log2f(l);
     }
   }
 
@@ -401,23 +439,52 @@ __device__ __forceinline__ uint64_t desc_k64(uint32_t base, int k) {
 __device__ __forceinline__ uint64_t desc_mn64(uint32_t base, int k) {
   return smem_desc_sw128(base + k * 16 * 128, 8192, 1024);
 }
-// One [128 rows][64 cols] K-major box (16 KB): K step k.
-__device__ __forceinline__ uint64_t desc_box(uint32_t base, int k) {
-  return smem_desc_sw128(base + k * 32, 16, 1024);
-}
 
-// Store 64 bf16 values (packed pairs) as row r of a [128][64] SW128 box.
-__device__ __forceinline__ void store_row64(uint32_t box, int r, const uint32_t (&pk)[32]) {
-  const uint32_t row = box + r * 128, sw = uint32_t(r & 7);
+
+// dS for this thread's 32 key columns of the dQ kernel:
+// ds = exp2(s*sl2 - lse) * (dp - Dsum).  MASK: columns c > lim are excluded.
+template <bool MASK>
+__device__ __forceinline__ void dq_row32(const uint32_t (&sv)[32], const uint32_t (&pv)[32], float sl2, float L,
+                                         float Dr, int lim, uint32_t (&pk)[16]) {
+  const float nl = -L;
 #pragma unroll
-  for (int c8 = 0; c8 < 8; ++c8)
-    st_shared_v4(row + ((uint32_t(c8) ^ sw) << 4), pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
+  for (int e = 0; e < 16; ++e) {
+    float d2[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int c = 2 * e + u;
+      float p = ex2(fmaf(__uint_as_float(sv[c]), sl2, nl));
+      if (MASK) p = c <= lim ? p : 0.f;
+      d2[u] = p * (__uint_as_float(pv[c]) - Dr);
+    }
+    pk[e] = pack_bf16x2(d2[0], d2[1]);
+  }
 }
 
-// Write 128 fp32 TMEM columns of this thread's row (times mul) as bf16.
-__device__ __forceinline__ void tmem_row_to_bf16(uint32_t taddr, float mul, uint16_t* dst) {
+// P^T and dS^T for this thread's 32 query columns of the dK/dV kernel (lse /
+// Dsum per column from shared memory).  MASK: columns c < lim are excluded.
+template <bool MASK>
+__device__ __forceinline__ void dkdv_row32(const uint32_t (&sv)[32], const uint32_t (&pv)[32], float sl2,
+                                           const float* st, int lim, uint32_t (&pp)[16], uint32_t (&dd)[16]) {
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const float2 lse2 = *reinterpret_cast<const float2*>(st + 2 * e);
+    const float2 ds2 = *reinterpret_cast<const float2*>(st + 64 + 2 * e);
+    float p0 = ex2(fmaf(__uint_as_float(sv[2 * e]), sl2, -lse2.x));
+    float p1 = ex2(fmaf(__uint_as_float(sv[2 * e + 1]), sl2, -lse2.y));
+    if (MASK) {
+      p0 = 2 * e >= lim ? p0 : 0.f;
+      p1 = 2 * e + 1 >= lim ? p1 : 0.f;
+    }
+    pp[e] = pack_bf16x2(p0, p1);
+    dd[e] = pack_bf16x2(p0 * (__uint_as_float(pv[2 * e]) - ds2.x), p1 * (__uint_as_float(pv[2 * e + 1]) - ds2.y));
+  }
+}
+
+// Write `chunks` x 32 fp32 TMEM columns of this thread's row (times mul) as bf16.
+__device__ __forceinline__ void tmem_cols_to_bf16(uint32_t taddr, int chunks, float mul, uint16_t* dst) {
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < chunks; ++c) {
     uint32_t o[32];
     tmem_ld_32x32b_x32(taddr + c * 32, o);
     tmem_wait_ld();
@@ -433,69 +500,50 @@ __device__ __forceinline__ void tmem_row_to_bf16(uint32_t taddr, float mul, uint
   }
 }
 
-// dS row (64 keys) of the dQ kernel: ds = exp2(s*sl2 - lse) * (dp - Dsum).
-// MASK: keys c > lim are causally excluded.
-template <bool MASK>
-__device__ __forceinline__ void dq_row(const uint32_t (&sv)[2][32], const uint32_t (&pv)[2][32], float sl2, float L,
-                                       float Dr, int lim, uint32_t (&pk)[32]) {
-  const float nl = -L;
-#pragma unroll
-  for (int e = 0; e < 32; ++e) {
-    float d2[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int c = 2 * e + u;
-      float p = ex2(fmaf(__uint_as_float(sv[c >> 5][c & 31]), sl2, nl));
-      if (MASK) p = c <= lim ? p : 0.f;
-      d2[u] = p * (__uint_as_float(pv[c >> 5][c & 31]) - Dr);
-    }
-    pk[e] = pack_bf16x2(d2[0], d2[1]);
-  }
-}
-
-// P^T and dS^T rows (64 queries) of the dK/dV kernel; lse / Dsum per query
-// column from shared memory.  MASK: queries c < lim are causally excluded.
-template <bool MASK>
-__device__ __forceinline__ void dkdv_row(const uint32_t (&sv)[2][32], const uint32_t (&pv)[2][32], float sl2,
-                                         const float* st, int lim, uint32_t (&pp)[32], uint32_t (&dd)[32]) {
-#pragma unroll
-  for (int e = 0; e < 32; ++e) {
-    const float2 lse2 = *reinterpret_cast<const float2*>(st + 2 * e);
-    const float2 ds2 = *reinterpret_cast<const float2*>(st + 64 + 2 * e);
-    float p0 = ex2(fmaf(__uint_as_float(sv[(2 * e) >> 5][(2 * e) & 31]), sl2, -lse2.x));
-    float p1 = ex2(fmaf(__uint_as_float(sv[(2 * e + 1) >> 5][(2 * e + 1) & 31]), sl2, -lse2.y));
-    if (MASK) {
-      p0 = 2 * e >= lim ? p0 : 0.f;
-      p1 = 2 * e + 1 >= lim ? p1 : 0.f;
-    }
-    pp[e] = pack_bf16x2(p0, p1);
-    dd[e] = pack_bf16x2(p0 * (__uint_as_float(pv[(2 * e) >> 5][(2 * e) & 31]) - ds2.x),
-                        p1 * (__uint_as_float(pv[(2 * e + 1) >> 5][(2 * e + 1) & 31]) - ds2.y));
-  }
+// ---------------------------------------------------------------------------
+// Backward warp layout (both kernels): warp 0 TMA, warp 1 MMA, warps 2..9
+// score warps.  Score steps are independent (no running statistics), so the
+// two warps of a TMEM lane quarter take alternate steps: half h owns steps
+// i = h, h+2, ... and with them TMEM buffer h (scores and their gradient
+// operands), which removes any sharing between warps.  The bf16 operand of
+// the second GEMM pair (P^T, dS^T or dS) is written back into TMEM over the
+// fp32 scores it came from and read from there by tcgen05.mma (A operand in
+// tensor memory), so shared memory only carries the TMA tiles.  A buffer is
+// rewritten by the MMA warp only after the GEMMs that read it (one thread,
+// in-order issue), and the score warps see the new scores through the
+// commit that also covers those GEMMs.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
 }
 
 // ---------------------------------------------------------------------------
-// dQ: CTA = 128 queries; key/value tiles of 64 through a 6-slot ring
+// dQ: CTA = 128 queries; key/value tiles of 64 through a ring
 // (K0, V0, K1, V1, ...).  K_j stays until dQ += dS_j K_j has read it.
-// TMEM: S[2] cols 0/64, dP[2] cols 128/192, dQ cols 256..383.
+// TMEM: S[2] cols 0/64 (dS bf16 pairs over their first 32 columns),
+// dP[2] cols 128/192, dQ cols 256..383.
 // ---------------------------------------------------------------------------
 namespace dqk {
-constexpr int kKV = 64 * 128 * 2;   // [64 keys][128 d] = two 8 KB boxes
-constexpr int kDS = 128 * 64 * 2;   // [128 q][64 keys] = one 16 KB box
-constexpr int kSlots = 6;
-constexpr int kSmem = 2 * kTile + kSlots * kKV + 2 * kDS + 1024 + 256;
-static_assert(kSmem <= 232448, "shared memory budget");
+constexpr int kKV = 64 * 128 * 2;  // [64 keys][128 d] = two 8 KB boxes
+constexpr int kSlots = 8;
 struct alignas(8) Bars {
   uint64_t q_full;
   uint64_t kv_full[kSlots];
   uint64_t kv_empty[kSlots];
   uint64_t s_full[2];
   uint64_t ds_full[2];
-  uint64_t dq_done;
+  uint64_t done;
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
 };
+constexpr int kSmem = 2 * kTile + kSlots * kKV + 1024 + int(sizeof(Bars));
+static_assert(kSmem <= 232448, "shared memory budget");
 }  // namespace dqk
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -503,15 +551,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const __grid_constant__ CUtensorMap tdo, const float* __restrict__ lse,
                   const float* __restrict__ dsum, uint16_t* __restrict__ dqkv, int64_t ld_dqkv, int seq, int Hl,
                   float scale, int* status) {
-  constexpr int kSlots = dqk::kSlots, kKV = dqk::kKV, kDS = dqk::kDS;
+  constexpr int kSlots = dqk::kSlots, kKV = dqk::kKV;
   using Bars = dqk::Bars;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sDO = sQ + kTile;
   uint8_t* sKV = sDO + kTile;
-  uint8_t* sDS = sKV + kSlots * kKV;
-  Bars* bars = reinterpret_cast<Bars*>(sDS + 2 * kDS);
+  Bars* bars = reinterpret_cast<Bars*>(sKV + kSlots * kKV);
 
   const int hb = blockIdx.x;
   const int h = hb % Hl, b = hb / Hl;
@@ -531,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->ds_full[i], 4);
     }
-    mbar_init(&bars->dq_done, 1);
+    mbar_init(&bars->done, 1);
     mbar_init(&bars->drain, 1);
     bars->abort_flag = 0;
     fence_barrier_init();
@@ -610,14 +657,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < n && ok; ++j) {
         if (!mbar_wait(&bars->ds_full[j & 1], (j >> 1) & 1, status, 102)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sds = smem_u32(sDS + (j & 1) * kDS);
         const uint32_t sk = smem_u32(sKV + ((2 * j) % kSlots) * kKV);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) umma_f16_ss(tmem + 256, desc_box(sds, k), desc_mn64(sk, k), idQ, (j | k) ? 1u : 0u);
+        for (int k = 0; k < 4; ++k)
+          umma_f16_ts(tmem + 256, tmem + (j & 1) * 64 + 8 * k, desc_mn64(sk, k), idQ, (j | k) ? 1u : 0u);
         umma_commit(&bars->kv_empty[(2 * j) % kSlots]);
-        umma_commit(&bars->dq_done);
         if (j + 2 < n) ok = issue_sdp(j + 2);
       }
+      if (ok) umma_commit(&bars->done);
       if (!ok) *abort_flag = 1;
       if (issued) {
         umma_commit(&bars->drain);
@@ -626,6 +673,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;  // this warp takes key tiles j = half, half + 2, ...
     const int r = quarter * 32 + lane;
     const int qi = qb * BM + r;
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
@@ -633,41 +681,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t stat = (int64_t(b) * Hl + h) * seq + qi;
     const float L = lse[stat], Dr = dsum[stat];
     bool ok = true;
-    int waited = 0;  // dq_done phases observed
-    for (int j = 0; j < n && ok; ++j) {
-      if (!mbar_wait(&bars->s_full[j & 1], (j >> 1) & 1, status, 110)) { ok = false; break; }
+    const uint32_t sbuf = tmem + lane_off + half * 64, pbuf = sbuf + 128;
+    for (int j = half; j < n && ok; j += 2) {
+      if (!mbar_wait(&bars->s_full[half], (j >> 1) & 1, status, 110)) { ok = false; break; }
       if (*abort_flag) { ok = false; break; }
       tc_fence_after();
-      uint32_t sv[2][32], pv[2][32];
-      tmem_ld_32x32b_x32(tmem + lane_off + (j & 1) * 64, sv[0]);
-      tmem_ld_32x32b_x32(tmem + lane_off + (j & 1) * 64 + 32, sv[1]);
-      tmem_ld_32x32b_x32(tmem + lane_off + 128 + (j & 1) * 64, pv[0]);
-      tmem_ld_32x32b_x32(tmem + lane_off + 128 + (j & 1) * 64 + 32, pv[1]);
-      tmem_wait_ld();
-      if (j >= 2) {  // dS buffer j%2 was read by dQ_{j-2}
-        if (!mbar_wait(&bars->dq_done, waited & 1, status, 111)) { ok = false; break; }
-        ++waited;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {  // 32 keys at a time; dS of keys [32c, +32) -> columns [16c, +16)
+        uint32_t sv[32], pv[32], pk[16];
+        tmem_ld_32x32b_x32(sbuf + 32 * c, sv);
+        tmem_ld_32x32b_x32(pbuf + 32 * c, pv);
+        tmem_wait_ld();
+        if (j >= 2 * qb) {
+          dq_row32<true>(sv, pv, sl2, L, Dr, qi - j * 64 - 32 * c, pk);
+        } else {
+          dq_row32<false>(sv, pv, sl2, L, Dr, 0, pk);
+        }
+        tmem_st_32x32b_x16(sbuf + 16 * c, pk);
       }
-      uint32_t pk[32];
-      if (j >= 2 * qb) {
-        dq_row<true>(sv, pv, sl2, L, Dr, qi - j * 64, pk);
-      } else {
-        dq_row<false>(sv, pv, sl2, L, Dr, 0, pk);
-      }
-      store_row64(smem_u32(sDS + (j & 1) * kDS), r, pk);
-      fence_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->ds_full[j & 1]);
+      if (lane == 0) mbar_arrive(&bars->ds_full[half]);
     }
     if (!ok) *abort_flag = 1;
-    while (ok && waited < n) {
-      if (!mbar_wait(&bars->dq_done, waited & 1, status, 112)) ok = false;
-      ++waited;
-    }
-    if (ok) {
+    if (ok && mbar_wait(&bars->done, 0, status, 112)) {
       tc_fence_after();
-      tmem_row_to_bf16(tmem + lane_off + 256, scale, dqkv + int64_t(row0 + qi) * ld_dqkv + h * D);
+      tmem_cols_to_bf16(tmem + lane_off + 256 + 64 * half, 2, scale,
+                        dqkv + int64_t(row0 + qi) * ld_dqkv + h * D + 64 * half);
     }
   }
   tc_fence_before();
@@ -678,29 +719,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------------------
 // dK, dV: CTA = 128 keys; query tiles of 64 (Q_i, dO_i, lse_i, Dsum_i)
-// through a 3-slot ring.  S^T = K Q_i^T, dP^T = V dO_i^T (thread = key row),
+// through a ring.  S^T = K Q_i^T, dP^T = V dO_i^T (thread = key row),
 // dV += P^T dO_i, dK += dS^T Q_i (the Q_i / dO_i tiles serve as the K-major B
-// operand of the first pair and the MN-major B operand of the second).
-// TMEM: S^T[2] cols 0/64, dP^T[2] cols 128/192, dV 256.., dK 384..
+// operand of the first pair and the MN-major B operand of the second; P^T
+// and dS^T are the TMEM A operands).
+// TMEM: S^T[2] cols 0/64 (P^T over their first 32), dP^T[2] cols 128/192
+// (dS^T over their first 32), dV 256.., dK 384..
 // ---------------------------------------------------------------------------
 namespace dkv {
 constexpr int kQ = 64 * 128 * 2;  // [64 q][128 d] = two 8 KB boxes
 constexpr int kSlot = 2 * kQ;     // Q_i then dO_i
-constexpr int kP = 128 * 64 * 2;  // [128 keys][64 q] box
-constexpr int kSlots = 3;
-constexpr int kSmem = 2 * kTile + kSlots * kSlot + 4 * kP + kSlots * 512 + 1024 + 256;
-static_assert(kSmem <= 232448, "shared memory budget");
+constexpr int kSlots = 4;
 struct alignas(8) Bars {
   uint64_t kv_full;
   uint64_t q_full[kSlots];
   uint64_t q_empty[kSlots];
   uint64_t s_full[2];
   uint64_t p_full[2];
-  uint64_t mm_done;
+  uint64_t done;
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
 };
+constexpr int kSmem = 2 * kTile + kSlots * kSlot + kSlots * 512 + 1024 + int(sizeof(Bars));
+static_assert(kSmem <= 232448, "shared memory budget");
 }  // namespace dkv
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -708,16 +750,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tdo, const float* __restrict__ lse,
                     const float* __restrict__ dsum, uint16_t* __restrict__ dqkv, int64_t ld_dqkv, int seq, int Hl,
                     float scale, int* status) {
-  constexpr int kSlots = dkv::kSlots, kQ = dkv::kQ, kSlot = dkv::kSlot, kP = dkv::kP;
+  constexpr int kSlots = dkv::kSlots, kQ = dkv::kQ, kSlot = dkv::kSlot;
   using Bars = dkv::Bars;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
   uint8_t* sV = sK + kTile;
   uint8_t* sRing = sV + kTile;
-  uint8_t* sPT = sRing + kSlots * kSlot;   // 2 buffers
-  uint8_t* sDST = sPT + 2 * kP;            // 2 buffers
-  float* sStat = reinterpret_cast<float*>(sDST + 2 * kP);  // per slot: lse[64], dsum[64]
+  float* sStat = reinterpret_cast<float*>(sRing + kSlots * kSlot);  // per slot: lse[64], dsum[64]
   Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(sStat) + kSlots * 512);
 
   const int hb = blockIdx.x;
@@ -741,7 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_full[i], 4);
     }
-    mbar_init(&bars->mm_done, 1);
+    mbar_init(&bars->done, 1);
     mbar_init(&bars->drain, 1);
     bars->abort_flag = 0;
     fence_barrier_init();
@@ -819,15 +859,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const int s = i % kSlots;
         const uint32_t sq = smem_u32(sRing + s * kSlot), sdo = sq + kQ;
-        const uint32_t spt = smem_u32(sPT + (i & 1) * kP), sdst = smem_u32(sDST + (i & 1) * kP);
+        const uint32_t tpt = tmem + (i & 1) * 64, tdst = tmem + 128 + (i & 1) * 64;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) umma_f16_ss(tmem + 256, desc_box(spt, k), desc_mn64(sdo, k), idG, (i | k) ? 1u : 0u);
+        for (int k = 0; k < 4; ++k) umma_f16_ts(tmem + 256, tpt + 8 * k, desc_mn64(sdo, k), idG, (i | k) ? 1u : 0u);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) umma_f16_ss(tmem + 384, desc_box(sdst, k), desc_mn64(sq, k), idG, (i | k) ? 1u : 0u);
+        for (int k = 0; k < 4; ++k) umma_f16_ts(tmem + 384, tdst + 8 * k, desc_mn64(sq, k), idG, (i | k) ? 1u : 0u);
         umma_commit(&bars->q_empty[s]);
-        umma_commit(&bars->mm_done);
         if (i + 2 < n) ok = issue_sdp(i + 2);
       }
+      if (ok) umma_commit(&bars->done);
       if (!ok) *abort_flag = 1;
       if (issued) {
         umma_commit(&bars->drain);
@@ -836,52 +876,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;  // this warp takes query tiles i = half, half + 2, ...
     const int r = quarter * 32 + lane;
     const int kj = kb * BM + r;  // this thread's key
     const uint32_t lane_off = uint32_t(quarter * 32) << 16;
     const float sl2 = scale * kLog2e;
     bool ok = true;
-    int waited = 0;
-    for (int i = 0; i < n && ok; ++i) {
-      if (!mbar_wait(&bars->s_full[i & 1], (i >> 1) & 1, status, 140)) { ok = false; break; }
+    const uint32_t sbuf = tmem + lane_off + half * 64, pbuf = sbuf + 128;
+    for (int i = half; i < n && ok; i += 2) {
+      if (!mbar_wait(&bars->s_full[half], (i >> 1) & 1, status, 140)) { ok = false; break; }
       // the lse / Dsum rows of this tile arrived with Q_i (same transaction barrier)
       if (!mbar_wait(&bars->q_full[i % kSlots], (i / kSlots) & 1, status, 141)) { ok = false; break; }
       if (*abort_flag) { ok = false; break; }
       tc_fence_after();
-      uint32_t sv[2][32], pv[2][32];
-      tmem_ld_32x32b_x32(tmem + lane_off + (i & 1) * 64, sv[0]);
-      tmem_ld_32x32b_x32(tmem + lane_off + (i & 1) * 64 + 32, sv[1]);
-      tmem_ld_32x32b_x32(tmem + lane_off + 128 + (i & 1) * 64, pv[0]);
-      tmem_ld_32x32b_x32(tmem + lane_off + 128 + (i & 1) * 64 + 32, pv[1]);
-      tmem_wait_ld();
-      if (i >= 2) {  // P^T / dS^T buffers i%2 were read by the GEMMs of step i-2
-        if (!mbar_wait(&bars->mm_done, waited & 1, status, 142)) { ok = false; break; }
-        ++waited;
-      }
       const float* st = sStat + (i % kSlots) * 128;
-      uint32_t pp[32], dd[32];
-      if (i < 2) {
-        dkdv_row<true>(sv, pv, sl2, st, kj - (t0 + i) * 64, pp, dd);
-      } else {
-        dkdv_row<false>(sv, pv, sl2, st, 0, pp, dd);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {  // 32 queries at a time -> bf16 pairs in columns [16c, +16)
+        uint32_t sv[32], pv[32], pp[16], dd[16];
+        tmem_ld_32x32b_x32(sbuf + 32 * c, sv);
+        tmem_ld_32x32b_x32(pbuf + 32 * c, pv);
+        tmem_wait_ld();
+        if (i < 2) {
+          dkdv_row32<true>(sv, pv, sl2, st + 32 * c, kj - (t0 + i) * 64 - 32 * c, pp, dd);
+        } else {
+          dkdv_row32<false>(sv, pv, sl2, st + 32 * c, 0, pp, dd);
+        }
+        tmem_st_32x32b_x16(sbuf + 16 * c, pp);
+        tmem_st_32x32b_x16(pbuf + 16 * c, dd);
       }
-      store_row64(smem_u32(sPT + (i & 1) * kP), r, pp);
-      store_row64(smem_u32(sDST + (i & 1) * kP), r, dd);
-      fence_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[i & 1]);
+      if (lane == 0) mbar_arrive(&bars->p_full[half]);
     }
     if (!ok) *abort_flag = 1;
-    while (ok && waited < n) {
-      if (!mbar_wait(&bars->mm_done, waited & 1, status, 143)) ok = false;
-      ++waited;
-    }
-    if (ok) {
+    if (ok && mbar_wait(&bars->done, 0, status, 143)) {
       tc_fence_after();
-      uint16_t* rowp = dqkv + int64_t(row0 + kj) * ld_dqkv;
-      tmem_row_to_bf16(tmem + lane_off + 256, 1.f, rowp + (2 * Hl + h) * D);
-      tmem_row_to_bf16(tmem + lane_off + 384, scale, rowp + (Hl + h) * D);
+      uint16_t* rowp = dqkv + int64_t(row0 + kj) * ld_dqkv + 64 * half;
+      tmem_cols_to_bf16(tmem + lane_off + 256 + 64 * half, 2, 1.f, rowp + (2 * Hl + h) * D);
+      tmem_cols_to_bf16(tmem + lane_off + 384 + 64 * half, 2, scale, rowp + (Hl + h) * D);
     }
   }
   tc_fence_before();

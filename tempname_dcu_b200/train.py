@@ -64,6 +64,17 @@ class Trainer:
         self._tokens = torch.empty((accum, m), dtype=torch.int64, device=self.device)
         self._labels = torch.empty((accum, m), dtype=torch.int64, device=self.device)
 
+    def save_checkpoint(self, directory, plan_sha256=None):
+        """Sharded checkpoint of masters + Adam state (utils/checkpoint.py);
+        collective over the tensor-parallel group."""
+        from .utils import checkpoint
+        return checkpoint.save(self, directory, plan_sha256=plan_sha256)
+
+    def load_checkpoint(self, directory, plan_sha256=None):
+        """Resume from ``save_checkpoint``; returns the restored optimizer step."""
+        from .utils import checkpoint
+        return checkpoint.load(self, directory, plan_sha256=plan_sha256)
+
     def step(self, tokens, labels):
         """One optimizer step over ``accumulation_steps`` micro-batches.
 
