@@ -156,7 +156,15 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
 
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_kernel(const __grid_constant__ CUtensorMap tm, uint16_t* __restrict__ out, int64_t ld_out,
-               float* __restrict__ lse, int seq, int Hl, int mb, float scale, int* status) {
+               float* __restrict__ lse, int seq, int Hl, int mb, float scale, int* status,
+               unsigned long long* __restrict__ tl) {
+  // Optional diagnostic timeline (clock64 per pipeline event of the first
+  // CTA, tl[16 * step + event]); null in normal use.
+  const bool tl_on = tl != nullptr && blockIdx.x == 0 && blockIdx.y == 0;
+#define TDB_TL(step, ev) \
+  do {                     \
+    if (tl_on) tl[16 * (step) + (ev)] = clock64(); \
+  } while (0)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
@@ -233,6 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (*abort_flag) { ok = false; break; }
         uint8_t* dst = sKV + s * kTile;
         const int col = (is_v ? 2 * Hl + h : Hl + h) * D;
+        TDB_TL(j, is_v ? 1 : 0);
         mbar_arrive_expect_tx(&bars->kv_full[s], kTile);
         tma_load_2d(dst, &tm, &bars->kv_full[s], col, row0 + j * BN);
         tma_load_2d(dst + kBox, &tm, &bars->kv_full[s], col + 64, row0 + j * BN);
@@ -263,6 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_s = [&](int j) -> bool {
         uint32_t sk;
         if (!next_slot(sk)) return false;
+        TDB_TL(j, 2);
         const uint32_t d = tmem + (j & 1) * BN;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) umma_f16_ss(d, desc_k(sq, k), desc_k(sk, k), idS, k > 0 ? 1u : 0u);
@@ -274,9 +284,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       auto issue_pv = [&](int j) -> bool {
         if (!mbar_wait(&bars->p_full[j & 1], (j >> 1) & 1, status, 72)) return false;
+        TDB_TL(j, 3);
         tc_fence_after();
         uint32_t sv;
         if (!next_slot(sv)) return false;
+        TDB_TL(j, 4);
         // P_j (bf16 pairs) sits in the first 64 columns of TMEM buffer S[j%2].
         const uint32_t tp = tmem + (j & 1) * BN;
 #pragma unroll
@@ -319,6 +331,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // never leave the other stuck on the named barrier.
     for (int j = 0; j < n; ++j) {
       if (ok && !mbar_wait(&bars->s_full[j & 1], (j >> 1) & 1, status, 80)) ok = false;
+      const bool stamp = warp == 2 && lane == 0;
+      if (stamp) TDB_TL(j, 5);
       if (*abort_flag) ok = false;
       ok = __all_sync(0xffffffffu, ok);
       uint32_t sr[2][32];
@@ -331,11 +345,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(sbase, sr[0]);
         tmem_ld_32x32b_x32(sbase + 32, sr[1]);
         tmem_wait_ld();
+        if (stamp) TDB_TL(j, 6);
         mx = diag ? row_max64<true>(sr, lim) : row_max64<false>(sr, lim);
       }
       bars->red[j & 1][half][r] = mx;
       if (lane == 0) bars->vote[j & 1][half][quarter] = ok ? 1 : 0;
       named_barrier(bar_id, 64);
+      if (stamp) TDB_TL(j, 7);
       ok = ok && bars->vote[j & 1][half ^ 1][quarter] != 0;
       if (!ok) continue;
       mx = fmaxf(mx, bars->red[j & 1][half ^ 1][r]);
@@ -357,9 +373,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_st_32x32b_x32(tmem + lane_off + (j & 1) * BN + 32 * half, pk);
       l = l * alpha + sum;
       tmem_wait_st();
+      if (stamp) TDB_TL(j, 8);
       if (j > 0) {
         // O correction needs PV_{j-1} landed; it was issued a full softmax step ago.
         ok = __all_sync(0xffffffffu, mbar_wait(&bars->pv_done, (j - 1) & 1, status, 81));
+        if (stamp) TDB_TL(j, 9);
         if (!ok) continue;
         tc_fence_after();
         if (__any_sync(0xffffffffu, rescale)) {
@@ -379,6 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[j & 1]);
+      if (stamp) TDB_TL(j, 10);
     }
     if (!ok) *abort_flag = 1;
     // combine the two partial row sums (one more barrier in both warps)
@@ -416,6 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, kTmemCols);
   (void)mb;
+#undef TDB_TL
 }
 
 
@@ -928,8 +948,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // qkv [mb*seq, ld] (Q|K|V column blocks of Hl*128), out [mb*seq, ld_out],
 // lse [mb, Hl, seq].  Requires seq % 128 == 0 and 16-byte aligned rows.
-TDB_API int tdb_attn_fwd_tc(const void* qkv, int64_t ld, void* out, int64_t ld_out, float* lse, int mb, int seq,
-                            int Hl, float scale, void* stream) {
+static int attn_fwd_tc_launch(const void* qkv, int64_t ld, void* out, int64_t ld_out, float* lse, int mb, int seq,
+                              int Hl, float scale, void* stream, unsigned long long* tl) {
   using namespace tdb::attn_tc;
   if (!qkv || !out || !lse || mb <= 0 || seq <= 0 || Hl <= 0 || seq % BM || ld % 8 || ld_out % 8 ||
       ld < int64_t(3) * Hl * D || ld_out < int64_t(Hl) * D || reinterpret_cast<uintptr_t>(out) % 16)
@@ -947,10 +967,22 @@ TDB_API int tdb_attn_fwd_tc(const void* qkv, int64_t ld, void* out, int64_t ld_o
   }
   dim3 grid(Hl * mb, seq / BM);
   fwd_kernel<<<grid, kThreads, kSmem, static_cast<cudaStream_t>(stream)>>>(
-      tm, static_cast<uint16_t*>(out), ld_out, lse, seq, Hl, mb, scale, tdb_host::status_ptr());
+      tm, static_cast<uint16_t*>(out), ld_out, lse, seq, Hl, mb, scale, tdb_host::status_ptr(), tl);
   tdb_host::launched(1);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : tdb_host::fail(int(e), "attention fwd (tcgen05) launch: %s", cudaGetErrorString(e));
+}
+
+TDB_API int tdb_attn_fwd_tc(const void* qkv, int64_t ld, void* out, int64_t ld_out, float* lse, int mb, int seq,
+                            int Hl, float scale, void* stream) {
+  return attn_fwd_tc_launch(qkv, ld, out, ld_out, lse, mb, seq, Hl, scale, stream, nullptr);
+}
+
+// Diagnostic variant: also records the pipeline timeline of the first CTA
+// into tl (uint64 [16 * steps], clock64 values; see fwd_kernel).
+TDB_API int tdb_attn_fwd_tc_timeline(const void* qkv, int64_t ld, void* out, int64_t ld_out, float* lse, int mb,
+                                     int seq, int Hl, float scale, void* stream, unsigned long long* tl) {
+  return attn_fwd_tc_launch(qkv, ld, out, ld_out, lse, mb, seq, Hl, scale, stream, tl);
 }
 
 TDB_API int tdb_attn_bwd_pre(const void* out, int64_t ld_out, const void* dout, int64_t ld_dout, float* dsum, int mb,

@@ -4,6 +4,7 @@
     python -m tempname_dcu_b200.ops.microbench ncu-gemm M N K [--mode fwd|dgrad|wgrad]
     python -m tempname_dcu_b200.ops.microbench attn [--seq 2048 --heads 32 --mb 1] [--iters 20]
     python -m tempname_dcu_b200.ops.microbench ncu-attn [--impl tc] [--seq 2048 --heads 8]
+    python -m tempname_dcu_b200.ops.microbench attn-timeline [--seq 2048 --heads 32]
 
 Each measurement: warm-up launches, then ``iters`` timed launches, each
 preceded by a write of a 256 MB buffer (larger than the 126 MB L2) so that
@@ -164,6 +165,43 @@ def bench_attn(mb, seq, heads, iters):
     return rows
 
 
+TIMELINE_EVENTS = ("tma_K", "tma_V", "mma_S", "mma_p_full", "mma_PV", "sm_s_full", "sm_S_loaded", "sm_max_xchg",
+                   "sm_P_stored", "sm_pv_done", "sm_p_full")
+
+
+def attn_timeline(seq, heads):
+    """Pipeline timeline of the heaviest forward CTA (clock64 cycles relative
+    to its first event) -- a diagnostic of the tcgen05 attention schedule."""
+    import ctypes
+    import torch
+    from . import kernels, native
+    lib = native.lib()
+    fn = lib.tdb_attn_fwd_tc_timeline
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int,
+                   ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]
+    fn.restype = ctypes.c_int
+    device = torch.device("cuda", 0)
+    qkv = torch.randn(seq, 3 * heads * 128, device=device).to(torch.bfloat16)
+    out = torch.empty(seq, heads * 128, dtype=torch.bfloat16, device=device)
+    lse = torch.empty(1, heads, seq, dtype=torch.float32, device=device)
+    steps = seq // 128
+    tl = torch.zeros(16 * steps, dtype=torch.int64, device=device)
+    for _ in range(3):
+        kernels.attention_fwd(qkv, 1, seq, heads, out=out, lse=lse)
+        native.check(fn(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0), lse.data_ptr(), 1, seq, heads,
+                        1.0 / 128 ** 0.5, native.stream_ptr(), tl.data_ptr()), "attn timeline")
+    torch.cuda.synchronize()
+    t = tl.view(steps, 16)[:, :len(TIMELINE_EVENTS)].cpu()
+    base = int(t[t > 0].min())
+    rows = []
+    for j in range(steps):
+        row = {name: (int(t[j, k]) - base if int(t[j, k]) else None) for k, name in enumerate(TIMELINE_EVENTS)}
+        row["step"] = j
+        rows.append(row)
+        print(json.dumps(row))
+    return rows
+
+
 def main(argv=None):
     parser = argparse.ArgumentParser()
     sub = parser.add_subparsers(dest="cmd", required=True)
@@ -186,8 +224,13 @@ def main(argv=None):
     t.add_argument("--seq", type=int, default=2048)
     t.add_argument("--heads", type=int, default=8)
     t.add_argument("--launches", type=int, default=3)
+    u = sub.add_parser("attn-timeline")
+    u.add_argument("--seq", type=int, default=2048)
+    u.add_argument("--heads", type=int, default=32)
     args = parser.parse_args(argv)
-    if args.cmd == "attn":
+    if args.cmd == "attn-timeline":
+        attn_timeline(args.seq, args.heads)
+    elif args.cmd == "attn":
         bench_attn(args.mb, args.seq, args.heads, args.iters)
     elif args.cmd == "ncu-attn":
         import torch
