@@ -2,11 +2,13 @@
 //   * out = x + bias[col] + residual            (after a reduce-scatter)
 //   * deterministic column sums (bias gradients): per-CTA partial sums over
 //     a fixed row range, then an ordered reduction of the partials added to
-//     the fp32 accumulator.
+//     the fp32 accumulator (colred.cuh for 16-byte aligned rows, a 4-byte
+//     variant otherwise).
 //
 // Reference parity: python/flux_dcu/model.py:257-263 (row-parallel output +
 // replicated bias + residual) and the bias gradients autograd produces for
 // ColumnLinear (:125) and the replicated biases.
+#include "colred.cuh"
 #include "common.cuh"
 
 namespace tdb {
@@ -80,12 +82,31 @@ TDB_API int tdb_bias_residual(const void* x, const void* bias, const void* res, 
   return int(cudaGetLastError());
 }
 
-TDB_API int tdb_colsum_scratch_floats(int rows, int cols) { return ((rows + kColRows - 1) / kColRows) * cols; }
+// Scratch for tdb_colsum in floats: ceil(rows / 16) * cols covers either path
+// below (the 16-byte path uses parts of at least 16 rows).
+TDB_API int tdb_colsum_scratch_floats(int rows, int cols) { return ((rows + 15) / 16) * cols; }
 
 TDB_API int tdb_colsum(const void* x, int64_t ld, int rows, int cols, float* partial, float* out, int accumulate,
                        void* stream) {
   if (cols % 2 || ld % 2 || rows <= 0) return tdb_host::fail(int(cudaErrorInvalidValue), "colsum: bad shape");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool wide = cols % 8 == 0 && ld % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(partial) % 16 == 0;
+  if (wide) {
+    // 16-byte loads, a few waves of CTAs (colred.cuh)
+    const int rpp = tdb::colred::rows_per_part(rows, cols, tdb_host::sm_count());
+    const int nparts = (rows + rpp - 1) / rpp;
+    if (int64_t(nparts) * cols <= int64_t(tdb_colsum_scratch_floats(rows, cols))) {
+      dim3 g1((cols + tdb::colred::kColsPerCta - 1) / tdb::colred::kColsPerCta, nparts);
+      tdb::colred::colred_partial<false><<<g1, tdb::colred::kThreads, 0, s>>>(
+          static_cast<const uint16_t*>(x), ld, nullptr, 0, nullptr, nullptr, rows, cols, rpp, partial);
+      tdb_host::launched(1);
+      tdb::colred::colred_finish<<<dim3((cols + 63) / 64, 1), 256, 0, s>>>(partial, nparts, cols, out, out,
+                                                                          accumulate);
+      tdb_host::launched(1);
+      return int(cudaGetLastError());
+    }
+  }
   const int nparts = (rows + kColRows - 1) / kColRows;
   dim3 grid((cols / 2 + 255) / 256, nparts);
   colsum_partial_kernel<<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(x), ld, rows, cols, partial);

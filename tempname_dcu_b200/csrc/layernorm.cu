@@ -6,13 +6,15 @@
 // Forward: one CTA per row, each thread owns VPT contiguous elements
 // (VPT/8 16-byte loads); two-pass mean/variance from registers; saves
 // mean and rstd (fp32) for the backward.
-// Backward: each CTA handles ROWS rows; dx (optionally plus an incoming
-// residual gradient) is written directly, and dgamma/dbeta are accumulated in
-// registers and written as per-CTA partials; a second kernel sums the
-// partials in fixed CTA order into the fp32 gradient accumulators, so the
-// result is bitwise deterministic (no floating-point atomics).
+// Backward (H a multiple of 256, <= 4096, 16-byte aligned rows): dx by one
+// warp per row with the row held in registers; dgamma / dbeta by the
+// two-stage deterministic column reduction of colred.cuh.  Other shapes (and
+// the allocation-free entry point): each CTA handles 16 rows, dgamma/dbeta
+// partials per CTA, then a fixed-order reduction.  Both are bitwise
+// deterministic (no floating-point atomics).
 #include <mutex>
 
+#include "colred.cuh"
 #include "common.cuh"
 
 namespace tdb {
@@ -142,6 +144,96 @@ __global__ void ln_bwd_kernel(const uint16_t* __restrict__ x, const uint16_t* __
   }
 }
 
+// dx for H = 256 * CH (CH <= 16): one warp per row, the row's x and dy kept in
+// registers as packed bf16 (CH 16-byte chunks per lane), so each input is read
+// once; no block-wide synchronisation.
+template <int CH>
+__global__ void __launch_bounds__(256) ln_bwd_dx_kernel(const uint16_t* __restrict__ x,
+                                                        const uint16_t* __restrict__ gamma,
+                                                        const float* __restrict__ mean_in,
+                                                        const float* __restrict__ rstd_in,
+                                                        const uint16_t* __restrict__ dy,
+                                                        const uint16_t* __restrict__ dres, uint16_t* __restrict__ dx,
+                                                        int rows) {
+  constexpr int H = 256 * CH;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + int64_t(row) * H);
+  const uint4* dr = reinterpret_cast<const uint4*>(dy + int64_t(row) * H);
+  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+  uint4 xv[CH], dv[CH];
+#pragma unroll
+  for (int ch = 0; ch < CH; ++ch) {
+    xv[ch] = xr[ch * 32 + lane];
+    dv[ch] = dr[ch * 32 + lane];
+  }
+  const float mean = mean_in[row], rstd = rstd_in[row];
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int ch = 0; ch < CH; ++ch) {
+    float xf[8], df[8], gf[8];
+    colred::unpack8(xv[ch], xf);
+    colred::unpack8(dv[ch], df);
+    colred::unpack8(gr[ch * 32 + lane], gf);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float d = df[j] * gf[j];
+      s1 += d;
+      s2 += d * ((xf[j] - mean) * rstd);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+  }
+  const float c2 = s1 / float(H), c1 = s2 / float(H);
+  const uint4* rr = dres ? reinterpret_cast<const uint4*>(dres + int64_t(row) * H) : nullptr;
+  uint4* out = reinterpret_cast<uint4*>(dx + int64_t(row) * H);
+#pragma unroll
+  for (int ch = 0; ch < CH; ++ch) {
+    float xf[8], df[8], gf[8], o[8];
+    colred::unpack8(xv[ch], xf);
+    colred::unpack8(dv[ch], df);
+    colred::unpack8(gr[ch * 32 + lane], gf);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = (df[j] * gf[j] - ((xf[j] - mean) * rstd) * c1 - c2) * rstd;
+    if (rr) {
+      float rf[8];
+      colred::unpack8(rr[ch * 32 + lane], rf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] += rf[j];
+    }
+    uint4 w;
+    w.x = pack_bf16x2(o[0], o[1]);
+    w.y = pack_bf16x2(o[2], o[3]);
+    w.z = pack_bf16x2(o[4], o[5]);
+    w.w = pack_bf16x2(o[6], o[7]);
+    out[ch * 32 + lane] = w;
+  }
+}
+
+template <int CH>
+static int bwd_fast_launch(const void* x, const void* g, const float* mean, const float* rstd, const void* dy,
+                           const void* dres, void* dx, float* dgamma, float* dbeta, float* partial, int rows,
+                           int accumulate, cudaStream_t s) {
+  constexpr int H = 256 * CH;
+  ln_bwd_dx_kernel<CH><<<(rows + 7) / 8, 256, 0, s>>>(
+      static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(g), mean, rstd, static_cast<const uint16_t*>(dy),
+      static_cast<const uint16_t*>(dres), static_cast<uint16_t*>(dx), rows);
+  tdb_host::launched(1);
+  const int rpp = colred::rows_per_part(rows, H, tdb_host::sm_count());
+  const int nparts = (rows + rpp - 1) / rpp;
+  colred::colred_partial<true><<<dim3((H + colred::kColsPerCta - 1) / colred::kColsPerCta, nparts), colred::kThreads,
+                                 0, s>>>(static_cast<const uint16_t*>(dy), H, static_cast<const uint16_t*>(x), H,
+                                         mean, rstd, rows, H, rpp, partial);
+  tdb_host::launched(1);
+  colred::colred_finish<<<dim3((H + 63) / 64, 2), 256, 0, s>>>(partial, nparts, H, dgamma, dbeta, accumulate);
+  tdb_host::launched(1);
+  return int(cudaGetLastError());
+}
+
 // Sum the per-CTA partials in CTA order and add into the fp32 accumulators.
 __global__ void ln_reduce_partials(const float* __restrict__ partial, int nparts, int H, float* __restrict__ dgamma,
                                    float* __restrict__ dbeta, int accumulate) {
@@ -210,6 +302,22 @@ TDB_API int tdb_layernorm_bwd(const void* x, const void* gamma, const float* mea
   if (!vpt || rows <= 0 || !partial)
     return tdb_host::fail(int(cudaErrorInvalidValue), "layernorm bwd: unsupported hidden size %d", H);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) |
+                         reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(gamma) |
+                         reinterpret_cast<uintptr_t>(dres) | reinterpret_cast<uintptr_t>(partial)) % 16) == 0;
+  // warp-per-row path (its partials need ceil(rows/16)*2*H floats at most,
+  // which is what tdb_layernorm_bwd_scratch_floats promises)
+  if (aligned && H % 256 == 0 && H <= 4096) {
+    switch (H / 256) {
+      case 1: return bwd_fast_launch<1>(x, gamma, mean, rstd, dy, dres, dx, dgamma, dbeta, partial, rows, accumulate, s);
+      case 2: return bwd_fast_launch<2>(x, gamma, mean, rstd, dy, dres, dx, dgamma, dbeta, partial, rows, accumulate, s);
+      case 4: return bwd_fast_launch<4>(x, gamma, mean, rstd, dy, dres, dx, dgamma, dbeta, partial, rows, accumulate, s);
+      case 8: return bwd_fast_launch<8>(x, gamma, mean, rstd, dy, dres, dx, dgamma, dbeta, partial, rows, accumulate, s);
+      case 16:
+        return bwd_fast_launch<16>(x, gamma, mean, rstd, dy, dres, dx, dgamma, dbeta, partial, rows, accumulate, s);
+      default: break;
+    }
+  }
   int rc;
   switch (vpt) {
     case 8: rc = bwd_launch<8>(x, gamma, mean, rstd, dy, dres, dx, partial, rows, H, s); break;

@@ -1,6 +1,6 @@
 """Kernel-time breakdown of training micro-steps (torch.profiler / CUPTI).
 
-    python -m tempname_dcu_b200.utils.trace [--layers L] [--micro 1] [--chrome out.json]
+    python -m tempname_dcu_b200.utils.trace [--layers L] [--micro 1 | --step] [--chrome out.json]
 
 Runs warm-up micro-steps, then profiles ``--micro`` micro-batches of the GPT
 training step and prints the device time per kernel name (sum, count, share),
@@ -26,6 +26,7 @@ def main(argv=None):
     ap.add_argument("--micro", type=int, default=1)
     ap.add_argument("--chrome", default="")
     ap.add_argument("--json", default="")
+    ap.add_argument("--step", action="store_true", help="profile one whole optimizer step instead")
     args = ap.parse_args(argv)
     import torch
     from torch.profiler import ProfilerActivity, profile
@@ -40,8 +41,11 @@ def main(argv=None):
     model = trainer.model
     with profile(activities=[ProfilerActivity.CUDA, ProfilerActivity.CPU]) as prof:
         t0 = time.perf_counter()
-        for i in range(args.micro):
-            model.forward_backward(tokens[i], labels[i], trainer.loss)
+        if args.step:
+            trainer.step(tokens, labels)
+        else:
+            for i in range(args.micro):
+                model.forward_backward(tokens[i], labels[i], trainer.loss)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
     if args.chrome:
@@ -53,7 +57,8 @@ def main(argv=None):
             per[evt.name][1] += 1
     total = sum(v[0] for v in per.values())
     rows = sorted(per.items(), key=lambda kv: -kv[1][0])
-    print(f"profiled {args.micro} micro-batch(es), {args.layers} layers: device {total / 1e3:.2f} ms, "
+    what = "one optimizer step" if args.step else f"{args.micro} micro-batch(es)"
+    print(f"profiled {what}, {args.layers} layers: device {total / 1e3:.2f} ms, "
           f"host wall {wall * 1e3:.2f} ms")
     for name, (us, n) in rows[:40]:
         print(f"{us / 1e3:10.3f} ms {100 * us / total:6.2f}% x{n:<6d} {name[:110]}")

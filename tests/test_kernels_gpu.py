@@ -155,11 +155,11 @@ def test_vocab_parallel_cross_entropy(cuda, world):
     assert g[:, vocab:].abs().max().item() == 0
 
 
-def test_adamw_matches_torch(cuda):
+@pytest.mark.parametrize("n,split", [(10_000, 6000), (10_001, 6001)])  # vectorised / scalar kernel
+def test_adamw_matches_torch(cuda, n, split):
     import torch
     from tempname_dcu_b200.ops import kernels as k
     torch.manual_seed(3)
-    n, split = 10_000, 6000
     master = torch.randn(n, device=cuda)
     pa = torch.nn.Parameter(master[:split].clone())
     pb = torch.nn.Parameter(master[split:].clone())
@@ -180,6 +180,24 @@ def test_adamw_matches_torch(cuda):
     ref = torch.cat([pa.detach(), pb.detach()])
     assert _rel(master, ref) < 1e-6
     assert torch.equal(bf, master.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("rows,cols,offset", [(2048, 4096, 0), (300, 12288, 0), (100, 1000, 0), (64, 514, 1)])
+def test_colsum_deterministic(cuda, rows, cols, offset):
+    """Column sums (bias gradients) on the 16-byte path and the 4-byte path."""
+    import torch
+    from tempname_dcu_b200.ops import kernels as k
+    torch.manual_seed(8)
+    base = torch.randn(rows, cols + offset, device=cuda).to(torch.bfloat16)
+    x = base[:, offset:]                       # offset 1: rows not 16-byte aligned
+    out = torch.full((cols,), 0.25, device=cuda)
+    scratch = torch.empty(k.colsum_scratch_floats(rows, cols), device=cuda)
+    k.colsum(x, out, scratch, accumulate=True)
+    ref = x.double().sum(0) + 0.25
+    assert (out.double() - ref).abs().max().item() < 1e-3 * max(1.0, ref.abs().max().item())
+    out2 = torch.full((cols,), 0.25, device=cuda)
+    k.colsum(x, out2, scratch, accumulate=True)
+    assert torch.equal(out, out2)
 
 
 def test_sumsq_and_clip(cuda):
