@@ -260,21 +260,28 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 // --------------------------------------------------------------------------
 __global__ void bwd_pre_kernel(const uint16_t* __restrict__ out, int64_t ld_out, const uint16_t* __restrict__ dout,
                                int64_t ld_dout, float* __restrict__ dsum, int seq, int Hl, int total_rows) {
-  // one warp per (token, head)
-  const int64_t w = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= int64_t(total_rows) * Hl) return;
-  const int64_t tok = w / Hl;
-  const int h = int(w % Hl);
-  const uint2 a = *reinterpret_cast<const uint2*>(out + tok * ld_out + h * D + lane * 4);
-  const uint2 c = *reinterpret_cast<const uint2*>(dout + tok * ld_dout + h * D + lane * 4);
-  float s = bf16_bits_to_float(a.x & 0xffff) * bf16_bits_to_float(c.x & 0xffff) +
-            bf16_bits_to_float(a.x >> 16) * bf16_bits_to_float(c.x >> 16) +
-            bf16_bits_to_float(a.y & 0xffff) * bf16_bits_to_float(c.y & 0xffff) +
-            bf16_bits_to_float(a.y >> 16) * bf16_bits_to_float(c.y >> 16);
+  // 16 lanes per (token, head) row of 128 values: one 16-byte load of O and
+  // of dO per lane, then a 16-lane butterfly.
+  const int64_t w = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
+  const int sub = threadIdx.x & 15;
+  const bool live = w < int64_t(total_rows) * Hl;
+  float s = 0.f;
+  int64_t tok = 0;
+  int h = 0;
+  if (live) {
+    tok = w / Hl;
+    h = int(w % Hl);
+    const uint4 a = *reinterpret_cast<const uint4*>(out + tok * ld_out + h * D + sub * 8);
+    const uint4 c = *reinterpret_cast<const uint4*>(dout + tok * ld_dout + h * D + sub * 8);
+    const uint32_t aa[4] = {a.x, a.y, a.z, a.w}, cc[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) {
+    for (int j = 0; j < 4; ++j)
+      s += bf16_bits_to_float(aa[j] & 0xffff) * bf16_bits_to_float(cc[j] & 0xffff) +
+           bf16_bits_to_float(aa[j] >> 16) * bf16_bits_to_float(cc[j] >> 16);
+  }
+#pragma unroll
+  for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (live && sub == 0) {
     const int64_t b = tok / seq, i = tok % seq;
     dsum[(b * Hl + h) * seq + i] = s;
   }
@@ -590,11 +597,12 @@ TDB_API int tdb_attn_fwd(const void* qkv, int64_t ld, void* out, int64_t ld_out,
 // Dsum[b, h, i] = sum_d dO[i, h, d] * O[i, h, d]  (one warp per (token, head)).
 TDB_API int tdb_attn_bwd_pre(const void* out, int64_t ld_out, const void* dout, int64_t ld_dout, float* dsum, int mb,
                              int seq, int Hl, void* stream) {
-  if (!out || !dout || !dsum || mb <= 0 || seq <= 0 || Hl <= 0)
-    return tdb_host::fail(int(cudaErrorInvalidValue), "attention bwd pre: bad arguments");
+  if (!out || !dout || !dsum || mb <= 0 || seq <= 0 || Hl <= 0 || ld_out % 8 || ld_dout % 8 ||
+      (reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(dout)) % 16)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "attention bwd pre: bad arguments (16-byte aligned rows needed)");
   const int rows = mb * seq;
-  const int64_t warps = int64_t(rows) * Hl;
-  tdb::attn::bwd_pre_kernel<<<unsigned((warps * 32 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  const int64_t groups = int64_t(rows) * Hl;  // 16 threads each
+  tdb::attn::bwd_pre_kernel<<<unsigned((groups * 16 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(out), ld_out, static_cast<const uint16_t*>(dout), ld_dout, dsum, seq, Hl, rows);
   tdb_host::launched(1);
   return int(cudaGetLastError());

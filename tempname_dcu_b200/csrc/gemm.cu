@@ -60,6 +60,11 @@ __device__ __forceinline__ void store_bf16x32(uint16_t* p, const float (&v)[32])
   }
 }
 
+__device__ __forceinline__ void red_add_f32x4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
 template <int MODE>
 struct PlainEpi {
   EpiParams p;
@@ -77,7 +82,13 @@ struct PlainEpi {
     const bool full = col + 32 <= p.N;
     if (MODE == kAccF32) {
       float* c = static_cast<float*>(p.C) + int64_t(row) * p.ldc + col;
-      if (full) {
+      if (full && p.beta == 1.f) {
+        // C += acc: each element has exactly one writer in this GEMM, so a
+        // fire-and-forget L2 reduction gives the same fp32 round-to-nearest
+        // sum as load-add-store, without the round trip in the epilogue.
+#pragma unroll
+        for (int i = 0; i < 8; ++i) red_add_f32x4(c + 4 * i, v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      } else if (full) {
         float4* c4 = reinterpret_cast<float4*>(c);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {

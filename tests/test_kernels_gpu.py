@@ -182,14 +182,14 @@ def test_adamw_matches_torch(cuda, n, split):
     assert torch.equal(bf, master.to(torch.bfloat16))
 
 
-@pytest.mark.parametrize("rows,cols,offset", [(2048, 4096, 0), (300, 12288, 0), (100, 1000, 0), (64, 514, 1)])
+@pytest.mark.parametrize("rows,cols,offset", [(2048, 4096, 0), (300, 12288, 0), (100, 1000, 0), (64, 514, 2)])
 def test_colsum_deterministic(cuda, rows, cols, offset):
     """Column sums (bias gradients) on the 16-byte path and the 4-byte path."""
     import torch
     from tempname_dcu_b200.ops import kernels as k
     torch.manual_seed(8)
     base = torch.randn(rows, cols + offset, device=cuda).to(torch.bfloat16)
-    x = base[:, offset:]                       # offset 1: rows not 16-byte aligned
+    x = base[:, offset:]                       # offset 2: rows 4-byte but not 16-byte aligned
     out = torch.full((cols,), 0.25, device=cuda)
     scratch = torch.empty(k.colsum_scratch_floats(rows, cols), device=cuda)
     k.colsum(x, out, scratch, accumulate=True)
