@@ -80,7 +80,18 @@ static __global__ void __launch_bounds__(256) colred_finish(const float* __restr
   const float* src = partial + int64_t(q) * nparts * cols;
   float2 s = make_float2(0.f, 0.f);
   if (c < cols) {
-    for (int p = warp; p < nparts; p += 8) {
+    int p = warp;
+    for (; p + 24 < nparts; p += 32) {  // four loads in flight, added in part order
+      float2 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const float2*>(src + int64_t(p + 8 * u) * cols + c);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        s.x += v[u].x;
+        s.y += v[u].y;
+      }
+    }
+    for (; p < nparts; p += 8) {
       const float2 v = *reinterpret_cast<const float2*>(src + int64_t(p) * cols + c);
       s.x += v.x;
       s.y += v.y;

@@ -20,9 +20,13 @@ enum EpiMode : int {
   kGeluBwd = 3,       // C(bf16) = acc * gelu'(aux[m,n])
   kAccF32 = 4,        // C(fp32) = acc + beta * C
   kBiasResidual = 5,  // C(bf16) = acc + bias[n] + aux[m,n]
+  // internal: kAccF32 with beta 0 or 1 and a 16-byte aligned C, written
+  // through shared memory by TMA bulk stores / bulk reduce-adds
+  kAccF32Tma = 6,
 };
 
-struct EpiParams {
+struct alignas(64) EpiParams {
+  CUtensorMap tmC;  // fp32 C, box {32 cols, 32 rows}, 128B swizzle (kAccF32Tma only)
   void* C;
   int64_t ldc;
   int M, N;
@@ -60,14 +64,9 @@ __device__ __forceinline__ void store_bf16x32(uint16_t* p, const float (&v)[32])
   }
 }
 
-__device__ __forceinline__ void red_add_f32x4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
-
 template <int MODE>
 struct PlainEpi {
-  EpiParams p;
+  const EpiParams& p;
 
   static constexpr int kSmemBytes = 0;
   __device__ __forceinline__ void set_smem(uint8_t*) {}
@@ -82,13 +81,7 @@ struct PlainEpi {
     const bool full = col + 32 <= p.N;
     if (MODE == kAccF32) {
       float* c = static_cast<float*>(p.C) + int64_t(row) * p.ldc + col;
-      if (full && p.beta == 1.f) {
-        // C += acc: each element has exactly one writer in this GEMM, so a
-        // fire-and-forget L2 reduction gives the same fp32 round-to-nearest
-        // sum as load-add-store, without the round trip in the epilogue.
-#pragma unroll
-        for (int i = 0; i < 8; ++i) red_add_f32x4(c + 4 * i, v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-      } else if (full) {
+      if (full) {
         float4* c4 = reinterpret_cast<float4*>(c);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -163,11 +156,76 @@ struct PlainEpi {
   }
 };
 
+// fp32 C through shared memory: each epilogue warp stages a 32 x 32 block
+// (its 32 rows x one 32-column chunk) in a 128B-swizzled 4 KB buffer
+// (double-buffered) and one lane issues a TMA bulk store (beta == 0) or a
+// TMA bulk reduce-add (beta == 1) of the block.  Coalesced, asynchronous, and
+// bitwise equal to the register path (one writer per element; the L2 add
+// rounds to nearest like a load-add-store).  Out-of-range rows and columns
+// are clipped by the tensor map.
+struct AccF32TmaEpi {
+  const EpiParams& p;
+  static constexpr int kBuf = 32 * 32 * 4;
+  static constexpr int kSmemBytes = 4 * 2 * kBuf + 1024;  // + alignment of the swizzled buffers
+  uint32_t base = 0;
+  int count = 0;
+
+  __device__ __forceinline__ void set_smem(uint8_t* s) {
+    const uint32_t a = smem_u32(s);
+    base = ((a + 1023u) & ~1023u) + uint32_t(((threadIdx.x >> 5) & 3) * 2 * kBuf);
+  }
+  __device__ __forceinline__ void tile_begin(int, int) {}
+  __device__ __forceinline__ void tile_end(int, int, int, int) {}
+  // Every bulk operation this thread issued has completed (its shared-memory
+  // reads and its global writes) before the kernel returns, on every path.
+  __device__ __forceinline__ ~AccF32TmaEpi() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+  __device__ __forceinline__ void chunk(int row, int col, int, const uint32_t (&r)[32]) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t buf = base + uint32_t((count & 1) * kBuf);
+    if (count >= 2) {  // the bulk op that last read this buffer must be done with it
+      if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+      __syncwarp();
+    }
+    const uint32_t rowa = buf + uint32_t(lane * 128), sw = uint32_t(lane & 7);
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(rowa + ((uint32_t(c) ^ sw) << 4)), "r"(r[4 * c]),
+                   "r"(r[4 * c + 1]), "r"(r[4 * c + 2]), "r"(r[4 * c + 3])
+                   : "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) {
+      const int row0 = row - lane;  // first row of this warp's block
+      const uint64_t tmap = reinterpret_cast<uint64_t>(&p.tmC);
+      if (p.beta != 0.f)
+        asm volatile(
+            "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+            "r"(buf), "r"(col), "r"(row0)
+            : "memory");
+      else
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+                     "r"(buf), "r"(col), "r"(row0)
+                     : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    ++count;
+  }
+};
+
+template <int MODE>
+struct EpiFor {
+  using type = PlainEpi<MODE>;
+};
+template <>
+struct EpiFor<kAccF32Tma> {
+  using type = AccF32TmaEpi;
+};
+
 template <int BN, bool A_MN, bool B_MN, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int K,
-                TileOrder order, EpiParams ep, int* status) {
-  PlainEpi<MODE> epi{ep};
+                TileOrder order, const __grid_constant__ EpiParams ep, int* status) {
+  typename EpiFor<MODE>::type epi{ep};
   gemm_mainloop<BN, A_MN, B_MN>(&tmA, &tmB, K, order, epi, status);
 }
 
@@ -175,12 +233,13 @@ template <int BN, bool A_MN, bool B_MN, int MODE>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiParams& ep,
                   cudaStream_t stream) {
   using Cfg = Config<BN>;
+  constexpr int kSmem = Cfg::kSmemBytes + EpiFor<MODE>::type::kSmemBytes;
   auto kern = gemm_kernel<BN, A_MN, B_MN, MODE>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return tdb_host::fail(int(e), "cudaFuncSetAttribute(gemm) failed");
     attr_set[dev & 63] = true;
   }
@@ -191,7 +250,7 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, in
   order.table = nullptr;
   order.num_tiles = order.num_m * order.num_n;
   const int grid = order.num_tiles < tdb_host::sm_count() ? order.num_tiles : tdb_host::sm_count();
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, K, order, ep, tdb_host::status_ptr());
+  kern<<<grid, kThreads, kSmem, stream>>>(ta, tb, K, order, ep, tdb_host::status_ptr());
   tdb_host::launched(1);
   return int(cudaGetLastError());
 }
@@ -204,15 +263,17 @@ constexpr int k2Stages = 6;
 template <bool A_MN, bool B_MN, int MODE>
 __global__ void __launch_bounds__(gemm2::kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int K,
-                 TileOrder order, EpiParams ep, int* status) {
-  PlainEpi<MODE> epi{ep};
-  gemm2::mainloop<A_MN, B_MN, PlainEpi<MODE>, k2Stages>(&tmA, &tmB, K, order, epi, status);
+                 TileOrder order, const __grid_constant__ EpiParams ep, int* status) {
+  using Epi = typename EpiFor<MODE>::type;
+  Epi epi{ep};
+  gemm2::mainloop<A_MN, B_MN, Epi, k2Stages>(&tmA, &tmB, K, order, epi, status);
 }
 
 template <bool A_MN, bool B_MN, int MODE>
 static int launch2(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiParams& ep,
                    cudaStream_t stream) {
   using Cfg = gemm2::Config<k2Stages>;
+  constexpr int kSmem = Cfg::kSmemBytes + EpiFor<MODE>::type::kSmemBytes;
   auto kern = gemm2_kernel<A_MN, B_MN, MODE>;
   static int max_clusters[64] = {0};
   int dev = 0;
@@ -224,12 +285,12 @@ static int launch2(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.blockDim = dim3(gemm2::kThreads);
-  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.dynamicSmemBytes = kSmem;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (!max_clusters[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm2: cudaFuncSetAttribute failed");
     cfg.gridDim = dim3(2 * tdb_host::sm_count() / 2);
     int n = 0;
@@ -261,6 +322,7 @@ static int dispatch2(int mode, const CUtensorMap& ta, const CUtensorMap& tb, int
     case kBiasGelu: return launch2<A_MN, B_MN, kBiasGelu>(ta, tb, M, N, K, ep, s);
     case kGeluBwd: return launch2<A_MN, B_MN, kGeluBwd>(ta, tb, M, N, K, ep, s);
     case kAccF32: return launch2<A_MN, B_MN, kAccF32>(ta, tb, M, N, K, ep, s);
+    case kAccF32Tma: return launch2<A_MN, B_MN, kAccF32Tma>(ta, tb, M, N, K, ep, s);
     case kBiasResidual: return launch2<A_MN, B_MN, kBiasResidual>(ta, tb, M, N, K, ep, s);
   }
   return tdb_host::fail(int(cudaErrorInvalidValue), "unknown epilogue mode %d", mode);
@@ -275,6 +337,7 @@ static int dispatch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb,
     case kBiasGelu: return launch<BN, A_MN, B_MN, kBiasGelu>(ta, tb, M, N, K, ep, s);
     case kGeluBwd: return launch<BN, A_MN, B_MN, kGeluBwd>(ta, tb, M, N, K, ep, s);
     case kAccF32: return launch<BN, A_MN, B_MN, kAccF32>(ta, tb, M, N, K, ep, s);
+    case kAccF32Tma: return launch<BN, A_MN, B_MN, kAccF32Tma>(ta, tb, M, N, K, ep, s);
     case kBiasResidual: return launch<BN, A_MN, B_MN, kBiasResidual>(ta, tb, M, N, K, ep, s);
   }
   return tdb_host::fail(int(cudaErrorInvalidValue), "unknown epilogue mode %d", mode);
@@ -312,8 +375,8 @@ using namespace tdb::gemm;
 TDB_API int tdb_gemm(const void* A, int a_mn, int64_t lda, const void* B, int b_mn, int64_t ldb, void* C,
                      int64_t ldc, int M, int N, int K, int mode, const void* bias, const void* aux, int64_t ld_aux,
                      void* aux_out, float alpha, float beta, int bn, void* stream) {
-  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0)
-    return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: bad pointers or sizes");
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || mode < kStore || mode > kBiasResidual)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: bad pointers, sizes or mode");
   if (K % 8 || (a_mn && M % 8) || (b_mn && N % 8) || N % 8 || ldc % 8)
     return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: K, N, ldc (and M / N for MN-major) must be multiples of 8");
   if ((mode == kBiasGelu && (!aux_out || ld_aux % 8)) || ((mode == kGeluBwd || mode == kBiasResidual) && (!aux || ld_aux % 8)))
@@ -348,6 +411,12 @@ TDB_API int tdb_gemm(const void* A, int a_mn, int64_t lda, const void* B, int b_
   ep.aux_out = static_cast<uint16_t*>(aux_out);
   ep.alpha = alpha;
   ep.beta = beta;
+  if (mode == kAccF32 && (beta == 0.f || beta == 1.f) && reinterpret_cast<uintptr_t>(C) % 16 == 0 && ldc % 4 == 0) {
+    rc = tdb_host::make_tmap_2d(&ep.tmC, C, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, uint64_t(N), uint64_t(M),
+                                uint64_t(ldc), 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    mode = kAccF32Tma;
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (bn == 512) {
     if (!a_mn && !b_mn) return dispatch2<false, false>(mode, ta, tb, M, N, K, ep, s);

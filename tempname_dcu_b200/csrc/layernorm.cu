@@ -3,9 +3,10 @@
 // Reference parity: python/flux_dcu/model.py:229-233 (F.layer_norm with
 // weight, bias and eps 1e-5 on the sequence-parallel residual rows).
 //
-// Forward: one CTA per row, each thread owns VPT contiguous elements
-// (VPT/8 16-byte loads); two-pass mean/variance from registers; saves
-// mean and rstd (fp32) for the backward.
+// Forward: one warp per row (H a multiple of 256, <= 4096, 16-byte aligned
+// rows) or one CTA per row (VPT contiguous elements per thread) otherwise;
+// two-pass mean/variance from registers; saves mean and rstd (fp32) for the
+// backward.
 // Backward (H a multiple of 256, <= 4096, 16-byte aligned rows): dx by one
 // warp per row with the row held in registers; dgamma / dbeta by the
 // two-stage deterministic column reduction of colred.cuh.  Other shapes (and
@@ -234,6 +235,77 @@ static int bwd_fast_launch(const void* x, const void* g, const float* mean, cons
   return int(cudaGetLastError());
 }
 
+// Forward for H = 256 * CH (CH <= 16): one warp per row, the row held in
+// registers as packed bf16; two-pass mean / variance over the registers.
+template <int CH>
+__global__ void __launch_bounds__(256) ln_fwd_warp_kernel(const uint16_t* __restrict__ x,
+                                                          const uint16_t* __restrict__ gamma,
+                                                          const uint16_t* __restrict__ beta, uint16_t* __restrict__ y,
+                                                          float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                                                          int rows, float eps) {
+  constexpr int H = 256 * CH;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + int64_t(row) * H);
+  uint4 xv[CH];
+#pragma unroll
+  for (int ch = 0; ch < CH; ++ch) xv[ch] = xr[ch * 32 + lane];
+  float s = 0.f;
+#pragma unroll
+  for (int ch = 0; ch < CH; ++ch) {
+    float f[8];
+    colred::unpack8(xv[ch], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += f[j];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / float(H);
+  float q = 0.f;
+#pragma unroll
+  for (int ch = 0; ch < CH; ++ch) {
+    float f[8];
+    colred::unpack8(xv[ch], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q += (f[j] - mean) * (f[j] - mean);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = rsqrtf(q / float(H) + eps);
+  const uint4* gr = reinterpret_cast<const uint4*>(gamma);
+  const uint4* br = reinterpret_cast<const uint4*>(beta);
+  uint4* out = reinterpret_cast<uint4*>(y + int64_t(row) * H);
+#pragma unroll
+  for (int ch = 0; ch < CH; ++ch) {
+    float f[8], g[8], b[8];
+    colred::unpack8(xv[ch], f);
+    colred::unpack8(gr[ch * 32 + lane], g);
+    colred::unpack8(br[ch * 32 + lane], b);
+    uint4 w;
+    w.x = pack_bf16x2((f[0] - mean) * rstd * g[0] + b[0], (f[1] - mean) * rstd * g[1] + b[1]);
+    w.y = pack_bf16x2((f[2] - mean) * rstd * g[2] + b[2], (f[3] - mean) * rstd * g[3] + b[3]);
+    w.z = pack_bf16x2((f[4] - mean) * rstd * g[4] + b[4], (f[5] - mean) * rstd * g[5] + b[5]);
+    w.w = pack_bf16x2((f[6] - mean) * rstd * g[6] + b[6], (f[7] - mean) * rstd * g[7] + b[7]);
+    out[ch * 32 + lane] = w;
+  }
+  if (lane == 0) {
+    mean_out[row] = mean;
+    rstd_out[row] = rstd;
+  }
+}
+
+template <int CH>
+static int fwd_warp_launch(const void* x, const void* g, const void* b, void* y, float* mean, float* rstd, int rows,
+                           float eps, cudaStream_t s) {
+  ln_fwd_warp_kernel<CH><<<(rows + 7) / 8, 256, 0, s>>>(static_cast<const uint16_t*>(x),
+                                                        static_cast<const uint16_t*>(g),
+                                                        static_cast<const uint16_t*>(b), static_cast<uint16_t*>(y),
+                                                        mean, rstd, rows, eps);
+  tdb_host::launched(1);
+  return int(cudaGetLastError());
+}
+
 // Sum the per-CTA partials in CTA order and add into the fp32 accumulators.
 __global__ void ln_reduce_partials(const float* __restrict__ partial, int nparts, int H, float* __restrict__ dgamma,
                                    float* __restrict__ dbeta, int accumulate) {
@@ -284,6 +356,18 @@ TDB_API int tdb_layernorm_fwd(const void* x, const void* gamma, const void* beta
   const int vpt = pick_vpt(H);
   if (!vpt || rows <= 0) return tdb_host::fail(int(cudaErrorInvalidValue), "layernorm: unsupported hidden size %d", H);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                         reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) % 16) == 0;
+  if (aligned && H % 256 == 0 && H <= 4096) {
+    switch (H / 256) {
+      case 1: return fwd_warp_launch<1>(x, gamma, beta, y, mean, rstd, rows, eps, s);
+      case 2: return fwd_warp_launch<2>(x, gamma, beta, y, mean, rstd, rows, eps, s);
+      case 4: return fwd_warp_launch<4>(x, gamma, beta, y, mean, rstd, rows, eps, s);
+      case 8: return fwd_warp_launch<8>(x, gamma, beta, y, mean, rstd, rows, eps, s);
+      case 16: return fwd_warp_launch<16>(x, gamma, beta, y, mean, rstd, rows, eps, s);
+      default: break;
+    }
+  }
   switch (vpt) {
     case 8: return fwd_launch<8>(x, gamma, beta, y, mean, rstd, rows, H, eps, s);
     case 16: return fwd_launch<16>(x, gamma, beta, y, mean, rstd, rows, H, eps, s);

@@ -44,7 +44,7 @@ def _peaks():
 
 def _operands(torch, M, N, K, kind, device):
     g = torch.Generator(device=device).manual_seed(0)
-    if kind == "fwd":      # x[M,K] @ w[N,K]^T
+    if kind in ("fwd", "fwd_f32"):      # x[M,K] @ w[N,K]^T
         a = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
         b = torch.randn(N, K, device=device, generator=g).to(torch.bfloat16)
     elif kind == "dgrad":  # dy[M,K'] @ w[K',N] where the GEMM is M x N x K
@@ -59,13 +59,17 @@ def _operands(torch, M, N, K, kind, device):
 def _ours(gemm, a, b, kind, out):
     if kind == "fwd":
         return lambda: gemm.gemm(a, b, out=out)
+    if kind == "wgrad_bf16":  # wgrad operand layouts, bf16 output (layout vs epilogue cost)
+        return lambda: gemm.gemm(a, b, a_mn=True, b_mn=True, out=out)
+    if kind == "fwd_f32":     # forward operand layouts, fp32 output
+        return lambda: gemm.gemm(a, b, out=out, mode=gemm.ACC_F32, beta=0.0)
     if kind == "dgrad":
         return lambda: gemm.gemm(a, b, b_mn=True, out=out)
     return lambda: gemm.gemm(a, b, a_mn=True, b_mn=True, out=out, mode=gemm.ACC_F32, beta=0.0)
 
 
 def _cublas(torch, a, b, kind, out):
-    if kind == "fwd":
+    if kind in ("fwd", "fwd_f32"):
         return lambda: torch.matmul(a, b.t(), out=out)
     if kind == "dgrad":
         return lambda: torch.matmul(a, b, out=out)
@@ -99,7 +103,7 @@ def bench_gemm(shapes, iters):
     rows = []
     for name, M, N, K, kind in shapes:
         a, b = _operands(torch, M, N, K, kind, device)
-        out_dtype = torch.float32 if kind == "wgrad" else torch.bfloat16
+        out_dtype = torch.float32 if kind in ("wgrad", "fwd_f32") else torch.bfloat16
         out = torch.empty(M, N, dtype=out_dtype, device=device)
         ref_out = torch.empty(M, N, dtype=torch.bfloat16, device=device)
         ours = time_fn(torch, _ours(gemm, a, b, kind, out), iters, flush=flush)

@@ -27,13 +27,28 @@ def main(argv=None):
     ap.add_argument("--chrome", default="")
     ap.add_argument("--json", default="")
     ap.add_argument("--step", action="store_true", help="profile one whole optimizer step instead")
+    ap.add_argument("--arm", default="flux", help="tensor-parallel arm when launched with torchrun (WORLD_SIZE > 1)")
     args = ap.parse_args(argv)
+    import os
     import torch
     from torch.profiler import ProfilerActivity, profile
     from ..models.config import BENCH_CONFIG
     from ..train import Trainer, synthetic_batches
     cfg = dict(BENCH_CONFIG, layers=args.layers)
-    trainer = Trainer(cfg, "flux", None)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    group, factory, rank = None, None, 0
+    if world > 1:  # one rank per GPU under torchrun; rank 0 prints
+        import datetime
+        import torch.distributed as dist
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        group, rank = dist.group.WORLD, dist.get_rank()
+        if args.arm != "nccl":
+            from ..runtime import operator_factory_for
+            factory = operator_factory_for(args.arm)
+    trainer = Trainer(cfg, args.arm if args.arm != "nccl" else "flux", group, operator_factory=factory)
     (tokens, labels), = synthetic_batches(trainer.config, 1)
     tokens, labels = tokens.cuda(), labels.cuda()
     trainer.step(tokens, labels)
@@ -48,6 +63,12 @@ def main(argv=None):
                 model.forward_backward(tokens[i], labels[i], trainer.loss)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        if rank != 0:
+            dist.destroy_process_group()
+            return
     if args.chrome:
         prof.export_chrome_trace(args.chrome)
     per = collections.defaultdict(lambda: [0.0, 0])
@@ -66,6 +87,9 @@ def main(argv=None):
         with open(args.json, "w") as fh:
             json.dump(dict(total_us=total, wall_s=wall, kernels=[dict(name=k, us=v[0], count=v[1])
                                                                   for k, v in rows]), fh, indent=1)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
