@@ -6,6 +6,8 @@
 // one persistent tcgen05 kernel; bias, exact-erf GELU (model.py:261), GELU
 // backward, residual adds and fp32 weight-gradient accumulation
 // (model.py:401-408) are fused into the epilogue instead of separate kernels.
+#include <type_traits>
+
 #include "gemm.cuh"
 #include "gemm2.cuh"
 #include "tensor_map.h"
@@ -23,10 +25,13 @@ enum EpiMode : int {
   // internal: kAccF32 with beta 0 or 1 and a 16-byte aligned C, written
   // through shared memory by TMA bulk stores / bulk reduce-adds
   kAccF32Tma = 6,
+  // internal: kTmaBase + m = bf16 mode m (0, 1, 2, 3, 5) with TMA bulk stores
+  kTmaBase = 8,
 };
 
 struct alignas(64) EpiParams {
-  CUtensorMap tmC;  // fp32 C, box {32 cols, 32 rows}, 128B swizzle (kAccF32Tma only)
+  CUtensorMap tmC;    // TMA epilogues: C (fp32 box {32, 32} or bf16 box {64, 32}), 128B swizzle
+  CUtensorMap tmAux;  // TMA bf16 epilogue of kBiasGelu: the saved pre-activation (aux_out)
   void* C;
   int64_t ldc;
   int M, N;
@@ -212,9 +217,126 @@ struct AccF32TmaEpi {
   }
 };
 
+// bf16 outputs through shared memory: the same math as PlainEpi, then each
+// epilogue warp stages 32 rows x 64 columns (two consecutive 32-column
+// chunks) in a 128B-swizzled 4 KB buffer and one lane issues a TMA bulk
+// store of the block (plus one of the pre-activation for kBiasGelu).  Two
+// buffers per warp: double-buffered C, or C + pre-activation for kBiasGelu.
+// Inputs (bias, residual, saved pre-activation) are read as in PlainEpi.
+template <int MODE>
+struct TmaBf16Epi {
+  const EpiParams& p;
+  static constexpr int kBuf = 32 * 128;
+  static constexpr int kSmemBytes = 4 * 2 * kBuf + 1024;
+  static constexpr bool kTwo = MODE == kBiasGelu;
+  uint32_t base = 0;
+  int blocks = 0;  // 64-column blocks issued by this warp
+
+  __device__ __forceinline__ void set_smem(uint8_t* s) {
+    const uint32_t a = smem_u32(s);
+    base = ((a + 1023u) & ~1023u) + uint32_t(((threadIdx.x >> 5) & 3) * 2 * kBuf);
+  }
+  __device__ __forceinline__ void tile_begin(int, int) {}
+  __device__ __forceinline__ void tile_end(int, int, int, int) {}
+  __device__ __forceinline__ ~TmaBf16Epi() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+  __device__ __forceinline__ static void stage(uint32_t buf, int lane, int half, const float (&v)[32]) {
+    const uint32_t rowa = buf + uint32_t(lane * 128), sw = uint32_t(lane & 7);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(rowa + ((uint32_t(4 * half + k) ^ sw) << 4)),
+                   "r"(pack_bf16x2(v[8 * k], v[8 * k + 1])), "r"(pack_bf16x2(v[8 * k + 2], v[8 * k + 3])),
+                   "r"(pack_bf16x2(v[8 * k + 4], v[8 * k + 5])), "r"(pack_bf16x2(v[8 * k + 6], v[8 * k + 7]))
+                   : "memory");
+  }
+  __device__ __forceinline__ static void store(const CUtensorMap* map, uint32_t buf, int col, int row) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(buf), "r"(col), "r"(row)
+                 : "memory");
+  }
+
+  __device__ __forceinline__ void chunk(int row, int col, int c, const uint32_t (&r)[32]) {
+    const int lane = threadIdx.x & 31;
+    const int half = c & 1;
+    float v[32], z[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    const bool inb = row < p.M;
+    const bool full = inb && col + 32 <= p.N;
+    if (MODE == kStore) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= p.alpha;
+    }
+    if ((MODE == kBias || MODE == kBiasGelu || MODE == kBiasResidual) && p.bias) {
+      if (full) {
+        float b[32];
+        load_bf16x32(p.bias + col, b);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += b[j];
+      } else if (inb) {
+        _Pragma("unroll") for (int j = 0; j < 32; ++j) if (col + j < p.N) v[j] += bf16_bits_to_float(p.bias[col + j]);
+      }
+    }
+    if (MODE == kBiasResidual) {
+      const uint16_t* a = p.aux + int64_t(row) * p.ld_aux + col;
+      if (full) {
+        float res[32];
+        load_bf16x32(a, res);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += res[j];
+      } else if (inb) {
+        _Pragma("unroll") for (int j = 0; j < 32; ++j) if (col + j < p.N) v[j] += bf16_bits_to_float(a[j]);
+      }
+    }
+    if (MODE == kBiasGelu) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        z[j] = bf16_bits_to_float(float_to_bf16_bits(v[j]));
+        v[j] = gelu_erf(z[j]);
+      }
+    }
+    if (MODE == kGeluBwd) {
+      const uint16_t* a = p.aux + int64_t(row) * p.ld_aux + col;
+      if (full) {
+        float zz[32];
+        load_bf16x32(a, zz);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = bf16_bits_to_float(float_to_bf16_bits(v[j])) * gelu_erf_grad(zz[j]);
+      } else if (inb) {
+        _Pragma("unroll") for (int j = 0; j < 32; ++j) if (col + j < p.N) v[j] = bf16_bits_to_float(float_to_bf16_bits(v[j])) * gelu_erf_grad(bf16_bits_to_float(a[j]));
+      }
+    }
+    // buffers: [b0][b1]; kBiasGelu uses b0 for C and b1 for the pre-activation
+    const uint32_t bufC = base + uint32_t((kTwo ? 0 : (blocks & 1)) * kBuf);
+    const uint32_t bufZ = base + uint32_t(kBuf);
+    if (half == 0 && blocks >= (kTwo ? 1 : 2)) {  // the bulk store that last read these buffers is done with them
+      if (lane == 0) {
+        if (kTwo)
+          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        else
+          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+      }
+      __syncwarp();
+    }
+    stage(bufC, lane, half, v);
+    if (kTwo) stage(bufZ, lane, half, z);
+    if (half == 1) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        store(&p.tmC, bufC, col - 32, row - lane);
+        if (kTwo) store(&p.tmAux, bufZ, col - 32, row - lane);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
+      ++blocks;
+    }
+  }
+};
+
 template <int MODE>
 struct EpiFor {
-  using type = PlainEpi<MODE>;
+  using type = typename std::conditional<(MODE >= kTmaBase), TmaBf16Epi<MODE - kTmaBase>, PlainEpi<MODE>>::type;
 };
 template <>
 struct EpiFor<kAccF32Tma> {
@@ -323,6 +445,11 @@ static int dispatch2(int mode, const CUtensorMap& ta, const CUtensorMap& tb, int
     case kGeluBwd: return launch2<A_MN, B_MN, kGeluBwd>(ta, tb, M, N, K, ep, s);
     case kAccF32: return launch2<A_MN, B_MN, kAccF32>(ta, tb, M, N, K, ep, s);
     case kAccF32Tma: return launch2<A_MN, B_MN, kAccF32Tma>(ta, tb, M, N, K, ep, s);
+    case kTmaBase + 0: return launch2<A_MN, B_MN, kTmaBase + 0>(ta, tb, M, N, K, ep, s);
+    case kTmaBase + 1: return launch2<A_MN, B_MN, kTmaBase + 1>(ta, tb, M, N, K, ep, s);
+    case kTmaBase + 2: return launch2<A_MN, B_MN, kTmaBase + 2>(ta, tb, M, N, K, ep, s);
+    case kTmaBase + 3: return launch2<A_MN, B_MN, kTmaBase + 3>(ta, tb, M, N, K, ep, s);
+    case kTmaBase + 5: return launch2<A_MN, B_MN, kTmaBase + 5>(ta, tb, M, N, K, ep, s);
     case kBiasResidual: return launch2<A_MN, B_MN, kBiasResidual>(ta, tb, M, N, K, ep, s);
   }
   return tdb_host::fail(int(cudaErrorInvalidValue), "unknown epilogue mode %d", mode);
@@ -338,6 +465,11 @@ static int dispatch_mode(int mode, const CUtensorMap& ta, const CUtensorMap& tb,
     case kGeluBwd: return launch<BN, A_MN, B_MN, kGeluBwd>(ta, tb, M, N, K, ep, s);
     case kAccF32: return launch<BN, A_MN, B_MN, kAccF32>(ta, tb, M, N, K, ep, s);
     case kAccF32Tma: return launch<BN, A_MN, B_MN, kAccF32Tma>(ta, tb, M, N, K, ep, s);
+    case kTmaBase + 0: return launch<BN, A_MN, B_MN, kTmaBase + 0>(ta, tb, M, N, K, ep, s);
+    case kTmaBase + 1: return launch<BN, A_MN, B_MN, kTmaBase + 1>(ta, tb, M, N, K, ep, s);
+    case kTmaBase + 2: return launch<BN, A_MN, B_MN, kTmaBase + 2>(ta, tb, M, N, K, ep, s);
+    case kTmaBase + 3: return launch<BN, A_MN, B_MN, kTmaBase + 3>(ta, tb, M, N, K, ep, s);
+    case kTmaBase + 5: return launch<BN, A_MN, B_MN, kTmaBase + 5>(ta, tb, M, N, K, ep, s);
     case kBiasResidual: return launch<BN, A_MN, B_MN, kBiasResidual>(ta, tb, M, N, K, ep, s);
   }
   return tdb_host::fail(int(cudaErrorInvalidValue), "unknown epilogue mode %d", mode);
@@ -416,6 +548,17 @@ TDB_API int tdb_gemm(const void* A, int a_mn, int64_t lda, const void* B, int b_
                                 uint64_t(ldc), 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     mode = kAccF32Tma;
+  } else if (mode != kAccF32 && reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
+             (mode != kBiasGelu || reinterpret_cast<uintptr_t>(aux_out) % 16 == 0)) {
+    rc = tdb_host::make_tmap_2d(&ep.tmC, C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(N), uint64_t(M),
+                                uint64_t(ldc), 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    if (mode == kBiasGelu) {
+      rc = tdb_host::make_tmap_2d(&ep.tmAux, aux_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(N), uint64_t(M),
+                                  uint64_t(ld_aux), 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+    }
+    mode += kTmaBase;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (bn == 512) {
