@@ -42,6 +42,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=("ours", "reference", "baseline"))
     p.add_argument("--arm", default="flux")
+    p.add_argument("--no-graph", action="store_true", help="issue every kernel from the host (no CUDA graph)")
     p.add_argument("--small", action="store_true", help="2-layer smoke configuration (not a headline number)")
     return p.parse_args()
 
@@ -176,7 +177,8 @@ def main():
         if world > 1:
             from tempname_dcu_b200.runtime import operator_factory_for
             factory = operator_factory_for(args.arm)
-        trainer = Trainer(config, args.arm, group, operator_factory=factory)
+        trainer = Trainer(config, args.arm, group, operator_factory=factory, cuda_graph=not args.no_graph,
+                          graph_warmup=min(2, max(0, args.warmup - 1)))
     from tempname_dcu_b200.train import synthetic_batches
     c = trainer.config
     (tokens_h, labels_h), = synthetic_batches(c, 1, seed=4321)
@@ -193,13 +195,16 @@ def main():
     sampler = ClockSampler(physical_gpu(local))
     sampler.start()
     launches0 = native.launch_count()
+    replays0 = getattr(trainer, "graph_replays", 0)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for _ in range(args.steps):
         loss, norm = trainer.step(tokens_d, labels_d)
     end.record()
     torch.cuda.synchronize()
-    launches = native.launch_count() - launches0
+    # host-issued library kernels plus those replayed from the captured step graph
+    launches = native.launch_count() - launches0 + \
+        getattr(trainer, "graph_kernels", 0) * (getattr(trainer, "graph_replays", 0) - replays0)
     clocks = sampler.stop()
     if world > 1:
         dist.barrier()
@@ -239,6 +244,7 @@ def main():
                         accumulation_steps=c["accumulation_steps"], vocab=c["vocab"], padded_vocab=c["padded_vocab"],
                         layers=c["layers"], hidden=c["hidden"], ffn=c["ffn"], heads=c["heads"],
                         tokens_per_step=tokens_per_step, arm=args.arm if args.impl == "ours" else None,
+                        cuda_graph=bool(args.impl == "ours" and not args.no_graph),
                         l2="inputs larger than L2 (13 GB of bf16 weights streamed per step); no flush",
                         model_tflops_per_gpu=round(flops / (ms_per_step / 1000.0) / world / 1e12, 1),
                         baseline_ref="published MA11 (8xH100, GPT-6.7B TP8): 18177.69 tok/s",
@@ -250,6 +256,9 @@ def main():
             gpu_launches=int(launches),
         )
         print(json.dumps(line), flush=True)
+    if hasattr(trainer, "release_graph"):
+        trainer.release_graph()  # graphs holding NCCL work go before the process group
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

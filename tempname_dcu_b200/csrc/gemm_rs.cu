@@ -67,16 +67,25 @@ struct Params {
   int delay_mb, delay_nb;
   uint64_t wait_ns;
   unsigned long long* phases;  // optional [grid][4]: start, produce done, first block ready, end
+  // optional device call state {set, expected, epoch, target0, target1}
+  // written by rs_advance_kernel before each call; when present it replaces
+  // `set` / `expected`, so a captured CUDA graph replays with fresh values
+  const uint32_t* call_state;
 };
+
+__device__ __forceinline__ int call_set(const Params& p) { return p.call_state ? int(__ldg(p.call_state)) : p.set; }
+__device__ __forceinline__ uint32_t call_expected(const Params& p) {
+  return p.call_state ? __ldg(p.call_state + 1) : p.expected;
+}
 
 __device__ __forceinline__ uint8_t* slot_ptr(const Params& p, int rank_of_heap, int source, int within) {
   return reinterpret_cast<uint8_t*>(p.peers[rank_of_heap] + p.recv_off +
-                                    (uint64_t(p.set * p.W + source) * p.per + within) * p.slot_bytes);
+                                    (uint64_t(call_set(p) * p.W + source) * p.per + within) * p.slot_bytes);
 }
 
 __device__ __forceinline__ uint32_t* flag_ptr(const Params& p, int rank_of_heap, int within, int source) {
   return reinterpret_cast<uint32_t*>(p.peers[rank_of_heap] + p.flags_off +
-                                     (uint64_t(p.set * p.per + within) * p.W + source) * 4);
+                                     (uint64_t(call_set(p) * p.per + within) * p.W + source) * 4);
 }
 
 __device__ __forceinline__ void red_release_sys(uint32_t* addr, uint32_t v) {
@@ -290,7 +299,7 @@ __device__ void signal_tiles(const Params& p, const gemm::TileOrder& order) {
 // Block readiness: all W sources delivered (acquire).
 __device__ __forceinline__ bool block_ready(const Params& p, int within) {
   for (int s = 0; s < p.W; ++s)
-    if (ld_acquire_sys(flag_ptr(p, p.rank, within, s)) < p.expected) return false;
+    if (ld_acquire_sys(flag_ptr(p, p.rank, within, s)) < call_expected(p)) return false;
   return true;
 }
 
@@ -313,7 +322,7 @@ __device__ __forceinline__ uint4 reduce_vec8(const Params& p, uint64_t local_bas
   for (int s = 0; s < kMaxWorld; ++s)
     if (s < p.W)
       src[s] = __ldcg(reinterpret_cast<const uint4*>(
-                          local_base + p.recv_off + (uint64_t(p.set * p.W + s) * p.per + within) * p.slot_bytes) + v);
+                          local_base + p.recv_off + (uint64_t(call_set(p) * p.W + s) * p.per + within) * p.slot_bytes) + v);
   const int64_t ov = int64_t(within) * p.chunk_rows * p.N / 8 + v;
   uint4 rw = make_uint4(0, 0, 0, 0), bw = make_uint4(0, 0, 0, 0);
   if (p.residual) rw = reinterpret_cast<const uint4*>(p.residual)[ov];
@@ -480,7 +489,7 @@ __device__ void consume_phase(const Params& p, int* status) {
     if (lane_id < 0 || (p.consume[k] % 2) == lane_id) mine |= 1ull << k;
   if (threadIdx.x == 0) s_done = 0;
   const uint32_t* flags = reinterpret_cast<const uint32_t*>(p.peers[p.rank] + p.flags_off) +
-                          uint64_t(p.set) * p.per * p.W;
+                          uint64_t(call_set(p)) * p.per * p.W;
   const uint64_t t_start = globaltimer();
   bool first = true;
   __syncthreads();
@@ -490,7 +499,7 @@ __device__ void consume_phase(const Params& p, int* status) {
     __syncthreads();
     bool saw = false;
     for (int i = threadIdx.x; i < p.per * p.W; i += blockDim.x) {
-      if (ld_relaxed_sys(flags + i) < p.expected) atomicAdd(&s_missing[i / p.W], 1);
+      if (ld_relaxed_sys(flags + i) < call_expected(p)) atomicAdd(&s_missing[i / p.W], 1);
       else saw = true;
     }
     if (saw) fence_acq_rel_sys();
@@ -569,6 +578,16 @@ __global__ void __launch_bounds__(gemm::kThreads, 1)
 // (the local producer kernel has completed), with bounded polling.
 constexpr int kReduceThreads = 256;
 
+// Per-call advance of the device call state (one thread): same arithmetic
+// as the host-side Context.next_call, so both agree in eager mode.
+__global__ void rs_advance_kernel(uint32_t* st, uint32_t signals) {
+  const uint32_t e = st[2], s = e & 1u;
+  st[3 + s] += signals;
+  st[0] = s;
+  st[1] = st[3 + s];
+  st[2] = e + 1u;
+}
+
 __global__ void __launch_bounds__(kReduceThreads)
     rs_reduce_kernel(const __grid_constant__ Params p, int* status) {
   unsigned long long* ph = p.phases ? p.phases + 4 * (blockIdx.x % 1024) : nullptr;
@@ -625,7 +644,8 @@ TDB_API int tdb_gemm_rs(const void* A, int64_t lda, const void* B, int b_mn, int
                         uint64_t recv_off, uint64_t slot_bytes, uint64_t flags_off, int set, unsigned int expected,
                         const uint8_t* qmask, void* out, const void* bias, const void* residual, const int* consume,
                         int policy, unsigned long long* timeline, long long delay_cycles, int delay_mb, int delay_nb,
-                        double wait_seconds, unsigned long long* phases, void* stream) {
+                        double wait_seconds, unsigned long long* phases, const uint32_t* call_state,
+                        void* stream) {
   if (!A || !B || !out || !tile_table || !peers || !qmask || !consume || W < 2 || W > rs::kMaxWorld || rank < 0 ||
       rank >= W)
     return tdb_host::fail(int(cudaErrorInvalidValue), "gemm_rs: bad pointers or ranks");
@@ -675,12 +695,22 @@ TDB_API int tdb_gemm_rs(const void* A, int64_t lda, const void* B, int b_mn, int
   p.delay_nb = delay_nb;
   p.wait_ns = uint64_t(wait_seconds * 1e9);
   p.phases = phases;
+  p.call_state = call_state;
   const int sms = tdb_host::sm_count();
   const int grid = order.num_tiles < sms ? order.num_tiles : sms;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (bn == 256) return b_mn ? rs::launch<256, true>(ta, tb, K, order, p, grid, s)
                              : rs::launch<256, false>(ta, tb, K, order, p, grid, s);
   return b_mn ? rs::launch<128, true>(ta, tb, K, order, p, grid, s) : rs::launch<128, false>(ta, tb, K, order, p, grid, s);
+}
+
+// Advance the device call state {set, expected, epoch, target0, target1}
+// (uint32 x 5, zero-initialised) before a call that passes it to tdb_gemm_rs.
+TDB_API int tdb_rs_advance(unsigned int* call_state, unsigned int signals, void* stream) {
+  if (!call_state) return tdb_host::fail(int(cudaErrorInvalidValue), "rs_advance: null state");
+  rs::rs_advance_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(call_state, signals);
+  tdb_host::launched(1);
+  return int(cudaGetLastError());
 }
 
 // Number of counter increments one (block, source) receives per call.

@@ -50,13 +50,21 @@ __global__ void sumsq_finish_kernel(const double* __restrict__ partial, int npar
 // norm_out = sqrt(total); coef = min(1, max_norm / (norm + 1e-6)); finite
 // flag cleared when the norm or the loss is not finite.
 __global__ void clip_kernel(const double* __restrict__ total, float max_norm, double* __restrict__ norm_out,
-                            float* __restrict__ coef, const float* __restrict__ loss, int* __restrict__ finite) {
+                            float* __restrict__ coef, const float* __restrict__ loss, int* __restrict__ finite,
+                            int* __restrict__ step_counter) {
+  if (step_counter) *step_counter += 1;  // optimizer step number on the device (CUDA-graph replayable)
   const double norm = sqrt(*total);
   *norm_out = norm;
   const float c = float(double(max_norm) / (norm + 1e-6));
   *coef = c < 1.f ? c : 1.f;
   const bool ok = isfinite(norm) && (loss == nullptr || isfinite(*loss));
   if (!ok) *finite = 0;
+}
+
+// Adam bias corrections of optimizer step `step` (same expressions as the host path).
+__device__ __forceinline__ void bias_corrections(int step, float beta1, float beta2, float& bc1, float& bc2_sqrt) {
+  bc1 = 1.f - powf(beta1, float(step));
+  bc2_sqrt = sqrtf(1.f - powf(beta2, float(step)));
 }
 
 struct WdRanges {
@@ -67,8 +75,10 @@ struct WdRanges {
 __global__ void adamw_kernel(float* __restrict__ master, float* __restrict__ grad, float* __restrict__ m,
                              float* __restrict__ v, uint16_t* __restrict__ param, int64_t n, WdRanges wd, float lr,
                              float beta1, float beta2, float eps, float weight_decay, float bc1, float bc2_sqrt,
-                             const float* __restrict__ coef_ptr, const int* __restrict__ finite, int zero_grad) {
+                             const float* __restrict__ coef_ptr, const int* __restrict__ finite, int zero_grad,
+                             const int* __restrict__ step_dev) {
   if (finite && *finite == 0) return;  // non-finite step: leave state untouched
+  if (step_dev) bias_corrections(*step_dev, beta1, beta2, bc1, bc2_sqrt);
   const float coef = coef_ptr ? *coef_ptr : 1.f;
   const float step = lr / bc1;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
@@ -105,8 +115,10 @@ __global__ void __launch_bounds__(256) adamw4_kernel(float4* __restrict__ master
                                                      uint2* __restrict__ param, int64_t n4, WdRanges wd, float lr,
                                                      float beta1, float beta2, float eps, float weight_decay,
                                                      float bc1, float bc2_sqrt, const float* __restrict__ coef_ptr,
-                                                     const int* __restrict__ finite, int zero_grad) {
+                                                     const int* __restrict__ finite, int zero_grad,
+                                                     const int* __restrict__ step_dev) {
   if (finite && *finite == 0) return;  // non-finite step: leave state untouched
+  if (step_dev) bias_corrections(*step_dev, beta1, beta2, bc1, bc2_sqrt);
   const float coef = coef_ptr ? *coef_ptr : 1.f;
   const float step = lr / bc1;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
@@ -154,9 +166,11 @@ TDB_API int tdb_sumsq(const float* g, int64_t n, double* partial, double* out, i
   return int(cudaGetLastError());
 }
 
+// step_counter (nullable): device int incremented once per call (the optimizer step).
 TDB_API int tdb_clip_coef(const double* total, float max_norm, double* norm_out, float* coef, const float* loss,
-                          int* finite, void* stream) {
-  clip_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(total, max_norm, norm_out, coef, loss, finite);
+                          int* finite, int* step_counter, void* stream) {
+  clip_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(total, max_norm, norm_out, coef, loss, finite,
+                                                              step_counter);
   tdb_host::launched(1);
   return int(cudaGetLastError());
 }
@@ -164,8 +178,10 @@ TDB_API int tdb_clip_coef(const double* total, float max_norm, double* norm_out,
 TDB_API int tdb_adamw(float* master, float* grad, float* m, float* v, void* param, int64_t n, int64_t wd_lo0,
                       int64_t wd_hi0, int64_t wd_lo1, int64_t wd_hi1, float lr, float beta1, float beta2, float eps,
                       float weight_decay, int step, const float* coef, const int* finite, int zero_grad,
-                      void* stream) {
-  if (step < 1 || n <= 0) return tdb_host::fail(int(cudaErrorInvalidValue), "adamw: bad step/size");
+                      const int* step_dev, void* stream) {
+  // step_dev (nullable): device step number read by the kernel instead of `step`
+  if ((!step_dev && step < 1) || n <= 0) return tdb_host::fail(int(cudaErrorInvalidValue), "adamw: bad step/size");
+  if (step < 1) step = 1;
   const float bc1 = 1.f - powf(beta1, float(step));
   const float bc2_sqrt = sqrtf(1.f - powf(beta2, float(step)));
   WdRanges wd{wd_lo0, wd_hi0, wd_lo1, wd_hi1};
@@ -180,11 +196,11 @@ TDB_API int tdb_adamw(float* master, float* grad, float* m, float* v, void* para
     adamw4_kernel<<<grid > 0 ? grid : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
         reinterpret_cast<float4*>(master), reinterpret_cast<float4*>(grad), reinterpret_cast<float4*>(m),
         reinterpret_cast<float4*>(v), static_cast<uint2*>(param), n4, wd, lr, beta1, beta2, eps, weight_decay, bc1,
-        bc2_sqrt, coef, finite, zero_grad);
+        bc2_sqrt, coef, finite, zero_grad, step_dev);
   } else {
     adamw_kernel<<<grid_for(n), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
         master, grad, m, v, static_cast<uint16_t*>(param), n, wd, lr, beta1, beta2, eps, weight_decay, bc1, bc2_sqrt,
-        coef, finite, zero_grad);
+        coef, finite, zero_grad, step_dev);
   }
   tdb_host::launched(1);
   return int(cudaGetLastError());

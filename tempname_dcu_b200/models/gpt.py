@@ -289,6 +289,7 @@ class Optimizer:
         self.norm = torch.zeros((), dtype=torch.float64, device=dev)
         self.coef = torch.ones((), dtype=torch.float32, device=dev)
         self.finite = torch.ones((), dtype=torch.int32, device=dev)
+        self.step_dev = torch.zeros((), dtype=torch.int32, device=dev)  # advanced by the clip kernel
 
     def step(self, loss=None):
         from ..ops import kernels as K
@@ -296,12 +297,12 @@ class Optimizer:
         m.reduce_replicated_gradients()
         m.global_grad_norm_sq(self.norm_sq)
         self.finite.fill_(1)
-        K.clip_coef(self.norm_sq, self.max_norm, self.norm, self.coef, loss, self.finite)
+        K.clip_coef(self.norm_sq, self.max_norm, self.norm, self.coef, loss, self.finite, step_counter=self.step_dev)
         self.step_count += 1
         P = m.params
         K.adamw(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.param, wd_ranges=P.decay_ranges, lr=self.lr,
                 beta1=self.betas[0], beta2=self.betas[1], eps=self.eps, weight_decay=self.wd,
-                step=self.step_count, coef=self.coef, finite=self.finite, zero_grad=True)
+                step_dev=self.step_dev, coef=self.coef, finite=self.finite, zero_grad=True)
         return self.norm
 
 

@@ -26,8 +26,8 @@ native.register("tdb_xent_combine", [V, I, I, V, V, V, F, I, V])
 native.register("tdb_xent_grad", [V, I64, V, I64, I, I, I, V, F, V])
 native.register("tdb_sumsq_partials_count", [])
 native.register("tdb_sumsq", [V, I64, V, V, I, V])
-native.register("tdb_clip_coef", [V, F, V, V, V, V, V])
-native.register("tdb_adamw", [V, V, V, V, V, I64, I64, I64, I64, I64, F, F, F, F, F, I, V, V, I, V])
+native.register("tdb_clip_coef", [V, F, V, V, V, V, V, V])
+native.register("tdb_adamw", [V, V, V, V, V, I64, I64, I64, I64, I64, F, F, F, F, F, I, V, V, I, V, V])
 native.register("tdb_to_bf16", [V, V, I64, V])
 native.register("tdb_embedding_fwd", [V, V, I64, I64, V, I64, I, I, I, V, V])
 native.register("tdb_add_positions", [V, V, I64, I, I, I, V])
@@ -161,18 +161,24 @@ def sumsq(g, partial, out, accumulate=False):
                                         int(accumulate), _s()), "sumsq")
 
 
-def clip_coef(total, max_norm, norm_out, coef, loss=None, finite=None):
+def clip_coef(total, max_norm, norm_out, coef, loss=None, finite=None, step_counter=None):
+    """norm = sqrt(total); coef = min(1, max_norm / (norm + 1e-6)); clears
+    ``finite`` on a non-finite norm or loss; increments ``step_counter``
+    (device int32) when given."""
     native.check(native.lib().tdb_clip_coef(total.data_ptr(), float(max_norm), norm_out.data_ptr(),
-                                            coef.data_ptr(), _p(loss), _p(finite), _s()), "clip coef")
+                                            coef.data_ptr(), _p(loss), _p(finite), _p(step_counter), _s()),
+                 "clip coef")
 
 
-def adamw(master, grad, m, v, param_bf16, *, wd_ranges, lr, beta1, beta2, eps, weight_decay, step, coef=None,
-          finite=None, zero_grad=True):
+def adamw(master, grad, m, v, param_bf16, *, wd_ranges, lr, beta1, beta2, eps, weight_decay, step=0, coef=None,
+          finite=None, zero_grad=True, step_dev=None):
+    """Fused AdamW over flat buffers.  The step number comes from ``step`` or,
+    when given, from the device int32 ``step_dev`` (CUDA-graph replayable)."""
     (a0, a1), (b0, b1) = (list(wd_ranges) + [(0, 0), (0, 0)])[:2]
     native.check(native.lib().tdb_adamw(master.data_ptr(), grad.data_ptr(), m.data_ptr(), v.data_ptr(),
                                         param_bf16.data_ptr(), master.numel(), a0, a1, b0, b1, float(lr),
                                         float(beta1), float(beta2), float(eps), float(weight_decay), int(step),
-                                        _p(coef), _p(finite), int(zero_grad), _s()), "adamw")
+                                        _p(coef), _p(finite), int(zero_grad), _p(step_dev), _s()), "adamw")
 
 
 def to_bf16(src, dst):

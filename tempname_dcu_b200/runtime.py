@@ -36,7 +36,8 @@ native.register("tdb_gemm_rs", [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p
                                 ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int, ctypes.c_uint, ctypes.c_void_p,
                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                 ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_double,
-                                ctypes.c_void_p, ctypes.c_void_p])
+                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p])
+native.register("tdb_rs_advance", [ctypes.c_void_p, ctypes.c_uint, ctypes.c_void_p])
 native.register("tdb_gemm_rs_signals_per_block", [ctypes.c_int, ctypes.c_int, ctypes.c_int])
 
 _CONTEXTS = {}
@@ -59,6 +60,9 @@ class Context:
         self.recv_off = FLAGS_BYTES
         self.epoch = 0
         self.targets = [0, 0]
+        # device copy of (set, expected, epoch, targets), advanced by a kernel
+        # before every call so that CUDA-graph replays see fresh values
+        self.call_state = torch.zeros(8, dtype=torch.int32, device=self.device)
         self.failed = False
         self.closed = False
         self.submission_lock = threading.Lock()
@@ -226,7 +230,10 @@ class FluxB200:
                     self.last_profile_delay = dict(physical=first0["physical"], lane=0, rank=0,
                                                    cycles=self.diagnostic_delay_cycles)
             heap = ctx.heap
-            native.check(native.lib().tdb_gemm_rs(
+            lib = native.lib()
+            stream = native.stream_ptr()
+            native.check(lib.tdb_rs_advance(ctx.call_state.data_ptr(), self.signals, stream), "rs advance")
+            native.check(lib.tdb_gemm_rs(
                 input_.data_ptr(), input_.stride(0), weight.data_ptr(), int(self.b_mn), weight.stride(0), self.m,
                 self.n, self.k, self.bn, self.tile_table.data_ptr(), heap.peers.data_ptr(), self.world, self.rank,
                 self.chunk_rows, ctx.recv_off, self.slot_bytes, ctx.flags_off, set_, expected,
@@ -235,7 +242,7 @@ class FluxB200:
                 1 if self.consumer_policy == "per_lane_ready" else 0,
                 0 if timeline is None else timeline.data_ptr(), delay, self._delay_tile[0], self._delay_tile[1],
                 PEER_WAIT_SECONDS, 0 if self.phase_buffer is None else self.phase_buffer.data_ptr(),
-                native.stream_ptr()), "fused gemm_rs")
+                ctx.call_state.data_ptr(), stream), "fused gemm_rs")
             self._last = (set_, expected, timeline)
             self.calls += 1
             ctx.calls += 1

@@ -51,8 +51,18 @@ def synthetic_batches(config, steps=1, seed=4321, pin=True):
 
 
 class Trainer:
+    """One tensor-parallel rank's trainer: model, fused AdamW, static inputs.
+
+    ``cuda_graph=True`` captures the whole optimizer step (every micro-batch's
+    forward and backward, the gradient collectives, clipping and AdamW) into
+    one CUDA graph after ``graph_warmup`` eager steps and replays it from then
+    on, so the host issues one launch per step instead of thousands.  Every
+    per-step quantity that a replay must refresh lives on the device (the
+    AdamW step number, the fused operators' call epochs); inputs are copied
+    into fixed device buffers before each replay."""
+
     def __init__(self, config, arm="flux", group=None, *, device="cuda", seed=1234, operator_factory=None,
-                 execution_plan=None):
+                 execution_plan=None, cuda_graph=False, graph_warmup=2):
         import torch
         self.model = GPT(config, arm, group, device=device, seed=seed, operator_factory=operator_factory,
                          execution_plan=execution_plan)
@@ -63,6 +73,12 @@ class Trainer:
         accum, m = c["accumulation_steps"], self.model.m
         self._tokens = torch.empty((accum, m), dtype=torch.int64, device=self.device)
         self._labels = torch.empty((accum, m), dtype=torch.int64, device=self.device)
+        self.cuda_graph = bool(cuda_graph)
+        self.graph_warmup = int(graph_warmup)
+        self._graph = None
+        self._eager_steps = 0
+        self.graph_kernels = 0   # library kernels recorded in the captured step
+        self.graph_replays = 0
 
     def save_checkpoint(self, directory, plan_sha256=None):
         """Sharded checkpoint of masters + Adam state (utils/checkpoint.py);
@@ -75,21 +91,52 @@ class Trainer:
         from .utils import checkpoint
         return checkpoint.load(self, directory, plan_sha256=plan_sha256)
 
+    def _body(self, tokens, labels):
+        c = self.config
+        self.loss.zero_()
+        for micro in range(c["accumulation_steps"]):
+            self.model.forward_backward(tokens[micro], labels[micro], self.loss)
+        return self.optimizer.step(self.loss)
+
     def step(self, tokens, labels):
         """One optimizer step over ``accumulation_steps`` micro-batches.
 
         tokens/labels: int64 [accumulation_steps, micro_batch*sequence] on the
         host (pinned, copied asynchronously here) or on the device."""
-        c = self.config
-        if tokens.device.type != "cuda":
+        import torch
+        if not self.cuda_graph:
+            if tokens.device.type != "cuda":
+                self._tokens.copy_(tokens, non_blocking=True)
+                self._labels.copy_(labels, non_blocking=True)
+                tokens, labels = self._tokens, self._labels
+            norm = self._body(tokens, labels)
+            return self.loss, norm
+        if tokens.data_ptr() != self._tokens.data_ptr():
             self._tokens.copy_(tokens, non_blocking=True)
+        if labels.data_ptr() != self._labels.data_ptr():
             self._labels.copy_(labels, non_blocking=True)
-            tokens, labels = self._tokens, self._labels
-        self.loss.zero_()
-        for micro in range(c["accumulation_steps"]):
-            self.model.forward_backward(tokens[micro], labels[micro], self.loss)
-        norm = self.optimizer.step(self.loss)
-        return self.loss, norm
+        if self._graph is None and self._eager_steps < self.graph_warmup:
+            self._eager_steps += 1
+            norm = self._body(self._tokens, self._labels)
+            return self.loss, norm
+        if self._graph is None:
+            from .ops import native
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            before = native.launch_count()
+            with torch.cuda.graph(graph):
+                self._graph_norm = self._body(self._tokens, self._labels)
+            self.graph_kernels = native.launch_count() - before
+            self._graph = graph  # capture recorded one step (host step count included); run it
+        else:
+            self.optimizer.step_count += 1
+        self._graph.replay()
+        self.graph_replays += 1
+        return self.loss, self._graph_norm
+
+    def release_graph(self):
+        """Drop the captured graph (before tearing down process groups)."""
+        self._graph = None
 
 
 def train_window(config, arm, group, warmup_steps, timed_steps, *, seed=1234, token_seed=4321, operator_factory=None,

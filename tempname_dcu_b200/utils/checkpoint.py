@@ -126,6 +126,8 @@ def load(trainer, directory, *, plan_sha256=None) -> int:
     P.param.copy_(P.master.to(torch.bfloat16))
     P.grad.zero_()
     opt.step_count = int(state["step"])
+    if getattr(opt, "step_dev", None) is not None:  # device step counter read by the AdamW kernel
+        opt.step_dev.fill_(opt.step_count)
     torch.set_rng_state(state["cpu_rng"])
     if state.get("cuda_rng") is not None and P.device.type == "cuda":
         torch.cuda.set_rng_state(state["cuda_rng"], P.device)

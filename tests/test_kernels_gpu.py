@@ -155,8 +155,9 @@ def test_vocab_parallel_cross_entropy(cuda, world):
     assert g[:, vocab:].abs().max().item() == 0
 
 
+@pytest.mark.parametrize("device_step", [False, True])
 @pytest.mark.parametrize("n,split", [(10_000, 6000), (10_001, 6001)])  # vectorised / scalar kernel
-def test_adamw_matches_torch(cuda, n, split):
+def test_adamw_matches_torch(cuda, n, split, device_step):
     import torch
     from tempname_dcu_b200.ops import kernels as k
     torch.manual_seed(3)
@@ -169,11 +170,20 @@ def test_adamw_matches_torch(cuda, n, split):
     v = torch.zeros(n, device=cuda)
     bf = torch.empty(n, dtype=torch.bfloat16, device=cuda)
     coef = torch.tensor([0.5], device=cuda)
+    step_dev = torch.zeros((), dtype=torch.int32, device=cuda)
+    total = torch.ones((), dtype=torch.float64, device=cuda)
+    scratch = [torch.empty((), dtype=torch.float64, device=cuda), torch.empty((), dtype=torch.float32, device=cuda)]
     for step in range(1, 4):
         g = torch.randn(n, device=cuda)
         grad = g.clone()
-        k.adamw(master, grad, m, v, bf, wd_ranges=[(0, split)], lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8,
-                weight_decay=0.01, step=step, coef=coef)
+        if device_step:  # the clip kernel advances the device step counter the AdamW kernel reads
+            k.clip_coef(total, 1.0, scratch[0], scratch[1], step_counter=step_dev)
+            k.adamw(master, grad, m, v, bf, wd_ranges=[(0, split)], lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8,
+                    weight_decay=0.01, step_dev=step_dev, coef=coef)
+            assert int(step_dev.item()) == step
+        else:
+            k.adamw(master, grad, m, v, bf, wd_ranges=[(0, split)], lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8,
+                    weight_decay=0.01, step=step, coef=coef)
         assert grad.abs().max().item() == 0  # gradient reset is fused
         pa.grad, pb.grad = g[:split] * 0.5, g[split:] * 0.5
         opt.step()
