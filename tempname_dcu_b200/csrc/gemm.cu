@@ -6,6 +6,7 @@
 // one persistent tcgen05 kernel; bias, exact-erf GELU (model.py:261), GELU
 // backward, residual adds and fp32 weight-gradient accumulation
 // (model.py:401-408) are fused into the epilogue instead of separate kernels.
+#include <cmath>
 #include <type_traits>
 
 #include "gemm.cuh"
@@ -494,11 +495,45 @@ int make_operand_map(CUtensorMap* map, const void* ptr, bool mn_major, int mn, i
                                 uint64_t(ld), 64, BK, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Tile shape for an M x N output: the candidate with the best product of
+// (a) wave efficiency -- work units over the units the machine runs in
+// ceil(units / slots) full waves (2-CTA tiles occupy SM pairs), (b) the useful
+// fraction of partial edge tiles and (c) a per-shape throughput factor (larger
+// tiles re-read less shared memory per MMA).  Returns the bn code of tdb_gemm.
+int pick_tile(int M, int N, int K, int sms) {
+  struct Cand {
+    int code, tm, tn, slots;
+    double speed;
+  };
+  const Cand cands[4] = {{512, 256, 256, sms / 2, 1.00}, {256, 128, 256, sms, 0.95}, {192, 128, 192, sms, 0.92},
+                         {128, 128, 128, sms, 0.85}};
+  int best = 128;
+  double best_score = -1.0;
+  for (const Cand& c : cands) {
+    if (c.code == 512 && (M < 256 || N < 256 || K < 256)) continue;
+    if (N <= 128 && c.tn > 128) continue;
+    const double tiles_m = double((M + c.tm - 1) / c.tm), tiles_n = double((N + c.tn - 1) / c.tn);
+    const double units = tiles_m * tiles_n;
+    const double waves = std::ceil(units / c.slots);
+    const double useful = (double(M) / c.tm) * (double(N) / c.tn) / units;
+    const double score = units / (waves * c.slots) * useful * c.speed;
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = c.code;
+    }
+  }
+  return best;
+}
+
 }  // namespace gemm
 }  // namespace tdb
 
 using namespace tdb;
 using namespace tdb::gemm;
+
+// Tile choice of tdb_gemm for a shape on a GPU with `sms` SMs (bn code: 128,
+// 192, 256, or 512 = 2-CTA 256 x 256).  Pure function of its arguments.
+TDB_API int tdb_gemm_pick_tile(int M, int N, int K, int sms) { return tdb::gemm::pick_tile(M, N, K, sms); }
 
 // C = epilogue(A * B^T).  a_mn / b_mn select the storage of A ([M,K] vs [K,M])
 // and B ([N,K] vs [K,N]); lda / ldb are the row strides of that storage in
@@ -515,18 +550,9 @@ TDB_API int tdb_gemm(const void* A, int a_mn, int64_t lda, const void* B, int b_
     return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: epilogue mode %d needs an aligned aux tensor", mode);
   if (bias && (reinterpret_cast<uintptr_t>(bias) % 16))
     return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: bias must be 16-byte aligned");
-  if (bn == 0) {
-    const int sms = tdb_host::sm_count();
-    const int tiles256 = ((M + 127) / 128) * ((N + 255) / 256);
-    const int pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
-    if (M >= 256 && N >= 256 && pair_tiles >= sms / 2 && K >= 256)
-      bn = 512;  // 2-CTA 256 x 256 tiles
-    else
-      bn = (tiles256 >= sms || N <= 128) ? 256 : 128;
-    if (N <= 128) bn = 128;
-  }
-  if (bn != 128 && bn != 256 && bn != 512)
-    return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: bn must be 128, 256 or 512 (2-CTA)");
+  if (bn == 0) bn = pick_tile(M, N, K, tdb_host::sm_count());
+  if (bn != 128 && bn != 192 && bn != 256 && bn != 512)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "gemm: bn must be 128, 192, 256 or 512 (2-CTA)");
   CUtensorMap ta, tb;
   int rc = make_operand_map(&ta, A, a_mn, M, K, lda, BM);
   if (rc) return rc;
@@ -568,5 +594,6 @@ TDB_API int tdb_gemm(const void* A, int a_mn, int64_t lda, const void* B, int b_
     return dispatch2<true, false>(mode, ta, tb, M, N, K, ep, s);
   }
   if (bn == 256) return dispatch_major<256>(a_mn, b_mn, mode, ta, tb, M, N, K, ep, s);
+  if (bn == 192) return dispatch_major<192>(a_mn, b_mn, mode, ta, tb, M, N, K, ep, s);
   return dispatch_major<128>(a_mn, b_mn, mode, ta, tb, M, N, K, ep, s);
 }

@@ -27,13 +27,14 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one 128B swizzle row
 constexpr int kThreads = 192;
 
-template <int BN, int STAGES = (BN == 256 ? 4 : 6)>
+template <int BN, int STAGES = (BN == 128 ? 6 : 4)>
 struct Config {
   static constexpr int kStages = STAGES;
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = 2 * BN;  // two accumulators
+  // two accumulators of BN columns; the allocation is a power of two
+  static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 

@@ -24,7 +24,7 @@ def test_linear_kk(cuda, M, N, K):
     assert g_status[0] == 0
 
 
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 192, 256])
 def test_both_tile_widths(cuda, bn):
     import torch
     from tempname_dcu_b200.ops import gemm as g
@@ -137,3 +137,31 @@ def test_two_cta_fused_epilogues(cuda):
     assert _rel(pre, z_ref) < 5e-3 and _rel(act, F.gelu(pre.float())) < 5e-3
     out = g.gemm(x, w, mode=g.BIAS_RESIDUAL, bias=b, aux=res, bn=512)
     assert _rel(out, z_ref + res.float()) < 5e-3
+
+
+@pytest.mark.parametrize("a_mn,b_mn,mode", [(False, False, "bias_gelu"), (False, True, "store"), (True, True, "acc")])
+def test_192_wide_tiles_ragged(cuda, a_mn, b_mn, mode):
+    """128 x 192 tiles with N not a multiple of 192 (TP-sized shapes)."""
+    import torch
+    import torch.nn.functional as F
+    from tempname_dcu_b200.ops import gemm as g
+    torch.manual_seed(9)
+    M, N, K = 512, 1000, 384
+    A = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    B = (torch.randn(N, K, device=cuda) / 8).to(torch.bfloat16)
+    a = A.t().contiguous() if a_mn else A
+    b = B.t().contiguous() if b_mn else B
+    ref = A.float() @ B.float().t()
+    if mode == "acc":
+        acc = torch.randn(M, N, device=cuda)
+        base = acc.clone()
+        g.gemm(a, b, a_mn=a_mn, b_mn=b_mn, out=acc, mode=g.ACC_F32, beta=1.0, bn=192)
+        assert _rel(acc, base + ref) < 2e-3
+    elif mode == "bias_gelu":
+        bias = torch.randn(N, device=cuda).to(torch.bfloat16)
+        pre = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+        act = g.gemm(a, b, mode=g.BIAS_GELU, bias=bias, aux_out=pre, bn=192)
+        assert _rel(pre, ref + bias.float()) < 5e-3 and _rel(act, F.gelu(pre.float())) < 5e-3
+    else:
+        out = g.gemm(a, b, a_mn=a_mn, b_mn=b_mn, bn=192)
+        assert _rel(out, ref) < 5e-3

@@ -240,3 +240,17 @@ def test_full_budget_allows_full_quantization():
 def test_invalid_or_failed_measurements_are_fatal(bad):
     with pytest.raises(ValueError):
         P.fit_role(*SHAPE, lambda *a: bad, config=CFG)
+
+
+def test_gemm_tile_picker_prefers_full_waves():
+    """The tcgen05 GEMM's tile choice (pure host function of the library)."""
+    import ctypes
+    from tempname_dcu_b200.ops import native
+    fn = native.lib().tdb_gemm_pick_tile
+    fn.argtypes = [ctypes.c_int] * 4
+    fn.restype = ctypes.c_int
+    assert fn(2048, 16384, 4096, 148) == 512   # large: 2-CTA 256 x 256
+    assert fn(2048, 1536, 4096, 148) == 192    # TP8 QKV: 128 x 192 fills one wave
+    assert fn(2048, 2048, 4096, 148) == 512    # TP8 FC1: 64 SM pairs in one wave
+    assert fn(128, 128, 64, 148) == 128
+    assert fn(64, 96, 64, 148) == 128          # N <= 128 keeps the narrow tile
