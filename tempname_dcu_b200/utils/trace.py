@@ -28,6 +28,7 @@ def main(argv=None):
     ap.add_argument("--json", default="")
     ap.add_argument("--step", action="store_true", help="profile one whole optimizer step instead")
     ap.add_argument("--arm", default="flux", help="tensor-parallel arm when launched with torchrun (WORLD_SIZE > 1)")
+    ap.add_argument("--graph", action="store_true", help="capture the step as a CUDA graph and profile a replay")
     args = ap.parse_args(argv)
     import os
     import torch
@@ -48,21 +49,24 @@ def main(argv=None):
         if args.arm != "nccl":
             from ..runtime import operator_factory_for
             factory = operator_factory_for(args.arm)
-    trainer = Trainer(cfg, args.arm if args.arm != "nccl" else "flux", group, operator_factory=factory)
+    trainer = Trainer(cfg, args.arm if args.arm != "nccl" else "flux", group, operator_factory=factory,
+                      cuda_graph=args.graph, graph_warmup=1)
     (tokens, labels), = synthetic_batches(trainer.config, 1)
     tokens, labels = tokens.cuda(), labels.cuda()
-    trainer.step(tokens, labels)
+    for _ in range(3 if args.graph else 1):  # graph: eager step, capture + replay, replay
+        trainer.step(tokens, labels)
     torch.cuda.synchronize()
     model = trainer.model
     with profile(activities=[ProfilerActivity.CUDA, ProfilerActivity.CPU]) as prof:
         t0 = time.perf_counter()
-        if args.step:
+        if args.step or args.graph:
             trainer.step(tokens, labels)
         else:
             for i in range(args.micro):
                 model.forward_backward(tokens[i], labels[i], trainer.loss)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
+    trainer.release_graph()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
