@@ -145,12 +145,16 @@ def split_sizes(world, rank, destination, elements):
     return send, receive
 
 
-def tile_table(m, n, world, chunk_rows, arm, plan=None, *, block_m=128, block_n=256, k=1):
-    """Device tile-order table for the fused GEMM-RS: the production schedule
-    expanded to (block_m x block_n) output tiles, row blocks in schedule order
-    and the N tiles of each row block consecutively.  Values are
-    ``m_tile * n_tiles + n_tile``."""
-    order = schedule(m, n, k, world, chunk_rows, arm, plan)
+def remote_first_order(order, world, rank):
+    """The same blocks with this rank's destinations rotated so that blocks
+    for rank+1, rank+2, ... are produced first and this rank's own blocks
+    last (their data then crosses NVLink while the local tiles compute).
+    Block order within a destination is kept."""
+    return sorted(order, key=lambda item: ((item["destination"] - rank - 1) % world, item["slot"]))
+
+
+def tiles_for_order(order, n, chunk_rows, *, block_m=128, block_n=256):
+    """Expand a block order to the device tile table (see tile_table)."""
     if chunk_rows % block_m:
         raise ValueError("chunk_rows must be a multiple of the tile height")
     n_tiles = -(-n // block_n)
@@ -161,3 +165,12 @@ def tile_table(m, n, world, chunk_rows, arm, plan=None, *, block_m=128, block_n=
             for nt in range(n_tiles):
                 table.append((first + sub) * n_tiles + nt)
     return table
+
+
+def tile_table(m, n, world, chunk_rows, arm, plan=None, *, block_m=128, block_n=256, k=1):
+    """Device tile-order table for the fused GEMM-RS: the production schedule
+    expanded to (block_m x block_n) output tiles, row blocks in schedule order
+    and the N tiles of each row block consecutively.  Values are
+    ``m_tile * n_tiles + n_tile``."""
+    order = schedule(m, n, k, world, chunk_rows, arm, plan)
+    return tiles_for_order(order, n, chunk_rows, block_m=block_m, block_n=block_n)

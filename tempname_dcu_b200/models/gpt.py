@@ -103,11 +103,13 @@ class GPT:
         # whenever the forward projections do.
         self._bwd_rs = {}
         if factory is not None and self.world > 1:
+            # sequence-parallel all-gathers over NVLink (same rows/cols everywhere)
+            self.tp.enable_symmetric_gather(self.ml, self.h)
             from ..runtime import FluxB200
             for k in (3 * self.h // self.world, self.f // self.world, self.vocab_local):
                 if k not in self._bwd_rs:
                     self._bwd_rs[k] = FluxB200(self.m, self.h, k, group, "flux", chunk_rows=c["chunk_rows"],
-                                               b_mn=True)
+                                               b_mn=True, remote_first=True)
 
     def _dgrad_rs(self, dy, weight):
         """RS(dy @ weight) -> [m/W, h]: fused kernel when available, else

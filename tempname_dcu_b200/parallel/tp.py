@@ -28,6 +28,15 @@ class TPGroup:
             self.backend = str(dist.get_backend(group))
         else:
             self.world, self.rank, self.backend = 1, 0, "none"
+        self.symm_gather = None
+
+    def enable_symmetric_gather(self, rows, cols):
+        """Route gathers of [rows, cols] bf16 blocks through the NVLink pull
+        kernel (parallel/allgather.py) instead of NCCL.  Collective."""
+        if self.world > 1 and self.backend == "nccl" and self.symm_gather is None:
+            from .allgather import SymmAllGather
+            self.symm_gather = SymmAllGather(self, rows, cols)
+        return self.symm_gather
 
     # ------------------------------------------------------------------ rows
     def gather(self, x_local, out=None):
@@ -35,6 +44,8 @@ class TPGroup:
         if self.world == 1:
             return x_local
         x_local = x_local.contiguous()
+        if self.symm_gather is not None and self.symm_gather.matches(x_local):
+            return self.symm_gather(x_local, out)
         rows = x_local.shape[0]
         if out is None:
             out = torch.empty((rows * self.world, *x_local.shape[1:]), dtype=x_local.dtype, device=x_local.device)

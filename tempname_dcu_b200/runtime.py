@@ -27,7 +27,8 @@ import hashlib
 import json
 import threading
 
-from .mapping import ARRIVAL_ARMS, BACKEND, block_selection, schedule, selection_statistics, tile_table
+from .mapping import (ARRIVAL_ARMS, BACKEND, block_selection, remote_first_order, schedule, selection_statistics,
+                      tile_table, tiles_for_order)
 from .ops import native
 
 native.register("tdb_gemm_rs", [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
@@ -144,7 +145,13 @@ class FluxB200:
     """Fused GEMM + reduce-scatter for one projection shape and arm."""
 
     def __init__(self, m, n, k, group, arm, codec=None, chunk_rows=128, plan=None, diagnostic_delay_cycles=0,
-                 b_mn=False, tile_n=None):
+                 b_mn=False, tile_n=None, remote_first=False):
+        """``remote_first`` (first three arms only): produce the blocks bound for
+        other ranks first and this rank's own blocks last, so the NVLink
+        transfers overlap the local tiles; results are bitwise unchanged (the
+        receiving side reduces sources in fixed order).  Off for the
+        reference experiment arms, whose production order is part of their
+        definition."""
         import torch
         if type(diagnostic_delay_cycles) is not int or not 0 <= diagnostic_delay_cycles <= 100_000_000:
             raise ValueError("diagnostic_delay_cycles must be an integer in [0, 100000000]")
@@ -175,7 +182,12 @@ class FluxB200:
         # Tile width: every rank derives it from the shape alone.
         sms = native.lib().tdb_sm_count(torch.cuda.current_device())
         self.bn = tile_n or (256 if (m // 128) * (n // 256) >= sms else 128)
-        self.tiles = tile_table(m, n, self.world, chunk_rows, arm, self.plan, block_m=128, block_n=self.bn, k=k)
+        self.remote_first = bool(remote_first) and arm not in ARRIVAL_ARMS
+        if self.remote_first:
+            self.tiles = tiles_for_order(remote_first_order(self.order, self.world, self.rank), n, chunk_rows,
+                                         block_m=128, block_n=self.bn)
+        else:
+            self.tiles = tile_table(m, n, self.world, chunk_rows, arm, self.plan, block_m=128, block_n=self.bn, k=k)
         self.tile_table = torch.tensor(self.tiles, dtype=torch.int32, device=self.device)
         self.qmask = torch.tensor([int(x) for x in self.selection_mask], dtype=torch.uint8, device=self.device)
         self.per = m // self.world // chunk_rows
@@ -354,6 +366,7 @@ class FluxB200:
         return dict(backend=BACKEND, arm=self.arm, rank=self.rank, calls=self.calls,
                     shape=[self.m, self.n, self.k], chunk_rows=self.chunk_rows,
                     production_schedule=self.order, mapping_sha256=self.mapping_sha256,
+                    production_order="remote_first" if self.remote_first else "schedule",
                     gemms_per_call=1, collectives_per_call=1, fused_kernel="tdb::rs::gemm_rs_kernel",
                     tile_n=self.bn, tiles_per_call=len(self.tiles), quantization=quantization,
                     selection_mask=list(self.selection_mask),
@@ -372,8 +385,9 @@ class FluxB200:
                     overlap_claim="epilogue peer stores overlap the MMA of later tiles in one kernel")
 
 
-def operator_factory_for(arm):
-    """Factory for ``GPT(operator_factory=...)``: a FluxB200 per row-parallel projection."""
-    def factory(m, n, k, group, arm=arm, chunk_rows=128, plan=None):
-        return FluxB200(m, n, k, group, arm, chunk_rows=chunk_rows, plan=plan)
+def operator_factory_for(arm, remote_first=True):
+    """Factory for ``GPT(operator_factory=...)``: a FluxB200 per row-parallel
+    projection (training uses the remote-first production order)."""
+    def factory(m, n, k, group, arm=arm, chunk_rows=128, plan=None, **kw):
+        return FluxB200(m, n, k, group, arm, chunk_rows=chunk_rows, plan=plan, remote_first=remote_first, **kw)
     return factory

@@ -79,6 +79,8 @@ def _worker(rank, world, port, result_path):
             out[f"bitwise.k{k}"] = dict(
                 b_c=bool(torch.equal(outputs[ARMS[1]], outputs[ARMS[2]])),
                 c_d=bool(torch.equal(outputs[ARMS[2]], outputs[ARMS[3]])))
+            rf = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, remote_first=True).forward(x, w)
+            out[f"bitwise.k{k}"]["remote_first"] = bool(torch.equal(rf, outputs[ARMS[0]]))
             plan_e_base = dict(plan_e, arrival_order=base_order(m, n, k, world, chunk))
             ebase = FluxB200(m, n, k, group, ARMS[4], chunk_rows=chunk, plan=plan_e_base).forward(x, w)
             out[f"bitwise.k{k}"]["e_ebase"] = bool(torch.equal(ebase, outputs[ARMS[4]]))
@@ -89,6 +91,36 @@ def _worker(rank, world, port, result_path):
             plain, _ = projection_reference(x, w, rank, world, group, False)
             ref = ((res.float() + plain.float()).to(torch.bfloat16).float() + bias.float()).to(torch.bfloat16)
             out[f"bias_residual.k{k}"] = relative_error(y, ref)
+        # NVLink all-gather (parallel/allgather.py) vs NCCL, eager and replayed
+        from tempname_dcu_b200.parallel.allgather import SymmAllGather
+        from tempname_dcu_b200.parallel.tp import TPGroup
+        tp = TPGroup(group)
+        ag = SymmAllGather(tp, 256, 4096)
+        ok = []
+        for i in range(5):
+            xl = torch.randn(256, 4096, device="cuda").to(torch.bfloat16)
+            ref = torch.empty(256 * world, 4096, dtype=torch.bfloat16, device="cuda")
+            dist.all_gather_into_tensor(ref, xl, group=group)
+            ok.append(bool(torch.equal(ag(xl), ref)))
+        xs = torch.zeros(256, 4096, dtype=torch.bfloat16, device="cuda")
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            y1 = ag(xs)
+            y2 = ag((xs * 2).to(torch.bfloat16))
+        for i in range(3):
+            xs.copy_(torch.randn(256, 4096, device="cuda").to(torch.bfloat16))
+            graph.replay()
+            ref = torch.empty(256 * world, 4096, dtype=torch.bfloat16, device="cuda")
+            dist.all_gather_into_tensor(ref, xs, group=group)
+            ref2 = torch.empty_like(ref)
+            dist.all_gather_into_tensor(ref2, (xs * 2).to(torch.bfloat16), group=group)
+            ok.append(bool(torch.equal(y1, ref)) and bool(torch.equal(y2, ref2)))
+        del graph
+        torch.cuda.synchronize()
+        out["allgather"] = ok
+        native.raise_on_status()
+        ag.close()
         torch.cuda.synchronize()
         native.raise_on_status()
         shutdown_context(group)
@@ -110,7 +142,10 @@ def test_fused_gemm_rs_all_arms(tmp_path):
     path = str(tmp_path / "result.json")
     mp.spawn(_worker, args=(world, _free_port(), path), nprocs=world, join=True)
     res = json.load(open(path))
+    assert res.get("allgather") and all(res["allgather"]), res.get("allgather")
     for key, value in res.items():
+        if key == "allgather":
+            continue
         if key.startswith("bitwise"):
             assert all(value.values()), (key, value)
         elif key.startswith("bias_residual"):

@@ -254,3 +254,19 @@ def test_gemm_tile_picker_prefers_full_waves():
     assert fn(2048, 2048, 4096, 148) == 512    # TP8 FC1: 64 SM pairs in one wave
     assert fn(128, 128, 64, 148) == 128
     assert fn(64, 96, 64, 148) == 128          # N <= 128 keeps the narrow tile
+
+
+def test_remote_first_order_rotates_destinations():
+    from tempname_dcu_b200.mapping import remote_first_order, schedule, tiles_for_order
+    m, n, k, world, chunk = 4096, 512, 256, 4, 128
+    order = schedule(m, n, k, world, chunk, "flux")
+    for rank in range(world):
+        rf = remote_first_order(order, world, rank)
+        dests = [item["destination"] for item in rf]
+        per = m // world // chunk
+        expect = [(rank + 1 + i) % world for i in range(world) for _ in range(per)]
+        assert dests == expect
+        for d in range(world):  # block order inside a destination is unchanged
+            assert [x["within"] for x in rf if x["destination"] == d] == list(range(per))
+        tiles = tiles_for_order(rf, n, chunk, block_m=128, block_n=256)
+        assert sorted(tiles) == list(range((m // 128) * (n // 256)))
