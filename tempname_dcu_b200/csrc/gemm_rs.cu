@@ -588,7 +588,7 @@ __global__ void rs_advance_kernel(uint32_t* st, uint32_t signals) {
   st[2] = e + 1u;
 }
 
-__global__ void __launch_bounds__(kReduceThreads)
+__global__ void __launch_bounds__(kReduceThreads, 2)
     rs_reduce_kernel(const __grid_constant__ Params p, int* status) {
   unsigned long long* ph = p.phases ? p.phases + 4 * (blockIdx.x % 1024) : nullptr;
   consume_phase(p, status);
@@ -615,7 +615,16 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int K, const gem
   tdb_host::launched(1);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs: producer launch failed");
-  const int rgrid = 4 * tdb_host::sm_count();
+  // Exactly the CTAs that are co-resident: every consumer CTA is polling and
+  // reducing at the same time (a second wave would start only after the
+  // first one drained, serialising the waits).
+  static int per_sm[64] = {0};
+  if (!per_sm[dev & 63]) {
+    int nb = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, rs_reduce_kernel, kReduceThreads, 0);
+    per_sm[dev & 63] = (e == cudaSuccess && nb > 0) ? nb : 1;
+  }
+  const int rgrid = per_sm[dev & 63] * tdb_host::sm_count();
   rs_reduce_kernel<<<rgrid, kReduceThreads, 0, stream>>>(p, status);
   tdb_host::launched(1);
   e = cudaGetLastError();
