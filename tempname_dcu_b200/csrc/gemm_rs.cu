@@ -557,7 +557,11 @@ __device__ void consume_phase(const Params& p, int* status) {
   }
 }
 
-constexpr int kStages = 3;
+// Shared memory: STAGES x (A + B tile) + the 4 x 32 x BN staging of PushEpi.
+// 128-wide tiles keep six stages in flight (latency of the TMA loads covered),
+// 256-wide tiles fit three.
+template <int BN>
+constexpr int kStagesFor = BN == 128 ? 6 : 3;
 
 template <int BN, bool B_MN>
 __global__ void __launch_bounds__(gemm::kThreads, 1)
@@ -568,7 +572,7 @@ __global__ void __launch_bounds__(gemm::kThreads, 1)
   epi.status = status;
   unsigned long long* ph = p.phases ? p.phases + 4 * blockIdx.x : nullptr;
   if (ph && threadIdx.x == 0) ph[0] = globaltimer();
-  gemm::gemm_mainloop<BN, false, B_MN, PushEpi<BN>, kStages>(&tmA, &tmB, K, order, epi, status);
+  gemm::gemm_mainloop<BN, false, B_MN, PushEpi<BN>, kStagesFor<BN>>(&tmA, &tmB, K, order, epi, status);
   signal_tiles(p, order);
   if (ph && threadIdx.x == 0) ph[1] = globaltimer();
 }
@@ -598,7 +602,7 @@ __global__ void __launch_bounds__(kReduceThreads, 2)
 template <int BN, bool B_MN>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int K, const gemm::TileOrder& order, const Params& p,
                   int grid, cudaStream_t stream) {
-  using Cfg = gemm::Config<BN, kStages>;
+  using Cfg = gemm::Config<BN, kStagesFor<BN>>;
   constexpr int kSmem = Cfg::kSmemBytes + PushEpi<BN>::kSmemBytes;
   static_assert(kSmem <= 227 * 1024, "fused GEMM-RS shared memory budget");
   auto kern = gemm_rs_kernel<BN, B_MN>;

@@ -33,6 +33,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--arms", default="all")
     ap.add_argument("--remote-first", action="store_true", help="produce remote-bound blocks first (training order)")
+    ap.add_argument("--tile-n", type=int, default=0, help="fused kernel tile width (128 or 256; 0 = automatic)")
     args = ap.parse_args(argv)
     import torch
     import torch.distributed as dist
@@ -87,7 +88,8 @@ def main(argv=None):
         compute_us = flops / (peak * 1e12) * 1e6
         for arm in arms:
             plan = make_role(m, n, k, world, chunk) if arm in ARMS[3:] else None
-            op = FluxB200(m, n, k, group, arm, chunk_rows=chunk, plan=plan, remote_first=args.remote_first)
+            op = FluxB200(m, n, k, group, arm, chunk_rows=chunk, plan=plan, remote_first=args.remote_first,
+                          tile_n=args.tile_n or None)
             us = timed(lambda: op.forward(x, w, bias, res))
             op.enable_phase_profile(True)
             op.forward(x, w, bias, res)
