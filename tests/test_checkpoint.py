@@ -3,7 +3,6 @@ refusals (missing manifest, tampered shard, other config / world / plan),
 and a 2-rank gloo save + load."""
 import json
 import os
-import socket
 import types
 
 import pytest
@@ -62,19 +61,12 @@ def test_refusals(tmp_path):
         ck.load(_trainer(), d)
 
 
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
 
 
-def _worker(rank, world, port, path, queue):
+def _worker(rank, world, init_file, path, queue):
     import torch
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
     try:
         from tempname_dcu_b200.parallel.tp import TPGroup
         from tempname_dcu_b200.utils import checkpoint as ck
@@ -95,7 +87,7 @@ def test_two_gloo_ranks(tmp_path):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
-    port = _free_port()
+    port = str(tmp_path / "rendezvous")  # file rendezvous path (no TCP port race)
     path = str(tmp_path / "ck2")
     procs = [ctx.Process(target=_worker, args=(r, 2, port, path, queue)) for r in range(2)]
     for p in procs:

@@ -12,32 +12,23 @@ Runs as child processes over NCCL (one per GPU, NVLS off); skipped with fewer
 than two GPUs.
 """
 import os
-import socket
 
 import pytest
 
 pytestmark = pytest.mark.gpu
 
 
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
 
 
-def _worker(rank, world, port, result_path):
+def _worker(rank, world, init_file, result_path):
     import json
     import math
     from datetime import timedelta
     import torch
     import torch.distributed as dist
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
-                            device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", init_method=f"file://{init_file}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=120), device_id=torch.device("cuda", rank))
     group = dist.group.WORLD
     from tempname_dcu_b200.mapping import ARMS
     from tempname_dcu_b200.ops import native
@@ -140,7 +131,8 @@ def test_fused_gemm_rs_all_arms(tmp_path):
     world = 2
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     path = str(tmp_path / "result.json")
-    mp.spawn(_worker, args=(world, _free_port(), path), nprocs=world, join=True)
+    # file rendezvous: no TCP port to race for
+    mp.spawn(_worker, args=(world, str(tmp_path / "rendezvous"), path), nprocs=world, join=True)
     res = json.load(open(path))
     assert res.get("allgather") and all(res["allgather"]), res.get("allgather")
     for key, value in res.items():

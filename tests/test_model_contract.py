@@ -3,7 +3,6 @@ tensor-parallel collectives over 2 gloo ranks (reference:
 tests/test_model_contract.py)."""
 import math
 import os
-import socket
 
 import pytest
 
@@ -74,19 +73,12 @@ def test_flat_parameter_layout_regions_and_alignment():
     assert not torch.equal(flat.p("embedding"), other.p("embedding"))    # sharded: rank-specific
 
 
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
 
 
-def _gloo_worker(rank, world, port, queue):
+def _gloo_worker(rank, world, init_file, queue):
     import torch
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
     try:
         from tempname_dcu_b200.parallel.tp import TPGroup
         tp = TPGroup(dist.group.WORLD)
@@ -108,13 +100,13 @@ def _gloo_worker(rank, world, port, queue):
         dist.destroy_process_group()
 
 
-def test_tp_collectives_two_gloo_ranks():
+def test_tp_collectives_two_gloo_ranks(tmp_path):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     world = 2
-    port = _free_port()
-    procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, queue)) for r in range(world)]
+    init_file = str(tmp_path / "rendezvous")  # file rendezvous: no TCP port to race for
+    procs = [ctx.Process(target=_gloo_worker, args=(r, world, init_file, queue)) for r in range(world)]
     for proc in procs:
         proc.start()
     results = [queue.get(timeout=120) for _ in range(world)]
