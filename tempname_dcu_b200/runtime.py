@@ -213,13 +213,13 @@ class FluxB200:
     # ------------------------------------------------------------------ call
     def _check(self, input_, weight):
         import torch
+        if self.failed or self.context.failed or self.context.closed:
+            raise RuntimeError("this operator/context previously failed or was closed and cannot be reused")
         wshape = (self.k, self.n) if self.b_mn else (self.n, self.k)
         for label, value, shape in (("input", input_, (self.m, self.k)), ("weight", weight, wshape)):
             if (tuple(value.shape) != shape or value.dtype != torch.bfloat16 or not value.is_cuda
                     or not value.is_contiguous()):
                 raise ValueError(f"{label} must be contiguous BF16 {shape} on the current device")
-        if self.failed or self.context.failed or self.context.closed:
-            raise RuntimeError("this operator/context previously failed or was closed and cannot be reused")
 
     def forward(self, input_, weight, bias=None, residual=None, out=None):
         import torch

@@ -45,10 +45,12 @@ def tensor_sha(tensor):
 
 
 def require_all(ok, message, group):
-    """Rank-coordinated gate: MIN all-reduce of the local verdict."""
+    """Rank-coordinated gate: MIN all-reduce of the local verdict (on the GPU
+    for NCCL groups, on the host for gloo)."""
     import torch
     import torch.distributed as dist
-    flag = torch.tensor(int(bool(ok)), dtype=torch.int32, device="cuda")
+    device = "cuda" if dist.is_initialized() and str(dist.get_backend(group)) == "nccl" else "cpu"
+    flag = torch.tensor(int(bool(ok)), dtype=torch.int32, device=device)
     if dist.is_initialized():
         dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
     if int(flag.item()) != 1:
