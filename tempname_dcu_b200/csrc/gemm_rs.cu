@@ -152,21 +152,23 @@ __device__ __forceinline__ void encode_group_thread(float (&x)[128], uint32_t (&
 
 template <int BN>
 struct PushEpi {
-  // Per epilogue warp: a 32-row x BN-column BF16 slab (also holds the TACO
-  // payload bytes of those rows), XOR-swizzled in 16-byte chunks so that
-  // both the row-per-lane writes and the row-contiguous reads are
-  // conflict-free.
-  static constexpr int kRowBytes = BN * 2;
-  static constexpr int kChunks = kRowBytes / 16;  // 16-byte chunks per row
+  // Per epilogue warp: a 32-row x 128-column BF16 slab (or the TACO payload
+  // of those rows), XOR-swizzled in 16-byte chunks so that both the
+  // row-per-lane writes and the row-contiguous reads are conflict-free.  A
+  // tile row is pushed in 128-column halves as soon as a half is complete,
+  // which halves the staging and leaves room for a deeper TMA ring.
+  static constexpr int kHalf = 128;
+  static constexpr int kRowBytes = kHalf * 2;
+  static constexpr int kChunks = kRowBytes / 16;  // 16-byte chunks per staged row
   static constexpr int kSmemBytes = 4 * 32 * kRowBytes;
   const Params* p;
   int* status;
   uint8_t* stage_base;
-  int within, dest, row0;
+  int within, dest, row0, quarter, nbase;
   bool quant;
   uint8_t* slot;
   float grp[128];
-  float qs[BN / 128], as_[BN / 128];
+  float q_half, a_half;
 
   __device__ __forceinline__ void set_smem(uint8_t* ptr) { stage_base = ptr; }
 
@@ -180,7 +182,7 @@ struct PushEpi {
 
   __device__ __forceinline__ static int swz(int row, int chunk) { return chunk ^ (row & (kChunks - 1)); }
 
-  __device__ __forceinline__ void tile_begin(int mb, int /*nb*/) {
+  __device__ __forceinline__ void tile_begin(int mb, int nb) {
     const int m0 = mb * BM;
     const int physical = m0 / p->chunk_rows;
     dest = physical / p->per;
@@ -188,59 +190,21 @@ struct PushEpi {
     row0 = m0 - physical * p->chunk_rows;
     quant = p->qmask[physical] != 0 && dest != p->rank;
     slot = slot_ptr(*p, dest, p->rank, within);
+    quarter = (threadIdx.x >> 5) & 3;
+    nbase = nb * BN;
   }
 
-  __device__ __forceinline__ void chunk(int /*row*/, int /*col*/, int c, const uint32_t (&r)[32]) {
+  // Copy this warp's staged 32 rows x 128 columns (or their TACO payload and
+  // scales) into the destination slot.
+  __device__ __forceinline__ void push_half(int half) {
     const int lane = threadIdx.x & 31;
-    uint4* srow = reinterpret_cast<uint4*>(stage() + lane * kRowBytes);
-    if (!quant) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint4 w;
-        w.x = pack_bf16x2(__uint_as_float(r[8 * i + 0]), __uint_as_float(r[8 * i + 1]));
-        w.y = pack_bf16x2(__uint_as_float(r[8 * i + 2]), __uint_as_float(r[8 * i + 3]));
-        w.z = pack_bf16x2(__uint_as_float(r[8 * i + 4]), __uint_as_float(r[8 * i + 5]));
-        w.w = pack_bf16x2(__uint_as_float(r[8 * i + 6]), __uint_as_float(r[8 * i + 7]));
-        srow[swz(lane, c * 4 + i)] = w;
-      }
-      return;
-    }
-    // TACO: gather the 128-column group (4 chunks) in registers, BF16 rounded.
-    // The chunk index is a runtime value (the epilogue loop is not unrolled),
-    // so dispatch to a compile-time register offset.
-    switch (c & 3) {
-      case 0: stash<0>(r); break;
-      case 1: stash<1>(r); break;
-      case 2: stash<2>(r); break;
-      default: stash<3>(r); break;
-    }
-    if ((c & 3) == 3) {
-      uint32_t words[32];
-      float q, a;
-      encode_group_thread(grp, words, q, a);
-      const int gi = c >> 2;  // group index inside the tile row
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        srow[swz(lane, gi * 8 + i)] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
-      if (gi == 0) {
-        qs[0] = q;
-        as_[0] = a;
-      } else if (BN / 128 > 1) {
-        qs[BN / 128 - 1] = q;
-        as_[BN / 128 - 1] = a;
-      }
-    }
-  }
-
-  __device__ __forceinline__ void tile_end(int mb, int nb, int quarter, int lane) {
-    __syncwarp();
     const int N = p->N;
-    const int n0 = nb * BN;
+    const int n0 = nbase + half * kHalf;
     const int rib0 = row0 + quarter * 32;  // first block row of this warp
     const uint8_t* st = stage();
+    __syncwarp();
     if (!quant) {
-      // bf16: each row is kRowBytes contiguous in the destination
-      constexpr int kRowsPerIter = 32 / kChunks;  // 1 (BN=256) or 2 (BN=128)
+      constexpr int kRowsPerIter = 32 / kChunks;  // 2 rows of 256 bytes per warp store
 #pragma unroll 4
       for (int j = 0; j < 32; j += kRowsPerIter) {
         const int rr = j + lane / kChunks, ch = lane % kChunks;
@@ -249,9 +213,8 @@ struct PushEpi {
         reinterpret_cast<uint4*>(dst)[ch] = v;
       }
     } else {
-      // TACO payload: BN bytes per row (BN/128 groups of 128 codes)
-      constexpr int kPayChunks = BN / 16;
-      constexpr int kRowsPerIter = 32 / kPayChunks;  // 2 (BN=256) or 4 (BN=128)
+      constexpr int kPayChunks = kHalf / 16;       // 128 payload bytes per row
+      constexpr int kRowsPerIter = 32 / kPayChunks;  // 4 rows per warp store
 #pragma unroll 4
       for (int j = 0; j < 32; j += kRowsPerIter) {
         const int rr = j + lane / kPayChunks, ch = lane % kPayChunks;
@@ -263,14 +226,49 @@ struct PushEpi {
       const int64_t groups = elements / 128;
       const int64_t g0 = (int64_t(rib0 + lane) * N + n0) / 128;
       float* scales = reinterpret_cast<float*>(slot + elements);
+      scales[g0] = q_half;
+      scales[groups + g0] = a_half;
+    }
+    __syncwarp();  // the next half may overwrite the staging
+  }
+
+  __device__ __forceinline__ void chunk(int /*row*/, int /*col*/, int c, const uint32_t (&r)[32]) {
+    const int lane = threadIdx.x & 31;
+    const int cl = c & 3;  // 32-column chunk inside the current 128-column half
+    uint4* srow = reinterpret_cast<uint4*>(stage() + lane * kRowBytes);
+    if (!quant) {
 #pragma unroll
-      for (int t = 0; t < BN / 128; ++t) {
-        scales[g0 + t] = qs[t];
-        scales[groups + g0 + t] = as_[t];
+      for (int i = 0; i < 4; ++i) {
+        uint4 w;
+        w.x = pack_bf16x2(__uint_as_float(r[8 * i + 0]), __uint_as_float(r[8 * i + 1]));
+        w.y = pack_bf16x2(__uint_as_float(r[8 * i + 2]), __uint_as_float(r[8 * i + 3]));
+        w.z = pack_bf16x2(__uint_as_float(r[8 * i + 4]), __uint_as_float(r[8 * i + 5]));
+        w.w = pack_bf16x2(__uint_as_float(r[8 * i + 6]), __uint_as_float(r[8 * i + 7]));
+        srow[swz(lane, cl * 4 + i)] = w;
+      }
+    } else {
+      // TACO: gather the 128-column group (4 chunks) in registers, BF16
+      // rounded; the chunk index is a runtime value (the epilogue loop is not
+      // unrolled), so dispatch to a compile-time register offset.
+      switch (cl) {
+        case 0: stash<0>(r); break;
+        case 1: stash<1>(r); break;
+        case 2: stash<2>(r); break;
+        default: stash<3>(r); break;
+      }
+      if (cl == 3) {
+        uint32_t words[32];
+        encode_group_thread(grp, words, q_half, a_half);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          srow[swz(lane, i)] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
       }
     }
+    if (cl == 3) push_half(c >> 2);
+  }
+
+  __device__ __forceinline__ void tile_end(int, int, int, int) {
     // Signals are issued once per CTA after the produce phase (signal_tiles).
-    __syncwarp();
   }
 };
 
@@ -557,11 +555,10 @@ __device__ void consume_phase(const Params& p, int* status) {
   }
 }
 
-// Shared memory: STAGES x (A + B tile) + the 4 x 32 x BN staging of PushEpi.
-// 128-wide tiles keep six stages in flight (latency of the TMA loads covered),
-// 256-wide tiles fit three.
+// Shared memory: STAGES x (A + B tile) + the 4 x 32 x 128 staging of PushEpi:
+// six stages of 128-wide tiles or four of 256-wide tiles.
 template <int BN>
-constexpr int kStagesFor = BN == 128 ? 6 : 3;
+constexpr int kStagesFor = BN == 128 ? 6 : 4;
 
 template <int BN, bool B_MN>
 __global__ void __launch_bounds__(gemm::kThreads, 1)
