@@ -1,0 +1,344 @@
+// All-gather fused into the tcgen05 GEMM: out = epilogue(AG(x) @ B^T).
+//
+// Reference parity: python/flux_dcu/model.py:110-126 (ColumnLinear: gather
+// the sequence-parallel rows, then a local GEMM with the weight shard) and the
+// row-parallel backward (:139-141: gather the output gradient, then the data
+// gradient GEMM).  The reference runs an NCCL all_gather and then torch.mm;
+// here ONE persistent kernel does both:
+//
+//   * the epilogue warps of every CTA first pull the gathered rows: work
+//     items (source rank, 128-row block, slice) in the order the GEMM consumes
+//     them -- this rank's rows first, then rank+1, rank+2, ... -- each copied
+//     with 16-byte loads from the source's symmetric send slot (own rows from
+//     the local slot) into the gathered output buffer; after an item the CTA
+//     release-adds the block's counter (gpu scope);
+//   * the TMA producer waits (bounded) for the counter of a tile's A rows,
+//     issues `fence.proxy.async.global` and loads them with TMA -- so the
+//     local tiles start at once and remote tiles follow their blocks' arrival
+//     while later blocks are still crossing NVLink;
+//   * the MMA warp and the TMA-store epilogue are the plain GEMM's.
+// The copy waits on other CTAs of the same grid, so the kernel is launched
+// cooperatively (all CTAs co-resident or no launch).  Peer readiness uses the
+// all-gather protocol of allgather.cu (epoch published per source; slot
+// parity and epochs on the device).  The gathered rows stay in the output
+// buffer (the weight gradient reads them in the backward).  No TMA multicast.
+#include <cmath>
+#include <type_traits>
+
+#include "gemm.cuh"
+#include "gemm2.cuh"
+#include "gemm_epi.cuh"
+#include "tensor_map.h"
+
+namespace tdb {
+namespace aggemm {
+
+using gemm::BM;
+using gemm::EpiParams;
+using gemm::TileOrder;
+
+constexpr uint64_t kFlagsBytes = 256;  // same region layout as allgather.cu
+
+struct Pull {
+  const uint64_t* peers;
+  uint64_t heap_off;
+  const uint32_t* state;  // {epoch, parity} advanced before the call
+  int W, rank;
+  int64_t rows, cols;     // per-rank block [rows, cols]
+  uint16_t* full;         // gathered rows [W * rows, cols]
+  uint32_t* ready;        // per 128-row block of `full`
+  int slices;             // items per 128-row block
+  uint64_t wait_ns;
+};
+
+__device__ __forceinline__ const uint16_t* src_slot(const Pull& a, int r, uint32_t parity) {
+  return reinterpret_cast<const uint16_t*>(a.peers[r] + a.heap_off + kFlagsBytes +
+                                           uint64_t(parity) * a.rows * a.cols * 2);
+}
+
+__device__ __forceinline__ void named_sync_epilogue() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void st_release_sys(uint32_t* addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu(uint32_t* addr, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+// Executed by the 128 epilogue threads of every CTA before their first tile.
+__device__ void pull_rows(const Pull& a, int* status) {
+  __shared__ int s_ok;
+  const int et = int(threadIdx.x) - 64;  // epilogue warps are 2..5
+  const uint32_t epoch = __ldg(a.state), parity = __ldg(a.state + 1);
+  if (blockIdx.x == 0 && et == 0) {
+    __threadfence_system();  // the staged rows (previous kernel) before the publish
+    for (int r = 0; r < a.W; ++r)
+      if (r != a.rank) st_release_sys(reinterpret_cast<uint32_t*>(a.peers[r] + a.heap_off) + a.rank, epoch);
+  }
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(a.peers[a.rank] + a.heap_off);
+  const int nblk = int(a.rows / 128);
+  const int rows_per_item = 128 / a.slices;
+  const int64_t vec_per_row = a.cols / 8;
+  const int64_t n = int64_t(rows_per_item) * vec_per_row;  // 16-byte vectors per item
+  const int items = a.W * nblk * a.slices;
+  int checked = -1;  // last source whose publish this CTA has seen
+  for (int w = blockIdx.x; w < items; w += gridDim.x) {
+    const int k = w / (nblk * a.slices);
+    const int s = (a.rank + k) % a.W;
+    const int b = (w / a.slices) % nblk, j = w % a.slices;
+    if (s != a.rank && s != checked) {
+      if (et == 0) {
+        s_ok = 1;
+        if (ld_acquire_sys(flags + s) < epoch) {
+          const uint64_t t0 = globaltimer();
+          while (ld_acquire_sys(flags + s) < epoch) {
+            if (globaltimer() - t0 > a.wait_ns) {
+              record_status(status, kTimeoutPeerFlag, 310, s, int(epoch));
+              s_ok = 0;
+              break;
+            }
+          }
+        }
+      }
+      named_sync_epilogue();
+      if (!s_ok) return;
+      checked = s;
+    }
+    const int64_t r0 = int64_t(b) * 128 + int64_t(j) * rows_per_item;  // row inside the source block
+    const uint4* src = reinterpret_cast<const uint4*>(src_slot(a, s, parity) + r0 * a.cols);
+    uint4* dst = reinterpret_cast<uint4*>(a.full + (int64_t(s) * a.rows + r0) * a.cols);
+    int64_t i = et;
+    for (; i + 3 * 128 < n; i += 4 * 128) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = src[i + u * 128];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) dst[i + u * 128] = v[u];
+    }
+    for (; i < n; i += 128) dst[i] = src[i];
+    named_sync_epilogue();
+    if (et == 0) {
+      __threadfence();
+      red_release_gpu(a.ready + s * nblk + b, 1u);
+    }
+  }
+}
+
+template <class Inner>
+struct PullEpi {
+  const EpiParams& p;
+  const Pull& a;
+  Inner inner;
+  static constexpr int kSmemBytes = Inner::kSmemBytes;
+  __device__ __forceinline__ PullEpi(const EpiParams& ep, const Pull& pull) : p(ep), a(pull), inner{ep} {}
+  __device__ __forceinline__ void set_smem(uint8_t* s) { inner.set_smem(s); }
+  __device__ __forceinline__ void prologue(int* status) { pull_rows(a, status); }
+  __device__ __forceinline__ void tile_begin(int mb, int nb) { inner.tile_begin(mb, nb); }
+  __device__ __forceinline__ void chunk(int row, int col, int c, const uint32_t (&r)[32]) { inner.chunk(row, col, c, r); }
+  __device__ __forceinline__ void tile_end(int mb, int nb, int q, int lane) { inner.tile_end(mb, nb, q, lane); }
+};
+
+template <int BN, bool B_MN, int MODE>
+__global__ void __launch_bounds__(gemm::kThreads, 1)
+    ag_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int K,
+                   TileOrder order, const __grid_constant__ EpiParams ep, const __grid_constant__ Pull pull,
+                   int* status) {
+  using Inner = typename gemm::EpiFor<MODE>::type;
+  PullEpi<Inner> epi(ep, pull);
+  gemm::gemm_mainloop<BN, false, B_MN>(&tmA, &tmB, K, order, epi, status);
+}
+
+constexpr int k2Stages = 6;
+
+template <bool B_MN, int MODE>
+__global__ void __launch_bounds__(gemm2::kThreads, 1)
+    ag_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int K,
+                    TileOrder order, const __grid_constant__ EpiParams ep, const __grid_constant__ Pull pull,
+                    int* status) {
+  using Inner = typename gemm::EpiFor<MODE>::type;
+  using Epi = PullEpi<Inner>;
+  Epi epi(ep, pull);
+  gemm2::mainloop<false, B_MN, Epi, k2Stages>(&tmA, &tmB, K, order, epi, status);
+}
+
+template <class Kern>
+static int launch_coop(Kern kern, dim3 grid, int threads, int smem, int cluster, cudaStream_t s, const CUtensorMap& ta,
+                       const CUtensorMap& tb, int K, const TileOrder& order, const EpiParams& ep, const Pull& pull,
+                       int* status) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeCooperative;
+  attr[na].val.cooperative = 1;
+  ++na;
+  if (cluster > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, K, order, ep, pull, status);
+  tdb_host::launched(1);
+  if (e != cudaSuccess) return tdb_host::fail(int(e), "ag_gemm: cooperative launch failed: %s", cudaGetErrorString(e));
+  return 0;
+}
+
+template <int BN, bool B_MN, int MODE>
+static int launch1(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, TileOrder order,
+                   const EpiParams& ep, const Pull& pull, cudaStream_t s) {
+  using Cfg = gemm::Config<BN>;
+  constexpr int kSmem = Cfg::kSmemBytes + gemm::EpiFor<MODE>::type::kSmemBytes;
+  auto kern = ag_gemm_kernel<BN, B_MN, MODE>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return tdb_host::fail(int(e), "ag_gemm: smem attribute");
+    attr[dev & 63] = true;
+  }
+  order.num_m = (M + BM - 1) / BM;
+  order.num_n = (N + BN - 1) / BN;
+  order.num_tiles = order.num_m * order.num_n;
+  const int grid = order.num_tiles < tdb_host::sm_count() ? order.num_tiles : tdb_host::sm_count();
+  return launch_coop(kern, dim3(grid), gemm::kThreads, kSmem, 1, s, ta, tb, K, order, ep, pull,
+                     tdb_host::status_ptr());
+}
+
+template <bool B_MN, int MODE>
+static int launch2(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, TileOrder order,
+                   const EpiParams& ep, const Pull& pull, cudaStream_t s) {
+  using Cfg = gemm2::Config<k2Stages>;
+  constexpr int kSmem = Cfg::kSmemBytes + gemm::EpiFor<MODE>::type::kSmemBytes;
+  auto kern = ag_gemm2_kernel<B_MN, MODE>;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return tdb_host::fail(int(e), "ag_gemm2: smem attribute");
+    attr[dev & 63] = true;
+  }
+  order.num_m = (M + 255) / 256;
+  order.num_n = (N + 255) / 256;
+  order.num_tiles = order.num_m * order.num_n;
+  const int pairs = tdb_host::sm_count() / 2;
+  const int clusters = order.num_tiles < pairs ? order.num_tiles : pairs;
+  return launch_coop(kern, dim3(2 * clusters), gemm2::kThreads, kSmem, 2, s, ta, tb, K, order, ep, pull,
+                     tdb_host::status_ptr());
+}
+
+template <bool B_MN, int MODE>
+static int dispatch_tile(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                         const TileOrder& order, const EpiParams& ep, const Pull& pull, cudaStream_t s) {
+  switch (bn) {
+    case 512: return launch2<B_MN, MODE>(ta, tb, M, N, K, order, ep, pull, s);
+    case 256: return launch1<256, B_MN, MODE>(ta, tb, M, N, K, order, ep, pull, s);
+    case 192: return launch1<192, B_MN, MODE>(ta, tb, M, N, K, order, ep, pull, s);
+    default: return launch1<128, B_MN, MODE>(ta, tb, M, N, K, order, ep, pull, s);
+  }
+}
+
+template <bool B_MN>
+static int dispatch_mode(int mode, int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                         const TileOrder& order, const EpiParams& ep, const Pull& pull, cudaStream_t s) {
+  using namespace gemm;
+  switch (mode) {
+    case kStore: return dispatch_tile<B_MN, kTmaBase + kStore>(bn, ta, tb, M, N, K, order, ep, pull, s);
+    case kBias: return dispatch_tile<B_MN, kTmaBase + kBias>(bn, ta, tb, M, N, K, order, ep, pull, s);
+    case kBiasGelu: return dispatch_tile<B_MN, kTmaBase + kBiasGelu>(bn, ta, tb, M, N, K, order, ep, pull, s);
+    case kGeluBwd: return dispatch_tile<B_MN, kTmaBase + kGeluBwd>(bn, ta, tb, M, N, K, order, ep, pull, s);
+  }
+  return tdb_host::fail(int(cudaErrorInvalidValue), "ag_gemm: mode %d unsupported (0-3)", mode);
+}
+
+}  // namespace aggemm
+namespace gemm {
+int make_operand_map(CUtensorMap* map, const void* ptr, bool mn_major, int mn, int K, int64_t ld, int tile_mn);
+int pick_tile(int M, int N, int K, int sms);
+}  // namespace gemm
+}  // namespace tdb
+
+TDB_API int tdb_ag_prepare(const void* x, long long ldx, long long rows, long long cols,
+                           const unsigned long long* peers, int W, int rank, unsigned long long heap_off,
+                           unsigned int* state, void* stream);
+
+// C = epilogue(AG(x) @ B^T) with the all-gather fused (see the header).
+//   x: this rank's rows [rows, K] (row stride ldx); full: [W*rows, K] output of
+//   the gathered rows; B: [N, K] or [K, N] (b_mn); C: [W*rows, N] bf16.
+//   peers / heap_off / state: an all-gather region (tdb_ag_region_bytes);
+//   ready: uint32 [W*rows/128] zero-initialised counters owned by this call site;
+//   tile_table: [tiles] production order (this rank's rows first) for tile code bn.
+// mode: 0 store (alpha), 1 bias, 2 bias + GELU (aux_out = pre-activation), 3 GELU backward (aux).
+TDB_API int tdb_ag_gemm(const void* x, long long ldx, void* full, long long rows, int K, const void* B, int b_mn,
+                        long long ldb, void* C, long long ldc, int N, int mode, const void* bias, const void* aux,
+                        long long ld_aux, void* aux_out, float alpha, int bn, const int* tile_table,
+                        const unsigned long long* peers, int W, int rank, unsigned long long heap_off,
+                        unsigned int* state, unsigned int* ready, double wait_seconds, void* stream) {
+  using namespace tdb;
+  using namespace tdb::gemm;
+  const long long M = rows * W;
+  if (!x || !full || !B || !C || !tile_table || !peers || !state || !ready || W < 2 || W > 64 || rank < 0 ||
+      rank >= W || rows % 256 || K % 64 || N % 8 || ldc % 8 || ldx % 8 || ldb % 8 ||
+      (mode >= 2 && ld_aux % 8) || ((reinterpret_cast<uintptr_t>(C) | reinterpret_cast<uintptr_t>(full) |
+                                     reinterpret_cast<uintptr_t>(x)) % 16))
+    return tdb_host::fail(int(cudaErrorInvalidValue), "ag_gemm: bad arguments (rows %% 256, K %% 64, 16-byte rows)");
+  if (bn != 128 && bn != 192 && bn != 256 && bn != 512)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "ag_gemm: bn must be 128, 192, 256 or 512");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = tdb_ag_prepare(x, ldx, rows, K, peers, W, rank, heap_off, state, stream);
+  if (rc) return rc;
+  CUtensorMap ta, tb;
+  if ((rc = make_operand_map(&ta, full, false, int(M), K, K, BM))) return rc;
+  if ((rc = make_operand_map(&tb, B, b_mn != 0, N, K, ldb, bn == 512 ? 128 : bn))) return rc;
+  EpiParams ep;
+  ep.C = C;
+  ep.ldc = ldc;
+  ep.M = int(M);
+  ep.N = N;
+  ep.bias = static_cast<const uint16_t*>(bias);
+  ep.aux = static_cast<const uint16_t*>(aux);
+  ep.ld_aux = ld_aux;
+  ep.aux_out = static_cast<uint16_t*>(aux_out);
+  ep.alpha = alpha;
+  ep.beta = 0.f;
+  if ((rc = tdb_host::make_tmap_2d(&ep.tmC, C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(N), uint64_t(M),
+                                   uint64_t(ldc), 64, 32, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if (mode == kBiasGelu &&
+      (rc = tdb_host::make_tmap_2d(&ep.tmAux, aux_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(N), uint64_t(M),
+                                   uint64_t(ld_aux), 64, 32, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  aggemm::Pull pull;
+  pull.peers = reinterpret_cast<const uint64_t*>(peers);
+  pull.heap_off = heap_off;
+  pull.state = state;
+  pull.W = W;
+  pull.rank = rank;
+  pull.rows = rows;
+  pull.cols = K;
+  pull.full = static_cast<uint16_t*>(full);
+  pull.ready = ready;
+  pull.slices = 16;
+  pull.wait_ns = uint64_t(wait_seconds * 1e9);
+  TileOrder order;
+  order.group_m = 1;
+  order.table = tile_table;
+  order.gate_ready = ready;
+  order.gate_epoch = state;
+  order.gate_per_call = uint32_t(pull.slices);
+  return b_mn ? aggemm::dispatch_mode<true>(mode, bn, ta, tb, int(M), N, K, order, ep, pull, s)
+              : aggemm::dispatch_mode<false>(mode, bn, ta, tb, int(M), N, K, order, ep, pull, s);
+}

@@ -124,6 +124,35 @@ TDB_API long long tdb_ag_region_bytes(long long rows, long long cols) {
   return (long long)(tdb::ag::kFlagsBytes + 2ull * uint64_t(rows) * uint64_t(cols) * 2ull);
 }
 
+// Advance the region's epoch and stage this rank's rows into its send slot
+// (the first two steps of a gather; the fused all-gather GEMM pulls itself).
+TDB_API int tdb_ag_prepare(const void* x, long long ldx, long long rows, long long cols,
+                           const unsigned long long* peers, int W, int rank, unsigned long long heap_off,
+                           unsigned int* state, void* stream) {
+  if (!x || !peers || !state || W < 2 || W > 64 || rank < 0 || rank >= W || rows <= 0 || cols <= 0 || cols % 8 ||
+      ldx % 8 || heap_off % 16 || reinterpret_cast<uintptr_t>(x) % 16)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "ag_prepare: bad arguments");
+  using namespace tdb::ag;
+  Params p;
+  p.peers = reinterpret_cast<const uint64_t*>(peers);
+  p.state = state;
+  p.W = W;
+  p.rank = rank;
+  p.rows = rows;
+  p.cols = cols;
+  p.heap_off = heap_off;
+  p.out = nullptr;
+  p.wait_ns = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int sms = tdb_host::sm_count();
+  ag_advance_kernel<<<1, 1, 0, s>>>(state);
+  const int64_t vec = rows * cols / 8;
+  const int stage_grid = int(vec / kThreads + 1 < 2 * sms ? vec / kThreads + 1 : 2 * sms);
+  ag_stage_kernel<<<stage_grid, kThreads, 0, s>>>(static_cast<const uint16_t*>(x), ldx, p);
+  tdb_host::launched(2);
+  return int(cudaGetLastError());
+}
+
 // out [W*rows, cols] = concat over ranks of every rank's x [rows, cols]
 // (row stride ldx).  peers: [W] heap bases; heap_off: this gather's region
 // (tdb_ag_region_bytes, zeroed once); state: device uint32 {epoch, parity}

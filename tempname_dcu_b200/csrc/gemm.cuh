@@ -46,6 +46,12 @@ struct TileOrder {
   int group_m;
   const int* table;  // optional: table[i] = m_blk * num_n + n_blk
   int num_tiles;
+  // Optional gate on the A rows (the all-gather fused into the GEMM): before
+  // loading the A rows of a tile, the producer waits until the counter of
+  // their 128-row block reaches (*gate_epoch) * gate_per_call.
+  const uint32_t* gate_ready = nullptr;
+  const uint32_t* gate_epoch = nullptr;
+  uint32_t gate_per_call = 0;
 
   __device__ __forceinline__ void tile(int i, int& m_blk, int& n_blk) const {
     if (table) {
@@ -63,6 +69,31 @@ struct TileOrder {
     n_blk = r / gsize;
   }
 };
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// Wait (bounded) until the A rows of 128-row block `blk` are in place, then
+// order those generic-proxy writes before this thread's TMA (async-proxy)
+// reads.  Returns false on timeout (status recorded).
+__device__ __forceinline__ bool gate_wait(const TileOrder& order, int blk, int* status) {
+  const uint32_t target = __ldg(order.gate_epoch) * order.gate_per_call;
+  const uint32_t* ctr = order.gate_ready + blk;
+  if (int32_t(ld_acquire_gpu_u32(ctr) - target) < 0) {
+    const uint64_t t0 = globaltimer();
+    while (int32_t(ld_acquire_gpu_u32(ctr) - target) < 0) {
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        record_status(status, kTimeoutLocal, 40, blk, int(target));
+        return false;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
 
 struct alignas(8) Barriers {
   uint64_t full[8];
@@ -136,6 +167,7 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
         int mb, nb;
         order.tile(i, mb, nb);
         const int m0 = mb * BM, n0 = nb * BN;
+        if (order.gate_ready && !gate_wait(order, m0 / 128, status)) { ok = false; *abort_flag = 1; break; }
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t round = it / S;
@@ -207,6 +239,7 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
   } else {
     // ---------------- Epilogue (warps 2..5) ----------------
     epi.set_smem(reinterpret_cast<uint8_t*>(bars) + 256);
+    epi.prologue(status);  // work before the first tile (e.g. the fused all-gather pull)
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
     const int row_in_tile = quarter * 32 + lane;
     int tc = 0;

@@ -171,6 +171,7 @@ __device__ __forceinline__ void mainloop(const CUtensorMap* tmA, const CUtensorM
         int mt, nt;
         order.tile(i, mt, nt);
         const int m0 = mt * 256 + rank * kHalf, n0 = nt * kTileN + rank * kHalf;
+        if (order.gate_ready && !gemm::gate_wait(order, m0 / 128, status)) { ok = false; *abort_flag = 1; break; }
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t round = it / S;
@@ -238,6 +239,7 @@ __device__ __forceinline__ void mainloop(const CUtensorMap* tmA, const CUtensorM
     }
   } else {
     epi.set_smem(reinterpret_cast<uint8_t*>(bars) + 256);
+    epi.prologue(status);
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
     int tc = 0;

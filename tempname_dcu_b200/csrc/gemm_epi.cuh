@@ -69,6 +69,7 @@ struct PlainEpi {
 
   static constexpr int kSmemBytes = 0;
   __device__ __forceinline__ void set_smem(uint8_t*) {}
+  __device__ __forceinline__ void prologue(int*) {}
   __device__ __forceinline__ void tile_begin(int, int) {}
   __device__ __forceinline__ void tile_end(int, int, int, int) {}
 
@@ -173,6 +174,7 @@ struct AccF32TmaEpi {
     const uint32_t a = smem_u32(s);
     base = ((a + 1023u) & ~1023u) + uint32_t(((threadIdx.x >> 5) & 3) * 2 * kBuf);
   }
+  __device__ __forceinline__ void prologue(int*) {}
   __device__ __forceinline__ void tile_begin(int, int) {}
   __device__ __forceinline__ void tile_end(int, int, int, int) {}
   // Every bulk operation this thread issued has completed (its shared-memory
@@ -230,6 +232,7 @@ struct TmaBf16Epi {
     const uint32_t a = smem_u32(s);
     base = ((a + 1023u) & ~1023u) + uint32_t(((threadIdx.x >> 5) & 3) * 2 * kBuf);
   }
+  __device__ __forceinline__ void prologue(int*) {}
   __device__ __forceinline__ void tile_begin(int, int) {}
   __device__ __forceinline__ void tile_end(int, int, int, int) {}
   __device__ __forceinline__ ~TmaBf16Epi() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }

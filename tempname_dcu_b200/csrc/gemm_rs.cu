@@ -171,6 +171,7 @@ struct PushEpi {
   float q_half, a_half;
 
   __device__ __forceinline__ void set_smem(uint8_t* ptr) { stage_base = ptr; }
+  __device__ __forceinline__ void prologue(int*) {}
 
   template <int Q>
   __device__ __forceinline__ void stash(const uint32_t (&r)[32]) {

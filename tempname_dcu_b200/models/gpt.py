@@ -102,9 +102,14 @@ class GPT:
         # (dX = RS(dY W)) run through the same fused kernel (BF16, ordered)
         # whenever the forward projections do.
         self._bwd_rs = {}
+        self.agg = None
         if factory is not None and self.world > 1:
             # sequence-parallel all-gathers over NVLink (same rows/cols everywhere)
             self.tp.enable_symmetric_gather(self.ml, self.h)
+            if self.ml % 256 == 0:
+                # ... and, where a GEMM consumes the gathered rows, fused into it
+                from ..parallel.allgather import SymmAgGemm
+                self.agg = SymmAgGemm(self.tp, self.ml, self.h)
             from ..runtime import FluxB200
             for k in (3 * self.h // self.world, self.f // self.world, self.vocab_local):
                 if k not in self._bwd_rs:
@@ -155,13 +160,20 @@ class GPT:
         c, p = self.config, f"layers.{i}."
         eps = c["layer_norm_epsilon"]
         ln1, mean1, rstd1 = K.layernorm_fwd(x, self.P(p + "ln1_weight"), self.P(p + "ln1_bias"), eps)
-        ln1f = self.tp.gather(ln1)
-        qkv = G.linear(ln1f, self.P(p + "qkv_weight"), self.P(p + "qkv_bias"))
+        if self.agg is not None:
+            qkv, ln1f = self.agg(ln1, self.P(p + "qkv_weight"), mode=self.agg.BIAS, bias=self.P(p + "qkv_bias"))
+        else:
+            ln1f = self.tp.gather(ln1)
+            qkv = G.linear(ln1f, self.P(p + "qkv_weight"), self.P(p + "qkv_bias"))
         attn, lse = K.attention_fwd(qkv, c["micro_batch"], c["sequence"], self.heads_local)
         x1 = self.operators[2 * i].forward(attn, self.P(p + "attn_weight"), self.P(p + "attn_bias"), x)
         ln2, mean2, rstd2 = K.layernorm_fwd(x1, self.P(p + "ln2_weight"), self.P(p + "ln2_bias"), eps)
-        ln2f = self.tp.gather(ln2)
-        h1, z = G.linear_gelu(ln2f, self.P(p + "fc1_weight"), self.P(p + "fc1_bias"))
+        if self.agg is not None:
+            h1, ln2f, z = self.agg(ln2, self.P(p + "fc1_weight"), mode=self.agg.BIAS_GELU,
+                                   bias=self.P(p + "fc1_bias"))
+        else:
+            ln2f = self.tp.gather(ln2)
+            h1, z = G.linear_gelu(ln2f, self.P(p + "fc1_weight"), self.P(p + "fc1_bias"))
         x2 = self.operators[2 * i + 1].forward(h1, self.P(p + "fc2_weight"), self.P(p + "fc2_bias"), x1)
         return x2, (x, mean1, rstd1, ln1f, qkv, attn, lse, x1, mean2, rstd2, ln2f, z, h1)
 
@@ -190,8 +202,11 @@ class GPT:
         xl = x
         eps = c["layer_norm_epsilon"]
         lnf, meanf, rstdf = K.layernorm_fwd(xl, self.P("final_weight"), self.P("final_bias"), eps)
-        lnff = self.tp.gather(lnf)
-        logits = G.linear(lnff, self.P("embedding"))  # [m, V/W]
+        if self.agg is not None:
+            logits, lnff = self.agg(lnf, self.P("embedding"))  # [m, V/W]
+        else:
+            lnff = self.tp.gather(lnf)
+            logits = G.linear(lnff, self.P("embedding"))  # [m, V/W]
         stats = K.xent_stats(logits, targets, self.vocab_start, self.valid_vocab_local)
         all_stats = self.tp.all_gather_stacked(stats)
         gstats = self._buf("gstats", self.m * 2, torch.float32).view(self.m, 2)
@@ -228,8 +243,11 @@ class GPT:
         x, mean1, rstd1, ln1f, qkv, attn, lse, x1, mean2, rstd2, ln2f, z, h1 = saved
         # FC2 (row-parallel): x2 = x1 + RS(h1 W2^T) + b2
         self._colsum(dx2, p + "fc2_bias")
-        dyf = self.tp.gather(dx2)
-        dz = G.matmul_nt(dyf, self.P(p + "fc2_weight"), gelu_pre=z)
+        if self.agg is not None:
+            dz, dyf = self.agg(dx2, self.P(p + "fc2_weight"), b_mn=True, mode=self.agg.GELU_BWD, aux=z)
+        else:
+            dyf = self.tp.gather(dx2)
+            dz = G.matmul_nt(dyf, self.P(p + "fc2_weight"), gelu_pre=z)
         G.weight_grad(dyf, h1, self.Gr(p + "fc2_weight"))
         # FC1 (column-parallel)
         self._colsum(dz, p + "fc1_bias")
@@ -239,8 +257,11 @@ class GPT:
                               self.Gr(p + "ln2_bias"), ln_scratch, dres=dx2)
         # attention out (row-parallel)
         self._colsum(dx1, p + "attn_bias")
-        dyf = self.tp.gather(dx1)
-        dattn = G.matmul_nt(dyf, self.P(p + "attn_weight"))
+        if self.agg is not None:
+            dattn, dyf = self.agg(dx1, self.P(p + "attn_weight"), b_mn=True)
+        else:
+            dyf = self.tp.gather(dx1)
+            dattn = G.matmul_nt(dyf, self.P(p + "attn_weight"))
         G.weight_grad(dyf, attn, self.Gr(p + "attn_weight"))
         dqkv = K.attention_bwd(qkv, attn, dattn, lse, c["micro_batch"], c["sequence"], self.heads_local)
         # QKV (column-parallel)

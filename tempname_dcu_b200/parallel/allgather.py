@@ -54,3 +54,96 @@ class SymmAllGather:
 
     def close(self):
         self.heap.close()
+
+
+native.register("tdb_ag_gemm", [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int,
+                                ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_void_p, ctypes.c_longlong,
+                                ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,
+                                ctypes.c_void_p, ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                ctypes.c_int, ctypes.c_int, ctypes.c_ulonglong, ctypes.c_void_p, ctypes.c_void_p,
+                                ctypes.c_double, ctypes.c_void_p])
+native.register("tdb_gemm_pick_tile", [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int])
+
+
+def ag_tile_table(world, rank, rows, n, bn):
+    """Tile order of the fused all-gather GEMM: this rank's rows first, then
+    rank+1, rank+2, ...; all N tiles of a row block consecutively.  ``bn`` is
+    the GEMM tile code (128/192/256: 128-row tiles of that width; 512: 2-CTA
+    256 x 256 tiles).  Values are ``m_tile * n_tiles + n_tile``."""
+    tm, tn = (256, 256) if bn == 512 else (128, bn)
+    if rows % tm:
+        raise ValueError("rows per rank must be a multiple of the tile height")
+    n_tiles = -(-n // tn)
+    per = rows // tm
+    table = []
+    for k in range(world):
+        s = (rank + k) % world
+        for mb in range(s * per, (s + 1) * per):
+            table.extend(mb * n_tiles + nb for nb in range(n_tiles))
+    return table
+
+
+class SymmAgGemm:
+    """All-gather fused into the tcgen05 GEMM (``csrc/ag_gemm.cu``):
+    ``out, full = agg(x_local, weight, ...)`` computes
+    ``out = epilogue(AG(x_local) @ weight^T)`` (weight [N, K], or [K, N] with
+    ``b_mn``) and returns the gathered rows ``full`` [world * rows, K] too.
+    Every call of an instance gathers the same [rows, K] block shape; creation
+    is collective."""
+
+    STORE, BIAS, BIAS_GELU, GELU_BWD = 0, 1, 2, 3
+
+    def __init__(self, tp, rows, cols):
+        import torch
+        from .symmetric import SymmetricHeap
+        if rows % 256 or cols % 64:
+            raise ValueError("the fused all-gather GEMM needs rows % 256 == 0 and K % 64 == 0")
+        self.tp, self.rows, self.cols = tp, int(rows), int(cols)
+        self.heap = SymmetricHeap(tp, int(native.lib().tdb_ag_region_bytes(self.rows, self.cols)))
+        dev = self.heap.device
+        self.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.ready = torch.zeros(tp.world * self.rows // 128, dtype=torch.int32, device=dev)
+        self.sms = int(native.lib().tdb_sm_count(torch.cuda.current_device()))
+        self.tables = {}
+        self.calls = 0
+
+    def _table(self, n, bn):
+        import torch
+        key = (n, bn)
+        if key not in self.tables:
+            self.tables[key] = torch.tensor(ag_tile_table(self.tp.world, self.tp.rank, self.rows, n, bn),
+                                            dtype=torch.int32, device=self.heap.device)
+        return self.tables[key]
+
+    def __call__(self, x, weight, *, b_mn=False, mode=0, bias=None, aux=None, aux_out=None, alpha=1.0, out=None,
+                 full=None):
+        import torch
+        if (tuple(x.shape) != (self.rows, self.cols) or x.dtype != torch.bfloat16 or x.stride(1) != 1
+                or x.stride(0) % 8):
+            raise ValueError(f"expected bf16 [{self.rows}, {self.cols}] rows")
+        M, K = self.tp.world * self.rows, self.cols
+        N = weight.shape[1] if b_mn else weight.shape[0]
+        if (weight.shape[0] if b_mn else weight.shape[1]) != K:
+            raise ValueError("weight inner dimension does not match the gathered rows")
+        bn = int(native.lib().tdb_gemm_pick_tile(M, N, K, self.sms))
+        if out is None:
+            out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+        if full is None:
+            full = torch.empty((M, K), dtype=torch.bfloat16, device=x.device)
+        if mode == self.BIAS_GELU and aux_out is None:
+            aux_out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+        aux_t = aux_out if mode == self.BIAS_GELU else aux
+        native.check(native.lib().tdb_ag_gemm(
+            x.data_ptr(), x.stride(0), full.data_ptr(), self.rows, K, weight.data_ptr(), int(bool(b_mn)),
+            weight.stride(0), out.data_ptr(), out.stride(0), N, int(mode), 0 if bias is None else bias.data_ptr(),
+            0 if aux is None else aux.data_ptr(), 0 if aux_t is None else aux_t.stride(0),
+            0 if aux_out is None else aux_out.data_ptr(), float(alpha), bn, self._table(N, bn).data_ptr(),
+            self.heap.peers.data_ptr(), self.tp.world, self.tp.rank, 0, self.state.data_ptr(),
+            self.ready.data_ptr(), PEER_WAIT_SECONDS, native.stream_ptr()), "fused all-gather GEMM")
+        self.calls += 1
+        if mode == self.BIAS_GELU:
+            return out, full, aux_out
+        return out, full
+
+    def close(self):
+        self.heap.close()

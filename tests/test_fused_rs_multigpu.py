@@ -112,6 +112,40 @@ def _worker(rank, world, init_file, result_path):
         out["allgather"] = ok
         native.raise_on_status()
         ag.close()
+        # all-gather fused into the GEMM (csrc/ag_gemm.cu) vs NCCL gather + fp32 math
+        from tempname_dcu_b200.parallel.allgather import SymmAgGemm
+        import torch.nn.functional as F
+        rows, K = 512, 1024
+        agg = SymmAgGemm(tp, rows, K)
+        errs, same = [], []
+        def rel(a, b):
+            return float((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30))
+        for N in (1536, 1000):
+            w = (torch.randn(N, K, device="cuda") / 32).to(torch.bfloat16)
+            bias = torch.randn(N, device="cuda").to(torch.bfloat16)
+            for rep in range(2):
+                xl = torch.randn(rows, K, device="cuda").to(torch.bfloat16)
+                ref_full = torch.empty(rows * world, K, dtype=torch.bfloat16, device="cuda")
+                dist.all_gather_into_tensor(ref_full, xl, group=group)
+                y, full = agg(xl, w, mode=agg.BIAS, bias=bias)
+                same.append(bool(torch.equal(full, ref_full)))
+                errs.append(rel(y, ref_full.float() @ w.float().t() + bias.float()))
+                act, full2, pre = agg(xl, w, mode=agg.BIAS_GELU, bias=bias)
+                zref = ref_full.float() @ w.float().t() + bias.float()
+                errs.append(rel(pre, zref))
+                errs.append(rel(act, F.gelu(pre.float())))
+                wt = (torch.randn(K, N, device="cuda") / 32).to(torch.bfloat16)   # [K, N] storage (b_mn)
+                zz = torch.randn(rows * world, N, device="cuda").to(torch.bfloat16)
+                dz, _ = agg(xl, wt, b_mn=True, mode=agg.GELU_BWD, aux=zz)
+                zr = zz.float().requires_grad_(True)
+                F.gelu(zr).backward((ref_full.float() @ wt.float()).to(torch.bfloat16).float())
+                errs.append(rel(dz, zr.grad))
+                st, _ = agg(xl, w, mode=agg.STORE)
+                errs.append(rel(st, ref_full.float() @ w.float().t()))
+        torch.cuda.synchronize()
+        native.raise_on_status()
+        out["ag_gemm"] = dict(full_equal=same, max_rel=max(errs))
+        agg.close()
         torch.cuda.synchronize()
         native.raise_on_status()
         shutdown_context(group)
@@ -135,8 +169,9 @@ def test_fused_gemm_rs_all_arms(tmp_path):
     mp.spawn(_worker, args=(world, str(tmp_path / "rendezvous"), path), nprocs=world, join=True)
     res = json.load(open(path))
     assert res.get("allgather") and all(res["allgather"]), res.get("allgather")
+    assert all(res["ag_gemm"]["full_equal"]) and res["ag_gemm"]["max_rel"] < 1e-2, res["ag_gemm"]
     for key, value in res.items():
-        if key == "allgather":
+        if key in ("allgather", "ag_gemm"):
             continue
         if key.startswith("bitwise"):
             assert all(value.values()), (key, value)

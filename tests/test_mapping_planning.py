@@ -270,3 +270,16 @@ def test_remote_first_order_rotates_destinations():
             assert [x["within"] for x in rf if x["destination"] == d] == list(range(per))
         tiles = tiles_for_order(rf, n, chunk, block_m=128, block_n=256)
         assert sorted(tiles) == list(range((m // 128) * (n // 256)))
+
+
+def test_ag_tile_table_local_rows_first():
+    from tempname_dcu_b200.parallel.allgather import ag_tile_table
+    world, rows, n = 4, 512, 1000
+    for bn in (128, 192, 256, 512):
+        tm, tn = (256, 256) if bn == 512 else (128, bn)
+        n_tiles = -(-n // tn)
+        for rank in range(world):
+            t = ag_tile_table(world, rank, rows, n, bn)
+            assert sorted(t) == list(range(world * rows // tm * n_tiles))
+            first_rows = {x // n_tiles * tm for x in t[: rows // tm * n_tiles]}
+            assert all(rank * rows <= r < (rank + 1) * rows for r in first_rows)
