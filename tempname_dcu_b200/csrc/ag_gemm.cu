@@ -223,18 +223,33 @@ static int launch2(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   using Cfg = gemm2::Config<k2Stages>;
   constexpr int kSmem = Cfg::kSmemBytes + gemm::EpiFor<MODE>::type::kSmemBytes;
   auto kern = ag_gemm2_kernel<B_MN, MODE>;
-  static bool attr[64] = {false};
+  static int max_clusters[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr[dev & 63]) {
+  if (!max_clusters[dev & 63]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return tdb_host::fail(int(e), "ag_gemm2: smem attribute");
-    attr[dev & 63] = true;
+    // clusters that can be resident at once (the cooperative launch needs all of them)
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(tdb_host::sm_count());
+    cfg.blockDim = dim3(gemm2::kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess || n <= 0) return tdb_host::fail(int(e), "ag_gemm2: no resident 2-CTA clusters");
+    max_clusters[dev & 63] = n;
   }
   order.num_m = (M + 255) / 256;
   order.num_n = (N + 255) / 256;
   order.num_tiles = order.num_m * order.num_n;
-  const int pairs = tdb_host::sm_count() / 2;
+  const int pairs = max_clusters[dev & 63];
   const int clusters = order.num_tiles < pairs ? order.num_tiles : pairs;
   return launch_coop(kern, dim3(2 * clusters), gemm2::kThreads, kSmem, 2, s, ta, tb, K, order, ep, pull,
                      tdb_host::status_ptr());
