@@ -71,8 +71,9 @@ __device__ __forceinline__ void red_release_gpu(uint32_t* addr, uint32_t v) {
 }
 
 // Executed by the 128 epilogue threads of every CTA before their first tile.
-__device__ void pull_rows(const Pull& a, int* status) {
-  __shared__ int s_ok;
+// `s_ok` is the epilogue scratch word of the mainloop's barrier slot (no static
+// shared memory: the dynamic allocation already uses the per-block maximum).
+__device__ void pull_rows(const Pull& a, volatile int& s_ok, int* status) {
   const int et = int(threadIdx.x) - 64;  // epilogue warps are 2..5
   const uint32_t epoch = __ldg(a.state), parity = __ldg(a.state + 1);
   if (blockIdx.x == 0 && et == 0) {
@@ -136,8 +137,12 @@ struct PullEpi {
   Inner inner;
   static constexpr int kSmemBytes = Inner::kSmemBytes;
   __device__ __forceinline__ PullEpi(const EpiParams& ep, const Pull& pull) : p(ep), a(pull), inner{ep} {}
-  __device__ __forceinline__ void set_smem(uint8_t* s) { inner.set_smem(s); }
-  __device__ __forceinline__ void prologue(int* status) { pull_rows(a, status); }
+  int* scratch = nullptr;
+  __device__ __forceinline__ void set_smem(uint8_t* s) {
+    scratch = reinterpret_cast<int*>(s - 16);
+    inner.set_smem(s);
+  }
+  __device__ __forceinline__ void prologue(int* status) { pull_rows(a, *scratch, status); }
   __device__ __forceinline__ void tile_begin(int mb, int nb) { inner.tile_begin(mb, nb); }
   __device__ __forceinline__ void chunk(int row, int col, int c, const uint32_t (&r)[32]) { inner.chunk(row, col, c, r); }
   __device__ __forceinline__ void tile_end(int mb, int nb, int q, int lane) { inner.tile_end(mb, nb, q, lane); }

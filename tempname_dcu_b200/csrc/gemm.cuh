@@ -104,6 +104,9 @@ struct alignas(8) Barriers {
   uint32_t tmem_base;
   int abort_flag;
 };
+// The barriers sit in a 256-byte slot before the epilogue's shared memory;
+// its last 16 bytes are scratch of the epilogue warps (set_smem pointer - 16).
+static_assert(sizeof(Barriers) <= 240, "barrier slot overlaps the epilogue scratch");
 
 // Descriptor of a K-major SW128 tile: rows of 128 bytes, 8-row atoms of
 // 1024 bytes.  LBO is unused for swizzled K-major operands (encoded as 16).

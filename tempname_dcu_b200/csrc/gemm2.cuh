@@ -117,6 +117,9 @@ struct alignas(8) Barriers {
   int abort_flag;
   uint32_t peer_done;
 };
+// The barriers sit in a 256-byte slot before the epilogue's shared memory;
+// its last 16 bytes are scratch of the epilogue warps (set_smem pointer - 16).
+static_assert(sizeof(Barriers) <= 240, "barrier slot overlaps the epilogue scratch");
 
 // `order` counts 256 x 256 tiles.  Epi receives 128-row block indices
 // (tile_m * 2 + rank) and 256-column tile indices, like the 1-CTA mainloop
