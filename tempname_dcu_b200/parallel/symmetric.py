@@ -8,6 +8,10 @@ the local heap as a torch tensor (for validation and tests).
 
 Creation and ``close()`` are collective: every rank of the group must call
 them in the same order.
+
+A 256-byte canary of 0xA5 bytes follows the usable ``nbytes`` of every heap;
+``canaries_intact()`` checks it (an overrun by any writer -- local or peer --
+shows up there).
 """
 from __future__ import annotations
 
@@ -43,6 +47,10 @@ def alias(ptr, shape, dtype, device):
     return torch.as_tensor(_CudaArray(ptr, tuple(shape), _DTYPE_STR[str(dtype)]), device=device)
 
 
+CANARY_BYTES = 256
+CANARY_VALUE = 0xA5
+
+
 class SymmetricHeap:
     def __init__(self, tp, nbytes):
         import torch
@@ -53,8 +61,11 @@ class SymmetricHeap:
         hbytes = int(lib.tdb_symm_handle_bytes())
         handle = (ctypes.c_uint8 * hbytes)()
         base = ctypes.c_void_p()
-        native.check(lib.tdb_symm_alloc(self.nbytes, ctypes.byref(base), ctypes.addressof(handle)), "symm alloc")
+        native.check(lib.tdb_symm_alloc(self.nbytes + CANARY_BYTES, ctypes.byref(base), ctypes.addressof(handle)),
+                     "symm alloc")
         self.base = int(base.value)
+        native.check(lib.tdb_memset_async(self.base + self.nbytes, CANARY_VALUE, CANARY_BYTES, native.stream_ptr()),
+                     "symm canary")
         mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
         everyone = tp.all_gather_stacked(mine).cpu()
         self.opened = []
@@ -73,6 +84,12 @@ class SymmetricHeap:
         torch.cuda.synchronize()
         tp.barrier()
         self.closed = False
+
+    def canaries_intact(self):
+        """True when the guard bytes after this rank's heap still hold the canary."""
+        import torch
+        guard = alias(self.base + self.nbytes, (CANARY_BYTES,), torch.uint8, self.device)
+        return bool((guard == CANARY_VALUE).all().item())
 
     def view(self, offset, shape, dtype):
         return alias(self.base + int(offset), shape, dtype, self.device)

@@ -145,6 +145,8 @@ def _worker(rank, world, init_file, result_path):
         torch.cuda.synchronize()
         native.raise_on_status()
         out["ag_gemm"] = dict(full_equal=same, max_rel=max(errs))
+        from tempname_dcu_b200.runtime import initialize_context
+        out["canaries"] = [agg.heap.canaries_intact(), initialize_context(group).heap.canaries_intact()]
         agg.close()
         torch.cuda.synchronize()
         native.raise_on_status()
@@ -170,8 +172,9 @@ def test_fused_gemm_rs_all_arms(tmp_path):
     res = json.load(open(path))
     assert res.get("allgather") and all(res["allgather"]), res.get("allgather")
     assert all(res["ag_gemm"]["full_equal"]) and res["ag_gemm"]["max_rel"] < 1e-2, res["ag_gemm"]
+    assert all(res["canaries"]), res["canaries"]
     for key, value in res.items():
-        if key in ("allgather", "ag_gemm"):
+        if key in ("allgather", "ag_gemm", "canaries"):
             continue
         if key.startswith("bitwise"):
             assert all(value.values()), (key, value)
