@@ -41,7 +41,16 @@ def arguments(argv=None):
     ap.add_argument("--execute", action="store_true", help="without this flag only print the plan")
     ap.add_argument("--out", type=Path)
     ap.add_argument("--python", default=sys.executable)
-    ap.add_argument("--world-size", type=int, choices=(2, 4, 8), default=8)
+    ap.add_argument("--world-size", type=int, choices=(1, 2, 4, 8), default=8,
+                    help="1 runs the flux arm alone (no collective to compare)")
+    ap.add_argument("--arm", action="append", choices=p.ARMS, dest="arms",
+                    help="compare only these arms (repeatable; default all five)")
+    ap.add_argument("--vocab", type=int, help="override the preset's vocabulary size")
+    ap.add_argument("--vocab-pad", action="store_true",
+                    help="pad the vocabulary up to a multiple of 128 x world_size (e.g. GPT-2's 50257)")
+    ap.add_argument("--accum", type=int, help="micro-batches accumulated per optimizer step")
+    ap.add_argument("--selective-mode", choices=("wire", "fp8-mma"), default="wire",
+                    help="wire: selected blocks cross NVLink as E4M3 packets (the only mode built)")
     ap.add_argument("--chunk-rows", type=int)
     ap.add_argument("--warmup-steps", type=int, default=10)
     ap.add_argument("--steps", type=int, default=50)
@@ -61,7 +70,12 @@ def arguments(argv=None):
     ap.add_argument("--worker-timeout", type=int, default=7200)
     ap.add_argument("--report", action="store_true", help="read-only audit of a completed --out directory")
     args = ap.parse_args(argv)
-    p.orders(args.trials, args.blocks)
+    args.arms = p.select_arms(args.arms)
+    p.orders(args.trials, args.blocks, args.arms)
+    p.require(args.world_size > 1 or args.arms == ("flux",),
+              "--world-size 1 has no reduce-scatter to compare: use --arm flux")
+    p.require(args.selective_mode == "wire",
+              "--selective-mode fp8-mma (block-scaled E4M3 MMA on the selected blocks) is not implemented")
     p.require(args.warmup_steps >= 0 and args.operator_warmup >= 0, "warm-up counts must be non-negative")
     p.require(args.steps > 0 and args.operator_iters > 0 and args.worker_timeout > 0,
               "timing counts and timeout must be positive")
@@ -75,6 +89,13 @@ def arguments(argv=None):
     model = dict(p.SMALL_MODEL if args.small_model else p.BENCH_MODEL if args.bench_model else p.MODEL)
     if args.chunk_rows is not None:
         model["chunk_rows"] = args.chunk_rows
+    if args.vocab is not None:
+        model["vocab"] = args.vocab
+    if args.vocab_pad:
+        model["pad_vocab"] = True
+    if args.accum is not None:
+        p.require(args.accum > 0, "--accum must be positive")
+        model["accumulation_steps"] = args.accum
     p.validate_model(model, args.world_size)
     p.require(model["sequence"] * model["micro_batch"] // args.world_size // model["chunk_rows"] >= 2,
               "at least two blocks per destination are needed to distinguish the schedules")
@@ -84,6 +105,7 @@ def arguments(argv=None):
         args.out = REPO / "logs" / "experiment" / f"five-arm-{stamp}"
     args.out = args.out.expanduser().resolve()
     args.scope = "preflight" if args.preflight_only else "operator" if args.operator_only else "train"
+    p.jobs(args.trials, args.blocks, args.scope, args.arms, args.world_size)
     p.require(args.report or args.scope != "train" or args.warmup_steps >= 1,
               "full training needs at least one warm-up step for the per-operator checks")
     return args
@@ -105,6 +127,7 @@ def source_files():
 
 def plan_for(args, manifest=None, run_id=None):
     config = dict(protocol=p.PROTOCOL, run_id=run_id or "PREVIEW", world_size=args.world_size, model=args.model,
+                  arms=list(args.arms), selective_mode=args.selective_mode,
                   timing=dict(warmup_steps=args.warmup_steps, timed_steps=args.steps,
                               operator_warmup=args.operator_warmup, operator_iterations=args.operator_iters),
                   seed=1234, token_seed=4321, build_dir=str(args.out / "build"), profile=args.profile,
@@ -112,8 +135,9 @@ def plan_for(args, manifest=None, run_id=None):
                   recommended_image=p.RECOMMENDED_IMAGE, backend=p.BACKEND, calibration=args.calibration,
                   execution_plan=None, execution_plan_sha256=None)
     return dict(config=config, scope=args.scope, trials=args.trials, blocks=args.blocks,
-                counterbalanced=p.balanced(args.blocks), schedule=p.orders(args.trials, args.blocks),
-                jobs=p.jobs(args.trials, args.blocks, args.scope))
+                arms=list(args.arms), counterbalanced=p.balanced(args.blocks, args.arms),
+                schedule=p.orders(args.trials, args.blocks, args.arms),
+                jobs=p.jobs(args.trials, args.blocks, args.scope, args.arms, args.world_size))
 
 
 def command_for(python, source_root, directory, job, world):
@@ -226,9 +250,9 @@ def execute(args):
                 identities = identity
                 group = groups.setdefault((job["trial"], job["block"]), {})
                 group[job["arm"]] = rows
-                for other in p.FULL_TACO_ARMS[1:]:
-                    if "flux_taco" in group and other in group:
-                        p.compare_taco_trajectories(group["flux_taco"], group[other])
+                taco = [a for a in p.FULL_TACO_ARMS if a in group]
+                for other in taco[1:]:
+                    p.compare_taco_trajectories(group[taco[0]], group[other])
             done = dict(job=job, command_sha256=p.sha(directory / "command.json"),
                         rank_sha256={f"rank{r}.json": p.sha(directory / f"rank{r}.json")
                                      for r in range(args.world_size)})

@@ -66,11 +66,27 @@ def validate_model(model, world):
     return model
 
 
-def orders(trials, blocks):
-    """Counterbalanced arm orders: the 5 rotations and their reverses, the
-    cycle reversed on odd trials."""
+def select_arms(arms=None):
+    """The arms one experiment compares, in the canonical order (all five by
+    default).  A subset keeps the rotation/reverse counterbalancing among the
+    chosen arms; the calibrate job runs only when an arrival arm is chosen."""
+    if arms is None:
+        return ARMS
+    arms = list(arms)
+    require(arms and len(set(arms)) == len(arms) and set(arms) <= set(ARMS), f"arms must be distinct names of {ARMS}")
+    return tuple(a for a in ARMS if a in arms)
+
+
+def needs_calibration(arms):
+    return any(a in (ARRIVAL, SELECTIVE) for a in arms)
+
+
+def orders(trials, blocks, arms=ARMS):
+    """Counterbalanced arm orders: the rotations of the arm list and their
+    reverses, the cycle reversed on odd trials."""
     require(positive_int(trials) and positive_int(blocks), "trials and blocks must be positive")
-    rotations = [list(ARMS[i:] + ARMS[:i]) for i in range(len(ARMS))]
+    arms = select_arms(arms)
+    rotations = [list(arms[i:] + arms[:i]) for i in range(len(arms))]
     cycle = rotations + [r[::-1] for r in rotations]
     out = []
     for trial in range(trials):
@@ -80,24 +96,33 @@ def orders(trials, blocks):
     return out
 
 
-def jobs(trials, blocks, scope):
+def jobs(trials, blocks, scope, arms=ARMS, world=None):
+    """preflight, then calibrate (arrival arms only), then the operator windows
+    (skipped on one rank: no reduce-scatter), then the training windows."""
     require(scope in ("preflight", "operator", "train"), "invalid experiment scope")
-    out = [dict(stage="preflight", arm="flux", trial=0, block=0, index=0, directory="preflight")]
+    require(world != 1 or scope != "operator", "the operator windows need at least two ranks")
+    arms = select_arms(arms)
+    out = [dict(stage="preflight", arm=arms[0], trial=0, block=0, index=0, directory="preflight")]
     if scope == "preflight":
         return out
-    out.append(dict(stage="calibrate", arm=ARRIVAL, trial=0, block=0, index=1, directory="calibrate"))
+    if needs_calibration(arms):
+        out.append(dict(stage="calibrate", arm=ARRIVAL, trial=0, block=0, index=1, directory="calibrate"))
     for stage in ("operator", "train"):
         if stage == "train" and scope != "train":
             break
-        for block in orders(trials, blocks):
+        if stage == "operator" and world == 1:
+            continue
+        for block in orders(trials, blocks, arms):
             for arm in block["arms"]:
                 out.append(dict(stage=stage, arm=arm, trial=block["trial"], block=block["block"], index=len(out),
                                 directory=f"{stage}/trial{block['trial']}/block{block['block']:03d}-{arm}"))
     return out
 
 
-def balanced(blocks):
-    return blocks >= 10 and blocks % 10 == 0
+def balanced(blocks, arms=ARMS):
+    """Every rotation and its reverse appear equally often."""
+    cycle = 2 * len(select_arms(arms))
+    return blocks >= cycle and blocks % cycle == 0
 
 
 def sha(path):
@@ -170,7 +195,8 @@ def config_for_job(base, job, execution_plan=None):
     require(base.get("execution_plan") is None and base.get("execution_plan_sha256") is None,
             "the base plan must stay uncalibrated and immutable")
     out = dict(base, job=job)
-    if job["stage"] in ("operator", "train"):
+    if job["stage"] in ("operator", "train") and (execution_plan is not None
+                                                   or needs_calibration(base.get("arms", ARMS))):
         validate_execution_plan(execution_plan, base)
         out.update(execution_plan=execution_plan, execution_plan_sha256=digest(execution_plan))
     return out

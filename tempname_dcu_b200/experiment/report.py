@@ -49,21 +49,22 @@ PAIRS = (("flux_taco", "flux"), ("flux_taco_interleaved", "flux_taco"), (p.ARRIV
          (p.SELECTIVE, p.ARRIVAL), ("flux_taco_interleaved", "flux"), (p.ARRIVAL, "flux"), (p.SELECTIVE, "flux"))
 
 
-def summarize_stage(samples, stage, trials, blocks):
+def summarize_stage(samples, stage, trials, blocks, arms=p.ARMS):
     out = {}
     roles = ("attn", "mlp") if stage == "operator" else ("full_step",)
     for trial in range(1, trials + 1):
         by_role = {}
         for role in roles:
             values = {arm: [next(s["value"] for s in samples if s["trial"] == trial and s["block"] == b
-                                 and s["arm"] == arm and s["role"] == role) for b in range(blocks)] for arm in p.ARMS}
-            pairs = {f"{x}/{y}": pair_statistics(values[x], values[y], p.balanced(blocks)) for x, y in PAIRS}
-            arms = {a: summary(v) for a, v in values.items()}
-            for arm in p.ARMS:
+                                 and s["arm"] == arm and s["role"] == role) for b in range(blocks)] for arm in arms}
+            pairs = {f"{x}/{y}": pair_statistics(values[x], values[y], p.balanced(blocks, arms))
+                     for x, y in PAIRS if x in values and y in values}
+            result = {a: summary(v) for a, v in values.items()}
+            for arm in arms:
                 chosen = [s for s in samples if s["trial"] == trial and s["arm"] == arm and s["role"] == role]
                 if stage == "train":
-                    arms[arm].update(
-                        tokens_per_second=chosen[0]["tokens_per_step"] * 1000 / arms[arm]["mean"],
+                    result[arm].update(
+                        tokens_per_second=chosen[0]["tokens_per_step"] * 1000 / result[arm]["mean"],
                         mean_training_loss=statistics.mean(s["mean_loss"] for s in chosen),
                         mean_final_loss=statistics.mean(s["final_loss"] for s in chosen),
                         mean_grad_norm=statistics.mean(s["mean_grad_norm"] for s in chosen),
@@ -71,13 +72,13 @@ def summarize_stage(samples, stage, trials, blocks):
                         max_peak_allocated_gib=max(s["peak_allocated_bytes"] for s in chosen) / 2 ** 30,
                         max_peak_reserved_gib=max(s["peak_reserved_bytes"] for s in chosen) / 2 ** 30)
                 else:
-                    arms[arm].update(
+                    result[arm].update(
                         full_gemm_only_mean_us=statistics.mean(s["full_gemm_only_us"] for s in chosen),
                         max_bf16_relative_l2=max(s["bf16_relative_l2"] for s in chosen),
                         max_codec_reference_relative_l2=max(s["codec_reference_relative_l2"] for s in chosen),
                         artificial_bypass_rank_windows=sum(len(s["artificial_bypass_ranks"]) for s in chosen),
                         artificial_diagnostic_rank_windows=sum(s["artificial_diagnostic_ranks"] for s in chosen))
-            by_role[role] = dict(unit="us/call" if stage == "operator" else "ms/step", arms=arms, pairs=pairs)
+            by_role[role] = dict(unit="us/call" if stage == "operator" else "ms/step", arms=result, pairs=pairs)
         out[f"trial{trial}"] = by_role
     return out
 
@@ -190,7 +191,10 @@ def replay(root):
     p.validate_calibration_options(config["calibration"])
     p.require(config.get("execution_plan") is None and config.get("execution_plan_sha256") is None,
               "the immutable base plan must not be rewritten after calibration")
-    p.require(plan["jobs"] == p.jobs(plan["trials"], plan["blocks"], plan["scope"]), "frozen schedule changed")
+    arms = p.select_arms(plan.get("arms"))
+    p.require(config.get("arms", list(p.ARMS)) == list(arms), "plan and config disagree on the arms")
+    p.require(plan["jobs"] == p.jobs(plan["trials"], plan["blocks"], plan["scope"], arms, config["world_size"]),
+              "frozen schedule changed")
     manifest = p.read(root / "source-manifest.json")
     p.require(p.digest(manifest) == config["source_manifest_sha256"], "source manifest changed")
     for name, expected in manifest.items():
@@ -265,20 +269,22 @@ def replay(root):
                                              and rec["arrival_diagnostic"]["ready_bypass_observed"]],
                     artificial_diagnostic_ranks=config["world_size"] if job["arm"] in (p.ARRIVAL, p.SELECTIVE) else 0))
     for group in trajectories.values():
-        p.require(set(group) == set(p.ARMS), "incomplete five-arm training block")
-        for other in p.FULL_TACO_ARMS[1:]:
-            p.compare_taco_trajectories(group["flux_taco"], group[other])
+        p.require(set(group) == set(arms), "incomplete training block")
+        taco = [a for a in p.FULL_TACO_ARMS if a in arms]
+        for other in taco[1:]:
+            p.compare_taco_trajectories(group[taco[0]], group[other])
     report = dict(protocol=p.PROTOCOL, run_id=config["run_id"], completed=True, completed_scope=plan["scope"],
                   hardware_target="B200, single node", world_size=config["world_size"], model=config["model"],
                   standard_tp8_workload=config["world_size"] == 8 and config["model"] in (p.MODEL, p.BENCH_MODEL),
                   implementation="fused tcgen05 GEMM + NVLink reduce-scatter kernel (tempname_dcu_b200)",
                   backend=p.BACKEND, original_cuda_flux=False, environment_identity=environment,
                   timing=config["timing"], recommended_image=p.RECOMMENDED_IMAGE, trials=plan["trials"],
-                  blocks=plan["blocks"], counterbalanced=p.balanced(plan["blocks"]),
-                  ci_available=p.balanced(plan["blocks"]) and bool(samples["operator"]),
-                  short_run=not p.balanced(plan["blocks"]), all_windows_retained=True, correctness_passed=True,
-                  full_quantized_trajectories_identical=bool(trajectories),
-                  trajectory_equivalence_arms=list(p.FULL_TACO_ARMS),
+                  blocks=plan["blocks"], arms=list(arms), counterbalanced=p.balanced(plan["blocks"], arms),
+                  ci_available=p.balanced(plan["blocks"], arms) and bool(samples["operator"]),
+                  short_run=not p.balanced(plan["blocks"], arms), all_windows_retained=True, correctness_passed=True,
+                  full_quantized_trajectories_identical=bool(trajectories)
+                  and sum(a in arms for a in p.FULL_TACO_ARMS) > 1,
+                  trajectory_equivalence_arms=[a for a in p.FULL_TACO_ARMS if a in arms],
                   formal_optimizer_steps=len(samples["train"]) * config["timing"]["timed_steps"],
                   training_windows=len(samples["train"]), rank_sha256=rank_files, artifact_sha256=artifacts,
                   native_build_by_rank=native_identity, profile_requested=config["profile"],
@@ -288,7 +294,7 @@ def replay(root):
                   samples=samples, results={})
     for stage in ("operator", "train"):
         if samples[stage]:
-            report["results"][stage] = summarize_stage(samples[stage], stage, plan["trials"], plan["blocks"])
+            report["results"][stage] = summarize_stage(samples[stage], stage, plan["trials"], plan["blocks"], arms)
     return report
 
 
@@ -334,7 +340,7 @@ def markdown(report):
                                      f"{v['max_bf16_relative_l2']:.6g} | {v['max_codec_reference_relative_l2']:.6g} |")
                     lines += ["", "| artificial skew diagnostic | bypass rank-windows / diagnosed rank-windows |",
                               "| --- | ---: |"]
-                    for arm in (p.ARRIVAL, p.SELECTIVE):
+                    for arm in (a for a in (p.ARRIVAL, p.SELECTIVE) if a in result["arms"]):
                         v = result["arms"][arm]
                         lines.append(f"| {arm} | {v['artificial_bypass_rank_windows']}/"
                                      f"{v['artificial_diagnostic_rank_windows']} |")

@@ -46,6 +46,45 @@ def test_job_counts():
     assert [j["stage"] for j in p.jobs(1, 1, "train")][:2] == ["preflight", "calibrate"]
 
 
+def test_arm_subsets_keep_counterbalancing_and_skip_unused_stages():
+    pair = ("flux", "flux_taco")
+    cycle = p.orders(1, 4, pair)
+    assert [b["arms"] for b in cycle] == [["flux", "flux_taco"], ["flux_taco", "flux"],
+                                          ["flux_taco", "flux"], ["flux", "flux_taco"]]
+    assert p.balanced(4, pair) and not p.balanced(2, ("flux", "flux_taco", p.ARRIVAL))
+    stages = [j["stage"] for j in p.jobs(1, 2, "train", pair)]
+    assert "calibrate" not in stages and stages.count("operator") == stages.count("train") == 4
+    assert [j["stage"] for j in p.jobs(1, 1, "train", (p.SELECTIVE,))][:2] == ["preflight", "calibrate"]
+    assert p.select_arms(["flux_taco", "flux"]) == pair  # canonical order
+    single = p.jobs(1, 2, "train", ("flux",), world=1)
+    assert [j["stage"] for j in single] == ["preflight", "train", "train"]
+    with pytest.raises(ValueError):
+        p.select_arms(["flux", "flux"])
+    with pytest.raises(ValueError):
+        p.jobs(1, 1, "operator", ("flux",), world=1)
+
+
+def test_cli_model_and_arm_flags(tmp_path):
+    args = C.arguments(["--out", str(tmp_path / "x"), "--arm", "flux_taco", "--arm", "flux", "--vocab", "50257",
+                        "--vocab-pad", "--accum", "8", "--world-size", "8"])
+    assert args.arms == ("flux", "flux_taco")
+    assert args.model["vocab"] == 50257 and args.model["pad_vocab"] and args.model["accumulation_steps"] == 8
+    plan = C.plan_for(args)
+    assert plan["arms"] == plan["config"]["arms"] == ["flux", "flux_taco"]
+    assert plan["config"]["selective_mode"] == "wire"
+    assert {j["arm"] for j in plan["jobs"] if j["stage"] == "train"} == {"flux", "flux_taco"}
+    one = C.arguments(["--out", str(tmp_path / "y"), "--world-size", "1", "--arm", "flux", "--small-model"])
+    assert [j["stage"] for j in C.plan_for(one)["jobs"]][:2] == ["preflight", "train"]
+
+
+@pytest.mark.parametrize("argv", [["--world-size", "1"], ["--world-size", "1", "--arm", "flux", "--operator-only"],
+                                  ["--selective-mode", "fp8-mma"], ["--arm", "nope"], ["--accum", "0"],
+                                  ["--vocab", "50257"]])
+def test_new_cli_flags_rejected(argv):
+    with pytest.raises((ValueError, SystemExit)):
+        C.arguments(argv)
+
+
 @pytest.mark.parametrize("argv", [["--blocks", "0"], ["--world-size", "3"], ["--steps", "0"],
                                   ["--report"], ["--quant-budget", "2"], ["--chunk-rows", "96"],
                                   ["--small-model", "--bench-model"]])
@@ -138,13 +177,13 @@ def _diag(config, arm):
                 ready_bypass_observed=True, evidence=dict(events=events), ordinary_speedup_claim=False)
 
 
-def _fixture(tmp_path):
+def _fixture(tmp_path, extra=()):
     """A complete operator-scope batch directory built by the real planner
     (calibration replays from synthetic timings)."""
     from tempname_dcu_b200 import planning as P
     args = C.arguments(["--out", str(tmp_path / "run"), "--small-model", "--world-size", "2", "--blocks", "1",
                         "--operator-only", "--operator-warmup", "1", "--operator-iters", "2",
-                        "--calibration-pairs", "1", "--quant-budget", "0.25"])
+                        "--calibration-pairs", "1", "--quant-budget", "0.25", *extra])
     out = args.out
     files = C.source_files()
     manifest = {str(f.relative_to(ROOT)): p.sha(f) for f in files}
@@ -234,6 +273,21 @@ def test_replay_accepts_fixture_and_renders_markdown(tmp_path):
     assert report["completed"] and report["results"]["operator"]
     text = R.markdown(report)
     assert "B200 five-arm experiment" in text and "flux_taco" in text
+
+
+def test_replay_accepts_an_arm_subset(tmp_path):
+    out = _fixture(tmp_path, ["--arm", "flux", "--arm", "flux_taco_interleaved"])
+    report = R.replay(out)
+    assert report["arms"] == ["flux", "flux_taco_interleaved"] and report["selection"] is None
+    result = report["results"]["operator"]["trial1"]["attn"]
+    assert set(result["arms"]) == {"flux", "flux_taco_interleaved"}
+    assert set(result["pairs"]) == {"flux_taco_interleaved/flux"}
+    assert "flux_taco_interleaved" in R.markdown(report)
+    plan = json.loads((out / "plan.json").read_text())
+    plan["arms"] = list(p.ARMS)  # a widened arm list no longer matches the frozen job list
+    p.write(out / "plan.json", plan)
+    with pytest.raises(ValueError):
+        R.replay(out)
 
 
 def _retamper(out, directory, rank, mutate):
