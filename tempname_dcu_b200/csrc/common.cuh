@@ -212,6 +212,62 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool a_mn, bool 
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// ---------------------------------------------------------------------------
+// Block-scaled FP8 (kind::mxf8f6f4): e4m3 A/B, one ue8m0 scale per 32 K values.
+// ---------------------------------------------------------------------------
+
+// Untiled bulk copy global -> this CTA's shared memory (16-byte aligned
+// addresses, size a multiple of 16), completing on an mbarrier.  No multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Descriptor of an unswizzled K-major shared-memory matrix: 8-row core
+// matrices of 16-byte rows, `sbo_bytes` apart along M/N; `lbo_bytes` apart
+// along K (unused when K spans one 16-byte core column).
+__device__ __forceinline__ uint64_t smem_desc_plain(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= 1ull << 46;  // version 1, layout 0 = no swizzle
+  return d;
+}
+
+// 32 rows x 128 bits of shared memory -> TMEM lanes [0,32) x 4 columns,
+// replicated into all four 32-lane sub-partitions (the scale-factor layout
+// the block-scaled MMA reads for M = 128).
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Instruction descriptor of kind::mxf8f6f4 with e4m3 A/B (format 0), K-major
+// operands, ue8m0 scales (bit 23) and the dense K = 32 shape (bit 31 = 0):
+//   [4,6) B scale byte; [7,10) A fmt; [10,13) B fmt; [17,23) N>>3;
+//   [24,29) M>>4; [29,31) A scale byte.
+__host__ __device__ constexpr uint32_t idesc_mxf8(int m, int n) {
+  return (static_cast<uint32_t>(n >> 3) << 17) | (1u << 23) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// D[tmem] (+)= (A * 2^sfa) (B * 2^sfb)^T for one K = 32 step.  sf_byte picks
+// the scale byte (the 32-value K block inside the scale column word); it goes
+// both into the descriptor and into bits [30,32) of the scale addresses.
+__device__ __forceinline__ void umma_mxf8_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t sfa_col, uint32_t sfb_col, uint32_t sf_byte,
+                                             uint32_t accumulate) {
+  const uint32_t id = idesc | (sf_byte << 29) | (sf_byte << 4);
+  const uint32_t ta = sfa_col | (sf_byte << 30), tb = sfb_col | (sf_byte << 30);
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(id), "r"(accumulate), "r"(ta), "r"(tb));
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

@@ -27,16 +27,42 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one 128B swizzle row
 constexpr int kThreads = 192;
 
-template <int BN, int STAGES = (BN == 128 ? 6 : 4)>
+template <int BN, int STAGES = (BN == 128 ? 6 : 4), bool MX = false>
 struct Config {
   static constexpr int kStages = STAGES;
-  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kABytes = BM * BK * 2;  // also 128 rows x 128 e4m3 (one block-scaled K step)
   static constexpr int kBBytes = BN * BK * 2;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  // two accumulators of BN columns; the allocation is a power of two
-  static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;
+  // block-scaled FP8 stages also carry the scale atoms of A (512 B) and B (BN*4 B)
+  static constexpr int kSfBytes = MX ? (512 + BN * 4 + 1023) / 1024 * 1024 : 0;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfBytes;
+  // TMEM: two accumulators of BN columns, then (FP8) a ring of scale columns
+  static constexpr int kSfCols = 4 + BN / 32;
+  static constexpr int kTmemCols = (MX || 2 * BN > 256) ? 512 : 256;
+  static_assert(!MX || (BN % 128 == 0 && 2 * BN + STAGES * kSfCols <= 512), "FP8 scale ring does not fit TMEM");
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
+
+// Block-scaled FP8 operands (kind::mxf8f6f4).  A is e4m3 [rows, K] and B is
+// e4m3 [N, K], both K-major with TMA boxes of {128 bytes, 128 | BN rows}.
+// Scales are ue8m0 (2^(byte-127)), one per 32 consecutive K values, stored
+// as 512-byte atoms: the atom of 128-row block `blk` and 128-wide K chunk
+// `kc` sits at (kc * blocks + blk) * 512, and inside it row r's scale for the
+// 32-value block j at (r % 32) * 16 + (r / 32) * 4 + j -- the byte order in
+// which one tcgen05.cp 32x128b.warpx4 lays them out in TMEM (lane r % 32,
+// column r / 32, byte j).
+struct MxOperands {
+  const CUtensorMap* tmA;
+  const CUtensorMap* tmB;
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  int a_blocks, b_blocks;
+  const uint8_t* mask;  // per 128-row m block: nonzero = block-scaled FP8 tile; null = every tile
+  __device__ __forceinline__ bool on(int m_blk) const { return mask == nullptr || mask[m_blk] != 0; }
+};
+
+// TMA map of an e4m3 operand [rows, K] (K-major, 128-byte swizzle), box
+// {128 bytes, box_rows} (csrc/gemm_mx.cu).
+int make_fp8_map(CUtensorMap* map, const void* ptr, int rows, int K, int box_rows);
 
 // Output-tile order.  Grouped raster (GROUP_M m-blocks per band) for L2 reuse,
 // or an explicit device table of tile ids (used by the fused collective
@@ -121,10 +147,15 @@ __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr) {
 
 // Epi may own shared memory (Epi::kSmemBytes, placed after the barriers);
 // the epilogue warps receive it through epi.set_smem().
-template <int BN, bool A_MN, bool B_MN, class Epi, int STAGES = Config<BN>::kStages>
+// MX = true adds block-scaled FP8 tiles (those whose m block mx->on()): they
+// stream 128-wide K steps of e4m3 plus scale atoms through the same stage
+// ring and issue kind::mxf8f6f4 MMAs; the other tiles run the bf16 path.
+template <int BN, bool A_MN, bool B_MN, class Epi, int STAGES = Config<BN>::kStages, bool MX = false>
 __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUtensorMap* tmB, int K,
-                                              const TileOrder& order, Epi& epi, int* status) {
-  using Cfg = Config<BN, STAGES>;
+                                              const TileOrder& order, Epi& epi, int* status,
+                                              const MxOperands* mx = nullptr) {
+  using Cfg = Config<BN, STAGES, MX>;
+  static_assert(!MX || (!A_MN && !B_MN), "block-scaled FP8 operands are K-major");
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -171,14 +202,28 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
         order.tile(i, mb, nb);
         const int m0 = mb * BM, n0 = nb * BN;
         if (order.gate_ready && !gate_wait(order, m0 / 128, status)) { ok = false; *abort_flag = 1; break; }
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        bool fp8 = false;
+        if constexpr (MX) fp8 = mx->on(mb);
+        const int tile_kb = fp8 ? K / 128 : num_kb;
+        for (int kb = 0; kb < tile_kb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t round = it / S;
           if (!mbar_wait(&bars->empty[s], (round & 1) ^ 1, status, 10)) { ok = false; *abort_flag = 1; break; }
           if (*abort_flag) { ok = false; break; }
           uint8_t* sa = smem + s * Cfg::kStageBytes;
           uint8_t* sb = sa + Cfg::kABytes;
-          mbar_arrive_expect_tx(&bars->full[s], Cfg::kStageBytes);
+          if constexpr (MX) {
+            if (fp8) {
+              uint8_t* sf = sb + Cfg::kBBytes;
+              mbar_arrive_expect_tx(&bars->full[s], Cfg::kABytes + Cfg::kBBytes + 512 + BN * 4);
+              tma_load_2d(sa, mx->tmA, &bars->full[s], kb * 128, m0);
+              tma_load_2d(sb, mx->tmB, &bars->full[s], kb * 128, n0);
+              bulk_g2s(sf, mx->sfa + (size_t(kb) * mx->a_blocks + mb) * 512, 512, &bars->full[s]);
+              bulk_g2s(sf + 512, mx->sfb + (size_t(kb) * mx->b_blocks + n0 / 128) * 512, BN * 4, &bars->full[s]);
+              continue;
+            }
+          }
+          mbar_arrive_expect_tx(&bars->full[s], Cfg::kABytes + Cfg::kBBytes);
           const int k0 = kb * BK;
           if (!A_MN) {
             tma_load_2d(sa, tmA, &bars->full[s], k0, m0);
@@ -214,7 +259,14 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
         if (!mbar_wait(&bars->tmem_empty[b], (use & 1) ^ 1, status, 20)) { ok = false; *abort_flag = 1; break; }
         tc_fence_after();
         const uint32_t dcol = tmem_base + b * BN;
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        bool fp8 = false;
+        if constexpr (MX) {
+          int mb, nb;
+          order.tile(i, mb, nb);
+          fp8 = mx->on(mb);
+        }
+        const int tile_kb = fp8 ? K / 128 : num_kb;
+        for (int kb = 0; kb < tile_kb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t round = it / S;
           if (!mbar_wait(&bars->full[s], round & 1, status, 21)) { ok = false; *abort_flag = 1; break; }
@@ -222,6 +274,25 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * Cfg::kStageBytes);
           const uint32_t sb = sa + Cfg::kABytes;
+          if constexpr (MX) {
+            if (fp8) {
+              // scales: smem atoms -> TMEM columns of this stage, then four K = 32 MMAs
+              const uint32_t sf = sb + Cfg::kBBytes;
+              const uint32_t sfa_col = tmem_base + 2 * BN + s * Cfg::kSfCols;
+              const uint32_t sfb_col = sfa_col + 4;
+              tmem_cp_32x128b_x4(sfa_col, smem_desc_plain(sf, 0, 128));
+#pragma unroll
+              for (int j = 0; j < BN / 128; ++j) tmem_cp_32x128b_x4(sfb_col + 4 * j, smem_desc_plain(sf + 512 + 512 * j, 0, 128));
+              constexpr uint32_t idesc8 = idesc_mxf8(BM, BN);
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                umma_mxf8_ss(dcol, desc_kmajor(sa + k * 32), desc_kmajor(sb + k * 32), idesc8, sfa_col, sfb_col,
+                             uint32_t(k), (kb | k) != 0 ? 1u : 0u);
+              issued = true;
+              umma_commit(&bars->empty[s]);
+              continue;
+            }
+          }
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = A_MN ? desc_mnmajor(sa + k * 16 * 128) : desc_kmajor(sa + k * 32);

@@ -597,6 +597,26 @@ __global__ void __launch_bounds__(kReduceThreads, 2)
   if (ph && threadIdx.x == 0) ph[3] = globaltimer();
 }
 
+// Producer for the selective arm's block-scaled FP8 mode: the tiles of the
+// calibrated blocks (mx.on(m block)) run as kind::mxf8f6f4 MMAs on e4m3
+// operands, the rest as bf16; every tile is pushed as bf16.
+constexpr int kMxStages = 5;
+
+__global__ void __launch_bounds__(gemm::kThreads, 1)
+    gemm_rs_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmA8, const __grid_constant__ CUtensorMap tmB8, int K,
+                      gemm::TileOrder order, const __grid_constant__ Params p, const uint8_t* sfa, const uint8_t* sfb,
+                      int a_blocks, int b_blocks, const uint8_t* mx_mask, int* status) {
+  PushEpi<128> epi;
+  epi.p = &p;
+  epi.status = status;
+  gemm::MxOperands mx{&tmA8, &tmB8, sfa, sfb, a_blocks, b_blocks, mx_mask};
+  gemm::gemm_mainloop<128, false, false, PushEpi<128>, kMxStages, true>(&tmA, &tmB, K, order, epi, status, &mx);
+  signal_tiles(p, order);
+}
+
+static int launch_consumer(const Params& p, cudaStream_t stream);
+
 template <int BN, bool B_MN>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int K, const gemm::TileOrder& order, const Params& p,
                   int grid, cudaStream_t stream) {
@@ -617,6 +637,36 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int K, const gem
   tdb_host::launched(1);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs: producer launch failed");
+  return launch_consumer(p, stream);
+}
+
+static int launch_mx(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta8, const CUtensorMap& tb8,
+                     int K, const gemm::TileOrder& order, const Params& p, const uint8_t* sfa, const uint8_t* sfb,
+                     const uint8_t* mx_mask, int grid, cudaStream_t stream) {
+  using Cfg = gemm::Config<128, kMxStages, true>;
+  constexpr int kSmem = Cfg::kSmemBytes + PushEpi<128>::kSmemBytes;
+  static_assert(kSmem <= 227 * 1024, "fused FP8 GEMM-RS shared memory budget");
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_rs_mx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs_mx: cudaFuncSetAttribute failed");
+    attr[dev & 63] = true;
+  }
+  gemm_rs_mx_kernel<<<grid, gemm::kThreads, kSmem, stream>>>(ta, tb, ta8, tb8, K, order, p, sfa, sfb, p.m / 128,
+                                                              p.N / 128, mx_mask, tdb_host::status_ptr());
+  tdb_host::launched(1);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs_mx: producer launch failed");
+  return launch_consumer(p, stream);
+}
+
+static int launch_consumer(const Params& p, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int* status = tdb_host::status_ptr();
+  cudaError_t e;
   // Exactly the CTAs that are co-resident: every consumer CTA is polling and
   // reducing at the same time (a second wave would start only after the
   // first one drained, serialising the waits).
@@ -650,13 +700,23 @@ using namespace tdb;
 // Fused GEMM + reduce-scatter.  A [m, K] (K contiguous, row stride lda);
 // B = weight: [N, K] (b_mn = 0) or [K, N] (b_mn = 1), row stride ldb.
 // tile_table: [num_tiles] production order (m_tile * (N / bn) + n_tile).
-TDB_API int tdb_gemm_rs(const void* A, int64_t lda, const void* B, int b_mn, int64_t ldb, int m, int N, int K,
-                        int bn, const int* tile_table, const uint64_t* peers, int W, int rank, int chunk_rows,
+namespace tdb {
+namespace rs {
+struct MxArgs {
+  const void* a8;
+  const void* sfa;
+  const void* b8;
+  const void* sfb;
+  const uint8_t* mask;  // per 128-row m block of A
+};
+
+static int gemm_rs_impl(const void* A, int64_t lda, const void* B, int b_mn, int64_t ldb, int m, int N, int K, int bn,
+                        const int* tile_table, const uint64_t* peers, int W, int rank, int chunk_rows,
                         uint64_t recv_off, uint64_t slot_bytes, uint64_t flags_off, int set, unsigned int expected,
                         const uint8_t* qmask, void* out, const void* bias, const void* residual, const int* consume,
                         int policy, unsigned long long* timeline, long long delay_cycles, int delay_mb, int delay_nb,
                         double wait_seconds, unsigned long long* phases, const uint32_t* call_state,
-                        void* stream) {
+                        const MxArgs* mx, void* stream) {
   if (!A || !B || !out || !tile_table || !peers || !qmask || !consume || W < 2 || W > rs::kMaxWorld || rank < 0 ||
       rank >= W)
     return tdb_host::fail(int(cudaErrorInvalidValue), "gemm_rs: bad pointers or ranks");
@@ -710,9 +770,52 @@ TDB_API int tdb_gemm_rs(const void* A, int64_t lda, const void* B, int b_mn, int
   const int sms = tdb_host::sm_count();
   const int grid = order.num_tiles < sms ? order.num_tiles : sms;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (mx) {
+    if (bn != 128 || b_mn || K % 128 || !mx->a8 || !mx->b8 || !mx->sfa || !mx->sfb || !mx->mask ||
+        (reinterpret_cast<uintptr_t>(mx->sfa) | reinterpret_cast<uintptr_t>(mx->sfb)) % 16)
+      return tdb_host::fail(int(cudaErrorInvalidValue), "gemm_rs_mx: needs bn 128, K-major B, K %% 128, aligned scales");
+    CUtensorMap ta8, tb8;
+    rc = gemm::make_fp8_map(&ta8, mx->a8, m, K, rs::BM);
+    if (rc) return rc;
+    rc = gemm::make_fp8_map(&tb8, mx->b8, N, K, 128);
+    if (rc) return rc;
+    return rs::launch_mx(ta, tb, ta8, tb8, K, order, p, static_cast<const uint8_t*>(mx->sfa),
+                         static_cast<const uint8_t*>(mx->sfb), mx->mask, grid, s);
+  }
   if (bn == 256) return b_mn ? rs::launch<256, true>(ta, tb, K, order, p, grid, s)
                              : rs::launch<256, false>(ta, tb, K, order, p, grid, s);
   return b_mn ? rs::launch<128, true>(ta, tb, K, order, p, grid, s) : rs::launch<128, false>(ta, tb, K, order, p, grid, s);
+}
+}  // namespace rs
+}  // namespace tdb
+
+TDB_API int tdb_gemm_rs(const void* A, int64_t lda, const void* B, int b_mn, int64_t ldb, int m, int N, int K,
+                        int bn, const int* tile_table, const uint64_t* peers, int W, int rank, int chunk_rows,
+                        uint64_t recv_off, uint64_t slot_bytes, uint64_t flags_off, int set, unsigned int expected,
+                        const uint8_t* qmask, void* out, const void* bias, const void* residual, const int* consume,
+                        int policy, unsigned long long* timeline, long long delay_cycles, int delay_mb, int delay_nb,
+                        double wait_seconds, unsigned long long* phases, const uint32_t* call_state,
+                        void* stream) {
+  return rs::gemm_rs_impl(A, lda, B, b_mn, ldb, m, N, K, bn, tile_table, peers, W, rank, chunk_rows, recv_off,
+                          slot_bytes, flags_off, set, expected, qmask, out, bias, residual, consume, policy, timeline,
+                          delay_cycles, delay_mb, delay_nb, wait_seconds, phases, call_state, nullptr, stream);
+}
+
+// tdb_gemm_rs whose tiles in the m blocks flagged by mx_mask run as
+// block-scaled FP8 MMAs on a8 / b8 (e4m3 copies of A and B, scale atoms
+// sfa / sfb from tdb_mx_quantize).  bn 128, B K-major, K % 128 == 0.
+TDB_API int tdb_gemm_rs_mx(const void* A, int64_t lda, const void* B, int b_mn, int64_t ldb, int m, int N, int K,
+                           int bn, const int* tile_table, const uint64_t* peers, int W, int rank, int chunk_rows,
+                           uint64_t recv_off, uint64_t slot_bytes, uint64_t flags_off, int set, unsigned int expected,
+                           const uint8_t* qmask, void* out, const void* bias, const void* residual, const int* consume,
+                           int policy, unsigned long long* timeline, long long delay_cycles, int delay_mb,
+                           int delay_nb, double wait_seconds, unsigned long long* phases, const uint32_t* call_state,
+                           const void* a8, const void* sfa, const void* b8, const void* sfb, const uint8_t* mx_mask,
+                           void* stream) {
+  const rs::MxArgs mx{a8, sfa, b8, sfb, mx_mask};
+  return rs::gemm_rs_impl(A, lda, B, b_mn, ldb, m, N, K, bn, tile_table, peers, W, rank, chunk_rows, recv_off,
+                          slot_bytes, flags_off, set, expected, qmask, out, bias, residual, consume, policy, timeline,
+                          delay_cycles, delay_mb, delay_nb, wait_seconds, phases, call_state, &mx, stream);
 }
 
 // Advance the device call state {set, expected, epoch, target0, target1}

@@ -38,6 +38,8 @@ native.register("tdb_gemm_rs", [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p
                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                 ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_double,
                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p])
+native.register("tdb_gemm_rs_mx", list(native.SIGNATURES["tdb_gemm_rs"][:-1])
+                + [ctypes.c_void_p] * 5 + [ctypes.c_void_p])
 native.register("tdb_rs_advance", [ctypes.c_void_p, ctypes.c_uint, ctypes.c_void_p])
 native.register("tdb_gemm_rs_signals_per_block", [ctypes.c_int, ctypes.c_int, ctypes.c_int])
 
@@ -145,14 +147,27 @@ class FluxB200:
     """Fused GEMM + reduce-scatter for one projection shape and arm."""
 
     def __init__(self, m, n, k, group, arm, codec=None, chunk_rows=128, plan=None, diagnostic_delay_cycles=0,
-                 b_mn=False, tile_n=None, remote_first=False):
+                 b_mn=False, tile_n=None, remote_first=False, selective_mode="wire"):
         """``remote_first`` (first three arms only): produce the blocks bound for
         other ranks first and this rank's own blocks last, so the NVLink
         transfers overlap the local tiles; results are bitwise unchanged (the
         receiving side reduces sources in fixed order).  Off for the
         reference experiment arms, whose production order is part of their
-        definition."""
+        definition.
+
+        ``selective_mode`` (selective arm only): ``"wire"`` quantizes the
+        calibrated blocks on the link (TACO packets, the reference's mode);
+        ``"fp8-mma"`` instead computes their GEMM tiles as block-scaled FP8
+        tcgen05 MMAs (e4m3 with one power-of-two scale per 32 K values) and
+        sends every block as BF16."""
         import torch
+        if selective_mode not in ("wire", "fp8-mma"):
+            raise ValueError("selective_mode must be 'wire' or 'fp8-mma'")
+        if selective_mode == "fp8-mma" and (not arm.endswith("_selective") or b_mn or tile_n not in (None, 128)
+                                            or k % 128 or m % 128 or n % 128):
+            raise ValueError("fp8-mma runs the selective arm with a K-major weight, 128-wide tiles and "
+                             "m, n, k multiples of 128")
+        self.selective_mode = selective_mode
         if type(diagnostic_delay_cycles) is not int or not 0 <= diagnostic_delay_cycles <= 100_000_000:
             raise ValueError("diagnostic_delay_cycles must be an integer in [0, 100000000]")
         self.context = initialize_context(group, receive_bytes(m, n, chunk_rows))
@@ -181,7 +196,7 @@ class FluxB200:
         self.selection = selection_statistics(m, n, self.world, chunk_rows, self.selection_mask)
         # Tile width: every rank derives it from the shape alone.
         sms = native.lib().tdb_sm_count(torch.cuda.current_device())
-        self.bn = tile_n or (256 if (m // 128) * (n // 256) >= sms else 128)
+        self.bn = tile_n or (256 if (m // 128) * (n // 256) >= sms and selective_mode == "wire" else 128)
         self.remote_first = bool(remote_first) and arm not in ARRIVAL_ARMS
         if self.remote_first:
             self.tiles = tiles_for_order(remote_first_order(self.order, self.world, self.rank), n, chunk_rows,
@@ -189,7 +204,25 @@ class FluxB200:
         else:
             self.tiles = tile_table(m, n, self.world, chunk_rows, arm, self.plan, block_m=128, block_n=self.bn, k=k)
         self.tile_table = torch.tensor(self.tiles, dtype=torch.int32, device=self.device)
-        self.qmask = torch.tensor([int(x) for x in self.selection_mask], dtype=torch.uint8, device=self.device)
+        # wire_mask: blocks that cross the link as TACO packets; mma_mask: blocks computed in block-scaled FP8
+        fp8 = selective_mode == "fp8-mma"
+        self.wire_mask = [False] * len(self.selection_mask) if fp8 else list(self.selection_mask)
+        self.mma_mask = list(self.selection_mask) if fp8 else [False] * len(self.selection_mask)
+        self.qmask = torch.tensor([int(x) for x in self.wire_mask], dtype=torch.uint8, device=self.device)
+        self.mx = None
+        if fp8:
+            from .ops import mx as _mx
+            rows_mask = [0] * (m // 128)
+            for item in self.order:
+                if self.mma_mask[item["physical"]]:
+                    for mb in range(item["row"] // 128, (item["row"] + chunk_rows) // 128):
+                        rows_mask[mb] = 1
+            self.mx = dict(
+                mask=torch.tensor(rows_mask, dtype=torch.uint8, device=self.device),
+                a8=torch.empty((m, k), dtype=torch.uint8, device=self.device),
+                sfa=torch.empty(_mx.scale_bytes(m, k), dtype=torch.uint8, device=self.device),
+                b8=torch.empty((n, k), dtype=torch.uint8, device=self.device),
+                sfb=torch.empty(_mx.scale_bytes(n, k), dtype=torch.uint8, device=self.device))
         self.per = m // self.world // chunk_rows
         local_in_order = [item["within"] for item in self.order if item["destination"] == self.rank]
         self.consume = torch.tensor(local_in_order, dtype=torch.int32, device=self.device)
@@ -245,16 +278,26 @@ class FluxB200:
             lib = native.lib()
             stream = native.stream_ptr()
             native.check(lib.tdb_rs_advance(ctx.call_state.data_ptr(), self.signals, stream), "rs advance")
-            native.check(lib.tdb_gemm_rs(
-                input_.data_ptr(), input_.stride(0), weight.data_ptr(), int(self.b_mn), weight.stride(0), self.m,
-                self.n, self.k, self.bn, self.tile_table.data_ptr(), heap.peers.data_ptr(), self.world, self.rank,
-                self.chunk_rows, ctx.recv_off, self.slot_bytes, ctx.flags_off, set_, expected,
-                self.qmask.data_ptr(), out.data_ptr(), 0 if bias is None else bias.data_ptr(),
-                0 if residual is None else residual.data_ptr(), self.consume.data_ptr(),
-                1 if self.consumer_policy == "per_lane_ready" else 0,
-                0 if timeline is None else timeline.data_ptr(), delay, self._delay_tile[0], self._delay_tile[1],
-                PEER_WAIT_SECONDS, 0 if self.phase_buffer is None else self.phase_buffer.data_ptr(),
-                ctx.call_state.data_ptr(), stream), "fused gemm_rs")
+            args = (input_.data_ptr(), input_.stride(0), weight.data_ptr(), int(self.b_mn), weight.stride(0), self.m,
+                    self.n, self.k, self.bn, self.tile_table.data_ptr(), heap.peers.data_ptr(), self.world, self.rank,
+                    self.chunk_rows, ctx.recv_off, self.slot_bytes, ctx.flags_off, set_, expected,
+                    self.qmask.data_ptr(), out.data_ptr(), 0 if bias is None else bias.data_ptr(),
+                    0 if residual is None else residual.data_ptr(), self.consume.data_ptr(),
+                    1 if self.consumer_policy == "per_lane_ready" else 0,
+                    0 if timeline is None else timeline.data_ptr(), delay, self._delay_tile[0], self._delay_tile[1],
+                    PEER_WAIT_SECONDS, 0 if self.phase_buffer is None else self.phase_buffer.data_ptr(),
+                    ctx.call_state.data_ptr())
+            if self.mx is None:
+                native.check(lib.tdb_gemm_rs(*args, stream), "fused gemm_rs")
+            else:
+                from .ops import mx as _mx
+                q = self.mx
+                # the operands change every call (activations) or step (weights): quantize both
+                _mx.quantize(input_, q["a8"], q["sfa"])
+                _mx.quantize(weight, q["b8"], q["sfb"])
+                native.check(lib.tdb_gemm_rs_mx(*args, q["a8"].data_ptr(), q["sfa"].data_ptr(), q["b8"].data_ptr(),
+                                                q["sfb"].data_ptr(), q["mask"].data_ptr(), stream),
+                             "fused gemm_rs (block-scaled fp8)")
             self._last = (set_, expected, timeline)
             self.calls += 1
             ctx.calls += 1
@@ -308,7 +351,7 @@ class FluxB200:
         for within in range(self.per):
             physical = self.rank * self.per + within
             for s in range(self.world):
-                if self.selection_mask[physical] and s != self.rank:
+                if self.wire_mask[physical] and s != self.rank:
                     continue
                 out.append((f"receive.{within}.{s}", self._slot_view(set_, s, within, self.slot_bytes,
                                                                      torch.bfloat16, (self.chunk_rows, self.n))))
@@ -321,7 +364,7 @@ class FluxB200:
         elements = self.chunk_rows * self.n
         for within in range(self.per):
             physical = self.rank * self.per + within
-            if not self.selection_mask[physical]:
+            if not self.wire_mask[physical]:
                 continue
             for s in range(self.world):
                 if s == self.rank:
@@ -363,6 +406,15 @@ class FluxB200:
     def state(self):
         quantization = ("selective_remote_h128_e4m3" if self.arm.endswith("_selective") else
                         "all_remote_h128_e4m3" if self.arm != "flux" else "none")
+        extra = {}
+        if self.mx is not None:
+            quantization = "selective_mma_e4m3_ue8m0_k32"
+            bf16 = self.chunk_rows * self.n * 2 * self.per
+            extra = dict(selective_mode="fp8-mma", mma_block_mask=list(self.mma_mask),
+                         remote_wire_bytes_by_source=[bf16 * (self.world - 1)] * self.world,
+                         remote_wire_bytes_per_source=bf16 * (self.world - 1),
+                         actual_remote_wire_bytes_per_rank=bf16 * (self.world - 1),
+                         fused_kernel="tdb::rs::gemm_rs_mx_kernel")
         return dict(backend=BACKEND, arm=self.arm, rank=self.rank, calls=self.calls,
                     shape=[self.m, self.n, self.k], chunk_rows=self.chunk_rows,
                     production_schedule=self.order, mapping_sha256=self.mapping_sha256,
@@ -382,7 +434,7 @@ class FluxB200:
                     consumer_policy=self.consumer_policy, validation_calls=self.validation_calls,
                     diagnostic_delay_cycles=self.diagnostic_delay_cycles, diagnostic_delay_in_normal_forward=False,
                     scheduling_granularity="tcgen05_tile_128x%d" % self.bn,
-                    overlap_claim="epilogue peer stores overlap the MMA of later tiles in one kernel")
+                    overlap_claim="epilogue peer stores overlap the MMA of later tiles in one kernel") | extra
 
 
 def operator_factory_for(arm, remote_first=True):

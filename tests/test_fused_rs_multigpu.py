@@ -75,6 +75,22 @@ def _worker(rank, world, init_file, result_path):
             plan_e_base = dict(plan_e, arrival_order=base_order(m, n, k, world, chunk))
             ebase = FluxB200(m, n, k, group, ARMS[4], chunk_rows=chunk, plan=plan_e_base).forward(x, w)
             out[f"bitwise.k{k}"]["e_ebase"] = bool(torch.equal(ebase, outputs[ARMS[4]]))
+            # selective arm with its blocks computed as block-scaled FP8 MMAs (BF16 on the wire)
+            from tempname_dcu_b200.ops import mx
+            op8 = FluxB200(m, n, k, group, ARMS[4], chunk_rows=chunk, plan=plan_e, selective_mode="fp8-mma")
+            y8 = op8.forward(x, w)
+            torch.cuda.synchronize()
+            native.raise_on_status()
+            qa, sfa = mx.quantize(x)
+            qb, sfb = mx.quantize(w)
+            rows_fp8 = op8.mx["mask"].bool().repeat_interleave(128)
+            partial = torch.where(rows_fp8[:, None], mx.dequantize(qa, sfa) @ mx.dequantize(qb, sfb).t(),
+                                  x.float() @ w.float().t())
+            ref8 = torch.empty((m // world, n), dtype=torch.float32, device="cuda")
+            dist.reduce_scatter_tensor(ref8, partial.contiguous(), group=group)
+            plain, _ = projection_reference(x, w, rank, world, group, False)
+            out[f"fp8mma.k{k}"] = dict(ref=relative_error(y8, ref8), plain=relative_error(y8, plain),
+                                       fp8_rows=int(rows_fp8.sum().item()))
             # fused bias + residual
             bias = torch.randn(n, device="cuda").to(torch.bfloat16)
             res = torch.randn(m // world, n, device="cuda").to(torch.bfloat16)
@@ -180,6 +196,8 @@ def test_fused_gemm_rs_all_arms(tmp_path):
             assert all(value.values()), (key, value)
         elif key.startswith("bias_residual"):
             assert value <= 0.01, (key, value)
+        elif key.startswith("fp8mma"):
+            assert value["fp8_rows"] > 0 and value["ref"] <= 0.01 and value["plain"] <= 0.05, (key, value)
         else:
             arm = key.split(".")[0]
             assert value["plain"] <= (0.01 if arm == "flux" else 0.05), (key, value)

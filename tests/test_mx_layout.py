@@ -1,0 +1,40 @@
+"""Block-scaled FP8 scale-atom layout and the quantizer's torch restatement
+(CPU): the atom byte order, the no-saturation scale rule and round trips."""
+import torch
+
+from tempname_dcu_b200.ops import mx
+
+
+def test_atom_layout_round_trip_and_byte_positions():
+    torch.manual_seed(0)
+    x = (torch.randn(256, 384) * torch.logspace(-3, 3, 384)).to(torch.bfloat16)
+    _, e = mx.quantize_reference(x)
+    sf = mx.pack_scales(e, 256, 384)
+    assert sf.numel() == mx.scale_bytes(256, 384) == 2 * 3 * 512
+    assert torch.equal(mx.scales_dense(sf, 256, 384).long(), (e + 127).long())
+    for r, kb in [(0, 0), (37, 5), (200, 11), (255, 7), (128, 4)]:
+        kc, j = kb // 4, kb % 4
+        off = (kc * 2 + r // 128) * 512 + (r % 32) * 16 + ((r % 128) // 32) * 4 + j
+        assert sf[off].item() == e[r, kb].item() + 127
+
+
+def test_scale_rule_never_saturates_and_is_tight():
+    torch.manual_seed(1)
+    x = (torch.randn(128, 256) * torch.logspace(-6, 6, 256)).to(torch.bfloat16)
+    values, e = mx.quantize_reference(x)
+    amax = x.float().view(128, 8, 32).abs().amax(-1)
+    scaled_max = amax / torch.exp2(e.float())
+    assert (scaled_max <= mx.E4M3_MAX).all()
+    assert (scaled_max > mx.E4M3_MAX / 2).all()  # one smaller exponent would overflow
+    assert (values.abs() <= mx.E4M3_MAX).all()
+
+
+def test_zero_blocks_and_dequantize_error():
+    x = torch.randn(128, 128).to(torch.bfloat16)
+    x[:, :32] = 0
+    values, e = mx.quantize_reference(x)
+    assert (e[:, 0] == -127).all() and (values[:, :32] == 0).all()
+    q = values.to(torch.float8_e4m3fn).view(torch.uint8)
+    d = mx.dequantize(q, mx.pack_scales(e, 128, 128))
+    rel = ((d - x.float()).norm() / x.float().norm()).item()
+    assert rel < 0.04
