@@ -611,8 +611,11 @@ __global__ void __launch_bounds__(gemm::kThreads, 1)
   epi.p = &p;
   epi.status = status;
   gemm::MxOperands mx{&tmA8, &tmB8, sfa, sfb, a_blocks, b_blocks, mx_mask};
+  unsigned long long* ph = p.phases ? p.phases + 4 * blockIdx.x : nullptr;
+  if (ph && threadIdx.x == 0) ph[0] = globaltimer();
   gemm::gemm_mainloop<128, false, false, PushEpi<128>, kMxStages, true>(&tmA, &tmB, K, order, epi, status, &mx);
   signal_tiles(p, order);
+  if (ph && threadIdx.x == 0) ph[1] = globaltimer();
 }
 
 static int launch_consumer(const Params& p, cudaStream_t stream);

@@ -94,6 +94,30 @@ def time_fn(torch, fn, iters, warmup=3, flush=None):
     return times[len(times) // 2]
 
 
+def _bench_mx(torch, name, M, N, K, iters, flush, peak, source):
+    """Block-scaled FP8 GEMM (operands quantized once, outside the timing)
+    against the bf16 GEMMs of the same shape; the quantizer is timed apart."""
+    from . import gemm, mx
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
+    qa, sfa = mx.quantize(x)
+    qb, sfb = mx.quantize(w)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ours = time_fn(torch, lambda: mx.gemm(qa, sfa, qb, sfb, out=out), iters, flush=flush)
+    quant = time_fn(torch, lambda: mx.quantize(x, qa, sfa), iters, flush=flush)
+    bf16 = time_fn(torch, lambda: gemm.gemm(x, w, out=out), iters, flush=flush)
+    theirs = time_fn(torch, lambda: torch.matmul(x, w.t()), iters, flush=flush)
+    mx.gemm(qa, sfa, qb, sfb, out=out)
+    ref = mx.dequantize(qa, sfa) @ mx.dequantize(qb, sfb).t()
+    err = ((out.float() - ref).norm() / ref.norm()).item()
+    flops = 2.0 * M * N * K
+    return dict(name=name, M=M, N=N, K=K, kind="mx", ours_ms=ours, quantize_a_ms=quant, ours_bf16_ms=bf16,
+                cublas_bf16_ms=theirs, ours_tflops=flops / ours / 1e9, speedup_vs_our_bf16=bf16 / ours,
+                speedup_vs_cublas_bf16=theirs / ours, frac_of_bf16_peak=flops / ours / 1e9 / peak,
+                rel_err_vs_dequantized=err, peak_source=source)
+
+
 def bench_gemm(shapes, iters):
     import torch
     from . import gemm, native
@@ -102,6 +126,10 @@ def bench_gemm(shapes, iters):
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
     rows = []
     for name, M, N, K, kind in shapes:
+        if kind == "mx":
+            rows.append(_bench_mx(torch, name, M, N, K, iters, flush, peak, source))
+            print(json.dumps(rows[-1]), flush=True)
+            continue
         a, b = _operands(torch, M, N, K, kind, device)
         out_dtype = torch.float32 if kind in ("wgrad", "fwd_f32") else torch.bfloat16
         out = torch.empty(M, N, dtype=out_dtype, device=device)

@@ -72,9 +72,9 @@ def gemm(qa, sfa, qb, sfb, *, bias=None, out=None, stream=None):
 def scales_dense(sf, rows: int, k: int):
     """Scale atoms -> ue8m0 bytes [rows, K/32] (row r, K block j)."""
     import torch
-    atoms = sf.view(k // 128, rows // 128, 4, 32, 4)  # kc, blk, row group, row % 32, j
+    atoms = sf.view(k // 128, rows // 128, 32, 4, 4)  # kc, blk, row % 32, row group, j
     # [blk, group, lane, kc, j] -> rows in order blk*128 + group*32 + lane
-    return atoms.permute(1, 2, 3, 0, 4).reshape(rows, k // 32)
+    return atoms.permute(1, 3, 2, 0, 4).reshape(rows, k // 32)
 
 
 def dequantize(q, sf):
@@ -106,4 +106,4 @@ def pack_scales(e, rows: int, k: int):
     """Inverse of ``scales_dense``: exponents [rows, K/32] -> scale atoms."""
     import torch
     dense = (e + 127).to(torch.uint8).view(rows // 128, 4, 32, k // 128, 4)  # blk, group, lane, kc, j
-    return dense.permute(3, 0, 1, 2, 4).contiguous().view(-1)
+    return dense.permute(3, 0, 2, 1, 4).contiguous().view(-1)  # kc, blk, lane, group, j

@@ -34,6 +34,8 @@ def main(argv=None):
     ap.add_argument("--arms", default="all")
     ap.add_argument("--remote-first", action="store_true", help="produce remote-bound blocks first (training order)")
     ap.add_argument("--tile-n", type=int, default=0, help="fused kernel tile width (128 or 256; 0 = automatic)")
+    ap.add_argument("--selective-mode", default="wire", choices=("wire", "fp8-mma"),
+                    help="fp8-mma: the selective arm computes every block as block-scaled FP8 (BF16 on the wire)")
     args = ap.parse_args(argv)
     import torch
     import torch.distributed as dist
@@ -88,18 +90,21 @@ def main(argv=None):
         compute_us = flops / (peak * 1e12) * 1e6
         for arm in arms:
             plan = make_role(m, n, k, world, chunk) if arm in ARMS[3:] else None
+            mode = args.selective_mode if arm == ARMS[4] else "wire"
+            if mode == "fp8-mma":
+                plan = make_role(m, n, k, world, chunk, mask=[True] * (m // chunk))
             op = FluxB200(m, n, k, group, arm, chunk_rows=chunk, plan=plan, remote_first=args.remote_first,
-                          tile_n=args.tile_n or None)
+                          tile_n=(args.tile_n or None) if mode == "wire" else None, selective_mode=mode)
             us = timed(lambda: op.forward(x, w, bias, res))
             op.enable_phase_profile(True)
             op.forward(x, w, bias, res)
             torch.cuda.synchronize()
             phases = op.phase_summary()
             op.enable_phase_profile(False)
-            quant = op.quantized
+            quant = op.quantized and mode == "wire"
             link_us = wire_bytes(m, n, world, quant) / (NVLINK_GBS * 1e9) * 1e6
-            roof = max(compute_us, link_us)
-            rows.append(dict(role=role, arm=arm, world=world, m=m, n=n, k=k, fused_us=round(us, 2),
+            roof = max(compute_us / (2.0 if mode == "fp8-mma" else 1.0), link_us)
+            rows.append(dict(role=role, arm=arm, selective_mode=mode, world=world, m=m, n=n, k=k, fused_us=round(us, 2),
                              gemm_plus_nccl_rs_us=round(base_us, 2), gemm_only_us=round(gemm_us, 2),
                              speedup_vs_nccl=round(base_us / us, 3), roofline_us=round(roof, 2),
                              roofline_fraction=round(roof / us, 3), bound="link" if link_us > compute_us else "compute",
