@@ -36,7 +36,7 @@ def calibrate(config, group, out):
     import torch
     import torch.distributed as dist
     from .runtime import FluxB200
-    from .worker import projection_reference, relative_error, require_all
+    from .worker import mx_projection_reference, projection_reference, relative_error, require_all
     cfg = settings(config.get("calibration"))
     model = config["model"]
     rank, world = dist.get_rank(group), dist.get_world_size(group)
@@ -51,11 +51,14 @@ def calibrate(config, group, out):
             gen = torch.Generator(device="cuda").manual_seed(seed + 173 * rank + 7919 * role_index)
             x = torch.randn((m, k), generator=gen, device="cuda").to(torch.bfloat16)
             w = (torch.randn((n, k), generator=gen, device="cuda") / math.sqrt(k)).to(torch.bfloat16)
-            op = FluxB200(m, n, k, group, arm, chunk_rows=chunk, plan=plan)
+            mode = config.get("selective_mode", "wire") if arm.endswith("_selective") else "wire"
+            op = FluxB200(m, n, k, group, arm, chunk_rows=chunk, plan=plan, selective_mode=mode)
             op.validate_next_call = True
             actual = op.forward(x, w)
             mask = plan["selective_mask"] if arm.endswith("_selective") else None
             plain, coded = projection_reference(x, w, rank, world, group, True, mask, chunk)
+            if mode == "fp8-mma":  # candidates time the FP8 MMA blocks; the gate is the FP8 reference
+                coded = mx_projection_reference(x, w, rank, world, group, op.mx["mask"])
             errors = torch.tensor([relative_error(actual, plain), relative_error(actual, coded)],
                                   dtype=torch.float64, device="cuda")
             dist.all_reduce(errors, op=dist.ReduceOp.MAX, group=group)

@@ -50,7 +50,8 @@ def arguments(argv=None):
                     help="pad the vocabulary up to a multiple of 128 x world_size (e.g. GPT-2's 50257)")
     ap.add_argument("--accum", type=int, help="micro-batches accumulated per optimizer step")
     ap.add_argument("--selective-mode", choices=("wire", "fp8-mma"), default="wire",
-                    help="wire: selected blocks cross NVLink as E4M3 packets (the only mode built)")
+                    help="wire: selected blocks cross NVLink as TACO E4M3 packets (the reference's mode); "
+                         "fp8-mma: their GEMM tiles run as block-scaled FP8 tcgen05 MMAs, BF16 on the wire")
     ap.add_argument("--chunk-rows", type=int)
     ap.add_argument("--warmup-steps", type=int, default=10)
     ap.add_argument("--steps", type=int, default=50)
@@ -74,8 +75,6 @@ def arguments(argv=None):
     p.orders(args.trials, args.blocks, args.arms)
     p.require(args.world_size > 1 or args.arms == ("flux",),
               "--world-size 1 has no reduce-scatter to compare: use --arm flux")
-    p.require(args.selective_mode == "wire",
-              "--selective-mode fp8-mma (block-scaled E4M3 MMA on the selected blocks) is not implemented")
     p.require(args.warmup_steps >= 0 and args.operator_warmup >= 0, "warm-up counts must be non-negative")
     p.require(args.steps > 0 and args.operator_iters > 0 and args.worker_timeout > 0,
               "timing counts and timeout must be positive")

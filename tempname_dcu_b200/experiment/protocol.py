@@ -224,8 +224,12 @@ def expected_schedule(model, world, arm, role_plan=None):
     return out
 
 
-def validate_operator_state(state, row, model, world, role, calls, execution_plan=None):
+def validate_operator_state(state, row, model, world, role, calls, execution_plan=None, selective_mode="wire"):
+    """The operator's own account of a call sequence against the frozen arm
+    contract.  With selective_mode "fp8-mma" the selective arm computes its
+    calibrated blocks as block-scaled FP8 MMAs and sends every block as BF16."""
     shape = role_shape(model, world, role)
+    fp8 = selective_mode == "fp8-mma" and row["arm"] == SELECTIVE
     role_plan = execution_plan["roles"][role] if row["arm"] in (ARRIVAL, SELECTIVE) else None
     sched = expected_schedule(model, world, row["arm"], role_plan)
     mapping_sha = hashlib.sha256(json.dumps(sched, sort_keys=True).encode()).hexdigest()
@@ -235,6 +239,8 @@ def validate_operator_state(state, row, model, world, role, calls, execution_pla
     remote = (world - 1) * per
     elements = model["chunk_rows"] * model["hidden"]
     wires = [q * (elements // 128 * 136) + (remote - q) * elements * 2 for q in selected]
+    if fp8:
+        wires = [remote * elements * 2] * world
     require(state.get("backend") == BACKEND and state.get("arm") == row["arm"] and state.get("rank") == row["rank"],
             "wrong operator backend/arm/rank")
     require(state.get("shape") == shape and state.get("chunk_rows") == model["chunk_rows"],
@@ -242,10 +248,13 @@ def validate_operator_state(state, row, model, world, role, calls, execution_pla
     require(state.get("calls") == calls, f"wrong actual {role} projection call count")
     require(state.get("production_schedule") == sched and state.get("mapping_sha256") == mapping_sha,
             "actual production mapping is not the frozen arm schedule")
+    kernel = "tdb::rs::gemm_rs_mx_kernel" if fp8 else "tdb::rs::gemm_rs_kernel"
     require(state.get("gemms_per_call") == 1 and state.get("collectives_per_call") == 1
-            and state.get("fused_kernel") == "tdb::rs::gemm_rs_kernel", "the operator must be one fused kernel")
-    quant = ("selective_remote_h128_e4m3" if row["arm"] == SELECTIVE else
+            and state.get("fused_kernel") == kernel, "the operator must be one fused kernel")
+    quant = ("selective_mma_e4m3_ue8m0_k32" if fp8 else "selective_remote_h128_e4m3" if row["arm"] == SELECTIVE else
              "none" if row["arm"] == "flux" else "all_remote_h128_e4m3")
+    require(not fp8 or (state.get("selective_mode") == "fp8-mma" and state.get("mma_block_mask") == mask),
+            "the FP8 MMA block mask is not the calibrated selective mask")
     require(state.get("quantization") == quant and state.get("reduction_order") == list(range(world))
             and state.get("rounding") == "bf16_after_each_source", "codec/reduction contract changed")
     require(state.get("remote_wire_bytes_per_source") == wires[row["rank"]]
@@ -350,7 +359,7 @@ def validate_rows(rows, job, config):
                 require(len(states) == 2 * model["layers"], "missing operator state")
                 for index, state in enumerate(states):
                     validate_operator_state(state, row, model, world, "attn" if index % 2 == 0 else "mlp", total,
-                                            config["execution_plan"])
+                                            config["execution_plan"], config.get("selective_mode", "wire"))
             memory = row.get("memory", {})
             require(all(type(memory.get(k)) is int and memory[k] >= 0 for k in
                         ("peak_allocated_bytes", "peak_reserved_bytes")), "missing allocator peak memory")
@@ -375,7 +384,8 @@ def validate_rows(rows, job, config):
                         "missing full-GEMM control timing")
                 validate_operator_state(record.get("execution", {}), row, config["model"], world, record["role"],
                                         2 + int(bool(config["profile"])) + config["timing"]["operator_warmup"]
-                                        + config["timing"]["operator_iterations"], config["execution_plan"])
+                                        + config["timing"]["operator_iterations"], config["execution_plan"],
+                                        config.get("selective_mode", "wire"))
                 profile = record.get("profile")
                 require(bool(profile) == bool(config["profile"]), "requested profile missing/unexpected")
             for key in ("initialization_sha256", "input_sha256"):

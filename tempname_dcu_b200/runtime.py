@@ -437,9 +437,12 @@ class FluxB200:
                     overlap_claim="epilogue peer stores overlap the MMA of later tiles in one kernel") | extra
 
 
-def operator_factory_for(arm, remote_first=True):
+def operator_factory_for(arm, remote_first=True, selective_mode="wire"):
     """Factory for ``GPT(operator_factory=...)``: a FluxB200 per row-parallel
-    projection (training uses the remote-first production order)."""
+    projection (training uses the remote-first production order;
+    ``selective_mode`` applies to the selective arm's forward projections)."""
     def factory(m, n, k, group, arm=arm, chunk_rows=128, plan=None, **kw):
+        if arm.endswith("_selective") and not kw.get("b_mn"):
+            kw.setdefault("selective_mode", selective_mode)
         return FluxB200(m, n, k, group, arm, chunk_rows=chunk_rows, plan=plan, remote_first=remote_first, **kw)
     return factory

@@ -150,6 +150,27 @@ def projection_reference(input_, weight, rank, world, group, quantized, selectio
     return reduce_reference_sources(sources, rank, quantized, selection_mask, chunk_rows)
 
 
+def mx_projection_reference(input_, weight, rank, world, group, fp8_rows):
+    """Reference of the selective arm in fp8-mma mode: the rows of the
+    calibrated blocks as the fp32 product of the dequantized block-scaled FP8
+    operands (quantized by the torch restatement in ops/mx.py, not by the
+    kernel), the other rows as the BF16 product; then the NCCL all-to-all and
+    the ordered BF16 sum."""
+    import torch
+    import torch.distributed as dist
+    from .ops import mx
+    a, ea = mx.quantize_reference(input_.cpu())
+    b, eb = mx.quantize_reference(weight.cpu())
+    deq_a = (a.view(a.shape[0], -1, 32) * torch.exp2(ea.float()).unsqueeze(-1)).view_as(a).to(input_.device)
+    deq_b = (b.view(b.shape[0], -1, 32) * torch.exp2(eb.float()).unsqueeze(-1)).view_as(b).to(input_.device)
+    rows = fp8_rows.bool().repeat_interleave(input_.shape[0] // fp8_rows.numel())[:, None]
+    partial = torch.where(rows, (deq_a @ deq_b.t()).to(torch.bfloat16), input_ @ weight.t()).contiguous()
+    sources = torch.empty_like(partial)
+    dist.all_to_all_single(sources.view(-1), partial.view(-1), group=group)
+    sources = sources.view(world, partial.shape[0] // world, partial.shape[1])
+    return reduce_reference_sources(sources, rank, False)[0]
+
+
 # --------------------------------------------------------------------------
 # stages
 # --------------------------------------------------------------------------
@@ -258,7 +279,7 @@ def _timed(fn, iters, group):
     return float(value.item()), local
 
 
-def arrival_diagnostic(config, arm, role_plan, input_, weight, group):
+def arrival_diagnostic(config, arm, role_plan, input_, weight, group, selective_mode="wire"):
     """Artificial skew: rank 0 delays the signal of the first lane-0 block by
     5e7 cycles; lane-1 blocks consumed before it completes show ready bypass.
     Outputs must stay bitwise equal.  Never part of timed runs."""
@@ -273,7 +294,8 @@ def arrival_diagnostic(config, arm, role_plan, input_, weight, group):
     plan = deepcopy(role_plan)
     plan["arrival_order"] = base_order(m, n, k, world, chunk)
     cycles = 50_000_000
-    probe = FluxB200(m, n, k, group, arm, chunk_rows=chunk, plan=plan, diagnostic_delay_cycles=cycles)
+    probe = FluxB200(m, n, k, group, arm, chunk_rows=chunk, plan=plan, diagnostic_delay_cycles=cycles,
+                     selective_mode=selective_mode)
     probe.validate_next_call = True
     normal = probe.forward(input_, weight).clone()
     delayed, diag = probe.profile_call(input_, weight)
@@ -297,6 +319,7 @@ def operators(config, arm, rank, world, group, out):
     from .runtime import FluxB200
     model, timing = config["model"], config["timing"]
     m, n = model["sequence"] * model["micro_batch"], model["hidden"]
+    mode = config.get("selective_mode", "wire") if arm == ARMS[4] else "wire"
     results, states, hashes = [], [], []
     for role, k in (("attn", model["hidden"] // world), ("mlp", model["ffn"] // world)):
         gen = torch.Generator(device="cuda").manual_seed(config["seed"] + 173 * rank + k)
@@ -305,10 +328,12 @@ def operators(config, arm, rank, world, group, out):
         hashes += [tensor_sha(x), tensor_sha(w)]
         role_plan = config["execution_plan"]["roles"][role] if arm in ARMS[3:] else None
         mask = role_plan["selective_mask"] if arm == ARMS[4] else None
-        op = FluxB200(m, n, k, group, arm, chunk_rows=model["chunk_rows"], plan=role_plan)
+        op = FluxB200(m, n, k, group, arm, chunk_rows=model["chunk_rows"], plan=role_plan, selective_mode=mode)
         op.validate_next_call = True
         output = op.forward(x, w)
         plain, coded = projection_reference(x, w, rank, world, group, arm != "flux", mask, model["chunk_rows"])
+        if mode == "fp8-mma":  # the "codec" reference is the block-scaled FP8 product on the selected blocks
+            coded = mx_projection_reference(x, w, rank, world, group, op.mx["mask"])
         e_plain, e_codec = relative_error(output, plain), relative_error(output, coded)
         require_all(e_plain <= (0.05 if arm != "flux" else 0.01) and e_codec <= 0.01,
                     f"{role} full-shape reference failed: BF16={e_plain}, codec={e_codec}", group)
@@ -317,6 +342,8 @@ def operators(config, arm, rank, world, group, out):
         op.validate_next_call = True
         changed = op.forward(x2, w)
         _, coded2 = projection_reference(x2, w, rank, world, group, arm != "flux", mask, model["chunk_rows"])
+        if mode == "fp8-mma":
+            coded2 = mx_projection_reference(x2, w, rank, world, group, op.mx["mask"])
         e_reuse = relative_error(changed, coded2)
         require_all(torch.equal(output, retained) and e_reuse <= 0.01,
                     f"{role} output lifetime / changed-input reuse failed", group)
@@ -331,10 +358,11 @@ def operators(config, arm, rank, world, group, out):
                 other_plan["arrival_order"] = base_order(m, n, k, world, model["chunk_rows"])
             else:
                 other = "flux_taco" if arm == "flux_taco_interleaved" else "flux_taco_interleaved"
-            control = FluxB200(m, n, k, group, other, chunk_rows=model["chunk_rows"], plan=other_plan)
+            control = FluxB200(m, n, k, group, other, chunk_rows=model["chunk_rows"], plan=other_plan,
+                               selective_mode=mode if other == ARMS[4] else "wire")
             bitwise = torch.equal(control.forward(x, w), retained)
             require_all(bitwise, f"{role} order-only output changed; no fair scheduling ablation", group)
-        diag = arrival_diagnostic(config, arm, role_plan, x, w, group) if arm in ARMS[3:] else None
+        diag = arrival_diagnostic(config, arm, role_plan, x, w, group, mode) if arm in ARMS[3:] else None
         profile = None
         if config.get("profile"):
             _, profile = op.profile_call(x, w)
@@ -414,7 +442,9 @@ def main(argv=None):
             row.update(train_window(config["model"], args.arm, group, config["timing"]["warmup_steps"],
                                     config["timing"]["timed_steps"], seed=config["seed"],
                                     token_seed=config["token_seed"],
-                                    operator_factory=operator_factory_for(args.arm) if world > 1 else None,
+                                    operator_factory=operator_factory_for(
+                                        args.arm, selective_mode=config.get("selective_mode", "wire"))
+                                    if world > 1 else None,
                                     execution_plan=config["execution_plan"] if args.arm in ARMS[3:] else None))
         torch.cuda.synchronize()
         row.update(completed=True, passed=True)

@@ -78,7 +78,7 @@ def test_cli_model_and_arm_flags(tmp_path):
 
 
 @pytest.mark.parametrize("argv", [["--world-size", "1"], ["--world-size", "1", "--arm", "flux", "--operator-only"],
-                                  ["--selective-mode", "fp8-mma"], ["--arm", "nope"], ["--accum", "0"],
+                                  ["--selective-mode", "fp8"], ["--arm", "nope"], ["--accum", "0"],
                                   ["--vocab", "50257"]])
 def test_new_cli_flags_rejected(argv):
     with pytest.raises((ValueError, SystemExit)):
@@ -141,7 +141,7 @@ def _sha(data: bytes):
     return hashlib.sha256(data).hexdigest()
 
 
-def _state(model, world, rank, arm, role, calls, plan_bundle):
+def _state(model, world, rank, arm, role, calls, plan_bundle, selective_mode="wire"):
     m = model["sequence"] * model["micro_batch"]
     k = (model["hidden"] if role == "attn" else model["ffn"]) // world
     role_plan = plan_bundle["roles"][role] if arm in (p.ARRIVAL, p.SELECTIVE) else None
@@ -162,7 +162,17 @@ def _state(model, world, rank, arm, role, calls, plan_bundle):
                 plan_sha256=p.digest(role_plan) if role_plan is not None else None, reduction_order=list(range(world)),
                 rounding="bf16_after_each_source", scratch_bytes=1, original_cuda_flux=False, transport_lanes=2,
                 consumer_policy=lay["consumer_policy"], validation_calls=2, diagnostic_delay_cycles=0,
-                diagnostic_delay_in_normal_forward=False)
+                diagnostic_delay_in_normal_forward=False) | _fp8_fields(model, world, arm, lay, selective_mode)
+
+
+def _fp8_fields(model, world, arm, lay, selective_mode):
+    if selective_mode != "fp8-mma" or arm != p.SELECTIVE:
+        return {}
+    per = model["sequence"] * model["micro_batch"] // world // model["chunk_rows"]
+    bf16 = (world - 1) * per * model["chunk_rows"] * model["hidden"] * 2
+    return dict(selective_mode="fp8-mma", mma_block_mask=lay["selection_mask"], fused_kernel="tdb::rs::gemm_rs_mx_kernel",
+                quantization="selective_mma_e4m3_ue8m0_k32", remote_wire_bytes_by_source=[bf16] * world,
+                remote_wire_bytes_per_source=bf16, actual_remote_wire_bytes_per_rank=bf16)
 
 
 def _diag(config, arm):
@@ -253,7 +263,7 @@ def _fixture(tmp_path, extra=()):
                                         full_gemm_only_seconds=0.0005, profile=None,
                                         arrival_diagnostic=_diag(config, job["arm"]),
                                         execution=_state(model, world, row["rank"], job["arm"], role, calls,
-                                                         execution_plan)))
+                                                         execution_plan, config.get("selective_mode", "wire"))))
                 row.update(operator_results=results, initialization_sha256="a" * 64, input_sha256="b" * 64)
         for row in rows:
             p.write(directory / f"rank{row['rank']}.json", row)
@@ -286,6 +296,20 @@ def test_replay_accepts_an_arm_subset(tmp_path):
     plan = json.loads((out / "plan.json").read_text())
     plan["arms"] = list(p.ARMS)  # a widened arm list no longer matches the frozen job list
     p.write(out / "plan.json", plan)
+    with pytest.raises(ValueError):
+        R.replay(out)
+
+
+def test_replay_checks_the_fp8_mma_selective_contract(tmp_path):
+    out = _fixture(tmp_path, ["--selective-mode", "fp8-mma"])
+    report = R.replay(out)
+    assert report["completed"]
+    sel = next(j["directory"] for j in json.loads((out / "plan.json").read_text())["jobs"]
+               if j["stage"] == "operator" and j["arm"] == p.SELECTIVE)
+
+    def wire_mode(row):  # a selective operator that still sent TACO packets breaks the fp8-mma contract
+        row["operator_results"][0]["execution"]["fused_kernel"] = "tdb::rs::gemm_rs_kernel"
+    _retamper(out, sel, 0, wire_mode)
     with pytest.raises(ValueError):
         R.replay(out)
 
