@@ -35,10 +35,13 @@ struct Config {
   // block-scaled FP8 stages also carry the scale atoms of A (512 B) and B (BN*4 B)
   static constexpr int kSfBytes = MX ? (512 + BN * 4 + 1023) / 1024 * 1024 : 0;
   static constexpr int kStageBytes = kABytes + kBBytes + kSfBytes;
-  // TMEM: two accumulators of BN columns, then (FP8) a ring of scale columns
+  // TMEM: accumulators of BN columns (two, so the epilogue of a tile overlaps
+  // the next tile's MMAs; one for 256-wide FP8 tiles, whose scale ring would
+  // not fit beside two), then (FP8) a ring of scale columns per stage
   static constexpr int kSfCols = 4 + BN / 32;
+  static constexpr int kAccums = (MX && BN > 128) ? 1 : 2;
   static constexpr int kTmemCols = (MX || 2 * BN > 256) ? 512 : 256;
-  static_assert(!MX || (BN % 128 == 0 && 2 * BN + STAGES * kSfCols <= 512), "FP8 scale ring does not fit TMEM");
+  static_assert(!MX || (BN % 128 == 0 && kAccums * BN + STAGES * kSfCols <= 512), "FP8 scale ring does not fit TMEM");
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
@@ -254,8 +257,8 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
       bool ok = true;
       bool issued = false;
       for (int i = blockIdx.x; i < order.num_tiles && ok; i += gridDim.x, ++tc) {
-        const int b = tc & 1;
-        const uint32_t use = tc >> 1;
+        const int b = Cfg::kAccums == 2 ? (tc & 1) : 0;
+        const uint32_t use = Cfg::kAccums == 2 ? uint32_t(tc >> 1) : uint32_t(tc);
         if (!mbar_wait(&bars->tmem_empty[b], (use & 1) ^ 1, status, 20)) { ok = false; *abort_flag = 1; break; }
         tc_fence_after();
         const uint32_t dcol = tmem_base + b * BN;
@@ -278,7 +281,7 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
             if (fp8) {
               // scales: smem atoms -> TMEM columns of this stage, then four K = 32 MMAs
               const uint32_t sf = sb + Cfg::kBBytes;
-              const uint32_t sfa_col = tmem_base + 2 * BN + s * Cfg::kSfCols;
+              const uint32_t sfa_col = tmem_base + Cfg::kAccums * BN + s * Cfg::kSfCols;
               const uint32_t sfb_col = sfa_col + 4;
               tmem_cp_32x128b_x4(sfa_col, smem_desc_plain(sf, 0, 128));
 #pragma unroll
@@ -320,8 +323,8 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
     for (int i = blockIdx.x; i < order.num_tiles; i += gridDim.x, ++tc) {
       int mb, nb;
       order.tile(i, mb, nb);
-      const int b = tc & 1;
-      const uint32_t use = tc >> 1;
+      const int b = Cfg::kAccums == 2 ? (tc & 1) : 0;
+      const uint32_t use = Cfg::kAccums == 2 ? uint32_t(tc >> 1) : uint32_t(tc);
       bool ok = mbar_wait(&bars->tmem_full[b], use & 1, status, 30);
       if (*abort_flag) ok = false;
       if (!ok) { *abort_flag = 1; break; }

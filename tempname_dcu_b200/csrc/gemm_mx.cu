@@ -21,8 +21,11 @@ namespace tdb {
 namespace gemm {
 namespace mx {
 
-constexpr int kStages = 5;
-constexpr int kBN = 128;
+// 256-wide tiles (one TMEM accumulator, three stages) when N allows: at 128
+// columns a K = 32 FP8 MMA reads as many shared-memory bytes per clock as the
+// SM delivers, so only the wider tile lets FP8 outrun BF16.
+template <int BN>
+constexpr int kStagesFor = BN == 256 ? 3 : 5;
 
 // Round-to-nearest-even, saturating fp32 pair -> e4m3 pair (low byte = lo).
 __device__ __forceinline__ uint16_t e4m3x2(float lo, float hi) {
@@ -73,24 +76,24 @@ __global__ void __launch_bounds__(256) quantize_kernel(const uint16_t* __restric
   sf[atom * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + j] = uint8_t(e + 127);
 }
 
-template <int MODE>
+template <int BN, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int K,
                    TileOrder order, const __grid_constant__ EpiParams ep, const uint8_t* sfa, const uint8_t* sfb,
                    int a_blocks, int b_blocks, int* status) {
   typename EpiFor<MODE>::type epi{ep};
   MxOperands mxo{&tmA, &tmB, sfa, sfb, a_blocks, b_blocks, nullptr};
-  gemm_mainloop<kBN, false, false, typename EpiFor<MODE>::type, kStages, true>(&tmA, &tmB, K, order, epi, status,
-                                                                              &mxo);
+  gemm_mainloop<BN, false, false, typename EpiFor<MODE>::type, kStagesFor<BN>, true>(&tmA, &tmB, K, order, epi,
+                                                                                    status, &mxo);
 }
 
-template <int MODE>
+template <int BN, int MODE>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiParams& ep,
                   const uint8_t* sfa, const uint8_t* sfb, cudaStream_t stream) {
-  using Cfg = Config<kBN, kStages, true>;
+  using Cfg = Config<BN, kStagesFor<BN>, true>;
   constexpr int kSmem = Cfg::kSmemBytes + EpiFor<MODE>::type::kSmemBytes;
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
-  auto kern = gemm_mx_kernel<MODE>;
+  auto kern = gemm_mx_kernel<BN, MODE>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -101,7 +104,7 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, in
   }
   TileOrder order;
   order.num_m = M / BM;
-  order.num_n = N / kBN;
+  order.num_n = N / BN;
   order.group_m = 16;
   order.table = nullptr;
   order.num_tiles = order.num_m * order.num_n;
@@ -156,7 +159,8 @@ TDB_API int tdb_gemm_mx(const void* A, const void* sfa, const void* B, const voi
   CUtensorMap ta, tb;
   int rc = make_fp8_map(&ta, A, M, K, BM);
   if (rc) return rc;
-  rc = make_fp8_map(&tb, B, N, K, mx::kBN);
+  const bool wide = N % 256 == 0;
+  rc = make_fp8_map(&tb, B, N, K, wide ? 256 : 128);
   if (rc) return rc;
   EpiParams ep;
   ep.C = C;
@@ -176,9 +180,15 @@ TDB_API int tdb_gemm_mx(const void* A, const void* sfa, const void* B, const voi
     rc = tdb_host::make_tmap_2d(&ep.tmC, C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, uint64_t(N), uint64_t(M),
                                 uint64_t(ldc), 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    return mode == kBias ? mx::launch<kTmaBase + kBias>(ta, tb, M, N, K, ep, a_sf, b_sf, s)
-                         : mx::launch<kTmaBase + kStore>(ta, tb, M, N, K, ep, a_sf, b_sf, s);
+    if (wide)
+      return mode == kBias ? mx::launch<256, kTmaBase + kBias>(ta, tb, M, N, K, ep, a_sf, b_sf, s)
+                           : mx::launch<256, kTmaBase + kStore>(ta, tb, M, N, K, ep, a_sf, b_sf, s);
+    return mode == kBias ? mx::launch<128, kTmaBase + kBias>(ta, tb, M, N, K, ep, a_sf, b_sf, s)
+                         : mx::launch<128, kTmaBase + kStore>(ta, tb, M, N, K, ep, a_sf, b_sf, s);
   }
-  return mode == kBias ? mx::launch<kBias>(ta, tb, M, N, K, ep, a_sf, b_sf, s)
-                       : mx::launch<kStore>(ta, tb, M, N, K, ep, a_sf, b_sf, s);
+  if (wide)
+    return mode == kBias ? mx::launch<256, kBias>(ta, tb, M, N, K, ep, a_sf, b_sf, s)
+                         : mx::launch<256, kStore>(ta, tb, M, N, K, ep, a_sf, b_sf, s);
+  return mode == kBias ? mx::launch<128, kBias>(ta, tb, M, N, K, ep, a_sf, b_sf, s)
+                       : mx::launch<128, kStore>(ta, tb, M, N, K, ep, a_sf, b_sf, s);
 }

@@ -600,20 +600,22 @@ __global__ void __launch_bounds__(kReduceThreads, 2)
 // Producer for the selective arm's block-scaled FP8 mode: the tiles of the
 // calibrated blocks (mx.on(m block)) run as kind::mxf8f6f4 MMAs on e4m3
 // operands, the rest as bf16; every tile is pushed as bf16.
-constexpr int kMxStages = 5;
+template <int BN>
+constexpr int kMxStages = BN == 256 ? 3 : 5;
 
+template <int BN>
 __global__ void __launch_bounds__(gemm::kThreads, 1)
     gemm_rs_mx_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmA8, const __grid_constant__ CUtensorMap tmB8, int K,
                       gemm::TileOrder order, const __grid_constant__ Params p, const uint8_t* sfa, const uint8_t* sfb,
                       int a_blocks, int b_blocks, const uint8_t* mx_mask, int* status) {
-  PushEpi<128> epi;
+  PushEpi<BN> epi;
   epi.p = &p;
   epi.status = status;
   gemm::MxOperands mx{&tmA8, &tmB8, sfa, sfb, a_blocks, b_blocks, mx_mask};
   unsigned long long* ph = p.phases ? p.phases + 4 * blockIdx.x : nullptr;
   if (ph && threadIdx.x == 0) ph[0] = globaltimer();
-  gemm::gemm_mainloop<128, false, false, PushEpi<128>, kMxStages, true>(&tmA, &tmB, K, order, epi, status, &mx);
+  gemm::gemm_mainloop<BN, false, false, PushEpi<BN>, kMxStages<BN>, true>(&tmA, &tmB, K, order, epi, status, &mx);
   signal_tiles(p, order);
   if (ph && threadIdx.x == 0) ph[1] = globaltimer();
 }
@@ -643,22 +645,23 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int K, const gem
   return launch_consumer(p, stream);
 }
 
+template <int BN>
 static int launch_mx(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta8, const CUtensorMap& tb8,
                      int K, const gemm::TileOrder& order, const Params& p, const uint8_t* sfa, const uint8_t* sfb,
                      const uint8_t* mx_mask, int grid, cudaStream_t stream) {
-  using Cfg = gemm::Config<128, kMxStages, true>;
-  constexpr int kSmem = Cfg::kSmemBytes + PushEpi<128>::kSmemBytes;
+  using Cfg = gemm::Config<BN, kMxStages<BN>, true>;
+  constexpr int kSmem = Cfg::kSmemBytes + PushEpi<BN>::kSmemBytes;
   static_assert(kSmem <= 227 * 1024, "fused FP8 GEMM-RS shared memory budget");
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_rs_mx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_rs_mx_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs_mx: cudaFuncSetAttribute failed");
     attr[dev & 63] = true;
   }
-  gemm_rs_mx_kernel<<<grid, gemm::kThreads, kSmem, stream>>>(ta, tb, ta8, tb8, K, order, p, sfa, sfb, p.m / 128,
-                                                              p.N / 128, mx_mask, tdb_host::status_ptr());
+  gemm_rs_mx_kernel<BN><<<grid, gemm::kThreads, kSmem, stream>>>(ta, tb, ta8, tb8, K, order, p, sfa, sfb, p.m / 128,
+                                                                  p.N / 128, mx_mask, tdb_host::status_ptr());
   tdb_host::launched(1);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs_mx: producer launch failed");
@@ -774,16 +777,18 @@ static int gemm_rs_impl(const void* A, int64_t lda, const void* B, int b_mn, int
   const int grid = order.num_tiles < sms ? order.num_tiles : sms;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (mx) {
-    if (bn != 128 || b_mn || K % 128 || !mx->a8 || !mx->b8 || !mx->sfa || !mx->sfb || !mx->mask ||
+    if (b_mn || K % 128 || !mx->a8 || !mx->b8 || !mx->sfa || !mx->sfb || !mx->mask ||
         (reinterpret_cast<uintptr_t>(mx->sfa) | reinterpret_cast<uintptr_t>(mx->sfb)) % 16)
-      return tdb_host::fail(int(cudaErrorInvalidValue), "gemm_rs_mx: needs bn 128, K-major B, K %% 128, aligned scales");
+      return tdb_host::fail(int(cudaErrorInvalidValue), "gemm_rs_mx: needs a K-major B, K %% 128, aligned scales");
     CUtensorMap ta8, tb8;
     rc = gemm::make_fp8_map(&ta8, mx->a8, m, K, rs::BM);
     if (rc) return rc;
-    rc = gemm::make_fp8_map(&tb8, mx->b8, N, K, 128);
+    rc = gemm::make_fp8_map(&tb8, mx->b8, N, K, bn);
     if (rc) return rc;
-    return rs::launch_mx(ta, tb, ta8, tb8, K, order, p, static_cast<const uint8_t*>(mx->sfa),
-                         static_cast<const uint8_t*>(mx->sfb), mx->mask, grid, s);
+    const uint8_t* sa = static_cast<const uint8_t*>(mx->sfa);
+    const uint8_t* sb = static_cast<const uint8_t*>(mx->sfb);
+    return bn == 256 ? rs::launch_mx<256>(ta, tb, ta8, tb8, K, order, p, sa, sb, mx->mask, grid, s)
+                     : rs::launch_mx<128>(ta, tb, ta8, tb8, K, order, p, sa, sb, mx->mask, grid, s);
   }
   if (bn == 256) return b_mn ? rs::launch<256, true>(ta, tb, K, order, p, grid, s)
                              : rs::launch<256, false>(ta, tb, K, order, p, grid, s);
@@ -806,7 +811,7 @@ TDB_API int tdb_gemm_rs(const void* A, int64_t lda, const void* B, int b_mn, int
 
 // tdb_gemm_rs whose tiles in the m blocks flagged by mx_mask run as
 // block-scaled FP8 MMAs on a8 / b8 (e4m3 copies of A and B, scale atoms
-// sfa / sfb from tdb_mx_quantize).  bn 128, B K-major, K % 128 == 0.
+// sfa / sfb from tdb_mx_quantize).  B K-major, K % 128 == 0.
 TDB_API int tdb_gemm_rs_mx(const void* A, int64_t lda, const void* B, int b_mn, int64_t ldb, int m, int N, int K,
                            int bn, const int* tile_table, const uint64_t* peers, int W, int rank, int chunk_rows,
                            uint64_t recv_off, uint64_t slot_bytes, uint64_t flags_off, int set, unsigned int expected,

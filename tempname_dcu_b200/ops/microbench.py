@@ -244,7 +244,7 @@ def main(argv=None):
     q.add_argument("M", type=int)
     q.add_argument("N", type=int)
     q.add_argument("K", type=int)
-    q.add_argument("--mode", default="fwd", choices=("fwd", "dgrad", "wgrad"))
+    q.add_argument("--mode", default="fwd", choices=("fwd", "dgrad", "wgrad", "mx"))
     q.add_argument("--launches", type=int, default=3)
     r = sub.add_parser("attn")
     r.add_argument("--mb", type=int, default=1)
@@ -279,6 +279,17 @@ def main(argv=None):
                 M, N, K, *kind = item.split(",")
                 shapes.append((item, int(M), int(N), int(K), kind[0] if kind else "fwd"))
         bench_gemm(shapes, args.iters)
+    elif args.mode == "mx":
+        import torch
+        from . import mx
+        x = torch.randn(args.M, args.K, device="cuda").to(torch.bfloat16)
+        w = torch.randn(args.N, args.K, device="cuda").to(torch.bfloat16)
+        qa, sfa = mx.quantize(x)
+        qb, sfb = mx.quantize(w)
+        out = torch.empty(args.M, args.N, dtype=torch.bfloat16, device="cuda")
+        for _ in range(args.launches):
+            mx.gemm(qa, sfa, qb, sfb, out=out)
+        torch.cuda.synchronize()
     else:
         import torch
         from . import gemm

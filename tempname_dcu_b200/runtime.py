@@ -163,10 +163,9 @@ class FluxB200:
         import torch
         if selective_mode not in ("wire", "fp8-mma"):
             raise ValueError("selective_mode must be 'wire' or 'fp8-mma'")
-        if selective_mode == "fp8-mma" and (not arm.endswith("_selective") or b_mn or tile_n not in (None, 128)
-                                            or k % 128 or m % 128 or n % 128):
-            raise ValueError("fp8-mma runs the selective arm with a K-major weight, 128-wide tiles and "
-                             "m, n, k multiples of 128")
+        if selective_mode == "fp8-mma" and (not arm.endswith("_selective") or b_mn or tile_n not in (None, 128, 256)
+                                            or k % 128 or m % 128 or n % 128 or (tile_n == 256 and n % 256)):
+            raise ValueError("fp8-mma runs the selective arm with a K-major weight and m, n, k multiples of 128")
         self.selective_mode = selective_mode
         if type(diagnostic_delay_cycles) is not int or not 0 <= diagnostic_delay_cycles <= 100_000_000:
             raise ValueError("diagnostic_delay_cycles must be an integer in [0, 100000000]")
@@ -196,7 +195,10 @@ class FluxB200:
         self.selection = selection_statistics(m, n, self.world, chunk_rows, self.selection_mask)
         # Tile width: every rank derives it from the shape alone.
         sms = native.lib().tdb_sm_count(torch.cuda.current_device())
-        self.bn = tile_n or (256 if (m // 128) * (n // 256) >= sms and selective_mode == "wire" else 128)
+        if selective_mode == "fp8-mma":  # FP8 outruns BF16 only with 256-wide tiles
+            self.bn = tile_n or (256 if n % 256 == 0 else 128)
+        else:
+            self.bn = tile_n or (256 if (m // 128) * (n // 256) >= sms else 128)
         self.remote_first = bool(remote_first) and arm not in ARRIVAL_ARMS
         if self.remote_first:
             self.tiles = tiles_for_order(remote_first_order(self.order, self.world, self.rank), n, chunk_rows,
@@ -292,9 +294,14 @@ class FluxB200:
             else:
                 from .ops import mx as _mx
                 q = self.mx
-                # the operands change every call (activations) or step (weights): quantize both
+                # activations change every call; the weight once per optimizer step: in eager mode its
+                # quantized copy is reused while the tensor is unmodified (same storage, same version);
+                # a captured graph re-quantizes on every replay
                 _mx.quantize(input_, q["a8"], q["sfa"])
-                _mx.quantize(weight, q["b8"], q["sfb"])
+                key = (weight.data_ptr(), weight._version)
+                if torch.cuda.is_current_stream_capturing() or q.get("weight_key") != key:
+                    _mx.quantize(weight, q["b8"], q["sfb"])
+                    q["weight_key"] = None if torch.cuda.is_current_stream_capturing() else key
                 native.check(lib.tdb_gemm_rs_mx(*args, q["a8"].data_ptr(), q["sfa"].data_ptr(), q["b8"].data_ptr(),
                                                 q["sfb"].data_ptr(), q["mask"].data_ptr(), stream),
                              "fused gemm_rs (block-scaled fp8)")
