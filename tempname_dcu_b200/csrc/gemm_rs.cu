@@ -38,6 +38,7 @@
 // consumers, ordered BF16 source reduction, final join) and
 // src/taco/codec.hip:78-148 (codec math, ordered reduce).
 #include <climits>
+#include <utility>
 
 #include "codec.cuh"
 #include "gemm.cuh"
@@ -71,6 +72,12 @@ struct Params {
   // written by rs_advance_kernel before each call; when present it replaces
   // `set` / `expected`, so a captured CUDA graph replays with fresh values
   const uint32_t* call_state;
+  // bit 0: every epilogue warp signals its tile right after pushing it (one
+  //        system fence per warp and tile) instead of one fence per CTA after
+  //        its whole produce phase;
+  // bit 1: the consumer runs inside the producer kernel (cooperative launch,
+  //        every CTA resident), each CTA reducing blocks once it has produced.
+  int variant;
 };
 
 __device__ __forceinline__ int call_set(const Params& p) { return p.call_state ? int(__ldg(p.call_state)) : p.set; }
@@ -268,8 +275,21 @@ struct PushEpi {
     if (cl == 3) push_half(c >> 2);
   }
 
-  __device__ __forceinline__ void tile_end(int, int, int, int) {
-    // Signals are issued once per CTA after the produce phase (signal_tiles).
+  __device__ __forceinline__ void tile_end(int mb, int nb, int, int lane) {
+    // Variant bit 0: this warp's 32 rows of the tile are complete at the
+    // destination once its stores are visible -- fence, then add 1 (four
+    // warps make the 4 per tile that signal_tiles adds otherwise).
+    if (!(p->variant & 1)) return;
+    __syncwarp();
+    if (lane == 0) {
+      if (p->delay_cycles > 0 && mb == p->delay_mb && nb == p->delay_nb) {
+        const long long t0 = clock64();
+        while (clock64() - t0 < p->delay_cycles) {
+        }
+      }
+      __threadfence_system();
+      red_release_sys(flag_ptr(*p, dest, within, p->rank), 1u);
+    }
   }
 };
 
@@ -278,6 +298,7 @@ struct PushEpi {
 // (block, source) counter of every tile it produced, in production order.
 // The diagnostic delay holds back the signal of one tile only.
 __device__ void signal_tiles(const Params& p, const gemm::TileOrder& order) {
+  if (p.variant & 1) return;  // signalled per tile by the epilogue warps
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x != 0) return;
@@ -573,6 +594,10 @@ __global__ void __launch_bounds__(gemm::kThreads, 1)
   gemm::gemm_mainloop<BN, false, B_MN, PushEpi<BN>, kStagesFor<BN>>(&tmA, &tmB, K, order, epi, status);
   signal_tiles(p, order);
   if (ph && threadIdx.x == 0) ph[1] = globaltimer();
+  if (p.variant & 2) {
+    consume_phase(p, status);
+    if (ph && threadIdx.x == 0) ph[3] = globaltimer();
+  }
 }
 
 // Consumer kernel: launched right after the producer on the same stream, at
@@ -618,9 +643,42 @@ __global__ void __launch_bounds__(gemm::kThreads, 1)
   gemm::gemm_mainloop<BN, false, false, PushEpi<BN>, kMxStages<BN>, true>(&tmA, &tmB, K, order, epi, status, &mx);
   signal_tiles(p, order);
   if (ph && threadIdx.x == 0) ph[1] = globaltimer();
+  if (p.variant & 2) {
+    consume_phase(p, status);
+    if (ph && threadIdx.x == 0) ph[3] = globaltimer();
+  }
 }
 
 static int launch_consumer(const Params& p, cudaStream_t stream);
+
+// Producer launch: plain, or cooperative (all CTAs co-resident, grid capped
+// at the resident count) when the consumer runs inside it (variant bit 1),
+// in which case no separate consumer kernel follows.
+template <class... KArgs, class... Args>
+static int launch_producer(void (*kern)(KArgs...), int smem, int grid, const Params& p, cudaStream_t stream,
+                           const char* what, Args&&... args) {
+  const bool coop = (p.variant & 2) != 0;
+  if (coop) {
+    int nb = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, gemm::kThreads, smem);
+    if (e != cudaSuccess || nb <= 0) return tdb_host::fail(int(e), "%s: no resident CTA possible", what);
+    if (grid > nb * tdb_host::sm_count()) grid = nb * tdb_host::sm_count();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(gemm::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = coop ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  tdb_host::launched(1);
+  if (e != cudaSuccess) return tdb_host::fail(int(e), "%s: producer launch failed", what);
+  return coop ? 0 : launch_consumer(p, stream);
+}
 
 template <int BN, bool B_MN>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int K, const gemm::TileOrder& order, const Params& p,
@@ -638,11 +696,7 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int K, const gem
     attr[dev & 63] = true;
   }
   int* status = tdb_host::status_ptr();
-  kern<<<grid, gemm::kThreads, kSmem, stream>>>(ta, tb, K, order, p, status);
-  tdb_host::launched(1);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs: producer launch failed");
-  return launch_consumer(p, stream);
+  return launch_producer(kern, kSmem, grid, p, stream, "gemm_rs", ta, tb, K, order, p, status);
 }
 
 template <int BN>
@@ -660,12 +714,9 @@ static int launch_mx(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
     if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs_mx: cudaFuncSetAttribute failed");
     attr[dev & 63] = true;
   }
-  gemm_rs_mx_kernel<BN><<<grid, gemm::kThreads, kSmem, stream>>>(ta, tb, ta8, tb8, K, order, p, sfa, sfb, p.m / 128,
-                                                                  p.N / 128, mx_mask, tdb_host::status_ptr());
-  tdb_host::launched(1);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return tdb_host::fail(int(e), "gemm_rs_mx: producer launch failed");
-  return launch_consumer(p, stream);
+  int* status = tdb_host::status_ptr();
+  return launch_producer(gemm_rs_mx_kernel<BN>, kSmem, grid, p, stream, "gemm_rs_mx", ta, tb, ta8, tb8, K, order, p,
+                         sfa, sfb, p.m / 128, p.N / 128, mx_mask, status);
 }
 
 static int launch_consumer(const Params& p, cudaStream_t stream) {
@@ -708,6 +759,9 @@ using namespace tdb;
 // tile_table: [num_tiles] production order (m_tile * (N / bn) + n_tile).
 namespace tdb {
 namespace rs {
+// Default 0; see Params::variant.  Set with tdb_rs_set_variant (tuning).
+static int g_variant = 0;
+
 struct MxArgs {
   const void* a8;
   const void* sfa;
@@ -773,6 +827,7 @@ static int gemm_rs_impl(const void* A, int64_t lda, const void* B, int b_mn, int
   p.wait_ns = uint64_t(wait_seconds * 1e9);
   p.phases = phases;
   p.call_state = call_state;
+  p.variant = g_variant;
   const int sms = tdb_host::sm_count();
   const int grid = order.num_tiles < sms ? order.num_tiles : sms;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -824,6 +879,15 @@ TDB_API int tdb_gemm_rs_mx(const void* A, int64_t lda, const void* B, int b_mn, 
   return rs::gemm_rs_impl(A, lda, B, b_mn, ldb, m, N, K, bn, tile_table, peers, W, rank, chunk_rows, recv_off,
                           slot_bytes, flags_off, set, expected, qmask, out, bias, residual, consume, policy, timeline,
                           delay_cycles, delay_mb, delay_nb, wait_seconds, phases, call_state, &mx, stream);
+}
+
+// Select the fused GEMM-RS signalling / consumer variant of the following
+// calls (bit 0 per-tile signals, bit 1 consumer inside the producer kernel);
+// returns the previous value.  Every rank must use the same variant.
+TDB_API int tdb_rs_set_variant(int variant) {
+  const int old = rs::g_variant;
+  if (variant >= 0 && variant <= 3) rs::g_variant = variant;
+  return old;
 }
 
 // Advance the device call state {set, expected, epoch, target0, target1}

@@ -34,6 +34,8 @@ def main(argv=None):
     ap.add_argument("--arms", default="all")
     ap.add_argument("--remote-first", action="store_true", help="produce remote-bound blocks first (training order)")
     ap.add_argument("--tile-n", type=int, default=0, help="fused kernel tile width (128 or 256; 0 = automatic)")
+    ap.add_argument("--variant", type=int, default=None, choices=(0, 1, 2, 3),
+                    help="fused GEMM-RS variant (bit 0 per-tile signals, bit 1 in-kernel consumer)")
     ap.add_argument("--selective-mode", default="wire", choices=("wire", "fp8-mma"),
                     help="fp8-mma: the selective arm computes every block as block-scaled FP8 (BF16 on the wire)")
     args = ap.parse_args(argv)
@@ -47,7 +49,9 @@ def main(argv=None):
     group = dist.group.WORLD
     from ..mapping import ARMS, wire_bytes
     from ..planning import make_role
-    from ..runtime import FluxB200, shutdown_context
+    from ..runtime import FluxB200, set_rs_variant, shutdown_context
+    if args.variant is not None:
+        set_rs_variant(args.variant)
     from . import gemm as G
     from . import kernels as K
     from . import native
@@ -104,7 +108,7 @@ def main(argv=None):
             quant = op.quantized and mode == "wire"
             link_us = wire_bytes(m, n, world, quant) / (NVLINK_GBS * 1e9) * 1e6
             roof = max(compute_us / (2.0 if mode == "fp8-mma" else 1.0), link_us)
-            rows.append(dict(role=role, arm=arm, selective_mode=mode, world=world, m=m, n=n, k=k, fused_us=round(us, 2),
+            rows.append(dict(role=role, arm=arm, selective_mode=mode, variant=args.variant, world=world, m=m, n=n, k=k, fused_us=round(us, 2),
                              gemm_plus_nccl_rs_us=round(base_us, 2), gemm_only_us=round(gemm_us, 2),
                              speedup_vs_nccl=round(base_us / us, 3), roofline_us=round(roof, 2),
                              roofline_fraction=round(roof / us, 3), bound="link" if link_us > compute_us else "compute",

@@ -41,6 +41,17 @@ native.register("tdb_gemm_rs", [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p
 native.register("tdb_gemm_rs_mx", list(native.SIGNATURES["tdb_gemm_rs"][:-1])
                 + [ctypes.c_void_p] * 5 + [ctypes.c_void_p])
 native.register("tdb_rs_advance", [ctypes.c_void_p, ctypes.c_uint, ctypes.c_void_p])
+native.register("tdb_rs_set_variant", [ctypes.c_int])
+
+
+def set_rs_variant(variant):
+    """Signalling / consumer variant of the following fused GEMM-RS calls on
+    this process (bit 0: per-tile signals; bit 1: consumer inside the
+    producer kernel).  Results are bitwise the same for every variant; all
+    ranks must use the same one.  Returns the previous variant."""
+    if variant not in (0, 1, 2, 3):
+        raise ValueError("variant must be 0..3")
+    return int(native.lib().tdb_rs_set_variant(int(variant)))
 native.register("tdb_gemm_rs_signals_per_block", [ctypes.c_int, ctypes.c_int, ctypes.c_int])
 
 _CONTEXTS = {}

@@ -72,6 +72,16 @@ def _worker(rank, world, init_file, result_path):
                 c_d=bool(torch.equal(outputs[ARMS[2]], outputs[ARMS[3]])))
             rf = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, remote_first=True).forward(x, w)
             out[f"bitwise.k{k}"]["remote_first"] = bool(torch.equal(rf, outputs[ARMS[0]]))
+            # signalling / consumer variants reduce in the same order: bitwise equal
+            from tempname_dcu_b200.runtime import set_rs_variant
+            for variant in (1, 2, 3):
+                set_rs_variant(variant)
+                for arm, plan in ((ARMS[0], None), (ARMS[1], None), (ARMS[4], plan_e)):
+                    yv = FluxB200(m, n, k, group, arm, chunk_rows=chunk, plan=plan).forward(x, w)
+                    torch.cuda.synchronize()
+                    native.raise_on_status()
+                    out[f"bitwise.k{k}"][f"variant{variant}.{arm}"] = bool(torch.equal(yv, outputs[arm]))
+            set_rs_variant(0)
             plan_e_base = dict(plan_e, arrival_order=base_order(m, n, k, world, chunk))
             ebase = FluxB200(m, n, k, group, ARMS[4], chunk_rows=chunk, plan=plan_e_base).forward(x, w)
             out[f"bitwise.k{k}"]["e_ebase"] = bool(torch.equal(ebase, outputs[ARMS[4]]))
