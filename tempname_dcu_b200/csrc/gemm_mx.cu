@@ -45,9 +45,13 @@ __device__ __forceinline__ int block_exponent(float amax) {
   return e < -127 ? -127 : (e > 127 ? 127 : e);
 }
 
-// One thread per (row, 32-value K block).
+// One thread per (row, 32-value K block).  With `version` set the whole
+// kernel is skipped while *version == *seen (the operand has not changed
+// since it was last quantized); mark_kernel then records the version.
 __global__ void __launch_bounds__(256) quantize_kernel(const uint16_t* __restrict__ x, int64_t ldx, int rows, int K,
-                                                       uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+                                                       uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
+                                                       const int* version, const int* seen) {
+  if (version && __ldg(version) == *seen) return;
   const int64_t blocks_per_row = K / 32;
   const int64_t id = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (id >= int64_t(rows) * blocks_per_row) return;
@@ -75,6 +79,8 @@ __global__ void __launch_bounds__(256) quantize_kernel(const uint16_t* __restric
   const int64_t atom = int64_t(kc) * (rows / 128) + r / 128;
   sf[atom * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + j] = uint8_t(e + 127);
 }
+
+__global__ void mark_kernel(const int* version, int* seen) { *seen = *version; }
 
 template <int BN, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -134,15 +140,29 @@ TDB_API long long tdb_mx_scale_bytes(long long rows, long long K) { return rows 
 
 // x bf16 [rows, K] (row stride ldx) -> q e4m3 [rows, K] (dense) and scale
 // atoms sf (tdb_mx_scale_bytes).  rows and K multiples of 128.
-TDB_API int tdb_mx_quantize(const void* x, long long ldx, int rows, int K, void* q, void* sf, void* stream) {
+// With version / seen (device int32 scalars, or both null): quantize only
+// when *version differs from *seen, then set *seen = *version -- e.g. a
+// weight re-quantized once per optimizer step, also under CUDA graph replay.
+TDB_API int tdb_mx_quantize_versioned(const void* x, long long ldx, int rows, int K, void* q, void* sf,
+                                      const int* version, int* seen, void* stream) {
   if (!x || !q || !sf || rows <= 0 || K <= 0 || rows % 128 || K % 128 || ldx % 8 ||
-      reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(q) % 16)
+      reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(q) % 16 || (!version != !seen))
     return tdb_host::fail(int(cudaErrorInvalidValue), "mx_quantize: rows and K must be multiples of 128, 16-byte rows");
   const int64_t n = int64_t(rows) * (K / 32);
-  mx::quantize_kernel<<<unsigned((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t*>(x), ldx, rows, K, static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  mx::quantize_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(static_cast<const uint16_t*>(x), ldx, rows, K,
+                                                                 static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf),
+                                                                 version, seen);
   tdb_host::launched(1);
+  if (version) {
+    mx::mark_kernel<<<1, 1, 0, s>>>(version, seen);
+    tdb_host::launched(1);
+  }
   return int(cudaGetLastError());
+}
+
+TDB_API int tdb_mx_quantize(const void* x, long long ldx, int rows, int K, void* q, void* sf, void* stream) {
+  return tdb_mx_quantize_versioned(x, ldx, rows, K, q, sf, nullptr, nullptr, stream);
 }
 
 // C bf16 [M, N] (row stride ldc) = (A * 2^sfa) (B * 2^sfb)^T (+ bias[N] for

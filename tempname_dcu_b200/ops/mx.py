@@ -21,6 +21,9 @@ from . import native
 native.register("tdb_mx_scale_bytes", [ctypes.c_longlong, ctypes.c_longlong], restype=ctypes.c_longlong)
 native.register("tdb_mx_quantize", [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                     ctypes.c_void_p, ctypes.c_void_p])
+native.register("tdb_mx_quantize_versioned", [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_void_p])
 native.register("tdb_gemm_mx", [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                  ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                  ctypes.c_void_p, ctypes.c_void_p])
@@ -32,9 +35,11 @@ def scale_bytes(rows: int, k: int) -> int:
     return rows // 128 * (k // 128) * 512
 
 
-def quantize(x, q=None, sf=None, stream=None):
+def quantize(x, q=None, sf=None, stream=None, version=None, seen=None):
     """bf16 ``x`` [rows, K] (rows, K multiples of 128) -> (q uint8 [rows, K]
-    holding e4m3 bits, sf uint8 scale atoms)."""
+    holding e4m3 bits, sf uint8 scale atoms).  With ``version`` / ``seen``
+    (device int32 scalars) the work is skipped on the device while
+    ``version == seen`` and ``seen`` takes ``version`` afterwards."""
     import torch
     rows, k = x.shape
     if x.dtype != torch.bfloat16 or x.stride(-1) != 1:
@@ -45,8 +50,14 @@ def quantize(x, q=None, sf=None, stream=None):
         q = torch.empty((rows, k), dtype=torch.uint8, device=x.device)
     if sf is None:
         sf = torch.empty(scale_bytes(rows, k), dtype=torch.uint8, device=x.device)
-    native.check(native.lib().tdb_mx_quantize(x.data_ptr(), x.stride(0), rows, k, q.data_ptr(), sf.data_ptr(),
-                                              native.stream_ptr(stream)), "mx quantize")
+    if (version is None) != (seen is None):
+        raise ValueError("version and seen go together")
+    for t in (version, seen):
+        if t is not None and (t.dtype != torch.int32 or t.numel() != 1 or not t.is_cuda):
+            raise ValueError("version / seen must be device int32 scalars")
+    native.check(native.lib().tdb_mx_quantize_versioned(
+        x.data_ptr(), x.stride(0), rows, k, q.data_ptr(), sf.data_ptr(), 0 if version is None else version.data_ptr(),
+        0 if seen is None else seen.data_ptr(), native.stream_ptr(stream)), "mx quantize")
     return q, sf
 
 

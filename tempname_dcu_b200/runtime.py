@@ -223,6 +223,7 @@ class FluxB200:
         self.mma_mask = list(self.selection_mask) if fp8 else [False] * len(self.selection_mask)
         self.qmask = torch.tensor([int(x) for x in self.wire_mask], dtype=torch.uint8, device=self.device)
         self.mx = None
+        self.weight_version = None  # optional device int32 scalar that changes when the weight does
         if fp8:
             from .ops import mx as _mx
             rows_mask = [0] * (m // 128)
@@ -235,7 +236,8 @@ class FluxB200:
                 a8=torch.empty((m, k), dtype=torch.uint8, device=self.device),
                 sfa=torch.empty(_mx.scale_bytes(m, k), dtype=torch.uint8, device=self.device),
                 b8=torch.empty((n, k), dtype=torch.uint8, device=self.device),
-                sfb=torch.empty(_mx.scale_bytes(n, k), dtype=torch.uint8, device=self.device))
+                sfb=torch.empty(_mx.scale_bytes(n, k), dtype=torch.uint8, device=self.device),
+                seen=torch.full((), -1, dtype=torch.int32, device=self.device))
         self.per = m // self.world // chunk_rows
         local_in_order = [item["within"] for item in self.order if item["destination"] == self.rank]
         self.consume = torch.tensor(local_in_order, dtype=torch.int32, device=self.device)
@@ -305,14 +307,14 @@ class FluxB200:
             else:
                 from .ops import mx as _mx
                 q = self.mx
-                # activations change every call; the weight once per optimizer step: in eager mode its
-                # quantized copy is reused while the tensor is unmodified (same storage, same version);
-                # a captured graph re-quantizes on every replay
+                # activations change every call; the weight only when the device counter in
+                # ``weight_version`` (the optimizer's step) moved -- decided on the device, so
+                # captured graphs replay it correctly; without a counter it is quantized every call
                 _mx.quantize(input_, q["a8"], q["sfa"])
-                key = (weight.data_ptr(), weight._version)
-                if torch.cuda.is_current_stream_capturing() or q.get("weight_key") != key:
+                if self.weight_version is None:
                     _mx.quantize(weight, q["b8"], q["sfb"])
-                    q["weight_key"] = None if torch.cuda.is_current_stream_capturing() else key
+                else:
+                    _mx.quantize(weight, q["b8"], q["sfb"], version=self.weight_version, seen=q["seen"])
                 native.check(lib.tdb_gemm_rs_mx(*args, q["a8"].data_ptr(), q["sfa"].data_ptr(), q["b8"].data_ptr(),
                                                 q["sfb"].data_ptr(), q["mask"].data_ptr(), stream),
                              "fused gemm_rs (block-scaled fp8)")

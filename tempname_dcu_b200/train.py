@@ -68,6 +68,9 @@ class Trainer:
                          execution_plan=execution_plan)
         c = self.config = self.model.config
         self.optimizer = Optimizer(self.model, c["learning_rate"], c["weight_decay"], c["max_grad_norm"])
+        for op in self.model.operators:  # block-scaled FP8 operators re-quantize weights once per step
+            if getattr(op, "mx", None) is not None:
+                op.weight_version = self.optimizer.step_dev
         self.device = self.model.device
         self.loss = torch.zeros((), dtype=torch.float32, device=self.device)
         accum, m = c["accumulation_steps"], self.model.m

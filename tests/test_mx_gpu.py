@@ -58,3 +58,20 @@ def test_mx_gemm_bias_and_strided_output(cuda):
     ref = mx.dequantize(qa, sfa) @ mx.dequantize(qb, sfb).t() + b.float()
     assert _rel(out, ref) < 5e-3
     assert big[:, 384:].abs().max().item() == 0
+
+
+def test_versioned_quantization_skips_until_the_version_moves(cuda):
+    import torch
+    from tempname_dcu_b200.ops import mx
+    x = torch.randn(256, 256, device=cuda).to(torch.bfloat16)
+    version = torch.zeros((), dtype=torch.int32, device=cuda)
+    seen = torch.full((), -1, dtype=torch.int32, device=cuda)
+    q, sf = mx.quantize(x, version=version, seen=seen)
+    first = q.clone()
+    assert seen.item() == 0
+    x2 = (x * 3).to(torch.bfloat16)
+    mx.quantize(x2, q, sf, version=version, seen=seen)  # same version: skipped on the device
+    assert torch.equal(q, first)
+    version.add_(1)
+    mx.quantize(x2, q, sf, version=version, seen=seen)
+    assert seen.item() == 1 and torch.equal(q, mx.quantize(x2)[0])
