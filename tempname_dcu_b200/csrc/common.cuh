@@ -28,6 +28,7 @@ enum StatusCode : int {
   kTimeoutPeerFlag = 2,   // a cross-rank flag never arrived
   kTimeoutLocal = 3,      // an intra-kernel flag never arrived
   kBadArgument = 4,
+  kDebugCheck = 5,        // a TDB_DEBUG index check failed (the access was skipped)
 };
 
 // The status word lives in runtime.cu; kernels receive its device address
@@ -40,6 +41,17 @@ __device__ __forceinline__ void record_status(int* status, int code, int where, 
     status[3] = d1;
   }
 }
+
+// Debug builds (-DTDB_DEBUG, the TDB_DEBUG=1 library): TDB_DEBUG_OK(status,
+// cond, where, a, b) evaluates `cond`, records a failure (code kDebugCheck,
+// location `where`, details a, b) and returns it, so the caller skips the
+// access instead of faulting.  Release builds compile it to `true`.
+#ifdef TDB_DEBUG
+#define TDB_DEBUG_OK(status, cond, where, a, b) \
+  ((cond) ? true : (::tdb::record_status((status), ::tdb::kDebugCheck, (where), int(a), int(b)), false))
+#else
+#define TDB_DEBUG_OK(status, cond, where, a, b) true
+#endif
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;

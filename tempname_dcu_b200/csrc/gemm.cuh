@@ -167,6 +167,15 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_kb = (K + BK - 1) / BK;
+#ifdef TDB_DEBUG
+  // Every thread checks this CTA's tiles before anything is allocated, so a
+  // bad tile table makes the whole CTA return uniformly (status recorded).
+  for (int i = blockIdx.x; i < order.num_tiles; i += gridDim.x) {
+    int mb, nb;
+    order.tile(i, mb, nb);
+    if (!TDB_DEBUG_OK(status, mb >= 0 && mb < order.num_m && nb >= 0 && nb < order.num_n, 50, mb, nb)) return;
+  }
+#endif
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {

@@ -531,6 +531,10 @@ __device__ void consume_phase(const Params& p, int* status) {
       for (int k = 0; k < p.per; ++k) {
         if (!((mine >> k) & 1) || ((done >> k) & 1)) continue;
         const int w = p.consume[k];
+        if (!TDB_DEBUG_OK(status, w >= 0 && w < p.per, 51, k, w)) {
+          taken |= 1ull << k;  // never read or written: the call reports the bad consumption table
+          continue;
+        }
         if (s_missing[w] == 0) {
           if (p.qmask[p.rank * p.per + w]) s_tq[nq++] = w;
           else s_bf[nb++] = w;

@@ -206,7 +206,7 @@ def execute(args):
         native_dir = source_root / "tempname_dcu_b200" / "_native"
         native_dir.mkdir(parents=True, exist_ok=True)
         shutil.copyfile(library, native_dir / "libtdb.so")
-        shutil.copyfile(_build.MANIFEST, native_dir / "manifest.json")
+        shutil.copyfile(_build.paths(_build.debug_requested())[1], native_dir / "manifest.json")
         (args.out / "build").mkdir()
         shutil.copyfile(library, args.out / "build" / "libtdb.so")
         p.write(args.out / "source-manifest.json", manifest)

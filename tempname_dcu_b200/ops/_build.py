@@ -9,6 +9,12 @@ records the key of every object and of the link, so an unchanged tree is
 never rebuilt and a changed header rebuilds everything that includes it.
 The build holds an ``flock`` so concurrent ranks or test workers build once.
 
+``TDB_DEBUG=1`` selects a separate debug library (``libtdb_debug.so``, its
+own objects and manifest) compiled with ``-DTDB_DEBUG``: kernels then check
+tile, block and rank indices (``TDB_DEBUG_OK`` in ``csrc/common.cuh``),
+record a failed check in the status word and skip the access -- a
+sanitizer substitute that never traps.
+
 Reference parity: ``python/flux_dcu/codec.py:58-109`` (content-addressed build
 cache under an flock with a manifest).  Here the library is built in the
 source tree so that it travels with the repository to the GPU host.
@@ -35,6 +41,22 @@ MANIFEST = NATIVE / "manifest.json"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
               "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
+DEBUG_FLAGS = ["-DTDB_DEBUG=1"]
+
+
+def debug_requested() -> bool:
+    return os.environ.get("TDB_DEBUG", "") not in ("", "0")
+
+
+def paths(debug: bool) -> tuple[Path, Path, Path]:
+    """(library, manifest, object directory) of the release or debug build."""
+    if debug:
+        return NATIVE / "libtdb_debug.so", NATIVE / "manifest_debug.json", NATIVE / "obj_debug"
+    return LIBRARY, MANIFEST, OBJ
+
+
+def flags(debug: bool) -> list[str]:
+    return ARCH_FLAGS + NVCC_FLAGS + (DEBUG_FLAGS if debug else [])
 
 
 def nvcc_path() -> str:
@@ -60,10 +82,10 @@ def headers() -> list[Path]:
     return sorted(list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")))
 
 
-def _keys(nvcc: str) -> dict:
+def _keys(nvcc: str, debug: bool = False) -> dict:
     version = _nvcc_version(nvcc)
     header_blob = b"".join(p.name.encode() + p.read_bytes() for p in headers())
-    flags = ARCH_FLAGS + NVCC_FLAGS
+    flags = globals()["flags"](debug)
     result = {}
     for src in sources():
         identity = json.dumps(dict(source=src.name, flags=flags, nvcc=version), sort_keys=True).encode()
@@ -83,25 +105,30 @@ def _compile(nvcc: str, src: Path, obj: Path, flags: list[str]) -> tuple[Path, s
     return obj, proc.stderr
 
 
-def up_to_date() -> bool:
+def up_to_date(debug: bool | None = None) -> bool:
+    debug = debug_requested() if debug is None else debug
+    LIBRARY, MANIFEST, _ = paths(debug)
     if not LIBRARY.is_file() or not MANIFEST.is_file():
         return False
     try:
         manifest = json.loads(MANIFEST.read_text())
-        keys = _keys(nvcc_path())
+        keys = _keys(nvcc_path(), debug)
     except (OSError, ValueError, RuntimeError, subprocess.SubprocessError):
         return False
     return manifest.get("link") == keys["link"] and manifest.get("library_sha256") == _sha(LIBRARY.read_bytes())
 
 
-def build(verbose: bool = False, jobs: int | None = None) -> Path:
-    """Compile and link ``libtdb.so`` if anything changed; return its path."""
+def build(verbose: bool = False, jobs: int | None = None, debug: bool | None = None) -> Path:
+    """Compile and link ``libtdb.so`` (or, with ``debug`` / ``TDB_DEBUG=1``,
+    ``libtdb_debug.so``) if anything changed; return its path."""
+    debug = debug_requested() if debug is None else debug
+    LIBRARY, MANIFEST, OBJ = paths(debug)
     nvcc = nvcc_path()
     NATIVE.mkdir(parents=True, exist_ok=True)
     OBJ.mkdir(parents=True, exist_ok=True)
     with open(NATIVE / ".build.lock", "a") as lock:
         fcntl.flock(lock, fcntl.LOCK_EX)
-        keys = _keys(nvcc)
+        keys = _keys(nvcc, debug)
         if LIBRARY.is_file() and MANIFEST.is_file():
             try:
                 old = json.loads(MANIFEST.read_text())
@@ -126,12 +153,12 @@ def build(verbose: bool = False, jobs: int | None = None) -> Path:
                     logs[futures[future].name] = log
                     if verbose:
                         print(f"[tdb build] compiled {futures[future].name}", flush=True)
-        tmp = NATIVE / f".libtdb.{uuid.uuid4().hex[:8]}.so"
+        tmp = NATIVE / f".{LIBRARY.stem}.{uuid.uuid4().hex[:8]}.so"
         cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *map(str, objects)]
         proc = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
         if proc.returncode:
             tmp.unlink(missing_ok=True)
-            raise RuntimeError(f"link of libtdb.so failed:\n{proc.stderr[-4000:]}")
+            raise RuntimeError(f"link of {LIBRARY.name} failed:\n{proc.stderr[-4000:]}")
         os.replace(tmp, LIBRARY)
         manifest = dict(keys, library_sha256=_sha(LIBRARY.read_bytes()), objects_built=sorted(logs),
                         ptxas_log={k: v[-2000:] for k, v in logs.items() if v.strip()})
@@ -145,7 +172,8 @@ def build(verbose: bool = False, jobs: int | None = None) -> Path:
 
 
 def manifest() -> dict:
-    return json.loads(MANIFEST.read_text()) if MANIFEST.is_file() else {}
+    path = paths(debug_requested())[1]
+    return json.loads(path.read_text()) if path.is_file() else {}
 
 
 def manifest_for_rows() -> dict:
@@ -154,8 +182,10 @@ def manifest_for_rows() -> dict:
     manifest, python/flux_dcu/codec.py:72-109)."""
     blob = b"".join(p.name.encode() + p.read_bytes() for p in sorted(sources() + headers()))
     m = manifest()
-    return dict(library=str(LIBRARY), library_sha256=_sha(LIBRARY.read_bytes()) if LIBRARY.is_file() else None,
-                identity=dict(source_sha256=_sha(blob), flags=ARCH_FLAGS + NVCC_FLAGS,
+    debug = debug_requested()
+    library = paths(debug)[0]
+    return dict(library=str(library), library_sha256=_sha(library.read_bytes()) if library.is_file() else None,
+                identity=dict(source_sha256=_sha(blob), flags=flags(debug),
                               nvcc_version=m.get("nvcc_version")),
                 link_key=m.get("link"))
 
