@@ -87,6 +87,7 @@ class GPT:
         self.params = FlatParams(gpt_param_specs(c, self.world), self.device, rank=self.rank, seed=seed,
                                  materialize=materialize)
         self.forward_calls = 0
+        self.trace_ranges = False  # per-layer profiler / NVTX ranges (utils.trace --ranges)
         self.operators = []
         factory = operator_factory
         for index in range(c["layers"]):
@@ -197,7 +198,8 @@ class GPT:
         x = self._embed(tokens)
         saved = []
         for i in range(c["layers"]):
-            x, s = self._layer_fwd(i, x)
+            with self._range(f"tdb/layer{i}/fwd"):
+                x, s = self._layer_fwd(i, x)
             saved.append(s)
         xl = x
         eps = c["layer_norm_epsilon"]
@@ -221,7 +223,8 @@ class GPT:
         dx = K.layernorm_bwd(xl, self.P("final_weight"), meanf, rstdf, dlnf, self.Gr("final_weight"),
                              self.Gr("final_bias"), ln_scratch)
         for i in reversed(range(c["layers"])):
-            dx = self._layer_bwd(i, dx, saved[i], ln_scratch)
+            with self._range(f"tdb/layer{i}/bwd"):
+                dx = self._layer_bwd(i, dx, saved[i], ln_scratch)
             saved[i] = None
         # ---- embedding / positions
         K.position_bwd(dx, self.rank * self.ml if self.world > 1 else 0, c["sequence"], self.Gr("position"))
@@ -229,6 +232,19 @@ class GPT:
         sorted_tokens, order = torch.sort(tokens, stable=True)
         K.embedding_bwd(sorted_tokens, order, dfull, self.vocab_start, self.vocab_local, self.Gr("embedding"))
         return loss_acc
+
+    def _range(self, name):
+        """Named range (torch.profiler record_function + NVTX) around a layer's
+        forward or backward when ``trace_ranges`` is set; a no-op otherwise."""
+        import contextlib
+        if not self.trace_ranges:
+            return contextlib.nullcontext()
+        import torch
+        stack = contextlib.ExitStack()
+        stack.enter_context(torch.profiler.record_function(name))
+        torch.cuda.nvtx.range_push(name)
+        stack.callback(torch.cuda.nvtx.range_pop)
+        return stack
 
     def _colsum(self, x, name):
         import torch

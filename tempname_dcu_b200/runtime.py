@@ -270,6 +270,13 @@ class FluxB200:
                 raise ValueError(f"{label} must be contiguous BF16 {shape} on the current device")
 
     def forward(self, input_, weight, bias=None, residual=None, out=None):
+        if self.profile_enabled:  # a named range per call in profiler traces (diagnostics only)
+            import torch
+            with torch.profiler.record_function(f"tdb/gemm_rs/{self.arm}/{self.m}x{self.n}x{self.k}"):
+                return self._forward(input_, weight, bias, residual, out)
+        return self._forward(input_, weight, bias, residual, out)
+
+    def _forward(self, input_, weight, bias=None, residual=None, out=None):
         import torch
         self._check(input_, weight)
         ctx = self.context

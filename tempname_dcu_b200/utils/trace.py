@@ -1,6 +1,6 @@
 """Kernel-time breakdown of training micro-steps (torch.profiler / CUPTI).
 
-    python -m tempname_dcu_b200.utils.trace [--layers L] [--micro 1 | --step] [--chrome out.json]
+    python -m tempname_dcu_b200.utils.trace [--layers L] [--micro 1 | --step] [--chrome out.json] [--ranges]
 
 Runs warm-up micro-steps, then profiles ``--micro`` micro-batches of the GPT
 training step and prints the device time per kernel name (sum, count, share),
@@ -29,6 +29,8 @@ def main(argv=None):
     ap.add_argument("--step", action="store_true", help="profile one whole optimizer step instead")
     ap.add_argument("--arm", default="flux", help="tensor-parallel arm when launched with torchrun (WORLD_SIZE > 1)")
     ap.add_argument("--graph", action="store_true", help="capture the step as a CUDA graph and profile a replay")
+    ap.add_argument("--ranges", action="store_true",
+                    help="name every layer's forward / backward (profiler + NVTX ranges) and print their host times")
     args = ap.parse_args(argv)
     import os
     import torch
@@ -57,6 +59,7 @@ def main(argv=None):
         trainer.step(tokens, labels)
     torch.cuda.synchronize()
     model = trainer.model
+    model.trace_ranges = args.ranges and not args.graph
     with profile(activities=[ProfilerActivity.CUDA, ProfilerActivity.CPU]) as prof:
         t0 = time.perf_counter()
         if args.step or args.graph:
@@ -87,6 +90,15 @@ def main(argv=None):
           f"host wall {wall * 1e3:.2f} ms")
     for name, (us, n) in rows[:40]:
         print(f"{us / 1e3:10.3f} ms {100 * us / total:6.2f}% x{n:<6d} {name[:110]}")
+    if model.trace_ranges:
+        ranges = collections.defaultdict(lambda: [0.0, 0])
+        for evt in prof.events():
+            if evt.name.startswith("tdb/layer"):
+                kind = evt.name.rsplit("/", 1)[-1]
+                ranges[kind][0] += evt.cpu_time_total
+                ranges[kind][1] += 1
+        for kind, (us, n) in sorted(ranges.items()):
+            print(f"layer {kind}: {n} ranges, host {us / 1e3:.2f} ms total, {us / max(n, 1) / 1e3:.3f} ms each")
     if args.json:
         with open(args.json, "w") as fh:
             json.dump(dict(total_us=total, wall_s=wall, kernels=[dict(name=k, us=v[0], count=v[1])

@@ -119,3 +119,16 @@ def test_tp_collectives_two_gloo_ranks(tmp_path):
 
 def test_default_config_untouched():
     assert DEFAULT_CONFIG["vocab"] == 33792 and DEFAULT_CONFIG["accumulation_steps"] == 4
+
+
+def test_layer_ranges_are_named_only_when_enabled():
+    import torch
+    from types import SimpleNamespace
+    from tempname_dcu_b200.models.gpt import GPT
+    with torch.profiler.profile() as prof:
+        with GPT._range(SimpleNamespace(trace_ranges=False), "tdb/layer0/fwd"):
+            torch.ones(3).sum()
+        with GPT._range(SimpleNamespace(trace_ranges=True), "tdb/layer1/bwd"):
+            torch.ones(3).sum()
+    names = [e.name for e in prof.events() if e.name.startswith("tdb/")]
+    assert names == ["tdb/layer1/bwd"]
