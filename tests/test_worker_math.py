@@ -1,0 +1,74 @@
+"""Worker helpers on CPU (reference: tests/test_worker_math.py): the
+closed-block selective reference, role plans reaching the right operators,
+the torch independent codec against the FP64 oracle, tensor-hash bit
+sensitivity, and the torch restatement of the FP8 quantizer used as the
+fp8-mma reference."""
+import torch
+
+from tempname_dcu_b200 import reference
+from tempname_dcu_b200.mapping import ARMS
+from tempname_dcu_b200.worker import independent_codec, reduce_reference_sources, tensor_sha
+
+
+def test_closed_block_selective_reference():
+    torch.manual_seed(0)
+    world, per, chunk, n = 2, 3, 128, 256
+    sources = torch.randn(world, per * chunk, n).to(torch.bfloat16)
+    mask = [True, False, True, False, False, True]  # physical blocks; rank 1 owns 3..5
+    plain, coded = reduce_reference_sources(sources, 1, True, mask, chunk)
+    for w in range(per):
+        blk = slice(w * chunk, (w + 1) * chunk)
+        if mask[per + w]:
+            assert not torch.equal(coded[blk], plain[blk])
+        else:
+            assert torch.equal(coded[blk], plain[blk])
+    # the local source (rank 1) is never coded: with one source the sums agree exactly
+    one = sources[:1]
+    p1, c1 = reduce_reference_sources(one, 0, True, [True] * per, chunk)
+    assert torch.equal(p1, c1)
+
+
+def test_role_plans_reach_the_right_operators():
+    from tempname_dcu_b200.models.config import SMALL_CONFIG
+    from tempname_dcu_b200.models.gpt import GPT
+    seen = []
+
+    def factory(m, n, k, group, arm, chunk_rows, plan):
+        seen.append((k, arm, plan))
+        return object()
+    roles = dict(attn=dict(tag="attn-plan"), mlp=dict(tag="mlp-plan"))
+    cfg = dict(SMALL_CONFIG)
+    GPT(cfg, ARMS[4], device="cpu", operator_factory=factory, execution_plan=dict(roles=roles), materialize=False)
+    assert len(seen) == 2 * cfg["layers"]
+    for i, (k, arm, plan) in enumerate(seen):
+        role = "attn" if i % 2 == 0 else "mlp"
+        assert k == (cfg["hidden"] if role == "attn" else cfg["ffn"]) and arm == ARMS[4]
+        assert plan == roles[role]
+    seen.clear()
+    GPT(cfg, ARMS[1], device="cpu", operator_factory=factory, execution_plan=dict(roles=roles), materialize=False)
+    assert all(plan is None for _, _, plan in seen)
+
+
+def test_torch_codec_matches_the_fp64_oracle():
+    torch.manual_seed(3)
+    x = (torch.randn(8 * 128) * torch.logspace(-2, 2, 8 * 128)).to(torch.bfloat16)
+    ours = independent_codec(x).float()
+    oracle = torch.tensor(reference.decode(reference.encode([float(v) for v in x.float()])))
+    assert float((ours - oracle).norm() / oracle.norm()) <= 0.02
+
+
+def test_tensor_hash_is_bit_sensitive():
+    x = torch.randn(64, 64).to(torch.bfloat16)
+    y = x.clone()
+    assert tensor_sha(x) == tensor_sha(y)
+    y.view(torch.int16)[3, 5] ^= 1  # one mantissa bit
+    assert tensor_sha(x) != tensor_sha(y)
+
+
+def test_fp8_reference_dequantizes_close_to_the_input():
+    from tempname_dcu_b200.ops import mx
+    torch.manual_seed(4)
+    x = torch.randn(128, 256).to(torch.bfloat16)
+    values, e = mx.quantize_reference(x)
+    deq = (values.view(128, -1, 32) * torch.exp2(e.float()).unsqueeze(-1)).view(128, 256)
+    assert float((deq - x.float()).norm() / x.float().norm()) < 0.04
