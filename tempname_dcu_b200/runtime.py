@@ -270,7 +270,7 @@ class FluxB200:
                 raise ValueError(f"{label} must be contiguous BF16 {shape} on the current device")
 
     def forward(self, input_, weight, bias=None, residual=None, out=None):
-        if self.profile_enabled:  # a named range per call in profiler traces (diagnostics only)
+        if getattr(self, "profile_enabled", False):  # a named range per call in profiler traces
             import torch
             with torch.profiler.record_function(f"tdb/gemm_rs/{self.arm}/{self.m}x{self.n}x{self.k}"):
                 return self._forward(input_, weight, bias, residual, out)
