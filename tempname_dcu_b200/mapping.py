@@ -174,3 +174,15 @@ def tile_table(m, n, world, chunk_rows, arm, plan=None, *, block_m=128, block_n=
     ``m_tile * n_tiles + n_tile``."""
     order = schedule(m, n, k, world, chunk_rows, arm, plan)
     return tiles_for_order(order, n, chunk_rows, block_m=block_m, block_n=block_n)
+
+
+def mma_row_blocks(order, mask, m, chunk_rows, block_m=128):
+    """Per ``block_m``-row block of a rank's [m, n] partial output: 1 if the
+    block belongs to a physical block selected by ``mask`` (the selective
+    arm's block-scaled FP8 MMA tiles), else 0."""
+    rows = [0] * (m // block_m)
+    for item in order:
+        if mask[item["physical"]]:
+            for mb in range(item["row"] // block_m, (item["row"] + chunk_rows) // block_m):
+                rows[mb] = 1
+    return rows

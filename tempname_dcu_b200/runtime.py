@@ -27,8 +27,8 @@ import hashlib
 import json
 import threading
 
-from .mapping import (ARRIVAL_ARMS, BACKEND, block_selection, remote_first_order, schedule, selection_statistics,
-                      tile_table, tiles_for_order)
+from .mapping import (ARRIVAL_ARMS, BACKEND, block_selection, mma_row_blocks, remote_first_order, schedule,
+                      selection_statistics, tile_table, tiles_for_order)
 from .ops import native
 
 native.register("tdb_gemm_rs", [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
@@ -226,11 +226,7 @@ class FluxB200:
         self.weight_version = None  # optional device int32 scalar that changes when the weight does
         if fp8:
             from .ops import mx as _mx
-            rows_mask = [0] * (m // 128)
-            for item in self.order:
-                if self.mma_mask[item["physical"]]:
-                    for mb in range(item["row"] // 128, (item["row"] + chunk_rows) // 128):
-                        rows_mask[mb] = 1
+            rows_mask = mma_row_blocks(self.order, self.mma_mask, m, chunk_rows)
             self.mx = dict(
                 mask=torch.tensor(rows_mask, dtype=torch.uint8, device=self.device),
                 a8=torch.empty((m, k), dtype=torch.uint8, device=self.device),

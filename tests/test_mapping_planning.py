@@ -283,3 +283,14 @@ def test_ag_tile_table_local_rows_first():
             assert sorted(t) == list(range(world * rows // tm * n_tiles))
             first_rows = {x // n_tiles * tm for x in t[: rows // tm * n_tiles]}
             assert all(rank * rows <= r < (rank + 1) * rows for r in first_rows)
+
+
+def test_mma_row_blocks_follow_the_selected_physical_blocks():
+    from tempname_dcu_b200.mapping import mma_row_blocks
+    m, n, k, world, chunk = 2048, 4096, 512, 8, 256
+    plan = P.make_role(m, n, k, world, chunk, mask=[i % 3 == 0 for i in range(m // chunk)])
+    order = schedule(m, n, k, world, chunk, ARMS[4], plan)
+    rows = mma_row_blocks(order, plan["selective_mask"], m, chunk)
+    assert len(rows) == m // 128
+    for p, selected in enumerate(plan["selective_mask"]):
+        assert rows[2 * p] == rows[2 * p + 1] == int(selected)  # two 128-row blocks per 256-row chunk
