@@ -117,6 +117,70 @@ __global__ void bwd_pos_kernel(const uint16_t* __restrict__ dy, int rows, int64_
 
 using namespace tdb::emb;
 
+namespace tdb {
+namespace emb {
+constexpr int kSortMax = 16384;  // 128 KB of keys in dynamic shared memory
+constexpr int kSortThreads = 1024;
+
+// Stable sort of a micro-batch's token ids (one CTA): bitonic sort of the
+// unique keys (token << 32 | position) in shared memory, so equal tokens keep
+// their position order -- the deterministic order the embedding gradient
+// accumulates in.  Padding keys (all ones) sort last.
+__global__ void __launch_bounds__(kSortThreads) sort_tokens_kernel(const int64_t* __restrict__ tokens, int n,
+                                                                   int64_t* __restrict__ sorted_tokens,
+                                                                   int64_t* __restrict__ order) {
+  extern __shared__ unsigned long long key[];  // [size], size = next power of two >= n
+  int size = 2;
+  while (size < n) size <<= 1;
+  for (int i = threadIdx.x; i < size; i += blockDim.x)
+    key[i] = i < n ? (static_cast<unsigned long long>(tokens[i]) << 32) | static_cast<unsigned int>(i) : ~0ull;
+  __syncthreads();
+  for (int k = 2; k <= size; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < size; i += blockDim.x) {
+        const int p = i ^ j;
+        if (p > i) {
+          const unsigned long long a = key[i], b = key[p];
+          const bool ascending = (i & k) == 0;
+          if ((a > b) == ascending) {
+            key[i] = b;
+            key[p] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    sorted_tokens[i] = static_cast<int64_t>(key[i] >> 32);
+    order[i] = static_cast<int64_t>(key[i] & 0xffffffffull);
+  }
+}
+}  // namespace emb
+}  // namespace tdb
+
+// tokens [n] (0 <= id < 2^31, n <= 16384) -> ids sorted ascending and the
+// original positions, equal ids in position order (a stable sort).
+TDB_API int tdb_sort_tokens(const int64_t* tokens, int n, int64_t* sorted_tokens, int64_t* order, void* stream) {
+  if (!tokens || !sorted_tokens || !order || n <= 0 || n > tdb::emb::kSortMax)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "sort_tokens: 1..%d tokens", tdb::emb::kSortMax);
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(tdb::emb::sort_tokens_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         tdb::emb::kSortMax * 8);
+    if (e != cudaSuccess) return tdb_host::fail(int(e), "sort_tokens: cudaFuncSetAttribute failed");
+    attr[dev & 63] = true;
+  }
+  int size = 2;
+  while (size < n) size <<= 1;
+  tdb::emb::sort_tokens_kernel<<<1, tdb::emb::kSortThreads, size * 8, static_cast<cudaStream_t>(stream)>>>(
+      tokens, n, sorted_tokens, order);
+  tdb_host::launched(1);
+  return int(cudaGetLastError());
+}
+
 TDB_API int tdb_embedding_fwd(const int64_t* tokens, const void* table, int64_t start, int64_t local_vocab,
                               const void* pos, int64_t pos_offset, int seq, int rows, int H, void* out, void* stream) {
   if (H % 8 || rows <= 0) return tdb_host::fail(int(cudaErrorInvalidValue), "embedding: H must be a multiple of 8");

@@ -229,7 +229,8 @@ class GPT:
         # ---- embedding / positions
         K.position_bwd(dx, self.rank * self.ml if self.world > 1 else 0, c["sequence"], self.Gr("position"))
         dfull = self.tp.gather(dx)
-        sorted_tokens, order = torch.sort(tokens, stable=True)
+        sorted_tokens, order = K.sort_tokens(tokens, self._buf("sorted_tokens", self.m, torch.int64),
+                                             self._buf("token_order", self.m, torch.int64))
         K.embedding_bwd(sorted_tokens, order, dfull, self.vocab_start, self.vocab_local, self.Gr("embedding"))
         return loss_acc
 

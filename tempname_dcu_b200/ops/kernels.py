@@ -200,6 +200,23 @@ def add_positions(x, pos, offset, seq):
                  "add positions")
 
 
+native.register("tdb_sort_tokens", [V, I, V, V, V])
+
+
+def sort_tokens(tokens, sorted_tokens=None, order=None):
+    """Stable ascending sort of int64 token ids (at most 16384, one CTA):
+    returns (sorted ids, original positions)."""
+    torch = _t()
+    n = tokens.numel()
+    if tokens.dtype != torch.int64 or not tokens.is_contiguous():
+        raise ValueError("tokens must be a contiguous int64 vector")
+    sorted_tokens = torch.empty_like(tokens) if sorted_tokens is None else sorted_tokens
+    order = torch.empty_like(tokens) if order is None else order
+    native.check(native.lib().tdb_sort_tokens(tokens.data_ptr(), n, sorted_tokens.data_ptr(), order.data_ptr(), _s()),
+                 "sort tokens")
+    return sorted_tokens, order
+
+
 def embedding_bwd(sorted_tokens, sorted_rows, dy, vocab_start, local_vocab, grad):
     rows, H = dy.shape
     native.check(native.lib().tdb_embedding_bwd(sorted_tokens.data_ptr(), sorted_rows.data_ptr(), rows,

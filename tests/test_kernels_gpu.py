@@ -256,3 +256,14 @@ def test_embedding_fwd_bwd(cuda):
     ref_p = torch.zeros(seq, H, device=cuda)
     ref_p.index_add_(0, torch.arange(rows, device=cuda) % seq, dy.float())
     assert _rel(gp, ref_p) < 1e-5
+
+
+@pytest.mark.parametrize("n,vocab", [(1, 10), (37, 5), (2048, 50257), (3000, 100), (16384, 50304)])
+def test_sort_tokens_is_a_stable_sort(cuda, n, vocab):
+    import torch
+    from tempname_dcu_b200.ops import kernels as k
+    torch.manual_seed(n)
+    tokens = torch.randint(0, vocab, (n,), device=cuda)
+    st, order = k.sort_tokens(tokens)
+    ref_t, ref_o = torch.sort(tokens, stable=True)
+    assert torch.equal(st, ref_t) and torch.equal(order, ref_o)
