@@ -43,6 +43,8 @@ def parse():
     p.add_argument("--impl", default="ours", choices=("ours", "reference", "baseline"))
     p.add_argument("--arm", default="flux")
     p.add_argument("--no-graph", action="store_true", help="issue every kernel from the host (no CUDA graph)")
+    p.add_argument("--taco-allgather", action="store_true",
+                   help="TACO-compress the fused all-gathers too (peers' rows cross NVLink as H128/E4M3 packets)")
     p.add_argument("--small", action="store_true", help="2-layer smoke configuration (not a headline number)")
     return p.parse_args()
 
@@ -178,7 +180,7 @@ def main():
             from tempname_dcu_b200.runtime import operator_factory_for
             factory = operator_factory_for(args.arm)
         trainer = Trainer(config, args.arm, group, operator_factory=factory, cuda_graph=not args.no_graph,
-                          graph_warmup=min(2, max(0, args.warmup - 1)))
+                          graph_warmup=min(2, max(0, args.warmup - 1)), taco_allgather=args.taco_allgather)
     from tempname_dcu_b200.train import synthetic_batches
     c = trainer.config
     (tokens_h, labels_h), = synthetic_batches(c, 1, seed=4321)
@@ -244,6 +246,7 @@ def main():
                         accumulation_steps=c["accumulation_steps"], vocab=c["vocab"], padded_vocab=c["padded_vocab"],
                         layers=c["layers"], hidden=c["hidden"], ffn=c["ffn"], heads=c["heads"],
                         tokens_per_step=tokens_per_step, arm=args.arm if args.impl == "ours" else None,
+                        taco_allgather=bool(args.taco_allgather) if args.impl == "ours" else None,
                         cuda_graph=bool(args.impl == "ours" and not args.no_graph),
                         l2="inputs larger than L2 (13 GB of bf16 weights streamed per step); no flush",
                         model_tflops_per_gpu=round(flops / (ms_per_step / 1000.0) / world / 1e12, 1),

@@ -25,6 +25,7 @@
 #include <cmath>
 #include <type_traits>
 
+#include "codec.cuh"
 #include "gemm.cuh"
 #include "gemm2.cuh"
 #include "gemm_epi.cuh"
@@ -49,6 +50,11 @@ struct Pull {
   uint32_t* ready;        // per 128-row block of `full`
   int slices;             // items per 128-row block
   uint64_t wait_ns;
+  // compressed gather: peers' slots hold TACO packets (decoded here); this
+  // rank's own rows are copied exact from x
+  int taco;
+  const uint16_t* x;
+  int64_t ldx;
 };
 
 __device__ __forceinline__ const uint16_t* src_slot(const Pull& a, int r, uint32_t parity) {
@@ -68,6 +74,43 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
 }
 __device__ __forceinline__ void red_release_gpu(uint32_t* addr, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+// Compressed gather: decode `nrows` rows starting at r0 of source s's TACO
+// packets into the gathered buffer; one warp per H128 group, four groups'
+// loads in flight per warp.
+__device__ __forceinline__ void decode_rows(const Pull& a, int s, uint32_t parity, int64_t r0, int nrows, int et) {
+  const int warp = et >> 5, lane = et & 31;
+  const uint8_t* pk = reinterpret_cast<const uint8_t*>(src_slot(a, s, parity));
+  const int64_t gpr = a.cols / 128, groups = a.rows * gpr;
+  const float* scales = reinterpret_cast<const float*>(pk + a.rows * a.cols);
+  const int total = int(nrows * gpr);
+  constexpr int U = 4;
+  for (int g0 = warp * U; g0 < total; g0 += 4 * U) {
+    uint32_t word[U];
+    float q[U], ad[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (g0 + u < total) {
+        const int64_t gi = (r0 + (g0 + u) / gpr) * gpr + (g0 + u) % gpr;
+        word[u] = reinterpret_cast<const uint32_t*>(pk + gi * 128)[lane];
+        q[u] = scales[gi];
+        ad[u] = scales[groups + gi];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (g0 + u < total) {
+        float v[4];
+        taco::decode_group_warp(word[u], q[u], ad[u], lane, v);
+        const int64_t row = r0 + (g0 + u) / gpr, col = ((g0 + u) % gpr) * 128;
+        uint2 o;
+        o.x = uint32_t(float_to_bf16_bits(v[0])) | (uint32_t(float_to_bf16_bits(v[1])) << 16);
+        o.y = uint32_t(float_to_bf16_bits(v[2])) | (uint32_t(float_to_bf16_bits(v[3])) << 16);
+        reinterpret_cast<uint2*>(a.full + (int64_t(s) * a.rows + row) * a.cols + col)[lane] = o;
+      }
+    }
+  }
 }
 
 // Executed by the 128 epilogue threads of every CTA before their first tile.
@@ -111,17 +154,28 @@ __device__ void pull_rows(const Pull& a, volatile int& s_ok, int* status) {
       checked = s;
     }
     const int64_t r0 = int64_t(b) * 128 + int64_t(j) * rows_per_item;  // row inside the source block
-    const uint4* src = reinterpret_cast<const uint4*>(src_slot(a, s, parity) + r0 * a.cols);
-    uint4* dst = reinterpret_cast<uint4*>(a.full + (int64_t(s) * a.rows + r0) * a.cols);
-    int64_t i = et;
-    for (; i + 3 * 128 < n; i += 4 * 128) {
-      uint4 v[4];
+    if (a.taco && s != a.rank) {
+      decode_rows(a, s, parity, r0, rows_per_item, et);
+    } else {
+      uint4* dst = reinterpret_cast<uint4*>(a.full + (int64_t(s) * a.rows + r0) * a.cols);
+      if (a.taco) {  // own rows, exact, from the caller's input (row stride ldx)
+        for (int64_t i = et; i < n; i += 128) {
+          const int64_t rr = i / vec_per_row, c = i % vec_per_row;
+          dst[i] = reinterpret_cast<const uint4*>(a.x + (r0 + rr) * a.ldx)[c];
+        }
+      } else {
+        const uint4* src = reinterpret_cast<const uint4*>(src_slot(a, s, parity) + r0 * a.cols);
+        int64_t i = et;
+        for (; i + 3 * 128 < n; i += 4 * 128) {
+          uint4 v[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) v[u] = src[i + u * 128];
+          for (int u = 0; u < 4; ++u) v[u] = src[i + u * 128];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) dst[i + u * 128] = v[u];
+          for (int u = 0; u < 4; ++u) dst[i + u * 128] = v[u];
+        }
+        for (; i < n; i += 128) dst[i] = src[i];
+      }
     }
-    for (; i < n; i += 128) dst[i] = src[i];
     named_sync_epilogue();
     if (et == 0) {
       __threadfence();
@@ -293,7 +347,7 @@ int pick_tile(int M, int N, int K, int sms);
 
 TDB_API int tdb_ag_prepare(const void* x, long long ldx, long long rows, long long cols,
                            const unsigned long long* peers, int W, int rank, unsigned long long heap_off,
-                           unsigned int* state, void* stream);
+                           unsigned int* state, int taco, void* stream);
 
 // C = epilogue(AG(x) @ B^T) with the all-gather fused (see the header).
 //   x: this rank's rows [rows, K] (row stride ldx); full: [W*rows, K] output of
@@ -306,7 +360,7 @@ TDB_API int tdb_ag_gemm(const void* x, long long ldx, void* full, long long rows
                         long long ldb, void* C, long long ldc, int N, int mode, const void* bias, const void* aux,
                         long long ld_aux, void* aux_out, float alpha, int bn, const int* tile_table,
                         const unsigned long long* peers, int W, int rank, unsigned long long heap_off,
-                        unsigned int* state, unsigned int* ready, double wait_seconds, void* stream) {
+                        unsigned int* state, unsigned int* ready, double wait_seconds, int taco, void* stream) {
   using namespace tdb;
   using namespace tdb::gemm;
   const long long M = rows * W;
@@ -318,7 +372,9 @@ TDB_API int tdb_ag_gemm(const void* x, long long ldx, void* full, long long rows
   if (bn != 128 && bn != 192 && bn != 256 && bn != 512)
     return tdb_host::fail(int(cudaErrorInvalidValue), "ag_gemm: bn must be 128, 192, 256 or 512");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int rc = tdb_ag_prepare(x, ldx, rows, K, peers, W, rank, heap_off, state, stream);
+  if (taco && K % 128)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "ag_gemm: the compressed gather needs K %% 128 == 0");
+  int rc = tdb_ag_prepare(x, ldx, rows, K, peers, W, rank, heap_off, state, taco, stream);
   if (rc) return rc;
   CUtensorMap ta, tb;
   if ((rc = make_operand_map(&ta, full, false, int(M), K, K, BM))) return rc;
@@ -353,6 +409,9 @@ TDB_API int tdb_ag_gemm(const void* x, long long ldx, void* full, long long rows
   pull.ready = ready;
   pull.slices = 16;
   pull.wait_ns = uint64_t(wait_seconds * 1e9);
+  pull.taco = taco;
+  pull.x = static_cast<const uint16_t*>(x);
+  pull.ldx = ldx;
   TileOrder order;
   order.group_m = 1;
   order.table = tile_table;

@@ -20,6 +20,7 @@
 // Slot reuse: a rank rewrites slot[p] two calls later, after its previous
 // pull kernel has seen every peer's publish of the call in between, which
 // each peer issues only after finishing its own earlier pulls.
+#include "codec.cuh"
 #include "common.cuh"
 
 namespace tdb {
@@ -57,6 +58,29 @@ __global__ void __launch_bounds__(kThreads) ag_stage_kernel(const uint16_t* __re
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t r = i / per_row, c = i % per_row;
     reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(x + r * ldx)[c];
+  }
+}
+
+// TACO staging (the compressed all-gather): one warp per H128 group of this
+// rank's rows (row stride ldx), packets written into the send slot as
+// [payload: rows*cols bytes][quant fp32 x groups][adaptive fp32 x groups].
+__global__ void __launch_bounds__(256) ag_stage_taco_kernel(const uint16_t* __restrict__ x, int64_t ldx, Params p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t gpr = p.cols / 128, groups = p.rows * gpr;
+  const int64_t g = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (g >= groups) return;
+  uint8_t* pk = reinterpret_cast<uint8_t*>(slot(p, p.rank, __ldg(p.state + 1)));
+  const int64_t r = g / gpr, c = (g % gpr) * 128;
+  const uint2 raw = reinterpret_cast<const uint2*>(x + r * ldx + c)[lane];
+  float v[4] = {bf16_bits_to_float(raw.x & 0xffff), bf16_bits_to_float(raw.x >> 16),
+                bf16_bits_to_float(raw.y & 0xffff), bf16_bits_to_float(raw.y >> 16)};
+  taco::GroupScales sc;
+  const uint32_t word = taco::encode_group_warp(v, lane, sc);
+  reinterpret_cast<uint32_t*>(pk + g * 128)[lane] = word;
+  if (lane == 0) {
+    float* scales = reinterpret_cast<float*>(pk + p.rows * p.cols);
+    scales[g] = sc.quant;
+    scales[groups + g] = sc.adaptive;
   }
 }
 
@@ -126,11 +150,12 @@ TDB_API long long tdb_ag_region_bytes(long long rows, long long cols) {
 
 // Advance the region's epoch and stage this rank's rows into its send slot
 // (the first two steps of a gather; the fused all-gather GEMM pulls itself).
+// taco = 1 stages TACO packets instead of BF16 rows (cols % 128 == 0).
 TDB_API int tdb_ag_prepare(const void* x, long long ldx, long long rows, long long cols,
                            const unsigned long long* peers, int W, int rank, unsigned long long heap_off,
-                           unsigned int* state, void* stream) {
+                           unsigned int* state, int taco, void* stream) {
   if (!x || !peers || !state || W < 2 || W > 64 || rank < 0 || rank >= W || rows <= 0 || cols <= 0 || cols % 8 ||
-      ldx % 8 || heap_off % 16 || reinterpret_cast<uintptr_t>(x) % 16)
+      ldx % 8 || heap_off % 16 || reinterpret_cast<uintptr_t>(x) % 16 || (taco && cols % 128))
     return tdb_host::fail(int(cudaErrorInvalidValue), "ag_prepare: bad arguments");
   using namespace tdb::ag;
   Params p;
@@ -146,9 +171,14 @@ TDB_API int tdb_ag_prepare(const void* x, long long ldx, long long rows, long lo
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int sms = tdb_host::sm_count();
   ag_advance_kernel<<<1, 1, 0, s>>>(state);
-  const int64_t vec = rows * cols / 8;
-  const int stage_grid = int(vec / kThreads + 1 < 2 * sms ? vec / kThreads + 1 : 2 * sms);
-  ag_stage_kernel<<<stage_grid, kThreads, 0, s>>>(static_cast<const uint16_t*>(x), ldx, p);
+  if (taco) {
+    const int64_t groups = rows * (cols / 128);
+    ag_stage_taco_kernel<<<unsigned((groups + 7) / 8), 256, 0, s>>>(static_cast<const uint16_t*>(x), ldx, p);
+  } else {
+    const int64_t vec = rows * cols / 8;
+    const int stage_grid = int(vec / kThreads + 1 < 2 * sms ? vec / kThreads + 1 : 2 * sms);
+    ag_stage_kernel<<<stage_grid, kThreads, 0, s>>>(static_cast<const uint16_t*>(x), ldx, p);
+  }
   tdb_host::launched(2);
   return int(cudaGetLastError());
 }

@@ -64,7 +64,7 @@ class GPT:
     """One rank's shard of the TP/SP GPT with flat parameter storage."""
 
     def __init__(self, config, arm="flux", group=None, *, device="cuda", seed=1234, operator_factory=None,
-                 execution_plan=None, materialize=True):
+                 execution_plan=None, materialize=True, taco_allgather=False):
         import torch
         from ..parallel.tp import TPGroup
         self.tp = TPGroup(group)
@@ -110,7 +110,8 @@ class GPT:
             if self.ml % 256 == 0:
                 # ... and, where a GEMM consumes the gathered rows, fused into it
                 from ..parallel.allgather import SymmAgGemm
-                self.agg = SymmAgGemm(self.tp, self.ml, self.h)
+                # taco_allgather: the gathered rows of peers cross NVLink as TACO packets
+                self.agg = SymmAgGemm(self.tp, self.ml, self.h, taco=taco_allgather)
             from ..runtime import FluxB200
             for k in (3 * self.h // self.world, self.f // self.world, self.vocab_local):
                 if k not in self._bwd_rs:

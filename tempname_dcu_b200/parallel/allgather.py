@@ -61,7 +61,7 @@ native.register("tdb_ag_gemm", [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_voi
                                 ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,
                                 ctypes.c_void_p, ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                 ctypes.c_int, ctypes.c_int, ctypes.c_ulonglong, ctypes.c_void_p, ctypes.c_void_p,
-                                ctypes.c_double, ctypes.c_void_p])
+                                ctypes.c_double, ctypes.c_int, ctypes.c_void_p])
 native.register("tdb_gemm_pick_tile", [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int])
 
 
@@ -89,16 +89,22 @@ class SymmAgGemm:
     ``out = epilogue(AG(x_local) @ weight^T)`` (weight [N, K], or [K, N] with
     ``b_mn``) and returns the gathered rows ``full`` [world * rows, K] too.
     Every call of an instance gathers the same [rows, K] block shape; creation
-    is collective."""
+    is collective.
+
+    ``taco=True`` compresses the gather: each rank stages its rows as TACO
+    H128/E4M3 packets (136 bytes per 128 values, 0.53 of BF16 on the link)
+    and the pulling CTAs decode peers' packets into the gathered buffer; a
+    rank's own rows stay exact.  All ranks must agree on ``taco``."""
 
     STORE, BIAS, BIAS_GELU, GELU_BWD = 0, 1, 2, 3
 
-    def __init__(self, tp, rows, cols):
+    def __init__(self, tp, rows, cols, taco=False):
         import torch
         from .symmetric import SymmetricHeap
-        if rows % 256 or cols % 64:
-            raise ValueError("the fused all-gather GEMM needs rows % 256 == 0 and K % 64 == 0")
+        if rows % 256 or cols % 64 or (taco and cols % 128):
+            raise ValueError("the fused all-gather GEMM needs rows % 256 == 0 and K % 64 == 0 (K % 128 compressed)")
         self.tp, self.rows, self.cols = tp, int(rows), int(cols)
+        self.taco = bool(taco)
         self.heap = SymmetricHeap(tp, int(native.lib().tdb_ag_region_bytes(self.rows, self.cols)))
         dev = self.heap.device
         self.state = torch.zeros(2, dtype=torch.int32, device=dev)
@@ -139,7 +145,7 @@ class SymmAgGemm:
             0 if aux is None else aux.data_ptr(), 0 if aux_t is None else aux_t.stride(0),
             0 if aux_out is None else aux_out.data_ptr(), float(alpha), bn, self._table(N, bn).data_ptr(),
             self.heap.peers.data_ptr(), self.tp.world, self.tp.rank, 0, self.state.data_ptr(),
-            self.ready.data_ptr(), PEER_WAIT_SECONDS, native.stream_ptr()), "fused all-gather GEMM")
+            self.ready.data_ptr(), PEER_WAIT_SECONDS, int(self.taco), native.stream_ptr()), "fused all-gather GEMM")
         self.calls += 1
         if mode == self.BIAS_GELU:
             return out, full, aux_out

@@ -62,10 +62,10 @@ class Trainer:
     into fixed device buffers before each replay."""
 
     def __init__(self, config, arm="flux", group=None, *, device="cuda", seed=1234, operator_factory=None,
-                 execution_plan=None, cuda_graph=False, graph_warmup=2):
+                 execution_plan=None, cuda_graph=False, graph_warmup=2, taco_allgather=False):
         import torch
         self.model = GPT(config, arm, group, device=device, seed=seed, operator_factory=operator_factory,
-                         execution_plan=execution_plan)
+                         execution_plan=execution_plan, taco_allgather=taco_allgather)
         c = self.config = self.model.config
         self.optimizer = Optimizer(self.model, c["learning_rate"], c["weight_decay"], c["max_grad_norm"])
         for op in self.model.operators:  # block-scaled FP8 operators re-quantize weights once per step

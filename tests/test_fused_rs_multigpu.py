@@ -171,6 +171,31 @@ def _worker(rank, world, init_file, result_path):
         torch.cuda.synchronize()
         native.raise_on_status()
         out["ag_gemm"] = dict(full_equal=same, max_rel=max(errs))
+        # compressed gather: peers' rows decoded from TACO packets, own rows exact
+        from tempname_dcu_b200.ops.codec import codec, packet_bytes
+        aggt = SymmAgGemm(tp, rows, K, taco=True)
+        c = codec()
+        tsame, terrs = [], []
+        w = (torch.randn(1536, K, device="cuda") / 32).to(torch.bfloat16)
+        for rep in range(3):
+            xl = torch.randn(rows, K, device="cuda").to(torch.bfloat16)
+            ref_full = torch.empty(rows * world, K, dtype=torch.bfloat16, device="cuda")
+            dist.all_gather_into_tensor(ref_full, xl, group=group)
+            expect = ref_full.clone()
+            for s in range(world):
+                if s != rank:
+                    blk = ref_full[s * rows:(s + 1) * rows].contiguous()
+                    pk = torch.empty(packet_bytes(blk.numel()), dtype=torch.uint8, device="cuda")
+                    c.encode(blk, pk)
+                    c.decode(pk, expect[s * rows:(s + 1) * rows])
+            y, full = aggt(xl, w, mode=aggt.STORE)
+            torch.cuda.synchronize()
+            tsame.append(bool(torch.equal(full, expect)))
+            terrs.append(rel(y, expect.float() @ w.float().t()))
+        native.raise_on_status()
+        out["ag_gemm_taco"] = dict(full_equal=tsame, max_rel=max(terrs),
+                                   vs_bf16=rel(full, ref_full))
+        aggt.close()
         from tempname_dcu_b200.runtime import initialize_context
         out["canaries"] = [agg.heap.canaries_intact(), initialize_context(group).heap.canaries_intact()]
         agg.close()
@@ -198,9 +223,11 @@ def test_fused_gemm_rs_all_arms(tmp_path):
     res = json.load(open(path))
     assert res.get("allgather") and all(res["allgather"]), res.get("allgather")
     assert all(res["ag_gemm"]["full_equal"]) and res["ag_gemm"]["max_rel"] < 1e-2, res["ag_gemm"]
+    t = res["ag_gemm_taco"]
+    assert all(t["full_equal"]) and t["max_rel"] < 1e-2 and 0 < t["vs_bf16"] < 0.05, t
     assert all(res["canaries"]), res["canaries"]
     for key, value in res.items():
-        if key in ("allgather", "ag_gemm", "canaries"):
+        if key in ("allgather", "ag_gemm", "ag_gemm_taco", "canaries"):
             continue
         if key.startswith("bitwise"):
             assert all(value.values()), (key, value)
