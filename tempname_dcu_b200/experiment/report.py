@@ -279,7 +279,8 @@ def replay(root):
                   implementation="fused tcgen05 GEMM + NVLink reduce-scatter kernel (tempname_dcu_b200)",
                   backend=p.BACKEND, original_cuda_flux=False, environment_identity=environment,
                   timing=config["timing"], recommended_image=p.RECOMMENDED_IMAGE, trials=plan["trials"],
-                  blocks=plan["blocks"], arms=list(arms), counterbalanced=p.balanced(plan["blocks"], arms),
+                  blocks=plan["blocks"], arms=list(arms), selective_mode=config.get("selective_mode", "wire"),
+                  counterbalanced=p.balanced(plan["blocks"], arms),
                   ci_available=p.balanced(plan["blocks"], arms) and bool(samples["operator"]),
                   short_run=not p.balanced(plan["blocks"], arms), all_windows_retained=True, correctness_passed=True,
                   full_quantized_trajectories_identical=bool(trajectories)
@@ -302,7 +303,12 @@ def markdown(report):
     lines = ["# B200 five-arm experiment", "",
              f"Protocol `{report['protocol']}`; completed scope `{report['completed_scope']}`; "
              f"world size {report['world_size']}.", "",
-             "Implementation: one fused tcgen05 GEMM + NVLink reduce-scatter kernel per projection call.", ""]
+             "Implementation: one fused tcgen05 GEMM + NVLink reduce-scatter kernel per projection call.", "",
+             f"Arms: {', '.join(report.get('arms', p.ARMS))}; selective arm mode: "
+             f"{report.get('selective_mode', 'wire')} ("
+             + ("calibrated blocks computed as block-scaled FP8 MMAs, BF16 on the wire"
+                if report.get("selective_mode") == "fp8-mma" else "calibrated blocks sent as TACO packets") + ").",
+             ""]
     if report["short_run"]:
         lines += ["Short run (not a balanced 10-block cycle): no confidence intervals.", ""]
     lines += [f"Training windows: {report['training_windows']}; formal optimizer steps: "
