@@ -303,7 +303,8 @@ def test_replay_accepts_an_arm_subset(tmp_path):
 def test_replay_checks_the_fp8_mma_selective_contract(tmp_path):
     out = _fixture(tmp_path, ["--selective-mode", "fp8-mma"])
     report = R.replay(out)
-    assert report["completed"]
+    assert report["completed"] and report["selective_mode"] == "fp8-mma"
+    assert "selective arm mode: fp8-mma" in R.markdown(report)
     sel = next(j["directory"] for j in json.loads((out / "plan.json").read_text())["jobs"]
                if j["stage"] == "operator" and j["arm"] == p.SELECTIVE)
 
