@@ -64,17 +64,6 @@ __device__ __forceinline__ const uint16_t* src_slot(const Pull& a, int r, uint32
 
 __device__ __forceinline__ void named_sync_epilogue() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* addr, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
-  return v;
-}
-__device__ __forceinline__ void red_release_gpu(uint32_t* addr, uint32_t v) {
-  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
-}
 
 // Compressed gather: decode `nrows` rows starting at r0 of source s's TACO
 // packets into the gathered buffer; one warp per H128 group, four groups'

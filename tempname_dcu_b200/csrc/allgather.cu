@@ -84,14 +84,6 @@ __global__ void __launch_bounds__(256) ag_stage_taco_kernel(const uint16_t* __re
   }
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* addr, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
-  return v;
-}
 
 __global__ void __launch_bounds__(kThreads) ag_pull_kernel(Params p, int* status) {
   __shared__ int s_ok;

@@ -95,23 +95,6 @@ __device__ __forceinline__ uint32_t* flag_ptr(const Params& p, int rank_of_heap,
                                      (uint64_t(call_set(p) * p.per + within) * p.W + source) * 4);
 }
 
-__device__ __forceinline__ void red_release_sys(uint32_t* addr, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* addr) {
-  uint32_t v;
-  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
-  return v;
-}
 
 // One thread encodes one H128 group held in registers (values already BF16
 // rounded).  Same math as codec.cuh; the butterfly pairs and their order are
