@@ -105,8 +105,8 @@ __device__ __forceinline__ void decode_rows(const Pull& a, int s, uint32_t parit
 // Executed by the 128 epilogue threads of every CTA before their first tile.
 // `s_ok` is the epilogue scratch word of the mainloop's barrier slot (no static
 // shared memory: the dynamic allocation already uses the per-block maximum).
-__device__ void pull_rows(const Pull& a, volatile int& s_ok, int* status) {
-  const int et = int(threadIdx.x) - 64;  // epilogue warps are 2..5
+// `et` is the thread's index among the 128 pulling threads (four warps).
+__device__ void pull_rows(const Pull& a, volatile int& s_ok, int* status, int et) {
   const uint32_t epoch = __ldg(a.state), parity = __ldg(a.state + 1);
   if (blockIdx.x == 0 && et == 0) {
     __threadfence_system();  // the staged rows (previous kernel) before the publish
@@ -173,43 +173,52 @@ __device__ void pull_rows(const Pull& a, volatile int& s_ok, int* status) {
   }
 }
 
-template <class Inner>
+// AUX = false: the epilogue warps (2..5) pull before their first tile, so the
+// epilogue of the first tiles waits for the whole pull.  AUX = true: four
+// extra warps (6..9) pull while the epilogue warps drain finished tiles.
+template <class Inner, bool AUX>
 struct PullEpi {
   const EpiParams& p;
   const Pull& a;
   Inner inner;
   static constexpr int kSmemBytes = Inner::kSmemBytes;
+  static constexpr int kAuxWarps = AUX ? 4 : 0;
   __device__ __forceinline__ PullEpi(const EpiParams& ep, const Pull& pull) : p(ep), a(pull), inner{ep} {}
   int* scratch = nullptr;
   __device__ __forceinline__ void set_smem(uint8_t* s) {
     scratch = reinterpret_cast<int*>(s - 16);
     inner.set_smem(s);
   }
-  __device__ __forceinline__ void prologue(int* status) { pull_rows(a, *scratch, status); }
+  __device__ __forceinline__ void prologue(int* status) {
+    if constexpr (!AUX) pull_rows(a, *scratch, status, int(threadIdx.x) - 64);
+  }
+  __device__ __forceinline__ void aux(int* status) {
+    if constexpr (AUX) pull_rows(a, *scratch, status, int(threadIdx.x) - 192);
+  }
   __device__ __forceinline__ void tile_begin(int mb, int nb) { inner.tile_begin(mb, nb); }
   __device__ __forceinline__ void chunk(int row, int col, int c, const uint32_t (&r)[32]) { inner.chunk(row, col, c, r); }
   __device__ __forceinline__ void tile_end(int mb, int nb, int q, int lane) { inner.tile_end(mb, nb, q, lane); }
 };
 
-template <int BN, bool B_MN, int MODE>
-__global__ void __launch_bounds__(gemm::kThreads, 1)
+template <int BN, bool B_MN, int MODE, bool AUX>
+__global__ void __launch_bounds__(gemm::kThreads + (AUX ? 128 : 0), 1)
     ag_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int K,
                    TileOrder order, const __grid_constant__ EpiParams ep, const __grid_constant__ Pull pull,
                    int* status) {
   using Inner = typename gemm::EpiFor<MODE>::type;
-  PullEpi<Inner> epi(ep, pull);
+  PullEpi<Inner, AUX> epi(ep, pull);
   gemm::gemm_mainloop<BN, false, B_MN>(&tmA, &tmB, K, order, epi, status);
 }
 
 constexpr int k2Stages = 6;
 
-template <bool B_MN, int MODE>
-__global__ void __launch_bounds__(gemm2::kThreads, 1)
+template <bool B_MN, int MODE, bool AUX>
+__global__ void __launch_bounds__(gemm2::kThreads + (AUX ? 128 : 0), 1)
     ag_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int K,
                     TileOrder order, const __grid_constant__ EpiParams ep, const __grid_constant__ Pull pull,
                     int* status) {
   using Inner = typename gemm::EpiFor<MODE>::type;
-  using Epi = PullEpi<Inner>;
+  using Epi = PullEpi<Inner, AUX>;
   Epi epi(ep, pull);
   gemm2::mainloop<false, B_MN, Epi, k2Stages>(&tmA, &tmB, K, order, epi, status);
 }
@@ -243,12 +252,12 @@ static int launch_coop(Kern kern, dim3 grid, int threads, int smem, int cluster,
   return 0;
 }
 
-template <int BN, bool B_MN, int MODE>
+template <int BN, bool B_MN, int MODE, bool AUX>
 static int launch1(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, TileOrder order,
                    const EpiParams& ep, const Pull& pull, cudaStream_t s) {
   using Cfg = gemm::Config<BN>;
   constexpr int kSmem = Cfg::kSmemBytes + gemm::EpiFor<MODE>::type::kSmemBytes;
-  auto kern = ag_gemm_kernel<BN, B_MN, MODE>;
+  auto kern = ag_gemm_kernel<BN, B_MN, MODE, AUX>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -261,16 +270,17 @@ static int launch1(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   order.num_n = (N + BN - 1) / BN;
   order.num_tiles = order.num_m * order.num_n;
   const int grid = order.num_tiles < tdb_host::sm_count() ? order.num_tiles : tdb_host::sm_count();
-  return launch_coop(kern, dim3(grid), gemm::kThreads, kSmem, 1, s, ta, tb, K, order, ep, pull,
+  return launch_coop(kern, dim3(grid), gemm::kThreads + (AUX ? 128 : 0), kSmem, 1, s, ta, tb, K, order, ep, pull,
                      tdb_host::status_ptr());
 }
 
-template <bool B_MN, int MODE>
+template <bool B_MN, int MODE, bool AUX>
 static int launch2(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, TileOrder order,
                    const EpiParams& ep, const Pull& pull, cudaStream_t s) {
   using Cfg = gemm2::Config<k2Stages>;
   constexpr int kSmem = Cfg::kSmemBytes + gemm::EpiFor<MODE>::type::kSmemBytes;
-  auto kern = ag_gemm2_kernel<B_MN, MODE>;
+  constexpr int kBlock = gemm2::kThreads + (AUX ? 128 : 0);
+  auto kern = ag_gemm2_kernel<B_MN, MODE, AUX>;
   static int max_clusters[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -285,7 +295,7 @@ static int launch2(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(tdb_host::sm_count());
-    cfg.blockDim = dim3(gemm2::kThreads);
+    cfg.blockDim = dim3(kBlock);
     cfg.dynamicSmemBytes = kSmem;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
@@ -299,19 +309,30 @@ static int launch2(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   order.num_tiles = order.num_m * order.num_n;
   const int pairs = max_clusters[dev & 63];
   const int clusters = order.num_tiles < pairs ? order.num_tiles : pairs;
-  return launch_coop(kern, dim3(2 * clusters), gemm2::kThreads, kSmem, 2, s, ta, tb, K, order, ep, pull,
+  return launch_coop(kern, dim3(2 * clusters), kBlock, kSmem, 2, s, ta, tb, K, order, ep, pull,
                      tdb_host::status_ptr());
 }
+
+template <bool B_MN, int MODE, bool AUX>
+static int dispatch_tile_aux(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+                             const TileOrder& order, const EpiParams& ep, const Pull& pull, cudaStream_t s) {
+  switch (bn) {
+    case 512: return launch2<B_MN, MODE, AUX>(ta, tb, M, N, K, order, ep, pull, s);
+    case 256: return launch1<256, B_MN, MODE, AUX>(ta, tb, M, N, K, order, ep, pull, s);
+    case 192: return launch1<192, B_MN, MODE, AUX>(ta, tb, M, N, K, order, ep, pull, s);
+    default: return launch1<128, B_MN, MODE, AUX>(ta, tb, M, N, K, order, ep, pull, s);
+  }
+}
+
+// Pull placement of the following calls: 0 epilogue-warp prologue, 1 four
+// auxiliary warps (set with tdb_ag_set_variant).
+static int g_variant = 0;
 
 template <bool B_MN, int MODE>
 static int dispatch_tile(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
                          const TileOrder& order, const EpiParams& ep, const Pull& pull, cudaStream_t s) {
-  switch (bn) {
-    case 512: return launch2<B_MN, MODE>(ta, tb, M, N, K, order, ep, pull, s);
-    case 256: return launch1<256, B_MN, MODE>(ta, tb, M, N, K, order, ep, pull, s);
-    case 192: return launch1<192, B_MN, MODE>(ta, tb, M, N, K, order, ep, pull, s);
-    default: return launch1<128, B_MN, MODE>(ta, tb, M, N, K, order, ep, pull, s);
-  }
+  return g_variant == 1 ? dispatch_tile_aux<B_MN, MODE, true>(bn, ta, tb, M, N, K, order, ep, pull, s)
+                        : dispatch_tile_aux<B_MN, MODE, false>(bn, ta, tb, M, N, K, order, ep, pull, s);
 }
 
 template <bool B_MN>
@@ -345,6 +366,15 @@ TDB_API int tdb_ag_prepare(const void* x, long long ldx, long long rows, long lo
 //   ready: uint32 [W*rows/128] zero-initialised counters owned by this call site;
 //   tile_table: [tiles] production order (this rank's rows first) for tile code bn.
 // mode: 0 store (alpha), 1 bias, 2 bias + GELU (aux_out = pre-activation), 3 GELU backward (aux).
+// Pull placement of the fused all-gather GEMM for the following calls
+// (0: the epilogue warps pull before their first tile; 1: four auxiliary
+// warps pull concurrently); returns the previous value.
+TDB_API int tdb_ag_set_variant(int variant) {
+  const int old = tdb::aggemm::g_variant;
+  if (variant == 0 || variant == 1) tdb::aggemm::g_variant = variant;
+  return old;
+}
+
 TDB_API int tdb_ag_gemm(const void* x, long long ldx, void* full, long long rows, int K, const void* B, int b_mn,
                         long long ldb, void* C, long long ldc, int N, int mode, const void* bias, const void* aux,
                         long long ld_aux, void* aux_out, float alpha, int bn, const int* tile_table,

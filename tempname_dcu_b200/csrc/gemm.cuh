@@ -18,6 +18,8 @@
 // loops, drains in-flight copies / MMAs with bounded waits, frees TMEM and
 // returns with the status word set.  There is no TMA multicast.
 #pragma once
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace tdb {
@@ -123,6 +125,20 @@ __device__ __forceinline__ bool gate_wait(const TileOrder& order, int blk, int* 
   asm volatile("fence.proxy.async.global;" ::: "memory");
   return true;
 }
+
+// Auxiliary warps: an Epi may declare `static constexpr int kAuxWarps = n`
+// and a method `aux(int* status)`; the kernel then runs with n extra warps
+// (after the epilogue warps 2..5) that execute aux() concurrently with the
+// pipeline -- e.g. the fused all-gather's pull, so that it no longer delays
+// the epilogue of the first tiles.  Launches must add 32 * n threads.
+template <class E, class = void>
+struct AuxWarps {
+  static constexpr int value = 0;
+};
+template <class E>
+struct AuxWarps<E, std::void_t<decltype(E::kAuxWarps)>> {
+  static constexpr int value = E::kAuxWarps;
+};
 
 struct alignas(8) Barriers {
   uint64_t full[8];
@@ -321,6 +337,12 @@ __device__ __forceinline__ void gemm_mainloop(const CUtensorMap* tmA, const CUte
         umma_commit(&bars->drain);
         mbar_wait(&bars->drain, 0, status, 22);
       }
+    }
+  } else if (AuxWarps<Epi>::value > 0 && warp >= 6) {
+    // ---------------- Auxiliary warps (6..) ----------------
+    if constexpr (AuxWarps<Epi>::value > 0) {
+      epi.set_smem(reinterpret_cast<uint8_t*>(bars) + 256);
+      epi.aux(status);
     }
   } else {
     // ---------------- Epilogue (warps 2..5) ----------------

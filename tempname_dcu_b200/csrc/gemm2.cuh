@@ -240,6 +240,12 @@ __device__ __forceinline__ void mainloop(const CUtensorMap* tmA, const CUtensorM
         mbar_wait(&bars->drain, 0, status, 122);
       }
     }
+  } else if (gemm::AuxWarps<Epi>::value > 0 && warp >= 6) {
+    // auxiliary warps (see gemm::AuxWarps)
+    if constexpr (gemm::AuxWarps<Epi>::value > 0) {
+      epi.set_smem(reinterpret_cast<uint8_t*>(bars) + 256);
+      epi.aux(status);
+    }
   } else {
     epi.set_smem(reinterpret_cast<uint8_t*>(bars) + 256);
     epi.prologue(status);

@@ -36,6 +36,8 @@ def main(argv=None):
     ap.add_argument("--tile-n", type=int, default=0, help="fused kernel tile width (128 or 256; 0 = automatic)")
     ap.add_argument("--variant", type=int, default=None, choices=(0, 1, 2, 3),
                     help="fused GEMM-RS variant (bit 0 per-tile signals, bit 1 in-kernel consumer)")
+    ap.add_argument("--ag", action="store_true",
+                    help="also time the fused all-gather GEMMs (QKV, FC1 shapes) for both pull variants")
     ap.add_argument("--selective-mode", default="wire", choices=("wire", "fp8-mma"),
                     help="fp8-mma: the selective arm computes every block as block-scaled FP8 (BF16 on the wire)")
     args = ap.parse_args(argv)
@@ -114,6 +116,41 @@ def main(argv=None):
                              roofline_fraction=round(roof / us, 3), bound="link" if link_us > compute_us else "compute",
                              wire_bytes_per_rank=wire_bytes(m, n, world, quant), peak_source=source,
                              phases=phases))
+    if args.ag:
+        from ..parallel.allgather import SymmAgGemm, set_ag_variant
+        from ..parallel.tp import TPGroup
+        tp = TPGroup(group)
+        ml, h = m // world, 4096
+        agg = SymmAgGemm(tp, ml, h)
+        xl = torch.randn(ml, h, device="cuda").to(torch.bfloat16)
+        full = torch.empty(m, h, dtype=torch.bfloat16, device="cuda")
+        for role, n_out, mode in (("qkv", 3 * h // world, agg.BIAS), ("fc1", 16384 // world, agg.BIAS_GELU)):
+            w = (torch.randn(n_out, h, device="cuda") / 64).to(torch.bfloat16)
+            bias = torch.zeros(n_out, device="cuda", dtype=torch.bfloat16)
+            out = torch.empty(m, n_out, dtype=torch.bfloat16, device="cuda")
+            pre = torch.empty(m, n_out, dtype=torch.bfloat16, device="cuda")
+
+            def nccl():
+                dist.all_gather_into_tensor(full, xl)
+                if mode == agg.BIAS_GELU:
+                    G.linear_gelu(full, w, bias, pre_out=pre, out=out)
+                else:
+                    G.linear(full, w, bias, out=out)
+            base = timed(nccl)
+            gemm_only = timed(lambda: G.linear(full, w, bias, out=out))
+            flops = 2.0 * m * n_out * h
+            link = (world - 1) * ml * h * 2 / (NVLINK_GBS * 1e9) * 1e6
+            roof = max(flops / (peak * 1e12) * 1e6, link)
+            for variant in (0, 1):
+                set_ag_variant(variant)
+                us = timed(lambda: agg(xl, w, mode=mode, bias=bias, out=out, full=full,
+                                       **({"aux_out": pre} if mode == agg.BIAS_GELU else {})))
+                rows.append(dict(role=f"ag_{role}", pull_variant=variant, world=world, m=m, n=n_out, k=h,
+                                 fused_us=round(us, 2), nccl_ag_plus_gemm_us=round(base, 2),
+                                 gemm_only_us=round(gemm_only, 2), roofline_us=round(roof, 2),
+                                 roofline_fraction=round(roof / us, 3), peak_source=source))
+            set_ag_variant(0)
+        agg.close()
     native.raise_on_status()
     if rank == 0:
         for r in rows:

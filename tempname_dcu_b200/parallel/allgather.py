@@ -63,6 +63,17 @@ native.register("tdb_ag_gemm", [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_voi
                                 ctypes.c_int, ctypes.c_int, ctypes.c_ulonglong, ctypes.c_void_p, ctypes.c_void_p,
                                 ctypes.c_double, ctypes.c_int, ctypes.c_void_p])
 native.register("tdb_gemm_pick_tile", [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int])
+native.register("tdb_ag_set_variant", [ctypes.c_int])
+
+
+def set_ag_variant(variant):
+    """Where the fused all-gather GEMM pulls the gathered rows on this process:
+    0 = the epilogue warps before their first tile, 1 = four auxiliary warps
+    concurrently with the pipeline.  Results are bitwise the same; all ranks
+    must use the same variant.  Returns the previous one."""
+    if variant not in (0, 1):
+        raise ValueError("variant must be 0 or 1")
+    return int(native.lib().tdb_ag_set_variant(int(variant)))
 
 
 def ag_tile_table(world, rank, rows, n, bn):

@@ -142,11 +142,13 @@ def _worker(rank, world, init_file, result_path):
         from tempname_dcu_b200.parallel.allgather import SymmAgGemm
         import torch.nn.functional as F
         rows, K = 512, 1024
+        from tempname_dcu_b200.parallel.allgather import set_ag_variant
         agg = SymmAgGemm(tp, rows, K)
         errs, same = [], []
         def rel(a, b):
             return float((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30))
-        for N in (1536, 1000):
+        for N, variant in ((1536, 0), (1000, 0), (1536, 1), (1000, 1)):
+            set_ag_variant(variant)
             w = (torch.randn(N, K, device="cuda") / 32).to(torch.bfloat16)
             bias = torch.randn(N, device="cuda").to(torch.bfloat16)
             for rep in range(2):
@@ -168,6 +170,7 @@ def _worker(rank, world, init_file, result_path):
                 errs.append(rel(dz, zr.grad))
                 st, _ = agg(xl, w, mode=agg.STORE)
                 errs.append(rel(st, ref_full.float() @ w.float().t()))
+        set_ag_variant(0)
         torch.cuda.synchronize()
         native.raise_on_status()
         out["ag_gemm"] = dict(full_equal=same, max_rel=max(errs))
@@ -177,7 +180,8 @@ def _worker(rank, world, init_file, result_path):
         c = codec()
         tsame, terrs = [], []
         w = (torch.randn(1536, K, device="cuda") / 32).to(torch.bfloat16)
-        for rep in range(3):
+        for rep in range(4):
+            set_ag_variant(rep % 2)
             xl = torch.randn(rows, K, device="cuda").to(torch.bfloat16)
             ref_full = torch.empty(rows * world, K, dtype=torch.bfloat16, device="cuda")
             dist.all_gather_into_tensor(ref_full, xl, group=group)
@@ -192,6 +196,7 @@ def _worker(rank, world, init_file, result_path):
             torch.cuda.synchronize()
             tsame.append(bool(torch.equal(full, expect)))
             terrs.append(rel(y, expect.float() @ w.float().t()))
+        set_ag_variant(0)
         native.raise_on_status()
         out["ag_gemm_taco"] = dict(full_equal=tsame, max_rel=max(terrs),
                                    vs_bf16=rel(full, ref_full))
