@@ -42,6 +42,7 @@ native.register("tdb_gemm_rs_mx", list(native.SIGNATURES["tdb_gemm_rs"][:-1])
                 + [ctypes.c_void_p] * 5 + [ctypes.c_void_p])
 native.register("tdb_rs_advance", [ctypes.c_void_p, ctypes.c_uint, ctypes.c_void_p])
 native.register("tdb_rs_set_variant", [ctypes.c_int])
+native.register("tdb_gemm_rs_signals_per_block", [ctypes.c_int, ctypes.c_int, ctypes.c_int])
 
 
 def set_rs_variant(variant):
@@ -52,7 +53,7 @@ def set_rs_variant(variant):
     if variant not in (0, 1, 2, 3):
         raise ValueError("variant must be 0..3")
     return int(native.lib().tdb_rs_set_variant(int(variant)))
-native.register("tdb_gemm_rs_signals_per_block", [ctypes.c_int, ctypes.c_int, ctypes.c_int])
+
 
 _CONTEXTS = {}
 _LOCK = threading.Lock()
