@@ -1,0 +1,85 @@
+"""Host model of the fused GEMM -> reduce-scatter signalling protocol (CPU).
+
+Every rank makes the same sequence of calls.  Call c uses receive set
+``epoch & 1`` and counter target ``targets[set] += signals(c)``
+(``runtime.Context.next_call``, mirrored on the device by rs_advance_kernel).
+A producer writes its blocks into the destination's slots of that set and adds
+``signals`` to the (block, source) counters; a consumer waits until every
+counter of its blocks reaches the target, then reads.  On a rank the producer
+of call c+1 starts only after that rank's consumer of call c finished (stream
+order).  The simulation interleaves ranks at random and checks that a
+consumer never accepts a stale counter, never reads a slot still holding an
+older call, and that no producer overwrites a slot a consumer has not read
+yet -- the reuse argument for two receive sets.
+"""
+import random
+from types import SimpleNamespace
+
+import pytest
+
+from tempname_dcu_b200.runtime import Context
+
+
+def _device_advance(state, signals):
+    """The arithmetic of rs_advance_kernel (csrc/gemm_rs.cu) on a host list
+    {set, expected, epoch, target0, target1}."""
+    e = state[2]
+    s = e & 1
+    state[3 + s] += signals
+    state[0] = s
+    state[1] = state[3 + s]
+    state[2] = e + 1
+    return state[0], state[1]
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_two_receive_sets_are_reused_safely(seed):
+    rng = random.Random(seed)
+    world, per, calls = rng.choice([2, 4, 8]), 2, 40
+    signals = [rng.choice([4, 8, 64]) for _ in range(calls)]  # operators of different shapes interleave
+    host = SimpleNamespace(epoch=0, targets=[0, 0])
+    device = [0] * 5
+    plan = []
+    for c in range(calls):
+        expect = Context.next_call(host, signals[c])
+        assert _device_advance(device, signals[c]) == expect
+        plan.append(expect)
+    # shared memory of every rank: counters[set][within][source], slots[set][source][within] = call id
+    counters = [[[[0] * world for _ in range(per)] for _ in range(2)] for _ in range(world)]
+    slots = [[[[None] * per for _ in range(world)] for _ in range(2)] for _ in range(world)]
+    unread = [[[[False] * per for _ in range(world)] for _ in range(2)] for _ in range(world)]
+    # per rank: next call to produce / consume
+    produced, consumed = [0] * world, [0] * world
+    steps = 0
+    while min(consumed) < calls:
+        steps += 1
+        assert steps < 100000, "the protocol deadlocked"
+        r = rng.randrange(world)
+        if produced[r] == consumed[r] and produced[r] < calls:
+            c = produced[r]
+            s, _ = plan[c]
+            for dest in range(world):
+                for w in range(per):
+                    assert not unread[dest][s][r][w], "a producer overwrote a slot before it was read"
+                    slots[dest][s][r][w] = c
+                    unread[dest][s][r][w] = True
+                    counters[dest][s][w][r] += signals[c]
+            produced[r] += 1
+        elif consumed[r] < produced[r]:
+            c = consumed[r]
+            s, target = plan[c]
+            if all(counters[r][s][w][src] >= target for w in range(per) for src in range(world)):
+                for w in range(per):
+                    for src in range(world):
+                        assert counters[r][s][w][src] == target, "a counter ran ahead into the next use of the set"
+                        assert slots[r][s][src][w] == c, "consumer accepted a stale or newer slot"
+                        unread[r][s][src][w] = False
+                consumed[r] += 1
+
+
+def test_a_stale_counter_never_satisfies_the_next_use_of_its_set():
+    host = SimpleNamespace(epoch=0, targets=[0, 0])
+    seq = [Context.next_call(host, n) for n in (4, 8, 4, 8, 64)]
+    assert [s for s, _ in seq] == [0, 1, 0, 1, 0]
+    for (s0, t0), (s1, t1) in zip(seq, seq[2:]):
+        assert s0 == s1 and t1 > t0  # the counters left by call c are below call c+2's target
