@@ -83,3 +83,43 @@ def test_a_stale_counter_never_satisfies_the_next_use_of_its_set():
     assert [s for s, _ in seq] == [0, 1, 0, 1, 0]
     for (s0, t0), (s1, t1) in zip(seq, seq[2:]):
         assert s0 == s1 and t1 > t0  # the counters left by call c are below call c+2's target
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_all_gather_slots_are_reused_safely(seed):
+    """The NVLink all-gather (csrc/allgather.cu, csrc/ag_gemm.cu): a call
+    advances the epoch, stages this rank's rows into its send slot
+    [epoch & 1], publishes the epoch to every peer, then pulls each source's
+    slot once that source's published epoch reaches the call's.  A rank
+    starts call c+1 only after its pulls of call c finished.  No pull may read
+    a slot restaged for a later call, none may return an older call's rows."""
+    rng = random.Random(1000 + seed)
+    world, calls = rng.choice([2, 4, 8]), 30
+    slot = [[None, None] for _ in range(world)]          # slot[rank][parity] = call staged there
+    published = [[0] * world for _ in range(world)]      # published[reader][source] = epoch
+    pending = [set() for _ in range(world)]              # sources still to pull in the current call
+    call = [-1] * world
+    wanted = {}                                           # (source, parity) -> {reader: call it will pull}
+    steps = 0
+    while min(call) < calls - 1 or any(pending):
+        steps += 1
+        assert steps < 100000, "the all-gather deadlocked"
+        r = rng.randrange(world)
+        if not pending[r] and call[r] < calls - 1:
+            call[r] += 1
+            c, parity = call[r], (call[r] + 1) & 1          # epoch = c + 1
+            waiting = wanted.get((r, parity), {})
+            assert all(w >= c for w in waiting.values()), "a rank restaged a slot that a peer had not pulled"
+            slot[r][parity] = c
+            for peer in range(world):
+                published[peer][r] = c + 1
+            pending[r] = set(range(world))
+            for s in range(world):
+                wanted.setdefault((s, parity), {})[r] = c
+        elif pending[r]:
+            s = rng.choice(sorted(pending[r]))
+            c, parity = call[r], (call[r] + 1) & 1
+            if s == r or published[r][s] >= c + 1:
+                assert slot[s][parity] == c, "pulled rows of another call"
+                pending[r].discard(s)
+                del wanted[(s, parity)][r]
