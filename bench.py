@@ -4,7 +4,7 @@
     # N > 1: python -m torch.distributed.run --nnodes=1 --nproc-per-node N \
     #            --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...
 
-Workload: GPT-6.7B (32 layers, d_model 4096, 32 heads x 128,
+Workload (the headline configuration): GPT-6.7B (32 layers, d_model 4096, 32 heads x 128,
 FFN 16384 exact GELU, vocab 50257 padded to 50304, pre-LayerNorm, learned
 positions, seq 2048), micro-batch 1 x gradient accumulation 8 = 16384 tokens
 per optimizer step, bf16 compute with fp32 masters, AdamW, synthetic uniform

@@ -3,8 +3,8 @@
 Torch BF16 GEMMs (cuBLAS via ``F.linear``), ``scaled_dot_product_attention``,
 ``F.layer_norm``, NCCL all-gather / reduce-scatter for sequence parallelism,
 autograd, FP32-master AdamW from ``torch.optim`` -- none of this framework's
-kernels.  It is what ``bench.py --impl baseline`` times, for the
-"torch-BF16-GEMM + NCCL" comparison BASELINE.json asks for.
+kernels.  It is what ``bench.py --impl baseline`` times: the same-box
+"torch BF16 GEMM + NCCL" comparison point for the fused kernels.
 
 Reference parity: python/flux_dcu/model.py:65-476 (the same model and
 training-step semantics, with plain NCCL reduce-scatter in place of the
