@@ -15,6 +15,7 @@
 // saturates; the stored byte is e + 127.  An all-zero block stores byte 0.
 #include "gemm.cuh"
 #include "gemm_epi.cuh"
+#include "mx_scale.cuh"
 #include "tensor_map.h"
 
 namespace tdb {
@@ -34,16 +35,7 @@ __device__ __forceinline__ uint16_t e4m3x2(float lo, float hi) {
   return r;
 }
 
-// Scale exponent of a block whose absolute maximum is `amax` (see the file
-// comment), clamped to the ue8m0 range.
-__device__ __forceinline__ int block_exponent(float amax) {
-  const uint32_t bits = __float_as_uint(amax);
-  const int field = int((bits >> 23) & 0xFF);
-  if (field == 0) return -127;  // zero or subnormal: the smallest scale keeps it in range
-  // amax = (1 + f) 2^E;  448 = 1.75 * 2^8
-  int e = field - 127 - 8 + ((bits & 0x7FFFFF) > 0x600000 ? 1 : 0);
-  return e < -127 ? -127 : (e > 127 ? 127 : e);
-}
+using mx_scale::block_exponent;  // the scale rule (mx_scale.cuh)
 
 // One thread per (row, 32-value K block).  With `version` set the whole
 // kernel is skipped while *version == *seen (the operand has not changed

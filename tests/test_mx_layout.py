@@ -38,3 +38,36 @@ def test_zero_blocks_and_dequantize_error():
     d = mx.dequantize(q, mx.pack_scales(e, 128, 128))
     rel = ((d - x.float()).norm() / x.float().norm()).item()
     assert rel < 0.04
+
+
+def _host_scale_rule():
+    """The device scale rule (csrc/mx_scale.cuh) compiled for the host."""
+    import ctypes
+    import shutil
+    import subprocess
+    import tempfile
+    from pathlib import Path
+    import pytest
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not Path(nvcc).is_file():
+        pytest.skip("nvcc unavailable")
+    csrc = Path(__file__).resolve().parents[1] / "tempname_dcu_b200" / "csrc"
+    folder = Path(tempfile.mkdtemp(prefix="tdb-mx-"))
+    (folder / "h.cu").write_text('#include "mx_scale.cuh"\n'
+                                 'extern "C" int mx_exp(float a) { return tdb::mx_scale::block_exponent(a); }\n')
+    subprocess.run([nvcc, "-std=c++17", "-shared", "-Xcompiler", "-fPIC", "-I", str(csrc), str(folder / "h.cu"),
+                    "-o", str(folder / "h.so")], check=True, capture_output=True, text=True)
+    lib = ctypes.CDLL(str(folder / "h.so"))
+    lib.mx_exp.argtypes, lib.mx_exp.restype = [ctypes.c_float], ctypes.c_int
+    return lib
+
+
+def test_device_scale_rule_matches_the_torch_restatement_on_every_bf16():
+    lib = _host_scale_rule()
+    bits = torch.arange(0, 0x7F80, dtype=torch.int32).to(torch.int16)  # every finite non-negative bf16
+    values = bits.view(torch.bfloat16)
+    block = torch.zeros(values.numel(), 32, dtype=torch.bfloat16)
+    block[:, 5] = values  # a one-value block: amax is the value
+    _, ref = mx.quantize_reference(block)
+    got = torch.tensor([lib.mx_exp(v) for v in values.float().tolist()], dtype=ref.dtype)
+    assert torch.equal(got, ref[:, 0])
