@@ -20,6 +20,31 @@ import json
 import time
 
 
+# Kernel-name buckets for the per-category summary (first match wins).
+CATEGORIES = (
+    ("fused GEMM -> reduce-scatter", ("gemm_rs_kernel", "gemm_rs_mx_kernel", "rs_reduce_kernel", "rs_advance")),
+    ("fused all-gather -> GEMM", ("ag_gemm", "ag_pull", "ag_stage", "ag_advance")),
+    ("GEMM (tcgen05)", ("gemm_kernel", "gemm2_kernel", "gemm_mx_kernel")),
+    ("attention", ("attn",)),
+    ("NCCL", ("nccl",)),
+    ("LayerNorm / reductions", ("layernorm", "ln_", "colred", "colsum")),
+    ("cross-entropy", ("xent",)),
+    ("optimizer", ("adamw", "clip", "norm")),
+    ("embedding", ("embedding", "emb::", "position", "sort_tokens")),
+)
+
+
+def categorize(kernels):
+    """{category: (microseconds, launches)} for [{"name", "us", "count"}]."""
+    out = {}
+    for k in kernels:
+        name = k["name"].lower()
+        cat = next((c for c, keys in CATEGORIES if any(key.lower() in name for key in keys)), "other")
+        us, n = out.get(cat, (0.0, 0))
+        out[cat] = (us + k["us"], n + k["count"])
+    return out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=32)
@@ -90,6 +115,9 @@ def main(argv=None):
           f"host wall {wall * 1e3:.2f} ms")
     for name, (us, n) in rows[:40]:
         print(f"{us / 1e3:10.3f} ms {100 * us / total:6.2f}% x{n:<6d} {name[:110]}")
+    cats = categorize([dict(name=k, us=v[0], count=v[1]) for k, v in rows])
+    for cat, (us, n) in sorted(cats.items(), key=lambda kv: -kv[1][0]):
+        print(f"{us / 1e3:10.3f} ms {100 * us / total:6.2f}% x{n:<6d} [{cat}]")
     if model.trace_ranges:
         ranges = collections.defaultdict(lambda: [0.0, 0])
         for evt in prof.events():

@@ -72,3 +72,17 @@ def test_fp8_reference_dequantizes_close_to_the_input():
     values, e = mx.quantize_reference(x)
     deq = (values.view(128, -1, 32) * torch.exp2(e.float()).unsqueeze(-1)).view(128, 256)
     assert float((deq - x.float()).norm() / x.float().norm()) < 0.04
+
+
+def test_trace_categories_bucket_kernel_names():
+    from tempname_dcu_b200.utils.trace import categorize
+    kernels = [dict(name="void tdb::rs::gemm_rs_kernel<256, true>(...)", us=10.0, count=2),
+               dict(name="tdb::rs::rs_reduce_kernel(tdb::rs::Params, int*)", us=5.0, count=2),
+               dict(name="void tdb::aggemm::ag_gemm2_kernel<true, 11, false>(...)", us=7.0, count=1),
+               dict(name="void tdb::gemm::gemm2_kernel<true, true, 6>(...)", us=3.0, count=1),
+               dict(name="ncclDevKernel_ReduceScatter_Sum_bf16_RING_LL(...)", us=1.0, count=1),
+               dict(name="something_else", us=0.5, count=1)]
+    cats = categorize(kernels)
+    assert cats["fused GEMM -> reduce-scatter"] == (15.0, 4)
+    assert cats["fused all-gather -> GEMM"] == (7.0, 1)
+    assert cats["GEMM (tcgen05)"] == (3.0, 1) and cats["NCCL"] == (1.0, 1) and cats["other"] == (0.5, 1)
