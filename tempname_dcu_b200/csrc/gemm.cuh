@@ -84,7 +84,7 @@ struct TileOrder {
   const uint32_t* gate_epoch = nullptr;
   uint32_t gate_per_call = 0;
 
-  __device__ __forceinline__ void tile(int i, int& m_blk, int& n_blk) const {
+  __host__ __device__ __forceinline__ void tile(int i, int& m_blk, int& n_blk) const {
     if (table) {
       const int t = table[i];
       m_blk = t / num_n;
