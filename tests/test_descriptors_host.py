@@ -67,3 +67,35 @@ def test_descriptors_match_the_cutlass_bit_fields(tmp_path):
     assert build.returncode == 0, build.stderr[-3000:]
     run = subprocess.run([str(tmp_path / "d")], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0 and run.stdout.strip() == "0", run.stdout
+
+
+SF_PROGRAM = r'''
+#include <cute/tensor.hpp>
+#include <cutlass/detail/sm100_blockscaled_layout.hpp>
+#include <cstdio>
+int main() {
+  using Atom = cutlass::detail::Sm1xxBlockScaledBasicChunk<32>::SfKMajorAtom;
+  Atom a;
+  int bad = 0;
+  for (int r = 0; r < 128; ++r)
+    for (int k = 0; k < 128; ++k) bad += int(a(r, k)) != (r % 32) * 16 + (r / 32) * 4 + k / 32;
+  printf("%d %d\n", bad, int(cute::cosize(a)));
+  return bad != 0;
+}
+'''
+
+
+def test_scale_atom_matches_the_cutlass_sf_atom(tmp_path):
+    """Inside a 512-byte atom (128 rows x 128 K values, one ue8m0 per 32) the
+    byte of row r and K value k is (r % 32) * 16 + (r / 32) * 4 + k / 32 --
+    the order quantize_kernel writes and tcgen05.cp 32x128b.warpx4 expects."""
+    inc = _cutlass_include()
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if inc is None or not Path(nvcc).is_file():
+        pytest.skip("CUTLASS headers or nvcc unavailable")
+    (tmp_path / "sf.cu").write_text(SF_PROGRAM)
+    build = subprocess.run([nvcc, "-std=c++17", "-I", str(inc), str(tmp_path / "sf.cu"), "-o", str(tmp_path / "sf")],
+                           capture_output=True, text=True, timeout=600)
+    assert build.returncode == 0, build.stderr[-3000:]
+    run = subprocess.run([str(tmp_path / "sf")], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and run.stdout.split() == ["0", "512"], run.stdout
