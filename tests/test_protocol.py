@@ -328,7 +328,8 @@ def _retamper(out, directory, rank, mutate):
 
 
 @pytest.mark.parametrize("tamper", ["row_bytes", "gate", "wire_bytes", "schedule", "library", "source",
-                                    "calibration_time", "missing_rank", "diagnostic"])
+                                    "calibration_time", "missing_rank", "diagnostic", "environment", "call_count",
+                                    "calibration_seed", "operator_time"])
 def test_replay_rejects_tampering(tmp_path, tamper):
     out = _fixture(tmp_path)
     op_dir = next(d for d in json.loads((out / "plan.json").read_text())["jobs"] if d["stage"] == "operator")["directory"]
@@ -358,5 +359,16 @@ def test_replay_rejects_tampering(tmp_path, tamper):
     elif tamper == "diagnostic":
         _retamper(out, arrival_dir, 0, lambda r: r["operator_results"][0]["arrival_diagnostic"].update(
             ready_bypass_observed=False))
+    elif tamper == "environment":  # hardware identity drifts between workers
+        _retamper(out, op_dir, 1, lambda r: r["environment_identity"].update(device_name="H100"))
+    elif tamper == "call_count":  # an operator reports calls it did not make
+        _retamper(out, op_dir, 0, lambda r: r["operator_results"][0]["execution"].update(
+            calls=r["operator_results"][0]["execution"]["calls"] + 1))
+    elif tamper == "calibration_seed":
+        def mutate(row):
+            row["calibration_results"]["raw_samples"][0]["seed"] += 1
+        _retamper(out, "calibrate", 0, mutate)
+    elif tamper == "operator_time":  # a rank's time that is not a positive finite number
+        _retamper(out, op_dir, 1, lambda r: r["operator_results"][0].update(elapsed_seconds=-1.0))
     with pytest.raises((ValueError, FileNotFoundError, KeyError)):
         R.replay(out)
