@@ -187,12 +187,15 @@ def _diag(config, arm):
                 ready_bypass_observed=True, evidence=dict(events=events), ordinary_speedup_claim=False)
 
 
-def _fixture(tmp_path, extra=()):
-    """A complete operator-scope batch directory built by the real planner
-    (calibration replays from synthetic timings)."""
+def _fixture(tmp_path, extra=(), train=False):
+    """A complete batch directory built by the real planner (calibration
+    replays from synthetic timings): operator scope, or (``train``) the full
+    scope with training windows whose order-only TACO arms trained
+    identically."""
     from tempname_dcu_b200 import planning as P
+    scope = ["--steps", "2", "--warmup-steps", "1"] if train else ["--operator-only"]
     args = C.arguments(["--out", str(tmp_path / "run"), "--small-model", "--world-size", "2", "--blocks", "1",
-                        "--operator-only", "--operator-warmup", "1", "--operator-iters", "2",
+                        *scope, "--operator-warmup", "1", "--operator-iters", "2",
                         "--calibration-pairs", "1", "--quant-budget", "0.25", *extra])
     out = args.out
     files = C.source_files()
@@ -265,6 +268,31 @@ def _fixture(tmp_path, extra=()):
                                         execution=_state(model, world, row["rank"], job["arm"], role, calls,
                                                          execution_plan, config.get("selective_mode", "wire"))))
                 row.update(operator_results=results, initialization_sha256="a" * 64, input_sha256="b" * 64)
+        elif job["stage"] == "train":
+            steps, warm = config["timing"]["timed_steps"], config["timing"]["warmup_steps"]
+            total = (steps + warm) * model["accumulation_steps"]
+            counts = p.expected_parameter_counts(model, world)
+            # order-only TACO arms train bitwise identically; flux and the selective arm differ
+            same = job["arm"] in p.FULL_TACO_ARMS
+            tag = "taco" if same else job["arm"]
+            for row in rows:
+                states = [_state(model, world, row["rank"], job["arm"], "attn" if i % 2 == 0 else "mlp", total,
+                                 execution_plan, config.get("selective_mode", "wire")) for i in range(2 * model["layers"])]
+                for st in states:
+                    st["validation_calls"] = 1
+                row.update(timed_steps=steps, warmup_steps=warm, elapsed_seconds=0.5 + 0.01 * row["rank"],
+                           losses=[9.0 - 0.1 * i - (0 if same else 0.001) for i in range(steps)],
+                           grad_norms=[1.0 + 0.01 * i for i in range(steps)],
+                           initialization_sha256="c" * 64, input_sha256="d" * 64,
+                           final_parameters_sha256=_sha(tag.encode()), actual_model_config=dict(model),
+                           parameter_counts=counts, actual_parameters_per_rank=counts["parameters_per_rank"],
+                           tokens_per_step=model["sequence"] * model["micro_batch"] * model["accumulation_steps"],
+                           dtype="bfloat16", optimizer="AdamW-fp32-master",
+                           operator_counters=dict(model_forwards=steps * model["accumulation_steps"],
+                                                  target_modules=2 * model["layers"],
+                                                  actual_calls_per_instance=[total] * (2 * model["layers"])),
+                           operator_states=states,
+                           memory=dict(peak_allocated_bytes=1 << 30, peak_reserved_bytes=1 << 31))
         for row in rows:
             p.write(directory / f"rank{row['rank']}.json", row)
         done = dict(job=job, command_sha256=p.sha(directory / "command.json"),
@@ -312,6 +340,34 @@ def test_replay_checks_the_fp8_mma_selective_contract(tmp_path):
         row["operator_results"][0]["execution"]["fused_kernel"] = "tdb::rs::gemm_rs_kernel"
     _retamper(out, sel, 0, wire_mode)
     with pytest.raises(ValueError):
+        R.replay(out)
+
+
+def test_replay_accepts_training_windows(tmp_path):
+    out = _fixture(tmp_path, train=True)
+    report = R.replay(out)
+    assert report["completed"] and report["training_windows"] == len(p.ARMS)
+    assert report["full_quantized_trajectories_identical"]
+    arms = report["results"]["train"]["trial1"]["full_step"]["arms"]
+    assert set(arms) == set(p.ARMS) and all(v["tokens_per_second"] > 0 for v in arms.values())
+    assert "tokens/s" in R.markdown(report)
+
+
+@pytest.mark.parametrize("tamper", ["loss", "missing_window", "final_parameters", "bypassed_operator"])
+def test_replay_rejects_training_tampering(tmp_path, tamper):
+    out = _fixture(tmp_path, train=True)
+    jobs = json.loads((out / "plan.json").read_text())["jobs"]
+    taco = next(j["directory"] for j in jobs if j["stage"] == "train" and j["arm"] == "flux_taco_interleaved")
+    if tamper == "loss":  # an order-only arm whose loss differs from the other TACO arms
+        _retamper(out, taco, 0, lambda r: r["losses"].__setitem__(0, r["losses"][0] + 1e-6))
+    elif tamper == "missing_window":
+        completed = json.loads((out / "completed-jobs.json").read_text())
+        p.write(out / "completed-jobs.json", completed[:-1])
+    elif tamper == "final_parameters":
+        _retamper(out, taco, 1, lambda r: r.update(final_parameters_sha256="0" * 64))
+    elif tamper == "bypassed_operator":  # a projection that did not go through the fused operator
+        _retamper(out, taco, 0, lambda r: r["operator_counters"]["actual_calls_per_instance"].__setitem__(0, 1))
+    with pytest.raises((ValueError, FileNotFoundError, KeyError)):
         R.replay(out)
 
 
