@@ -70,11 +70,16 @@ def validate_config(config, world_size=8):
     return c
 
 
+MAX_MICRO_BATCH_TOKENS = 16384  # one-CTA stable token sort of the embedding gradient (tdb_sort_tokens)
+
+
 def native_shape_ok(c, world_size) -> bool:
     """True when the sm_100a kernels support this configuration (head_dim 128,
-    hidden and shard widths multiples of 8)."""
+    hidden and shard widths multiples of 8, at most 16384 tokens per
+    micro-batch)."""
     return (c["hidden"] // c["heads"] == HEAD_DIM and c["hidden"] % 8 == 0 and
-            (c["padded_vocab"] // world_size) % 8 == 0 and (c["ffn"] // world_size) % 8 == 0)
+            (c["padded_vocab"] // world_size) % 8 == 0 and (c["ffn"] // world_size) % 8 == 0 and
+            c["sequence"] * c["micro_batch"] <= MAX_MICRO_BATCH_TOKENS)
 
 
 def parameter_counts(config, world_size=8):

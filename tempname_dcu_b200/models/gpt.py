@@ -71,7 +71,8 @@ class GPT:
         self.world, self.rank = self.tp.world, self.tp.rank
         self.config = c = validate_config(config, self.world)
         if not native_shape_ok(c, self.world):
-            raise ValueError("the sm_100a kernels need head_dim 128 and 8-aligned shard widths")
+            raise ValueError("the sm_100a kernels need head_dim 128, 8-aligned shard widths and at most "
+                             "16384 tokens per micro-batch")
         if arm not in ARMS and arm != "nccl":
             raise ValueError(f"unknown arm {arm}")
         self.arm = arm

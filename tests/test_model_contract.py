@@ -132,3 +132,11 @@ def test_layer_ranges_are_named_only_when_enabled():
             torch.ones(3).sum()
     names = [e.name for e in prof.events() if e.name.startswith("tdb/")]
     assert names == ["tdb/layer1/bwd"]
+
+
+def test_native_shape_limits():
+    from tempname_dcu_b200.models.config import BENCH_CONFIG, native_shape_ok, validate_config
+    c = validate_config(dict(BENCH_CONFIG), 8)
+    assert native_shape_ok(c, 8)
+    assert not native_shape_ok(validate_config(dict(BENCH_CONFIG, micro_batch=16), 8), 8)  # 32768 tokens
+    assert not native_shape_ok(validate_config(dict(BENCH_CONFIG, heads=64), 8), 8)  # head_dim 64
