@@ -137,54 +137,7 @@ def test_trajectory_mismatch_rejected():
 
 
 # --------------------------------------------------------------- fixture
-def _sha(data: bytes):
-    return hashlib.sha256(data).hexdigest()
-
-
-def _state(model, world, rank, arm, role, calls, plan_bundle, selective_mode="wire"):
-    m = model["sequence"] * model["micro_batch"]
-    k = (model["hidden"] if role == "attn" else model["ffn"]) // world
-    role_plan = plan_bundle["roles"][role] if arm in (p.ARRIVAL, p.SELECTIVE) else None
-    lay = operator_layout(m, model["hidden"], k, world, rank, arm, role_plan, model["chunk_rows"])
-    from tempname_dcu_b200.mapping import selection_statistics
-    sel = selection_statistics(m, model["hidden"], world, model["chunk_rows"], lay["selection_mask"])
-    return dict(backend=p.BACKEND, arm=arm, rank=rank, calls=calls, shape=p.role_shape(model, world, role),
-                chunk_rows=model["chunk_rows"], production_schedule=lay["order"],
-                mapping_sha256=hashlib.sha256(json.dumps(lay["order"], sort_keys=True).encode()).hexdigest(),
-                gemms_per_call=1, collectives_per_call=1, fused_kernel="tdb::rs::gemm_rs_kernel",
-                quantization=("selective_remote_h128_e4m3" if arm == p.SELECTIVE else
-                              "none" if arm == "flux" else "all_remote_h128_e4m3"),
-                selection_mask=lay["selection_mask"],
-                selected_remote_blocks_by_source=sel["selected_remote_blocks_by_source"],
-                remote_wire_bytes_by_source=sel["remote_wire_bytes_by_source"],
-                remote_wire_bytes_per_source=sel["remote_wire_bytes_by_source"][rank],
-                actual_remote_wire_bytes_per_rank=sel["remote_wire_bytes_by_source"][rank],
-                plan_sha256=p.digest(role_plan) if role_plan is not None else None, reduction_order=list(range(world)),
-                rounding="bf16_after_each_source", scratch_bytes=1, original_cuda_flux=False, transport_lanes=2,
-                consumer_policy=lay["consumer_policy"], validation_calls=2, diagnostic_delay_cycles=0,
-                diagnostic_delay_in_normal_forward=False) | _fp8_fields(model, world, arm, lay, selective_mode)
-
-
-def _fp8_fields(model, world, arm, lay, selective_mode):
-    if selective_mode != "fp8-mma" or arm != p.SELECTIVE:
-        return {}
-    per = model["sequence"] * model["micro_batch"] // world // model["chunk_rows"]
-    bf16 = (world - 1) * per * model["chunk_rows"] * model["hidden"] * 2
-    return dict(selective_mode="fp8-mma", mma_block_mask=lay["selection_mask"], fused_kernel="tdb::rs::gemm_rs_mx_kernel",
-                quantization="selective_mma_e4m3_ue8m0_k32", remote_wire_bytes_by_source=[bf16] * world,
-                remote_wire_bytes_per_source=bf16, actual_remote_wire_bytes_per_rank=bf16)
-
-
-def _diag(config, arm):
-    if arm not in (p.ARRIVAL, p.SELECTIVE):
-        return None
-    base = p.expected_schedule(config["model"], config["world_size"], "flux_taco_interleaved")
-    pending = next(it["physical"] for it in base if it["lane"] == 0)
-    events = [dict(stage="consumer", physical=pending, lane=0, start_ms=0.0, end_ms=5.0),
-              dict(stage="consumer", physical=pending + 1, lane=1, start_ms=0.0, end_ms=1.0)]
-    return dict(passed=True, numerical_bitwise_equal=True, artificial=True, delayed_rank=0, delayed_lane=0,
-                delayed_physical=pending, delay_cycles=50_000_000, later_blocks_completed_before_pending=[pending + 1],
-                ready_bypass_observed=True, evidence=dict(events=events), ordinary_speedup_claim=False)
+from _fake_batch import _diag, _sha, _state, fake_rows  # noqa: E402
 
 
 def _fixture(tmp_path, extra=(), train=False):
@@ -192,7 +145,6 @@ def _fixture(tmp_path, extra=(), train=False):
     replays from synthetic timings): operator scope, or (``train``) the full
     scope with training windows whose order-only TACO arms trained
     identically."""
-    from tempname_dcu_b200 import planning as P
     scope = ["--steps", "2", "--warmup-steps", "1"] if train else ["--operator-only"]
     args = C.arguments(["--out", str(tmp_path / "run"), "--small-model", "--world-size", "2", "--blocks", "1",
                         *scope, "--operator-warmup", "1", "--operator-iters", "2",
@@ -208,11 +160,9 @@ def _fixture(tmp_path, extra=(), train=False):
     library = b"stand-in native library"
     (out / "build").mkdir(parents=True)
     (out / "build" / "libtdb.so").write_bytes(library)
-    build = dict(library_sha256=_sha(library), identity=dict(source_sha256="e" * 64))
     p.write(out / "source-manifest.json", manifest)
     p.write(out / "plan.json", plan)
     config, world, model = plan["config"], 2, plan["config"]["model"]
-    env = dict(device_name="B200", host="h")
     completed, execution_plan = [], None
     for job in plan["jobs"]:
         directory = out / "results" / job["directory"]
@@ -220,79 +170,10 @@ def _fixture(tmp_path, extra=(), train=False):
         job_config = p.config_for_job(config, job, execution_plan)
         p.write(directory / "config.json", job_config)
         p.write(directory / "command.json", dict(job=job, command=["x"], environment={}))
-        rows = []
-        for rank in range(world):
-            row = dict(rank=rank, world_size=world, stage=job["stage"], arm=job["arm"], run_id=config["run_id"],
-                       completed=True, passed=True, execution_plan_sha256=job_config.get("execution_plan_sha256"),
-                       backend=p.BACKEND, original_cuda_flux=False, environment_identity=env, codec_build=build)
-            rows.append(row)
-        if job["stage"] == "calibrate":
-            samples = []
-            roles = {}
-            for index, role in enumerate(("attn", "mlp")):
-                m, n, k = p.role_shape(model, world, role)
-
-                def evaluate(cand, seed, arm, label, role=role):
-                    t = 1.0 - 0.001 * sum(cand["selective_mask"])
-                    samples.append(dict(role=role, label=label, seed=seed, arm=arm,
-                                        plan_digest=P.role_digest(cand), arrival_order=cand["arrival_order"],
-                                        selective_mask=cand["selective_mask"], iterations=config["calibration"]["iterations"],
-                                        warmup=config["calibration"]["warmup"], max_rank_elapsed_seconds=t,
-                                        bf16_relative_l2=0.01, codec_reference_relative_l2=0.001,
-                                        correctness_passed=True))
-                    return t
-                roles[role] = P.fit_role(m, n, k, world, model["chunk_rows"], evaluate, config=config["calibration"],
-                                         seed=8_000_000 + 10_000_000 * index + config["seed"])
-            bundle = dict(schema=P.SCHEMA, world_size=world, transport_lanes=2, roles=roles)
-            for row in rows:
-                mine = [dict(s, local_elapsed_seconds=s["max_rank_elapsed_seconds"] * (1 if row["rank"] else 0.9))
-                        for s in samples]
-                name = f"calibration-rank{row['rank']}-samples.json"
-                p.write(directory / name, dict(schema="b200-calibration-samples-v1", rank=row["rank"], samples=mine))
-                row.update(calibration_plan=bundle, calibration_results=dict(
-                    plan_sha256=p.digest(bundle), raw_samples=mine, raw_samples_file=name))
+        rows, bundle = fake_rows(job, job_config, directory, _sha(library), world)
+        if bundle is not None:
             execution_plan = bundle
             p.write(out / "selection-plan.json", bundle)
-        elif job["stage"] == "operator":
-            calls = 2 + config["timing"]["operator_warmup"] + config["timing"]["operator_iterations"]
-            for row in rows:
-                results = []
-                for role in ("attn", "mlp"):
-                    results.append(dict(role=role, elapsed_seconds=0.001 * (1 + row["rank"]),
-                                        timed_iterations=config["timing"]["operator_iterations"],
-                                        correctness_passed=True, bf16_relative_l2=0.004,
-                                        codec_reference_relative_l2=0.001, changed_input_relative_l2=0.001,
-                                        order_bitwise_equal=True if job["arm"] != "flux" else None,
-                                        full_gemm_only_seconds=0.0005, profile=None,
-                                        arrival_diagnostic=_diag(config, job["arm"]),
-                                        execution=_state(model, world, row["rank"], job["arm"], role, calls,
-                                                         execution_plan, config.get("selective_mode", "wire"))))
-                row.update(operator_results=results, initialization_sha256="a" * 64, input_sha256="b" * 64)
-        elif job["stage"] == "train":
-            steps, warm = config["timing"]["timed_steps"], config["timing"]["warmup_steps"]
-            total = (steps + warm) * model["accumulation_steps"]
-            counts = p.expected_parameter_counts(model, world)
-            # order-only TACO arms train bitwise identically; flux and the selective arm differ
-            same = job["arm"] in p.FULL_TACO_ARMS
-            tag = "taco" if same else job["arm"]
-            for row in rows:
-                states = [_state(model, world, row["rank"], job["arm"], "attn" if i % 2 == 0 else "mlp", total,
-                                 execution_plan, config.get("selective_mode", "wire")) for i in range(2 * model["layers"])]
-                for st in states:
-                    st["validation_calls"] = 1
-                row.update(timed_steps=steps, warmup_steps=warm, elapsed_seconds=0.5 + 0.01 * row["rank"],
-                           losses=[9.0 - 0.1 * i - (0 if same else 0.001) for i in range(steps)],
-                           grad_norms=[1.0 + 0.01 * i for i in range(steps)],
-                           initialization_sha256="c" * 64, input_sha256="d" * 64,
-                           final_parameters_sha256=_sha(tag.encode()), actual_model_config=dict(model),
-                           parameter_counts=counts, actual_parameters_per_rank=counts["parameters_per_rank"],
-                           tokens_per_step=model["sequence"] * model["micro_batch"] * model["accumulation_steps"],
-                           dtype="bfloat16", optimizer="AdamW-fp32-master",
-                           operator_counters=dict(model_forwards=steps * model["accumulation_steps"],
-                                                  target_modules=2 * model["layers"],
-                                                  actual_calls_per_instance=[total] * (2 * model["layers"])),
-                           operator_states=states,
-                           memory=dict(peak_allocated_bytes=1 << 30, peak_reserved_bytes=1 << 31))
         for row in rows:
             p.write(directory / f"rank{row['rank']}.json", row)
         done = dict(job=job, command_sha256=p.sha(directory / "command.json"),
@@ -428,3 +309,40 @@ def test_replay_rejects_tampering(tmp_path, tamper):
         _retamper(out, op_dir, 1, lambda r: r["operator_results"][0].update(elapsed_seconds=-1.0))
     with pytest.raises((ValueError, FileNotFoundError, KeyError)):
         R.replay(out)
+
+
+FAKE_WORKER = r'''
+import sys
+from pathlib import Path
+sys.path.insert(0, sys.argv[3])
+from _fake_batch import fake_rows
+from tempname_dcu_b200.experiment import protocol as p
+directory, out = Path(sys.argv[1]), Path(sys.argv[2])
+cfg = p.read(directory / "config.json")
+rows, _ = fake_rows(cfg["job"], cfg, directory, p.sha(out / "build" / "libtdb.so"), cfg["world_size"])
+for row in rows:
+    p.write(directory / f"rank{row['rank']}.json", row)
+'''
+
+
+@pytest.mark.parametrize("scope", [["--operator-only"], ["--steps", "2", "--warmup-steps", "1"]])
+def test_execute_runs_the_job_sequence_and_writes_an_auditable_report(tmp_path, monkeypatch, scope):
+    """controller.execute end to end with a stand-in worker per job: snapshot,
+    frozen plan, calibration freeze, per-job validation, trajectory checks,
+    report, batch state -- and the result passes the read-only replay."""
+    tests_dir = str(Path(__file__).resolve().parent)
+
+    def command(python, source_root, directory, job, world):
+        return [python, "-c", FAKE_WORKER, str(directory), str(out), tests_dir]
+    monkeypatch.setattr(C, "command_for", command)
+    args = C.arguments(["--execute", "--out", str(tmp_path / "run"), "--small-model", "--world-size", "2",
+                        "--blocks", "1", *scope, "--operator-warmup", "1", "--operator-iters", "2",
+                        "--calibration-pairs", "1"])
+    out = args.out
+    C.execute(args)
+    state = json.loads((out / "batch-state.json").read_text())
+    assert state["completed"] and state["status"] in ("completed", "operator_completed")
+    report = R.replay(out)
+    assert report["completed"] and json.loads((out / "report.json").read_text())["run_id"] == report["run_id"]
+    assert (out / "report.md").read_text().startswith("# B200 five-arm experiment")
+    assert (out / "selection-plan.json").is_file() and (out / "sources" / "tempname_dcu_b200").is_dir()
