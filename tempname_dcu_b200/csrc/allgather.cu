@@ -20,6 +20,7 @@
 // Slot reuse: a rank rewrites slot[p] two calls later, after its previous
 // pull kernel has seen every peer's publish of the call in between, which
 // each peer issues only after finishing its own earlier pulls.
+#include "call_state.cuh"
 #include "codec.cuh"
 #include "common.cuh"
 
@@ -46,10 +47,7 @@ __device__ __forceinline__ uint16_t* slot(const Params& p, int r, uint32_t parit
   return reinterpret_cast<uint16_t*>(region(p, r) + kFlagsBytes + uint64_t(parity) * p.rows * p.cols * 2);
 }
 
-__global__ void ag_advance_kernel(uint32_t* state) {
-  state[0] += 1u;
-  state[1] = state[0] & 1u;
-}
+__global__ void ag_advance_kernel(uint32_t* state) { advance_ag_state(state); }
 
 __global__ void __launch_bounds__(kThreads) ag_stage_kernel(const uint16_t* __restrict__ x, int64_t ldx, Params p) {
   uint16_t* dst = slot(p, p.rank, __ldg(p.state + 1));

@@ -40,6 +40,7 @@
 #include <climits>
 #include <utility>
 
+#include "call_state.cuh"
 #include "codec.cuh"
 #include "gemm.cuh"
 #include "tensor_map.h"
@@ -594,13 +595,7 @@ constexpr int kReduceThreads = 256;
 
 // Per-call advance of the device call state (one thread): same arithmetic
 // as the host-side Context.next_call, so both agree in eager mode.
-__global__ void rs_advance_kernel(uint32_t* st, uint32_t signals) {
-  const uint32_t e = st[2], s = e & 1u;
-  st[3 + s] += signals;
-  st[0] = s;
-  st[1] = st[3 + s];
-  st[2] = e + 1u;
-}
+__global__ void rs_advance_kernel(uint32_t* st, uint32_t signals) { advance_rs_state(st, signals); }
 
 __global__ void __launch_bounds__(kReduceThreads, 2)
     rs_reduce_kernel(const __grid_constant__ Params p, int* status) {

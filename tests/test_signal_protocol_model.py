@@ -20,29 +20,49 @@ import pytest
 from tempname_dcu_b200.runtime import Context
 
 
-def _device_advance(state, signals):
-    """The arithmetic of rs_advance_kernel (csrc/gemm_rs.cu) on a host list
+@pytest.fixture(scope="module")
+def native_state():
+    """csrc/call_state.cuh (the arithmetic of rs_advance_kernel and
+    ag_advance_kernel) compiled for the host."""
+    import ctypes
+    import shutil
+    import subprocess
+    import tempfile
+    from pathlib import Path
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not Path(nvcc).is_file():
+        pytest.skip("nvcc unavailable")
+    csrc = Path(__file__).resolve().parents[1] / "tempname_dcu_b200" / "csrc"
+    folder = Path(tempfile.mkdtemp(prefix="tdb-state-"))
+    (folder / "s.cu").write_text('#include "call_state.cuh"\n'
+                                 'extern "C" void rs(unsigned* st, unsigned n) { tdb::advance_rs_state(st, n); }\n'
+                                 'extern "C" void ag(unsigned* st) { tdb::advance_ag_state(st); }\n')
+    subprocess.run([nvcc, "-std=c++17", "-shared", "-Xcompiler", "-fPIC", "-I", str(csrc), str(folder / "s.cu"),
+                    "-o", str(folder / "s.so")], check=True, capture_output=True, text=True)
+    lib = ctypes.CDLL(str(folder / "s.so"))
+    lib.rs.argtypes, lib.ag.argtypes = [ctypes.c_void_p, ctypes.c_uint], [ctypes.c_void_p]
+    return lib
+
+
+def _device_advance(lib, state, signals):
+    """One rs_advance_kernel step on a host copy of the device call state
     {set, expected, epoch, target0, target1}."""
-    e = state[2]
-    s = e & 1
-    state[3 + s] += signals
-    state[0] = s
-    state[1] = state[3 + s]
-    state[2] = e + 1
+    lib.rs(state, signals)
     return state[0], state[1]
 
 
 @pytest.mark.parametrize("seed", range(12))
-def test_two_receive_sets_are_reused_safely(seed):
+def test_two_receive_sets_are_reused_safely(seed, native_state):
+    import ctypes
     rng = random.Random(seed)
     world, per, calls = rng.choice([2, 4, 8]), 2, 40
     signals = [rng.choice([4, 8, 64]) for _ in range(calls)]  # operators of different shapes interleave
     host = SimpleNamespace(epoch=0, targets=[0, 0])
-    device = [0] * 5
+    device = (ctypes.c_uint * 5)()
     plan = []
     for c in range(calls):
         expect = Context.next_call(host, signals[c])
-        assert _device_advance(device, signals[c]) == expect
+        assert _device_advance(native_state, device, signals[c]) == expect
         plan.append(expect)
     # shared memory of every rank: counters[set][within][source], slots[set][source][within] = call id
     counters = [[[[0] * world for _ in range(per)] for _ in range(2)] for _ in range(world)]
@@ -83,6 +103,16 @@ def test_a_stale_counter_never_satisfies_the_next_use_of_its_set():
     assert [s for s, _ in seq] == [0, 1, 0, 1, 0]
     for (s0, t0), (s1, t1) in zip(seq, seq[2:]):
         assert s0 == s1 and t1 > t0  # the counters left by call c are below call c+2's target
+
+
+def test_all_gather_state_counts_epochs_and_alternates_slots(native_state):
+    import ctypes
+    st = (ctypes.c_uint * 2)()
+    seen = []
+    for _ in range(5):
+        native_state.ag(st)
+        seen.append((st[0], st[1]))
+    assert seen == [(1, 1), (2, 0), (3, 1), (4, 0), (5, 1)]  # call c: epoch c + 1, slot (c + 1) & 1
 
 
 @pytest.mark.parametrize("seed", range(12))
