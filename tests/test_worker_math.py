@@ -86,3 +86,20 @@ def test_trace_categories_bucket_kernel_names():
     assert cats["fused GEMM -> reduce-scatter"] == (15.0, 4)
     assert cats["fused all-gather -> GEMM"] == (7.0, 1)
     assert cats["GEMM (tcgen05)"] == (3.0, 1) and cats["NCCL"] == (1.0, 1) and cats["other"] == (0.5, 1)
+
+
+def test_fused_path_rooflines_for_gpt67b_tp8():
+    from tempname_dcu_b200.models.config import BENCH_CONFIG
+    from tempname_dcu_b200.ops import roofline as rf
+    paths = {p["name"]: p for p in rf.fused_paths(BENCH_CONFIG, 8)}
+    assert abs(paths["qkv.fwd"]["flops"] - 25.77e9) < 0.01e9 and paths["qkv.fwd"]["link_bytes"] == 14_680_064
+    assert abs(paths["fc2.fwd"]["flops"] - 34.36e9) < 0.01e9
+    taco = {p["name"]: p for p in rf.fused_paths(BENCH_CONFIG, 8, taco=True)}
+    assert taco["attn_out.fwd"]["link_bytes"] == 7_798_784  # the reference's TACO byte budget
+    us, bound = rf.roofline_us(paths["attn_out.fwd"], 1651.0, 770.0)
+    assert bound == "link" and abs(us - 14_680_064 / 770e3) < 1e-9
+    # per step: 8 micro-batches x (32 layers x 8 paths + LM head fwd / dgrad)
+    total = rf.step_roofline(BENCH_CONFIG, 8, tflops=1651.0, nvlink_gbs=770.0)
+    per_layer = sum(rf.roofline_us(p, 1651.0, 770.0)[0] for p in rf.fused_paths(BENCH_CONFIG, 8))
+    head = sum(rf.roofline_us(p, 1651.0, 770.0)[0] for p in rf.head_paths(BENCH_CONFIG, 8))
+    assert abs(total - 8 * (32 * per_layer + head)) < 1e-6
