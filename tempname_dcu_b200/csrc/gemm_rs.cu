@@ -2,36 +2,43 @@
 //
 //   out[rows of this rank] = bias + residual + sum_{s=0..W-1} (A_s @ W_s^T)[rows of this rank]
 //
-// One persistent kernel per call, two phases:
+// A call is a one-thread call-state advance (rs_advance_kernel) and two
+// kernels on the caller's stream:
 //
-// 1. Produce.  The tcgen05 mainloop (gemm.cuh) computes the full [m, N]
-//    partial product tile by tile in the order of a device tile table (the
-//    arm's production schedule: contiguous, the common interleave, or the
-//    calibrated arrival order).  The epilogue stores each 128 x BN tile straight
-//    into the destination rank's receive slot [source = this rank] through its
-//    peer pointer: BF16, or -- for blocks selected by the TACO mask and remote
-//    destinations -- H128/E4M3 encoded in registers (one thread owns one row's
-//    128-column group), so only compressed bytes cross NVLink.  After its
-//    stores each epilogue warp fences (system scope) and adds 1 to the
-//    destination's (block, source) counter with a release-ordered remote
-//    atomic.
-// 2. Consume.  Each CTA then reduces this rank's output blocks: it waits until
-//    all W sources of a block are complete (bounded acquire polling), decodes
-//    TACO sources in registers (one warp per H128 group) and adds the sources
-//    in rank order 0..W-1 with BF16 rounding after every addition, then adds
-//    the residual and the bias.  Consumer policy "ordered" walks blocks in
-//    schedule order with all CTAs; "per-lane ready" (arrival arms) splits the
-//    CTAs into two lanes (lane = within % 2) and each lane consumes whichever
-//    of its blocks is complete first.  Summation order never depends on
-//    arrival, so arms that only reorder are bitwise identical.
+// 1. Produce (gemm_rs_kernel, persistent).  The tcgen05 mainloop (gemm.cuh)
+//    computes the full [m, N] partial product tile by tile in the order of a
+//    device tile table (the arm's production schedule: contiguous, the common
+//    interleave, the calibrated arrival order, or remote-first for training).
+//    The epilogue stores each 128 x BN tile straight into the destination
+//    rank's receive slot [source = this rank] through its peer pointer: BF16,
+//    or -- for blocks selected by the TACO mask and remote destinations --
+//    H128/E4M3 encoded in registers (one thread owns one row's 128-column
+//    group), so only compressed bytes cross NVLink.  After its last tile each
+//    CTA issues one system-scope fence and release-adds the (block, source)
+//    counters of every tile it produced.  gemm_rs_mx_kernel is the same
+//    producer with the calibrated blocks' tiles as block-scaled FP8 MMAs.
+// 2. Consume (rs_reduce_kernel, all co-resident CTAs).  Each CTA reduces this
+//    rank's output blocks: it waits until all W sources of a block are
+//    complete (bounded acquire polling), decodes TACO sources in registers
+//    (one warp per H128 group) and adds the sources in rank order 0..W-1 with
+//    BF16 rounding after every addition, then adds the residual and the bias.
+//    Consumer policy "ordered" walks blocks in schedule order with all CTAs;
+//    "per-lane ready" (arrival arms) splits the CTAs into two lanes
+//    (lane = within % 2) and each lane consumes whichever of its blocks is
+//    complete first.  Summation order never depends on arrival, so arms that
+//    only reorder are bitwise identical.
+//
+// Params::variant selects alternatives (same results, measured slower):
+// per-warp signals right after each tile, and the consumer run inside the
+// producer kernel under a cooperative launch.
 //
 // Buffers live in the symmetric heap (symm.cu): receive slots
 // [2 sets][W sources][per blocks][chunk_rows * N * 2 bytes] and counters
-// [2 sets][per][W] (uint32, monotonically increasing; the host passes the
-// value that means "complete" for this call).  Calls alternate sets, which
-// makes reuse safe: a rank can only start call k+2 after every rank finished
-// consuming call k.  The launch is cooperative so all CTAs are co-resident.
-// Every wait is bounded by %globaltimer and reports through the status word.
+// [2 sets][per][W] (uint32, monotonically increasing; the call state holds
+// the value that means "complete" for this call).  Calls alternate sets,
+// which makes reuse safe: a rank can only start call k+2 after every rank
+// finished consuming call k.  Every wait is bounded by %globaltimer and
+// reports through the status word.
 //
 // Reference parity: python/flux_dcu/runtime.py:84-268 (FluxDCU: schedule,
 // TACO encode of remote blocks, two lanes, ordered vs per-lane-ready
