@@ -18,7 +18,11 @@
 //     while later blocks are still crossing NVLink;
 //   * the MMA warp and the TMA-store epilogue are the plain GEMM's.
 // The copy waits on other CTAs of the same grid, so the kernel is launched
-// cooperatively (all CTAs co-resident or no launch).  Peer readiness uses the
+// cooperatively (all CTAs co-resident or no launch).  Variant 1
+// (tdb_ag_set_variant) moves the pull onto four extra warps so that the
+// epilogue warps drain finished tiles while rows are still arriving.  With
+// taco = 1 the send slots hold TACO packets (allgather.cu stages them) and
+// the pull decodes peers' rows; a rank's own rows are copied exact.  Peer readiness uses the
 // all-gather protocol of allgather.cu (epoch published per source; slot
 // parity and epochs on the device).  The gathered rows stay in the output
 // buffer (the weight gradient reads them in the backward).  No TMA multicast.

@@ -11,6 +11,7 @@
 //   ag_advance  (1 thread)   epoch += 1 in a device state word, so a captured
 //                            CUDA graph replays with fresh epochs
 //   ag_stage    (grid)       copy this rank's rows into its send slot[parity]
+//                            (or, compressed, ag_stage_taco: TACO packets)
 //   ag_pull     (grid)       CTA 0 publishes "epoch ready" to every peer
 //                            (system fence, then a release store into the
 //                            peer's flag[rank]); every CTA waits (bounded) for

@@ -13,7 +13,10 @@
 //   warps 2..5  epilogue: tcgen05.ld 32x32b from TMEM -> registers -> Epi
 // Pipelines:
 //   smem ring of STAGES (A,B) tiles, full[] (TMA tx) / empty[] (tcgen05.commit)
-//   two TMEM accumulators (2*BN columns), tmem_full[] / tmem_empty[]
+//   two TMEM accumulators (2*BN columns), tmem_full[] / tmem_empty[] (one
+//   for 256-wide block-scaled FP8 tiles, whose scale columns need the room)
+// Optional: block-scaled FP8 tiles (MX = true, MxOperands) and auxiliary
+// warps after the epilogue warps (Epi::kAuxWarps, see AuxWarps).
 // Every mbarrier wait is bounded (common.cuh); on expiry the CTA abandons its
 // loops, drains in-flight copies / MMAs with bounded waits, frees TMEM and
 // returns with the status word set.  There is no TMA multicast.
