@@ -7,6 +7,10 @@ library's own pull kernel -- the NCCL all-gather is not on the data path.
 Epochs and slot parity live on the device, so calls can be captured in a
 CUDA graph.  Creation is collective (every rank, same order).
 
+``SymmAgGemm`` fuses the gather into the tcgen05 GEMM that consumes it
+(``csrc/ag_gemm.cu``), optionally TACO-compressed (``taco=True``);
+``set_ag_variant`` chooses where the rows are pulled.
+
 Reference parity: python/flux_dcu/model.py:75-81 (gather_rows).
 """
 from __future__ import annotations

@@ -2,13 +2,14 @@
 
 ``FluxB200(m, n, k, group, arm, codec=None, chunk_rows=128, plan=None)``
 computes the row-parallel projection ``out = RS(input @ weight^T) (+ residual
-+ bias)`` with ONE fused persistent kernel (``csrc/gemm_rs.cu``): tcgen05 GEMM
-tiles are produced in the arm's schedule (``mapping.schedule``) and pushed by
-the epilogue into the destination rank's receive slot over NVLink (BF16, or
-TACO-encoded for the selected blocks), and the same kernel then performs the
-ordered BF16 reduction of this rank's blocks, polling per-block counters --
-in schedule order ("ordered") or per lane, ready block first ("per-lane
-ready", arrival arms).
++ bias)`` with a fused producer / consumer kernel pair (``csrc/gemm_rs.cu``):
+tcgen05 GEMM tiles are produced in the arm's schedule (``mapping.schedule``)
+and pushed by the epilogue into the destination rank's receive slot over
+NVLink (BF16, or TACO-encoded for the selected blocks; with
+``selective_mode="fp8-mma"`` the selected blocks are computed as block-scaled
+FP8 MMAs instead), and the consumer performs the ordered BF16 reduction of
+this rank's blocks, polling per-block counters -- in schedule order
+("ordered") or per lane, ready block first ("per-lane ready", arrival arms).
 
 ``initialize_context`` / ``shutdown_context`` manage the per-(device, group)
 state shared by all operators: the symmetric heap (receive slots for two
