@@ -28,9 +28,8 @@ global grad norm) and :339-476 (train_window).
 """
 from __future__ import annotations
 
-import math
 
-from .config import HEAD_DIM, native_shape_ok, validate_config
+from .config import native_shape_ok, validate_config
 from .params import FlatParams, gpt_param_specs
 
 ARMS = ("flux", "flux_taco", "flux_taco_interleaved", "flux_taco_interleaved_arrival",
