@@ -28,7 +28,6 @@ global grad norm) and :339-476 (train_window).
 """
 from __future__ import annotations
 
-
 from .config import native_shape_ok, validate_config
 from .params import FlatParams, gpt_param_specs
 
