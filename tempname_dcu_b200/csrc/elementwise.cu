@@ -101,7 +101,8 @@ TDB_API int tdb_colsum(const void* x, int64_t ld, int rows, int cols, float* par
       tdb::colred::colred_partial<false><<<g1, tdb::colred::kThreads, 0, s>>>(
           static_cast<const uint16_t*>(x), ld, nullptr, 0, nullptr, nullptr, rows, cols, rpp, partial);
       tdb_host::launched(1);
-      tdb::colred::colred_finish<<<dim3((cols + 63) / 64, 1), 256, 0, s>>>(partial, nparts, cols, out, out,
+      // one quantity (grid y = 1): only out0 is written
+      tdb::colred::colred_finish<<<dim3((cols + 63) / 64, 1), 256, 0, s>>>(partial, nparts, cols, out, nullptr,
                                                                           accumulate);
       tdb_host::launched(1);
       return int(cudaGetLastError());
