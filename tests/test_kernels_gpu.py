@@ -267,3 +267,12 @@ def test_sort_tokens_is_a_stable_sort(cuda, n, vocab):
     st, order = k.sort_tokens(tokens)
     ref_t, ref_o = torch.sort(tokens, stable=True)
     assert torch.equal(st, ref_t) and torch.equal(order, ref_o)
+
+
+def test_native_library_is_the_in_tree_build(cuda):
+    from pathlib import Path
+    from tempname_dcu_b200.ops import _build, native
+    native.lib()
+    loaded = Path(native.LOADED_PATH).resolve()
+    assert loaded == _build.paths(_build.debug_requested())[0].resolve()
+    assert loaded.parent == (Path(__file__).resolve().parents[1] / "tempname_dcu_b200" / "_native")
