@@ -293,7 +293,26 @@ def main(argv=None):
     else:
         import json
         print(json.dumps(dict(preview=True, writes_files=False, uses_gpu=False, output=str(args.out),
-                              **plan_for(args)), ensure_ascii=False, indent=2))
+                              operator_rooflines=operator_rooflines(args), **plan_for(args)),
+                         ensure_ascii=False, indent=2))
+
+
+def operator_rooflines(args):
+    """Per role, the fused operator's roofline at the measured (or fallback)
+    peaks with BF16 and with TACO bytes on the link (preview only; no GPU)."""
+    if args.world_size < 2:
+        return None
+    from ..ops import roofline as rf
+    tflops, nvlink, source = rf.peaks()
+    out = dict(peaks=dict(bf16_tflops=tflops, nvlink_gbs=nvlink, source=source))
+    for taco in (False, True):
+        for path in rf.fused_paths(args.model, args.world_size, taco):
+            if path["name"] in ("attn_out.fwd", "fc2.fwd"):
+                us, bound = rf.roofline_us(path, tflops, nvlink)
+                role = "attn" if path["name"].startswith("attn") else "mlp"
+                out[f"{role}.{'taco' if taco else 'bf16'}"] = dict(us=round(us, 2), bound=bound,
+                                                                     link_bytes=int(path["link_bytes"]))
+    return out
 
 
 if __name__ == "__main__":
