@@ -14,6 +14,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include "tdb.h"  // prototypes of every exported entry point (checked against the definitions)
+
 #define TDB_API extern "C" __attribute__((visibility("default")))
 
 namespace tdb {

@@ -13,6 +13,7 @@
 // the allocation-free entry point): each CTA handles 16 rows, dgamma/dbeta
 // partials per CTA, then a fixed-order reduction.  Both are bitwise
 // deterministic (no floating-point atomics).
+#include <atomic>
 #include <mutex>
 
 #include "colred.cuh"
@@ -338,6 +339,14 @@ static int bwd_launch(const void* x, const void* g, const float* mean, const flo
   return int(cudaGetLastError());
 }
 
+// Every row kernel moves bf16 rows 16 bytes at a time (uint4), so each bf16
+// base pointer must be 16-byte aligned (H % 8 == 0 keeps every row aligned);
+// a misaligned view is refused with an error code instead of faulting.
+template <class... P>
+static bool rows_aligned(const P*... ptrs) {
+  return ((reinterpret_cast<uintptr_t>(ptrs) | ...) % 16) == 0;
+}
+
 static int pick_vpt(int H) {
   // threads = H / VPT must be a multiple of 32 and <= 1024
   for (int vpt : {8, 16, 32, 64}) {
@@ -356,9 +365,9 @@ TDB_API int tdb_layernorm_fwd(const void* x, const void* gamma, const void* beta
   const int vpt = pick_vpt(H);
   if (!vpt || rows <= 0) return tdb_host::fail(int(cudaErrorInvalidValue), "layernorm: unsupported hidden size %d", H);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
-                         reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) % 16) == 0;
-  if (aligned && H % 256 == 0 && H <= 4096) {
+  if (!rows_aligned(x, y, gamma, beta))
+    return tdb_host::fail(int(cudaErrorInvalidValue), "layernorm: x, y, gamma and beta must be 16-byte aligned");
+  if (H % 256 == 0 && H <= 4096) {
     switch (H / 256) {
       case 1: return fwd_warp_launch<1>(x, gamma, beta, y, mean, rstd, rows, eps, s);
       case 2: return fwd_warp_launch<2>(x, gamma, beta, y, mean, rstd, rows, eps, s);
@@ -386,12 +395,12 @@ TDB_API int tdb_layernorm_bwd(const void* x, const void* gamma, const float* mea
   if (!vpt || rows <= 0 || !partial)
     return tdb_host::fail(int(cudaErrorInvalidValue), "layernorm bwd: unsupported hidden size %d", H);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) |
-                         reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(gamma) |
-                         reinterpret_cast<uintptr_t>(dres) | reinterpret_cast<uintptr_t>(partial)) % 16) == 0;
+  if (!rows_aligned(x, dy, dx, gamma, dres, partial))
+    return tdb_host::fail(int(cudaErrorInvalidValue),
+                          "layernorm bwd: x, dy, dx, gamma, dres and the scratch must be 16-byte aligned");
   // warp-per-row path (its partials need ceil(rows/16)*2*H floats at most,
   // which is what tdb_layernorm_bwd_scratch_floats promises)
-  if (aligned && H % 256 == 0 && H <= 4096) {
+  if (H % 256 == 0 && H <= 4096) {
     switch (H / 256) {
       case 1: return bwd_fast_launch<1>(x, gamma, mean, rstd, dy, dres, dx, dgamma, dbeta, partial, rows, accumulate, s);
       case 2: return bwd_fast_launch<2>(x, gamma, mean, rstd, dy, dres, dx, dgamma, dbeta, partial, rows, accumulate, s);
@@ -437,7 +446,11 @@ TDB_API int tdb_layernorm_bwd(const void* x, const void* gamma, const float* mea
 //     limit (use tdb_layernorm_bwd with your own scratch for those).
 //   * The first call on a device looks up the array's device address with
 //     cudaGetSymbolAddress while that device is current, and caches it per
-//     device.  Make that first call before any stream capture begins.
+//     device (an atomic per device ordinal; the lookup itself runs under a
+//     mutex).  Make that first call before any stream capture begins.  The
+//     cached address is not refreshed after a cudaDeviceReset of that device.
+//   * x, dy, dx, gamma and dres (if given) must be 16-byte aligned, like every
+//     LayerNorm entry point; misaligned pointers return cudaErrorInvalidValue.
 //   * Nothing in the array has to start at zero: every partial that is read
 //     is written earlier by the same call.  The array keeps the contents of the
 //     last call.
@@ -450,7 +463,9 @@ namespace tdb {
 namespace ln {
 constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 20;
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
-static float* g_noalloc_addr[64];
+// device address of the array per device ordinal, looked up once; not
+// refreshed if the process resets a device (cudaDeviceReset) afterwards
+static std::atomic<float*> g_noalloc_addr[64];
 static std::mutex g_noalloc_mutex;
 }  // namespace ln
 }  // namespace tdb
@@ -464,6 +479,9 @@ TDB_API int tdb_layernorm_bwd_noalloc(const void* x, const void* gamma, const fl
   const int vpt = pick_vpt(H);
   if (!vpt || rows <= 0)
     return tdb_host::fail(int(cudaErrorInvalidValue), "layernorm bwd (no-alloc): unsupported hidden size %d", H);
+  if (!rows_aligned(x, dy, dx, gamma, dres))
+    return tdb_host::fail(int(cudaErrorInvalidValue),
+                          "layernorm bwd (no-alloc): x, dy, dx, gamma and dres must be 16-byte aligned");
   const int64_t need = int64_t((rows + kBwdRows - 1) / kBwdRows) * 2 * H;
   if (need > tdb::ln::kNoAllocScratchFloats)
     return tdb_host::fail(int(cudaErrorInvalidValue),
@@ -474,17 +492,18 @@ TDB_API int tdb_layernorm_bwd_noalloc(const void* x, const void* gamma, const fl
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return tdb_host::fail(int(e), "layernorm bwd (no-alloc): cudaGetDevice failed");
   if (dev < 0 || dev >= 64) return tdb_host::fail(int(cudaErrorInvalidDevice), "layernorm bwd (no-alloc): device %d", dev);
-  float* scratch = tdb::ln::g_noalloc_addr[dev];
+  float* scratch = tdb::ln::g_noalloc_addr[dev].load(std::memory_order_acquire);
   if (scratch == nullptr) {
     std::lock_guard<std::mutex> guard(tdb::ln::g_noalloc_mutex);
-    if (tdb::ln::g_noalloc_addr[dev] == nullptr) {
+    scratch = tdb::ln::g_noalloc_addr[dev].load(std::memory_order_relaxed);
+    if (scratch == nullptr) {
       void* p = nullptr;
       e = cudaGetSymbolAddress(&p, tdb::ln::g_noalloc_scratch);
       if (e != cudaSuccess)
         return tdb_host::fail(int(e), "layernorm bwd (no-alloc): cudaGetSymbolAddress failed on device %d", dev);
-      tdb::ln::g_noalloc_addr[dev] = static_cast<float*>(p);
+      scratch = static_cast<float*>(p);
+      tdb::ln::g_noalloc_addr[dev].store(scratch, std::memory_order_release);
     }
-    scratch = tdb::ln::g_noalloc_addr[dev];
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc;
