@@ -18,6 +18,7 @@ preview, snapshot, job loop, stop_process, batch-state.json).
 from __future__ import annotations
 
 import argparse
+import contextlib
 from datetime import datetime, timezone
 import os
 from pathlib import Path
@@ -145,43 +146,161 @@ def command_for(python, source_root, directory, job, world):
             "--out", str(directory), "--stage", job["stage"], "--arm", job["arm"]]
 
 
+# --------------------------------------------------------------- workers
+#
+# A job is one torchrun launch.  It runs in a session of its own, so the whole
+# tree it spawns (torchrun, its rank processes) forms one process group that
+# this controller can signal without touching anything else on the machine.
+
+_ESCALATION = ((signal.SIGTERM, 10.0), (signal.SIGKILL, 10.0))
+
+
 def stop_process(process):
-    """Terminate this controller's worker process group only (SIGTERM, then SIGKILL)."""
-    if process.poll() is not None:
-        return
-    try:
-        os.killpg(process.pid, signal.SIGTERM)
-        process.wait(timeout=10)
-    except ProcessLookupError:
-        pass
-    except subprocess.TimeoutExpired:
+    """Stop the worker group led by ``process``: each signal of the escalation
+    goes to that group only, and the next one is sent if the leader has not
+    exited within its grace period."""
+    for number, grace in _ESCALATION:
+        if process.poll() is not None:
+            return
         try:
-            os.killpg(process.pid, signal.SIGKILL)
+            os.killpg(process.pid, number)
         except ProcessLookupError:
-            pass
-        process.wait(timeout=10)
+            return
+        try:
+            process.wait(timeout=grace)
+            return
+        except subprocess.TimeoutExpired:
+            continue
+
+
+class WorkerGroup:
+    """One worker job: started in its own session with its output in
+    ``process.log``; ``run`` waits for it within the timeout and stops its
+    process group on any way out (timeout, interrupt, error)."""
+
+    PASSED_ENV = {"PYTHONDONTWRITEBYTECODE": "1", "PYTHONUNBUFFERED": "1"}
+    TAIL_LINES = 40
+
+    def __init__(self, command, directory, source_root):
+        self.command = command
+        self.log_path = directory / "process.log"
+        self.source_root = source_root
+
+    def environment(self):
+        env = dict(os.environ, PYTHONPATH=str(self.source_root), **self.PASSED_ENV)
+        env.setdefault("OMP_NUM_THREADS", "1")
+        return env
+
+    def run(self, timeout):
+        with self.log_path.open("w") as log:
+            process = subprocess.Popen(self.command, cwd=self.source_root, env=self.environment(), stdout=log,
+                                       stderr=subprocess.STDOUT, start_new_session=True)
+            try:
+                code = process.wait(timeout=timeout)
+            finally:
+                stop_process(process)  # no-op once the leader has exited
+        if code != 0:
+            lines = self.log_path.read_text(errors="replace").splitlines()[-self.TAIL_LINES:]
+            raise RuntimeError("worker exited %d (log: %s)\n%s" % (code, self.log_path, "\n".join(lines)))
 
 
 def launch(command, directory, source_root, timeout):
-    env = os.environ.copy()
-    env["PYTHONPATH"] = str(source_root)
-    env["PYTHONDONTWRITEBYTECODE"] = "1"
-    env["PYTHONUNBUFFERED"] = "1"
-    env.setdefault("OMP_NUM_THREADS", "1")
-    with (directory / "process.log").open("w") as log:
-        process = subprocess.Popen(command, stdout=log, stderr=subprocess.STDOUT, cwd=source_root, env=env,
-                                   start_new_session=True)
-        try:
-            code = process.wait(timeout=timeout)
-        except BaseException:
-            stop_process(process)
-            raise
-    if code:
-        tail = (directory / "process.log").read_text(errors="replace").splitlines()[-35:]
-        raise RuntimeError(f"worker exited {code}; {directory / 'process.log'}\n" + "\n".join(tail))
+    WorkerGroup(command, directory, source_root).run(timeout)
+
+
+# --------------------------------------------------------------- batch bookkeeping
+
+class BatchRecord:
+    """The batch directory's bookkeeping files: ``batch-state.json`` (status
+    and progress, rewritten on every transition) and ``completed-jobs.json``
+    (one entry per validated job, with the hashes of what it left behind)."""
+
+    def __init__(self, out, run_id, scope):
+        self.out = out
+        self.state = dict(protocol=p.PROTOCOL, run_id=run_id, status="preparing", completed=False, scope=scope,
+                          finished_jobs=0)
+        self.completed = []
+
+    def save_state(self, **changes):
+        self.state.update(changes)
+        p.write(self.out / "batch-state.json", self.state)
+
+    def start_ledger(self):
+        p.write(self.out / "completed-jobs.json", self.completed)
+
+    def finish_job(self, job, directory, world, plan_digest=None):
+        entry = dict(job=job, command_sha256=p.sha(directory / "command.json"),
+                     rank_sha256={name: p.sha(directory / name) for name in (f"rank{r}.json" for r in range(world))})
+        if plan_digest is not None:
+            entry["execution_plan_sha256"] = plan_digest
+            entry["selection_plan_file_sha256"] = p.sha(self.out / "selection-plan.json")
+        self.completed.append(entry)
+        p.write(self.out / "completed-jobs.json", self.completed)
+        self.save_state(finished_jobs=len(self.completed))
+
+
+class Invariants:
+    """Facts that must not change from one job of a batch to the next: the
+    rank environment, the native library the ranks loaded, the initial
+    weights/input of every training window, and -- within one five-arm block
+    -- the trajectories of the TACO arms that differ only in production
+    order."""
+
+    def __init__(self):
+        self.first = {}
+        self.windows = {}
+
+    def same_as_before(self, key, value, message):
+        expected = self.first.setdefault(key, value)
+        p.require(expected == value, message)
+
+    def rows(self, rows):
+        self.same_as_before("environment", [r["environment_identity"] for r in rows],
+                            "hardware/software changed between workers")
+        self.same_as_before("native", [r["codec_build"] for r in rows], "native library changed between workers")
+
+    def training(self, job, rows):
+        self.same_as_before("training", p.training_identity(rows), "initial weights/input differ across windows")
+        block = self.windows.setdefault((job["trial"], job["block"]), {})
+        block[job["arm"]] = rows
+        present = [arm for arm in p.FULL_TACO_ARMS if arm in block]
+        for arm in present[1:]:
+            p.compare_taco_trajectories(block[present[0]], block[arm])
+
+
+def freeze_sources(files, manifest, out):
+    """Copy the sources into ``out/sources`` (verifying every copy against
+    the manifest) and place this tree's native library beside them and under
+    ``out/build``.  Returns the snapshot root the workers run from."""
+    root = out / "sources"
+    for f in files:
+        rel = str(f.relative_to(REPO))
+        dest = root / rel
+        dest.parent.mkdir(parents=True, exist_ok=True)
+        shutil.copyfile(f, dest)
+        p.require(p.sha(dest) == manifest[rel], "source changed while freezing")
+    from ..ops import _build
+    library = _build.build()
+    native_dir = root / "tempname_dcu_b200" / "_native"
+    native_dir.mkdir(parents=True, exist_ok=True)
+    for src, name in ((library, "libtdb.so"), (_build.paths(_build.debug_requested())[1], "manifest.json")):
+        shutil.copyfile(src, native_dir / name)
+    (out / "build").mkdir()
+    shutil.copyfile(library, out / "build" / "libtdb.so")
+    return root
+
+
+_RECORDED_ENV_PREFIXES = ("NCCL_", "TORCH_NCCL_")
+_RECORDED_ENV_NAMES = ("CUDA_VISIBLE_DEVICES", "OMP_NUM_THREADS")
+
+
+def _recorded_environment():
+    return {k: v for k, v in os.environ.items() if k.startswith(_RECORDED_ENV_PREFIXES) or k in _RECORDED_ENV_NAMES}
 
 
 def execute(args):
+    """Run every job of the plan in order (see the module docstring) and
+    write the replayed report."""
     from . import report as reporting
     p.require(not args.out.exists(), "output directory exists; use a fresh --out")
     python = shutil.which(args.python)
@@ -190,91 +309,68 @@ def execute(args):
     manifest = {str(f.relative_to(REPO)): p.sha(f) for f in files}
     plan = plan_for(args, manifest=manifest, run_id=uuid.uuid4().hex)
     args.out.mkdir(parents=True, exist_ok=False)
-    state = dict(protocol=p.PROTOCOL, run_id=plan["config"]["run_id"], status="preparing", completed=False,
-                 scope=args.scope, finished_jobs=0)
-    p.write(args.out / "batch-state.json", state)
+    record = BatchRecord(args.out, plan["config"]["run_id"], args.scope)
+    record.save_state()
     try:
-        source_root = args.out / "sources"
-        for f in files:
-            dest = source_root / f.relative_to(REPO)
-            dest.parent.mkdir(parents=True, exist_ok=True)
-            shutil.copyfile(f, dest)
-            p.require(p.sha(dest) == manifest[str(f.relative_to(REPO))], "source changed while freezing")
-        # The frozen sources import their own native library: build it once into the snapshot.
-        from ..ops import _build
-        library = _build.build()
-        native_dir = source_root / "tempname_dcu_b200" / "_native"
-        native_dir.mkdir(parents=True, exist_ok=True)
-        shutil.copyfile(library, native_dir / "libtdb.so")
-        shutil.copyfile(_build.paths(_build.debug_requested())[1], native_dir / "manifest.json")
-        (args.out / "build").mkdir()
-        shutil.copyfile(library, args.out / "build" / "libtdb.so")
+        source_root = freeze_sources(files, manifest, args.out)
         p.write(args.out / "source-manifest.json", manifest)
         p.write(args.out / "plan.json", plan)
-        completed = []
-        p.write(args.out / "completed-jobs.json", completed)
-        identities = environment = native = execution_plan = None
-        groups = {}
+        record.start_ledger()
+        invariants = Invariants()
+        frozen_plan = None
+        total = len(plan["jobs"])
         for job in plan["jobs"]:
             directory = args.out / "results" / job["directory"]
             directory.mkdir(parents=True, exist_ok=False)
-            job_config = p.config_for_job(plan["config"], job, execution_plan)
+            job_config = p.config_for_job(plan["config"], job, frozen_plan)
             p.write(directory / "config.json", job_config)
             command = command_for(python, source_root, directory, job, args.world_size)
-            p.write(directory / "command.json", dict(job=job, command=command, environment={
-                k: v for k, v in os.environ.items()
-                if k.startswith(("NCCL_", "TORCH_NCCL_")) or k in ("CUDA_VISIBLE_DEVICES", "OMP_NUM_THREADS")}))
-            state.update(status="running", active_job=job)
-            p.write(args.out / "batch-state.json", state)
-            print(f"[{job['index'] + 1}/{len(plan['jobs'])}] {job['directory']}", flush=True)
+            p.write(directory / "command.json", dict(job=job, command=command, environment=_recorded_environment()))
+            record.save_state(status="running", active_job=job)
+            print(f"[{job['index'] + 1}/{total}] {job['directory']}", flush=True)
             launch(command, directory, source_root, args.worker_timeout)
-            rows = p.validate_rows([p.read(directory / f"rank{r}.json") for r in range(args.world_size)], job,
-                                   job_config)
-            env = [r["environment_identity"] for r in rows]
-            p.require(environment is None or env == environment, "hardware/software changed between workers")
-            environment = env
-            built = [r["codec_build"] for r in rows]
-            p.require(native is None or built == native, "native library changed between workers")
-            native = built
+            rows = [p.read(directory / f"rank{r}.json") for r in range(args.world_size)]
+            rows = p.validate_rows(rows, job, job_config)
+            invariants.rows(rows)
             reporting.validate_artifacts(args.out, directory, rows, job_config)
+            digest = None
             if job["stage"] == "calibrate":
-                p.require(execution_plan is None, "calibration runs once per fresh experiment")
-                execution_plan = p.calibration_from_rows(rows, job_config)
+                p.require(frozen_plan is None, "calibration runs once per fresh experiment")
+                frozen_plan = p.calibration_from_rows(rows, job_config)
                 reporting.validate_calibration_evidence(args.out, directory, rows, job_config)
-                p.write(args.out / "selection-plan.json", execution_plan)
-                state.update(execution_plan_sha256=p.digest(execution_plan))
+                p.write(args.out / "selection-plan.json", frozen_plan)
+                digest = p.digest(frozen_plan)
+                record.save_state(execution_plan_sha256=digest)
             elif job["stage"] == "train":
-                identity = p.training_identity(rows)
-                p.require(identities is None or identity == identities, "initial weights/input differ across windows")
-                identities = identity
-                group = groups.setdefault((job["trial"], job["block"]), {})
-                group[job["arm"]] = rows
-                taco = [a for a in p.FULL_TACO_ARMS if a in group]
-                for other in taco[1:]:
-                    p.compare_taco_trajectories(group[taco[0]], group[other])
-            done = dict(job=job, command_sha256=p.sha(directory / "command.json"),
-                        rank_sha256={f"rank{r}.json": p.sha(directory / f"rank{r}.json")
-                                     for r in range(args.world_size)})
-            if job["stage"] == "calibrate":
-                done.update(execution_plan_sha256=p.digest(execution_plan),
-                            selection_plan_file_sha256=p.sha(args.out / "selection-plan.json"))
-            completed.append(done)
-            p.write(args.out / "completed-jobs.json", completed)
-            state.update(finished_jobs=len(completed))
-            p.write(args.out / "batch-state.json", state)
+                invariants.training(job, rows)
+            record.finish_job(job, directory, args.world_size, digest)
         report = reporting.replay(args.out)
         p.write(args.out / "report.json", report)
         (args.out / "report.md").write_text(reporting.markdown(report))
-        state.update(status="completed" if args.scope == "train" else args.scope + "_completed", completed=True,
-                     active_job=None, report_sha256=p.sha(args.out / "report.json"),
-                     formal_optimizer_steps=report["formal_optimizer_steps"])
-        p.write(args.out / "batch-state.json", state)
+        record.save_state(status="completed" if args.scope == "train" else f"{args.scope}_completed", completed=True,
+                          active_job=None, report_sha256=p.sha(args.out / "report.json"),
+                          formal_optimizer_steps=report["formal_optimizer_steps"])
         print(f"completed scope: {args.scope}\nreport: {args.out / 'report.md'}", flush=True)
-    except BaseException as exc:
-        state.update(status="interrupted" if isinstance(exc, KeyboardInterrupt) else "failed", completed=False,
-                     error=f"{type(exc).__name__}: {exc}")
-        p.write(args.out / "batch-state.json", state)
+    except KeyboardInterrupt as exc:
+        record.save_state(status="interrupted", completed=False, error=f"KeyboardInterrupt: {exc}")
         raise
+    except Exception as exc:
+        record.save_state(status="failed", completed=False, error=f"{type(exc).__name__}: {exc}")
+        raise
+
+
+@contextlib.contextmanager
+def _sigterm_interrupts():
+    """While active, SIGTERM raises KeyboardInterrupt in the main thread, so
+    a scheduler's stop unwinds ``execute`` (which stops the running worker
+    group and marks the batch interrupted) instead of orphaning torchrun."""
+    def interrupt(_number, _frame):
+        raise KeyboardInterrupt("received SIGTERM")
+    previous = signal.signal(signal.SIGTERM, interrupt)
+    try:
+        yield
+    finally:
+        signal.signal(signal.SIGTERM, previous)
 
 
 def main(argv=None):
@@ -282,19 +378,15 @@ def main(argv=None):
     if args.report:
         from . import report as reporting
         print(reporting.markdown(reporting.replay(args.out)))
-    elif args.execute:
-        def terminate(_number, _frame):
-            raise KeyboardInterrupt("received SIGTERM")
-        previous = signal.signal(signal.SIGTERM, terminate)
-        try:
+        return
+    if args.execute:
+        with _sigterm_interrupts():
             execute(args)
-        finally:
-            signal.signal(signal.SIGTERM, previous)
-    else:
-        import json
-        print(json.dumps(dict(preview=True, writes_files=False, uses_gpu=False, output=str(args.out),
-                              operator_rooflines=operator_rooflines(args), **plan_for(args)),
-                         ensure_ascii=False, indent=2))
+        return
+    import json
+    preview = dict(preview=True, writes_files=False, uses_gpu=False, output=str(args.out),
+                   operator_rooflines=operator_rooflines(args), **plan_for(args))
+    print(json.dumps(preview, ensure_ascii=False, indent=2))
 
 
 def operator_rooflines(args):
@@ -315,12 +407,21 @@ def operator_rooflines(args):
     return out
 
 
-if __name__ == "__main__":
+# exit status of the command line per failure class (first match wins)
+_EXIT_CODES = ((KeyboardInterrupt, 130, "interrupted; only this controller's worker process group was stopped"),
+               ((ValueError, RuntimeError, OSError, subprocess.TimeoutExpired), 1, None))
+
+
+def _cli():
     try:
         main()
-    except KeyboardInterrupt:
-        print("interrupted; only this controller's worker process group was terminated", file=sys.stderr)
-        raise SystemExit(130)
-    except (ValueError, RuntimeError, OSError, subprocess.TimeoutExpired) as error:
-        print(f"ERROR: {error}", file=sys.stderr)
-        raise SystemExit(1)
+    except BaseException as error:  # noqa: BLE001 - mapped to an exit status below
+        for kinds, code, text in _EXIT_CODES:
+            if isinstance(error, kinds):
+                print(text or f"ERROR: {error}", file=sys.stderr)
+                raise SystemExit(code) from None
+        raise
+
+
+if __name__ == "__main__":
+    _cli()

@@ -17,7 +17,10 @@ from __future__ import annotations
 import hashlib
 import json
 import math
+import os
 from pathlib import Path
+import re
+import tempfile
 
 from ..mapping import ARMS, BACKEND
 from ..planning import SCHEMA as PLAN_SCHEMA
@@ -40,13 +43,130 @@ SMALL_MODEL = dict(layers=2, hidden=1024, ffn=4096, heads=8, sequence=2048, micr
 _OPTIONAL_MODEL_KEYS = {"pad_vocab"}
 
 
-def require(value, message):
-    if not value:
+# --------------------------------------------------------------- basic checks and files
+
+class _Missing:
+    def __repr__(self):
+        return "<missing>"
+
+
+MISSING = _Missing()
+_HASH = re.compile(r"[0-9a-f]{64}")
+
+
+def require(condition, message):
+    """The protocol's single failure path: a violated rule raises ValueError."""
+    if not condition:
         raise ValueError(message)
 
 
 def positive_int(value):
-    return type(value) is int and value > 0
+    return isinstance(value, int) and not isinstance(value, bool) and value > 0
+
+
+def finite_number(value, nonnegative=False):
+    if isinstance(value, bool) or not isinstance(value, (int, float)) or not math.isfinite(value):
+        return False
+    return value >= 0 or not nonnegative
+
+
+def valid_hash(value):
+    return isinstance(value, str) and _HASH.fullmatch(value) is not None
+
+
+def canonical(value):
+    """Canonical JSON bytes of a plan or manifest: sorted keys, no spaces, no NaN."""
+    return json.dumps(value, sort_keys=True, separators=(",", ":"), allow_nan=False).encode()
+
+
+def digest(value):
+    return hashlib.sha256(canonical(value)).hexdigest()
+
+
+def sha(path):
+    with open(path, "rb") as fh:
+        return hashlib.file_digest(fh, "sha256").hexdigest()
+
+
+def read(path):
+    with open(path, encoding="utf-8") as fh:
+        return json.load(fh)
+
+
+def write(path, value):
+    """Write JSON atomically: a temporary file in the same directory, then a rename."""
+    path = Path(path)
+    path.parent.mkdir(parents=True, exist_ok=True)
+    text = json.dumps(value, indent=2, ensure_ascii=False, allow_nan=False) + "\n"
+    fd, tmp = tempfile.mkstemp(dir=path.parent, prefix=path.name + ".", suffix=".tmp")
+    try:
+        with os.fdopen(fd, "w", encoding="utf-8") as fh:
+            fh.write(text)
+        os.replace(tmp, path)
+    except BaseException:
+        Path(tmp).unlink(missing_ok=True)
+        raise
+
+
+# --------------------------------------------------------------- declarative field checks
+#
+# A rule is (dotted path, predicate, reason).  check_fields looks every path
+# up in a rank row / record / state and raises with the reason and the value
+# found when the predicate does not hold.
+
+def lookup(obj, path):
+    for key in path.split("."):
+        if not isinstance(obj, dict) or key not in obj:
+            return MISSING
+        obj = obj[key]
+    return obj
+
+
+def check_fields(obj, rules, what):
+    for path, ok, reason in rules:
+        value = lookup(obj, path)
+        require(value is not MISSING and ok(value), f"{what}: {reason} ({path} = {value!r:.80})")
+
+
+def equals(expected):
+    return lambda v: v == expected
+
+
+def is_true(v):
+    return v is True
+
+
+def is_false(v):
+    return v is False
+
+
+def positive_finite(v):
+    return finite_number(v) and v > 0
+
+
+def at_most(limit):
+    return lambda v: finite_number(v, True) and v <= limit
+
+
+def nonnegative_int(v):
+    return isinstance(v, int) and not isinstance(v, bool) and v >= 0
+
+
+def series(length):
+    """A list of ``length`` finite non-negative numbers (losses, norms)."""
+    return lambda v: isinstance(v, list) and len(v) == length and all(finite_number(x, True) for x in v)
+
+
+def validate_calibration_options(options):
+    require(isinstance(options, dict) and set(options) == set(CALIBRATION), "wrong calibration option keys")
+    check_fields(options, [
+        ("iterations", positive_int, "positive integer required"),
+        ("training_pairs", positive_int, "positive integer required"),
+        ("confirmation_pairs", positive_int, "positive integer required"),
+        ("warmup", nonnegative_int, "non-negative integer required"),
+        ("quant_budget", lambda v: finite_number(v) and 0 <= v <= 1, "must lie in [0, 1]"),
+        ("min_gain", lambda v: finite_number(v) and 0 <= v < 1, "must lie in [0, 1)"),
+    ], "calibration options")
 
 
 def validate_model(model, world):
@@ -125,289 +245,336 @@ def balanced(blocks, arms=ARMS):
     return blocks >= cycle and blocks % cycle == 0
 
 
-def sha(path):
-    return hashlib.sha256(Path(path).read_bytes()).hexdigest()
-
-
-def digest(value):
-    return hashlib.sha256(json.dumps(value, sort_keys=True, separators=(",", ":"), allow_nan=False).encode()).hexdigest()
-
-
-def read(path):
-    return json.loads(Path(path).read_text())
-
-
-def write(path, value):
-    """Atomic JSON write (temp file + replace)."""
-    path = Path(path)
-    path.parent.mkdir(parents=True, exist_ok=True)
-    tmp = path.with_name(path.name + ".tmp")
-    tmp.write_text(json.dumps(value, indent=2, ensure_ascii=False, allow_nan=False) + "\n")
-    tmp.replace(path)
-
-
-def finite_number(value, nonnegative=False):
-    return type(value) in (int, float) and math.isfinite(value) and (not nonnegative or value >= 0)
-
-
-def valid_hash(value):
-    return isinstance(value, str) and len(value) == 64 and all(c in "0123456789abcdef" for c in value)
-
-
-def validate_calibration_options(options):
-    require(set(options) == set(CALIBRATION), "wrong calibration option keys")
-    for key in ("iterations", "training_pairs", "confirmation_pairs"):
-        require(positive_int(options[key]), f"positive calibration {key} required")
-    require(type(options["warmup"]) is int and options["warmup"] >= 0, "invalid calibration warmup")
-    require(finite_number(options["quant_budget"]) and 0 <= options["quant_budget"] <= 1, "quant_budget in [0,1]")
-    require(finite_number(options["min_gain"]) and 0 <= options["min_gain"] < 1, "min_gain in [0,1)")
-
+# --------------------------------------------------------------- frozen plans and job configs
 
 def role_shape(model, world, role):
-    return [model["sequence"] * model["micro_batch"], model["hidden"],
-            model["hidden" if role == "attn" else "ffn"] // world]
+    """[M, N, K] of a role's projection: M = rows of a micro-batch, N = hidden,
+    K = the input width on one rank (attention-out h/W, FC2 f/W)."""
+    k = model["hidden"] if role == "attn" else model["ffn"]
+    return [model["sequence"] * model["micro_batch"], model["hidden"], k // world]
+
+
+def physical_blocks(model):
+    return model["sequence"] * model["micro_batch"] // model["chunk_rows"]
 
 
 def validate_execution_plan(bundle, config):
     model, world = config["model"], config["world_size"]
-    require(isinstance(bundle, dict) and bundle.get("schema") == PLAN_SCHEMA and bundle.get("world_size") == world
-            and bundle.get("transport_lanes") == 2, "wrong calibrated execution-plan identity")
-    require(set(bundle.get("roles", {})) == {"attn", "mlp"}, "missing calibrated role")
-    count = model["sequence"] * model["micro_batch"] // model["chunk_rows"]
+    require(isinstance(bundle, dict), "calibrated execution plan missing")
+    check_fields(bundle, [("schema", equals(PLAN_SCHEMA), "unknown plan schema"),
+                          ("world_size", equals(world), "plan for another world size"),
+                          ("transport_lanes", equals(2), "two transport lanes required")], "execution plan")
+    require(isinstance(bundle.get("roles"), dict) and set(bundle["roles"]) == {"attn", "mlp"},
+            "the plan needs exactly the attn and mlp roles")
+    count = physical_blocks(model)
+    per = count // world
+    budget = math.floor(count * config["calibration"]["quant_budget"] + 1e-12)
+
+    def bijection(order):
+        return isinstance(order, list) and all(type(i) is int for i in order) and sorted(order) == list(range(count))
+
+    def keeps_slots(order):  # slot s still feeds destination s % W (the interleaved slot structure)
+        return all(physical // per == slot % world for slot, physical in enumerate(order))
+
+    def block_mask(mask):
+        return isinstance(mask, list) and len(mask) == count and all(type(x) is bool for x in mask)
+
     for role, plan in bundle["roles"].items():
-        require(plan.get("shape") == role_shape(model, world, role) and plan.get("chunk_rows") == model["chunk_rows"],
-                "calibrated plan shape/chunk mismatch")
-        order, mask = plan.get("arrival_order"), plan.get("selective_mask")
-        require(isinstance(order, list) and len(order) == count and all(type(i) is int for i in order)
-                and sorted(order) == list(range(count)), "arrival order must be a physical-block bijection")
-        require(all(p // (count // world) == slot % world for slot, p in enumerate(order)),
-                "arrival plan must keep interleaved destination slots")
-        require(isinstance(mask, list) and len(mask) == count and all(type(x) is bool for x in mask),
-                "selection mask needs one bool per physical block")
-        require(sum(mask) <= math.floor(count * config["calibration"]["quant_budget"] + 1e-12),
-                "selection exceeds the frozen block budget")
-        require(isinstance(plan.get("diagnostics"), dict), "missing calibration diagnostics")
-    digest(bundle)
+        check_fields(plan, [
+            ("shape", equals(role_shape(model, world, role)), "calibrated for another shape"),
+            ("chunk_rows", equals(model["chunk_rows"]), "calibrated for another chunk size"),
+            ("arrival_order", bijection, "arrival order must permute the physical blocks"),
+            ("arrival_order", keeps_slots, "arrival order must keep the interleaved destination slots"),
+            ("selective_mask", block_mask, "selection mask needs one bool per physical block"),
+            ("selective_mask", lambda m: sum(m) <= budget, "selection exceeds the frozen block budget"),
+            ("diagnostics", lambda d: isinstance(d, dict), "calibration diagnostics missing"),
+        ], f"{role} plan")
+    digest(bundle)  # must be canonical JSON (finite numbers only)
     return bundle
 
 
 def config_for_job(base, job, execution_plan=None):
+    """The job's config: the immutable base config plus the job, and -- for
+    operator / training windows of an experiment that calibrates -- the
+    frozen plan with its digest."""
     require(base.get("execution_plan") is None and base.get("execution_plan_sha256") is None,
             "the base plan must stay uncalibrated and immutable")
-    out = dict(base, job=job)
-    if job["stage"] in ("operator", "train") and (execution_plan is not None
-                                                   or needs_calibration(base.get("arms", ARMS))):
-        validate_execution_plan(execution_plan, base)
-        out.update(execution_plan=execution_plan, execution_plan_sha256=digest(execution_plan))
-    return out
+    config = {**base, "job": job}
+    windowed = job["stage"] in ("operator", "train")
+    if windowed and (execution_plan is not None or needs_calibration(base.get("arms", ARMS))):
+        config["execution_plan"] = validate_execution_plan(execution_plan, base)
+        config["execution_plan_sha256"] = digest(execution_plan)
+    return config
 
 
 def calibration_from_rows(rows, config):
-    plans = [row.get("calibration_plan") for row in rows]
-    require(plans and all(p == plans[0] for p in plans), "ranks disagree on the calibrated execution plan")
-    return validate_execution_plan(plans[0], config)
+    """The plan every rank froze; ranks must agree byte for byte."""
+    require(rows, "no calibration rows")
+    found = {canonical(row.get("calibration_plan")) for row in rows}
+    require(len(found) == 1, "ranks disagree on the calibrated execution plan")
+    return validate_execution_plan(rows[0].get("calibration_plan"), config)
+
+
+# --------------------------------------------------------------- the operator contract
+
+def _production_pairs(arm, world, per, role_plan):
+    """(destination, block within destination) in production order."""
+    if arm in (ARRIVAL, SELECTIVE):
+        return [divmod(physical, per) for physical in role_plan["arrival_order"]]
+    if arm == "flux_taco_interleaved":
+        return [(d, w) for w in range(per) for d in range(world)]
+    return [(d, w) for d in range(world) for w in range(per)]
 
 
 def expected_schedule(model, world, arm, role_plan=None):
-    per = model["sequence"] * model["micro_batch"] // world // model["chunk_rows"]
-    out = []
-    for slot in range(world * per):
-        if arm in (ARRIVAL, SELECTIVE):
-            physical = role_plan["arrival_order"][slot]
-            destination, within = divmod(physical, per)
-        else:
-            destination, within = ((slot % world, slot // world) if arm == "flux_taco_interleaved"
-                                   else divmod(slot, per))
-            physical = destination * per + within
-        out.append(dict(slot=slot, destination=destination, within=within, physical=physical,
-                        row=physical * model["chunk_rows"], rows=model["chunk_rows"], lane=within % 2))
-    return out
+    """The arm's production schedule as the operator must report it."""
+    per = physical_blocks(model) // world
+    rows = model["chunk_rows"]
+    return [dict(slot=slot, destination=d, within=w, physical=d * per + w, row=(d * per + w) * rows, rows=rows,
+                 lane=w % 2)
+            for slot, (d, w) in enumerate(_production_pairs(arm, world, per, role_plan))]
+
+
+def expected_operator_state(model, world, arm, rank, role, calls, stage, execution_plan=None,
+                            selective_mode="wire"):
+    """Every exactly-known field of a correct operator's ``state()`` for this
+    job: identity, shape, schedule and its hash, the one fused kernel, codec
+    and reduction contract, per-source wire bytes from the frozen selection,
+    plan hash, lanes / consumer policy, validation calls, no diagnostic delay."""
+    arrival = arm in (ARRIVAL, SELECTIVE)
+    role_plan = execution_plan["roles"][role] if arrival else None
+    schedule = expected_schedule(model, world, arm, role_plan)
+    count = len(schedule)
+    per = count // world
+    mask = list(role_plan["selective_mask"]) if arm == SELECTIVE else [arm != "flux"] * count
+    # remote blocks each source quantizes: masked blocks owned by another rank
+    selected = [sum(1 for phys, q in enumerate(mask) if q and phys // per != src) for src in range(world)]
+    elements = model["chunk_rows"] * model["hidden"]
+    packet, plain = elements // 128 * 136, elements * 2
+    remote = (world - 1) * per
+    fp8 = selective_mode == "fp8-mma" and arm == SELECTIVE
+    wires = [remote * plain] * world if fp8 else [q * packet + (remote - q) * plain for q in selected]
+    if fp8:
+        quantization = "selective_mma_e4m3_ue8m0_k32"
+    elif arm == SELECTIVE:
+        quantization = "selective_remote_h128_e4m3"
+    else:
+        quantization = "none" if arm == "flux" else "all_remote_h128_e4m3"
+    state = dict(
+        backend=BACKEND, arm=arm, rank=rank, shape=role_shape(model, world, role), chunk_rows=model["chunk_rows"],
+        calls=calls, production_schedule=schedule,
+        mapping_sha256=hashlib.sha256(json.dumps(schedule, sort_keys=True).encode()).hexdigest(),
+        gemms_per_call=1, collectives_per_call=1,
+        fused_kernel="tdb::rs::gemm_rs_mx_kernel" if fp8 else "tdb::rs::gemm_rs_kernel",
+        quantization=quantization, reduction_order=list(range(world)), rounding="bf16_after_each_source",
+        selection_mask=mask, selected_remote_blocks_by_source=selected, remote_wire_bytes_by_source=wires,
+        remote_wire_bytes_per_source=wires[rank], actual_remote_wire_bytes_per_rank=wires[rank],
+        plan_sha256=digest(role_plan) if role_plan is not None else None, original_cuda_flux=False,
+        transport_lanes=2, consumer_policy="per_lane_ready" if arrival else "ordered",
+        validation_calls=2 if stage == "operator" else 1, diagnostic_delay_cycles=0,
+        diagnostic_delay_in_normal_forward=False)
+    if fp8:
+        state.update(selective_mode="fp8-mma", mma_block_mask=mask)
+    return state
 
 
 def validate_operator_state(state, row, model, world, role, calls, execution_plan=None, selective_mode="wire"):
-    """The operator's own account of a call sequence against the frozen arm
-    contract.  With selective_mode "fp8-mma" the selective arm computes its
-    calibrated blocks as block-scaled FP8 MMAs and sends every block as BF16."""
-    shape = role_shape(model, world, role)
-    fp8 = selective_mode == "fp8-mma" and row["arm"] == SELECTIVE
-    role_plan = execution_plan["roles"][role] if row["arm"] in (ARRIVAL, SELECTIVE) else None
-    sched = expected_schedule(model, world, row["arm"], role_plan)
-    mapping_sha = hashlib.sha256(json.dumps(sched, sort_keys=True).encode()).hexdigest()
-    mask = role_plan["selective_mask"] if row["arm"] == SELECTIVE else [row["arm"] != "flux"] * len(sched)
-    per = len(sched) // world
-    selected = [sum(flag and p // per != s for p, flag in enumerate(mask)) for s in range(world)]
-    remote = (world - 1) * per
-    elements = model["chunk_rows"] * model["hidden"]
-    wires = [q * (elements // 128 * 136) + (remote - q) * elements * 2 for q in selected]
-    if fp8:
-        wires = [remote * elements * 2] * world
-    require(state.get("backend") == BACKEND and state.get("arm") == row["arm"] and state.get("rank") == row["rank"],
-            "wrong operator backend/arm/rank")
-    require(state.get("shape") == shape and state.get("chunk_rows") == model["chunk_rows"],
-            "wrong projection shape/chunk size")
-    require(state.get("calls") == calls, f"wrong actual {role} projection call count")
-    require(state.get("production_schedule") == sched and state.get("mapping_sha256") == mapping_sha,
-            "actual production mapping is not the frozen arm schedule")
-    kernel = "tdb::rs::gemm_rs_mx_kernel" if fp8 else "tdb::rs::gemm_rs_kernel"
-    require(state.get("gemms_per_call") == 1 and state.get("collectives_per_call") == 1
-            and state.get("fused_kernel") == kernel, "the operator must be one fused kernel")
-    quant = ("selective_mma_e4m3_ue8m0_k32" if fp8 else "selective_remote_h128_e4m3" if row["arm"] == SELECTIVE else
-             "none" if row["arm"] == "flux" else "all_remote_h128_e4m3")
-    require(not fp8 or (state.get("selective_mode") == "fp8-mma" and state.get("mma_block_mask") == mask),
-            "the FP8 MMA block mask is not the calibrated selective mask")
-    require(state.get("quantization") == quant and state.get("reduction_order") == list(range(world))
-            and state.get("rounding") == "bf16_after_each_source", "codec/reduction contract changed")
-    require(state.get("remote_wire_bytes_per_source") == wires[row["rank"]]
-            and state.get("actual_remote_wire_bytes_per_rank") == wires[row["rank"]]
-            and state.get("remote_wire_bytes_by_source") == wires
-            and state.get("selected_remote_blocks_by_source") == selected and state.get("selection_mask") == mask,
-            "remote wire-byte accounting mismatch")
-    require(state.get("plan_sha256") == (digest(role_plan) if role_plan is not None else None),
-            "actual role-plan hash changed")
-    require(state.get("original_cuda_flux") is False, "the B200 operator is not upstream CUDA Flux")
-    require(type(state.get("scratch_bytes")) is int and state["scratch_bytes"] >= 0, "invalid scratch accounting")
-    require(state.get("transport_lanes") == 2 and state.get("consumer_policy") ==
-            ("per_lane_ready" if row["arm"] in (ARRIVAL, SELECTIVE) else "ordered")
-            and state.get("validation_calls") == (2 if row["stage"] == "operator" else 1),
-            "missing untimed per-instance validation or unexpected consumer policy")
-    require(state.get("diagnostic_delay_cycles") == 0 and state.get("diagnostic_delay_in_normal_forward") is False,
-            "the artificial lane delay must not enter measured operators")
+    """Compare the operator's own account field by field with the contract
+    (expected_operator_state) of this job."""
+    require(isinstance(state, dict), "operator state missing")
+    expected = expected_operator_state(model, world, row["arm"], row["rank"], role, calls, row["stage"],
+                                       execution_plan, selective_mode)
+    for key, want in expected.items():
+        got = state.get(key, MISSING)
+        require(got == want, f"{role} operator state: {key} is {got!r:.80}, the frozen contract says {want!r:.80}")
+    require(nonnegative_int(state.get("scratch_bytes")), "invalid scratch accounting")
+
+
+# --------------------------------------------------------------- the artificial lane-skew diagnostic
+
+LANE_SKEW = dict(delayed_rank=0, delayed_lane=0, delay_cycles=50_000_000)
+
+
+def _first_lane0_block(config):
+    """Physical block of the first lane-0 slot of the common interleave (the
+    block whose signal the diagnostic holds back)."""
+    schedule = expected_schedule(config["model"], config["world_size"], "flux_taco_interleaved")
+    return next(item["physical"] for item in schedule if item["lane"] == 0)
+
+
+def _consumer_event(e):
+    return (isinstance(e, dict) and e.get("stage") == "consumer" and type(e.get("physical")) is int
+            and e.get("lane") in (0, 1) and finite_number(e.get("start_ms")) and finite_number(e.get("end_ms"))
+            and e["end_ms"] >= e["start_ms"] - 1e-9)
 
 
 def validate_arrival_diagnostic(record, row, config):
+    """Arrival arms carry a passed artificial lane-skew check whose bypass
+    claim is recomputed here from its own consumer events; control arms
+    carry none."""
     diag = record.get("arrival_diagnostic")
     if row["arm"] not in (ARRIVAL, SELECTIVE):
         require(diag is None, "unexpected arrival diagnostic on a control arm")
         return
-    require(isinstance(diag, dict) and diag.get("passed") is True and diag.get("numerical_bitwise_equal") is True
-            and diag.get("artificial") is True and diag.get("ordinary_speedup_claim") is False,
-            "missing successful artificial lane-skew check")
-    require(diag.get("delayed_rank") == 0 and diag.get("delayed_lane") == 0 and diag.get("delay_cycles") == 50_000_000,
-            "artificial lane-skew protocol changed")
-    base = expected_schedule(config["model"], config["world_size"], "flux_taco_interleaved")
-    pending = next(item["physical"] for item in base if item["lane"] == 0)
-    require(diag.get("delayed_physical") == pending, "wrong delayed physical block")
-    events = diag.get("evidence", {}).get("events")
-    require(isinstance(events, list), "missing lane-skew event evidence")
-    for event in events:
-        require(event.get("stage") == "consumer" and type(event.get("physical")) is int
-                and event.get("lane") in (0, 1) and finite_number(event.get("start_ms"))
-                and finite_number(event.get("end_ms")) and event["end_ms"] >= event["start_ms"] - 1e-9,
-                "invalid lane-skew event interval")
-    rows = [e for e in events if e["physical"] == pending]
-    overtakes = []
-    if rows:
-        overtakes = [e["physical"] for e in events if e["lane"] != 0 and e["end_ms"] < rows[0]["end_ms"]]
-    require(diag.get("later_blocks_completed_before_pending") == overtakes
-            and diag.get("ready_bypass_observed") is bool(overtakes),
+    require(isinstance(diag, dict), "missing artificial lane-skew check")
+    pending = _first_lane0_block(config)
+    rules = [("passed", is_true, "the check did not pass"),
+             ("numerical_bitwise_equal", is_true, "delayed and normal outputs differ"),
+             ("artificial", is_true, "must be labelled artificial"),
+             ("ordinary_speedup_claim", is_false, "claims an ordinary speed-up"),
+             ("delayed_physical", equals(pending), "wrong delayed physical block"),
+             ("evidence.events", lambda v: isinstance(v, list) and all(_consumer_event(e) for e in v),
+              "invalid consumer event intervals")]
+    rules += [(key, equals(value), "artificial lane-skew protocol changed") for key, value in LANE_SKEW.items()]
+    check_fields(diag, rules, "arrival diagnostic")
+    events = diag["evidence"]["events"]
+    held = [e for e in events if e["physical"] == pending]
+    bypass = [e["physical"] for e in events if held and e["lane"] != 0 and e["end_ms"] < held[0]["end_ms"]]
+    require(diag.get("later_blocks_completed_before_pending") == bypass
+            and diag.get("ready_bypass_observed") is bool(bypass),
             "artificial bypass claim disagrees with receiver-local evidence")
 
+
+# --------------------------------------------------------------- rank rows
 
 def expected_parameter_counts(model, world):
     from ..models.config import parameter_counts
     return parameter_counts(model, world)
 
 
-def validate_rows(rows, job, config):
+def _identity_rules(job, config):
     world = config["world_size"]
-    require(len(rows) == world and {r.get("rank") for r in rows} == set(range(world)),
-            "missing, duplicate or unexpected rank")
+    return [
+        ("world_size", equals(world), "worker world size does not match the job"),
+        ("stage", equals(job["stage"]), "worker stage does not match the job"),
+        ("arm", equals(job["arm"]), "worker arm does not match the job"),
+        ("completed", is_true, "the rank did not complete"),
+        ("passed", is_true, "the rank's correctness checks failed"),
+        ("run_id", equals(config["run_id"]), "worker run_id mismatch"),
+        ("environment_identity", lambda v: isinstance(v, dict) and bool(v), "missing hardware/software identity"),
+        ("backend", equals(BACKEND), "wrong worker backend"),
+        ("original_cuda_flux", is_false, "the B200 operator is not upstream CUDA Flux"),
+        ("codec_build.library_sha256", valid_hash, "missing native library hash"),
+        ("codec_build.identity.source_sha256", valid_hash, "missing native source hash"),
+        ("execution_plan_sha256", equals(config.get("execution_plan_sha256")), "worker plan hash changed"),
+    ]
+
+
+def _train_rules(config, world):
+    model, timing = config["model"], config["timing"]
+    steps = timing["timed_steps"]
+    counts = expected_parameter_counts(model, world)
+    layers2 = 2 * model["layers"]
+    rules = [
+        ("timed_steps", equals(steps), "wrong timed step count"),
+        ("warmup_steps", equals(timing["warmup_steps"]), "wrong warm-up step count"),
+        ("elapsed_seconds", positive_finite, "invalid training elapsed time"),
+        ("losses", series(steps), "incomplete or non-finite losses"),
+        ("grad_norms", series(steps), "incomplete or non-finite gradient norms"),
+        ("initialization_sha256", valid_hash, "missing initial-weight hash"),
+        ("input_sha256", valid_hash, "missing input hash"),
+        ("final_parameters_sha256", valid_hash, "missing final-parameter hash"),
+        ("actual_model_config", lambda v: isinstance(v, dict) and all(v.get(k) == x for k, x in model.items()),
+         "the trained model differs from the frozen config"),
+        ("parameter_counts", equals(counts), "wrong trainable parameter count"),
+        ("actual_parameters_per_rank", equals(counts["parameters_per_rank"]), "wrong parameters per rank"),
+        ("tokens_per_step", equals(model["sequence"] * model["micro_batch"] * model["accumulation_steps"]),
+         "token budget changed"),
+        ("dtype", equals("bfloat16"), "compute dtype changed"),
+        ("optimizer", equals("AdamW-fp32-master"), "optimizer changed"),
+        ("operator_counters.model_forwards", equals(steps * model["accumulation_steps"]), "wrong forward count"),
+        ("operator_counters.target_modules", equals(layers2), "wrong projection module count"),
+        ("memory.peak_allocated_bytes", nonnegative_int, "missing allocator peak"),
+        ("memory.peak_reserved_bytes", nonnegative_int, "missing allocator peak"),
+    ]
+    if world > 1:
+        total = (steps + timing["warmup_steps"]) * model["accumulation_steps"]
+        rules += [("operator_counters.actual_calls_per_instance", equals([total] * layers2),
+                   "a projection bypassed the fused operator"),
+                  ("operator_states", lambda v: isinstance(v, list) and len(v) == layers2, "missing operator state")]
+    return rules
+
+
+def _check_train_row(row, config, world):
+    check_fields(row, _train_rules(config, world), f"rank {row['rank']} training window")
+    if world > 1:
+        model, timing = config["model"], config["timing"]
+        total = (timing["timed_steps"] + timing["warmup_steps"]) * model["accumulation_steps"]
+        for index, state in enumerate(row["operator_states"]):
+            validate_operator_state(state, row, model, world, ("attn", "mlp")[index % 2], total,
+                                    config["execution_plan"], config.get("selective_mode", "wire"))
+
+
+def _check_operator_row(row, config, world):
+    records = row.get("operator_results")
+    require(isinstance(records, list) and len(records) == 2 and {r.get("role") for r in records} == {"attn", "mlp"},
+            "need both output-projection roles")
+    timing = config["timing"]
+    calls = 2 + int(bool(config["profile"])) + timing["operator_warmup"] + timing["operator_iterations"]
+    plain_limit = 0.01 if row["arm"] == "flux" else 0.05
+    rules = [
+        ("correctness_passed", is_true, "independent operator correctness check failed"),
+        ("timed_iterations", equals(timing["operator_iterations"]), "wrong operator timing denominator"),
+        ("elapsed_seconds", positive_finite, "invalid operator elapsed time"),
+        ("bf16_relative_l2", at_most(plain_limit), "gate vs plain BF16 failed"),
+        ("codec_reference_relative_l2", at_most(0.01), "gate vs the codec reference failed"),
+        ("changed_input_relative_l2", at_most(0.01), "changed-input reuse gate failed"),
+        ("full_gemm_only_seconds", positive_finite, "missing full-GEMM control timing"),
+    ]
+    if row["arm"] != "flux":
+        rules.append(("order_bitwise_equal", is_true, "order-only numerical equivalence not verified"))
+    for record in records:
+        check_fields(record, rules, f"rank {row['rank']} {record['role']} operator window")
+        validate_arrival_diagnostic(record, row, config)
+        validate_operator_state(record.get("execution"), row, config["model"], world, record["role"], calls,
+                                config["execution_plan"], config.get("selective_mode", "wire"))
+        require(bool(record.get("profile")) == bool(config["profile"]), "requested profile missing/unexpected")
+    check_fields(row, [("initialization_sha256", valid_hash, "missing operator weight hash"),
+                       ("input_sha256", valid_hash, "missing operator input hash")], f"rank {row['rank']}")
+
+
+def _check_calibrate_row(row, config, world):
+    validate_execution_plan(row.get("calibration_plan"), config)
+    require(isinstance(row.get("calibration_results"), dict) and row["calibration_results"],
+            "missing rank-local calibration evidence")
+
+
+_STAGE_CHECKS = {"train": _check_train_row, "operator": _check_operator_row, "calibrate": _check_calibrate_row}
+
+
+def validate_rows(rows, job, config):
+    """All rank rows of one job against the job's frozen config; returns
+    them sorted by rank."""
+    world = config["world_size"]
+    ranks = [r.get("rank") for r in rows]
+    require(len(ranks) == world and set(ranks) == set(range(world)), "missing, duplicate or unexpected rank")
+    identity = _identity_rules(job, config)
+    stage_check = _STAGE_CHECKS.get(job["stage"])
     for row in rows:
-        require(row.get("world_size") == world and row.get("stage") == job["stage"] and row.get("arm") == job["arm"],
-                "worker identity does not match the job")
-        require(row.get("completed") is True and row.get("passed") is True,
-                f"rank {row.get('rank')} did not complete its correctness checks")
-        require(row.get("run_id") == config["run_id"], "worker run_id mismatch")
-        require(isinstance(row.get("environment_identity"), dict) and row["environment_identity"],
-                "missing hardware/software identity")
-        require(row.get("backend") == BACKEND and row.get("original_cuda_flux") is False,
-                "wrong worker implementation identity")
-        build = row.get("codec_build", {})
-        require(valid_hash(build.get("library_sha256")) and valid_hash(build.get("identity", {}).get("source_sha256")),
-                "missing native library provenance")
-        require(row.get("execution_plan_sha256") == config.get("execution_plan_sha256"), "worker plan hash changed")
-        if job["stage"] == "train":
-            model, steps = config["model"], config["timing"]["timed_steps"]
-            require(row.get("timed_steps") == steps and row.get("warmup_steps") == config["timing"]["warmup_steps"],
-                    "wrong training step counts")
-            require(finite_number(row.get("elapsed_seconds")) and row["elapsed_seconds"] > 0,
-                    "invalid training elapsed time")
-            for key in ("losses", "grad_norms"):
-                values = row.get(key)
-                require(isinstance(values, list) and len(values) == steps and all(finite_number(v, True) for v in values),
-                        f"incomplete or non-finite {key}")
-            for key in ("initialization_sha256", "input_sha256", "final_parameters_sha256"):
-                require(valid_hash(row.get(key)), f"missing/invalid {key}")
-            actual = row.get("actual_model_config", {})
-            require(all(actual.get(k) == v for k, v in model.items()), "actual training model changed")
-            counts = expected_parameter_counts(model, world)
-            require(row.get("parameter_counts") == counts and
-                    row.get("actual_parameters_per_rank") == counts["parameters_per_rank"],
-                    "wrong trainable parameter count")
-            tokens = model["sequence"] * model["micro_batch"] * model["accumulation_steps"]
-            require(row.get("tokens_per_step") == tokens and row.get("dtype") == "bfloat16"
-                    and row.get("optimizer") == "AdamW-fp32-master", "training dtype/optimizer/token budget changed")
-            forwards = steps * model["accumulation_steps"]
-            counters = row.get("operator_counters", {})
-            require(counters.get("model_forwards") == forwards and counters.get("target_modules") == 2 * model["layers"],
-                    "wrong formal model/module coverage")
-            if world > 1:
-                total = (steps + config["timing"]["warmup_steps"]) * model["accumulation_steps"]
-                require(counters.get("actual_calls_per_instance") == [total] * (2 * model["layers"]),
-                        "a projection bypassed the fused operator")
-                states = row.get("operator_states", [])
-                require(len(states) == 2 * model["layers"], "missing operator state")
-                for index, state in enumerate(states):
-                    validate_operator_state(state, row, model, world, "attn" if index % 2 == 0 else "mlp", total,
-                                            config["execution_plan"], config.get("selective_mode", "wire"))
-            memory = row.get("memory", {})
-            require(all(type(memory.get(k)) is int and memory[k] >= 0 for k in
-                        ("peak_allocated_bytes", "peak_reserved_bytes")), "missing allocator peak memory")
-        elif job["stage"] == "operator":
-            records = row.get("operator_results", [])
-            require(len(records) == 2 and {r.get("role") for r in records} == {"attn", "mlp"},
-                    "need both output-projection roles")
-            for record in records:
-                require(record.get("correctness_passed") is True, "independent operator correctness check failed")
-                require(record.get("timed_iterations") == config["timing"]["operator_iterations"],
-                        "wrong operator timing denominator")
-                require(finite_number(record.get("elapsed_seconds")) and record["elapsed_seconds"] > 0,
-                        "invalid operator elapsed time")
-                for key, limit in (("bf16_relative_l2", 0.01 if row["arm"] == "flux" else 0.05),
-                                   ("codec_reference_relative_l2", 0.01), ("changed_input_relative_l2", 0.01)):
-                    require(finite_number(record.get(key), True) and record[key] <= limit,
-                            f"operator numerical gate failed: {key}")
-                require(row["arm"] == "flux" or record.get("order_bitwise_equal") is True,
-                        "order-only numerical equivalence not verified")
-                validate_arrival_diagnostic(record, row, config)
-                require(finite_number(record.get("full_gemm_only_seconds")) and record["full_gemm_only_seconds"] > 0,
-                        "missing full-GEMM control timing")
-                validate_operator_state(record.get("execution", {}), row, config["model"], world, record["role"],
-                                        2 + int(bool(config["profile"])) + config["timing"]["operator_warmup"]
-                                        + config["timing"]["operator_iterations"], config["execution_plan"],
-                                        config.get("selective_mode", "wire"))
-                profile = record.get("profile")
-                require(bool(profile) == bool(config["profile"]), "requested profile missing/unexpected")
-            for key in ("initialization_sha256", "input_sha256"):
-                require(valid_hash(row.get(key)), f"missing operator {key}")
-        elif job["stage"] == "calibrate":
-            validate_execution_plan(row.get("calibration_plan"), config)
-            require(isinstance(row.get("calibration_results"), dict) and row["calibration_results"],
-                    "missing rank-local calibration evidence")
+        check_fields(row, identity, f"rank {row['rank']}")
+        if stage_check is not None:
+            stage_check(row, config, world)
     if job["stage"] == "calibrate":
         calibration_from_rows(rows, config)
     return sorted(rows, key=lambda r: r["rank"])
 
 
+# --------------------------------------------------------------- training trajectories
+
+IDENTITY_KEYS = ("initialization_sha256", "input_sha256")
+
+
 def training_identity(rows):
-    return [[r["initialization_sha256"], r["input_sha256"]] for r in rows]
+    """Per rank, the hashes of the initial weights and the input batch."""
+    return [[row[key] for key in IDENTITY_KEYS] for row in rows]
 
 
 def compare_taco_trajectories(left, right):
-    """Arms that only reorder production must train bitwise identically."""
+    """Arms that only reorder production must train bitwise identically:
+    same start, same loss and gradient-norm series, same final parameters."""
     require(training_identity(left) == training_identity(right), "TACO arms have different initialisation/input")
     for a, b in zip(left, right):
-        for key in ("losses", "grad_norms"):
-            require(a[key] == b[key], f"TACO ordering changed {key}; investigate before timing claims")
-        require(a.get("final_parameters_sha256") == b.get("final_parameters_sha256")
-                and a.get("final_parameters_sha256"), "TACO final parameters differ")
+        differs = [key for key in ("losses", "grad_norms") if a[key] != b[key]]
+        require(not differs, f"TACO ordering changed {', '.join(differs)}; investigate before timing claims")
+        final = a.get("final_parameters_sha256")
+        require(final and final == b.get("final_parameters_sha256"), "TACO final parameters differ")

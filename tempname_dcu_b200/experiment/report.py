@@ -21,6 +21,7 @@ from pathlib import Path
 import random
 import statistics
 
+from ..mapping import selection_statistics
 from . import protocol as p
 
 BOOTSTRAP_SEED = 20261108
@@ -156,30 +157,44 @@ def validate_calibration_evidence(root, directory, rows, config):
     return evidence
 
 
+def _role_bytes(model, world, mask):
+    """Remote bytes one projection call puts on the links, summed over all
+    sources, for a selection mask (from the mapping's per-source accounting)."""
+    m = model["sequence"] * model["micro_batch"]
+    stats = selection_statistics(m, model["hidden"], world, model["chunk_rows"], list(mask))
+    return sum(stats["remote_wire_bytes_by_source"])
+
+
 def execution_plan_summary(bundle, config):
+    """Per role of the frozen plan: how far the arrival order moved from the
+    common interleave, how many blocks the selective arm quantizes, and the
+    remote bytes that selection puts on the links against all-BF16 and
+    all-TACO traffic."""
     if bundle is None:
         return None
     model, world = config["model"], config["world_size"]
-    base = [item["physical"] for item in p.expected_schedule(model, world, "flux_taco_interleaved")]
-    elements = model["chunk_rows"] * model["hidden"]
-    count = len(base)
-    plain = (world - 1) * count * elements * 2
-    full = (world - 1) * count * (elements // 128 * 136)
+    interleave = [item["physical"] for item in p.expected_schedule(model, world, "flux_taco_interleaved")]
+    count = len(interleave)
+    bf16 = _role_bytes(model, world, [False] * count)
+    full = _role_bytes(model, world, [True] * count)
     roles = {}
     for role, plan in bundle["roles"].items():
-        chosen = sum(plan["selective_mask"])
-        wire = plain - (world - 1) * chosen * (elements // 128 * 120)
-        roles[role] = dict(arrival_identity=plan["arrival_order"] == base,
-                           arrival_changed_slots=sum(a != b for a, b in zip(plan["arrival_order"], base)),
-                           selective_blocks=chosen, physical_blocks=count,
-                           actual_quantized_remote_fraction=chosen / count, remote_bytes_all_sources=wire,
-                           bf16_remote_bytes_all_sources=plain, full_quantized_remote_bytes_all_sources=full,
-                           remote_bytes_ratio_to_bf16=wire / plain, remote_bytes_ratio_to_full_quantized=wire / full,
-                           remote_bytes_reduction_vs_bf16_percent=100 * (1 - wire / plain),
-                           role_plan_sha256=p.digest(plan), diagnostics=plan["diagnostics"])
+        order, mask = plan["arrival_order"], plan["selective_mask"]
+        moved = sum(1 for slot, physical in enumerate(order) if physical != interleave[slot])
+        wire = _role_bytes(model, world, mask)
+        chosen = sum(mask)
+        roles[role] = dict(
+            arrival_identity=moved == 0, arrival_changed_slots=moved, selective_blocks=chosen,
+            physical_blocks=count, actual_quantized_remote_fraction=chosen / count,
+            remote_bytes_all_sources=wire, bf16_remote_bytes_all_sources=bf16,
+            full_quantized_remote_bytes_all_sources=full, remote_bytes_ratio_to_bf16=wire / bf16,
+            remote_bytes_ratio_to_full_quantized=wire / full,
+            remote_bytes_reduction_vs_bf16_percent=100.0 * (bf16 - wire) / bf16,
+            role_plan_sha256=p.digest(plan), diagnostics=plan["diagnostics"])
     return dict(execution_plan_sha256=p.digest(bundle), budget=config["calibration"]["quant_budget"],
                 transport_lanes=2, roles=roles,
-                limitation="Arrival identity describes the producer order only; D/E still use per-lane ready consumers.")
+                limitation="The arrival order changes which blocks are produced first; the arrival arms "
+                           "still consume with per-lane ready consumers whatever the order.")
 
 
 def replay(root):
