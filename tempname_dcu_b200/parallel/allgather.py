@@ -104,7 +104,8 @@ class SymmAgGemm:
     ``out = epilogue(AG(x_local) @ weight^T)`` (weight [N, K], or [K, N] with
     ``b_mn``) and returns the gathered rows ``full`` [world * rows, K] too.
     Every call of an instance gathers the same [rows, K] block shape; creation
-    is collective.
+    is collective.  ``wait_seconds`` bounds the wait for each peer's rows (on
+    expiry the kernel records a peer-flag timeout and returns).
 
     ``taco=True`` compresses the gather: each rank stages its rows as TACO
     H128/E4M3 packets (136 bytes per 128 values, 0.53 of BF16 on the link)
@@ -113,9 +114,12 @@ class SymmAgGemm:
 
     STORE, BIAS, BIAS_GELU, GELU_BWD = 0, 1, 2, 3
 
-    def __init__(self, tp, rows, cols, taco=False):
+    def __init__(self, tp, rows, cols, taco=False, wait_seconds=PEER_WAIT_SECONDS):
         import torch
         from .symmetric import SymmetricHeap
+        if not 0 < wait_seconds <= 600:
+            raise ValueError("wait_seconds must be in (0, 600]")
+        self.wait_seconds = float(wait_seconds)
         if rows % 256 or cols % 64 or (taco and cols % 128):
             raise ValueError("the fused all-gather GEMM needs rows % 256 == 0 and K % 64 == 0 (K % 128 compressed)")
         self.tp, self.rows, self.cols = tp, int(rows), int(cols)
@@ -160,7 +164,7 @@ class SymmAgGemm:
             0 if aux is None else aux.data_ptr(), 0 if aux_t is None else aux_t.stride(0),
             0 if aux_out is None else aux_out.data_ptr(), float(alpha), bn, self._table(N, bn).data_ptr(),
             self.heap.peers.data_ptr(), self.tp.world, self.tp.rank, 0, self.state.data_ptr(),
-            self.ready.data_ptr(), PEER_WAIT_SECONDS, int(self.taco), native.stream_ptr()), "fused all-gather GEMM")
+            self.ready.data_ptr(), self.wait_seconds, int(self.taco), native.stream_ptr()), "fused all-gather GEMM")
         self.calls += 1
         if mode == self.BIAS_GELU:
             return out, full, aux_out

@@ -66,9 +66,23 @@ class SymmetricHeap:
         self.base = int(base.value)
         native.check(lib.tdb_memset_async(self.base + self.nbytes, CANARY_VALUE, CANARY_BYTES, native.stream_ptr()),
                      "symm canary")
+        self.opened = []
+        if getattr(tp, "loopback", False):  # every peer is this GPU's own heap (one-GPU wait tests)
+            addrs = [self.base] * tp.world
+        else:
+            addrs = self._map_peers(tp, handle, hbytes)
+        self.addrs = addrs
+        self.peers = torch.tensor(addrs, dtype=torch.int64, device=self.device)
+        torch.cuda.synchronize()
+        tp.barrier()
+        self.closed = False
+
+    def _map_peers(self, tp, handle, hbytes):
+        """Exchange IPC handles over the group and open every peer's heap."""
+        import torch
+        lib = native.lib()
         mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
         everyone = tp.all_gather_stacked(mine).cpu()
-        self.opened = []
         addrs = []
         for r in range(tp.world):
             if r == tp.rank:
@@ -79,11 +93,7 @@ class SymmetricHeap:
             native.check(lib.tdb_symm_open(ctypes.addressof(buf), ctypes.byref(ptr)), f"symm open rank {r}")
             addrs.append(int(ptr.value))
             self.opened.append(int(ptr.value))
-        self.addrs = addrs
-        self.peers = torch.tensor(addrs, dtype=torch.int64, device=self.device)
-        torch.cuda.synchronize()
-        tp.barrier()
-        self.closed = False
+        return addrs
 
     def canaries_intact(self):
         """True when the guard bytes after this rank's heap still hold the canary."""

@@ -99,3 +99,36 @@ class TPGroup:
     def barrier(self):
         if self.world > 1:
             self.dist.barrier(group=self.group)
+
+
+class LoopbackGroup:
+    """A stand-in tensor-parallel group of ``world`` ranks on ONE GPU: this
+    process is rank 0 and every peer's symmetric heap is this GPU's own heap,
+    so no data is exchanged and nothing ever signals on behalf of the missing
+    ranks.  It exists to drive the fused kernels' bounded waits to expiry on
+    a single device (failure-detection tests): a wait for another rank's flag
+    runs out, the kernel records the status and returns, and the host raises.
+    It is not a way to compute anything."""
+
+    loopback = True
+    backend = "loopback"
+
+    def __init__(self, world=2):
+        if world < 2:
+            raise ValueError("a loopback group stands in for at least two ranks")
+        self.world, self.rank, self.group = int(world), 0, None
+        self.symm_gather = None
+
+    def all_gather_stacked(self, t, out=None):
+        stacked = t.unsqueeze(0).expand(self.world, *t.shape)
+        if out is None:
+            return stacked.clone()
+        out.copy_(stacked)
+        return out
+
+    def all_reduce_(self, t, op=None):
+        return t
+
+    def barrier(self):
+        pass
+

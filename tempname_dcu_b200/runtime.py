@@ -108,7 +108,7 @@ def initialize_context(group, capacity_bytes=None):
                 raise ValueError("context receive capacity too small for this operator; create the context "
                                  "with the model's largest projection first")
             return ctx
-        tp = TPGroup(group)
+        tp = group if getattr(group, "loopback", False) else TPGroup(group)
         if tp.world < 2:
             raise ValueError("the fused operator needs a group of at least two ranks")
         ctx = Context(tp, capacity_bytes or (64 << 20))
@@ -160,7 +160,7 @@ class FluxB200:
     """Fused GEMM + reduce-scatter for one projection shape and arm."""
 
     def __init__(self, m, n, k, group, arm, codec=None, chunk_rows=128, plan=None, diagnostic_delay_cycles=0,
-                 b_mn=False, tile_n=None, remote_first=False, selective_mode="wire"):
+                 b_mn=False, tile_n=None, remote_first=False, selective_mode="wire", wait_seconds=PEER_WAIT_SECONDS):
         """``remote_first`` (first three arms only): produce the blocks bound for
         other ranks first and this rank's own blocks last, so the NVLink
         transfers overlap the local tiles; results are bitwise unchanged (the
@@ -172,8 +172,15 @@ class FluxB200:
         calibrated blocks on the link (TACO packets, the reference's mode);
         ``"fp8-mma"`` instead computes their GEMM tiles as block-scaled FP8
         tcgen05 MMAs (e4m3 with one power-of-two scale per 32 K values) and
-        sends every block as BF16."""
+        sends every block as BF16.
+
+        ``wait_seconds`` bounds every wait of the consumer for other ranks'
+        blocks; on expiry the kernel records a peer-flag timeout in the status
+        word and returns (``check_status`` raises and poisons)."""
         import torch
+        if not 0 < wait_seconds <= 600:
+            raise ValueError("wait_seconds must be in (0, 600]")
+        self.wait_seconds = float(wait_seconds)
         if selective_mode not in ("wire", "fp8-mma"):
             raise ValueError("selective_mode must be 'wire' or 'fp8-mma'")
         if selective_mode == "fp8-mma" and (not arm.endswith("_selective") or b_mn or tile_n not in (None, 128, 256)
@@ -305,7 +312,7 @@ class FluxB200:
                     0 if residual is None else residual.data_ptr(), self.consume.data_ptr(),
                     1 if self.consumer_policy == "per_lane_ready" else 0,
                     0 if timeline is None else timeline.data_ptr(), delay, self._delay_tile[0], self._delay_tile[1],
-                    PEER_WAIT_SECONDS, 0 if self.phase_buffer is None else self.phase_buffer.data_ptr(),
+                    self.wait_seconds, 0 if self.phase_buffer is None else self.phase_buffer.data_ptr(),
                     ctx.call_state.data_ptr())
             if self.mx is None:
                 native.check(lib.tdb_gemm_rs(*args, stream), "fused gemm_rs")
@@ -340,6 +347,21 @@ class FluxB200:
             ctx.submission_lock.release()
 
     __call__ = forward
+
+    def check_status(self):
+        """Wait for this device's queued work, then read the library status
+        word; if a kernel recorded a bounded-wait expiry (a peer that never
+        delivered) or another device-side error, poison this operator and its
+        context -- both refuse every later call -- and raise NativeError.
+        Reference parity: python/flux_dcu/runtime.py:264-266 (an exception
+        during a call marks the operator and the shared context failed)."""
+        import torch
+        torch.cuda.synchronize(self.device)
+        try:
+            native.raise_on_status()
+        except native.NativeError:
+            self.failed = self.context.failed = True
+            raise
 
     def enable_phase_profile(self, on=True):
         """Record per-CTA {start, produce done, first block ready, end} device
