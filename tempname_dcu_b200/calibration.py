@@ -9,6 +9,11 @@ ranks is what the planner sees.  Raw per-rank samples are written
 atomically after every measurement so the controller can replay the planner
 on the CPU and require the same plan.
 
+With ``selection_mode="error_budget"`` (not in the reference) each role's
+selective mask is instead chosen from codec error statistics of one
+calibration batch (``block_statistics``); the arrival order is timed as
+before.
+
 Reference parity: python/flux_dcu/calibration.py:10-127.
 """
 from __future__ import annotations
@@ -28,6 +33,32 @@ def _write(path, value):
     tmp = path.with_suffix(".tmp")
     tmp.write_text(json.dumps(value, indent=2, allow_nan=False) + "\n")
     tmp.replace(path)
+
+
+def block_statistics(x, w, rank, world, group, chunk_rows):
+    """Codec statistics of one projection on a calibration batch, per
+    physical output block (the planner's error-budget input): ``error_sq``
+    sums, over the block's remote sources, the squared TACO round-trip error
+    of their partial products (tdb_taco_block_stats on this rank's partial,
+    SUM over ranks); ``output_sq`` is the squared norm of the reduced output
+    block.  Identical on every rank."""
+    import torch
+    import torch.distributed as dist
+    from .ops import gemm as G
+    from .ops.codec import codec
+    partial = G.linear(x, w)
+    stats = codec().block_stats(partial, chunk_rows)
+    per = stats.shape[0] // world
+    error_sq = stats[:, 2].clone()
+    error_sq[rank * per:(rank + 1) * per] = 0  # a rank's own blocks never cross the link
+    dist.all_reduce(error_sq, group=group)
+    reduced = torch.empty((partial.shape[0] // world, partial.shape[1]), dtype=partial.dtype, device=partial.device)
+    dist.reduce_scatter_tensor(reduced, partial, group=group)
+    mine = codec().block_stats(reduced, chunk_rows)[:, 0].contiguous()
+    output_sq = torch.empty(world * per, dtype=torch.float64, device=partial.device)
+    dist.all_gather_into_tensor(output_sq, mine, group=group)
+    return dict(error_sq=[float(v) for v in error_sq.cpu().tolist()],
+                output_sq=[float(v) for v in output_sq.cpu().tolist()])
 
 
 def calibrate(config, group, out):
@@ -87,8 +118,15 @@ def calibrate(config, group, out):
             _write(destination, dict(schema=SAMPLES_SCHEMA, rank=rank, samples=samples))
             return elapsed
 
+        stats = None
+        if cfg.get("selection_mode") == "error_budget":  # one calibration batch per role
+            gen = torch.Generator(device="cuda").manual_seed(9_000_000 + 173 * rank + 7919 * role_index)
+            x = torch.randn((m, k), generator=gen, device="cuda").to(torch.bfloat16)
+            w = (torch.randn((n, k), generator=gen, device="cuda") / math.sqrt(k)).to(torch.bfloat16)
+            stats = block_statistics(x, w, rank, world, group, chunk)
         roles[role] = fit_role(m, n, k, world, chunk, evaluate, config=cfg,
-                               seed=8_000_000 + 10_000_000 * role_index + int(config.get("seed", 1234)))
+                               seed=8_000_000 + 10_000_000 * role_index + int(config.get("seed", 1234)),
+                               block_stats=stats)
     bundle = dict(schema=SCHEMA, world_size=world, transport_lanes=2, roles=roles)
     digest = role_digest(bundle)
     gathered = [None] * world

@@ -63,6 +63,11 @@ def arguments(argv=None):
     ap.add_argument("--calibration-pairs", type=int, default=3)
     ap.add_argument("--calibration-warmup", type=int, default=2)
     ap.add_argument("--calibration-min-gain", type=float, default=0.002)
+    ap.add_argument("--selection", choices=("timing", "error-budget"), default="timing",
+                    help="how the selective arm picks its blocks: paired timing (the reference) or the codec error "
+                         "measured on a calibration batch, within --error-budget")
+    ap.add_argument("--error-budget", type=float, default=0.01,
+                    help="relative L2 error of a projection output the selected blocks may add (error-budget mode)")
     scopes = ap.add_mutually_exclusive_group()
     scopes.add_argument("--operator-only", action="store_true")
     scopes.add_argument("--preflight-only", action="store_true")
@@ -82,6 +87,8 @@ def arguments(argv=None):
     args.calibration = dict(warmup=args.calibration_warmup, iterations=args.calibration_iters,
                             training_pairs=args.calibration_pairs, confirmation_pairs=args.calibration_pairs,
                             min_gain=args.calibration_min_gain, quant_budget=args.quant_budget)
+    if args.selection == "error-budget":
+        args.calibration.update(selection_mode="error_budget", error_budget=args.error_budget)
     p.validate_calibration_options(args.calibration)
     p.require(not args.report or (args.out is not None and not args.execute and not args.operator_only
                                   and not args.preflight_only), "--report needs --out and cannot execute a stage")

@@ -23,7 +23,9 @@ import re
 import tempfile
 
 from ..mapping import ARMS, BACKEND
+from ..planning import OPTIONAL as OPTIONAL_CALIBRATION
 from ..planning import SCHEMA as PLAN_SCHEMA
+from ..planning import SELECTION_MODES
 
 PROTOCOL = "b200-flux-five-arm-arrival-selective-v1"
 ARRIVAL = "flux_taco_interleaved_arrival"
@@ -158,7 +160,15 @@ def series(length):
 
 
 def validate_calibration_options(options):
-    require(isinstance(options, dict) and set(options) == set(CALIBRATION), "wrong calibration option keys")
+    require(isinstance(options, dict) and set(CALIBRATION) <= set(options) <= set(CALIBRATION) | set(OPTIONAL_CALIBRATION),
+            "wrong calibration option keys")
+    mode = options.get("selection_mode", "timing")
+    require(mode in SELECTION_MODES, f"selection_mode must be one of {SELECTION_MODES}")
+    require(("error_budget" in options) == (mode == "error_budget"),
+            "error_budget is given exactly when selection_mode is 'error_budget'")
+    if mode == "error_budget":
+        require(finite_number(options["error_budget"]) and 0 < options["error_budget"] <= 1,
+                "error_budget must lie in (0, 1]")
     check_fields(options, [
         ("iterations", positive_int, "positive integer required"),
         ("training_pairs", positive_int, "positive integer required"),

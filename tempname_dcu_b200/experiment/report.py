@@ -150,8 +150,11 @@ def validate_calibration_evidence(root, directory, rows, config):
                       "calibration candidate/seed/order differs from the frozen planner replay")
             return sample["max_rank_elapsed_seconds"]
         shape = p.role_shape(model, world, role)
+        # error-budget mode: the mask is recomputed from the statistics frozen in the plan
+        stats = (plan["roles"][role]["diagnostics"].get("selective", {}).get("block_statistics")
+                 if cfg.get("selection_mode") == "error_budget" else None)
         rebuilt = planner.fit_role(shape[0], shape[1], shape[2], world, model["chunk_rows"], evaluate, config=cfg,
-                                   seed=8_000_000 + 10_000_000 * index + config["seed"])
+                                   seed=8_000_000 + 10_000_000 * index + config["seed"], block_stats=stats)
         p.require(rebuilt == plan["roles"][role], "calibration replay does not reproduce the frozen role plan")
     p.require(next(stream, None) is None, "unexpected extra calibration samples")
     return evidence

@@ -23,6 +23,13 @@ calibrations are interchangeable):
    only when the budget allows every block.
 3. The frozen plan records every measurement in ``diagnostics``.
 
+Optional error-budget mode (``selection_mode="error_budget"``, not in the
+reference): step 2 instead ranks blocks by the TACO round-trip error measured
+on a calibration batch and keeps the largest prefix whose predicted relative
+error of the projection output stays within ``error_budget``
+(``_fit_mask_error``); the statistics are frozen into the plan, so replay
+reproduces the mask from the plan alone.
+
 Reference parity: ``python/flux_dcu/planning.py:11-280`` (schema, digest,
 base order, validation, candidates, quantization statistics, settings,
 paired measurement, confirmation, fit_role).
@@ -39,6 +46,11 @@ ARRIVAL_ARM = "flux_taco_interleaved_arrival"
 SELECTIVE_ARM = "flux_taco_interleaved_arrival_selective"
 DEFAULTS = dict(warmup=2, iterations=5, training_pairs=3, confirmation_pairs=3, min_gain=0.002,
                 quant_budget=0.25)
+# Optional settings (absent = the reference's timing-based selection, so plans
+# frozen in that mode stay byte-compatible): selection_mode "error_budget"
+# picks the selective mask from measured codec error instead of timing.
+SELECTION_MODES = ("timing", "error_budget")
+OPTIONAL = dict(selection_mode="timing", error_budget=0.01)
 PLAN_KEYS = frozenset({"shape", "chunk_rows", "arrival_order", "selective_mask", "diagnostics"})
 
 
@@ -157,9 +169,21 @@ def quantization_statistics(plan, world):
 def settings(values=None):
     cfg = dict(DEFAULTS)
     if values is not None:
-        if not isinstance(values, dict) or set(values) - set(DEFAULTS):
+        if not isinstance(values, dict) or set(values) - set(DEFAULTS) - set(OPTIONAL):
             raise ValueError("unknown calibration settings")
         cfg.update(values)
+    mode = cfg.get("selection_mode", "timing")
+    if mode not in SELECTION_MODES:
+        raise ValueError(f"selection_mode must be one of {SELECTION_MODES}")
+    if mode == "timing":
+        if "error_budget" in cfg:
+            raise ValueError("error_budget applies to selection_mode 'error_budget' only")
+        cfg.pop("selection_mode", None)
+    else:
+        budget = cfg.setdefault("error_budget", OPTIONAL["error_budget"])
+        if type(budget) not in (int, float) or not math.isfinite(budget) or not 0 < budget <= 1:
+            raise ValueError("error_budget must be in (0, 1]")
+        cfg["error_budget"] = float(budget)
     for key in ("warmup", "iterations", "training_pairs", "confirmation_pairs"):
         floor = 0 if key == "warmup" else 1
         if type(cfg[key]) is not int or cfg[key] < floor:
@@ -283,12 +307,64 @@ def _fit_mask(shape, order, evaluate, cfg, seed):
     return mask, diag
 
 
-def fit_role(m, n, k, world, chunk_rows, evaluate, *, config=None, seed=8_000_000):
-    """Measure, confirm and freeze one role plan."""
+def validate_block_statistics(stats, blocks):
+    """Codec statistics of one role on a calibration batch, per physical
+    output block: ``error_sq`` = sum over the block's remote sources of the
+    squared TACO round-trip error of their partial products, ``output_sq`` =
+    squared norm of the reduced output block."""
+    if not isinstance(stats, dict) or set(stats) != {"error_sq", "output_sq"}:
+        raise ValueError("block statistics need exactly error_sq and output_sq")
+    for key in ("error_sq", "output_sq"):
+        values = stats[key]
+        if (not isinstance(values, list) or len(values) != blocks
+                or any(type(v) not in (int, float) or not math.isfinite(v) or v < 0 for v in values)):
+            raise ValueError(f"block statistics {key}: one finite non-negative number per physical block")
+    if sum(stats["output_sq"]) <= 0:
+        raise ValueError("block statistics: the reduced output is all zero")
+    return stats
+
+
+def _fit_mask_error(shape, order, stats, cfg):
+    """Selective mask by error budget: blocks in ascending order of their
+    codec error (ties by block index) are added while the predicted relative
+    L2 error of the whole projection output, sqrt(sum chosen error_sq / sum
+    output_sq), stays within ``error_budget`` and the count within the block
+    budget.  Every block saves the same wire bytes, so the cheapest-error
+    blocks are the ones worth compressing.  No timing is involved."""
+    blocks = len(order)
+    validate_block_statistics(stats, blocks)
+    cap = math.floor(blocks * cfg["quant_budget"])
+    err, out_total = stats["error_sq"], sum(stats["output_sq"])
+    ranked = sorted(range(blocks), key=lambda p: (err[p], p))
+    chosen, spent = [], 0.0
+    for physical in ranked:
+        if len(chosen) == cap or math.sqrt((spent + err[physical]) / out_total) > cfg["error_budget"]:
+            break
+        chosen.append(physical)
+        spent += err[physical]
+    mask = [p in set(chosen) for p in range(blocks)]
+    diag = dict(method="error_budget", selected_candidate=f"error_budget{len(chosen)}", accepted=bool(chosen),
+                zero_fallback=not chosen, budget_fraction=cfg["quant_budget"], budget_cap_blocks=cap,
+                error_budget=cfg["error_budget"], ranked_blocks=ranked, selected_physical_blocks=sorted(chosen),
+                predicted_relative_l2=math.sqrt(spent / out_total),
+                block_statistics=dict(error_sq=list(err), output_sq=list(stats["output_sq"])))
+    return mask, diag
+
+
+def fit_role(m, n, k, world, chunk_rows, evaluate, *, config=None, seed=8_000_000, block_stats=None):
+    """Measure, confirm and freeze one role plan.  With ``selection_mode``
+    "error_budget" the selective mask comes from ``block_stats`` (see
+    ``validate_block_statistics``) instead of paired timing; the arrival
+    order is always chosen by timing."""
     cfg = settings(config)
     shape = (m, n, k, world, chunk_rows)
     order, arrival = _fit_order(shape, evaluate, cfg, seed)
-    mask, selective = _fit_mask(shape, order, evaluate, cfg, seed)
+    if cfg.get("selection_mode") == "error_budget":
+        if block_stats is None:
+            raise ValueError("selection_mode 'error_budget' needs the calibration batch's block statistics")
+        mask, selective = _fit_mask_error(shape, order, block_stats, cfg)
+    else:
+        mask, selective = _fit_mask(shape, order, evaluate, cfg, seed)
     final = make_role(*shape, order=order, mask=mask)
     final["diagnostics"] = dict(
         method="same-codec-paired-complete-operator-selection-v2", settings=cfg,

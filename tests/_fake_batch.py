@@ -92,8 +92,12 @@ def fake_rows(job, job_config, directory, library_sha256, world=2):
                                     bf16_relative_l2=0.01, codec_reference_relative_l2=0.001,
                                     correctness_passed=True))
                 return t
+            stats = None
+            if config["calibration"].get("selection_mode") == "error_budget":
+                blocks = m // model["chunk_rows"]
+                stats = dict(error_sq=[1e-5 * (1 + (7 * b) % 5) for b in range(blocks)], output_sq=[1.0] * blocks)
             roles[role] = P.fit_role(m, n, k, world, model["chunk_rows"], evaluate, config=config["calibration"],
-                                     seed=8_000_000 + 10_000_000 * index + config["seed"])
+                                     seed=8_000_000 + 10_000_000 * index + config["seed"], block_stats=stats)
         bundle = dict(schema=P.SCHEMA, world_size=world, transport_lanes=2, roles=roles)
         for row in rows:
             mine = [dict(s, local_elapsed_seconds=s["max_rank_elapsed_seconds"] * (1 if row["rank"] else 0.9))

@@ -3,6 +3,7 @@ tests/test_mapping.py and tests/test_planning.py), plus the fused operator's
 device tables (tile order, consumption order, signal counts)."""
 import copy
 import json
+import math
 
 import pytest
 
@@ -240,6 +241,46 @@ def test_full_budget_allows_full_quantization():
 def test_invalid_or_failed_measurements_are_fatal(bad):
     with pytest.raises(ValueError):
         P.fit_role(*SHAPE, lambda *a: bad, config=CFG)
+
+
+def test_error_budget_mode_selects_cheapest_blocks_within_budget():
+    """selection_mode="error_budget": blocks are taken in ascending codec
+    error while sqrt(sum error_sq / sum output_sq) <= error_budget and the
+    count <= floor(blocks * quant_budget); no mask timing is measured."""
+    evaluate, calls = evaluator()
+    stats = dict(error_sq=[4e-4, 1e-4, 9e-4, 2e-4], output_sq=[1.0, 1.0, 1.0, 1.0])
+    cfg = dict(CFG, quant_budget=1.0, selection_mode="error_budget", error_budget=0.01)
+    plan = P.fit_role(*SHAPE, evaluate, config=cfg, block_stats=stats)
+    # 1e-4 (block 1) + 2e-4 (block 3) -> sqrt(3e-4 / 4) = 0.0087 <= 0.01; adding 4e-4 -> 0.0132 > 0.01
+    assert plan["selective_mask"] == [False, True, False, True]
+    sel = plan["diagnostics"]["selective"]
+    assert sel["method"] == "error_budget" and sel["ranked_blocks"] == [1, 3, 0, 2]
+    assert math.isclose(sel["predicted_relative_l2"], math.sqrt(3e-4 / 4))
+    assert sel["block_statistics"] == stats
+    assert not any(c["arm"] == P.SELECTIVE_ARM for c in calls)  # the mask was not timed
+    # the block budget still caps the count
+    capped = P.fit_role(*SHAPE, evaluate, config=dict(cfg, quant_budget=0.25, error_budget=1.0), block_stats=stats)
+    assert capped["selective_mask"] == [False, True, False, False]
+    # replay from the frozen statistics reproduces the plan exactly
+    again = P.fit_role(*SHAPE, evaluator()[0], config=cfg, block_stats=sel["block_statistics"])
+    assert again == plan
+
+
+def test_error_budget_settings_and_statistics_are_checked():
+    assert "selection_mode" not in P.settings(CFG)  # timing plans keep the reference's settings exactly
+    with pytest.raises(ValueError):
+        P.settings(dict(CFG, error_budget=0.01))  # a budget without the mode
+    with pytest.raises(ValueError):
+        P.settings(dict(CFG, selection_mode="error_budget", error_budget=0.0))
+    with pytest.raises(ValueError):
+        P.settings(dict(CFG, selection_mode="fastest"))
+    cfg = dict(CFG, selection_mode="error_budget")
+    with pytest.raises(ValueError):
+        P.fit_role(*SHAPE, evaluator()[0], config=cfg)  # statistics required
+    for bad in (dict(error_sq=[0.1] * 3, output_sq=[1.0] * 4), dict(error_sq=[0.1] * 4, output_sq=[0.0] * 4),
+                dict(error_sq=[float("nan")] * 4, output_sq=[1.0] * 4), dict(error_sq=[0.1] * 4)):
+        with pytest.raises(ValueError):
+            P.fit_role(*SHAPE, evaluator()[0], config=cfg, block_stats=bad)
 
 
 def test_gemm_tile_picker_prefers_full_waves():

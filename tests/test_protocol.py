@@ -224,6 +224,20 @@ def test_replay_checks_the_fp8_mma_selective_contract(tmp_path):
         R.replay(out)
 
 
+def test_replay_reproduces_an_error_budget_selection(tmp_path):
+    out = _fixture(tmp_path, ["--selection", "error-budget", "--error-budget", "0.01"])
+    report = R.replay(out)
+    assert report["completed"]
+    plan = json.loads((out / "selection-plan.json").read_text())
+    for role in ("attn", "mlp"):
+        sel = plan["roles"][role]["diagnostics"]["selective"]
+        assert sel["method"] == "error_budget" and sel["predicted_relative_l2"] <= 0.01
+        assert sum(plan["roles"][role]["selective_mask"]) == len(sel["selected_physical_blocks"]) > 0
+    assert C.arguments(["--selection", "error-budget", "--error-budget", "0.02"]).calibration["error_budget"] == 0.02
+    with pytest.raises(ValueError):
+        C.arguments(["--selection", "error-budget", "--error-budget", "0"])
+
+
 def test_replay_accepts_training_windows(tmp_path):
     out = _fixture(tmp_path, train=True)
     report = R.replay(out)
