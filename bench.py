@@ -31,8 +31,14 @@ import threading
 import time
 
 METRIC = "GPT-6.7B TP8 train tokens/s (max over ranks) at 1/2/4/8 B200; fused-op roofline %"
-# Best published predecessor number: MA11 on 8xH100, GPT-6.7B TP8, train tokens/s.
-BASELINE_TOKENS_PER_S = 18177.69
+# Same-box baseline ("same-box baseline" table): the reference
+# design on CUDA -- stock PyTorch with cuBLAS GEMMs, SDPA and NCCL all-gather /
+# reduce-scatter, `bench.py --impl baseline` -- measured on B200 with this
+# script at the same N and config.  vs_baseline divides by the entry for the
+# run's N (null where none was measured).
+SAME_BOX_BASELINE_TOKENS_PER_S = {8: 38951.11}
+# Best published predecessor number (8xH100, GPT-6.7B TP8, 8192 tok/step), context only.
+PUBLISHED_MA11_TOKENS_PER_S = 18177.69
 
 
 def parse():
@@ -237,7 +243,9 @@ def main():
         line = dict(
             metric=METRIC, value=round(value, 2), unit="tokens/s", n_gpus=world, steps=args.steps,
             warmup=args.warmup, ms_per_step=round(ms_per_step, 3), higher_is_better=True, scaling="strong",
-            vs_baseline=round(value / BASELINE_TOKENS_PER_S, 4), dtype="bf16",
+            vs_baseline=(round(value / SAME_BOX_BASELINE_TOKENS_PER_S[world], 4)
+                         if world in SAME_BOX_BASELINE_TOKENS_PER_S and args.impl == "ours" and not args.small
+                         else None), dtype="bf16",
             data="synthetic uniform tokens, random-init N(0,0.02) weights",
             impl=args.impl,
             config=dict(model="GPT-6.7B" if not args.small else "GPT-small-2L (smoke)",
@@ -250,7 +258,10 @@ def main():
                         cuda_graph=bool(args.impl == "ours" and not args.no_graph),
                         l2="inputs larger than L2 (13 GB of bf16 weights streamed per step); no flush",
                         model_tflops_per_gpu=round(flops / (ms_per_step / 1000.0) / world / 1e12, 1),
-                        baseline_ref="published MA11 (8xH100, GPT-6.7B TP8): 18177.69 tok/s",
+                        baseline_ref=dict(
+                            same_box=SAME_BOX_BASELINE_TOKENS_PER_S.get(world),
+                            same_box_impl="stock PyTorch (cuBLAS, SDPA, NCCL): bench.py --impl baseline",
+                            published_ma11_8xh100=PUBLISHED_MA11_TOKENS_PER_S),
                         final_loss=final_loss, e2e_last_loss=loss_value),
             clocks=clocks,
             e2e=dict(value=round(tokens_per_step * 1000.0 / e2e_ms, 2), unit="tokens/s",

@@ -110,6 +110,7 @@ __device__ __forceinline__ void decode_rows(const Pull& a, int s, uint32_t parit
 // `s_ok` is the epilogue scratch word of the mainloop's barrier slot (no static
 // shared memory: the dynamic allocation already uses the per-block maximum).
 // `et` is the thread's index among the 128 pulling threads (four warps).
+template <int U>
 __device__ void pull_rows(const Pull& a, volatile int& s_ok, int* status, int et) {
   const uint32_t epoch = __ldg(a.state), parity = __ldg(a.state + 1);
   if (blockIdx.x == 0 && et == 0) {
@@ -159,12 +160,12 @@ __device__ void pull_rows(const Pull& a, volatile int& s_ok, int* status, int et
       } else {
         const uint4* src = reinterpret_cast<const uint4*>(src_slot(a, s, parity) + r0 * a.cols);
         int64_t i = et;
-        for (; i + 3 * 128 < n; i += 4 * 128) {
-          uint4 v[4];
+        for (; i + (U - 1) * 128 < n; i += U * 128) {  // U 16-byte loads in flight per thread
+          uint4 v[U];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) v[u] = src[i + u * 128];
+          for (int u = 0; u < U; ++u) v[u] = src[i + u * 128];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) dst[i + u * 128] = v[u];
+          for (int u = 0; u < U; ++u) dst[i + u * 128] = v[u];
         }
         for (; i < n; i += 128) dst[i] = src[i];
       }
@@ -177,11 +178,15 @@ __device__ void pull_rows(const Pull& a, volatile int& s_ok, int* status, int et
   }
 }
 
-// AUX = false: the epilogue warps (2..5) pull before their first tile, so the
-// epilogue of the first tiles waits for the whole pull.  AUX = true: four
-// extra warps (6..9) pull while the epilogue warps drain finished tiles.
-template <class Inner, bool AUX>
+// PULL = 0: the epilogue warps (2..5) pull before their first tile, so the
+// epilogue of the first tiles waits for the whole pull.  PULL = 1: four
+// extra warps (6..9) pull while the epilogue warps drain finished tiles, four
+// 16-byte loads in flight per thread; PULL = 2: the same warps with sixteen
+// loads in flight per thread (32 KB per SM), for a link whose latency under
+// all-to-all load needs more bytes in flight to reach its bandwidth.
+template <class Inner, int PULL>
 struct PullEpi {
+  static constexpr bool AUX = PULL != 0;
   const EpiParams& p;
   const Pull& a;
   Inner inner;
@@ -194,35 +199,35 @@ struct PullEpi {
     inner.set_smem(s);
   }
   __device__ __forceinline__ void prologue(int* status) {
-    if constexpr (!AUX) pull_rows(a, *scratch, status, int(threadIdx.x) - 64);
+    if constexpr (!AUX) pull_rows<4>(a, *scratch, status, int(threadIdx.x) - 64);
   }
   __device__ __forceinline__ void aux(int* status) {
-    if constexpr (AUX) pull_rows(a, *scratch, status, int(threadIdx.x) - 192);
+    if constexpr (AUX) pull_rows<PULL == 2 ? 16 : 4>(a, *scratch, status, int(threadIdx.x) - 192);
   }
   __device__ __forceinline__ void tile_begin(int mb, int nb) { inner.tile_begin(mb, nb); }
   __device__ __forceinline__ void chunk(int row, int col, int c, const uint32_t (&r)[32]) { inner.chunk(row, col, c, r); }
   __device__ __forceinline__ void tile_end(int mb, int nb, int q, int lane) { inner.tile_end(mb, nb, q, lane); }
 };
 
-template <int BN, bool B_MN, int MODE, bool AUX>
-__global__ void __launch_bounds__(gemm::kThreads + (AUX ? 128 : 0), 1)
+template <int BN, bool B_MN, int MODE, int PULL>
+__global__ void __launch_bounds__(gemm::kThreads + (PULL ? 128 : 0), 1)
     ag_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int K,
                    TileOrder order, const __grid_constant__ EpiParams ep, const __grid_constant__ Pull pull,
                    int* status) {
   using Inner = typename gemm::EpiFor<MODE>::type;
-  PullEpi<Inner, AUX> epi(ep, pull);
+  PullEpi<Inner, PULL> epi(ep, pull);
   gemm::gemm_mainloop<BN, false, B_MN>(&tmA, &tmB, K, order, epi, status);
 }
 
 constexpr int k2Stages = 6;
 
-template <bool B_MN, int MODE, bool AUX>
-__global__ void __launch_bounds__(gemm2::kThreads + (AUX ? 128 : 0), 1)
+template <bool B_MN, int MODE, int PULL>
+__global__ void __launch_bounds__(gemm2::kThreads + (PULL ? 128 : 0), 1)
     ag_gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int K,
                     TileOrder order, const __grid_constant__ EpiParams ep, const __grid_constant__ Pull pull,
                     int* status) {
   using Inner = typename gemm::EpiFor<MODE>::type;
-  using Epi = PullEpi<Inner, AUX>;
+  using Epi = PullEpi<Inner, PULL>;
   Epi epi(ep, pull);
   gemm2::mainloop<false, B_MN, Epi, k2Stages>(&tmA, &tmB, K, order, epi, status);
 }
@@ -256,12 +261,12 @@ static int launch_coop(Kern kern, dim3 grid, int threads, int smem, int cluster,
   return 0;
 }
 
-template <int BN, bool B_MN, int MODE, bool AUX>
+template <int BN, bool B_MN, int MODE, int PULL>
 static int launch1(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, TileOrder order,
                    const EpiParams& ep, const Pull& pull, cudaStream_t s) {
   using Cfg = gemm::Config<BN>;
   constexpr int kSmem = Cfg::kSmemBytes + gemm::EpiFor<MODE>::type::kSmemBytes;
-  auto kern = ag_gemm_kernel<BN, B_MN, MODE, AUX>;
+  auto kern = ag_gemm_kernel<BN, B_MN, MODE, PULL>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -274,17 +279,17 @@ static int launch1(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   order.num_n = (N + BN - 1) / BN;
   order.num_tiles = order.num_m * order.num_n;
   const int grid = order.num_tiles < tdb_host::sm_count() ? order.num_tiles : tdb_host::sm_count();
-  return launch_coop(kern, dim3(grid), gemm::kThreads + (AUX ? 128 : 0), kSmem, 1, s, ta, tb, K, order, ep, pull,
+  return launch_coop(kern, dim3(grid), gemm::kThreads + (PULL ? 128 : 0), kSmem, 1, s, ta, tb, K, order, ep, pull,
                      tdb_host::status_ptr());
 }
 
-template <bool B_MN, int MODE, bool AUX>
+template <bool B_MN, int MODE, int PULL>
 static int launch2(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, TileOrder order,
                    const EpiParams& ep, const Pull& pull, cudaStream_t s) {
   using Cfg = gemm2::Config<k2Stages>;
   constexpr int kSmem = Cfg::kSmemBytes + gemm::EpiFor<MODE>::type::kSmemBytes;
-  constexpr int kBlock = gemm2::kThreads + (AUX ? 128 : 0);
-  auto kern = ag_gemm2_kernel<B_MN, MODE, AUX>;
+  constexpr int kBlock = gemm2::kThreads + (PULL ? 128 : 0);
+  auto kern = ag_gemm2_kernel<B_MN, MODE, PULL>;
   static int max_clusters[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -317,26 +322,30 @@ static int launch2(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
                      tdb_host::status_ptr());
 }
 
-template <bool B_MN, int MODE, bool AUX>
+template <bool B_MN, int MODE, int PULL>
 static int dispatch_tile_aux(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
                              const TileOrder& order, const EpiParams& ep, const Pull& pull, cudaStream_t s) {
   switch (bn) {
-    case 512: return launch2<B_MN, MODE, AUX>(ta, tb, M, N, K, order, ep, pull, s);
-    case 256: return launch1<256, B_MN, MODE, AUX>(ta, tb, M, N, K, order, ep, pull, s);
-    case 192: return launch1<192, B_MN, MODE, AUX>(ta, tb, M, N, K, order, ep, pull, s);
-    default: return launch1<128, B_MN, MODE, AUX>(ta, tb, M, N, K, order, ep, pull, s);
+    case 512: return launch2<B_MN, MODE, PULL>(ta, tb, M, N, K, order, ep, pull, s);
+    case 256: return launch1<256, B_MN, MODE, PULL>(ta, tb, M, N, K, order, ep, pull, s);
+    case 192: return launch1<192, B_MN, MODE, PULL>(ta, tb, M, N, K, order, ep, pull, s);
+    default: return launch1<128, B_MN, MODE, PULL>(ta, tb, M, N, K, order, ep, pull, s);
   }
 }
 
 // Pull placement of the following calls: 0 epilogue-warp prologue, 1 four
-// auxiliary warps (set with tdb_ag_set_variant).
+// auxiliary warps, 2 four auxiliary warps with 16 loads in flight per thread
+// (set with tdb_ag_set_variant).
 static int g_variant = 0;
 
 template <bool B_MN, int MODE>
 static int dispatch_tile(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
                          const TileOrder& order, const EpiParams& ep, const Pull& pull, cudaStream_t s) {
-  return g_variant == 1 ? dispatch_tile_aux<B_MN, MODE, true>(bn, ta, tb, M, N, K, order, ep, pull, s)
-                        : dispatch_tile_aux<B_MN, MODE, false>(bn, ta, tb, M, N, K, order, ep, pull, s);
+  switch (g_variant) {
+    case 1: return dispatch_tile_aux<B_MN, MODE, 1>(bn, ta, tb, M, N, K, order, ep, pull, s);
+    case 2: return dispatch_tile_aux<B_MN, MODE, 2>(bn, ta, tb, M, N, K, order, ep, pull, s);
+    default: return dispatch_tile_aux<B_MN, MODE, 0>(bn, ta, tb, M, N, K, order, ep, pull, s);
+  }
 }
 
 template <bool B_MN>
@@ -372,10 +381,11 @@ TDB_API int tdb_ag_prepare(const void* x, long long ldx, long long rows, long lo
 // mode: 0 store (alpha), 1 bias, 2 bias + GELU (aux_out = pre-activation), 3 GELU backward (aux).
 // Pull placement of the fused all-gather GEMM for the following calls
 // (0: the epilogue warps pull before their first tile; 1: four auxiliary
-// warps pull concurrently); returns the previous value.
+// warps pull concurrently; 2: as 1 with sixteen loads in flight per thread);
+// returns the previous value.
 TDB_API int tdb_ag_set_variant(int variant) {
   const int old = tdb::aggemm::g_variant;
-  if (variant == 0 || variant == 1) tdb::aggemm::g_variant = variant;
+  if (variant >= 0 && variant <= 2) tdb::aggemm::g_variant = variant;
   return old;
 }
 

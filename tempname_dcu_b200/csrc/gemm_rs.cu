@@ -104,6 +104,77 @@ __device__ __forceinline__ uint32_t* flag_ptr(const Params& p, int rank_of_heap,
 }
 
 
+// Variant bit 2: BF16 tiles leave the epilogue as TMA bulk stores
+// (cp.async.bulk shared::cta -> the destination's global memory), one 8 KB
+// store per warp and 128-column half, instead of 16-byte st.global from the
+// warp's lanes; every warp then signals each tile once its stores are
+// complete (deferred by one tile, so the wait overlaps the next tile).
+constexpr int kVariantBulk = 4;
+
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Receive-slot layout of bulk-pushed BF16 tiles: 8 KB slabs of 32 rows x 128
+// columns in slab-major order over the [chunk_rows / 32, N / 128] grid; in a
+// slab, row r holds its sixteen 16-byte chunks XOR-swizzled (physical chunk =
+// logical chunk ^ (r & 15)), exactly as the epilogue staged them.
+constexpr int kSlabBytes = 32 * 128 * 2;
+
+__device__ __forceinline__ int64_t slab_of(int row, int col, int N) { return int64_t(row >> 5) * (N >> 7) + (col >> 7); }
+
+// 16-byte vector v of a slab-layout slot -> its vector index in the
+// row-major [chunk_rows, N] block.
+__device__ __forceinline__ int64_t slab_vec_to_rowmajor(int64_t v, int N) {
+  const int64_t slab = v >> 9;  // 512 vectors per slab
+  const int r = int(v >> 4) & 31, pc = int(v) & 15;
+  const int per_band = N >> 7;
+  const int64_t row = (slab / per_band) * 32 + r;
+  const int64_t col8 = (slab % per_band) * 16 + (pc ^ (r & 15));
+  return row * (N >> 3) + col8;
+}
+
+// Byte offset of element (row, col) (col % 4 == 0) in a slab-layout slot.
+__device__ __forceinline__ int64_t slab_byte(int row, int col, int N) {
+  const int r = row & 31, lc = (col & 127) >> 3;
+  return slab_of(row, col, N) * kSlabBytes + r * 256 + ((lc ^ (r & 15)) << 4) + (col & 7) * 2;
+}
+
+// Consumer policy 2 (training operators, remote-first production order, BF16
+// wire): there is no consumer kernel.  Remote tiles are bulk-pushed (slab
+// layout) and each epilogue warp, once its stores are complete, writes the
+// call's epoch into a per-(block, tile, quarter, source) flag at the
+// destination.  The epilogue of a tile of this rank's own blocks waits for
+// the matching quarter of every peer, then sums the sources in rank order
+// 0..W-1 -- its own partial straight from TMEM, the peers' from the receive
+// slots -- with BF16 rounding after every addition, adds residual and bias,
+// and writes the output rows.  Same arithmetic, hence bitwise the same
+// result, as the consumer kernel.
+constexpr int kPolicyEpilogue = 2;
+constexpr uint64_t kFineFlagsOff = 32768;  // inside the 64 KB flag region
+constexpr uint64_t kFineFlagsBytes = 32768;
+
+__device__ __forceinline__ uint32_t call_epoch(const Params& p) { return __ldg(p.call_state + 2); }
+
+// Flag of (block `within`, tile `t` of the block, row quarter q, source) in
+// the heap of `rank_of_heap`, for the current set.
+__device__ __forceinline__ uint32_t* fine_flag_ptr(const Params& p, int rank_of_heap, int within, int t, int tiles,
+                                                  int q, int source) {
+  const uint64_t idx = ((uint64_t(call_set(p) * p.per + within) * tiles + t) * 4 + q) * p.W + source;
+  return reinterpret_cast<uint32_t*>(p.peers[rank_of_heap] + p.flags_off + kFineFlagsOff + idx * 4);
+}
+
 // One thread encodes one H128 group held in registers (values already BF16
 // rounded).  Same math as codec.cuh; the butterfly pairs and their order are
 // those of the warp version.
@@ -148,7 +219,132 @@ __device__ __forceinline__ void encode_group_thread(float (&x)[128], uint32_t (&
   }
 }
 
-template <int BN>
+constexpr int kMaxWorldEpi = 8;
+
+// Called by lane 0 of an epilogue warp (bulk pushes): wait until this
+// thread's bulk groups, except the `keep_one` most recent, have written,
+// then fence and signal the tile at its destination -- +1 on the (block,
+// source) counter, or (policy 2) the call's epoch in the tile quarter's flag.
+// Out of line: it runs once per tile and keeps the epilogue's registers free.
+__device__ __forceinline__ void signal_stored_tile_inline(const Params* p, int tiles, int dest, int within, int tile,
+                                                         int quarter, int mb, int nb, bool keep_one) {
+  if (keep_one) bulk_wait<1>();
+  else bulk_wait<0>();
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  if (p->delay_cycles > 0 && mb == p->delay_mb && nb == p->delay_nb) {
+    const long long t0 = clock64();
+    while (clock64() - t0 < p->delay_cycles) {
+    }
+  }
+  __threadfence_system();
+  if (p->policy == kPolicyEpilogue)
+    st_release_sys(fine_flag_ptr(*p, dest, within, tile, tiles, quarter, p->rank), call_epoch(*p));
+  else
+    red_release_sys(flag_ptr(*p, dest, within, p->rank), 1u);
+}
+
+__device__ __noinline__ void signal_stored_tile(const Params* p, int tiles, int dest, int within, int tile, int quarter,
+                                                int mb, int nb, bool keep_one) {
+  signal_stored_tile_inline(p, tiles, dest, within, tile, quarter, mb, nb, keep_one);
+}
+
+__device__ __forceinline__ void unpack8(const uint4& w, float (&v)[8]) {
+  const uint32_t a[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[2 * j] = bf16_bits_to_float(a[j] & 0xffff);
+    v[2 * j + 1] = bf16_bits_to_float(a[j] >> 16);
+  }
+}
+
+// Policy 2, own tile, after the epilogue staged one warp's 32 rows x 128
+// columns (BF16, the slab layout of the receive slots) at `own`: the warp
+// reduces them with 16-byte vectors -- lane i takes vectors i, i + 32, ... of
+// the slab, so every load of a peer's slab is coalesced -- in rank order
+// 0..W-1 with BF16 rounding after each addition, then residual and bias, and
+// writes the output rows.  Out of line, so that its registers do not add to
+// the epilogue's.
+__device__ __noinline__ void reduce_staged_half(const Params* p, const uint8_t* own_stage, int within, int rib0, int n0) {
+  const int lane = threadIdx.x & 31;
+  const int N = p->N;
+  const uint4* own = reinterpret_cast<const uint4*>(own_stage);
+  const int64_t slab_off = slab_of(rib0, n0, N) * kSlabBytes;
+  const int64_t out_row0 = int64_t(within) * p->chunk_rows + rib0;
+  __syncwarp();
+#pragma unroll 1
+  for (int i0 = 0; i0 < 16; i0 += 4) {
+    // the residual and bias of these four vectors load with the first
+    // sources, so one memory round trip serves both
+    int64_t o[4];
+    uint4 rw[4], bw[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int v = lane + 32 * (i0 + u);
+      const int r = v >> 4, lc = (v & 15) ^ (r & 15);
+      o[u] = (out_row0 + r) * N + n0 + lc * 8;
+      if (p->residual) rw[u] = *reinterpret_cast<const uint4*>(p->residual + o[u]);
+      if (p->bias) bw[u] = __ldg(reinterpret_cast<const uint4*>(p->bias + n0 + lc * 8));
+    }
+    float acc[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[u][j] = 0.f;
+#pragma unroll
+    for (int s0 = 0; s0 < kMaxWorldEpi; s0 += 4) {
+      uint4 w[4][4];  // [source][vector]
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int s = s0 + t;
+        if (s >= p->W) continue;
+        const uint4* src = s == p->rank ? own
+                                        : reinterpret_cast<const uint4*>(slot_ptr(*p, p->rank, s, within) + slab_off);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int v = lane + 32 * (i0 + u);
+          w[t][u] = s == p->rank ? src[v] : __ldcg(src + v);
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        if (s0 + t >= p->W) continue;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float x[8];
+          unpack8(w[t][u], x);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[u][j] = bf16_bits_to_float(float_to_bf16_bits(acc[u][j] + x[j]));
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (p->residual) {
+        float x[8];
+        unpack8(rw[u], x);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[u][j] = bf16_bits_to_float(float_to_bf16_bits(x[j] + acc[u][j]));
+      }
+      if (p->bias) {
+        float x[8];
+        unpack8(bw[u], x);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[u][j] = bf16_bits_to_float(float_to_bf16_bits(acc[u][j] + x[j]));
+      }
+      uint4 ov;
+      ov.x = pack_bf16x2(acc[u][0], acc[u][1]);
+      ov.y = pack_bf16x2(acc[u][2], acc[u][3]);
+      ov.z = pack_bf16x2(acc[u][4], acc[u][5]);
+      ov.w = pack_bf16x2(acc[u][6], acc[u][7]);
+      *reinterpret_cast<uint4*>(p->out + o[u]) = ov;
+    }
+  }
+  __syncwarp();  // the next half may overwrite the staging
+}
+
+// QUANT = false compiles the TACO wire path out (operators whose blocks all
+// cross as BF16), which frees the 128 registers of the per-row encoder.
+template <int BN, bool QUANT = true>
 struct PushEpi {
   // Per epilogue warp: a 32-row x 128-column BF16 slab (or the TACO payload
   // of those rows), XOR-swizzled in 16-byte chunks so that both the
@@ -165,16 +361,24 @@ struct PushEpi {
   int within, dest, row0, quarter, nbase;
   bool quant;
   uint8_t* slot;
-  float grp[128];
+  float grp[QUANT ? 128 : 1];
   float q_half, a_half;
+  bool bulk = false;
+  // bulk mode, lane 0 of each epilogue warp: the tile whose signal is pending
+  int pend_dest = -1, pend_within = 0, pend_mb = 0, pend_nb = 0, pend_tile = 0;
+  // policy 2: this tile belongs to this rank and is reduced here; its index in the block
+  bool local_reduce = false;
+  int tile_in_block = 0;
 
   __device__ __forceinline__ void set_smem(uint8_t* ptr) { stage_base = ptr; }
   __device__ __forceinline__ void prologue(int*) {}
 
   template <int Q>
   __device__ __forceinline__ void stash(const uint32_t (&r)[32]) {
+    if constexpr (QUANT) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) grp[Q * 32 + j] = bf16_bits_to_float(float_to_bf16_bits(__uint_as_float(r[j])));
+      for (int j = 0; j < 32; ++j) grp[Q * 32 + j] = bf16_bits_to_float(float_to_bf16_bits(__uint_as_float(r[j])));
+    }
   }
 
   __device__ __forceinline__ uint8_t* stage() const { return stage_base + ((threadIdx.x >> 5) & 3) * 32 * kRowBytes; }
@@ -187,10 +391,62 @@ struct PushEpi {
     dest = physical / p->per;
     within = physical % p->per;
     row0 = m0 - physical * p->chunk_rows;
-    quant = p->qmask[physical] != 0 && dest != p->rank;
+    quant = QUANT && p->qmask[physical] != 0 && dest != p->rank;
     slot = slot_ptr(*p, dest, p->rank, within);
     quarter = (threadIdx.x >> 5) & 3;
     nbase = nb * BN;
+    const bool epi_policy = p->policy == kPolicyEpilogue;
+    bulk = epi_policy || (p->variant & kVariantBulk) != 0;
+    tile_in_block = (row0 / BM) * (p->N / BN) + nb;
+    local_reduce = epi_policy && dest == p->rank;
+    if (local_reduce) {
+      // a peer may be waiting in its own epilogue for the tile pushed last:
+      // release it before waiting here
+      if ((threadIdx.x & 31) == 0) signal_pending(false);
+      wait_peer_quarters();
+    }
+  }
+
+  // Policy 2, own tile: every lane waits (bounded) until each peer's copy of
+  // this warp's 32 rows of the tile is in the receive slot.
+  __device__ __forceinline__ void wait_peer_quarters() {
+    const uint32_t epoch = call_epoch(*p);
+    const int tiles = (p->chunk_rows / BM) * (p->N / BN);
+    for (int s = 0; s < p->W; ++s) {
+      if (s == p->rank) continue;
+      const uint32_t* f = fine_flag_ptr(*p, p->rank, within, tile_in_block, tiles, quarter, s);
+      if (int32_t(ld_acquire_sys(f) - epoch) < 0) {
+        const uint64_t t0 = globaltimer();
+        while (int32_t(ld_acquire_sys(f) - epoch) < 0) {
+          if (globaltimer() - t0 > p->wait_ns) {
+            if ((threadIdx.x & 31) == 0) record_status(status, kTimeoutPeerFlag, 41, s, tile_in_block);
+            return;  // the output of this call is invalid; the host raises on the status
+          }
+        }
+      }
+    }
+  }
+
+  __device__ __forceinline__ void reduce_half(int half) {
+    reduce_staged_half(p, stage(), within, row0 + quarter * 32, nbase + half * kHalf);
+  }
+
+  // Lane 0, bulk mode: the pending tile's stores by this warp are complete
+  // (all bulk groups but the `keep_one` most recent retired), then one system
+  // fence and the signal (signal_stored_tile).
+  __device__ __forceinline__ void signal_pending(bool keep_one) {
+    if (pend_dest < 0) return;
+    const int tiles = (p->chunk_rows / BM) * (p->N / BN);
+    if constexpr (QUANT)  // a call here would have to save the encoder's registers
+      signal_stored_tile_inline(p, tiles, pend_dest, pend_within, pend_tile, quarter, pend_mb, pend_nb, keep_one);
+    else
+      signal_stored_tile(p, tiles, pend_dest, pend_within, pend_tile, quarter, pend_mb, pend_nb, keep_one);
+    pend_dest = -1;
+  }
+
+  // After the last tile (epilogue warps): signal what is still pending.
+  __device__ __forceinline__ void finish() {
+    if ((threadIdx.x & 31) == 0) signal_pending(false);
   }
 
   // Copy this warp's staged 32 rows x 128 columns (or their TACO payload and
@@ -201,6 +457,19 @@ struct PushEpi {
     const int n0 = nbase + half * kHalf;
     const int rib0 = row0 + quarter * 32;  // first block row of this warp
     const uint8_t* st = stage();
+    if (bulk && !quant) {
+      // the staged slab goes out as one bulk store; its smem is reusable once read
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        bulk_s2g(slot + slab_of(rib0, n0, N) * kSlabBytes, st, kSlabBytes);
+        bulk_commit();
+        if (half == 0) signal_pending(true);  // the previous tile's groups are older than this one
+        bulk_wait_read<0>();
+      }
+      __syncwarp();
+      return;
+    }
     __syncwarp();
     if (!quant) {
       constexpr int kRowsPerIter = 32 / kChunks;  // 2 rows of 256 bytes per warp store
@@ -211,7 +480,7 @@ struct PushEpi {
         uint16_t* dst = reinterpret_cast<uint16_t*>(slot) + int64_t(rib0 + rr) * N + n0;
         reinterpret_cast<uint4*>(dst)[ch] = v;
       }
-    } else {
+    } else if constexpr (QUANT) {
       constexpr int kPayChunks = kHalf / 16;       // 128 payload bytes per row
       constexpr int kRowsPerIter = 32 / kPayChunks;  // 4 rows per warp store
 #pragma unroll 4
@@ -229,6 +498,7 @@ struct PushEpi {
       scales[groups + g0] = a_half;
     }
     __syncwarp();  // the next half may overwrite the staging
+    if (bulk && half == 0 && lane == 0) signal_pending(false);  // no bulk group of this tile to keep
   }
 
   __device__ __forceinline__ void chunk(int /*row*/, int /*col*/, int c, const uint32_t (&r)[32]) {
@@ -245,7 +515,7 @@ struct PushEpi {
         w.w = pack_bf16x2(__uint_as_float(r[8 * i + 6]), __uint_as_float(r[8 * i + 7]));
         srow[swz(lane, cl * 4 + i)] = w;
       }
-    } else {
+    } else if constexpr (QUANT) {
       // TACO: gather the 128-column group (4 chunks) in registers, BF16
       // rounded; the chunk index is a runtime value (the epilogue loop is not
       // unrolled), so dispatch to a compile-time register offset.
@@ -263,10 +533,29 @@ struct PushEpi {
           srow[swz(lane, i)] = make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2], words[4 * i + 3]);
       }
     }
-    if (cl == 3) push_half(c >> 2);
+    if (cl == 3) {
+      if constexpr (!QUANT) {  // policy 2 never runs with TACO blocks
+        if (local_reduce) {
+          reduce_half(c >> 2);
+          return;
+        }
+      }
+      push_half(c >> 2);
+    }
   }
 
   __device__ __forceinline__ void tile_end(int mb, int nb, int, int lane) {
+    if (local_reduce) return;  // reduced in place: nothing was sent
+    if (bulk) {  // signalled once its stores are complete (next tile's first push or finish())
+      if (lane == 0) {
+        pend_dest = dest;
+        pend_within = within;
+        pend_mb = mb;
+        pend_nb = nb;
+        pend_tile = tile_in_block;
+      }
+      return;
+    }
     // Variant bit 0: this warp's 32 rows of the tile are complete at the
     // destination once its stores are visible -- fence, then add 1 (four
     // warps make the 4 per tile that signal_tiles adds otherwise).
@@ -289,7 +578,9 @@ struct PushEpi {
 // (block, source) counter of every tile it produced, in production order.
 // The diagnostic delay holds back the signal of one tile only.
 __device__ void signal_tiles(const Params& p, const gemm::TileOrder& order) {
-  if (p.variant & 1) return;  // signalled per tile by the epilogue warps
+  // signalled per tile by the epilogue warps (and policy 2 never touches the
+  // per-block counters: its calls do not advance their targets)
+  if ((p.variant & (1 | kVariantBulk)) || p.policy == kPolicyEpilogue) return;
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x != 0) return;
@@ -314,30 +605,28 @@ __device__ __forceinline__ bool block_ready(const Params& p, int within) {
   return true;
 }
 
-__device__ __forceinline__ void unpack8(const uint4& w, float (&v)[8]) {
-  const uint32_t a[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    v[2 * j] = bf16_bits_to_float(a[j] & 0xffff);
-    v[2 * j + 1] = bf16_bits_to_float(a[j] >> 16);
-  }
-}
 
 constexpr int kMaxWorld = 8;
 
 // One 16-byte vector (8 outputs) of a BF16 block: ordered source sum, then
 // residual, then bias.
-__device__ __forceinline__ uint4 reduce_vec8(const Params& p, uint64_t local_base, int within, int64_t v) {
+// Vector v of a BF16 slot -> the block's row-major vector index (slab layout
+// under bulk pushes, identity otherwise).
+__device__ __forceinline__ int64_t out_vec(const Params& p, int64_t v) {
+  return (p.variant & kVariantBulk) ? slab_vec_to_rowmajor(v, p.N) : v;
+}
+
+__device__ __forceinline__ uint4 reduce_vec8(const Params& p, uint64_t local_base, int within, int64_t v, int64_t vo) {
   uint4 src[kMaxWorld];
 #pragma unroll
   for (int s = 0; s < kMaxWorld; ++s)
     if (s < p.W)
       src[s] = __ldcg(reinterpret_cast<const uint4*>(
                           local_base + p.recv_off + (uint64_t(call_set(p) * p.W + s) * p.per + within) * p.slot_bytes) + v);
-  const int64_t ov = int64_t(within) * p.chunk_rows * p.N / 8 + v;
+  const int64_t ov = int64_t(within) * p.chunk_rows * p.N / 8 + vo;
   uint4 rw = make_uint4(0, 0, 0, 0), bw = make_uint4(0, 0, 0, 0);
   if (p.residual) rw = reinterpret_cast<const uint4*>(p.residual)[ov];
-  if (p.bias) bw = reinterpret_cast<const uint4*>(p.bias)[uint32_t(v) % uint32_t(p.N >> 3)];
+  if (p.bias) bw = reinterpret_cast<const uint4*>(p.bias)[uint32_t(vo) % uint32_t(p.N >> 3)];
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int s = 0; s < kMaxWorld; ++s) {
@@ -401,10 +690,10 @@ __device__ void consume_bf16_batch(const Params& p, const int* blocks, int count
     uint4 o[U];
 #pragma unroll
     for (int u = 0; u < U; ++u)
-      if (u < n) o[u] = reduce_vec8(p, local_base, ib[u], iv[u]);
+      if (u < n) o[u] = reduce_vec8(p, local_base, ib[u], iv[u], out_vec(p, iv[u]));
 #pragma unroll
     for (int u = 0; u < U; ++u)
-      if (u < n) reinterpret_cast<uint4*>(p.out)[int64_t(ib[u]) * nvec + iv[u]] = o[u];
+      if (u < n) reinterpret_cast<uint4*>(p.out)[int64_t(ib[u]) * nvec + out_vec(p, iv[u])] = o[u];
   }
 }
 
@@ -433,6 +722,8 @@ __device__ void consume_block_taco(const Params& p, int within, int part, int np
         word[s] = __ldcg(reinterpret_cast<const unsigned int*>(slot + e0));
         qv[s] = __ldcg(scales + gi);
         av[s] = __ldcg(scales + groups + gi);
+      } else if (p.variant & kVariantBulk) {  // this rank's own BF16 tile, bulk-pushed in slab layout
+        plain[s] = __ldcg(reinterpret_cast<const uint2*>(slot + slab_byte(rho, g * 128 + lane * 4, p.N)));
       } else {
         plain[s] = __ldcg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(slot) + e0));
       }
@@ -577,16 +868,17 @@ __device__ void consume_phase(const Params& p, int* status) {
 template <int BN>
 constexpr int kStagesFor = BN == 128 ? 6 : 4;
 
-template <int BN, bool B_MN>
+template <int BN, bool B_MN, bool QUANT>
 __global__ void __launch_bounds__(gemm::kThreads, 1)
     gemm_rs_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int K,
                    gemm::TileOrder order, const __grid_constant__ Params p, int* status) {
-  PushEpi<BN> epi;
+  PushEpi<BN, QUANT> epi;
   epi.p = &p;
   epi.status = status;
   unsigned long long* ph = p.phases ? p.phases + 4 * blockIdx.x : nullptr;
   if (ph && threadIdx.x == 0) ph[0] = globaltimer();
-  gemm::gemm_mainloop<BN, false, B_MN, PushEpi<BN>, kStagesFor<BN>>(&tmA, &tmB, K, order, epi, status);
+  gemm::gemm_mainloop<BN, false, B_MN, PushEpi<BN, QUANT>, kStagesFor<BN>>(&tmA, &tmB, K, order, epi, status);
+  if (threadIdx.x >= 64 && threadIdx.x < 192) epi.finish();
   signal_tiles(p, order);
   if (ph && threadIdx.x == 0) ph[1] = globaltimer();
   if (p.variant & 2) {
@@ -623,13 +915,15 @@ __global__ void __launch_bounds__(gemm::kThreads, 1)
                       const __grid_constant__ CUtensorMap tmA8, const __grid_constant__ CUtensorMap tmB8, int K,
                       gemm::TileOrder order, const __grid_constant__ Params p, const uint8_t* sfa, const uint8_t* sfb,
                       int a_blocks, int b_blocks, const uint8_t* mx_mask, int* status) {
-  PushEpi<BN> epi;
+  PushEpi<BN, false> epi;  // every block crosses as BF16
   epi.p = &p;
   epi.status = status;
   gemm::MxOperands mx{&tmA8, &tmB8, sfa, sfb, a_blocks, b_blocks, mx_mask};
   unsigned long long* ph = p.phases ? p.phases + 4 * blockIdx.x : nullptr;
   if (ph && threadIdx.x == 0) ph[0] = globaltimer();
-  gemm::gemm_mainloop<BN, false, false, PushEpi<BN>, kMxStages<BN>, true>(&tmA, &tmB, K, order, epi, status, &mx);
+  gemm::gemm_mainloop<BN, false, false, PushEpi<BN, false>, kMxStages<BN>, true>(&tmA, &tmB, K, order, epi, status,
+                                                                                 &mx);
+  if (threadIdx.x >= 64 && threadIdx.x < 192) epi.finish();
   signal_tiles(p, order);
   if (ph && threadIdx.x == 0) ph[1] = globaltimer();
   if (p.variant & 2) {
@@ -666,16 +960,16 @@ static int launch_producer(void (*kern)(KArgs...), int smem, int grid, const Par
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
   tdb_host::launched(1);
   if (e != cudaSuccess) return tdb_host::fail(int(e), "%s: producer launch failed", what);
-  return coop ? 0 : launch_consumer(p, stream);
+  return (coop || p.policy == kPolicyEpilogue) ? 0 : launch_consumer(p, stream);
 }
 
-template <int BN, bool B_MN>
+template <int BN, bool B_MN, bool QUANT>
 static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int K, const gemm::TileOrder& order, const Params& p,
                   int grid, cudaStream_t stream) {
   using Cfg = gemm::Config<BN, kStagesFor<BN>>;
-  constexpr int kSmem = Cfg::kSmemBytes + PushEpi<BN>::kSmemBytes;
+  constexpr int kSmem = Cfg::kSmemBytes + PushEpi<BN, QUANT>::kSmemBytes;
   static_assert(kSmem <= 227 * 1024, "fused GEMM-RS shared memory budget");
-  auto kern = gemm_rs_kernel<BN, B_MN>;
+  auto kern = gemm_rs_kernel<BN, B_MN, QUANT>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -693,7 +987,7 @@ static int launch_mx(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
                      int K, const gemm::TileOrder& order, const Params& p, const uint8_t* sfa, const uint8_t* sfb,
                      const uint8_t* mx_mask, int grid, cudaStream_t stream) {
   using Cfg = gemm::Config<BN, kMxStages<BN>, true>;
-  constexpr int kSmem = Cfg::kSmemBytes + PushEpi<BN>::kSmemBytes;
+  constexpr int kSmem = Cfg::kSmemBytes + PushEpi<BN, false>::kSmemBytes;
   static_assert(kSmem <= 227 * 1024, "fused FP8 GEMM-RS shared memory budget");
   static bool attr[64] = {false};
   int dev = 0;
@@ -746,6 +1040,8 @@ using namespace tdb;
 // Fused GEMM + reduce-scatter.  A [m, K] (K contiguous, row stride lda);
 // B = weight: [N, K] (b_mn = 0) or [K, N] (b_mn = 1), row stride ldb.
 // tile_table: [num_tiles] production order (m_tile * (N / bn) + n_tile).
+// quantized: nonzero when qmask selects any block for the TACO wire format
+// (otherwise the producer is built without the encoder).
 namespace tdb {
 namespace rs {
 // Default 0; see Params::variant.  Set with tdb_rs_set_variant (tuning).
@@ -765,7 +1061,7 @@ static int gemm_rs_impl(const void* A, int64_t lda, const void* B, int b_mn, int
                         const uint8_t* qmask, void* out, const void* bias, const void* residual, const int* consume,
                         int policy, unsigned long long* timeline, long long delay_cycles, int delay_mb, int delay_nb,
                         double wait_seconds, unsigned long long* phases, const uint32_t* call_state,
-                        const MxArgs* mx, void* stream) {
+                        const MxArgs* mx, int quantized, void* stream) {
   if (!A || !B || !out || !tile_table || !peers || !qmask || !consume || W < 2 || W > rs::kMaxWorld || rank < 0 ||
       rank >= W)
     return tdb_host::fail(int(cudaErrorInvalidValue), "gemm_rs: bad pointers or ranks");
@@ -779,6 +1075,16 @@ static int gemm_rs_impl(const void* A, int64_t lda, const void* B, int b_mn, int
     return tdb_host::fail(int(cudaErrorInvalidValue), "gemm_rs: receive slot too small");
   if (delay_cycles < 0 || delay_cycles > 100000000ll)
     return tdb_host::fail(int(cudaErrorInvalidValue), "gemm_rs: diagnostic delay out of range");
+  if (policy < 0 || policy > 2) return tdb_host::fail(int(cudaErrorInvalidValue), "gemm_rs: policy must be 0, 1 or 2");
+  if (policy == rs::kPolicyEpilogue && quantized)
+    return tdb_host::fail(int(cudaErrorInvalidValue), "gemm_rs: the epilogue-reduction policy sends BF16 only");
+  if (policy == rs::kPolicyEpilogue) {
+    const uint64_t fine = 2ull * per * (chunk_rows / rs::BM) * (N / bn) * 4 * W * 4;
+    if (!call_state || W > rs::kMaxWorldEpi || fine > rs::kFineFlagsBytes || flags_off + rs::kFineFlagsOff + fine > recv_off)
+      return tdb_host::fail(int(cudaErrorInvalidValue),
+                            "gemm_rs: the epilogue-reduction policy needs a device call state, W <= 8 and %llu flag "
+                            "bytes", (unsigned long long)fine);
+  }
   CUtensorMap ta, tb;
   int rc = rs::make_operand_map(&ta, A, false, m, K, lda, rs::BM);
   if (rc) return rc;
@@ -816,7 +1122,7 @@ static int gemm_rs_impl(const void* A, int64_t lda, const void* B, int b_mn, int
   p.wait_ns = uint64_t(wait_seconds * 1e9);
   p.phases = phases;
   p.call_state = call_state;
-  p.variant = g_variant;
+  p.variant = policy == kPolicyEpilogue ? 0 : g_variant;
   const int sms = tdb_host::sm_count();
   const int grid = order.num_tiles < sms ? order.num_tiles : sms;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -834,9 +1140,16 @@ static int gemm_rs_impl(const void* A, int64_t lda, const void* B, int b_mn, int
     return bn == 256 ? rs::launch_mx<256>(ta, tb, ta8, tb8, K, order, p, sa, sb, mx->mask, grid, s)
                      : rs::launch_mx<128>(ta, tb, ta8, tb8, K, order, p, sa, sb, mx->mask, grid, s);
   }
-  if (bn == 256) return b_mn ? rs::launch<256, true>(ta, tb, K, order, p, grid, s)
-                             : rs::launch<256, false>(ta, tb, K, order, p, grid, s);
-  return b_mn ? rs::launch<128, true>(ta, tb, K, order, p, grid, s) : rs::launch<128, false>(ta, tb, K, order, p, grid, s);
+  if (quantized) {
+    if (bn == 256) return b_mn ? rs::launch<256, true, true>(ta, tb, K, order, p, grid, s)
+                               : rs::launch<256, false, true>(ta, tb, K, order, p, grid, s);
+    return b_mn ? rs::launch<128, true, true>(ta, tb, K, order, p, grid, s)
+                : rs::launch<128, false, true>(ta, tb, K, order, p, grid, s);
+  }
+  if (bn == 256) return b_mn ? rs::launch<256, true, false>(ta, tb, K, order, p, grid, s)
+                             : rs::launch<256, false, false>(ta, tb, K, order, p, grid, s);
+  return b_mn ? rs::launch<128, true, false>(ta, tb, K, order, p, grid, s)
+              : rs::launch<128, false, false>(ta, tb, K, order, p, grid, s);
 }
 }  // namespace rs
 }  // namespace tdb
@@ -846,11 +1159,12 @@ TDB_API int tdb_gemm_rs(const void* A, int64_t lda, const void* B, int b_mn, int
                         uint64_t recv_off, uint64_t slot_bytes, uint64_t flags_off, int set, unsigned int expected,
                         const uint8_t* qmask, void* out, const void* bias, const void* residual, const int* consume,
                         int policy, unsigned long long* timeline, long long delay_cycles, int delay_mb, int delay_nb,
-                        double wait_seconds, unsigned long long* phases, const uint32_t* call_state,
+                        double wait_seconds, unsigned long long* phases, const uint32_t* call_state, int quantized,
                         void* stream) {
   return rs::gemm_rs_impl(A, lda, B, b_mn, ldb, m, N, K, bn, tile_table, peers, W, rank, chunk_rows, recv_off,
                           slot_bytes, flags_off, set, expected, qmask, out, bias, residual, consume, policy, timeline,
-                          delay_cycles, delay_mb, delay_nb, wait_seconds, phases, call_state, nullptr, stream);
+                          delay_cycles, delay_mb, delay_nb, wait_seconds, phases, call_state, nullptr, quantized != 0,
+                          stream);
 }
 
 // tdb_gemm_rs whose tiles in the m blocks flagged by mx_mask run as
@@ -867,15 +1181,16 @@ TDB_API int tdb_gemm_rs_mx(const void* A, int64_t lda, const void* B, int b_mn, 
   const rs::MxArgs mx{a8, sfa, b8, sfb, mx_mask};
   return rs::gemm_rs_impl(A, lda, B, b_mn, ldb, m, N, K, bn, tile_table, peers, W, rank, chunk_rows, recv_off,
                           slot_bytes, flags_off, set, expected, qmask, out, bias, residual, consume, policy, timeline,
-                          delay_cycles, delay_mb, delay_nb, wait_seconds, phases, call_state, &mx, stream);
+                          delay_cycles, delay_mb, delay_nb, wait_seconds, phases, call_state, &mx, 0, stream);
 }
 
 // Select the fused GEMM-RS signalling / consumer variant of the following
-// calls (bit 0 per-tile signals, bit 1 consumer inside the producer kernel);
+// calls (bit 0 per-tile signals, bit 1 consumer inside the producer kernel,
+// bit 2 bulk TMA pushes with per-tile signals after completion);
 // returns the previous value.  Every rank must use the same variant.
 TDB_API int tdb_rs_set_variant(int variant) {
   const int old = rs::g_variant;
-  if (variant >= 0 && variant <= 3) rs::g_variant = variant;
+  if (variant >= 0 && variant <= 7) rs::g_variant = variant;
   return old;
 }
 

@@ -68,7 +68,8 @@ int tdb_gemm_rs(const void* A, int64_t lda, const void* B, int b_mn, int64_t ldb
                 uint64_t slot_bytes, uint64_t flags_off, int set, unsigned int expected, const uint8_t* qmask,
                 void* out, const void* bias, const void* residual, const int* consume, int policy,
                 unsigned long long* timeline, long long delay_cycles, int delay_mb, int delay_nb,
-                double wait_seconds, unsigned long long* phases, const uint32_t* call_state, void* stream);
+                double wait_seconds, unsigned long long* phases, const uint32_t* call_state, int quantized,
+                void* stream);
 int tdb_gemm_rs_mx(const void* A, int64_t lda, const void* B, int b_mn, int64_t ldb, int m, int N, int K, int bn,
                    const int* tile_table, const uint64_t* peers, int W, int rank, int chunk_rows, uint64_t recv_off,
                    uint64_t slot_bytes, uint64_t flags_off, int set, unsigned int expected, const uint8_t* qmask,

@@ -345,6 +345,16 @@ def expected_schedule(model, world, arm, role_plan=None):
             for slot, (d, w) in enumerate(_production_pairs(arm, world, per, role_plan))]
 
 
+def expected_consumer_policy(arm, stage):
+    """Arrival arms consume per lane, ready block first; the other arms in
+    order -- except the BF16 flux arm's training windows, whose remote-first
+    operators reduce their own blocks in the producer's epilogue (same sum
+    order and rounding, no consumer kernel)."""
+    if arm in (ARRIVAL, SELECTIVE):
+        return "per_lane_ready"
+    return "epilogue" if arm == "flux" and stage == "train" else "ordered"
+
+
 def expected_operator_state(model, world, arm, rank, role, calls, stage, execution_plan=None,
                             selective_mode="wire"):
     """Every exactly-known field of a correct operator's ``state()`` for this
@@ -380,7 +390,7 @@ def expected_operator_state(model, world, arm, rank, role, calls, stage, executi
         selection_mask=mask, selected_remote_blocks_by_source=selected, remote_wire_bytes_by_source=wires,
         remote_wire_bytes_per_source=wires[rank], actual_remote_wire_bytes_per_rank=wires[rank],
         plan_sha256=digest(role_plan) if role_plan is not None else None, original_cuda_flux=False,
-        transport_lanes=2, consumer_policy="per_lane_ready" if arrival else "ordered",
+        transport_lanes=2, consumer_policy=expected_consumer_policy(arm, stage),
         validation_calls=2 if stage == "operator" else 1, diagnostic_delay_cycles=0,
         diagnostic_delay_in_normal_forward=False)
     if fp8:

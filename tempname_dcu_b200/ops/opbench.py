@@ -34,8 +34,15 @@ def main(argv=None):
     ap.add_argument("--arms", default="all")
     ap.add_argument("--remote-first", action="store_true", help="produce remote-bound blocks first (training order)")
     ap.add_argument("--tile-n", type=int, default=0, help="fused kernel tile width (128 or 256; 0 = automatic)")
-    ap.add_argument("--variant", type=int, default=None, choices=(0, 1, 2, 3),
-                    help="fused GEMM-RS variant (bit 0 per-tile signals, bit 1 in-kernel consumer)")
+    ap.add_argument("--variant", type=int, default=None, choices=tuple(range(8)),
+                    help="fused GEMM-RS variant (bit 0 per-tile signals, bit 1 in-kernel consumer, "
+                         "bit 2 bulk TMA pushes)")
+    ap.add_argument("--variants", default=None,
+                    help="comma-separated fused GEMM-RS variants to time one after another (e.g. 0,4)")
+    ap.add_argument("--no-rs", action="store_true", help="skip the fused GEMM-RS timings")
+    ap.add_argument("--consumers", default="auto",
+                    help="comma list of consumer forms to time for remote-first operators: auto (epilogue reduction "
+                         "where eligible), kernel (separate consumer kernel)")
     ap.add_argument("--ag", action="store_true",
                     help="also time the fused all-gather GEMMs (QKV, FC1 shapes) for both pull variants")
     ap.add_argument("--selective-mode", default="wire", choices=("wire", "fp8-mma"),
@@ -51,7 +58,7 @@ def main(argv=None):
     group = dist.group.WORLD
     from ..mapping import ARMS, wire_bytes
     from ..planning import make_role
-    from ..runtime import FluxB200, set_rs_variant, shutdown_context
+    from ..runtime import FluxB200, set_epilogue_reduction, set_rs_variant, shutdown_context
     if args.variant is not None:
         set_rs_variant(args.variant)
     from . import gemm as G
@@ -94,7 +101,13 @@ def main(argv=None):
         gemm_us = timed(lambda: G.linear(x, w, out=partial))
         flops = 2.0 * m * n * k
         compute_us = flops / (peak * 1e12) * 1e6
-        for arm in arms:
+        variants = [int(v) for v in args.variants.split(",")] if args.variants else [args.variant]
+        consumers = args.consumers.split(",")
+        for variant, arm, consumer in ((v, a, c) for v in variants for a in (() if args.no_rs else arms)
+                                       for c in consumers):
+            if variant is not None:
+                set_rs_variant(variant)
+            set_epilogue_reduction(consumer == "auto")
             plan = make_role(m, n, k, world, chunk) if arm in ARMS[3:] else None
             mode = args.selective_mode if arm == ARMS[4] else "wire"
             if mode == "fp8-mma":
@@ -110,7 +123,9 @@ def main(argv=None):
             quant = op.quantized and mode == "wire"
             link_us = wire_bytes(m, n, world, quant) / (NVLINK_GBS * 1e9) * 1e6
             roof = max(compute_us / (2.0 if mode == "fp8-mma" else 1.0), link_us)
-            rows.append(dict(role=role, arm=arm, selective_mode=mode, variant=args.variant, world=world, m=m, n=n, k=k, fused_us=round(us, 2),
+            rows.append(dict(role=role, arm=arm, selective_mode=mode, variant=variant, consumer=op.consumer_policy,
+                             world=world, m=m, n=n, k=k,
+                             fused_us=round(us, 2),
                              gemm_plus_nccl_rs_us=round(base_us, 2), gemm_only_us=round(gemm_us, 2),
                              speedup_vs_nccl=round(base_us / us, 3), roofline_us=round(roof, 2),
                              roofline_fraction=round(roof / us, 3), bound="link" if link_us > compute_us else "compute",
@@ -141,7 +156,7 @@ def main(argv=None):
             flops = 2.0 * m * n_out * h
             link = (world - 1) * ml * h * 2 / (NVLINK_GBS * 1e9) * 1e6
             roof = max(flops / (peak * 1e12) * 1e6, link)
-            for variant in (0, 1):
+            for variant in (0, 1, 2):
                 set_ag_variant(variant)
                 us = timed(lambda: agg(xl, w, mode=mode, bias=bias, out=out, full=full,
                                        **({"aux_out": pre} if mode == agg.BIAS_GELU else {})))

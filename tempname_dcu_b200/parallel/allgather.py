@@ -73,10 +73,11 @@ native.register("tdb_ag_set_variant", [ctypes.c_int])
 def set_ag_variant(variant):
     """Where the fused all-gather GEMM pulls the gathered rows on this process:
     0 = the epilogue warps before their first tile, 1 = four auxiliary warps
-    concurrently with the pipeline.  Results are bitwise the same; all ranks
-    must use the same variant.  Returns the previous one."""
-    if variant not in (0, 1):
-        raise ValueError("variant must be 0 or 1")
+    concurrently with the pipeline, 2 = the same auxiliary warps with sixteen
+    16-byte loads in flight per thread.  Results are bitwise the same; all
+    ranks must use the same variant.  Returns the previous one."""
+    if variant not in (0, 1, 2):
+        raise ValueError("variant must be 0, 1 or 2")
     return int(native.lib().tdb_ag_set_variant(int(variant)))
 
 

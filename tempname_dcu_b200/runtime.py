@@ -38,8 +38,8 @@ native.register("tdb_gemm_rs", [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p
                                 ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int, ctypes.c_uint, ctypes.c_void_p,
                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                 ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_double,
-                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p])
-native.register("tdb_gemm_rs_mx", list(native.SIGNATURES["tdb_gemm_rs"][:-1])
+                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p])
+native.register("tdb_gemm_rs_mx", list(native.SIGNATURES["tdb_gemm_rs"][:-2])
                 + [ctypes.c_void_p] * 5 + [ctypes.c_void_p])
 native.register("tdb_rs_advance", [ctypes.c_void_p, ctypes.c_uint, ctypes.c_void_p])
 native.register("tdb_rs_set_variant", [ctypes.c_int])
@@ -49,11 +49,28 @@ native.register("tdb_gemm_rs_signals_per_block", [ctypes.c_int, ctypes.c_int, ct
 def set_rs_variant(variant):
     """Signalling / consumer variant of the following fused GEMM-RS calls on
     this process (bit 0: per-tile signals; bit 1: consumer inside the
-    producer kernel).  Results are bitwise the same for every variant; all
-    ranks must use the same one.  Returns the previous variant."""
-    if variant not in (0, 1, 2, 3):
-        raise ValueError("variant must be 0..3")
+    producer kernel; bit 2: BF16 tiles pushed with TMA bulk stores and
+    signalled per tile once written).  Results are bitwise the same for
+    every variant; all ranks must use the same one.  Returns the previous
+    variant."""
+    if variant not in range(8):
+        raise ValueError("variant must be 0..7")
     return int(native.lib().tdb_rs_set_variant(int(variant)))
+
+
+# Default of FluxB200(epilogue_reduction=None) for eligible operators (see
+# FluxB200); a process-wide switch for A/B measurements.
+_EPILOGUE_REDUCTION = True
+FINE_FLAG_BYTES = 32768
+
+
+def set_epilogue_reduction(on):
+    """Whether eligible operators created from now on reduce their own blocks
+    in the producer's epilogue (True, the default) or in a separate consumer
+    kernel.  Results are bitwise the same.  Returns the previous setting."""
+    global _EPILOGUE_REDUCTION
+    old, _EPILOGUE_REDUCTION = _EPILOGUE_REDUCTION, bool(on)
+    return old
 
 
 _CONTEXTS = {}
@@ -160,7 +177,8 @@ class FluxB200:
     """Fused GEMM + reduce-scatter for one projection shape and arm."""
 
     def __init__(self, m, n, k, group, arm, codec=None, chunk_rows=128, plan=None, diagnostic_delay_cycles=0,
-                 b_mn=False, tile_n=None, remote_first=False, selective_mode="wire", wait_seconds=PEER_WAIT_SECONDS):
+                 b_mn=False, tile_n=None, remote_first=False, selective_mode="wire", wait_seconds=PEER_WAIT_SECONDS,
+                 epilogue_reduction=None):
         """``remote_first`` (first three arms only): produce the blocks bound for
         other ranks first and this rank's own blocks last, so the NVLink
         transfers overlap the local tiles; results are bitwise unchanged (the
@@ -176,7 +194,14 @@ class FluxB200:
 
         ``wait_seconds`` bounds every wait of the consumer for other ranks'
         blocks; on expiry the kernel records a peer-flag timeout in the status
-        word and returns (``check_status`` raises and poisons)."""
+        word and returns (``check_status`` raises and poisons).
+
+        ``epilogue_reduction`` (remote-first BF16 operators, up to 8 ranks):
+        no consumer kernel -- the producer's epilogue reduces this rank's own
+        tiles (produced last) once every peer's copy of the tile has arrived,
+        in the same rank order and rounding as the consumer kernel, so the
+        result is bitwise the same.  None chooses it whenever eligible (see
+        ``set_epilogue_reduction``)."""
         import torch
         if not 0 < wait_seconds <= 600:
             raise ValueError("wait_seconds must be in (0, 600]")
@@ -244,6 +269,16 @@ class FluxB200:
                 sfb=torch.empty(_mx.scale_bytes(n, k), dtype=torch.uint8, device=self.device),
                 seen=torch.full((), -1, dtype=torch.int32, device=self.device))
         self.per = m // self.world // chunk_rows
+        fine_bytes = 2 * self.per * (chunk_rows // 128) * (n // self.bn) * 4 * self.world * 4
+        eligible = (self.remote_first and not any(self.wire_mask) and self.mx is None and self.world <= 8
+                    and fine_bytes <= FINE_FLAG_BYTES)
+        if epilogue_reduction is None:
+            epilogue_reduction = eligible and _EPILOGUE_REDUCTION
+        elif epilogue_reduction and not eligible:
+            raise ValueError("epilogue reduction needs a remote-first BF16 operator of at most 8 ranks")
+        self.epilogue_reduction = bool(epilogue_reduction)
+        if self.epilogue_reduction:
+            self.consumer_policy = "epilogue"
         local_in_order = [item["within"] for item in self.order if item["destination"] == self.rank]
         self.consume = torch.tensor(local_in_order, dtype=torch.int32, device=self.device)
         self.signals = int(native.lib().tdb_gemm_rs_signals_per_block(chunk_rows, n, self.bn))
@@ -291,7 +326,10 @@ class FluxB200:
             rows = self.m // self.world
             if out is None:
                 out = torch.empty((rows, self.n), dtype=torch.bfloat16, device=self.device)
-            set_, expected = ctx.next_call(self.signals)
+            # epilogue-reduction calls signal per-tile epoch flags, not the
+            # per-block counters: their targets must not move
+            counted = 0 if self.epilogue_reduction else self.signals
+            set_, expected = ctx.next_call(counted)
             timeline = None
             delay = 0
             if self.profile_enabled:
@@ -304,18 +342,18 @@ class FluxB200:
             heap = ctx.heap
             lib = native.lib()
             stream = native.stream_ptr()
-            native.check(lib.tdb_rs_advance(ctx.call_state.data_ptr(), self.signals, stream), "rs advance")
+            native.check(lib.tdb_rs_advance(ctx.call_state.data_ptr(), counted, stream), "rs advance")
             args = (input_.data_ptr(), input_.stride(0), weight.data_ptr(), int(self.b_mn), weight.stride(0), self.m,
                     self.n, self.k, self.bn, self.tile_table.data_ptr(), heap.peers.data_ptr(), self.world, self.rank,
                     self.chunk_rows, ctx.recv_off, self.slot_bytes, ctx.flags_off, set_, expected,
                     self.qmask.data_ptr(), out.data_ptr(), 0 if bias is None else bias.data_ptr(),
                     0 if residual is None else residual.data_ptr(), self.consume.data_ptr(),
-                    1 if self.consumer_policy == "per_lane_ready" else 0,
+                    {"ordered": 0, "per_lane_ready": 1, "epilogue": 2}[self.consumer_policy],
                     0 if timeline is None else timeline.data_ptr(), delay, self._delay_tile[0], self._delay_tile[1],
                     self.wait_seconds, 0 if self.phase_buffer is None else self.phase_buffer.data_ptr(),
                     ctx.call_state.data_ptr())
             if self.mx is None:
-                native.check(lib.tdb_gemm_rs(*args, stream), "fused gemm_rs")
+                native.check(lib.tdb_gemm_rs(*args, int(any(self.wire_mask)), stream), "fused gemm_rs")
             else:
                 from .ops import mx as _mx
                 q = self.mx
@@ -375,6 +413,11 @@ class FluxB200:
         t = self.phase_buffer.cpu().double()
         prod = t[t[:, 0] > 0]
         cons = t[t[:, 2] > 0]
+        if cons.shape[0] == 0:  # epilogue reduction: no consumer kernel
+            produce = (prod[:, 1] - prod[:, 0]) / 1e3
+            return dict(ctas=int(prod.shape[0]), kernel_span_us=round((prod[:, 1].max() - prod[:, 0].min()).item() / 1e3, 2),
+                        produce_mean_us=round(produce.mean().item(), 2), produce_max_us=round(produce.max().item(), 2),
+                        consumer="epilogue")
         produce = (prod[:, 1] - prod[:, 0]) / 1e3
         end_of_produce = prod[:, 1].max()
         wait = (cons[:, 2] - end_of_produce).clamp_min(0) / 1e3

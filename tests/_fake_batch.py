@@ -133,6 +133,7 @@ def fake_rows(job, job_config, directory, library_sha256, world=2):
                              execution_plan, config.get("selective_mode", "wire")) for i in range(2 * model["layers"])]
             for st in states:
                 st["validation_calls"] = 1
+                st["consumer_policy"] = p.expected_consumer_policy(job["arm"], "train")
             row.update(timed_steps=steps, warmup_steps=warm, elapsed_seconds=0.5 + 0.01 * row["rank"],
                        losses=[9.0 - 0.1 * i - (0 if same else 0.001) for i in range(steps)],
                        grad_norms=[1.0 + 0.01 * i for i in range(steps)],

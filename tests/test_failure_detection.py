@@ -84,6 +84,7 @@ def test_operator_poisoning_refuses_reuse():
     op.context, op.failed = ctx, False
     op._check = lambda *a: None
     op.world, op.m, op.n, op.device, op.signals = 2, 256, 128, "cpu", 4
+    op.epilogue_reduction = False
     import torch
     with pytest.raises(RuntimeError, match="peer flag timeout"):
         op.forward(torch.zeros(1), torch.zeros(1), out=torch.zeros(1))

@@ -53,7 +53,10 @@ def _worker(rank, world, init_file, result_path):
                               (ARMS[4], plan_e)):
                 op = FluxB200(m, n, k, group, arm, chunk_rows=chunk, plan=plan)
                 op.validate_next_call = True
-                y = op.forward(x, w)
+                try:
+                    y = op.forward(x, w)
+                except RuntimeError as exc:
+                    raise RuntimeError(f"k={k} arm={arm} rank={rank}: {exc}") from exc
                 torch.cuda.synchronize()
                 native.raise_on_status()
                 sel = mask if arm == ARMS[4] else None
@@ -72,9 +75,28 @@ def _worker(rank, world, init_file, result_path):
                 c_d=bool(torch.equal(outputs[ARMS[2]], outputs[ARMS[3]])))
             rf = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, remote_first=True).forward(x, w)
             out[f"bitwise.k{k}"]["remote_first"] = bool(torch.equal(rf, outputs[ARMS[0]]))
+            # remote-first operators reduce in the producer's epilogue by default; the
+            # consumer-kernel form of the same order must agree bit for bit, over several
+            # calls (both receive sets), with bias + residual, and with a [K, N] weight
+            rk = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, remote_first=True, epilogue_reduction=False)
+            re_ = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, remote_first=True)
+            assert re_.consumer_policy == "epilogue" and rk.consumer_policy == "ordered"
+            bias_e = torch.randn(n, device="cuda").to(torch.bfloat16)
+            res_e = torch.randn(m // world, n, device="cuda").to(torch.bfloat16)
+            for call in range(3):
+                xe = (x * (1 + call)).to(torch.bfloat16)
+                a, b = re_.forward(xe, w, bias_e, res_e), rk.forward(xe, w, bias_e, res_e)
+                out[f"bitwise.k{k}"][f"epilogue_call{call}"] = bool(torch.equal(a, b))
+            wt = w.t().contiguous()
+            eb = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, b_mn=True, remote_first=True).forward(x, wt)
+            kb = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, b_mn=True, remote_first=True,
+                          epilogue_reduction=False).forward(x, wt)
+            out[f"bitwise.k{k}"]["epilogue_b_mn"] = bool(torch.equal(eb, kb))
+            torch.cuda.synchronize()
+            native.raise_on_status()
             # signalling / consumer variants reduce in the same order: bitwise equal
             from tempname_dcu_b200.runtime import set_rs_variant
-            for variant in (1, 2, 3):
+            for variant in (1, 2, 3, 4, 6):
                 set_rs_variant(variant)
                 for arm, plan in ((ARMS[0], None), (ARMS[1], None), (ARMS[4], plan_e)):
                     yv = FluxB200(m, n, k, group, arm, chunk_rows=chunk, plan=plan).forward(x, w)
@@ -147,7 +169,7 @@ def _worker(rank, world, init_file, result_path):
         errs, same = [], []
         def rel(a, b):
             return float((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30))
-        for N, variant in ((1536, 0), (1000, 0), (1536, 1), (1000, 1)):
+        for N, variant in ((1536, 0), (1000, 0), (1536, 1), (1000, 1), (1536, 2), (1000, 2)):
             set_ag_variant(variant)
             w = (torch.randn(N, K, device="cuda") / 32).to(torch.bfloat16)
             bias = torch.randn(N, device="cuda").to(torch.bfloat16)
@@ -181,7 +203,7 @@ def _worker(rank, world, init_file, result_path):
         tsame, terrs = [], []
         w = (torch.randn(1536, K, device="cuda") / 32).to(torch.bfloat16)
         for rep in range(4):
-            set_ag_variant(rep % 2)
+            set_ag_variant(rep % 3)
             xl = torch.randn(rows, K, device="cuda").to(torch.bfloat16)
             ref_full = torch.empty(rows * world, K, dtype=torch.bfloat16, device="cuda")
             dist.all_gather_into_tensor(ref_full, xl, group=group)
