@@ -51,6 +51,10 @@ def parse():
     p.add_argument("--no-graph", action="store_true", help="issue every kernel from the host (no CUDA graph)")
     p.add_argument("--taco-allgather", action="store_true",
                    help="TACO-compress the fused all-gathers too (peers' rows cross NVLink as H128/E4M3 packets)")
+    p.add_argument("--codec-calibration-steps", type=int, default=0,
+                   help="TACO arms: observe the codec error on this many first (warm-up) steps, then freeze the "
+                        "block masks within --error-budget (must not exceed --warmup)")
+    p.add_argument("--error-budget", type=float, default=0.01)
     p.add_argument("--small", action="store_true", help="2-layer smoke configuration (not a headline number)")
     return p.parse_args()
 
@@ -185,8 +189,11 @@ def main():
         if world > 1:
             from tempname_dcu_b200.runtime import operator_factory_for
             factory = operator_factory_for(args.arm)
+        if args.codec_calibration_steps > args.warmup:
+            raise SystemExit("--codec-calibration-steps must run inside the warm-up steps")
         trainer = Trainer(config, args.arm, group, operator_factory=factory, cuda_graph=not args.no_graph,
-                          graph_warmup=min(2, max(0, args.warmup - 1)), taco_allgather=args.taco_allgather)
+                          graph_warmup=min(2, max(0, args.warmup - 1)), taco_allgather=args.taco_allgather,
+                          codec_calibration_steps=args.codec_calibration_steps, error_budget=args.error_budget)
     from tempname_dcu_b200.train import synthetic_batches
     c = trainer.config
     (tokens_h, labels_h), = synthetic_batches(c, 1, seed=4321)
@@ -255,6 +262,8 @@ def main():
                         layers=c["layers"], hidden=c["hidden"], ffn=c["ffn"], heads=c["heads"],
                         tokens_per_step=tokens_per_step, arm=args.arm if args.impl == "ours" else None,
                         taco_allgather=bool(args.taco_allgather) if args.impl == "ours" else None,
+                        codec_calibration=(dict(steps=args.codec_calibration_steps, error_budget=args.error_budget)
+                                           if args.codec_calibration_steps else None),
                         cuda_graph=bool(args.impl == "ours" and not args.no_graph),
                         l2="inputs larger than L2 (13 GB of bf16 weights streamed per step); no flush",
                         model_tflops_per_gpu=round(flops / (ms_per_step / 1000.0) / world / 1e12, 1),

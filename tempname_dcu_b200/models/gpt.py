@@ -86,6 +86,8 @@ class GPT:
         self.params = FlatParams(gpt_param_specs(c, self.world), self.device, rank=self.rank, seed=seed,
                                  materialize=materialize)
         self.forward_calls = 0
+        # warm-up codec calibration (warmup_calibration.CodecObserver) while attached
+        self.codec_observer = None
         self.trace_ranges = False  # per-layer profiler / NVTX ranges (utils.trace --ranges)
         self.operators = []
         factory = operator_factory
@@ -167,6 +169,8 @@ class GPT:
             ln1f = self.tp.gather(ln1)
             qkv = G.linear(ln1f, self.P(p + "qkv_weight"), self.P(p + "qkv_bias"))
         attn, lse = K.attention_fwd(qkv, c["micro_batch"], c["sequence"], self.heads_local)
+        if self.codec_observer is not None:
+            self.codec_observer.observe("attn", attn, self.P(p + "attn_weight"))
         x1 = self.operators[2 * i].forward(attn, self.P(p + "attn_weight"), self.P(p + "attn_bias"), x)
         ln2, mean2, rstd2 = K.layernorm_fwd(x1, self.P(p + "ln2_weight"), self.P(p + "ln2_bias"), eps)
         if self.agg is not None:
@@ -175,6 +179,8 @@ class GPT:
         else:
             ln2f = self.tp.gather(ln2)
             h1, z = G.linear_gelu(ln2f, self.P(p + "fc1_weight"), self.P(p + "fc1_bias"))
+        if self.codec_observer is not None:
+            self.codec_observer.observe("mlp", h1, self.P(p + "fc2_weight"))
         x2 = self.operators[2 * i + 1].forward(h1, self.P(p + "fc2_weight"), self.P(p + "fc2_bias"), x1)
         return x2, (x, mean1, rstd1, ln1f, qkv, attn, lse, x1, mean2, rstd2, ln2f, z, h1)
 

@@ -386,6 +386,28 @@ class FluxB200:
 
     __call__ = forward
 
+    def freeze_selection(self, mask):
+        """Adopt a frozen per-physical-block wire format (TACO arms): True
+        blocks cross NVLink as TACO packets, False blocks as BF16 -- e.g. the
+        mask chosen on the first training steps (warmup_calibration).  Call
+        between steps, before a CUDA graph of the step is captured."""
+        import torch
+        if self.arm == "flux" or self.mx is not None:
+            raise ValueError("only the TACO wire-format arms take a selection mask")
+        mask = list(mask)
+        if len(mask) != len(self.selection_mask) or any(type(v) is not bool for v in mask):
+            raise ValueError("the mask needs one bool per physical output block")
+        self.selection_mask = list(mask)
+        self.wire_mask = list(mask)
+        self.qmask.copy_(torch.tensor([int(v) for v in mask], dtype=torch.uint8))
+        self.quantized = any(mask)
+        self.selection = selection_statistics(self.m, self.n, self.world, self.chunk_rows, self.selection_mask)
+        if self.plan is not None:
+            from .planning import role_digest
+            self.plan["selective_mask"] = list(mask)
+            self.plan_sha256 = role_digest(self.plan)
+        self.frozen_selection = True
+
     def check_status(self):
         """Wait for this device's queued work, then read the library status
         word; if a kernel recorded a bounded-wait expiry (a peer that never
@@ -496,6 +518,8 @@ class FluxB200:
     def state(self):
         quantization = ("selective_remote_h128_e4m3" if self.arm.endswith("_selective") else
                         "all_remote_h128_e4m3" if self.arm != "flux" else "none")
+        if getattr(self, "frozen_selection", False):
+            quantization = "warmup_calibrated_remote_h128_e4m3"
         extra = {}
         if self.mx is not None:
             quantization = "selective_mma_e4m3_ue8m0_k32"

@@ -62,7 +62,13 @@ class Trainer:
     into fixed device buffers before each replay."""
 
     def __init__(self, config, arm="flux", group=None, *, device="cuda", seed=1234, operator_factory=None,
-                 execution_plan=None, cuda_graph=False, graph_warmup=2, taco_allgather=False):
+                 execution_plan=None, cuda_graph=False, graph_warmup=2, taco_allgather=False,
+                 codec_calibration_steps=0, error_budget=0.01):
+        """``codec_calibration_steps`` > 0 (TACO arms on two or more ranks):
+        observe the codec error of every forward reduce-scatter input during
+        that many first steps, then freeze one block mask per role within
+        ``error_budget`` (warmup_calibration) and keep it; ``codec_plan``
+        holds the frozen bundle afterwards.  Those steps run eagerly."""
         import torch
         self.model = GPT(config, arm, group, device=device, seed=seed, operator_factory=operator_factory,
                          execution_plan=execution_plan, taco_allgather=taco_allgather)
@@ -82,6 +88,16 @@ class Trainer:
         self._eager_steps = 0
         self.graph_kernels = 0   # library kernels recorded in the captured step
         self.graph_replays = 0
+        self.codec_calibration_steps = int(codec_calibration_steps)
+        self.error_budget = float(error_budget)
+        self.codec_plan = None
+        self._steps_done = 0
+        if self.codec_calibration_steps:
+            if self.model.world < 2 or arm == "flux" or operator_factory is None:
+                raise ValueError("codec calibration needs a TACO arm's fused operators on two or more ranks")
+            if not 0 < self.error_budget <= 1:
+                raise ValueError("error_budget must be in (0, 1]")
+            self.graph_warmup = max(self.graph_warmup, self.codec_calibration_steps)
 
     def save_checkpoint(self, directory, plan_sha256=None):
         """Sharded checkpoint of masters + Adam state (utils/checkpoint.py);
@@ -96,10 +112,21 @@ class Trainer:
 
     def _body(self, tokens, labels):
         c = self.config
+        calibrating = self._steps_done < self.codec_calibration_steps
+        if calibrating and self.model.codec_observer is None:
+            from .warmup_calibration import CodecObserver
+            self.model.codec_observer = CodecObserver(self.model)
         self.loss.zero_()
         for micro in range(c["accumulation_steps"]):
             self.model.forward_backward(tokens[micro], labels[micro], self.loss)
-        return self.optimizer.step(self.loss)
+        norm = self.optimizer.step(self.loss)
+        self._steps_done += 1
+        if calibrating and self._steps_done == self.codec_calibration_steps:
+            from . import warmup_calibration
+            self.codec_plan = self.model.codec_observer.freeze(self.error_budget)
+            self.model.codec_observer = None
+            warmup_calibration.apply(self.model, self.codec_plan)
+        return norm
 
     def step(self, tokens, labels):
         """One optimizer step over ``accumulation_steps`` micro-batches.
