@@ -95,6 +95,16 @@ int tdb_ag_gemm(const void* x, long long ldx, void* full, long long rows, int K,
                 const unsigned long long* peers, int W, int rank, unsigned long long heap_off, unsigned int* state,
                 unsigned int* ready, double wait_seconds, int taco, void* stream);
 
+/* ---- sparse vocabulary-parallel embedding exchange (embed_exchange.cu) --- */
+long long tdb_embx_region_bytes(long long ml, long long H, int W);
+int tdb_embx_forward(const int64_t* tokens, const void* table, long long start, long long local_vocab, const void* pos,
+                     long long pos_offset, int seq, void* x, const unsigned long long* peers, int W, int rank,
+                     long long ml, long long H, unsigned long long heap_off, unsigned int* state, double wait_seconds,
+                     void* stream);
+int tdb_embx_backward(const int64_t* tokens, const void* dy, long long ld, long long start, long long local_vocab,
+                      void* out, const unsigned long long* peers, int W, int rank, long long ml, long long H,
+                      unsigned long long heap_off, unsigned int* state, double wait_seconds, void* stream);
+
 /* ---- attention (attn_tc.cu: tcgen05; attention.cu: other lengths) -------- */
 int tdb_attn_fwd(const void* qkv, int64_t ld, void* out, int64_t ld_out, float* lse, int mb, int seq, int Hl,
                  float scale, void* stream);

@@ -15,7 +15,10 @@ backward mirrors it: data gradients through the transposed GEMMs (the
 collective order reversed), weight gradients accumulated directly into the
 fp32 gradient buffer by the GEMM epilogue, bias gradients by deterministic
 column sums, GELU backward fused into the FC2 data-gradient epilogue.
-The LM head is the tied vocabulary-sharded embedding; the vocab-parallel
+With fused operators on 2..8 ranks the embedding's reduce-scatter and its
+backward gather become a sparse exchange (parallel/embedding_exchange.py):
+each token row moves only from its vocabulary shard's owner, bit for bit the
+same result.  The LM head is the tied vocabulary-sharded embedding; the vocab-parallel
 cross-entropy writes its gradient over the logits in place, so the backward
 starts inside the loss.
 
@@ -105,6 +108,11 @@ class GPT:
         # whenever the forward projections do.
         self._bwd_rs = {}
         self.agg = None
+        self.embx = None
+        if factory is not None and 1 < self.world <= 8:
+            # sparse embedding exchange instead of the dense reduce-scatter / gather
+            from ..parallel.embedding_exchange import EmbeddingExchange
+            self.embx = EmbeddingExchange(self.tp, self.ml, self.h, self.vocab_local)
         if factory is not None and self.world > 1:
             # sequence-parallel all-gathers over NVLink (same rows/cols everywhere)
             self.tp.enable_symmetric_gather(self.ml, self.h)
@@ -148,6 +156,9 @@ class GPT:
         import torch
         from ..ops import kernels as K
         c = self.config
+        if self.embx is not None:
+            return self.embx.forward(tokens, self.P("embedding"), self.vocab_start, self.P("position"),
+                                     self.rank * self.ml, c["sequence"])
         out = torch.empty((self.m, self.h), dtype=torch.bfloat16, device=self.device)
         if self.world == 1:
             K.embedding_fwd(tokens, self.P("embedding"), 0, out, self.P("position"), 0, c["sequence"])
@@ -234,7 +245,11 @@ class GPT:
             saved[i] = None
         # ---- embedding / positions
         K.position_bwd(dx, self.rank * self.ml if self.world > 1 else 0, c["sequence"], self.Gr("position"))
-        dfull = self.tp.gather(dx)
+        if self.embx is not None:  # only the rows of tokens in this rank's shard, from their holders
+            dfull = self.embx.backward(tokens, dx, self.vocab_start,
+                                       self._buf("emb_dfull", self.m * self.h, torch.bfloat16).view(self.m, self.h))
+        else:
+            dfull = self.tp.gather(dx)
         sorted_tokens, order = K.sort_tokens(tokens, self._buf("sorted_tokens", self.m, torch.int64),
                                              self._buf("token_order", self.m, torch.int64))
         K.embedding_bwd(sorted_tokens, order, dfull, self.vocab_start, self.vocab_local, self.Gr("embedding"))
