@@ -27,7 +27,6 @@
 // TMEM columns: S0 [0,128), S1 [128,256), O [256,384).
 // All waits are bounded (common.cuh); there is no TMA multicast.
 #include "common.cuh"
-#include "exp2_fma.cuh"
 #include "tensor_map.h"
 
 namespace tdb {
@@ -128,9 +127,8 @@ __device__ __forceinline__ float exp_row64(const uint32_t (&sr)[2][32], int lim,
 #pragma unroll
   for (int e = 0; e < 32; ++e) {
     const int c0 = 2 * e;
-    // even columns on the MUFU unit, odd columns on the FMA pipe
     float p0 = ex2(fmaf(__uint_as_float(sr[c0 >> 5][c0 & 31]), sl2, neg));
-    float p1 = exp2_fma(fmaf(__uint_as_float(sr[(c0 + 1) >> 5][(c0 + 1) & 31]), sl2, neg));
+    float p1 = ex2(fmaf(__uint_as_float(sr[(c0 + 1) >> 5][(c0 + 1) & 31]), sl2, neg));
     if (MASK) {
       p0 = c0 <= lim ? p0 : 0.f;
       p1 = c0 + 1 <= lim ? p1 : 0.f;
