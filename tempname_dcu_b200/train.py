@@ -192,6 +192,11 @@ def train_window(config, arm, group, warmup_steps, timed_steps, *, seed=1234, to
     input_hash = tensor_digest([(f"tokens.{i}", tokens[i]) for i in range(len(tokens))] +
                                [(f"labels.{i}", labels[i]) for i in range(len(labels))])
     tokens, labels = tokens.to(trainer.device), labels.to(trainer.device)
+    # the first warm-up call of every fused operator validates its buffers
+    # (untimed, rank-coordinated; python/flux_dcu/model.py:366-367)
+    for op in model.operators:
+        if hasattr(op, "validate_next_call"):
+            op.validate_next_call = True
     for _ in range(warmup_steps):
         trainer.step(tokens, labels)
     torch.cuda.synchronize()

@@ -414,7 +414,7 @@ def main(argv=None):
         group = dist.group.WORLD if world > 1 else None
         if args.stage in ("operator", "train"):
             from .planning import validate_role_plan
-            from .protocol import digest
+            from .experiment.protocol import digest
             bundle = config.get("execution_plan")
             if not bundle or digest(bundle) != config.get("execution_plan_sha256"):
                 raise ValueError("missing or changed frozen calibration plan")
