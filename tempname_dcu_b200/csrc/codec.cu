@@ -87,14 +87,18 @@ __global__ void reduce_kernel(const uint16_t* __restrict__ local, const uint16_t
   }
 }
 
-// Test probe: hardware E4M3 conversion of an fp32 array (one code per value).
+// Test probe: hardware E4M3 conversion of an fp32 array (one code per value);
+// decoded[i] is code i's value (i < 256) through the decoder's conversion.
 __global__ void e4m3_probe_kernel(const float* __restrict__ in, uint8_t* __restrict__ codes,
                                   float* __restrict__ decoded, int64_t n) {
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const uint16_t pair = e4m3x2(in[i], 0.0f);
   codes[i] = uint8_t(pair & 0xff);
-  decoded[i] = e4m3_to_float(i < 256 ? uint32_t(i) : uint32_t(pair & 0xff));
+  // the decode path the codec kernels use (hardware e4m3 -> f16 conversion)
+  float four[4];
+  e4m3x4_to_float(i < 256 ? uint32_t(i) : uint32_t(pair & 0xff), four);
+  decoded[i] = four[0];
 }
 
 

@@ -14,6 +14,7 @@
 // 4L..4L+3.  Butterfly strides 1 and 2 stay inside a thread; strides 4..64
 // are lane-xor shuffles with masks 1..16.
 #pragma once
+#include <cuda_fp16.h>
 #include <string.h>
 
 #include "common.cuh"
@@ -58,6 +59,21 @@ __host__ __device__ __forceinline__ float e4m3_to_float(uint32_t code) {
     v = bits_as_float((e << 23) | ((mag & 7u) << 20));
   }
   return (code & 0x80u) ? -v : v;
+}
+
+// Four E4M3FN codes packed in a word (code j in byte j) -> fp32, with the
+// hardware conversion (two codes per instruction into f16, exact: every E4M3
+// value, NaN included, is representable in f16).  Same values as
+// e4m3_to_float, which stays the host-testable definition.
+__device__ __forceinline__ void e4m3x4_to_float(uint32_t word, float (&out)[4]) {
+  uint32_t lo, hi;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(lo) : "h"(uint16_t(word & 0xffffu)));
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(hi) : "h"(uint16_t(word >> 16)));
+  const __half2 a = *reinterpret_cast<const __half2*>(&lo), b = *reinterpret_cast<const __half2*>(&hi);
+  out[0] = __low2float(a);
+  out[1] = __high2float(a);
+  out[2] = __low2float(b);
+  out[3] = __high2float(b);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -143,8 +159,9 @@ __device__ __forceinline__ uint32_t encode_group_warp(const float (&in)[4], int 
 // in byte 0) -> 4 fp32 values (already divided by the adaptive scale).
 __device__ __forceinline__ void decode_group_warp(uint32_t payload, float quant, float adaptive, int lane,
                                                   float (&out)[4]) {
+  e4m3x4_to_float(payload, out);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) out[j] = e4m3_to_float((payload >> (8 * j)) & 0xffu) * quant;
+  for (int j = 0; j < 4; ++j) out[j] *= quant;
   fwht128_warp(out, lane);
   const float den = fmaxf(adaptive, 1e-12f);
 #pragma unroll

@@ -109,6 +109,8 @@ __device__ __forceinline__ uint32_t* flag_ptr(const Params& p, int rank_of_heap,
 // store per warp and 128-column half, instead of 16-byte st.global from the
 // warp's lanes; every warp then signals each tile once its stores are
 // complete (deferred by one tile, so the wait overlaps the next tile).
+// Operators with TACO blocks ignore the bit (their producer is built
+// without the bulk path).
 constexpr int kVariantBulk = 4;
 
 __device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
@@ -396,7 +398,8 @@ struct PushEpi {
     quarter = (threadIdx.x >> 5) & 3;
     nbase = nb * BN;
     const bool epi_policy = p->policy == kPolicyEpilogue;
-    bulk = epi_policy || (p->variant & kVariantBulk) != 0;
+    // bulk pushes move BF16 slabs; operators with TACO blocks keep the lane stores
+    bulk = !QUANT && (epi_policy || (p->variant & kVariantBulk) != 0);
     tile_in_block = (row0 / BM) * (p->N / BN) + nb;
     local_reduce = epi_policy && dest == p->rank;
     if (local_reduce) {
