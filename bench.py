@@ -56,7 +56,35 @@ def parse():
                         "block masks within --error-budget (must not exceed --warmup)")
     p.add_argument("--error-budget", type=float, default=0.01)
     p.add_argument("--small", action="store_true", help="2-layer smoke configuration (not a headline number)")
+    # transport choices (defaults: the framework's); all ranks must agree
+    p.add_argument("--ag-variant", type=int, choices=(0, 1, 2, 3), default=None,
+                   help="fused all-gather GEMM row movement: 0-2 pull, 3 push")
+    p.add_argument("--rs-variant", type=int, choices=tuple(range(8)), default=None,
+                   help="fused GEMM-RS variant bits: 1 per-tile signals, 2 in-kernel consumer, 4 bulk pushes")
+    p.add_argument("--epilogue-reduction", choices=("on", "off"), default=None,
+                   help="remote-first BF16 operators reduce their own blocks in the producer epilogue")
+    p.add_argument("--embedding-exchange", choices=("on", "off"), default=None,
+                   help="sparse vocabulary-parallel embedding exchange instead of the dense collectives")
     return p.parse_args()
+
+
+def apply_transport(args):
+    """Apply the transport options and return the settings in effect."""
+    from tempname_dcu_b200.ops import native
+    from tempname_dcu_b200.parallel import allgather, embedding_exchange
+    from tempname_dcu_b200 import runtime
+    if args.ag_variant is not None:
+        allgather.set_ag_variant(args.ag_variant)
+    if args.rs_variant is not None:
+        runtime.set_rs_variant(args.rs_variant)
+    if args.epilogue_reduction is not None:
+        runtime.set_epilogue_reduction(args.epilogue_reduction == "on")
+    if args.embedding_exchange is not None:
+        embedding_exchange.set_embedding_exchange(args.embedding_exchange == "on")
+    lib = native.lib()
+    return dict(ag_variant=int(lib.tdb_ag_set_variant(-1)), rs_variant=int(lib.tdb_rs_set_variant(-1)),
+                epilogue_reduction=runtime.epilogue_reduction_default(),
+                embedding_exchange=embedding_exchange.enabled())
 
 
 class ClockSampler:
@@ -180,6 +208,7 @@ def main():
     from tempname_dcu_b200.models.config import BENCH_CONFIG, SMALL_CONFIG, train_flops_per_step
     from tempname_dcu_b200.ops import native
     config = dict(SMALL_CONFIG if args.small else BENCH_CONFIG)
+    transport = apply_transport(args) if args.impl == "ours" else None
     if args.impl == "baseline":
         from tempname_dcu_b200.models.torch_baseline import BaselineTrainer as TrainerCls
         trainer = TrainerCls(config, group)
@@ -265,6 +294,7 @@ def main():
                         codec_calibration=(dict(steps=args.codec_calibration_steps, error_budget=args.error_budget)
                                            if args.codec_calibration_steps else None),
                         cuda_graph=bool(args.impl == "ours" and not args.no_graph),
+                        transport=transport if world > 1 else None,
                         l2="inputs larger than L2 (13 GB of bf16 weights streamed per step); no flush",
                         model_tflops_per_gpu=round(flops / (ms_per_step / 1000.0) / world / 1e12, 1),
                         baseline_ref=dict(

@@ -20,7 +20,15 @@
 // The copy waits on other CTAs of the same grid, so the kernel is launched
 // cooperatively (all CTAs co-resident or no launch).  Variant 1
 // (tdb_ag_set_variant) moves the pull onto four extra warps so that the
-// epilogue warps drain finished tiles while rows are still arriving.  With
+// epilogue warps drain finished tiles while rows are still arriving; variant
+// 2 keeps sixteen loads in flight per pulling thread.  Variant 3 turns the
+// pull into a push: the four extra warps of every CTA write this rank's rows
+// with plain 16-byte stores straight into every peer's receive buffer (posted
+// writes need no round trip per load, so a few bytes in flight per thread
+// reach the link's bandwidth), stamp a per-slice flag there, and copy the
+// slices that peers pushed into this rank's receive buffer on to the
+// gathered output (a local copy, then the same per-block counters gate the
+// TMA loads).  No send slot is staged.  With
 // taco = 1 the send slots hold TACO packets (allgather.cu stages them) and
 // the pull decodes peers' rows; a rank's own rows are copied exact.  Peer readiness uses the
 // all-gather protocol of allgather.cu (epoch published per source; slot
@@ -29,6 +37,7 @@
 #include <cmath>
 #include <type_traits>
 
+#include "call_state.cuh"
 #include "codec.cuh"
 #include "gemm.cuh"
 #include "gemm2.cuh"
@@ -59,7 +68,27 @@ struct Pull {
   int taco;
   const uint16_t* x;
   int64_t ldx;
+  uint64_t push_off;      // push area inside the region (variant 3): slice flags, then 2 receive buffers
 };
+
+constexpr int kSlices = 16;  // items per 128-row block (8 rows each)
+
+// Push area (variant 3), at heap_off + push_off of every rank: epoch stamps
+// flags[source][block][slice] (uint32, rounded up to 256 bytes), then two
+// receive buffers [W * rows, cols] bf16 (by call parity).
+__host__ __device__ __forceinline__ uint64_t push_flags_bytes(int64_t rows, int W) {
+  return (uint64_t(W) * uint64_t(rows / 128) * kSlices * 4 + 255) / 256 * 256;
+}
+__host__ __device__ __forceinline__ uint64_t push_area_bytes(int64_t rows, int64_t cols, int W) {
+  return push_flags_bytes(rows, W) + 2ull * uint64_t(W) * uint64_t(rows) * uint64_t(cols) * 2ull;
+}
+__device__ __forceinline__ uint8_t* push_area(const Pull& a, int r) {
+  return reinterpret_cast<uint8_t*>(a.peers[r] + a.heap_off + a.push_off);
+}
+__device__ __forceinline__ uint16_t* recv_rows(const Pull& a, int r, uint32_t parity, int s, int64_t r0) {
+  return reinterpret_cast<uint16_t*>(push_area(a, r) + push_flags_bytes(a.rows, a.W) +
+                                     (uint64_t(parity) * a.W * a.rows + uint64_t(s) * a.rows + r0) * a.cols * 2);
+}
 
 __device__ __forceinline__ const uint16_t* src_slot(const Pull& a, int r, uint32_t parity) {
   return reinterpret_cast<const uint16_t*>(a.peers[r] + a.heap_off + kFlagsBytes +
@@ -178,6 +207,108 @@ __device__ void pull_rows(const Pull& a, volatile int& s_ok, int* status, int et
   }
 }
 
+// Variant 3, executed by the four auxiliary warps of every CTA.  Items, in
+// index order (CTA c takes c, c + grid, ...; a CTA's pushes precede its
+// collects, and pushes never wait, so every collect is eventually served):
+//   own:     copy a slice of this rank's rows from x into the gathered output;
+//   push:    write a slice of this rank's rows into peer d's receive buffer
+//            (d = rank-1, rank-2, ...: the peer that consumes this rank's rows
+//            soonest first), then stamp flags[rank][block][slice] = epoch there;
+//   collect: wait (bounded) for source s's stamp (s = rank+1, rank+2, ...: the
+//            GEMM's order), copy the slice from the receive buffer (local
+//            memory, L2-only loads) into the gathered output.
+// After own and collect items the block's counter is release-added (gpu
+// scope) for the TMA producer's gate.  Receive-buffer reuse: a peer writes
+// buffer[p] again two calls later, after its previous kernel has consumed this
+// rank's pushes of the call in between, which this rank issues only after its
+// own earlier kernel -- the one that read buffer[p] -- has ended.
+template <int U>
+__device__ __forceinline__ void copy_item(uint4* dst, const uint16_t* src, int64_t lds, int64_t vec_per_row, int64_t n,
+                                          int et, bool l2_only) {
+  int64_t i = et;
+  for (; i + (U - 1) * 128 < n; i += U * 128) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t k = i + u * 128, rr = k / vec_per_row, c = k % vec_per_row;
+      const uint4* sp = reinterpret_cast<const uint4*>(src + rr * lds) + c;
+      v[u] = l2_only ? __ldcg(sp) : *sp;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) dst[i + u * 128] = v[u];
+  }
+  for (; i < n; i += 128) {
+    const int64_t rr = i / vec_per_row, c = i % vec_per_row;
+    const uint4* sp = reinterpret_cast<const uint4*>(src + rr * lds) + c;
+    dst[i] = l2_only ? __ldcg(sp) : *sp;
+  }
+}
+
+__device__ void push_rows(const Pull& a, volatile int& s_ok, int* status, int et) {
+  const uint32_t epoch = __ldg(a.state), parity = __ldg(a.state + 1);
+  const int nblk = int(a.rows / 128);
+  const int rows_per_item = 128 / kSlices;
+  const int64_t vec_per_row = a.cols / 8;
+  const int64_t n = int64_t(rows_per_item) * vec_per_row;  // 16-byte vectors per item
+  const int per_source = nblk * kSlices;
+  const int own = per_source, pushes = (a.W - 1) * per_source;
+  const int items = own + 2 * pushes;
+  for (int w = blockIdx.x; w < items; w += gridDim.x) {
+    if (w < own) {
+      const int b = w / kSlices, j = w % kSlices;
+      const int64_t r0 = int64_t(b) * 128 + int64_t(j) * rows_per_item;
+      copy_item<8>(reinterpret_cast<uint4*>(a.full + (int64_t(a.rank) * a.rows + r0) * a.cols), a.x + r0 * a.ldx,
+                   a.ldx, vec_per_row, n, et, false);
+      named_sync_epilogue();
+      if (et == 0) {
+        __threadfence();
+        red_release_gpu(a.ready + a.rank * nblk + b, 1u);
+      }
+    } else if (w < own + pushes) {
+      const int q = w - own;
+      const int d = (a.rank - 1 - q / per_source + a.W) % a.W;
+      const int b = (q % per_source) / kSlices, j = q % kSlices;
+      const int64_t r0 = int64_t(b) * 128 + int64_t(j) * rows_per_item;
+      copy_item<8>(reinterpret_cast<uint4*>(recv_rows(a, d, parity, a.rank, r0)), a.x + r0 * a.ldx, a.ldx,
+                   vec_per_row, n, et, false);
+      __threadfence_system();  // this thread's peer stores, before the CTA's stamp
+      named_sync_epilogue();
+      if (et == 0) {
+        uint32_t* flag = reinterpret_cast<uint32_t*>(push_area(a, d)) + (a.rank * nblk + b) * kSlices + j;
+        st_release_sys(flag, epoch);
+      }
+    } else {
+      const int q = w - own - pushes;
+      const int s = (a.rank + 1 + q / per_source) % a.W;
+      const int b = (q % per_source) / kSlices, j = q % kSlices;
+      const int64_t r0 = int64_t(b) * 128 + int64_t(j) * rows_per_item;
+      if (et == 0) {
+        const uint32_t* flag = reinterpret_cast<const uint32_t*>(push_area(a, a.rank)) + (s * nblk + b) * kSlices + j;
+        s_ok = 1;
+        if (int32_t(ld_acquire_sys(flag) - epoch) < 0) {
+          const uint64_t t0 = globaltimer();
+          while (int32_t(ld_acquire_sys(flag) - epoch) < 0) {
+            if (globaltimer() - t0 > a.wait_ns) {
+              record_status(status, kTimeoutPeerFlag, 311, s, int(epoch));
+              s_ok = 0;
+              break;
+            }
+          }
+        }
+      }
+      named_sync_epilogue();
+      if (!s_ok) return;
+      copy_item<8>(reinterpret_cast<uint4*>(a.full + (int64_t(s) * a.rows + r0) * a.cols),
+                   recv_rows(a, a.rank, parity, s, r0), a.cols, vec_per_row, n, et, true);
+      named_sync_epilogue();
+      if (et == 0) {
+        __threadfence();
+        red_release_gpu(a.ready + s * nblk + b, 1u);
+      }
+    }
+  }
+}
+
 // PULL = 0: the epilogue warps (2..5) pull before their first tile, so the
 // epilogue of the first tiles waits for the whole pull.  PULL = 1: four
 // extra warps (6..9) pull while the epilogue warps drain finished tiles, four
@@ -202,7 +333,8 @@ struct PullEpi {
     if constexpr (!AUX) pull_rows<4>(a, *scratch, status, int(threadIdx.x) - 64);
   }
   __device__ __forceinline__ void aux(int* status) {
-    if constexpr (AUX) pull_rows<PULL == 2 ? 16 : 4>(a, *scratch, status, int(threadIdx.x) - 192);
+    if constexpr (PULL == 3) push_rows(a, *scratch, status, int(threadIdx.x) - 192);
+    else if constexpr (AUX) pull_rows<PULL == 2 ? 16 : 4>(a, *scratch, status, int(threadIdx.x) - 192);
   }
   __device__ __forceinline__ void tile_begin(int mb, int nb) { inner.tile_begin(mb, nb); }
   __device__ __forceinline__ void chunk(int row, int col, int c, const uint32_t (&r)[32]) { inner.chunk(row, col, c, r); }
@@ -333,33 +465,38 @@ static int dispatch_tile_aux(int bn, const CUtensorMap& ta, const CUtensorMap& t
   }
 }
 
-// Pull placement of the following calls: 0 epilogue-warp prologue, 1 four
-// auxiliary warps, 2 four auxiliary warps with 16 loads in flight per thread
-// (set with tdb_ag_set_variant).
+// Row movement of the following calls: 0 epilogue-warp pull prologue, 1 four
+// auxiliary warps pull, 2 the same with 16 loads in flight per thread, 3 four
+// auxiliary warps push (set with tdb_ag_set_variant).
 static int g_variant = 0;
 
 template <bool B_MN, int MODE>
-static int dispatch_tile(int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
+static int dispatch_tile(int variant, int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
                          const TileOrder& order, const EpiParams& ep, const Pull& pull, cudaStream_t s) {
-  switch (g_variant) {
+  switch (variant) {
     case 1: return dispatch_tile_aux<B_MN, MODE, 1>(bn, ta, tb, M, N, K, order, ep, pull, s);
     case 2: return dispatch_tile_aux<B_MN, MODE, 2>(bn, ta, tb, M, N, K, order, ep, pull, s);
+    case 3: return dispatch_tile_aux<B_MN, MODE, 3>(bn, ta, tb, M, N, K, order, ep, pull, s);
     default: return dispatch_tile_aux<B_MN, MODE, 0>(bn, ta, tb, M, N, K, order, ep, pull, s);
   }
 }
 
 template <bool B_MN>
-static int dispatch_mode(int mode, int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
-                         const TileOrder& order, const EpiParams& ep, const Pull& pull, cudaStream_t s) {
+static int dispatch_mode(int variant, int mode, int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
+                         int K, const TileOrder& order, const EpiParams& ep, const Pull& pull, cudaStream_t s) {
   using namespace gemm;
   switch (mode) {
-    case kStore: return dispatch_tile<B_MN, kTmaBase + kStore>(bn, ta, tb, M, N, K, order, ep, pull, s);
-    case kBias: return dispatch_tile<B_MN, kTmaBase + kBias>(bn, ta, tb, M, N, K, order, ep, pull, s);
-    case kBiasGelu: return dispatch_tile<B_MN, kTmaBase + kBiasGelu>(bn, ta, tb, M, N, K, order, ep, pull, s);
-    case kGeluBwd: return dispatch_tile<B_MN, kTmaBase + kGeluBwd>(bn, ta, tb, M, N, K, order, ep, pull, s);
+    case kStore: return dispatch_tile<B_MN, kTmaBase + kStore>(variant, bn, ta, tb, M, N, K, order, ep, pull, s);
+    case kBias: return dispatch_tile<B_MN, kTmaBase + kBias>(variant, bn, ta, tb, M, N, K, order, ep, pull, s);
+    case kBiasGelu:
+      return dispatch_tile<B_MN, kTmaBase + kBiasGelu>(variant, bn, ta, tb, M, N, K, order, ep, pull, s);
+    case kGeluBwd:
+      return dispatch_tile<B_MN, kTmaBase + kGeluBwd>(variant, bn, ta, tb, M, N, K, order, ep, pull, s);
   }
   return tdb_host::fail(int(cudaErrorInvalidValue), "ag_gemm: mode %d unsupported (0-3)", mode);
 }
+
+__global__ void push_advance_kernel(uint32_t* state) { advance_ag_state(state); }
 
 }  // namespace aggemm
 namespace gemm {
@@ -368,14 +505,21 @@ int pick_tile(int M, int N, int K, int sms);
 }  // namespace gemm
 }  // namespace tdb
 
-TDB_API int tdb_ag_prepare(const void* x, long long ldx, long long rows, long long cols,
-                           const unsigned long long* peers, int W, int rank, unsigned long long heap_off,
-                           unsigned int* state, int taco, void* stream);
+
+// Bytes of the fused all-gather GEMM's region: the all-gather region
+// (tdb_ag_region_bytes: flags and send slots for the pull variants) followed
+// by the push area of variant 3 (slice flags and two receive buffers).
+TDB_API long long tdb_ag_gemm_region_bytes(long long rows, long long cols, int W) {
+  if (rows <= 0 || cols <= 0 || rows % 128 || W < 2 || W > 64) return 0;
+  return tdb_ag_region_bytes(rows, cols) + (long long)tdb::aggemm::push_area_bytes(rows, cols, W);
+}
 
 // C = epilogue(AG(x) @ B^T) with the all-gather fused (see the header).
 //   x: this rank's rows [rows, K] (row stride ldx); full: [W*rows, K] output of
 //   the gathered rows; B: [N, K] or [K, N] (b_mn); C: [W*rows, N] bf16.
-//   peers / heap_off / state: an all-gather region (tdb_ag_region_bytes);
+//   peers / heap_off / region_bytes / state: a fused all-gather region
+//   (tdb_ag_gemm_region_bytes; with fewer bytes, tdb_ag_region_bytes, the
+//   push variant is refused);
 //   ready: uint32 [W*rows/128] zero-initialised counters owned by this call site;
 //   tile_table: [tiles] production order (this rank's rows first) for tile code bn.
 // mode: 0 store (alpha), 1 bias, 2 bias + GELU (aux_out = pre-activation), 3 GELU backward (aux).
@@ -385,7 +529,7 @@ TDB_API int tdb_ag_prepare(const void* x, long long ldx, long long rows, long lo
 // returns the previous value.
 TDB_API int tdb_ag_set_variant(int variant) {
   const int old = tdb::aggemm::g_variant;
-  if (variant >= 0 && variant <= 2) tdb::aggemm::g_variant = variant;
+  if (variant >= 0 && variant <= 3) tdb::aggemm::g_variant = variant;
   return old;
 }
 
@@ -393,7 +537,8 @@ TDB_API int tdb_ag_gemm(const void* x, long long ldx, void* full, long long rows
                         long long ldb, void* C, long long ldc, int N, int mode, const void* bias, const void* aux,
                         long long ld_aux, void* aux_out, float alpha, int bn, const int* tile_table,
                         const unsigned long long* peers, int W, int rank, unsigned long long heap_off,
-                        unsigned int* state, unsigned int* ready, double wait_seconds, int taco, void* stream) {
+                        unsigned long long region_bytes, unsigned int* state, unsigned int* ready,
+                        double wait_seconds, int taco, void* stream) {
   using namespace tdb;
   using namespace tdb::gemm;
   const long long M = rows * W;
@@ -407,8 +552,18 @@ TDB_API int tdb_ag_gemm(const void* x, long long ldx, void* full, long long rows
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (taco && K % 128)
     return tdb_host::fail(int(cudaErrorInvalidValue), "ag_gemm: the compressed gather needs K %% 128 == 0");
-  int rc = tdb_ag_prepare(x, ldx, rows, K, peers, W, rank, heap_off, state, taco, stream);
-  if (rc) return rc;
+  // the compressed gather stages TACO packets, so it keeps the deep pull
+  const int variant = (aggemm::g_variant == 3 && taco) ? 2 : aggemm::g_variant;
+  if (variant == 3 && region_bytes < (unsigned long long)tdb_ag_gemm_region_bytes(rows, K, W))
+    return tdb_host::fail(int(cudaErrorInvalidValue),
+                          "ag_gemm: the push variant needs a region of tdb_ag_gemm_region_bytes(rows, K, W) bytes");
+  int rc = 0;
+  if (variant == 3) {  // no send slot: only the epoch advances
+    aggemm::push_advance_kernel<<<1, 1, 0, s>>>(state);
+    tdb_host::launched(1);
+  } else if ((rc = tdb_ag_prepare(x, ldx, rows, K, peers, W, rank, heap_off, state, taco, stream))) {
+    return rc;
+  }
   CUtensorMap ta, tb;
   if ((rc = make_operand_map(&ta, full, false, int(M), K, K, BM))) return rc;
   if ((rc = make_operand_map(&tb, B, b_mn != 0, N, K, ldb, bn == 512 ? 128 : bn))) return rc;
@@ -440,7 +595,8 @@ TDB_API int tdb_ag_gemm(const void* x, long long ldx, void* full, long long rows
   pull.cols = K;
   pull.full = static_cast<uint16_t*>(full);
   pull.ready = ready;
-  pull.slices = 16;
+  pull.slices = aggemm::kSlices;
+  pull.push_off = uint64_t(tdb_ag_region_bytes(rows, K));
   pull.wait_ns = uint64_t(wait_seconds * 1e9);
   pull.taco = taco;
   pull.x = static_cast<const uint16_t*>(x);
@@ -451,6 +607,6 @@ TDB_API int tdb_ag_gemm(const void* x, long long ldx, void* full, long long rows
   order.gate_ready = ready;
   order.gate_epoch = state;
   order.gate_per_call = uint32_t(pull.slices);
-  return b_mn ? aggemm::dispatch_mode<true>(mode, bn, ta, tb, int(M), N, K, order, ep, pull, s)
-              : aggemm::dispatch_mode<false>(mode, bn, ta, tb, int(M), N, K, order, ep, pull, s);
+  return b_mn ? aggemm::dispatch_mode<true>(variant, mode, bn, ta, tb, int(M), N, K, order, ep, pull, s)
+              : aggemm::dispatch_mode<false>(variant, mode, bn, ta, tb, int(M), N, K, order, ep, pull, s);
 }

@@ -27,6 +27,7 @@
 // TMEM columns: S0 [0,128), S1 [128,256), O [256,384).
 // All waits are bounded (common.cuh); there is no TMA multicast.
 #include "common.cuh"
+#include "exp2_fma.cuh"
 #include "tensor_map.h"
 
 namespace tdb {
@@ -127,8 +128,10 @@ __device__ __forceinline__ float exp_row64(const uint32_t (&sr)[2][32], int lim,
 #pragma unroll
   for (int e = 0; e < 32; ++e) {
     const int c0 = 2 * e;
+    // even columns on the special-function unit, odd columns on the FMA and
+    // integer pipes (which leaves that unit the ex2 and the bf16 packing only)
     float p0 = ex2(fmaf(__uint_as_float(sr[c0 >> 5][c0 & 31]), sl2, neg));
-    float p1 = ex2(fmaf(__uint_as_float(sr[(c0 + 1) >> 5][(c0 + 1) & 31]), sl2, neg));
+    float p1 = exp2_fma(fmaf(__uint_as_float(sr[(c0 + 1) >> 5][(c0 + 1) & 31]), sl2, neg));
     if (MASK) {
       p0 = c0 <= lim ? p0 : 0.f;
       p1 = c0 + 1 <= lim ? p1 : 0.f;

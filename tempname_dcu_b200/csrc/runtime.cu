@@ -106,7 +106,7 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 // ---------------------------------------------------------------------------
 // C ABI
 // ---------------------------------------------------------------------------
-static constexpr int kAbiVersion = 4;
+static constexpr int kAbiVersion = 5;
 
 TDB_API int tdb_abi_version() { return kAbiVersion; }
 

@@ -92,8 +92,10 @@ int tdb_ag_set_variant(int variant);
 int tdb_ag_gemm(const void* x, long long ldx, void* full, long long rows, int K, const void* B, int b_mn,
                 long long ldb, void* C, long long ldc, int N, int mode, const void* bias, const void* aux,
                 long long ld_aux, void* aux_out, float alpha, int bn, const int* tile_table,
-                const unsigned long long* peers, int W, int rank, unsigned long long heap_off, unsigned int* state,
-                unsigned int* ready, double wait_seconds, int taco, void* stream);
+                const unsigned long long* peers, int W, int rank, unsigned long long heap_off,
+                unsigned long long region_bytes, unsigned int* state, unsigned int* ready, double wait_seconds,
+                int taco, void* stream);
+long long tdb_ag_gemm_region_bytes(long long rows, long long cols, int W);
 
 /* ---- sparse vocabulary-parallel embedding exchange (embed_exchange.cu) --- */
 long long tdb_embx_region_bytes(long long ml, long long H, int W);

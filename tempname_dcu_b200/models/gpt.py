@@ -109,10 +109,10 @@ class GPT:
         self._bwd_rs = {}
         self.agg = None
         self.embx = None
-        if factory is not None and 1 < self.world <= 8:
+        from ..parallel import embedding_exchange as embx
+        if factory is not None and 1 < self.world <= 8 and embx.enabled():
             # sparse embedding exchange instead of the dense reduce-scatter / gather
-            from ..parallel.embedding_exchange import EmbeddingExchange
-            self.embx = EmbeddingExchange(self.tp, self.ml, self.h, self.vocab_local)
+            self.embx = embx.EmbeddingExchange(self.tp, self.ml, self.h, self.vocab_local)
         if factory is not None and self.world > 1:
             # sequence-parallel all-gathers over NVLink (same rows/cols everywhere)
             self.tp.enable_symmetric_gather(self.ml, self.h)

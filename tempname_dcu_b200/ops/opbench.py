@@ -44,7 +44,9 @@ def main(argv=None):
                     help="comma list of consumer forms to time for remote-first operators: auto (epilogue reduction "
                          "where eligible), kernel (separate consumer kernel)")
     ap.add_argument("--ag", action="store_true",
-                    help="also time the fused all-gather GEMMs (QKV, FC1 shapes) for both pull variants")
+                    help="also time the fused all-gather GEMMs (QKV, FC1 shapes) for each row-movement variant")
+    ap.add_argument("--ag-variants", default="0,1,2,3",
+                    help="comma list of fused all-gather variants to time (0-2 pull, 3 push)")
     ap.add_argument("--selective-mode", default="wire", choices=("wire", "fp8-mma"),
                     help="fp8-mma: the selective arm computes every block as block-scaled FP8 (BF16 on the wire)")
     args = ap.parse_args(argv)
@@ -156,7 +158,7 @@ def main(argv=None):
             flops = 2.0 * m * n_out * h
             link = (world - 1) * ml * h * 2 / (NVLINK_GBS * 1e9) * 1e6
             roof = max(flops / (peak * 1e12) * 1e6, link)
-            for variant in (0, 1, 2):
+            for variant in (int(v) for v in args.ag_variants.split(",")):
                 set_ag_variant(variant)
                 us = timed(lambda: agg(xl, w, mode=mode, bias=bias, out=out, full=full,
                                        **({"aux_out": pre} if mode == agg.BIAS_GELU else {})))

@@ -9,7 +9,8 @@ CUDA graph.  Creation is collective (every rank, same order).
 
 ``SymmAgGemm`` fuses the gather into the tcgen05 GEMM that consumes it
 (``csrc/ag_gemm.cu``), optionally TACO-compressed (``taco=True``);
-``set_ag_variant`` chooses where the rows are pulled.
+``set_ag_variant`` chooses how the rows move (pulled by the consuming GEMM,
+or pushed by their owner into every peer's receive buffer).
 
 Reference parity: python/flux_dcu/model.py:75-81 (gather_rows).
 """
@@ -64,20 +65,24 @@ native.register("tdb_ag_gemm", [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_voi
                                 ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_void_p, ctypes.c_longlong,
                                 ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,
                                 ctypes.c_void_p, ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
-                                ctypes.c_int, ctypes.c_int, ctypes.c_ulonglong, ctypes.c_void_p, ctypes.c_void_p,
-                                ctypes.c_double, ctypes.c_int, ctypes.c_void_p])
+                                ctypes.c_int, ctypes.c_int, ctypes.c_ulonglong, ctypes.c_ulonglong, ctypes.c_void_p,
+                                ctypes.c_void_p, ctypes.c_double, ctypes.c_int, ctypes.c_void_p])
+native.register("tdb_ag_gemm_region_bytes", [ctypes.c_longlong, ctypes.c_longlong, ctypes.c_int], ctypes.c_longlong)
 native.register("tdb_gemm_pick_tile", [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int])
 native.register("tdb_ag_set_variant", [ctypes.c_int])
 
 
 def set_ag_variant(variant):
-    """Where the fused all-gather GEMM pulls the gathered rows on this process:
-    0 = the epilogue warps before their first tile, 1 = four auxiliary warps
-    concurrently with the pipeline, 2 = the same auxiliary warps with sixteen
-    16-byte loads in flight per thread.  Results are bitwise the same; all
-    ranks must use the same variant.  Returns the previous one."""
-    if variant not in (0, 1, 2):
-        raise ValueError("variant must be 0, 1 or 2")
+    """How the fused all-gather GEMM moves the gathered rows on this process:
+    0 = the epilogue warps pull them before their first tile, 1 = four
+    auxiliary warps pull concurrently with the pipeline, 2 = the same
+    auxiliary warps with sixteen 16-byte loads in flight per thread, 3 = the
+    auxiliary warps push this rank's rows into every peer's receive buffer
+    and copy the received rows locally (the compressed gather keeps 2).
+    Results are bitwise the same; all ranks must use the same variant.
+    Returns the previous one."""
+    if variant not in (0, 1, 2, 3):
+        raise ValueError("variant must be 0, 1, 2 or 3")
     return int(native.lib().tdb_ag_set_variant(int(variant)))
 
 
@@ -125,7 +130,8 @@ class SymmAgGemm:
             raise ValueError("the fused all-gather GEMM needs rows % 256 == 0 and K % 64 == 0 (K % 128 compressed)")
         self.tp, self.rows, self.cols = tp, int(rows), int(cols)
         self.taco = bool(taco)
-        self.heap = SymmetricHeap(tp, int(native.lib().tdb_ag_region_bytes(self.rows, self.cols)))
+        self.region_bytes = int(native.lib().tdb_ag_gemm_region_bytes(self.rows, self.cols, tp.world))
+        self.heap = SymmetricHeap(tp, self.region_bytes)
         dev = self.heap.device
         self.state = torch.zeros(2, dtype=torch.int32, device=dev)
         self.ready = torch.zeros(tp.world * self.rows // 128, dtype=torch.int32, device=dev)
@@ -164,7 +170,7 @@ class SymmAgGemm:
             weight.stride(0), out.data_ptr(), out.stride(0), N, int(mode), 0 if bias is None else bias.data_ptr(),
             0 if aux is None else aux.data_ptr(), 0 if aux_t is None else aux_t.stride(0),
             0 if aux_out is None else aux_out.data_ptr(), float(alpha), bn, self._table(N, bn).data_ptr(),
-            self.heap.peers.data_ptr(), self.tp.world, self.tp.rank, 0, self.state.data_ptr(),
+            self.heap.peers.data_ptr(), self.tp.world, self.tp.rank, 0, self.region_bytes, self.state.data_ptr(),
             self.ready.data_ptr(), self.wait_seconds, int(self.taco), native.stream_ptr()), "fused all-gather GEMM")
         self.calls += 1
         if mode == self.BIAS_GELU:

@@ -39,6 +39,21 @@ native.register("tdb_embx_backward", [ctypes.c_void_p, ctypes.c_void_p, ctypes.c
 
 PEER_WAIT_SECONDS = 20.0
 _HEADER = 256
+# Whether models built from now on use the exchange (True, the default) or
+# the dense reduce-scatter / all-gather; a process-wide switch for A/B runs.
+_ENABLED = True
+
+
+def set_embedding_exchange(on):
+    """Enable or disable the sparse exchange for models created afterwards;
+    returns the previous setting.  Both forms give bitwise the same rows."""
+    global _ENABLED
+    old, _ENABLED = _ENABLED, bool(on)
+    return old
+
+
+def enabled():
+    return _ENABLED
 
 
 class EmbeddingExchange:

@@ -73,6 +73,11 @@ def set_epilogue_reduction(on):
     return old
 
 
+def epilogue_reduction_default():
+    """The current process-wide setting of ``set_epilogue_reduction``."""
+    return _EPILOGUE_REDUCTION
+
+
 _CONTEXTS = {}
 _LOCK = threading.Lock()
 FLAGS_BYTES = 1 << 16

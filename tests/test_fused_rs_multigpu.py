@@ -169,7 +169,8 @@ def _worker(rank, world, init_file, result_path):
         errs, same = [], []
         def rel(a, b):
             return float((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30))
-        for N, variant in ((1536, 0), (1000, 0), (1536, 1), (1000, 1), (1536, 2), (1000, 2)):
+        for N, variant in ((1536, 0), (1000, 0), (1536, 1), (1000, 1), (1536, 2), (1000, 2), (1536, 3), (1000, 3),
+                           (1536, 1), (1536, 3)):
             set_ag_variant(variant)
             w = (torch.randn(N, K, device="cuda") / 32).to(torch.bfloat16)
             bias = torch.randn(N, device="cuda").to(torch.bfloat16)
@@ -203,7 +204,7 @@ def _worker(rank, world, init_file, result_path):
         tsame, terrs = [], []
         w = (torch.randn(1536, K, device="cuda") / 32).to(torch.bfloat16)
         for rep in range(4):
-            set_ag_variant(rep % 3)
+            set_ag_variant(rep % 4)  # 3 (push) falls back to the deep pull for compressed rows
             xl = torch.randn(rows, K, device="cuda").to(torch.bfloat16)
             ref_full = torch.empty(rows * world, K, dtype=torch.bfloat16, device="cuda")
             dist.all_gather_into_tensor(ref_full, xl, group=group)
