@@ -476,7 +476,9 @@ __device__ __forceinline__ void dq_row32(const uint32_t (&sv)[32], const uint32_
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int c = 2 * e + u;
-      float p = ex2(fmaf(__uint_as_float(sv[c]), sl2, nl));
+      // odd columns off the special-function unit (exp2_fma.cuh)
+      const float arg = fmaf(__uint_as_float(sv[c]), sl2, nl);
+      float p = u == 0 ? ex2(arg) : exp2_fma(arg);
       if (MASK) p = c <= lim ? p : 0.f;
       d2[u] = p * (__uint_as_float(pv[c]) - Dr);
     }
@@ -494,7 +496,7 @@ __device__ __forceinline__ void dkdv_row32(const uint32_t (&sv)[32], const uint3
     const float2 lse2 = *reinterpret_cast<const float2*>(st + 2 * e);
     const float2 ds2 = *reinterpret_cast<const float2*>(st + 64 + 2 * e);
     float p0 = ex2(fmaf(__uint_as_float(sv[2 * e]), sl2, -lse2.x));
-    float p1 = ex2(fmaf(__uint_as_float(sv[2 * e + 1]), sl2, -lse2.y));
+    float p1 = exp2_fma(fmaf(__uint_as_float(sv[2 * e + 1]), sl2, -lse2.y));  // off the special-function unit
     if (MASK) {
       p0 = 2 * e >= lim ? p0 : 0.f;
       p1 = 2 * e + 1 >= lim ? p1 : 0.f;
