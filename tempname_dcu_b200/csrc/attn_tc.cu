@@ -27,7 +27,6 @@
 // TMEM columns: S0 [0,128), S1 [128,256), O [256,384).
 // All waits are bounded (common.cuh); there is no TMA multicast.
 #include "common.cuh"
-#include "exp2_fma.cuh"
 #include "tensor_map.h"
 
 namespace tdb {
@@ -128,10 +127,8 @@ __device__ __forceinline__ float exp_row64(const uint32_t (&sr)[2][32], int lim,
 #pragma unroll
   for (int e = 0; e < 32; ++e) {
     const int c0 = 2 * e;
-    // even columns on the special-function unit, odd columns on the FMA and
-    // integer pipes (which leaves that unit the ex2 and the bf16 packing only)
     float p0 = ex2(fmaf(__uint_as_float(sr[c0 >> 5][c0 & 31]), sl2, neg));
-    float p1 = exp2_fma(fmaf(__uint_as_float(sr[(c0 + 1) >> 5][(c0 + 1) & 31]), sl2, neg));
+    float p1 = ex2(fmaf(__uint_as_float(sr[(c0 + 1) >> 5][(c0 + 1) & 31]), sl2, neg));
     if (MASK) {
       p0 = c0 <= lim ? p0 : 0.f;
       p1 = c0 + 1 <= lim ? p1 : 0.f;
@@ -476,9 +473,7 @@ __device__ __forceinline__ void dq_row32(const uint32_t (&sv)[32], const uint32_
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int c = 2 * e + u;
-      // odd columns off the special-function unit (exp2_fma.cuh)
-      const float arg = fmaf(__uint_as_float(sv[c]), sl2, nl);
-      float p = u == 0 ? ex2(arg) : exp2_fma(arg);
+      float p = ex2(fmaf(__uint_as_float(sv[c]), sl2, nl));
       if (MASK) p = c <= lim ? p : 0.f;
       d2[u] = p * (__uint_as_float(pv[c]) - Dr);
     }
@@ -496,7 +491,7 @@ __device__ __forceinline__ void dkdv_row32(const uint32_t (&sv)[32], const uint3
     const float2 lse2 = *reinterpret_cast<const float2*>(st + 2 * e);
     const float2 ds2 = *reinterpret_cast<const float2*>(st + 64 + 2 * e);
     float p0 = ex2(fmaf(__uint_as_float(sv[2 * e]), sl2, -lse2.x));
-    float p1 = exp2_fma(fmaf(__uint_as_float(sv[2 * e + 1]), sl2, -lse2.y));  // off the special-function unit
+    float p1 = ex2(fmaf(__uint_as_float(sv[2 * e + 1]), sl2, -lse2.y));
     if (MASK) {
       p0 = 2 * e >= lim ? p0 : 0.f;
       p1 = 2 * e + 1 >= lim ? p1 : 0.f;

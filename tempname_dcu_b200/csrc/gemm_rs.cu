@@ -1125,7 +1125,10 @@ static int gemm_rs_impl(const void* A, int64_t lda, const void* B, int b_mn, int
   p.wait_ns = uint64_t(wait_seconds * 1e9);
   p.phases = phases;
   p.call_state = call_state;
-  p.variant = policy == kPolicyEpilogue ? 0 : g_variant;
+  // Producers of TACO blocks are built without the bulk-push path, so their
+  // calls drop that bit: the tiles then travel (and are signalled and read
+  // back by the reducer) as lane stores in row-major layout.
+  p.variant = policy == kPolicyEpilogue ? 0 : (quantized ? (g_variant & ~kVariantBulk) : g_variant);
   const int sms = tdb_host::sm_count();
   const int grid = order.num_tiles < sms ? order.num_tiles : sms;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
