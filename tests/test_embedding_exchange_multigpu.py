@@ -93,7 +93,9 @@ def test_embedding_exchange_matches_dense_nccl_path(tmp_path):
         pytest.skip("needs at least two GPUs")
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     path = str(tmp_path / "result.json")
-    mp.spawn(_worker, args=(2, str(tmp_path / "rendezvous"), path), nprocs=2, join=True)
+    # TDB_TEST_WORLD runs the same checks on more ranks (up to the visible GPUs)
+    world = min(int(os.environ.get("TDB_TEST_WORLD", "2")), torch.cuda.device_count())
+    mp.spawn(_worker, args=(world, str(tmp_path / "rendezvous"), path), nprocs=world, join=True)
     res = json.load(open(path))
     assert res["fwd"] and all(res["fwd"]), res
     assert res["bwd"] and all(res["bwd"]), res

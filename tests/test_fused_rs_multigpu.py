@@ -243,7 +243,8 @@ def test_fused_gemm_rs_all_arms(tmp_path):
     import torch.multiprocessing as mp
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs at least two GPUs")
-    world = 2
+    # TDB_TEST_WORLD runs the same checks on more ranks (up to the visible GPUs)
+    world = min(int(os.environ.get("TDB_TEST_WORLD", "2")), torch.cuda.device_count())
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     path = str(tmp_path / "result.json")
     # file rendezvous: no TCP port to race for
