@@ -57,12 +57,15 @@ def parse():
     p.add_argument("--error-budget", type=float, default=0.01)
     p.add_argument("--small", action="store_true", help="2-layer smoke configuration (not a headline number)")
     # transport choices (defaults: the framework's); all ranks must agree
-    p.add_argument("--ag-variant", type=int, choices=(0, 1, 2, 3), default=None,
-                   help="fused all-gather GEMM row movement: 0-2 pull, 3 push")
+    p.add_argument("--ag-variant", type=int, choices=(-1, 0, 1, 2, 3), default=None,
+                   help="fused all-gather GEMM row movement: -1 automatic, 0-2 pull, 3 push")
     p.add_argument("--rs-variant", type=int, choices=tuple(range(8)), default=None,
                    help="fused GEMM-RS variant bits: 1 per-tile signals, 2 in-kernel consumer, 4 bulk pushes")
     p.add_argument("--epilogue-reduction", choices=("on", "off"), default=None,
                    help="remote-first BF16 operators reduce their own blocks in the producer epilogue")
+    p.add_argument("--wgrad-sms", type=int, default=None,
+                   help="overlap the backward's weight-gradient GEMMs with the fused collectives on this many SMs "
+                        "(0 off; default: the framework's choice for the run's world size)")
     p.add_argument("--embedding-exchange", choices=("on", "off"), default=None,
                    help="sparse vocabulary-parallel embedding exchange instead of the dense collectives")
     return p.parse_args()
@@ -82,7 +85,7 @@ def apply_transport(args):
     if args.embedding_exchange is not None:
         embedding_exchange.set_embedding_exchange(args.embedding_exchange == "on")
     lib = native.lib()
-    return dict(ag_variant=int(lib.tdb_ag_set_variant(-1)), rs_variant=int(lib.tdb_rs_set_variant(-1)),
+    return dict(ag_variant=allgather.ag_variant(), rs_variant=int(lib.tdb_rs_set_variant(-1)),
                 epilogue_reduction=runtime.epilogue_reduction_default(),
                 embedding_exchange=embedding_exchange.enabled())
 
@@ -220,9 +223,13 @@ def main():
             factory = operator_factory_for(args.arm)
         if args.codec_calibration_steps > args.warmup:
             raise SystemExit("--codec-calibration-steps must run inside the warm-up steps")
+        from tempname_dcu_b200.models.gpt import default_wgrad_sms
+        wgrad_sms = args.wgrad_sms if args.wgrad_sms is not None else default_wgrad_sms(world)
+        transport["wgrad_sms"] = wgrad_sms
         trainer = Trainer(config, args.arm, group, operator_factory=factory, cuda_graph=not args.no_graph,
                           graph_warmup=min(2, max(0, args.warmup - 1)), taco_allgather=args.taco_allgather,
-                          codec_calibration_steps=args.codec_calibration_steps, error_budget=args.error_budget)
+                          codec_calibration_steps=args.codec_calibration_steps, error_budget=args.error_budget,
+                          wgrad_sms=wgrad_sms)
     from tempname_dcu_b200.train import synthetic_batches
     c = trainer.config
     (tokens_h, labels_h), = synthetic_batches(c, 1, seed=4321)

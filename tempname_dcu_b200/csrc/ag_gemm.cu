@@ -410,7 +410,8 @@ static int launch1(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   order.num_m = (M + BM - 1) / BM;
   order.num_n = (N + BN - 1) / BN;
   order.num_tiles = order.num_m * order.num_n;
-  const int grid = order.num_tiles < tdb_host::sm_count() ? order.num_tiles : tdb_host::sm_count();
+  const int sms = tdb_host::grid_sms();
+  const int grid = order.num_tiles < sms ? order.num_tiles : sms;
   return launch_coop(kern, dim3(grid), gemm::kThreads + (PULL ? 128 : 0), kSmem, 1, s, ta, tb, K, order, ep, pull,
                      tdb_host::status_ptr());
 }
@@ -448,7 +449,8 @@ static int launch2(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   order.num_m = (M + 255) / 256;
   order.num_n = (N + 255) / 256;
   order.num_tiles = order.num_m * order.num_n;
-  const int pairs = max_clusters[dev & 63];
+  int pairs = max_clusters[dev & 63];
+  if (pairs > tdb_host::grid_sms() / 2) pairs = tdb_host::grid_sms() / 2 > 0 ? tdb_host::grid_sms() / 2 : 1;
   const int clusters = order.num_tiles < pairs ? order.num_tiles : pairs;
   return launch_coop(kern, dim3(2 * clusters), kBlock, kSmem, 2, s, ta, tb, K, order, ep, pull,
                      tdb_host::status_ptr());
@@ -467,8 +469,13 @@ static int dispatch_tile_aux(int bn, const CUtensorMap& ta, const CUtensorMap& t
 
 // Row movement of the following calls: 0 epilogue-warp pull prologue, 1 four
 // auxiliary warps pull, 2 the same with 16 loads in flight per thread, 3 four
-// auxiliary warps push (set with tdb_ag_set_variant).
-static int g_variant = 0;
+// auxiliary warps push (set with tdb_ag_set_variant).  kAuto (the default)
+// takes 2 from four ranks up and 0 below: measured on 8 B200 (QKV / FC1
+// shapes, us) 0: 94.8 / 103.5, 2: 84.8 / 96.7, 3: 94.5 / 104.1; on 2 B200
+// 0: 96.8 / 138.3, 2: 103.2 / 142.7, 3: 95.1 / 139.0.
+constexpr int kAuto = -1;
+static int g_variant = kAuto;
+static int resolve_variant(int W) { return g_variant != kAuto ? g_variant : (W >= 4 ? 2 : 0); }
 
 template <bool B_MN, int MODE>
 static int dispatch_tile(int variant, int bn, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K,
@@ -523,13 +530,14 @@ TDB_API long long tdb_ag_gemm_region_bytes(long long rows, long long cols, int W
 //   ready: uint32 [W*rows/128] zero-initialised counters owned by this call site;
 //   tile_table: [tiles] production order (this rank's rows first) for tile code bn.
 // mode: 0 store (alpha), 1 bias, 2 bias + GELU (aux_out = pre-activation), 3 GELU backward (aux).
-// Pull placement of the fused all-gather GEMM for the following calls
-// (0: the epilogue warps pull before their first tile; 1: four auxiliary
-// warps pull concurrently; 2: as 1 with sixteen loads in flight per thread);
-// returns the previous value.
+// Row movement of the fused all-gather GEMM for the following calls
+// (-1: automatic by world size; 0: the epilogue warps pull before their first
+// tile; 1: four auxiliary warps pull concurrently; 2: as 1 with sixteen loads
+// in flight per thread; 3: the auxiliary warps push); returns the previous
+// value.  Any other value only returns the current one.
 TDB_API int tdb_ag_set_variant(int variant) {
   const int old = tdb::aggemm::g_variant;
-  if (variant >= 0 && variant <= 3) tdb::aggemm::g_variant = variant;
+  if (variant >= tdb::aggemm::kAuto && variant <= 3) tdb::aggemm::g_variant = variant;
   return old;
 }
 
@@ -553,7 +561,8 @@ TDB_API int tdb_ag_gemm(const void* x, long long ldx, void* full, long long rows
   if (taco && K % 128)
     return tdb_host::fail(int(cudaErrorInvalidValue), "ag_gemm: the compressed gather needs K %% 128 == 0");
   // the compressed gather stages TACO packets, so it keeps the deep pull
-  const int variant = (aggemm::g_variant == 3 && taco) ? 2 : aggemm::g_variant;
+  const int chosen = aggemm::resolve_variant(W);
+  const int variant = (chosen == 3 && taco) ? 2 : chosen;
   if (variant == 3 && region_bytes < (unsigned long long)tdb_ag_gemm_region_bytes(rows, K, W))
     return tdb_host::fail(int(cudaErrorInvalidValue),
                           "ag_gemm: the push variant needs a region of tdb_ag_gemm_region_bytes(rows, K, W) bytes");

@@ -368,4 +368,8 @@ void launched(int n);
 int* status_ptr();
 // SM count of the current device (cached).
 int sm_count();
+// SMs that persistent GEMM-shaped kernels (plain, fused collective) launched
+// from this host thread may occupy: sm_count(), or less under
+// tdb_set_grid_limit (so that a kernel on another stream can run beside them).
+int grid_sms();
 }  // namespace tdb_host

@@ -45,7 +45,8 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, in
   order.group_m = 16;
   order.table = nullptr;
   order.num_tiles = order.num_m * order.num_n;
-  const int grid = order.num_tiles < tdb_host::sm_count() ? order.num_tiles : tdb_host::sm_count();
+  const int sms = tdb_host::grid_sms();
+  const int grid = order.num_tiles < sms ? order.num_tiles : sms;
   kern<<<grid, kThreads, kSmem, stream>>>(ta, tb, K, order, ep, tdb_host::status_ptr());
   tdb_host::launched(1);
   return int(cudaGetLastError());
@@ -100,7 +101,8 @@ static int launch2(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   order.group_m = 8;
   order.table = nullptr;
   order.num_tiles = order.num_m * order.num_n;
-  const int clusters = order.num_tiles < max_clusters[dev & 63] ? order.num_tiles : max_clusters[dev & 63];
+  int clusters = order.num_tiles < max_clusters[dev & 63] ? order.num_tiles : max_clusters[dev & 63];
+  if (clusters > tdb_host::grid_sms() / 2) clusters = tdb_host::grid_sms() / 2 > 0 ? tdb_host::grid_sms() / 2 : 1;
   cfg.gridDim = dim3(2 * clusters);
   int* status = tdb_host::status_ptr();
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, K, order, ep, status);

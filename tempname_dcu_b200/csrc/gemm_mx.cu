@@ -106,7 +106,8 @@ static int launch(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, in
   order.group_m = 16;
   order.table = nullptr;
   order.num_tiles = order.num_m * order.num_n;
-  const int grid = order.num_tiles < tdb_host::sm_count() ? order.num_tiles : tdb_host::sm_count();
+  const int sms = tdb_host::grid_sms();
+  const int grid = order.num_tiles < sms ? order.num_tiles : sms;
   kern<<<grid, kThreads, kSmem, stream>>>(ta, tb, K, order, ep, sfa, sfb, M / 128, N / 128, tdb_host::status_ptr());
   tdb_host::launched(1);
   return int(cudaGetLastError());

@@ -1019,7 +1019,7 @@ static int launch_consumer(const Params& p, cudaStream_t stream) {
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, rs_reduce_kernel, kReduceThreads, 0);
     per_sm[dev & 63] = (e == cudaSuccess && nb > 0) ? nb : 1;
   }
-  const int rgrid = per_sm[dev & 63] * tdb_host::sm_count();
+  const int rgrid = per_sm[dev & 63] * tdb_host::grid_sms();
   rs_reduce_kernel<<<rgrid, kReduceThreads, 0, stream>>>(p, status);
   tdb_host::launched(1);
   e = cudaGetLastError();
@@ -1129,7 +1129,7 @@ static int gemm_rs_impl(const void* A, int64_t lda, const void* B, int b_mn, int
   // calls drop that bit: the tiles then travel (and are signalled and read
   // back by the reducer) as lane stores in row-major layout.
   p.variant = policy == kPolicyEpilogue ? 0 : (quantized ? (g_variant & ~kVariantBulk) : g_variant);
-  const int sms = tdb_host::sm_count();
+  const int sms = tdb_host::grid_sms();
   const int grid = order.num_tiles < sms ? order.num_tiles : sms;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (mx) {

@@ -60,6 +60,15 @@ int sm_count() {
   return cache[dev] > 0 ? cache[dev] : 148;
 }
 
+// Per host thread: launches (and CUDA-graph captures) on one thread do not
+// change another thread's grids.
+static thread_local int t_grid_limit = 0;
+
+int grid_sms() {
+  const int n = sm_count();
+  return (t_grid_limit > 0 && t_grid_limit < n) ? t_grid_limit : n;
+}
+
 // ---------------------------------------------------------------------------
 // cuTensorMapEncodeTiled through the runtime's driver entry point, so that the
 // library does not link libcuda directly.
@@ -145,6 +154,17 @@ TDB_API int tdb_diagnostic_delay(unsigned long long cycles, void* stream) {
 }
 
 // Per-device SM count cache for persistent grids.
+// Cap the grid of the persistent GEMM-shaped kernels launched next from this
+// host thread at `ctas` CTAs (2-CTA kernels: ctas / 2 clusters); 0 removes
+// the cap.  Used to run a weight-gradient GEMM on one stream beside a
+// communication-bound fused kernel on another, each on its own share of the
+// SMs.  Returns the previous cap.
+TDB_API int tdb_set_grid_limit(int ctas) {
+  const int old = tdb_host::t_grid_limit;
+  if (ctas >= 0) tdb_host::t_grid_limit = ctas;
+  return old;
+}
+
 TDB_API int tdb_sm_count(int device) {
   int n = 0;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return -1;

@@ -31,6 +31,7 @@ int tdb_read_status(int* out4);
 int tdb_clear_status(void);
 int tdb_diagnostic_delay(unsigned long long cycles, void* stream);
 int tdb_sm_count(int device);
+int tdb_set_grid_limit(int ctas);
 
 /* ---- symmetric memory (symm.cu) ----------------------------------------- */
 int tdb_symm_handle_bytes(void);

@@ -347,12 +347,12 @@ def expected_schedule(model, world, arm, role_plan=None):
 
 def expected_consumer_policy(arm, stage):
     """Arrival arms consume per lane, ready block first; the other arms in
-    order -- except the BF16 flux arm's training windows, whose remote-first
-    operators reduce their own blocks in the producer's epilogue (same sum
-    order and rounding, no consumer kernel)."""
+    order, in every stage (the optional epilogue reduction of remote-first
+    BF16 operators is off by default and not part of an experiment)."""
+    del stage
     if arm in (ARRIVAL, SELECTIVE):
         return "per_lane_ready"
-    return "epilogue" if arm == "flux" and stage == "train" else "ordered"
+    return "ordered"
 
 
 def expected_operator_state(model, world, arm, rank, role, calls, stage, execution_plan=None,

@@ -61,11 +61,22 @@ class NcclRowOperator:
         return dict(backend="nccl-reduce-scatter", calls=self.calls)
 
 
+def default_wgrad_sms(world):
+    """SMs given to the backward's weight-gradient stream by default at this
+    tensor-parallel world size (0: no overlap)."""
+    return 0
+
+
 class GPT:
     """One rank's shard of the TP/SP GPT with flat parameter storage."""
 
     def __init__(self, config, arm="flux", group=None, *, device="cuda", seed=1234, operator_factory=None,
-                 execution_plan=None, materialize=True, taco_allgather=False):
+                 execution_plan=None, materialize=True, taco_allgather=False, wgrad_sms=0):
+        """``wgrad_sms`` > 0 (two or more ranks): in the backward, every
+        layer's weight-gradient GEMMs run on a second stream, each on at most
+        that many SMs, while the communication-bound fused all-gather and
+        reduce-scatter kernels on the compute stream keep the other SMs
+        (``set_wgrad_overlap``)."""
         import torch
         from ..parallel.tp import TPGroup
         self.tp = TPGroup(group)
@@ -103,6 +114,10 @@ class GPT:
                     self.operators.append(factory(m=self.m, n=self.h, k=k, group=group, arm=arm,
                                                   chunk_rows=c["chunk_rows"], plan=plan))
         self._scratch = {}
+        self._overlap = None   # (fused-kernel CTAs, weight-gradient CTAs) when the backward overlaps them
+        self._wgrad_stream = None
+        self._wgrad_pending = None
+        self.set_wgrad_overlap(wgrad_sms)
         # Backward reduce-scatters of the column-parallel data gradients
         # (dX = RS(dY W)) run through the same fused kernel (BF16, ordered)
         # whenever the forward projections do.
@@ -133,8 +148,72 @@ class GPT:
         from ..ops import gemm as G
         op = self._bwd_rs.get(dy.shape[1])
         if op is not None:
-            return op.forward(dy, weight)
+            with self._fused_share():
+                return op.forward(dy, weight)
         return self.tp.scatter_sum(G.matmul_nt(dy, weight))
+
+    # ------------------------------------------------ backward overlap
+    def set_wgrad_overlap(self, wgrad_sms):
+        """Run the per-layer weight-gradient GEMMs of the backward on a
+        second stream, on at most ``wgrad_sms`` SMs, beside the fused
+        collective kernels, which are then limited to the remaining SMs (0:
+        off, everything on one stream).  With tensor parallelism the fused
+        kernels wait on NVLink for most of their time, so the GEMMs fill SMs
+        that would idle.  Each weight's gradient still accumulates in
+        micro-batch order, so the result is bitwise the same.  Takes effect
+        for the next backward (and the next captured graph)."""
+        import torch
+        wgrad_sms = int(wgrad_sms)
+        if wgrad_sms <= 0 or self.world < 2:
+            self._overlap = None
+            return
+        from ..ops import native
+        sms = int(native.lib().tdb_sm_count(torch.cuda.current_device()))
+        wgrad_sms = min(max(2, wgrad_sms - wgrad_sms % 2), sms - 2)
+        self._overlap = (sms - wgrad_sms, wgrad_sms)
+        if self._wgrad_stream is None:
+            self._wgrad_stream = torch.cuda.Stream(device=self.device)
+
+    def _fused_share(self):
+        import contextlib
+        from ..ops import native
+        return native.grid_limit(self._overlap[0]) if self._overlap else contextlib.nullcontext()
+
+    def _wgrad(self, dy, x, name, keep):
+        """Gr(name) += dy^T x: on the weight-gradient stream when overlapping
+        (``keep`` holds the operands until the compute stream has waited for
+        it), else in line."""
+        import torch
+        from ..ops import gemm as G
+        from ..ops import native
+        if self._overlap is None:
+            G.weight_grad(dy, x, self.Gr(name))
+            return
+        side = self._wgrad_stream
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side), native.grid_limit(self._overlap[1]):
+            G.weight_grad(dy, x, self.Gr(name))
+        keep.extend((dy, x))
+
+    def _wgrad_layer_done(self, keep):
+        """After a layer's backward: the compute stream waits for the PREVIOUS
+        layer's weight gradients (so they overlap this layer's collectives)
+        and releases their operands; this layer's stay pending."""
+        import torch
+        if self._overlap is None:
+            return
+        done = torch.cuda.Event()
+        done.record(self._wgrad_stream)
+        if self._wgrad_pending is not None:
+            torch.cuda.current_stream().wait_event(self._wgrad_pending[0])
+        self._wgrad_pending = (done, keep)
+
+    def _wgrad_join(self):
+        import torch
+        if self._overlap is None:
+            return
+        torch.cuda.current_stream().wait_stream(self._wgrad_stream)
+        self._wgrad_pending = None
 
     # ------------------------------------------------------------ helpers
     def _buf(self, key, numel, dtype):
@@ -243,6 +322,7 @@ class GPT:
             with self._range(f"tdb/layer{i}/bwd"):
                 dx = self._layer_bwd(i, dx, saved[i], ln_scratch)
             saved[i] = None
+        self._wgrad_join()
         # ---- embedding / positions
         K.position_bwd(dx, self.rank * self.ml if self.world > 1 else 0, c["sequence"], self.Gr("position"))
         if self.embx is not None:  # only the rows of tokens in this rank's shard, from their holders
@@ -279,35 +359,40 @@ class GPT:
         from ..ops import kernels as K
         c, p = self.config, f"layers.{i}."
         x, mean1, rstd1, ln1f, qkv, attn, lse, x1, mean2, rstd2, ln2f, z, h1 = saved
+        keep = []  # operands of weight gradients still running on the overlap stream
         # FC2 (row-parallel): x2 = x1 + RS(h1 W2^T) + b2
         self._colsum(dx2, p + "fc2_bias")
         if self.agg is not None:
-            dz, dyf = self.agg(dx2, self.P(p + "fc2_weight"), b_mn=True, mode=self.agg.GELU_BWD, aux=z)
+            with self._fused_share():
+                dz, dyf = self.agg(dx2, self.P(p + "fc2_weight"), b_mn=True, mode=self.agg.GELU_BWD, aux=z)
         else:
             dyf = self.tp.gather(dx2)
             dz = G.matmul_nt(dyf, self.P(p + "fc2_weight"), gelu_pre=z)
-        G.weight_grad(dyf, h1, self.Gr(p + "fc2_weight"))
+        self._wgrad(dyf, h1, p + "fc2_weight", keep)
         # FC1 (column-parallel)
         self._colsum(dz, p + "fc1_bias")
+        self._wgrad(dz, ln2f, p + "fc1_weight", keep)
         dln2 = self._dgrad_rs(dz, self.P(p + "fc1_weight"))
-        G.weight_grad(dz, ln2f, self.Gr(p + "fc1_weight"))
         dx1 = K.layernorm_bwd(x1, self.P(p + "ln2_weight"), mean2, rstd2, dln2, self.Gr(p + "ln2_weight"),
                               self.Gr(p + "ln2_bias"), ln_scratch, dres=dx2)
         # attention out (row-parallel)
         self._colsum(dx1, p + "attn_bias")
         if self.agg is not None:
-            dattn, dyf = self.agg(dx1, self.P(p + "attn_weight"), b_mn=True)
+            with self._fused_share():
+                dattn, dyf = self.agg(dx1, self.P(p + "attn_weight"), b_mn=True)
         else:
             dyf = self.tp.gather(dx1)
             dattn = G.matmul_nt(dyf, self.P(p + "attn_weight"))
-        G.weight_grad(dyf, attn, self.Gr(p + "attn_weight"))
+        self._wgrad(dyf, attn, p + "attn_weight", keep)
         dqkv = K.attention_bwd(qkv, attn, dattn, lse, c["micro_batch"], c["sequence"], self.heads_local)
         # QKV (column-parallel)
         self._colsum(dqkv, p + "qkv_bias")
+        self._wgrad(dqkv, ln1f, p + "qkv_weight", keep)
         dln1 = self._dgrad_rs(dqkv, self.P(p + "qkv_weight"))
-        G.weight_grad(dqkv, ln1f, self.Gr(p + "qkv_weight"))
-        return K.layernorm_bwd(x, self.P(p + "ln1_weight"), mean1, rstd1, dln1, self.Gr(p + "ln1_weight"),
-                               self.Gr(p + "ln1_bias"), ln_scratch, dres=dx1)
+        dx = K.layernorm_bwd(x, self.P(p + "ln1_weight"), mean1, rstd1, dln1, self.Gr(p + "ln1_weight"),
+                             self.Gr(p + "ln1_bias"), ln_scratch, dres=dx1)
+        self._wgrad_layer_done(keep)
+        return dx
 
     # ------------------------------------------------------------ gradients
     def reduce_replicated_gradients(self):

@@ -29,6 +29,7 @@ SIGNATURES = {
     "tdb_read_status": [c_void_p],
     "tdb_clear_status": [],
     "tdb_sm_count": [c_int],
+    "tdb_set_grid_limit": [c_int],
     "tdb_diagnostic_delay": [ctypes.c_ulonglong, c_void_p],
     "tdb_taco_encode": [c_void_p, c_void_p, c_int64, c_void_p],
     "tdb_taco_decode": [c_void_p, c_void_p, c_int64, c_void_p],
@@ -128,3 +129,23 @@ def raise_on_status() -> None:
 def launch_count() -> int:
     """Kernels launched through libtdb.so in this process so far."""
     return int(lib().tdb_launch_count())
+
+
+class grid_limit:
+    """``with grid_limit(n):`` -- the persistent GEMM-shaped kernels (plain
+    GEMMs, fused collectives) launched inside, from this thread, use at most
+    ``n`` CTAs (0: no cap), so that two of them on different streams share the
+    SMs instead of queueing.  Launch geometry is fixed when a CUDA graph is
+    captured, so the cap also holds on replay."""
+
+    def __init__(self, ctas):
+        self.ctas = int(ctas)
+        self.previous = 0
+
+    def __enter__(self):
+        self.previous = int(lib().tdb_set_grid_limit(self.ctas))
+        return self
+
+    def __exit__(self, *exc):
+        lib().tdb_set_grid_limit(self.previous)
+        return False

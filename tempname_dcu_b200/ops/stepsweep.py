@@ -5,9 +5,9 @@
         --configs "ag=2;ag=3;ag=3,epi=off;ag=3,embx=off" [--steps K] [--warmup W]
 
 For each configuration (``;``-separated; each a ``,``-separated list of
-``ag=0..3`` fused all-gather variant, ``rs=0..7`` fused GEMM-RS variant bits,
+``ag=-1..3`` fused all-gather variant (-1 automatic), ``rs=0..7`` fused GEMM-RS variant bits,
 ``epi=on|off`` epilogue reduction, ``embx=on|off`` sparse embedding
-exchange; unnamed keys keep the framework default) this builds the GPT-6.7B
+exchange, ``wg=N`` weight-gradient overlap on N SMs (0 off); unnamed keys keep the framework default) this builds the GPT-6.7B
 tensor-parallel trainer (flux arm, CUDA graph), runs W warm-up steps, times K
 steps with CUDA events between two barriers and takes the max over ranks --
 the same step and timing as ``bench.py`` -- then drops the trainer before the
@@ -23,7 +23,7 @@ import json
 import os
 from datetime import timedelta
 
-KEYS = ("ag", "rs", "epi", "embx")
+KEYS = ("ag", "rs", "epi", "embx", "wg")
 
 
 def parse_config(text):
@@ -32,7 +32,7 @@ def parse_config(text):
         key, _, value = item.partition("=")
         if key not in KEYS:
             raise ValueError(f"unknown key {key!r} (expected one of {KEYS})")
-        if key in ("ag", "rs"):
+        if key in ("ag", "rs", "wg"):
             out[key] = int(value)
         elif value in ("on", "off"):
             out[key] = value == "on"
@@ -55,6 +55,7 @@ def main(argv=None):
     ap.add_argument("--configs", required=True)
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--wgrad-sms", type=int, default=0, help="default of the wg key")
     args = ap.parse_args(argv)
     configs = [parse_config(c) for c in args.configs.split(";") if c.strip()]
     import torch
@@ -67,16 +68,17 @@ def main(argv=None):
     from .. import runtime
     from ..models.config import BENCH_CONFIG
     from ..ops import native
-    from ..parallel import embedding_exchange
+    from ..parallel import allgather, embedding_exchange
     from ..train import Trainer, synthetic_batches
     lib = native.lib()
-    defaults = dict(ag=int(lib.tdb_ag_set_variant(-1)), rs=int(lib.tdb_rs_set_variant(-1)),
-                    epi=runtime.epilogue_reduction_default(), embx=embedding_exchange.enabled())
+    defaults = dict(ag=allgather.ag_variant(), rs=int(lib.tdb_rs_set_variant(-1)),
+                    epi=runtime.epilogue_reduction_default(), embx=embedding_exchange.enabled(), wg=args.wgrad_sms)
     tokens = labels = None
     for cfg in configs:
         apply(cfg, defaults)
         trainer = Trainer(dict(BENCH_CONFIG), "flux", group, operator_factory=runtime.operator_factory_for("flux"),
-                          cuda_graph=True, graph_warmup=min(2, max(0, args.warmup - 1)))
+                          cuda_graph=True, graph_warmup=min(2, max(0, args.warmup - 1)),
+                          wgrad_sms=cfg.get("wg", defaults["wg"]))
         c = trainer.config
         if tokens is None:
             (th, lh), = synthetic_batches(c, 1, seed=4321)

@@ -72,17 +72,23 @@ native.register("tdb_gemm_pick_tile", [ctypes.c_int, ctypes.c_int, ctypes.c_int,
 native.register("tdb_ag_set_variant", [ctypes.c_int])
 
 
+def ag_variant():
+    """The current ``set_ag_variant`` setting (-1 = automatic)."""
+    return int(native.lib().tdb_ag_set_variant(-100))
+
+
 def set_ag_variant(variant):
     """How the fused all-gather GEMM moves the gathered rows on this process:
     0 = the epilogue warps pull them before their first tile, 1 = four
     auxiliary warps pull concurrently with the pipeline, 2 = the same
     auxiliary warps with sixteen 16-byte loads in flight per thread, 3 = the
     auxiliary warps push this rank's rows into every peer's receive buffer
-    and copy the received rows locally (the compressed gather keeps 2).
-    Results are bitwise the same; all ranks must use the same variant.
-    Returns the previous one."""
-    if variant not in (0, 1, 2, 3):
-        raise ValueError("variant must be 0, 1, 2 or 3")
+    and copy the received rows locally (the compressed gather keeps 2);
+    -1 = automatic (the default): 2 from four ranks up, else 0 -- the faster
+    one measured on 8 and on 2 B200s.  Results are bitwise the same; all
+    ranks must use the same variant.  Returns the previous one."""
+    if variant not in (-1, 0, 1, 2, 3):
+        raise ValueError("variant must be -1 (automatic), 0, 1, 2 or 3")
     return int(native.lib().tdb_ag_set_variant(int(variant)))
 
 

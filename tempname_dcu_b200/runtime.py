@@ -59,15 +59,19 @@ def set_rs_variant(variant):
 
 
 # Default of FluxB200(epilogue_reduction=None) for eligible operators (see
-# FluxB200); a process-wide switch for A/B measurements.
-_EPILOGUE_REDUCTION = True
+# FluxB200); a process-wide switch for A/B measurements.  Off: on 8 B200 the
+# epilogue form took 116 / 128 us per attention-out / FC2 call against 66 / 80
+# for the consumer kernel (its producer CTAs stall on peers' tiles), and the
+# training step 311 against 271 ms.
+_EPILOGUE_REDUCTION = False
 FINE_FLAG_BYTES = 32768
 
 
 def set_epilogue_reduction(on):
     """Whether eligible operators created from now on reduce their own blocks
-    in the producer's epilogue (True, the default) or in a separate consumer
-    kernel.  Results are bitwise the same.  Returns the previous setting."""
+    in the producer's epilogue (True) or in a separate consumer kernel (False,
+    the default).  Results are bitwise the same.  Returns the previous
+    setting."""
     global _EPILOGUE_REDUCTION
     old, _EPILOGUE_REDUCTION = _EPILOGUE_REDUCTION, bool(on)
     return old
@@ -205,8 +209,8 @@ class FluxB200:
         no consumer kernel -- the producer's epilogue reduces this rank's own
         tiles (produced last) once every peer's copy of the tile has arrived,
         in the same rank order and rounding as the consumer kernel, so the
-        result is bitwise the same.  None chooses it whenever eligible (see
-        ``set_epilogue_reduction``)."""
+        result is bitwise the same.  None follows ``set_epilogue_reduction``
+        (off by default: slower on 2 and 8 B200s)."""
         import torch
         if not 0 < wait_seconds <= 600:
             raise ValueError("wait_seconds must be in (0, 600]")

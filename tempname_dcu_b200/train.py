@@ -63,15 +63,17 @@ class Trainer:
 
     def __init__(self, config, arm="flux", group=None, *, device="cuda", seed=1234, operator_factory=None,
                  execution_plan=None, cuda_graph=False, graph_warmup=2, taco_allgather=False,
-                 codec_calibration_steps=0, error_budget=0.01):
+                 codec_calibration_steps=0, error_budget=0.01, wgrad_sms=0):
         """``codec_calibration_steps`` > 0 (TACO arms on two or more ranks):
         observe the codec error of every forward reduce-scatter input during
         that many first steps, then freeze one block mask per role within
         ``error_budget`` (warmup_calibration) and keep it; ``codec_plan``
-        holds the frozen bundle afterwards.  Those steps run eagerly."""
+        holds the frozen bundle afterwards.  Those steps run eagerly.
+        ``wgrad_sms`` > 0 overlaps the backward's weight-gradient GEMMs with
+        the fused collectives (``GPT.set_wgrad_overlap``)."""
         import torch
         self.model = GPT(config, arm, group, device=device, seed=seed, operator_factory=operator_factory,
-                         execution_plan=execution_plan, taco_allgather=taco_allgather)
+                         execution_plan=execution_plan, taco_allgather=taco_allgather, wgrad_sms=wgrad_sms)
         c = self.config = self.model.config
         self.optimizer = Optimizer(self.model, c["learning_rate"], c["weight_decay"], c["max_grad_norm"])
         for op in self.model.operators:  # block-scaled FP8 operators re-quantize weights once per step

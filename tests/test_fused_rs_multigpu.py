@@ -75,11 +75,12 @@ def _worker(rank, world, init_file, result_path):
                 c_d=bool(torch.equal(outputs[ARMS[2]], outputs[ARMS[3]])))
             rf = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, remote_first=True).forward(x, w)
             out[f"bitwise.k{k}"]["remote_first"] = bool(torch.equal(rf, outputs[ARMS[0]]))
-            # remote-first operators reduce in the producer's epilogue by default; the
-            # consumer-kernel form of the same order must agree bit for bit, over several
-            # calls (both receive sets), with bias + residual, and with a [K, N] weight
-            rk = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, remote_first=True, epilogue_reduction=False)
-            re_ = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, remote_first=True)
+            # remote-first operators can reduce in the producer's epilogue (opt-in); the
+            # consumer-kernel form of the same order (the default) must agree bit for bit,
+            # over several calls (both receive sets), with bias + residual, and with a
+            # [K, N] weight
+            rk = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, remote_first=True)
+            re_ = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, remote_first=True, epilogue_reduction=True)
             assert re_.consumer_policy == "epilogue" and rk.consumer_policy == "ordered"
             bias_e = torch.randn(n, device="cuda").to(torch.bfloat16)
             res_e = torch.randn(m // world, n, device="cuda").to(torch.bfloat16)
@@ -88,7 +89,8 @@ def _worker(rank, world, init_file, result_path):
                 a, b = re_.forward(xe, w, bias_e, res_e), rk.forward(xe, w, bias_e, res_e)
                 out[f"bitwise.k{k}"][f"epilogue_call{call}"] = bool(torch.equal(a, b))
             wt = w.t().contiguous()
-            eb = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, b_mn=True, remote_first=True).forward(x, wt)
+            eb = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, b_mn=True, remote_first=True,
+                          epilogue_reduction=True).forward(x, wt)
             kb = FluxB200(m, n, k, group, ARMS[0], chunk_rows=chunk, b_mn=True, remote_first=True,
                           epilogue_reduction=False).forward(x, wt)
             out[f"bitwise.k{k}"]["epilogue_b_mn"] = bool(torch.equal(eb, kb))
