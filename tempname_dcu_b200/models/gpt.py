@@ -74,12 +74,12 @@ class GPT:
     """One rank's shard of the TP/SP GPT with flat parameter storage."""
 
     def __init__(self, config, arm="flux", group=None, *, device="cuda", seed=1234, operator_factory=None,
-                 execution_plan=None, materialize=True, taco_allgather=False, wgrad_sms=0):
+                 execution_plan=None, materialize=True, taco_allgather=False, wgrad_sms=None):
         """``wgrad_sms`` > 0 (two or more ranks): in the backward, every
         layer's weight-gradient GEMMs run on a second stream, each on at most
         that many SMs, while the communication-bound fused all-gather and
         reduce-scatter kernels on the compute stream keep the other SMs
-        (``set_wgrad_overlap``)."""
+        (``set_wgrad_overlap``); None takes ``default_wgrad_sms(world)``."""
         import torch
         from ..parallel.tp import TPGroup
         self.tp = TPGroup(group)
@@ -120,7 +120,7 @@ class GPT:
         self._overlap = None   # (fused-kernel CTAs, weight-gradient CTAs) when the backward overlaps them
         self._wgrad_stream = None
         self._wgrad_pending = None
-        self.set_wgrad_overlap(wgrad_sms)
+        self.set_wgrad_overlap(default_wgrad_sms(self.world) if wgrad_sms is None else wgrad_sms)
         # Backward reduce-scatters of the column-parallel data gradients
         # (dX = RS(dY W)) run through the same fused kernel (BF16, ordered)
         # whenever the forward projections do.

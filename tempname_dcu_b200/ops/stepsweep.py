@@ -55,7 +55,8 @@ def main(argv=None):
     ap.add_argument("--configs", required=True)
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--wgrad-sms", type=int, default=0, help="default of the wg key")
+    ap.add_argument("--wgrad-sms", type=int, default=None,
+                    help="default of the wg key (default: the framework's choice for the world size)")
     args = ap.parse_args(argv)
     configs = [parse_config(c) for c in args.configs.split(";") if c.strip()]
     import torch
@@ -70,6 +71,9 @@ def main(argv=None):
     from ..ops import native
     from ..parallel import allgather, embedding_exchange
     from ..train import Trainer, synthetic_batches
+    from ..models.gpt import default_wgrad_sms
+    if args.wgrad_sms is None:
+        args.wgrad_sms = default_wgrad_sms(world)
     lib = native.lib()
     defaults = dict(ag=allgather.ag_variant(), rs=int(lib.tdb_rs_set_variant(-1)),
                     epi=runtime.epilogue_reduction_default(), embx=embedding_exchange.enabled(), wg=args.wgrad_sms)

@@ -63,14 +63,15 @@ class Trainer:
 
     def __init__(self, config, arm="flux", group=None, *, device="cuda", seed=1234, operator_factory=None,
                  execution_plan=None, cuda_graph=False, graph_warmup=2, taco_allgather=False,
-                 codec_calibration_steps=0, error_budget=0.01, wgrad_sms=0):
+                 codec_calibration_steps=0, error_budget=0.01, wgrad_sms=None):
         """``codec_calibration_steps`` > 0 (TACO arms on two or more ranks):
         observe the codec error of every forward reduce-scatter input during
         that many first steps, then freeze one block mask per role within
         ``error_budget`` (warmup_calibration) and keep it; ``codec_plan``
         holds the frozen bundle afterwards.  Those steps run eagerly.
         ``wgrad_sms`` > 0 overlaps the backward's weight-gradient GEMMs with
-        the fused collectives (``GPT.set_wgrad_overlap``)."""
+        the fused collectives (``GPT.set_wgrad_overlap``); None: the default
+        for the world size (``models.gpt.default_wgrad_sms``)."""
         import torch
         self.model = GPT(config, arm, group, device=device, seed=seed, operator_factory=operator_factory,
                          execution_plan=execution_plan, taco_allgather=taco_allgather, wgrad_sms=wgrad_sms)
