@@ -65,8 +65,8 @@ def default_wgrad_sms(world):
     """SMs given to the backward's weight-gradient stream by default at this
     tensor-parallel world size (0: no overlap).  Measured on 8 B200s (GPT-6.7B
     step, ms): 0 -> 258.7, 24 -> 243.6, 40 -> 242.4, 56 -> 243.3, 72 -> 247.1;
-    on 2 (where the fused kernels are compute-bound): 0 -> 453.7, 32 -> 509.9,
-    48 -> 453.2, so no overlap there."""
+    on 4: 0 -> 297.6, 40 -> 275.7; on 2 (where the fused kernels are
+    compute-bound): 0 -> 453.7, 32 -> 509.9, 48 -> 453.2, so no overlap there."""
     return 40 if world >= 4 else 0
 
 
