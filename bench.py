@@ -36,7 +36,7 @@ METRIC = "GPT-6.7B TP8 train tokens/s (max over ranks) at 1/2/4/8 B200; fused-op
 # reduce-scatter, `bench.py --impl baseline` -- measured on B200 with this
 # script at the same N and config.  vs_baseline divides by the entry for the
 # run's N (null where none was measured).
-SAME_BOX_BASELINE_TOKENS_PER_S = {2: 27054.36, 4: 36142.31, 8: 38951.11}
+SAME_BOX_BASELINE_TOKENS_PER_S = {1: 16906.14, 2: 27054.36, 4: 36142.31, 8: 38951.11}
 # Best published predecessor number (8xH100, GPT-6.7B TP8, 8192 tok/step), context only.
 PUBLISHED_MA11_TOKENS_PER_S = 18177.69
 
