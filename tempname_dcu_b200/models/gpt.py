@@ -182,20 +182,20 @@ class GPT:
         from ..ops import native
         return native.grid_limit(self._overlap[0]) if self._overlap else contextlib.nullcontext()
 
-    def _wgrad(self, dy, x, name, keep):
-        """Gr(name) += dy^T x: on the weight-gradient stream when overlapping
-        (``keep`` holds the operands until the compute stream has waited for
-        it), else in line."""
+    def _wgrad(self, dy, x, name, keep, acc=True):
+        """Gr(name) (+)= dy^T x: on the weight-gradient stream when
+        overlapping (``keep`` holds the operands until the compute stream has
+        waited for it), else in line."""
         import torch
         from ..ops import gemm as G
         from ..ops import native
         if self._overlap is None:
-            G.weight_grad(dy, x, self.Gr(name))
+            G.weight_grad(dy, x, self.Gr(name), accumulate=acc)
             return
         side = self._wgrad_stream
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side), native.grid_limit(self._overlap[1]):
-            G.weight_grad(dy, x, self.Gr(name))
+            G.weight_grad(dy, x, self.Gr(name), accumulate=acc)
         keep.extend((dy, x))
 
     def _wgrad_layer_done(self, keep):
@@ -277,10 +277,15 @@ class GPT:
         x2 = self.operators[2 * i + 1].forward(h1, self.P(p + "fc2_weight"), self.P(p + "fc2_bias"), x1)
         return x2, (x, mean1, rstd1, ln1f, qkv, attn, lse, x1, mean2, rstd2, ln2f, z, h1)
 
-    def forward_backward(self, tokens, targets, loss_acc=None, *, grad_scale=None, loss_scale=None):
+    def forward_backward(self, tokens, targets, loss_acc=None, *, grad_scale=None, loss_scale=None,
+                         overwrite_grads=False):
         """One micro-batch: forward, loss (added into ``loss_acc``) and the
-        full backward, accumulating fp32 gradients.  ``tokens``/``targets``
-        are the flattened micro-batch [micro_batch*sequence] (int64, device)."""
+        full backward, accumulating fp32 gradients -- or, with
+        ``overwrite_grads`` (the first micro-batch of a step), writing them, so
+        that the gradient buffer needs no zeroing between steps (every
+        parameter receives a gradient in every micro-batch; x written equals
+        0 + x accumulated, bit for bit).  ``tokens``/``targets`` are the
+        flattened micro-batch [micro_batch*sequence] (int64, device)."""
         import torch
         from ..ops import gemm as G
         from ..ops import kernels as K
@@ -315,18 +320,22 @@ class GPT:
         K.xent_combine(all_stats, self.world, self.m, gstats, row_loss, loss_acc, loss_scale, accumulate=True)
         # ---- backward (starts inside the loss: logits <- dlogits)
         K.xent_grad(logits, targets, self.vocab_start, self.valid_vocab_local, gstats, grad_scale)
+        acc = not overwrite_grads
         dlnf = self._dgrad_rs(logits, self.P("embedding"))
-        G.weight_grad(logits, lnff, self.Gr("embedding"))
+        # the LM-head weight gradient comes first: the embedding backward adds onto it below
+        G.weight_grad(logits, lnff, self.Gr("embedding"), accumulate=acc)
         del logits
         ln_scratch = self._buf("ln_scratch", K.layernorm_scratch_floats(self.ml, self.h), torch.float32)
         dx = K.layernorm_bwd(xl, self.P("final_weight"), meanf, rstdf, dlnf, self.Gr("final_weight"),
-                             self.Gr("final_bias"), ln_scratch)
+                             self.Gr("final_bias"), ln_scratch, accumulate=acc)
         for i in reversed(range(c["layers"])):
             with self._range(f"tdb/layer{i}/bwd"):
-                dx = self._layer_bwd(i, dx, saved[i], ln_scratch)
+                dx = self._layer_bwd(i, dx, saved[i], ln_scratch, acc)
             saved[i] = None
         self._wgrad_join()
         # ---- embedding / positions
+        if overwrite_grads:
+            self.Gr("position").zero_()
         K.position_bwd(dx, self.rank * self.ml if self.world > 1 else 0, c["sequence"], self.Gr("position"))
         if self.embx is not None:  # only the rows of tokens in this rank's shard, from their holders
             dfull = self.embx.backward(tokens, dx, self.vocab_start,
@@ -351,49 +360,49 @@ class GPT:
         stack.callback(torch.cuda.nvtx.range_pop)
         return stack
 
-    def _colsum(self, x, name):
+    def _colsum(self, x, name, acc=True):
         import torch
         from ..ops import kernels as K
         scratch = self._buf("colsum", K.colsum_scratch_floats(x.shape[0], x.shape[1]), torch.float32)
-        K.colsum(x, self.Gr(name), scratch, accumulate=True)
+        K.colsum(x, self.Gr(name), scratch, accumulate=acc)
 
-    def _layer_bwd(self, i, dx2, saved, ln_scratch):
+    def _layer_bwd(self, i, dx2, saved, ln_scratch, acc=True):
         from ..ops import gemm as G
         from ..ops import kernels as K
         c, p = self.config, f"layers.{i}."
         x, mean1, rstd1, ln1f, qkv, attn, lse, x1, mean2, rstd2, ln2f, z, h1 = saved
         keep = []  # operands of weight gradients still running on the overlap stream
         # FC2 (row-parallel): x2 = x1 + RS(h1 W2^T) + b2
-        self._colsum(dx2, p + "fc2_bias")
+        self._colsum(dx2, p + "fc2_bias", acc)
         if self.agg is not None:
             with self._fused_share():
                 dz, dyf = self.agg(dx2, self.P(p + "fc2_weight"), b_mn=True, mode=self.agg.GELU_BWD, aux=z)
         else:
             dyf = self.tp.gather(dx2)
             dz = G.matmul_nt(dyf, self.P(p + "fc2_weight"), gelu_pre=z)
-        self._wgrad(dyf, h1, p + "fc2_weight", keep)
+        self._wgrad(dyf, h1, p + "fc2_weight", keep, acc)
         # FC1 (column-parallel)
-        self._colsum(dz, p + "fc1_bias")
-        self._wgrad(dz, ln2f, p + "fc1_weight", keep)
+        self._colsum(dz, p + "fc1_bias", acc)
+        self._wgrad(dz, ln2f, p + "fc1_weight", keep, acc)
         dln2 = self._dgrad_rs(dz, self.P(p + "fc1_weight"))
         dx1 = K.layernorm_bwd(x1, self.P(p + "ln2_weight"), mean2, rstd2, dln2, self.Gr(p + "ln2_weight"),
-                              self.Gr(p + "ln2_bias"), ln_scratch, dres=dx2)
+                              self.Gr(p + "ln2_bias"), ln_scratch, dres=dx2, accumulate=acc)
         # attention out (row-parallel)
-        self._colsum(dx1, p + "attn_bias")
+        self._colsum(dx1, p + "attn_bias", acc)
         if self.agg is not None:
             with self._fused_share():
                 dattn, dyf = self.agg(dx1, self.P(p + "attn_weight"), b_mn=True)
         else:
             dyf = self.tp.gather(dx1)
             dattn = G.matmul_nt(dyf, self.P(p + "attn_weight"))
-        self._wgrad(dyf, attn, p + "attn_weight", keep)
+        self._wgrad(dyf, attn, p + "attn_weight", keep, acc)
         dqkv = K.attention_bwd(qkv, attn, dattn, lse, c["micro_batch"], c["sequence"], self.heads_local)
         # QKV (column-parallel)
-        self._colsum(dqkv, p + "qkv_bias")
-        self._wgrad(dqkv, ln1f, p + "qkv_weight", keep)
+        self._colsum(dqkv, p + "qkv_bias", acc)
+        self._wgrad(dqkv, ln1f, p + "qkv_weight", keep, acc)
         dln1 = self._dgrad_rs(dqkv, self.P(p + "qkv_weight"))
         dx = K.layernorm_bwd(x, self.P(p + "ln1_weight"), mean1, rstd1, dln1, self.Gr(p + "ln1_weight"),
-                             self.Gr(p + "ln1_bias"), ln_scratch, dres=dx1)
+                             self.Gr(p + "ln1_bias"), ln_scratch, dres=dx1, accumulate=acc)
         self._wgrad_layer_done(keep)
         return dx
 
@@ -439,6 +448,9 @@ class Optimizer:
         self.coef = torch.ones((), dtype=torch.float32, device=dev)
         self.finite = torch.ones((), dtype=torch.int32, device=dev)
         self.step_dev = torch.zeros((), dtype=torch.int32, device=dev)  # advanced by the clip kernel
+        # False when every step's first micro-batch overwrites the gradients
+        # (Trainer): the update then does not zero them
+        self.zero_grad = True
 
     def step(self, loss=None):
         from ..ops import kernels as K
@@ -451,7 +463,7 @@ class Optimizer:
         P = m.params
         K.adamw(P.master, P.grad, P.exp_avg, P.exp_avg_sq, P.param, wd_ranges=P.decay_ranges, lr=self.lr,
                 beta1=self.betas[0], beta2=self.betas[1], eps=self.eps, weight_decay=self.wd,
-                step_dev=self.step_dev, coef=self.coef, finite=self.finite, zero_grad=True)
+                step_dev=self.step_dev, coef=self.coef, finite=self.finite, zero_grad=self.zero_grad)
         return self.norm
 
 

@@ -77,6 +77,7 @@ class Trainer:
                          execution_plan=execution_plan, taco_allgather=taco_allgather, wgrad_sms=wgrad_sms)
         c = self.config = self.model.config
         self.optimizer = Optimizer(self.model, c["learning_rate"], c["weight_decay"], c["max_grad_norm"])
+        self.optimizer.zero_grad = False  # _body's first micro-batch overwrites every gradient
         for op in self.model.operators:  # block-scaled FP8 operators re-quantize weights once per step
             if getattr(op, "mx", None) is not None:
                 op.weight_version = self.optimizer.step_dev
@@ -121,7 +122,8 @@ class Trainer:
             self.model.codec_observer = CodecObserver(self.model)
         self.loss.zero_()
         for micro in range(c["accumulation_steps"]):
-            self.model.forward_backward(tokens[micro], labels[micro], self.loss)
+            # the first micro-batch writes the gradients: no zeroing pass in the update
+            self.model.forward_backward(tokens[micro], labels[micro], self.loss, overwrite_grads=micro == 0)
         norm = self.optimizer.step(self.loss)
         self._steps_done += 1
         if calibrating and self._steps_done == self.codec_calibration_steps:
