@@ -360,20 +360,33 @@ class GPT:
         stack.callback(torch.cuda.nvtx.range_pop)
         return stack
 
-    def _colsum(self, x, name, acc=True):
+    def _colsum(self, x, name, acc=True, keep=None):
+        """Gr(name) (+)= column sums of x (a bias gradient).  With the
+        backward overlap and a ``keep`` list it runs on the weight-gradient
+        stream too (off the compute stream's critical path; same order per
+        bias, so the same bits).  One scratch buffer per shape, allocated on
+        first use and kept, so no buffer is shared across streams."""
         import torch
         from ..ops import kernels as K
-        scratch = self._buf("colsum", K.colsum_scratch_floats(x.shape[0], x.shape[1]), torch.float32)
-        K.colsum(x, self.Gr(name), scratch, accumulate=acc)
+        rows, cols = x.shape
+        scratch = self._buf(f"colsum{rows}x{cols}", K.colsum_scratch_floats(rows, cols), torch.float32)
+        if self._overlap is None or keep is None:
+            K.colsum(x, self.Gr(name), scratch, accumulate=acc)
+            return
+        side = self._wgrad_stream
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            K.colsum(x, self.Gr(name), scratch, accumulate=acc)
+        keep.append(x)
 
     def _layer_bwd(self, i, dx2, saved, ln_scratch, acc=True):
         from ..ops import gemm as G
         from ..ops import kernels as K
         c, p = self.config, f"layers.{i}."
         x, mean1, rstd1, ln1f, qkv, attn, lse, x1, mean2, rstd2, ln2f, z, h1 = saved
-        keep = []  # operands of weight gradients still running on the overlap stream
+        keep = []  # operands of weight / bias gradients still running on the overlap stream
         # FC2 (row-parallel): x2 = x1 + RS(h1 W2^T) + b2
-        self._colsum(dx2, p + "fc2_bias", acc)
+        self._colsum(dx2, p + "fc2_bias", acc, keep)
         if self.agg is not None:
             with self._fused_share():
                 dz, dyf = self.agg(dx2, self.P(p + "fc2_weight"), b_mn=True, mode=self.agg.GELU_BWD, aux=z)
@@ -382,13 +395,13 @@ class GPT:
             dz = G.matmul_nt(dyf, self.P(p + "fc2_weight"), gelu_pre=z)
         self._wgrad(dyf, h1, p + "fc2_weight", keep, acc)
         # FC1 (column-parallel)
-        self._colsum(dz, p + "fc1_bias", acc)
+        self._colsum(dz, p + "fc1_bias", acc, keep)
         self._wgrad(dz, ln2f, p + "fc1_weight", keep, acc)
         dln2 = self._dgrad_rs(dz, self.P(p + "fc1_weight"))
         dx1 = K.layernorm_bwd(x1, self.P(p + "ln2_weight"), mean2, rstd2, dln2, self.Gr(p + "ln2_weight"),
                               self.Gr(p + "ln2_bias"), ln_scratch, dres=dx2, accumulate=acc)
         # attention out (row-parallel)
-        self._colsum(dx1, p + "attn_bias", acc)
+        self._colsum(dx1, p + "attn_bias", acc, keep)
         if self.agg is not None:
             with self._fused_share():
                 dattn, dyf = self.agg(dx1, self.P(p + "attn_weight"), b_mn=True)
@@ -398,7 +411,7 @@ class GPT:
         self._wgrad(dyf, attn, p + "attn_weight", keep, acc)
         dqkv = K.attention_bwd(qkv, attn, dattn, lse, c["micro_batch"], c["sequence"], self.heads_local)
         # QKV (column-parallel)
-        self._colsum(dqkv, p + "qkv_bias", acc)
+        self._colsum(dqkv, p + "qkv_bias", acc, keep)
         self._wgrad(dqkv, ln1f, p + "qkv_weight", keep, acc)
         dln1 = self._dgrad_rs(dqkv, self.P(p + "qkv_weight"))
         dx = K.layernorm_bwd(x, self.P(p + "ln1_weight"), mean1, rstd1, dln1, self.Gr(p + "ln1_weight"),
