@@ -21,14 +21,15 @@
 // cooperatively (all CTAs co-resident or no launch).  Variant 1
 // (tdb_ag_set_variant) moves the pull onto four extra warps so that the
 // epilogue warps drain finished tiles while rows are still arriving; variant
-// 2 keeps sixteen loads in flight per pulling thread.  Variant 3 turns the
-// pull into a push: the four extra warps of every CTA write this rank's rows
-// with plain 16-byte stores straight into every peer's receive buffer (posted
-// writes need no round trip per load, so a few bytes in flight per thread
-// reach the link's bandwidth), stamp a per-slice flag there, and copy the
-// slices that peers pushed into this rank's receive buffer on to the
-// gathered output (a local copy, then the same per-block counters gate the
-// TMA loads).  No send slot is staged.  With
+// 2 keeps sixteen loads in flight per pulling thread (the default from four
+// ranks up).  Variant 3 turns the pull into a push: the four extra warps of
+// every CTA write this rank's rows with plain 16-byte stores straight into
+// every peer's receive buffer (posted writes, no round trip per load), stamp
+// a per-slice flag there, and copy the slices that peers pushed into this
+// rank's receive buffer on to the gathered output (a local copy, then the
+// same per-block counters gate the TMA loads); no send slot is staged.
+// Measured on 8 B200s it is no faster than the deep pull: the same bytes
+// cross the switch at the same effective rate in either direction.  With
 // taco = 1 the send slots hold TACO packets (allgather.cu stages them) and
 // the pull decodes peers' rows; a rank's own rows are copied exact.  Peer readiness uses the
 // all-gather protocol of allgather.cu (epoch published per source; slot
