@@ -1,6 +1,7 @@
 """Rooflines of the fused tensor-parallel paths of a GPT training step.
 
     python -m tempname_dcu_b200.ops.roofline [--world 8] [--taco] [--trace trace.json]
+    python -m tempname_dcu_b200.ops.roofline --world 8 --opbench rows.jsonl --step-ms 243.4
 
 For every fused collective+GEMM path of one layer and micro-batch (forward:
 QKV and FC1 all-gather -> GEMM, attention-out and FC2 GEMM -> reduce-scatter;
@@ -9,6 +10,14 @@ roofline time is the slower of the GEMM at the measured bf16 peak and the
 bytes this rank moves over NVLink at the measured peer bandwidth.  With
 ``--trace`` (the JSON of ``utils/trace.py --step --json``) the measured device
 time of the fused kernels is set against the step's fused roofline.
+
+With ``--opbench`` (the JSON lines of ``ops/opbench.py --ag`` at this world
+size) the exposed communication of a step is estimated: per fused path, the
+fused call's time minus the GEMM alone (what the collective adds), summed over
+layers and micro-batches; the backward's paths take the forward row of the
+same kind and nearest inner size (the all-gather of the attention-out data
+gradient, N = h / W, takes the QKV row; the QKV data-gradient reduce-scatter,
+K = 3h / W, the FC2 row).  ``--step-ms`` sets it against a measured step.
 
 Peaks: ``MEASURED_PEAKS.json`` at the repository root when present (bf16 GEMM
 burst rate, HBM copy); NVLink 770 GB/s per direction (measured peer copy) --
@@ -81,11 +90,44 @@ def step_roofline(config, world, taco=False, tflops=None, nvlink_gbs=None):
     return c["accumulation_steps"] * (c["layers"] * per_layer + head)
 
 
+# forward rows of ops/opbench.py standing in for each fused path of a layer
+_OPBENCH_ROW = {"qkv.fwd": "ag_qkv", "fc1.fwd": "ag_fc1", "attn_out.fwd": "attn", "fc2.fwd": "mlp",
+                "qkv.dgrad": "mlp", "fc1.dgrad": "mlp", "attn_out.dgrad": "ag_qkv", "fc2.dgrad": "ag_fc1"}
+
+
+def exposed_from_opbench(rows, config, world):
+    """(per-path list, total us per optimizer step) of fused time minus GEMM
+    time, from opbench rows (the fastest fused form of each role, flux arm
+    for the reduce-scatters)."""
+    from ..models.config import validate_config
+    c = validate_config(config, world)
+    best = {}
+    for r in rows:
+        if r.get("world") != world or "fused_us" not in r:
+            continue
+        if r["role"] in ("attn", "mlp") and r.get("arm") != "flux":
+            continue
+        if r["role"] not in best or r["fused_us"] < best[r["role"]]["fused_us"]:
+            best[r["role"]] = r
+    missing = sorted(set(_OPBENCH_ROW.values()) - set(best))
+    if missing:
+        raise ValueError(f"opbench rows missing for {missing} at world {world}")
+    per_path = []
+    for path, role in _OPBENCH_ROW.items():
+        r = best[role]
+        per_path.append(dict(path=path, row=role, fused_us=r["fused_us"], gemm_us=r["gemm_only_us"],
+                             exposed_us=max(0.0, r["fused_us"] - r["gemm_only_us"])))
+    per_layer = sum(p["exposed_us"] for p in per_path)
+    return per_path, c["accumulation_steps"] * c["layers"] * per_layer
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--world", type=int, default=8)
     ap.add_argument("--taco", action="store_true", help="TACO-compressed link bytes")
     ap.add_argument("--trace", default="", help="utils/trace.py --json output of one step at this world size")
+    ap.add_argument("--opbench", default="", help="JSON lines of ops/opbench.py --ag at this world size")
+    ap.add_argument("--step-ms", type=float, default=0.0, help="measured step time for the exposed fraction")
     args = ap.parse_args(argv)
     from ..models.config import BENCH_CONFIG
     tflops, nvlink, source = peaks()
@@ -102,6 +144,16 @@ def main(argv=None):
         cats = categorize(data["kernels"])
         measured = sum(cats.get(k, (0.0, 0))[0] for k in ("fused GEMM -> reduce-scatter", "fused all-gather -> GEMM"))
         print(f"measured fused kernels: {measured / 1e3:.1f} ms -> {total / measured:.3f} of roofline")
+    if args.opbench:
+        rows = [json.loads(line) for line in Path(args.opbench).read_text().splitlines() if line.startswith("{")]
+        per_path, exposed = exposed_from_opbench(rows, BENCH_CONFIG, args.world)
+        for p in per_path:
+            print(f"{p['path']:16s} from {p['row']:7s} fused {p['fused_us']:7.1f} us  GEMM {p['gemm_us']:6.1f} us  "
+                  f"exposed {p['exposed_us']:6.1f} us")
+        line = f"exposed communication per step (layers x micro-batches, LM head excluded): {exposed / 1e3:.1f} ms"
+        if args.step_ms > 0:
+            line += f" = {exposed / 1e3 / args.step_ms:.2f} of a {args.step_ms:.1f} ms step"
+        print(line)
 
 
 if __name__ == "__main__":

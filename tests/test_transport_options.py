@@ -62,3 +62,21 @@ def test_grid_limit_is_scoped():
             assert lib.tdb_set_grid_limit(-1) == 40
         assert lib.tdb_set_grid_limit(-1) == 100
     assert lib.tdb_set_grid_limit(-1) == 0
+
+
+def test_exposed_communication_estimate_from_opbench_rows():
+    from tempname_dcu_b200.models.config import BENCH_CONFIG
+    from tempname_dcu_b200.ops.roofline import exposed_from_opbench
+    rows = [dict(role="attn", arm="flux", world=8, fused_us=66.5, gemm_only_us=24.1),
+            dict(role="attn", arm="flux_taco", world=8, fused_us=10.0, gemm_only_us=24.1),  # not a BF16 row
+            dict(role="mlp", arm="flux", world=8, fused_us=80.3, gemm_only_us=31.4),
+            dict(role="ag_qkv", world=8, fused_us=94.8, gemm_only_us=30.8),
+            dict(role="ag_qkv", world=8, fused_us=84.8, gemm_only_us=30.8),  # the fastest form counts
+            dict(role="ag_fc1", world=8, fused_us=96.7, gemm_only_us=33.2),
+            dict(role="ag_fc1", world=4, fused_us=1.0, gemm_only_us=0.0)]   # another world size
+    per_path, total = exposed_from_opbench(rows, BENCH_CONFIG, 8)
+    per_layer = (84.8 - 30.8) * 2 + (96.7 - 33.2) * 2 + (66.5 - 24.1) + (80.3 - 31.4) * 3
+    assert len(per_path) == 8
+    assert abs(total - 32 * 8 * per_layer) < 1e-6
+    with pytest.raises(ValueError, match="missing"):
+        exposed_from_opbench(rows[:2], BENCH_CONFIG, 8)
