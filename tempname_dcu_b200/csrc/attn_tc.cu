@@ -988,8 +988,38 @@ TDB_API int tdb_attn_fwd_tc_timeline(const void* qkv, int64_t ld, void* out, int
 TDB_API int tdb_attn_bwd_pre(const void* out, int64_t ld_out, const void* dout, int64_t ld_dout, float* dsum, int mb,
                              int seq, int Hl, void* stream);
 
+// The dK/dV and dQ kernels are independent (they read the same inputs and
+// write disjoint columns of dqkv), so the dQ kernel runs on a second stream
+// of this library, forked from and joined back into the caller's stream with
+// events (a CUDA graph capture follows the fork and the join).  With few local
+// heads -- 4 at TP8, i.e. 64 CTAs per kernel on 148 SMs -- the two then share
+// the GPU instead of running one after the other.  Per host thread and device.
+namespace {
+struct BwdFork {
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+thread_local BwdFork t_bwd_fork[64];
+
+int bwd_fork_for_device(BwdFork** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) return tdb_host::fail(int(cudaErrorInvalidDevice), "attention bwd: device");
+  BwdFork& f = t_bwd_fork[dev];
+  if (!f.side) {
+    if ((e = cudaStreamCreateWithFlags(&f.side, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&f.fork, cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&f.join, cudaEventDisableTiming)) != cudaSuccess)
+      return tdb_host::fail(int(e), "attention bwd: second stream: %s", cudaGetErrorString(e));
+  }
+  *out = &f;
+  return 0;
+}
+}  // namespace
+
 // Backward on the tensor cores: Dsum pre-pass, then the dK/dV and dQ
-// kernels.  Same contract as tdb_attn_bwd; needs seq % 128 == 0.
+// kernels (concurrently, see above).  Same contract as tdb_attn_bwd; needs
+// seq % 128 == 0.
 TDB_API int tdb_attn_bwd_tc(const void* qkv, int64_t ld, const void* out, int64_t ld_out, const void* dout,
                             int64_t ld_dout, const float* lse, float* dsum, void* dqkv, int64_t ld_dqkv, int mb,
                             int seq, int Hl, float scale, void* stream) {
@@ -1025,14 +1055,22 @@ TDB_API int tdb_attn_bwd_tc(const void* qkv, int64_t ld, const void* out, int64_
     if (e != cudaSuccess) return tdb_host::fail(int(e), "attention bwd (tcgen05): smem attribute");
     init = true;
   }
+  BwdFork* fork = nullptr;
+  if ((rc = bwd_fork_for_device(&fork))) return rc;
   const dim3 grid(Hl * mb, seq / BM);
   uint16_t* dq = static_cast<uint16_t*>(dqkv);
+  cudaError_t e = cudaEventRecord(fork->fork, s);  // after the Dsum pre-pass
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(fork->side, fork->fork, 0);
+  if (e != cudaSuccess) return tdb_host::fail(int(e), "attention bwd: fork: %s", cudaGetErrorString(e));
   bwd_dkdv_kernel<<<grid, kThreads, dkv::kSmem, s>>>(tkv128, tkv64, tdo64, lse, dsum, dq, ld_dqkv, seq, Hl, scale,
                                                       tdb_host::status_ptr());
   tdb_host::launched(1);
-  bwd_dq_kernel<<<grid, kThreads, dqk::kSmem, s>>>(tkv128, tkv64, tdo128, lse, dsum, dq, ld_dqkv, seq, Hl, scale,
-                                                    tdb_host::status_ptr());
+  bwd_dq_kernel<<<grid, kThreads, dqk::kSmem, fork->side>>>(tkv128, tkv64, tdo128, lse, dsum, dq, ld_dqkv, seq, Hl,
+                                                             scale, tdb_host::status_ptr());
   tdb_host::launched(1);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 0 : tdb_host::fail(int(e), "attention bwd (tcgen05) launch: %s", cudaGetErrorString(e));
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return tdb_host::fail(int(e), "attention bwd (tcgen05) launch: %s", cudaGetErrorString(e));
+  e = cudaEventRecord(fork->join, fork->side);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s, fork->join, 0);
+  return e == cudaSuccess ? 0 : tdb_host::fail(int(e), "attention bwd: join: %s", cudaGetErrorString(e));
 }
