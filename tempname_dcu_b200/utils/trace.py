@@ -23,14 +23,14 @@ import time
 # Kernel-name buckets for the per-category summary (first match wins).
 CATEGORIES = (
     ("fused GEMM -> reduce-scatter", ("gemm_rs_kernel", "gemm_rs_mx_kernel", "rs_reduce_kernel", "rs_advance")),
-    ("fused all-gather -> GEMM", ("ag_gemm", "ag_pull", "ag_stage", "ag_advance")),
+    ("fused all-gather -> GEMM", ("ag_gemm", "ag_pull", "ag_stage", "ag_advance", "push_advance")),
     ("GEMM (tcgen05)", ("gemm_kernel", "gemm2_kernel", "gemm_mx_kernel")),
     ("attention", ("attn",)),
     ("NCCL", ("nccl",)),
     ("LayerNorm / reductions", ("layernorm", "ln_", "colred", "colsum")),
     ("cross-entropy", ("xent",)),
     ("optimizer", ("adamw", "clip", "norm")),
-    ("embedding", ("embedding", "emb::", "position", "sort_tokens")),
+    ("embedding", ("embedding", "emb::", "embx::", "position", "sort_tokens")),
 )
 
 

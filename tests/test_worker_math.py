@@ -81,10 +81,13 @@ def test_trace_categories_bucket_kernel_names():
                dict(name="void tdb::aggemm::ag_gemm2_kernel<true, 11, false>(...)", us=7.0, count=1),
                dict(name="void tdb::gemm::gemm2_kernel<true, true, 6>(...)", us=3.0, count=1),
                dict(name="ncclDevKernel_ReduceScatter_Sum_bf16_RING_LL(...)", us=1.0, count=1),
+               dict(name="tdb::aggemm::push_advance_kernel(unsigned int*)", us=0.25, count=1),
+               dict(name="tdb::embx::push_fwd_kernel(tdb::embx::Params, ...)", us=2.0, count=1),
                dict(name="something_else", us=0.5, count=1)]
     cats = categorize(kernels)
     assert cats["fused GEMM -> reduce-scatter"] == (15.0, 4)
-    assert cats["fused all-gather -> GEMM"] == (7.0, 1)
+    assert cats["fused all-gather -> GEMM"] == (7.25, 2)
+    assert cats["embedding"] == (2.0, 1)
     assert cats["GEMM (tcgen05)"] == (3.0, 1) and cats["NCCL"] == (1.0, 1) and cats["other"] == (0.5, 1)
 
 
