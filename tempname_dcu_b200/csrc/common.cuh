@@ -147,7 +147,8 @@ __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_re
 
 // ---------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor) -- plain loads into this CTA's shared memory.
-// No .multicast::cluster form exists in this code base.
+// No TMA or bulk load with .multicast::cluster exists in this code base (the
+// only multicast is the 2-CTA MMA's tcgen05.commit to both CTAs' barriers).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x,
                                             int y) {
